@@ -1,0 +1,53 @@
+"""Pins the CPU oracle to the reference: every golden fixture must be reproduced bit for bit."""
+
+import os
+
+import numpy as np
+import torch
+
+from conftest import GOLDEN
+from oracle import cdg_oracle as oracle
+
+
+def test_oracle_matches_reference_gemm(gemm_case):
+    c = gemm_case
+    d = torch.full_like(c["d"], 7.0)
+    a = (c["a"], c["sa"]) if c["sa"] is not None else c["a"]
+    oracle.m_grouped_fp8_fp4_gemm_nt_contiguous(a, (c["b"], c["sb"]), d, c["m_indices"])
+    assert torch.equal(d.view(torch.int16) if d.dtype == torch.bfloat16 else d,
+                       c["d"].view(torch.int16) if d.dtype == torch.bfloat16 else c["d"]), c["name"]
+
+
+def _z(name):
+    return np.load(os.path.join(GOLDEN, f"{name}.npz"))
+
+
+def test_oracle_sf_atom_reorder_bit_exact():
+    for name in ("sf_reorder_arange", "sf_reorder_padded"):
+        z = _z(name)
+        assert np.array_equal(oracle.reorder_scale_to_sf_atom(z["src"]), z["dst"]), name
+
+
+def test_oracle_fp4_dequant_all_bytes():
+    z = _z("fp4_dequant_all_bytes")
+    out = oracle.dequant_fp4_block(torch.from_numpy(z["src"]), torch.from_numpy(z["scale"]))
+    assert np.array_equal(out.view(torch.int16).numpy(), z["dst"])
+
+
+def test_oracle_float_scale_to_e8m0():
+    z = _z("float_scale_to_e8m0")
+    assert np.array_equal(oracle.float_scale_to_e8m0(torch.from_numpy(z["src"])).numpy(), z["dst"])
+
+
+def test_known_answers_values():
+    """The reference tests' literal expectations (tests/test_fp4_fallback.py:52,72; test_native_abi.py:290; test_scale_reorder.py:398)."""
+    from conftest import load_gemm_case
+    exp = {
+        "kat_grouped_b": [5.0, 8.0, 0.0, 5.0],
+        "kat_interleaved": [8.0, 5.0, 8.0, 5.0],
+    }
+    for name, col in exp.items():
+        assert load_gemm_case(name)["d"][:, 0].float().tolist() == col
+    assert bool((load_gemm_case("kat_all_128")["d"].float() == 128).all())
+    assert bool((load_gemm_case("kat_scale_1536")["d"].float() == 1536).all())
+    assert bool((load_gemm_case("kat_vllm_padding_zero")["d"].float() == 0).all())
