@@ -1,0 +1,106 @@
+"""Grouped FP8 x MXFP4 GEMM with the reference's Python signature.
+
+``m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs)``
+(reference: consumer_deep_gemm/gemm.py:467-470) computes, for every row ``r``
+of ``a`` whose group id ``g = m_indices[r]`` lies in ``[0, G)``::
+
+    d[r, :] = deq(a)[r, :] @ deq(b[g]).T        (FP32 accumulation, cast to d.dtype)
+
+and writes 0 to every other row.  ``deq`` follows the reference's dequant
+(gemm.py:31-52, 147-187).  The work runs in libcdg_b200.so on the current CUDA
+stream without host synchronisation; this module only normalises the argument
+forms the reference accepts and never computes on the host.
+
+Accepted forms (as in the reference):
+  a          ``(fp8 [M,K], fp32 [M,K/128])``; ``(bf16|fp32 [M,K], any)`` (scale ignored);
+             a bare tensor (cast to BF16 like ``a.to(torch.bfloat16)``)
+  b          ``(int8|uint8 [G,N,K/2], scale)`` or ``[N,K/2]`` for one group; scale is
+             uint8/float8_e8m0fnu UE8M0 ``[G,N,K/32]``, a float ``[G,N,K/32]``, the
+             int32 output of ``transform_sf_into_required_layout``, or absent (1.0)
+  m_indices  int32/int64 per-row ids (-1 = padding), psum ends (length G), or None (G == 1)
+  kwargs     ``recipe_a=(1,128)``, ``recipe_b=(1,32)``, ``disable_ue8m0_cast`` (accepted;
+             the FP32 activation scales are always used exactly)
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import native
+
+__all__ = ["m_grouped_fp8_fp4_gemm_nt_contiguous"]
+
+_FLOAT_SCALES = (torch.float32, torch.float16, torch.bfloat16, torch.float64)
+
+
+def _normalize(a, b, d, m_indices):
+    """Map the reference's argument forms onto ``_C.grouped_gemm``'s tensors."""
+    if isinstance(a, tuple):
+        if len(a) != 2:
+            raise ValueError("a must be a (tensor, scale) tuple")
+        x, sa = a
+        if x.dtype == torch.float8_e4m3fn:
+            if sa is None:
+                raise ValueError("FP8 a needs its scale")
+            if sa.dim() != 2 or sa.shape[0] != x.shape[0]:
+                raise ValueError(f"a scale must be [M, K/128], got {tuple(sa.shape)}")
+            sa = sa.float() if sa.dtype != torch.float32 else sa
+        elif x.dtype in (torch.bfloat16, torch.float32):
+            sa = None  # the reference passes BF16/FP32 activations through unscaled (gemm.py:33-34)
+        else:
+            raise ValueError(f"a must be FP8/BF16/FP32, got {x.dtype}")
+    else:
+        x, sa = a, None
+        if x.dtype == torch.float8_e4m3fn:
+            # bare FP8 is cast to BF16 without a scale (gemm.py:289-293): scale 1 is exact
+            sa = torch.ones(x.shape[0], (x.shape[1] + 127) // 128, dtype=torch.float32, device=x.device)
+        elif x.dtype != torch.bfloat16:
+            x = x.to(torch.bfloat16)
+    if isinstance(b, tuple):
+        if len(b) != 2:
+            raise ValueError("b must be a (tensor, scale) tuple")
+        bt, bs = b
+    else:
+        bt, bs = b, None
+    if bt.dtype not in (torch.int8, torch.uint8):
+        raise NotImplementedError(f"b must be packed FP4 (int8/uint8), got {bt.dtype}")
+    single = bt.dim() == 2
+    if single:
+        bt = bt.unsqueeze(0)
+        if bs is not None and bs.dim() == 2:
+            bs = bs.unsqueeze(0)
+        m_indices = None  # one group: every row uses it (gemm.py:347-350)
+    if bt.dim() != 3:
+        raise ValueError(f"grouped B must be 2D or 3D, got shape {tuple(bt.shape)}")
+    bt = bt.view(torch.uint8)
+    k = x.shape[1]
+    if bs is None:
+        bs = torch.full((bt.shape[0], bt.shape[1], (k + 31) // 32), 127, dtype=torch.uint8, device=bt.device)
+    elif bs.dtype == torch.float8_e8m0fnu:
+        bs = bs.view(torch.uint8)
+    elif bs.dtype in _FLOAT_SCALES:
+        bs = bs.float() if bs.dtype != torch.float32 else bs
+    elif bs.dtype not in (torch.uint8, torch.int32):
+        raise ValueError(f"b scale must be UE8M0 bytes, float or transformed int32, got {bs.dtype}")
+    if bs.dtype != torch.int32 and bs.dim() != 3:
+        raise ValueError(f"b scale must be [G, N, K/32], got {tuple(bs.shape)}")
+    if m_indices is None and bt.shape[0] != 1:
+        raise ValueError("m_indices is required when b has multiple groups")
+    return x, sa, bt, bs, d, m_indices
+
+
+def _check_recipes(kwargs):
+    ra = kwargs.get("recipe_a")
+    rb = kwargs.get("recipe_b")
+    if ra is not None and tuple(ra) != (1, 128):
+        raise NotImplementedError(f"recipe_a {tuple(ra)} is not supported; this kernel takes (1, 128)")
+    if rb is not None and tuple(rb) != (1, 32):
+        raise NotImplementedError(f"recipe_b {tuple(rb)} is not supported; this kernel takes (1, 32)")
+
+
+def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs) -> None:
+    """M-grouped FP8 x FP4 GEMM for the MoE contiguous layout (see module docstring)."""
+    _check_recipes(kwargs)
+    x, sa, bt, bs, d, ids = _normalize(a, b, d, m_indices)
+    flags = 1 if kwargs.get("_force_exact_path") else 0
+    native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags)

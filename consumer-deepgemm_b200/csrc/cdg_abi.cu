@@ -1,0 +1,413 @@
+// Host side of libcdg_b200.so: argument checks, workspace carving, TMA
+// descriptors and kernel launches behind the C ABI declared in cdg_b200.h.
+//
+// No call here blocks the host or copies device data to the host (except
+// cdg_read_device_status, a diagnostic).  The only state kept between calls is a
+// per-device, initialise-once record (SM count, compute capability, kernel
+// attributes) and the resolved driver entry point for tensor-map encoding.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "cdg_b200.h"
+#include "cdg_kernels.cuh"
+#include "cdg_layout.h"
+
+namespace cdg {
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int cc_major = 0;
+  bool ok = false;
+};
+
+constexpr int kMaxDevices = 64;
+
+const DeviceInfo& device_info(int dev) {
+  static DeviceInfo infos[kMaxDevices];
+  static std::once_flag flags[kMaxDevices];
+  std::call_once(flags[dev], [dev] {
+    DeviceInfo& d = infos[dev];
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return;
+    if (cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return;
+    if (d.cc_major == 10) {
+      if (cudaFuncSetAttribute(cdg_gemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GemmSmem<32>::kBytes) != cudaSuccess)
+        return;
+      if (cudaFuncSetAttribute(cdg_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GemmSmem<128>::kBytes) != cudaSuccess)
+        return;
+      if (cudaFuncSetAttribute(cdg_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
+          cudaSuccess)
+        return;
+    }
+    d.ok = true;
+  });
+  return infos[dev];
+}
+
+// Optional events recorded around the tensor-core GEMM launches (per host thread).
+thread_local cudaEvent_t t_prof_start = nullptr;
+thread_local cudaEvent_t t_prof_stop = nullptr;
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Shape/dtype validation shared by every entry point; does not look at alignment.
+int validate(const cdg_gemm_args* g) {
+  if (!g) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->M < 0 || g->N <= 0 || g->K <= 0 || g->E <= 0) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->M > (int64_t(1) << 31) - 256 || g->N > (int64_t(1) << 24) || g->K > (int64_t(1) << 20) ||
+      g->E > (int64_t(1) << 20))
+    return CDG_ERR_UNSUPPORTED;
+  if (g->K % 2) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->M > 0 && (!g->a || !g->d)) return CDG_ERR_INVALID_ARGUMENT;
+  if (!g->b || !g->sfb) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->a_dtype != CDG_DTYPE_E4M3 && g->a_dtype != CDG_DTYPE_BF16 && g->a_dtype != CDG_DTYPE_F32)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (g->a_dtype == CDG_DTYPE_E4M3) {
+    if (!g->sa || g->sa_cols <= 0) return CDG_ERR_INVALID_ARGUMENT;
+    // Same rule as the reference: sa_cols > 1 gives blocks of K / sa_cols;
+    // a single column is one scale per row only when K fits one 128 block.
+    if (g->sa_cols == 1 && g->K > 128) return CDG_ERR_UNSUPPORTED;
+    if (g->sa_cols > 1 && (g->K % g->sa_cols)) return CDG_ERR_INVALID_ARGUMENT;
+  }
+  if (g->sfb_dtype != CDG_DTYPE_UE8M0 && g->sfb_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->sfb_layout != CDG_SF_ROW_MAJOR && g->sfb_layout != CDG_SF_ATOMS) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->sfb_layout == CDG_SF_ATOMS && (g->sfb_dtype != CDG_DTYPE_UE8M0 || g->K % 128 || g->N % 128))
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (g->d_dtype != CDG_DTYPE_BF16 && g->d_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->a_row_stride < g->K || g->d_row_stride < g->N) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->b_stride_n < g->K / 2 || g->b_stride_e < g->b_stride_n * g->N) return CDG_ERR_INVALID_ARGUMENT;
+  switch (g->index_form) {
+    case CDG_INDEX_NONE:
+      if (g->E != 1) return CDG_ERR_INVALID_ARGUMENT;
+      break;
+    case CDG_INDEX_PER_ROW:
+      if (!g->m_indices && g->M > 0) return CDG_ERR_INVALID_ARGUMENT;
+      if (g->m_indices_len != g->M) return CDG_ERR_INVALID_ARGUMENT;
+      break;
+    case CDG_INDEX_PSUM:
+      if (!g->m_indices || g->m_indices_len != g->E) return CDG_ERR_INVALID_ARGUMENT;
+      break;
+    default:
+      return CDG_ERR_INVALID_ARGUMENT;
+  }
+  if (g->index_form != CDG_INDEX_NONE && g->m_indices_dtype != CDG_DTYPE_I32 && g->m_indices_dtype != CDG_DTYPE_I64)
+    return CDG_ERR_INVALID_ARGUMENT;
+  return CDG_OK;
+}
+
+// True when the tensor-core kernel can run these (validated) arguments.
+bool fast_path(const cdg_gemm_args* g) {
+  if (g->flags & CDG_FLAG_FORCE_GENERIC) return false;
+  if (g->a_dtype != CDG_DTYPE_E4M3 || g->sfb_dtype != CDG_DTYPE_UE8M0 || g->d_dtype != CDG_DTYPE_BF16) return false;
+  if (g->K % 128 || g->N % 128 || g->sa_cols != g->K / 128) return false;
+  if (g->a_row_stride % 16 || !aligned(g->a, 16)) return false;
+  if (g->b_stride_n != g->K / 2 || g->b_stride_e != g->b_stride_n * g->N || !aligned(g->b, 32)) return false;
+  if (g->d_row_stride % 8 || !aligned(g->d, 16)) return false;
+  if (g->sfb_layout == CDG_SF_ATOMS && !aligned(g->sfb, 16)) return false;
+  return true;
+}
+
+bool sfw_needs_transform(const cdg_gemm_args* g) { return g->sfb_layout == CDG_SF_ROW_MAJOR; }
+
+WorkspaceLayout layout_for(const cdg_gemm_args* g) {
+  const bool fast = fast_path(g);
+  return WorkspaceLayout::make(g->M, g->K, g->N, g->E, fast, g->index_form == CDG_INDEX_PSUM,
+                               fast && sfw_needs_transform(g));
+}
+
+int launch_sf_atoms(const uint8_t* sf, int64_t se, int64_t sn, int64_t E, int64_t N, int64_t KB, uint32_t* out,
+                    cudaStream_t stream, int sm_count) {
+  const int64_t words = E * ((N + 127) / 128) * ((KB + 3) / 4) * 128;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((words + threads - 1) / threads, int64_t(sm_count) * 32);
+  if (blocks <= 0) return CDG_OK;
+  cdg_sf_atom_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(sf, se, sn, out, static_cast<int>(E),
+                                                                           static_cast<int>(N), static_cast<int>(KB));
+  return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
+}
+
+int make_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap* tw, CUtensorMap* ta) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return CDG_ERR_CUDA;
+  {
+    // Weights: [E*N rows, K] packed E2M1, unpacked into one byte per element in shared memory.
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(g->E * g->N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->K / 2)};
+    cuuint32_t box[2] = {128, 128};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(tw, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(g->b), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return CDG_ERR_CUDA;
+  }
+  {
+    // Activation planes: [2 * nblk * 128 rows, K] e4m3 bytes, 16-row boxes.
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(2 * nblk * 128)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->K)};
+    cuuint32_t box[2] = {128, 16};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, hilo, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return CDG_ERR_CUDA;
+  }
+  return CDG_OK;
+}
+
+int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int st = validate(g);
+  if (st != CDG_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return CDG_ERR_CUDA;
+  const DeviceInfo& di = device_info(dev);
+  if (!di.ok) return CDG_ERR_CUDA;
+  if (di.cc_major != 10) return CDG_ERR_NO_SM100;
+  if (g->M == 0) return CDG_OK;
+
+  const WorkspaceLayout wl = layout_for(g);
+  if (!workspace || workspace_bytes < wl.total) return CDG_ERR_WORKSPACE;
+  if (!aligned(workspace, 1024)) return CDG_ERR_ALIGNMENT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* ctrl = reinterpret_cast<int*>(ws + wl.ctrl);
+  if (cudaMemsetAsync(ctrl, 0, kCtrlWords * 4, stream) != cudaSuccess) return CDG_ERR_CUDA;
+
+  const int64_t nblk = (g->M + 127) / 128;
+  const void* ids = g->index_form == CDG_INDEX_NONE ? nullptr : g->m_indices;
+  int ids_dtype = g->m_indices_dtype;
+  if (g->index_form == CDG_INDEX_PSUM) {
+    int32_t* rows = reinterpret_cast<int32_t*>(ws + wl.row_ids);
+    const unsigned blocks = static_cast<unsigned>((g->M + 255) / 256);
+    if (ids_dtype == CDG_DTYPE_I64)
+      cdg_psum_rows_kernel<int64_t><<<blocks, 256, 0, stream>>>(static_cast<const int64_t*>(ids),
+                                                                 static_cast<int>(g->E), static_cast<int>(g->M), rows);
+    else
+      cdg_psum_rows_kernel<int32_t><<<blocks, 256, 0, stream>>>(static_cast<const int32_t*>(ids),
+                                                                 static_cast<int>(g->E), static_cast<int>(g->M), rows);
+    ids = rows;
+    ids_dtype = CDG_DTYPE_I32;
+  }
+  int* lists = reinterpret_cast<int*>(ws + wl.lists);
+  int4* blk_info = reinterpret_cast<int4*>(ws + wl.blk_info);
+
+  GenericArgs ga{};
+  ga.a = g->a;
+  ga.a_dtype = g->a_dtype;
+  ga.a_row_stride = g->a_row_stride;
+  ga.sa = g->sa;
+  ga.sa_stride_m = g->sa_stride_m;
+  ga.sa_stride_k = g->sa_stride_k;
+  ga.sa_block_k = g->a_dtype == CDG_DTYPE_E4M3 ? (g->sa_cols > 1 ? static_cast<int>(g->K / g->sa_cols) : 128) : 128;
+  ga.b = static_cast<const uint8_t*>(g->b);
+  ga.b_stride_e = g->b_stride_e;
+  ga.b_stride_n = g->b_stride_n;
+  ga.sb = g->sfb;
+  ga.sb_dtype = g->sfb_dtype;
+  ga.sb_atoms = g->sfb_layout == CDG_SF_ATOMS;
+  ga.sb_stride_e = g->sfb_stride_e;
+  ga.sb_stride_n = g->sfb_stride_n;
+  ga.d = g->d;
+  ga.d_dtype = g->d_dtype;
+  ga.d_row_stride = g->d_row_stride;
+  ga.M = static_cast<int>(g->M);
+  ga.N = static_cast<int>(g->N);
+  ga.K = static_cast<int>(g->K);
+  ga.E = static_cast<int>(g->E);
+  ga.nblk = static_cast<int>(nblk);
+  const size_t generic_smem = static_cast<size_t>(g->K) * 4;
+  if (generic_smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
+  const int64_t generic_units = nblk * ((g->N + 255) / 256);
+
+  if (!fast_path(g)) {
+    ga.ids = ids;
+    ga.ids_is_64 = ids_dtype == CDG_DTYPE_I64;
+    ga.list = nullptr;
+    ga.count = nullptr;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(di.sm_count) * 8));
+    cdg_generic_kernel<<<grid, 256, generic_smem, stream>>>(ga);
+    return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
+  }
+
+  // ---------------------------------------------------------------- tensor-core path
+  const uint32_t* sfw = static_cast<const uint32_t*>(g->sfb);
+  if (sfw_needs_transform(g)) {
+    uint32_t* out = reinterpret_cast<uint32_t*>(ws + wl.sfw_atoms);
+    st = launch_sf_atoms(static_cast<const uint8_t*>(g->sfb), g->sfb_stride_e, g->sfb_stride_n, g->E, g->N, g->K / 32,
+                         out, stream, di.sm_count);
+    if (st != CDG_OK) return st;
+    sfw = out;
+  }
+  uint8_t* hilo = ws + wl.hilo;
+  uint32_t* sfa_atoms = reinterpret_cast<uint32_t*>(ws + wl.sfa_atoms);
+
+  PrepArgs pa{};
+  pa.a = static_cast<const uint8_t*>(g->a);
+  pa.a_row_stride = g->a_row_stride;
+  pa.sa = g->sa;
+  pa.sa_stride_m = g->sa_stride_m;
+  pa.sa_stride_k = g->sa_stride_k;
+  pa.ids = ids;
+  pa.M = static_cast<int>(g->M);
+  pa.K = static_cast<int>(g->K);
+  pa.E = static_cast<int>(g->E);
+  pa.nblk = static_cast<int>(nblk);
+  pa.hilo = hilo;
+  pa.sfa_atoms = sfa_atoms;
+  pa.blk_info = blk_info;
+  pa.ctrl = ctrl;
+  pa.lists = lists;
+  if (ids_dtype == CDG_DTYPE_I64)
+    cdg_prep_kernel<int64_t><<<static_cast<unsigned>(nblk), 256, 0, stream>>>(pa);
+  else
+    cdg_prep_kernel<int32_t><<<static_cast<unsigned>(nblk), 256, 0, stream>>>(pa);
+  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+
+  CUtensorMap tw, ta;
+  st = make_tmaps(g, hilo, nblk, &tw, &ta);
+  if (st != CDG_OK) return st;
+
+  GemmArgs ka{};
+  ka.blk_info = blk_info;
+  ka.ctrl = ctrl;
+  ka.ids = ids;
+  ka.ids_is_64 = ids_dtype == CDG_DTYPE_I64;
+  ka.sfw_atoms = sfw;
+  ka.sfa_atoms = sfa_atoms;
+  ka.d = static_cast<__nv_bfloat16*>(g->d);
+  ka.d_row_stride = g->d_row_stride;
+  ka.M = static_cast<int>(g->M);
+  ka.N = static_cast<int>(g->N);
+  ka.K = static_cast<int>(g->K);
+  ka.E = static_cast<int>(g->E);
+  ka.nblk = static_cast<int>(nblk);
+  ka.status = ctrl + kCtrlStatus;
+  ka.zero_list = lists + kClassZero * nblk;
+
+  if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
+  // Narrow blocks (decode-like) and all-padding blocks.
+  ka.list = lists + kClassNarrow * nblk;
+  ka.count_slot = kCtrlCount0 + kClassNarrow;
+  ka.do_zero_blocks = 1;
+  cdg_gemm_kernel<32><<<di.sm_count, 256, GemmSmem<32>::kBytes, stream>>>(tw, ta, ka);
+  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  // Wide blocks (prefill-like).
+  ka.list = lists + kClassWide * nblk;
+  ka.count_slot = kCtrlCount0 + kClassWide;
+  ka.do_zero_blocks = 0;
+  cdg_gemm_kernel<128><<<di.sm_count, 256, GemmSmem<128>::kBytes, stream>>>(tw, ta, ka);
+  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  if (t_prof_stop && cudaEventRecord(t_prof_stop, stream) != cudaSuccess) return CDG_ERR_CUDA;
+  // Blocks holding rows of several experts: exact SIMT path over the listed blocks.
+  ga.ids = ids;
+  ga.ids_is_64 = ids_dtype == CDG_DTYPE_I64;
+  ga.list = lists + kClassIrregular * nblk;
+  ga.count = ctrl + kCtrlCount0 + kClassIrregular;
+  {
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(di.sm_count)));
+    cdg_generic_kernel<<<grid, 256, generic_smem, stream>>>(ga);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  }
+  return CDG_OK;
+}
+
+}  // namespace
+}  // namespace cdg
+
+extern "C" {
+
+int cdg_grouped_fp8_fp4_gemm_nt_contiguous(const cdg_gemm_args* args, void* workspace, size_t workspace_bytes,
+                                           cdg_stream_t stream) {
+  return cdg::run(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t cdg_grouped_fp8_fp4_workspace_bytes(const cdg_gemm_args* args) {
+  if (cdg::validate(args) != CDG_OK) return 0;
+  return cdg::layout_for(args).total;
+}
+
+int cdg_can_implement(const cdg_gemm_args* args) {
+  if (cdg::validate(args) != CDG_OK) return -1;
+  return cdg::fast_path(args) ? 1 : 0;
+}
+
+int cdg_transform_sf(const uint8_t* sf, int64_t stride_e, int64_t stride_n, int64_t E, int64_t N, int64_t KB,
+                     uint8_t* out, cdg_stream_t stream) {
+  if (!sf || !out || E <= 0 || N <= 0 || KB <= 0 || stride_n < KB || stride_e < stride_n * N)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(out) % 4) return CDG_ERR_ALIGNMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= cdg::kMaxDevices) return CDG_ERR_CUDA;
+  const cdg::DeviceInfo& di = cdg::device_info(dev);
+  if (!di.ok) return CDG_ERR_CUDA;
+  return cdg::launch_sf_atoms(sf, stride_e, stride_n, E, N, KB, reinterpret_cast<uint32_t*>(out),
+                              reinterpret_cast<cudaStream_t>(stream), di.sm_count);
+}
+
+size_t cdg_sf_atoms_bytes(int64_t E, int64_t N, int64_t KB) {
+  if (E <= 0 || N <= 0 || KB <= 0) return 0;
+  return static_cast<size_t>(E) * ((N + 127) / 128) * ((KB + 3) / 4) * 512;
+}
+
+int cdg_read_device_status(const void* workspace, cdg_stream_t stream) {
+  if (!workspace) return CDG_ERR_INVALID_ARGUMENT;
+  int word = 0;
+  const int* src = static_cast<const int*>(workspace) + cdg::kCtrlStatus;
+  if (cudaMemcpyAsync(&word, src, sizeof(int), cudaMemcpyDeviceToHost, reinterpret_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return CDG_ERR_CUDA;
+  if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return CDG_ERR_CUDA;
+  return (word & cdg::kStatusTimeout) ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
+}
+
+const char* cdg_build_info(void) {
+  return "consumer-deepgemm-b200; arch=sm_100a; abi=1; kernels=tcgen05.mma.kind::mxf8f6f4.block_scale "
+         "(TMA 16U4_ALIGN16B weights, e4m3 hi/lo activation planes), exact SIMT fallback";
+}
+
+int cdg_mk_alignment_for_contiguous_layout(void) { return 128; }
+
+int cdg_set_profile_events(void* start_event, void* stop_event) {
+  if ((start_event == nullptr) != (stop_event == nullptr)) return CDG_ERR_INVALID_ARGUMENT;
+  cdg::t_prof_start = static_cast<cudaEvent_t>(start_event);
+  cdg::t_prof_stop = static_cast<cudaEvent_t>(stop_event);
+  return CDG_OK;
+}
+
+const char* cdg_status_string(int status) {
+  switch (status) {
+    case CDG_OK: return "ok";
+    case CDG_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case CDG_ERR_UNSUPPORTED: return "unsupported";
+    case CDG_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case CDG_ERR_WORKSPACE: return "workspace missing or too small";
+    case CDG_ERR_CUDA: return "CUDA runtime error";
+    case CDG_ERR_DEVICE_TIMEOUT: return "device pipeline wait timed out";
+    case CDG_ERR_NO_SM100: return "device is not compute capability 10.x (B200)";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

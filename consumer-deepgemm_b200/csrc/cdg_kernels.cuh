@@ -1,0 +1,592 @@
+// Device kernels of the B200 grouped FP8 x MXFP4 MoE GEMM.
+//
+//   cdg_sf_atom_kernel      weight scales [E, N, K/32] -> 128x4 scale-factor atoms (weight-load time)
+//   cdg_psum_rows_kernel    psum-form m_indices -> one group id per row
+//   cdg_prep_kernel         per 128-row block: plan (expert, rows, class) + oracle-faithful split of the
+//                           activations into two e4m3 planes (hi, lo) and their UE8M0 scale atoms;
+//                           the last CTA orders the blocks of each class into work lists
+//   cdg_gemm_kernel<TOK>    persistent tcgen05 block-scaled GEMM over one class of blocks
+//   cdg_generic_kernel      exact SIMT path for blocks/layouts the tensor-core kernel does not take
+//
+// Layout facts shared by the host code live in cdg_layout.h.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cstdint>
+
+#include "cdg_layout.h"
+#include "cdg_ptx.cuh"
+
+namespace cdg {
+
+// =====================================================================================
+// Scale-factor atoms.
+// One atom holds the UE8M0 scales of 128 rows x 4 consecutive 32-wide K blocks (512 B):
+// byte (r, c) of a [rows, kb] matrix goes to atom (r/128, c/4), offset
+// (r%32)*16 + ((r%128)/32)*4 + c%4; missing rows/columns read 127 (scale 1.0).
+// This is the order in which tcgen05.cp.32x128b.warpx4 feeds the MMA's scale
+// columns, and the reorder of consumer_deep_gemm/gemm.py:76-116.
+// =====================================================================================
+__global__ void cdg_sf_atom_kernel(const uint8_t* __restrict__ src, int64_t src_stride_e, int64_t src_stride_n,
+                                   uint32_t* __restrict__ dst, int E, int N, int KB32) {
+  const int n_tiles = (N + 127) / 128;
+  const int k_tiles = (KB32 + 3) / 4;
+  const int64_t words_per_e = static_cast<int64_t>(n_tiles) * k_tiles * 128;
+  const int64_t total = words_per_e * E;
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; w < total;
+       w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = static_cast<int>(w / words_per_e);
+    const int64_t rem = w - e * words_per_e;
+    const int atom = static_cast<int>(rem >> 7);
+    const int j = static_cast<int>(rem & 127);
+    const int mt = atom / k_tiles, kt = atom - mt * k_tiles;
+    const int row = mt * 128 + (j & 3) * 32 + (j >> 2);
+    uint32_t v = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int col = kt * 4 + b;
+      uint32_t byte = 127u;
+      if (row < N && col < KB32) byte = src[e * src_stride_e + row * src_stride_n + col];
+      v |= byte << (8 * b);
+    }
+    dst[w] = v;
+  }
+}
+
+// =====================================================================================
+// psum form: m_indices[g] is the cumulative end row of group g (group g owns rows
+// [end[g-1], end[g]) with end[-1] = 0).  Later groups win where ranges overlap, as
+// in the reference's per-group index_copy_ (consumer_deep_gemm/gemm.py:318-324, 358-367).
+// =====================================================================================
+template <typename IdT>
+__global__ void cdg_psum_rows_kernel(const IdT* __restrict__ ends, int G, int M, int32_t* __restrict__ row_ids) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= M) return;
+  int32_t id = -1;
+  int64_t start = 0;
+  for (int g = 0; g < G; ++g) {
+    const int64_t end = static_cast<int64_t>(ends[g]);
+    if (r >= start && r < end) id = g;
+    start = end;
+  }
+  row_ids[r] = id;
+}
+
+// =====================================================================================
+// Prep: block plan + activation split.
+//
+// For a row r with valid expert id and a K block kb (128 wide) the reference's
+// activation value is x = bf16(bf16(a[r,k]) * bf16(sa[r,kb])) (gemm.py:44-48).
+// With s = bf16(sa[r,kb]) = m * 2^E, m in [0.5, 1), every x / 2^E is a BF16
+// number below 448 in magnitude, so it splits exactly into hi = e4m3(x/2^E) and
+// lo = e4m3(x/2^E - hi) whenever |x/2^E| >= 2^-2 (elements below that lose at most
+// 2^-10 * 2^E).  The tensor core then multiplies both planes with the weights
+// under the common UE8M0 scale E+127: sum_k (hi+lo) * 2^E * w = sum_k x * w.
+// =====================================================================================
+struct PrepArgs {
+  const uint8_t* a;  // e4m3 [M, K]
+  int64_t a_row_stride;
+  const float* sa;  // [M, K/128]
+  int64_t sa_stride_m, sa_stride_k;
+  const void* ids;  // per-row group ids (int32 or int64)
+  int M, K, E;
+  int nblk;
+  uint8_t* hilo;           // [2][nblk*128][K]
+  uint32_t* sfa_atoms;     // [nblk][K/128][128] words
+  int4* blk_info;          // [nblk]
+  int* ctrl;               // control words (zeroed by the host before launch)
+  int* lists;              // [kNumClasses][nblk]
+};
+
+// Group id of row r; a null id vector means every row belongs to group 0.
+__device__ __forceinline__ int64_t load_id(const void* ids, int is64, int r) {
+  if (!ids) return 0;
+  return is64 ? static_cast<const int64_t*>(ids)[r] : static_cast<int64_t>(static_cast<const int32_t*>(ids)[r]);
+}
+
+__device__ __forceinline__ uint8_t f32_to_e4m3(float v) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+template <typename IdT>
+__global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
+  __shared__ int s_min_id, s_max_id, s_max_row;
+  __shared__ int s_last;
+  __shared__ int s_cls_count[kNumClasses][257];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_min_id = 0x7fffffff;
+    s_max_id = -1;
+    s_max_row = -1;
+  }
+  __syncthreads();
+  if (tid < 128) {
+    const int r = b * 128 + tid;
+    if (r < p.M) {
+      const int64_t id = load_id(p.ids, sizeof(IdT) == 8, r);
+      if (id >= 0 && id < p.E) {
+        atomicMin(&s_min_id, static_cast<int>(id));
+        atomicMax(&s_max_id, static_cast<int>(id));
+        atomicMax(&s_max_row, tid);
+      }
+    }
+  }
+  __syncthreads();
+  const int eff = s_max_row + 1;
+  int cls, expert;
+  if (eff == 0) {
+    cls = kClassZero;
+    expert = -1;
+  } else if (s_min_id != s_max_id) {
+    cls = kClassIrregular;
+    expert = -2;
+  } else {
+    cls = eff <= kNarrowTok ? kClassNarrow : kClassWide;
+    expert = s_min_id;
+  }
+
+  if (cls == kClassNarrow || cls == kClassWide) {
+    const int ntok = (eff + 15) & ~15;
+    const int K = p.K;
+    const int kb_count = K / 128;
+    const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
+    // (1) activation planes, 16 bytes per step
+    const int chunks_per_row = K / 16;
+    const int total = ntok * chunks_per_row;
+    for (int c = tid; c < total; c += blockDim.x) {
+      const int rr = c / chunks_per_row;
+      const int kc = c - rr * chunks_per_row;
+      const int r = b * 128 + rr;
+      uint4 hi4 = make_uint4(0, 0, 0, 0), lo4 = make_uint4(0, 0, 0, 0);
+      bool valid = false;
+      if (r < p.M) valid = load_id(p.ids, sizeof(IdT) == 8, r) == expert;
+      if (valid) {
+        const int kb = (kc * 16) / 128;
+        const float s = p.sa[r * p.sa_stride_m + kb * p.sa_stride_k];
+        const float sbf = __bfloat162float(__float2bfloat16_rn(s));
+        int ex = 0;
+        if (sbf != 0.0f && isfinite(sbf)) frexpf(fabsf(sbf), &ex);
+        const float inv = ldexpf(1.0f, -ex);
+        const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + kc * 16);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(&raw);
+        uint8_t* hb = reinterpret_cast<uint8_t*>(&hi4);
+        uint8_t* lb = reinterpret_cast<uint8_t*>(&lo4);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float xf = e4m3_to_f32(src[i]);
+          const float x = __bfloat162float(__float2bfloat16_rn(xf * sbf));
+          const float v = x * inv;
+          const uint8_t h = f32_to_e4m3(v);
+          hb[i] = h;
+          lb[i] = f32_to_e4m3(v - e4m3_to_f32(h));
+        }
+      }
+      uint8_t* dst = p.hilo + static_cast<int64_t>(r) * K + kc * 16;
+      *reinterpret_cast<uint4*>(dst) = hi4;
+      *reinterpret_cast<uint4*>(dst + plane) = lo4;
+    }
+    // (2) UE8M0 scale atoms of the activation planes (value replicated over the 4 sub-blocks of 32)
+    for (int w = tid; w < kb_count * 128; w += blockDim.x) {
+      const int kb = w >> 7;
+      const int j = w & 127;
+      const int rr = (j & 3) * 32 + (j >> 2);
+      const int r = b * 128 + rr;
+      uint32_t byte = 127u;
+      if (rr < eff && r < p.M && load_id(p.ids, sizeof(IdT) == 8, r) == expert) {
+        const float s = p.sa[r * p.sa_stride_m + kb * p.sa_stride_k];
+        const float sbf = __bfloat162float(__float2bfloat16_rn(s));
+        int ex = 0;
+        if (sbf != 0.0f && isfinite(sbf)) frexpf(fabsf(sbf), &ex);
+        byte = static_cast<uint32_t>(min(max(ex + 127, 0), 255));
+      }
+      p.sfa_atoms[(static_cast<int64_t>(b) * kb_count + kb) * 128 + j] = byte * 0x01010101u;
+    }
+  }
+  if (tid == 0) p.blk_info[b] = make_int4(expert, eff, cls, 0);
+
+  // Last CTA: stable per-class ordering of the blocks (block order = expert order
+  // in the contiguous layout, which keeps blocks of one expert adjacent).
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(&p.ctrl[kCtrlTicket], 1) == p.nblk - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int per = (p.nblk + blockDim.x - 1) / blockDim.x;
+  const int lo = min(p.nblk, tid * per), hi = min(p.nblk, lo + per);
+  int cnt[kNumClasses] = {0, 0, 0, 0};
+  for (int i = lo; i < hi; ++i) {
+    const int c = __ldcg(&p.blk_info[i].z);
+    cnt[c]++;
+  }
+#pragma unroll
+  for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][tid + 1] = cnt[c];
+  if (tid == 0) {
+#pragma unroll
+    for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][0] = 0;
+  }
+  __syncthreads();
+  if (tid < kNumClasses) {
+    int run = 0;
+    for (int t = 0; t <= static_cast<int>(blockDim.x); ++t) {
+      const int v = s_cls_count[tid][t];
+      s_cls_count[tid][t] = run;
+      run += v;
+    }
+    p.ctrl[kCtrlCount0 + tid] = run;
+  }
+  __syncthreads();
+  int pos[kNumClasses];
+#pragma unroll
+  for (int c = 0; c < kNumClasses; ++c) pos[c] = s_cls_count[c][tid + 1];
+  for (int i = lo; i < hi; ++i) {
+    const int c = __ldcg(&p.blk_info[i].z);
+    p.lists[c * p.nblk + pos[c]++] = i;
+  }
+}
+
+// =====================================================================================
+// Persistent tcgen05 grouped GEMM, weights as the MMA's M side ("swap AB").
+//
+// A work tile is (128-row block of one expert, 128 output columns).  Per K step
+// of 128: the weight tile [128 n x 128 k] arrives through TMA with the
+// 16U4_ALIGN16B type (packed E2M1 in global memory, one byte per element in
+// shared memory, 128-byte swizzle), the two activation planes [ntok x 128] and
+// the two scale atoms through TMA/bulk copies.  One elected thread issues, per
+// 32-wide K slice, tcgen05.mma.kind::mxf8f6f4.block_scale twice (hi and lo
+// planes) into a TMEM accumulator of 128 lanes (n) x ntok columns (rows of D).
+// Four epilogue warps drain TMEM, cast to BF16 and store D[row, n]; rows of the
+// block without a valid id, and blocks without any, are written as zeros.
+//
+// Warp roles: 0 = TMA producer, 1 = MMA issuer (also owns TMEM), 2-3 idle,
+// 4-7 = epilogue.
+// =====================================================================================
+struct GemmArgs {
+  const int4* blk_info;
+  const int* ctrl;
+  const int* list;        // blocks of this kernel's class, in order
+  const int* zero_list;   // all-padding blocks (zero-filled by the narrow kernel only)
+  const void* ids;        // per-row ids (to zero rows without a valid id)
+  int ids_is_64;
+  const uint32_t* sfw_atoms;  // [E][N/128][K/128][128] words
+  const uint32_t* sfa_atoms;  // [nblk][K/128][128] words
+  __nv_bfloat16* d;
+  int64_t d_row_stride;
+  int M, N, K, E, nblk;
+  int count_slot;        // ctrl index of this class's block count
+  int do_zero_blocks;    // 1 for the narrow kernel
+  int* status;
+};
+
+template <int TOK>
+struct GemmSmem {
+  static constexpr int kStages = TOK <= 32 ? 8 : 4;
+  static constexpr int kW = 128 * 128;       // bytes per stage, weight tile
+  static constexpr int kA = TOK * 128;       // bytes per stage, per activation plane
+  static constexpr int kStageBytes = kW + 2 * kA + 1024;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
+};
+
+__device__ __forceinline__ bool row_has_id(const void* ids, int is64, int r, int expert) {
+  return load_id(ids, is64, r) == expert;
+}
+
+template <int TOK>
+__global__ void __launch_bounds__(256, 1)
+    cdg_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                    GemmArgs p) {
+  using L = GemmSmem<TOK>;
+  constexpr int S = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  auto stage_w = [&](int s) { return smem + s * L::kStageBytes; };
+  auto stage_hi = [&](int s) { return smem + s * L::kStageBytes + L::kW; };
+  auto stage_lo = [&](int s) { return smem + s * L::kStageBytes + L::kW + L::kA; };
+  auto stage_sfw = [&](int s) { return smem + s * L::kStageBytes + L::kW + 2 * L::kA; };
+  auto stage_sfa = [&](int s) { return smem + s * L::kStageBytes + L::kW + 2 * L::kA + 512; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t kTmemCols = 512;
+  constexpr uint32_t kSfwCol = 256, kSfaCol = 260;
+
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_a);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 128);
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int n_tiles = p.N / 128;
+  const int k_steps = p.K / 128;
+  const int count = __ldcg(&p.ctrl[p.count_slot]);
+  const int zero_count = p.do_zero_blocks ? __ldcg(&p.ctrl[kCtrlCount0 + kClassZero]) : 0;
+  const int reg_tiles = count * n_tiles;
+  const int total_tiles = reg_tiles + zero_count * n_tiles;
+  const int64_t plane_rows = static_cast<int64_t>(p.nblk) * 128;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < reg_tiles && ok; t += gridDim.x) {
+        const int blk = p.list[t / n_tiles];
+        const int nt = t % n_tiles;
+        const int4 info = p.blk_info[blk];
+        const int expert = info.x;
+        const int ntok = (info.y + 15) & ~15;
+        const int wrow = expert * p.N + nt * 128;
+        const uint32_t a_bytes = static_cast<uint32_t>(ntok) * 128u;
+        for (int kb = 0; kb < k_steps; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], 128u * 64u + 2u * a_bytes + 1024u);
+          tma_load_2d(stage_w(stage), &tmap_w, &full[stage], kb * 128, wrow);
+          for (int r = 0; r < ntok; r += 16) {
+            tma_load_2d(stage_hi(stage) + r * 128, &tmap_a, &full[stage], kb * 128, blk * 128 + r);
+            tma_load_2d(stage_lo(stage) + r * 128, &tmap_a, &full[stage], kb * 128,
+                        static_cast<int32_t>(plane_rows + blk * 128 + r));
+          }
+          const uint32_t* sfw = p.sfw_atoms + ((static_cast<int64_t>(expert) * n_tiles + nt) * k_steps + kb) * 128;
+          const uint32_t* sfa = p.sfa_atoms + (static_cast<int64_t>(blk) * k_steps + kb) * 128;
+          bulk_load(stage_sfw(stage), sfw, 512, &full[stage]);
+          bulk_load(stage_sfa(stage), sfa, 512, &full[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: wait (bounded) until the copies of every stage issued so far landed.
+      if (!ok) {
+        for (int s = 0; s < S; ++s) mbar_wait(&full[s], 0, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < reg_tiles && ok; t += gridDim.x, ++local) {
+        const int blk = p.list[t / n_tiles];
+        const int4 info = p.blk_info[blk];
+        const uint32_t ntok = static_cast<uint32_t>((info.y + 15) & ~15);
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 128;
+        for (int kb = 0; kb < k_steps; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status)) { ok = false; break; }
+          tc_fence_after();
+          tc_cp_sf_atom(tmem_base + kSfwCol, smem_desc_sf(smem_u32(stage_sfw(stage))));
+          tc_cp_sf_atom(tmem_base + kSfaCol, smem_desc_sf(smem_u32(stage_sfa(stage))));
+          const uint32_t w_addr = smem_u32(stage_w(stage));
+          const uint32_t hi_addr = smem_u32(stage_hi(stage));
+          const uint32_t lo_addr = smem_u32(stage_lo(stage));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t idesc = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 128, ntok, k, k);
+            const uint64_t wd = smem_desc_sw128(w_addr + k * 32);
+            tc_mma_mxf8f6f4(d_tmem, wd, smem_desc_sw128(hi_addr + k * 32), idesc, (kb | k) != 0,
+                            tmem_base + kSfwCol, tmem_base + kSfaCol);
+            tc_mma_mxf8f6f4(d_tmem, wd, smem_desc_sw128(lo_addr + k * 32), idesc, 1u, tmem_base + kSfwCol,
+                            tmem_base + kSfaCol);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int tid = threadIdx.x - 128;
+    int local = 0;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const bool regular = t < reg_tiles;
+      const int blk = regular ? p.list[t / n_tiles] : p.zero_list[(t - reg_tiles) / n_tiles];
+      const int nt = t % n_tiles;
+      const int row0 = blk * 128;
+      int zero_from = 0;
+      if (regular) {
+        const int4 info = p.blk_info[blk];
+        const int expert = info.x;
+        const int ntok = (info.y + 15) & ~15;
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
+        if (!mbar_wait(&tfull[acc], acc_phase, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const int n = nt * 128 + q * 32 + lane;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 128;
+        for (int j0 = 0; j0 < ntok; j0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(taddr + j0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int r = row0 + j0 + j;
+            if (r < p.M) {
+              const float x = row_has_id(p.ids, p.ids_is_64, r, expert) ? __uint_as_float(v[j]) : 0.0f;
+              p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        zero_from = ntok;
+      }
+      // zero rows [zero_from, 128) of this block, columns [nt*128, nt*128+128), 16 B per store
+      const int rows = min(128, p.M - row0) - zero_from;
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      for (int c = tid; c < rows * 16; c += 128) {
+        const int r = row0 + zero_from + (c >> 4);
+        *reinterpret_cast<uint4*>(p.d + r * p.d_row_stride + nt * 128 + (c & 15) * 8) = z;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// =====================================================================================
+// Generic exact path (SIMT).  One CTA per (128-row block, 256 output columns).
+// Follows the reference's arithmetic element by element: activations as
+// bf16(bf16(a) * bf16(sa)) for e4m3, unchanged for BF16/FP32 (gemm.py:31-52);
+// weights as bf16(e2m1 * scale) with scale 2^(e-127) or a float (gemm.py:147-187);
+// FP32 accumulation; result cast to D's dtype.  Rows whose id is outside [0, E)
+// are written as zeros.  Used for the blocks the tensor-core kernel does not take
+// (rows of several experts in one 128-row block) and for inputs outside its
+// envelope (K or N not multiples of 128, BF16/FP32 activations, float weight
+// scales, FP32 output).
+// =====================================================================================
+struct GenericArgs {
+  const void* a;
+  int a_dtype;  // CDG_DTYPE_*
+  int64_t a_row_stride;
+  const float* sa;
+  int64_t sa_stride_m, sa_stride_k;
+  int sa_block_k;
+  const uint8_t* b;  // packed [E][N][K/2]
+  int64_t b_stride_e, b_stride_n;
+  const void* sb;
+  int sb_dtype;   // CDG_DTYPE_UE8M0 or CDG_DTYPE_F32
+  int sb_atoms;   // 1: sb is in the 128x4 atom layout of cdg_sf_atom_kernel (UE8M0 only)
+  int64_t sb_stride_e, sb_stride_n;
+  const void* ids;
+  int ids_is_64;
+  void* d;
+  int d_dtype;  // CDG_DTYPE_BF16 or CDG_DTYPE_F32
+  int64_t d_row_stride;
+  int M, N, K, E;
+  int nblk;
+  const int* list;   // nullptr: every block; else the listed blocks
+  const int* count;  // number of listed blocks (device)
+};
+
+__constant__ float kE2M1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                                -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
+__device__ __forceinline__ float ue8m0_to_f32(uint32_t e) {
+  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
+__global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
+  extern __shared__ float s_row[];  // K floats: the dequantised activation row
+  const int n_chunks = (p.N + 255) / 256;
+  const int units = (p.list ? __ldcg(p.count) : p.nblk) * n_chunks;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int bi = u / n_chunks;
+    const int blk = p.list ? p.list[bi] : bi;
+    const int n = (u % n_chunks) * 256 + threadIdx.x;
+    for (int r = blk * 128; r < min(p.M, blk * 128 + 128); ++r) {
+      const int64_t id = load_id(p.ids, p.ids_is_64, r);
+      const bool valid = id >= 0 && id < p.E;
+      if (valid) {
+        __syncthreads();
+        for (int k = threadIdx.x; k < p.K; k += blockDim.x) {
+          float x;
+          if (p.a_dtype == CDG_DTYPE_E4M3) {
+            const uint8_t raw = static_cast<const uint8_t*>(p.a)[r * p.a_row_stride + k];
+            const float s = bf16r(p.sa[r * p.sa_stride_m + (k / p.sa_block_k) * p.sa_stride_k]);
+            x = bf16r(e4m3_to_f32(raw) * s);
+          } else if (p.a_dtype == CDG_DTYPE_BF16) {
+            x = __bfloat162float(static_cast<const __nv_bfloat16*>(p.a)[r * p.a_row_stride + k]);
+          } else {
+            x = static_cast<const float*>(p.a)[r * p.a_row_stride + k];
+          }
+          s_row[k] = x;
+        }
+        __syncthreads();
+      }
+      if (n >= p.N) continue;
+      float acc = 0.0f;
+      if (valid) {
+        const uint8_t* wrow = p.b + id * p.b_stride_e + static_cast<int64_t>(n) * p.b_stride_n;
+        for (int k = 0; k < p.K; k += 2) {
+          const uint8_t byte = __ldg(wrow + (k >> 1));
+          float sc;
+          const int kb = k >> 5;
+          if (p.sb_atoms) {
+            const int64_t atom = (id * ((p.N + 127) / 128) + n / 128) * ((p.K / 32 + 3) / 4) + (kb >> 2);
+            const uint8_t e = static_cast<const uint8_t*>(p.sb)[atom * 512 + (n & 31) * 16 + ((n & 127) >> 5) * 4 +
+                                                                (kb & 3)];
+            sc = ue8m0_to_f32(e);
+          } else if (p.sb_dtype == CDG_DTYPE_UE8M0) {
+            const uint8_t e = static_cast<const uint8_t*>(p.sb)[id * p.sb_stride_e + n * p.sb_stride_n + kb];
+            sc = ue8m0_to_f32(e);
+          } else {
+            sc = static_cast<const float*>(p.sb)[id * p.sb_stride_e + n * p.sb_stride_n + kb];
+          }
+          acc = fmaf(s_row[k], bf16r(kE2M1[byte & 15] * sc), acc);
+          if (k + 1 < p.K) acc = fmaf(s_row[k + 1], bf16r(kE2M1[byte >> 4] * sc), acc);
+        }
+      }
+      if (p.d_dtype == CDG_DTYPE_BF16)
+        static_cast<__nv_bfloat16*>(p.d)[r * p.d_row_stride + n] = __float2bfloat16_rn(acc);
+      else
+        static_cast<float*>(p.d)[r * p.d_row_stride + n] = acc;
+    }
+  }
+}
+
+}  // namespace cdg

@@ -1,0 +1,191 @@
+// consumer_deep_gemm._C: the PyTorch binding of libcdg_b200.so.
+//
+// Mirrors the reference's pybind module (csrc/bindings.cpp:133-148): the same
+// tuple arguments, the same shape/dtype checks (csrc/bindings.cpp:50-101), but
+// every call ends in the C ABI of cdg_b200.h on the current CUDA stream with a
+// workspace taken from PyTorch's caching allocator.  There is no host fallback:
+// CPU tensors are rejected.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <string>
+
+#include "cdg_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+void check_status(int st, const char* what) {
+  if (st == CDG_OK) return;
+  const std::string msg = std::string(what) + ": " + cdg_status_string(st);
+  if (st == CDG_ERR_INVALID_ARGUMENT || st == CDG_ERR_ALIGNMENT) throw std::invalid_argument(msg);
+  if (st == CDG_ERR_UNSUPPORTED) throw std::runtime_error(msg + " (not implemented by this build)");
+  TORCH_CHECK(false, msg);
+}
+
+int32_t dtype_code(const torch::Tensor& t) {
+  switch (t.scalar_type()) {
+    case torch::kFloat8_e4m3fn: return CDG_DTYPE_E4M3;
+    case torch::kBFloat16: return CDG_DTYPE_BF16;
+    case torch::kFloat32: return CDG_DTYPE_F32;
+    case torch::kUInt8: return CDG_DTYPE_UE8M0;
+    case torch::kInt32: return CDG_DTYPE_I32;
+    case torch::kInt64: return CDG_DTYPE_I64;
+    default: return 0;
+  }
+}
+
+void check_cuda(const torch::Tensor& t, const char* name, const torch::Device& dev) {
+  TORCH_CHECK(t.defined(), name, " must be defined");
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor (this build has no CPU path)");
+  TORCH_CHECK(t.device() == dev, name, " must be on ", dev, ", got ", t.device());
+}
+
+// Fill the C-ABI argument block from already-normalised tensors (see gemm.py).
+//   a: [M,K] e4m3/bf16/f32;  sa: [M,C] f32 or undefined;  b: [E,N,K/2] uint8
+//   sfb: [E,N,K/32] uint8/f32 or int32 atoms [E,N/128,K/128,128];  d: [M,N] bf16/f32
+cdg_gemm_args make_args(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
+                        const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids,
+                        int64_t flags) {
+  const auto dev = a.device();
+  check_cuda(a, "a", dev);
+  check_cuda(b, "b", dev);
+  check_cuda(sfb, "b scale", dev);
+  check_cuda(d, "d", dev);
+  TORCH_CHECK_VALUE(a.dim() == 2, "a must be [M, K], got dim ", a.dim());
+  TORCH_CHECK_VALUE(b.dim() == 3, "b must be [G, N, K/2] packed FP4, got dim ", b.dim());
+  TORCH_CHECK_VALUE(d.dim() == 2, "d must be [M, N], got dim ", d.dim());
+  TORCH_CHECK_VALUE(a.stride(1) == 1 && d.stride(1) == 1, "a and d must have unit stride along their last dim");
+  TORCH_CHECK_VALUE(b.is_contiguous(), "b must be contiguous");
+  TORCH_CHECK_VALUE(b.scalar_type() == torch::kUInt8 || b.scalar_type() == torch::kInt8,
+                    "b must be int8/uint8 packed FP4, got ", b.scalar_type());
+  const int64_t M = a.size(0), K = a.size(1), E = b.size(0), N = b.size(1);
+  TORCH_CHECK_VALUE(b.size(2) * 2 == K, "b packed K must equal a K/2, got b.size(2)=", b.size(2), " and a K=", K);
+  TORCH_CHECK_VALUE(d.size(0) == M, "d M must match a M");
+  TORCH_CHECK_VALUE(d.size(1) == N, "d N must match b N");
+
+  cdg_gemm_args g{};
+  g.a = a.data_ptr();
+  g.a_dtype = dtype_code(a);
+  TORCH_CHECK_VALUE(g.a_dtype == CDG_DTYPE_E4M3 || g.a_dtype == CDG_DTYPE_BF16 || g.a_dtype == CDG_DTYPE_F32,
+                    "a must be FP8/BF16/FP32, got ", a.scalar_type());
+  g.a_row_stride = a.stride(0);
+  if (g.a_dtype == CDG_DTYPE_E4M3) {
+    TORCH_CHECK_VALUE(sa.has_value(), "FP8 a needs its scale");
+    const auto& s = *sa;
+    check_cuda(s, "a scale", dev);
+    TORCH_CHECK_VALUE(s.scalar_type() == torch::kFloat32 && s.dim() == 2 && s.size(0) == M,
+                      "a scale must be float32 [M, K/128]");
+    g.sa = s.data_ptr<float>();
+    g.sa_stride_m = s.stride(0);
+    g.sa_stride_k = s.stride(1);
+    g.sa_cols = static_cast<int32_t>(s.size(1));
+  }
+  g.b = b.data_ptr();
+  g.b_stride_e = b.stride(0);
+  g.b_stride_n = b.stride(1);
+  g.sfb = sfb.data_ptr();
+  if (sfb.scalar_type() == torch::kInt32) {
+    const int64_t NT = (N + 127) / 128, KT = (K / 32 + 3) / 4;
+    TORCH_CHECK_VALUE(sfb.is_contiguous() && sfb.dim() == 4 && sfb.size(0) == E && sfb.size(1) == NT &&
+                          sfb.size(2) == KT && sfb.size(3) == 128,
+                      "transformed b scale must be int32 [E, N/128, K/128, 128]");
+    g.sfb_dtype = CDG_DTYPE_UE8M0;
+    g.sfb_layout = CDG_SF_ATOMS;
+  } else {
+    TORCH_CHECK_VALUE(sfb.dim() == 3 && sfb.size(0) == E && sfb.size(1) == N && sfb.stride(2) == 1,
+                      "b scale must be [G, N, K/32] with unit last stride");
+    TORCH_CHECK_VALUE(sfb.size(2) == (K + 31) / 32, "b scale must have ceil(K/32) columns");
+    g.sfb_dtype = dtype_code(sfb);
+    TORCH_CHECK_VALUE(g.sfb_dtype == CDG_DTYPE_UE8M0 || g.sfb_dtype == CDG_DTYPE_F32,
+                      "b scale must be uint8 (UE8M0) or float32, got ", sfb.scalar_type());
+    g.sfb_layout = CDG_SF_ROW_MAJOR;
+    g.sfb_stride_e = sfb.stride(0);
+    g.sfb_stride_n = sfb.stride(1);
+  }
+  if (ids.has_value()) {
+    const auto& t = *ids;
+    check_cuda(t, "m_indices", dev);
+    TORCH_CHECK_VALUE(t.dim() == 1 && t.is_contiguous(), "m_indices must be a contiguous 1D tensor");
+    g.m_indices_dtype = dtype_code(t);
+    TORCH_CHECK_VALUE(g.m_indices_dtype == CDG_DTYPE_I32 || g.m_indices_dtype == CDG_DTYPE_I64,
+                      "m_indices must be int32/int64, got ", t.scalar_type());
+    TORCH_CHECK_VALUE(t.numel() == M || t.numel() == E, "m_indices length must be M or G, got ", t.numel(), ", M=", M,
+                      ", G=", E);
+    g.m_indices = t.data_ptr();
+    g.m_indices_len = t.numel();
+    g.index_form = t.numel() == M ? CDG_INDEX_PER_ROW : CDG_INDEX_PSUM;
+  } else {
+    TORCH_CHECK_VALUE(E == 1, "m_indices is required when b has multiple groups");
+    g.index_form = CDG_INDEX_NONE;
+  }
+  g.d = d.data_ptr();
+  g.d_dtype = dtype_code(d);
+  TORCH_CHECK_VALUE(g.d_dtype == CDG_DTYPE_BF16 || g.d_dtype == CDG_DTYPE_F32, "d must be BF16/FP32, got ",
+                    d.scalar_type());
+  g.d_row_stride = d.stride(0);
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.E = E;
+  g.flags = static_cast<int32_t>(flags);
+  return g;
+}
+
+void grouped_gemm(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
+                  const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids,
+                  int64_t flags) {
+  const cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, flags);
+  const c10::cuda::CUDAGuard guard(a.device());
+  const size_t ws_bytes = cdg_grouped_fp8_fp4_workspace_bytes(&g);
+  TORCH_CHECK(ws_bytes > 0, "invalid GEMM arguments");
+  // 1024 bytes of slack so the workspace can start on a 1024-byte boundary.
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes + 1024)}, a.options().dtype(torch::kUInt8));
+  auto* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 1023) & ~uintptr_t(1023));
+  const auto stream = at::cuda::getCurrentCUDAStream(a.get_device()).stream();
+  check_status(cdg_grouped_fp8_fp4_gemm_nt_contiguous(&g, base, ws_bytes, reinterpret_cast<cdg_stream_t>(stream)),
+               "m_grouped_fp8_fp4_gemm_nt_contiguous");
+}
+
+int64_t can_implement(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
+                      const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids) {
+  const cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, 0);
+  return cdg_can_implement(&g);
+}
+
+torch::Tensor transform_sf_atoms(const torch::Tensor& sf) {
+  TORCH_CHECK(sf.is_cuda(), "scale must be a CUDA tensor");
+  TORCH_CHECK_VALUE(sf.dim() == 3 && sf.scalar_type() == torch::kUInt8 && sf.stride(2) == 1,
+                    "scale must be uint8 [E, N, K/32] with unit last stride");
+  const c10::cuda::CUDAGuard guard(sf.device());
+  const int64_t E = sf.size(0), N = sf.size(1), KB = sf.size(2);
+  auto out = torch::empty({E, (N + 127) / 128, (KB + 3) / 4, 128}, sf.options().dtype(torch::kInt32));
+  const auto stream = at::cuda::getCurrentCUDAStream(sf.get_device()).stream();
+  check_status(cdg_transform_sf(sf.data_ptr<uint8_t>(), sf.stride(0), sf.stride(1), E, N, KB,
+                                reinterpret_cast<uint8_t*>(out.data_ptr()), reinterpret_cast<cdg_stream_t>(stream)),
+               "transform_sf_into_required_layout");
+  return out;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200 grouped FP8 x MXFP4 MoE GEMM (binding of libcdg_b200.so)";
+  m.def("is_available", []() { return true; });
+  m.def("build_info", []() { return std::string(cdg_build_info()); });
+  m.def("mk_alignment_for_contiguous_layout", []() { return cdg_mk_alignment_for_contiguous_layout(); });
+  m.def("grouped_gemm", &grouped_gemm, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
+        py::arg("m_indices"), py::arg("flags") = 0);
+  m.def("can_implement", &can_implement, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
+        py::arg("m_indices"));
+  m.def("transform_sf_atoms", &transform_sf_atoms, py::arg("sf"));
+  m.def(
+      "set_profile_events",
+      [](uint64_t start, uint64_t stop) {
+        check_status(cdg_set_profile_events(reinterpret_cast<void*>(start), reinterpret_cast<void*>(stop)),
+                     "set_profile_events");
+      },
+      py::arg("start"), py::arg("stop"));
+}

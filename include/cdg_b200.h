@@ -1,0 +1,169 @@
+/*
+ * cdg_b200.h -- C ABI of the B200 (sm_100a) grouped FP8 x MXFP4 MoE GEMM.
+ *
+ * One library, libcdg_b200.so, with plain pointers, sizes and a CUDA stream in
+ * every signature (no torch types), so that any FFI (ctypes, cgo, JNI, a C++
+ * host) can drive it.  The Python package consumer_deep_gemm binds it through
+ * its torch extension; tests bind it through ctypes.
+ *
+ * Each entry point names the reference interface (lmxxf/Consumer-DeepGEMM) it
+ * replaces.
+ *
+ * Conventions
+ *   - All device pointers belong to the caller; nothing here allocates device
+ *     memory.  Temporaries live in a caller-provided workspace whose size is
+ *     given by cdg_grouped_fp8_fp4_workspace_bytes().
+ *   - Work is enqueued on `stream` and nothing blocks the host; no device to host
+ *     copy happens on the GEMM path.
+ *   - Return values are cdg_status codes.  Input errors are detected on the host
+ *     before anything is launched.  Errors seen on the device (a pipeline wait
+ *     that timed out) are recorded in the workspace status word, readable with
+ *     cdg_read_device_status().
+ */
+#ifndef CDG_B200_H_
+#define CDG_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* cdg_stream_t; /* == cudaStream_t */
+
+#define CDG_ABI_VERSION 1
+
+typedef enum cdg_status {
+  CDG_OK = 0,
+  CDG_ERR_INVALID_ARGUMENT = 1, /* shapes, strides or dtypes that the operation cannot mean */
+  CDG_ERR_UNSUPPORTED = 2,      /* a well-formed request this build does not implement */
+  CDG_ERR_ALIGNMENT = 3,        /* a pointer or stride breaks an alignment rule */
+  CDG_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
+  CDG_ERR_CUDA = 5,             /* a CUDA runtime call failed (see cudaGetLastError) */
+  CDG_ERR_DEVICE_TIMEOUT = 6,   /* a kernel gave up waiting on its pipeline */
+  CDG_ERR_NO_SM100 = 7          /* the current device is not compute capability 10.x */
+} cdg_status;
+
+typedef enum cdg_dtype {
+  CDG_DTYPE_E4M3 = 1,   /* float8 e4m3fn */
+  CDG_DTYPE_BF16 = 2,   /* bfloat16 */
+  CDG_DTYPE_F32 = 3,    /* float32 */
+  CDG_DTYPE_UE8M0 = 4,  /* unsigned 8-bit power-of-two scale, value 2^(b-127) */
+  CDG_DTYPE_I32 = 5,    /* int32 group ids */
+  CDG_DTYPE_I64 = 6     /* int64 group ids */
+} cdg_dtype;
+
+/* How the weight scales `sfb` are laid out. */
+typedef enum cdg_sf_layout {
+  CDG_SF_ROW_MAJOR = 0, /* [E, N, K/32] with the given strides (bytes or floats) */
+  CDG_SF_ATOMS = 1      /* output of cdg_transform_sf(): 512-byte 128x4 atoms, dense */
+} cdg_sf_layout;
+
+/* What `m_indices` holds. */
+typedef enum cdg_index_form {
+  CDG_INDEX_PER_ROW = 0, /* one group id per row of A, -1 (any id outside [0,E)) = no group */
+  CDG_INDEX_PSUM = 1,    /* E cumulative row ends: group g owns rows [end[g-1], end[g]) */
+  CDG_INDEX_NONE = 2     /* no ids: E must be 1 and every row belongs to group 0 */
+} cdg_index_form;
+
+/*
+ * Arguments of D[r, :] = deq(A[r, :]) . deq(B[g(r)])^T for every row r whose
+ * group g(r) is in [0, E); every other row of D is written as 0.
+ *
+ *   a          [M, K] activations, a_dtype E4M3 (with sa) or BF16/F32 (sa ignored)
+ *   sa         [M, sa_cols] float32 activation scales, one per row and K block of
+ *              K / sa_cols elements (1x128 blocks: sa_cols = K/128)
+ *   b          [E, N, K/2] packed E2M1 weights, low nibble = even k
+ *   sfb        weight scales, UE8M0 bytes or float32, per 32 K (see sfb_layout)
+ *   m_indices  group ids, int32 or int64 (see index_form)
+ *   d          [M, N] output, BF16 or F32
+ * Strides are in elements of the tensor's own dtype (bytes for b).
+ */
+typedef struct cdg_gemm_args {
+  const void* a;
+  int32_t a_dtype;
+  int64_t a_row_stride;
+  const float* sa;
+  int64_t sa_stride_m, sa_stride_k;
+  int32_t sa_cols;
+  const void* b;
+  int64_t b_stride_e, b_stride_n;
+  const void* sfb;
+  int32_t sfb_dtype;
+  int32_t sfb_layout;
+  int64_t sfb_stride_e, sfb_stride_n;
+  const void* m_indices;
+  int32_t m_indices_dtype;
+  int32_t index_form;
+  int64_t m_indices_len;
+  void* d;
+  int32_t d_dtype;
+  int64_t d_row_stride;
+  int64_t M, N, K, E;
+  int32_t flags; /* CDG_FLAG_* */
+} cdg_gemm_args;
+
+#define CDG_FLAG_FORCE_GENERIC 1 /* run the exact SIMT path even where the tensor-core path applies */
+
+/* Grouped FP8 x MXFP4 GEMM, contiguous layout.
+ * Replaces m_grouped_fp8_fp4_gemm_nt_contiguous (consumer_deep_gemm/gemm.py:467-470),
+ * its native stub (csrc/bindings.cpp:103-129) and launcher
+ * (csrc/cutlass_mxfp8_mxfp4_probe.cu:444-614, exported at :660-673). */
+int cdg_grouped_fp8_fp4_gemm_nt_contiguous(const cdg_gemm_args* args, void* workspace, size_t workspace_bytes,
+                                           cdg_stream_t stream);
+
+/* Workspace the call above needs for these arguments (0 on invalid arguments).
+ * Replaces the launcher's process-global workspace and segment buffers
+ * (csrc/cutlass_mxfp8_mxfp4_probe.cu:391-438). */
+size_t cdg_grouped_fp8_fp4_workspace_bytes(const cdg_gemm_args* args);
+
+/* 1 if the tensor-core kernel takes these arguments, 0 if the exact SIMT path
+ * will run them, -1 if they are invalid.
+ * Replaces cutlass_mxfp8_mxfp4_can_implement_probe (csrc/cutlass_mxfp8_mxfp4_probe.cu:158-188,633-639). */
+int cdg_can_implement(const cdg_gemm_args* args);
+
+/* Weight scale factors [E, N, KB] (KB = K/32, UE8M0 bytes, strides in bytes) ->
+ * dense 512-byte atoms [E][ceil(N/128)][ceil(KB/4)][128 rows x 4], padding 127.
+ * Run once at weight-load time; pass the result with CDG_SF_ATOMS.
+ * Replaces transform_sf_into_required_layout (consumer_deep_gemm/layout.py:6-19),
+ * reorder_scale_kernel (csrc/cutlass_mxfp8_mxfp4_probe.cu:258-295) and the
+ * lazily filled per-expert cache (:340-385). */
+int cdg_transform_sf(const uint8_t* sf, int64_t stride_e, int64_t stride_n, int64_t E, int64_t N, int64_t KB,
+                     uint8_t* out, cdg_stream_t stream);
+
+/* Bytes cdg_transform_sf() writes.
+ * Replaces cutlass_mxfp8_mxfp4_scale_layout_sizes (csrc/cutlass_mxfp8_mxfp4_probe.cu:641-657). */
+size_t cdg_sf_atoms_bytes(int64_t E, int64_t N, int64_t KB);
+
+/* Reads (synchronising `stream`) the device status word a GEMM call left in its
+ * workspace; returns CDG_OK or CDG_ERR_DEVICE_TIMEOUT.  No reference counterpart:
+ * the reference reports device failures only as a launch result
+ * (csrc/cutlass_mxfp8_mxfp4_probe.cu:598-613). */
+int cdg_read_device_status(const void* workspace, cdg_stream_t stream);
+
+/* Static description of the build ("sm_100a; ...").
+ * Replaces native.build_info (consumer_deep_gemm/native.py:26-39) and the SM120
+ * probes (csrc/cutlass_sm120_probe.cu:6-22). */
+const char* cdg_build_info(void);
+
+/* Row alignment of each group in the contiguous layout (128).
+ * Replaces get_mk_alignment_for_contiguous_layout (consumer_deep_gemm/layout.py:32-34). */
+int cdg_mk_alignment_for_contiguous_layout(void);
+
+/* Profiling hook: when both are non-NULL, every later GEMM call made from this
+ * host thread records `start_event` on its stream just before the tensor-core
+ * GEMM kernels and `stop_event` just after them (cudaEvent_t handles created
+ * with timing enabled).  NULL, NULL switches it off.  Replaces the reference's
+ * CDG_PROFILE wrappers (consumer_deep_gemm/__init__.py:62-114), which
+ * synchronised the whole device around every call. */
+int cdg_set_profile_events(void* start_event, void* stop_event);
+
+/* Human-readable name of a cdg_status value. */
+const char* cdg_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CDG_B200_H_ */

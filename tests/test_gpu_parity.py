@@ -1,0 +1,155 @@
+"""GPU parity of the grouped FP8 x MXFP4 GEMM, driven through the C ABI (ctypes).
+
+Every golden case (outputs of the reference itself, see tests/golden/make_golden.py)
+is run twice: through the default dispatch (tensor-core kernel where the inputs
+fit it, exact SIMT kernel for the rest) and with the SIMT kernel forced.
+
+Tolerances, against the reference's BF16 output over the routed rows:
+  * max |out - ref| / max |ref|      <= 1e-2   (TOL_NORMWISE)
+  * per-row ||out - ref|| / ||ref||  <= 2e-3   (TOL_ROW_L2)
+  * rows without a valid group id are exactly zero, bit for bit;
+  * known-answer cases (small integers) are exact.
+At the benchmark sizes (configs c1-c3) the full outputs are checked on sampled
+rows against the CPU oracle, plus bit-identical repeat runs and exact zero rows.
+"""
+
+import pytest
+import torch
+
+import cabi
+from conftest import GEMM_CASES, load_gemm_case
+from metrics import TOL_NORMWISE, TOL_ROW_L2, errors
+from oracle import cdg_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _invalid_rows(c) -> torch.Tensor:
+    m = c["a"].shape[0]
+    ids = c["m_indices"]
+    e = c["b"].shape[0]
+    if ids is None:
+        return torch.zeros(m, dtype=torch.bool)
+    ids = ids.to(torch.int64)
+    if ids.numel() == m:
+        return (ids < 0) | (ids >= e)
+    covered = torch.zeros(m, dtype=torch.bool)
+    start = 0
+    for end in ids.tolist():
+        covered[start:max(start, min(end, m))] = True
+        start = end
+    return ~covered
+
+
+def _run_case(c, flags):
+    a = c["a"].to(DEV)
+    sa = c["sa"].to(DEV).float() if (c["sa"] is not None and a.dtype == torch.float8_e4m3fn) else None
+    if a.dtype == torch.float8_e4m3fn and sa is None:
+        sa = torch.ones(a.shape[0], (a.shape[1] + 127) // 128, device=DEV)
+    b = c["b"].to(DEV)
+    sb = c["sb"].to(DEV)
+    ids = c["m_indices"].to(DEV) if c["m_indices"] is not None else None
+    d = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    cabi.gemm(a, sa, b, sb, d, ids, flags=flags)
+    torch.cuda.synchronize()
+    return d.cpu()
+
+
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_FORCE_GENERIC], ids=["dispatch", "simt"])
+@pytest.mark.parametrize("name", GEMM_CASES)
+def test_golden_case(name, flags):
+    c = load_gemm_case(name)
+    out = _run_case(c, flags)
+    ref = c["d"]
+    assert not torch.isnan(out).any(), "rows left unwritten"
+    bad = _invalid_rows(c)
+    if bool(bad.any()):
+        assert bool((out[bad].float() == 0).all()) and bool((torch.signbit(out[bad].float()) == 0).all())
+    if name.startswith("kat_"):
+        assert torch.equal(out, ref)
+        return
+    nw, rl2 = errors(out, ref, ~bad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+
+
+def test_sf_transform_bit_exact_vs_oracle():
+    g = torch.Generator().manual_seed(3)
+    for e, n, kb in [(3, 256, 16), (2, 384, 128), (1, 128, 4)]:
+        sb = torch.randint(0, 256, (e, n, kb), dtype=torch.uint8, generator=g)
+        out = cabi.transform_sf(sb.to(DEV)).cpu().numpy()
+        ref = [oracle.reorder_scale_to_sf_atom(sb[i].numpy()) for i in range(e)]
+        import numpy as np
+        assert np.array_equal(out, np.concatenate(ref)), (e, n, kb)
+
+
+def test_atoms_and_row_major_scales_agree():
+    """The GEMM given pre-transformed scale atoms equals the GEMM given row-major scales, bit for bit."""
+    c = load_gemm_case("c0")
+    a, sa = c["a"].to(DEV), c["sa"].to(DEV)
+    b, sb, ids = c["b"].to(DEV), c["sb"].to(DEV), c["m_indices"].to(DEV)
+    d1 = torch.empty(c["d"].shape, dtype=torch.bfloat16, device=DEV)
+    d2 = torch.empty_like(d1)
+    cabi.gemm(a, sa, b, sb, d1, ids)
+    atoms = cabi.transform_sf(sb)
+    cabi.gemm(a, sa, b, atoms, d2, ids, sb_atoms=True)
+    torch.cuda.synchronize()
+    assert torch.equal(d1.view(torch.int16), d2.view(torch.int16))
+
+
+def test_padding_rows_with_garbage_do_not_leak():
+    """vLLM reuses workspaces: padding rows of A can hold any bytes (NaN included)."""
+    c = load_gemm_case("c0")
+    a = c["a"].clone()
+    ids = c["m_indices"]
+    pad = ids < 0
+    g = torch.Generator().manual_seed(11)
+    a.view(torch.uint8)[pad] = torch.randint(0, 256, (int(pad.sum()), a.shape[1]), dtype=torch.uint8, generator=g)
+    sa = c["sa"].clone()
+    sa[pad] = float("nan")
+    c2 = dict(c, a=a, sa=sa)
+    out = _run_case(c2, 0)
+    assert bool((out[pad].float() == 0).all())
+    nw, rl2 = errors(out, c["d"], ~pad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2
+
+
+def _sampled_oracle(inp, rows):
+    """Oracle output for a subset of rows of a full-size problem."""
+    ids = inp["m_indices"].cpu()[rows]
+    experts = torch.unique(ids[ids >= 0])
+    remap = torch.full((inp["b"].shape[0],), -1, dtype=torch.int32)
+    remap[experts] = torch.arange(experts.numel(), dtype=torch.int32)
+    sub_ids = torch.where(ids >= 0, remap[ids.clamp(min=0).long()], ids)
+    a = inp["a"][rows.to(inp["a"].device)].cpu()
+    sa = inp["sa"][rows.to(inp["sa"].device)].cpu()
+    b = inp["b"][experts.to(inp["b"].device)].cpu()
+    sb = inp["sb"][experts.to(inp["sb"].device)].cpu()
+    d = torch.empty(rows.numel(), b.shape[1], dtype=torch.bfloat16)
+    oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (b, sb), d, sub_ids)
+    return d
+
+
+@pytest.mark.parametrize("cfg", ["c1", "c2", "c3"])
+def test_benchmark_config_sampled_rows(cfg):
+    from consumer_deep_gemm import synthetic
+
+    inp = synthetic.make_inputs(synthetic.CONFIGS[cfg], device=DEV, seed=0)
+    a, sa, b, sb, ids = inp["a"], inp["sa"], inp["b"], inp["sb"], inp["m_indices"]
+    m, n = a.shape[0], b.shape[1]
+    d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cabi.gemm(a, sa, b, sb, d, ids)
+    d2 = torch.empty_like(d)
+    cabi.gemm(a, sa, b, sb, d2, ids)
+    torch.cuda.synchronize()
+    assert torch.equal(d.view(torch.int16), d2.view(torch.int16)), "repeat run differs"
+    pad = ids < 0
+    assert bool((d[pad] == 0).all()), "padding rows must be zero"
+    assert not bool(torch.isnan(d).any())
+    valid = (~pad).nonzero().flatten().cpu()
+    g = torch.Generator().manual_seed(7)
+    rows = valid[torch.randperm(valid.numel(), generator=g)[:24]].sort().values
+    ref = _sampled_oracle(inp, rows)
+    nw, rl2 = errors(d[rows.to(DEV)], ref)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (cfg, nw, rl2)
