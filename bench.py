@@ -172,7 +172,7 @@ def run_reference(args, cfg_name):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -210,6 +210,7 @@ def main():
         cdg.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (b, atoms), d, ids, recipe_a=(1, 128), recipe_b=(1, 32))
 
     stream = torch.cuda.current_stream(dev)
+    sampler = ClockSampler(local)
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize(dev)
@@ -220,7 +221,6 @@ def main():
         s.record(stream)
         e.record(stream)
     torch.cuda.synchronize(dev)
-    sampler = ClockSampler(local)
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -234,7 +234,6 @@ def main():
     torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
-    clocks = sampler.stop()
     ms = t0.elapsed_time(t1) / args.steps
     kernel_ms = statistics.fmean(s.elapsed_time(e) for s, e in kev)
 
@@ -262,6 +261,7 @@ def main():
     t1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = t0.elapsed_time(t1) / args.steps
+    clocks = sampler.stop()
     h2d = h_a.numel() * h_a.element_size() + h_sa.numel() * 4 + h_ids.numel() * h_ids.element_size()
     d2h = h_d.numel() * h_d.element_size()
 
