@@ -406,8 +406,54 @@ const char* cdg_status_string(int status) {
     case CDG_ERR_CUDA: return "CUDA runtime error";
     case CDG_ERR_DEVICE_TIMEOUT: return "device pipeline wait timed out";
     case CDG_ERR_NO_SM100: return "device is not compute capability 10.x (B200)";
+    case CDG_ERR_SCRATCH_TOO_SMALL:
+      return "problem needs more workspace than the 64 MiB static scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// No-allocation entry point: the workspace is a file-scope device array instead of caller memory.
+// ---------------------------------------------------------------------------------------------
+namespace cdg {
+namespace {
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CDG_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on each device, looked up once with that device current.
+// In host code the array's name only stands in for the symbol; kernels need this address.
+struct NoallocScratch {
+  uint8_t* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+
+const NoallocScratch& noalloc_scratch(int dev) {
+  static NoallocScratch slots[kMaxDevices];
+  static std::once_flag flags[kMaxDevices];
+  std::call_once(flags[dev], [dev] {
+    void* p = nullptr;
+    slots[dev].err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    slots[dev].ptr = static_cast<uint8_t*>(p);
+  });
+  return slots[dev];
+}
+
+}  // namespace
+}  // namespace cdg
+
+extern "C" int cdg_grouped_fp8_fp4_gemm_nt_contiguous_noalloc(const cdg_gemm_args* args, cdg_stream_t stream) {
+  const int st = cdg::validate(args);
+  if (st != CDG_OK) return st;
+  // The shared workspace layout wants 1024-byte alignment; the array is 256-aligned.
+  const size_t need = cdg::layout_for(args).total + 1024;
+  if (need > CDG_NOALLOC_SCRATCH_BYTES) return CDG_ERR_SCRATCH_TOO_SMALL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= cdg::kMaxDevices) return CDG_ERR_CUDA;
+  const cdg::NoallocScratch& sc = cdg::noalloc_scratch(dev);
+  if (sc.err != cudaSuccess || sc.ptr == nullptr) return CDG_ERR_CUDA;
+  const uintptr_t base = (reinterpret_cast<uintptr_t>(sc.ptr) + 1023) & ~uintptr_t(1023);
+  const size_t usable = CDG_NOALLOC_SCRATCH_BYTES - (base - reinterpret_cast<uintptr_t>(sc.ptr));
+  return cdg::run(args, reinterpret_cast<void*>(base), usable, reinterpret_cast<cudaStream_t>(stream));
+}

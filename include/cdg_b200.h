@@ -42,7 +42,8 @@ typedef enum cdg_status {
   CDG_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
   CDG_ERR_CUDA = 5,             /* a CUDA runtime call failed (see cudaGetLastError) */
   CDG_ERR_DEVICE_TIMEOUT = 6,   /* a kernel gave up waiting on its pipeline */
-  CDG_ERR_NO_SM100 = 7          /* the current device is not compute capability 10.x */
+  CDG_ERR_NO_SM100 = 7,         /* the current device is not compute capability 10.x */
+  CDG_ERR_SCRATCH_TOO_SMALL = 8 /* the problem needs more than the static scratch of the no-allocation entry */
 } cdg_status;
 
 typedef enum cdg_dtype {
@@ -158,6 +159,32 @@ int cdg_mk_alignment_for_contiguous_layout(void);
  * CDG_PROFILE wrappers (consumer_deep_gemm/__init__.py:62-114), which
  * synchronised the whole device around every call. */
 int cdg_set_profile_events(void* start_event, void* stop_event);
+
+/* Size of the static device scratch that the no-allocation entry point below uses (64 MiB). */
+#define CDG_NOALLOC_SCRATCH_BYTES (64u << 20)
+
+/* Grouped FP8 x MXFP4 GEMM that allocates nothing.  No counterpart in the
+ * reference: it exists for callers that cannot hand this library a workspace,
+ * because they cannot allocate device memory at call time -- for example a
+ * service whose device memory is entirely reserved up front by another caching
+ * allocator (a raw allocation then fails for lack of free memory), or a
+ * foreign host (JNI, cgo, a plugin) with no path to the owning allocator.
+ *
+ * Same arguments and results as cdg_grouped_fp8_fp4_gemm_nt_contiguous, but the
+ * temporaries live in a file-scope device array of CDG_NOALLOC_SCRATCH_BYTES,
+ * which every GPU that loads the library keeps until the process exits.
+ *   - Problems whose workspace (cdg_grouped_fp8_fp4_workspace_bytes + 1 KiB of
+ *     alignment) exceeds that size are refused with CDG_ERR_SCRATCH_TOO_SMALL
+ *     before anything is launched.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls share one array, which keeps the previous call's contents (the
+ *     call clears the words that must start at zero).  Calls that overlap on the
+ *     GPU -- on different streams, or from several host threads -- race on it
+ *     and must be serialised by the caller.
+ *   - No cudaMalloc, cudaFree or allocating library routine is called. */
+int cdg_grouped_fp8_fp4_gemm_nt_contiguous_noalloc(const cdg_gemm_args* args, cdg_stream_t stream);
 
 /* Human-readable name of a cdg_status value. */
 const char* cdg_status_string(int status);
