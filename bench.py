@@ -37,7 +37,8 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 METRIC = "grouped FP8×FP4 MoE GEMM TFLOPS and HBM GB/s vs roofline at 1/2/4/8 B200"
-LAUNCHES_PER_CALL = 4  # cdg_prep_kernel, cdg_gemm_kernel<32>, cdg_gemm_kernel<128>, cdg_generic_kernel
+# cdg_prep_kernel, cdg_gemm_kernel<16>, cdg_gemm_kernel<32>, cdg_gemm_kernel<128>, cdg_generic_kernel
+LAUNCHES_PER_CALL = 5
 
 
 def algorithmic(inp):

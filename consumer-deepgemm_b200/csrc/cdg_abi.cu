@@ -53,6 +53,9 @@ const DeviceInfo& device_info(int dev) {
     if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return;
     if (cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return;
     if (d.cc_major == 10) {
+      if (cudaFuncSetAttribute(cdg_gemm_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               GemmSmem<16>::kBytes) != cudaSuccess)
+        return;
       if (cudaFuncSetAttribute(cdg_gemm_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                GemmSmem<32>::kBytes) != cudaSuccess)
         return;
@@ -150,7 +153,23 @@ int launch_sf_atoms(const uint8_t* sf, int64_t se, int64_t sn, int64_t E, int64_
   return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
 }
 
-int make_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap* tw, CUtensorMap* ta) {
+// Activation planes: 3-D view [2 planes][nblk*128 rows][K] e4m3 bytes; one box brings
+// `tok` rows of both planes, landing as [hi tok rows][lo tok rows] in shared memory.
+int make_plane_tmap(EncodeTiledFn enc, const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, uint32_t tok,
+                    CUtensorMap* ta) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(nblk * 128), 2};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(nblk * 128 * g->K)};
+  cuuint32_t box[3] = {128, tok, 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, hilo, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? CDG_OK
+             : CDG_ERR_CUDA;
+}
+
+int make_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap* tw, CUtensorMap* ta16,
+               CUtensorMap* ta32, CUtensorMap* ta128) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return CDG_ERR_CUDA;
   {
@@ -164,18 +183,10 @@ int make_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap*
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return CDG_ERR_CUDA;
   }
-  {
-    // Activation planes: [2 * nblk * 128 rows, K] e4m3 bytes, 16-row boxes.
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(2 * nblk * 128)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->K)};
-    cuuint32_t box[2] = {128, 16};
-    cuuint32_t estr[2] = {1, 1};
-    if (enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, hilo, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return CDG_ERR_CUDA;
-  }
-  return CDG_OK;
+  int st = make_plane_tmap(enc, g, hilo, nblk, 16, ta16);
+  if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 32, ta32);
+  if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 128, ta128);
+  return st;
 }
 
 int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -212,6 +223,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   }
   int* lists = reinterpret_cast<int*>(ws + wl.lists);
   int4* blk_info = reinterpret_cast<int4*>(ws + wl.blk_info);
+  uint4* blk_mask = reinterpret_cast<uint4*>(ws + wl.blk_mask);
 
   GenericArgs ga{};
   ga.a = g->a;
@@ -261,7 +273,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     sfw = out;
   }
   uint8_t* hilo = ws + wl.hilo;
-  uint32_t* sfa_atoms = reinterpret_cast<uint32_t*>(ws + wl.sfa_atoms);
+  int32_t* row_exp = reinterpret_cast<int32_t*>(ws + wl.row_exp);
 
   PrepArgs pa{};
   pa.a = static_cast<const uint8_t*>(g->a);
@@ -275,27 +287,28 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.E = static_cast<int>(g->E);
   pa.nblk = static_cast<int>(nblk);
   pa.hilo = hilo;
-  pa.sfa_atoms = sfa_atoms;
+  pa.row_exp = row_exp;
   pa.blk_info = blk_info;
+  pa.blk_mask = blk_mask;
   pa.ctrl = ctrl;
   pa.lists = lists;
+  const dim3 prep_grid(static_cast<unsigned>(nblk), static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
   if (ids_dtype == CDG_DTYPE_I64)
-    cdg_prep_kernel<int64_t><<<static_cast<unsigned>(nblk), 256, 0, stream>>>(pa);
+    cdg_prep_kernel<int64_t><<<prep_grid, 256, 0, stream>>>(pa);
   else
-    cdg_prep_kernel<int32_t><<<static_cast<unsigned>(nblk), 256, 0, stream>>>(pa);
+    cdg_prep_kernel<int32_t><<<prep_grid, 256, 0, stream>>>(pa);
   if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
 
-  CUtensorMap tw, ta;
-  st = make_tmaps(g, hilo, nblk, &tw, &ta);
+  CUtensorMap tw, ta16, ta32, ta128;
+  st = make_tmaps(g, hilo, nblk, &tw, &ta16, &ta32, &ta128);
   if (st != CDG_OK) return st;
 
   GemmArgs ka{};
   ka.blk_info = blk_info;
+  ka.blk_mask = blk_mask;
   ka.ctrl = ctrl;
-  ka.ids = ids;
-  ka.ids_is_64 = ids_dtype == CDG_DTYPE_I64;
   ka.sfw_atoms = sfw;
-  ka.sfa_atoms = sfa_atoms;
+  ka.row_exp = row_exp;
   ka.d = static_cast<__nv_bfloat16*>(g->d);
   ka.d_row_stride = g->d_row_stride;
   ka.M = static_cast<int>(g->M);
@@ -307,17 +320,22 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.zero_list = lists + kClassZero * nblk;
 
   if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
-  // Narrow blocks (decode-like) and all-padding blocks.
+  // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.
+  ka.list = lists + kClassTiny * nblk;
+  ka.count_slot = kCtrlCount0 + kClassTiny;
+  ka.do_zero_blocks = 1;
+  cdg_gemm_kernel<16><<<di.sm_count, 256, GemmSmem<16>::kBytes, stream>>>(tw, ta16, ka);
+  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  // Narrow blocks (17 to 32 routed rows).
+  ka.do_zero_blocks = 0;
   ka.list = lists + kClassNarrow * nblk;
   ka.count_slot = kCtrlCount0 + kClassNarrow;
-  ka.do_zero_blocks = 1;
-  cdg_gemm_kernel<32><<<di.sm_count, 256, GemmSmem<32>::kBytes, stream>>>(tw, ta, ka);
+  cdg_gemm_kernel<32><<<di.sm_count, 256, GemmSmem<32>::kBytes, stream>>>(tw, ta32, ka);
   if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
   // Wide blocks (prefill-like).
   ka.list = lists + kClassWide * nblk;
   ka.count_slot = kCtrlCount0 + kClassWide;
-  ka.do_zero_blocks = 0;
-  cdg_gemm_kernel<128><<<di.sm_count, 256, GemmSmem<128>::kBytes, stream>>>(tw, ta, ka);
+  cdg_gemm_kernel<128><<<di.sm_count, 256, GemmSmem<128>::kBytes, stream>>>(tw, ta128, ka);
   if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
   if (t_prof_stop && cudaEventRecord(t_prof_stop, stream) != cudaSuccess) return CDG_ERR_CUDA;
   // Blocks holding rows of several experts: exact SIMT path over the listed blocks.

@@ -78,11 +78,12 @@ __global__ void cdg_psum_rows_kernel(const IdT* __restrict__ ends, int G, int M,
 //
 // For a row r with valid expert id and a K block kb (128 wide) the reference's
 // activation value is x = bf16(bf16(a[r,k]) * bf16(sa[r,kb])) (gemm.py:44-48).
-// With s = bf16(sa[r,kb]) = m * 2^E, m in [0.5, 1), every x / 2^E is a BF16
-// number below 448 in magnitude, so it splits exactly into hi = e4m3(x/2^E) and
-// lo = e4m3(x/2^E - hi) whenever |x/2^E| >= 2^-2 (elements below that lose at most
-// 2^-10 * 2^E).  The tensor core then multiplies both planes with the weights
-// under the common UE8M0 scale E+127: sum_k (hi+lo) * 2^E * w = sum_k x * w.
+// Let 2^E bound |bf16(sa[r,kb])| over all K blocks of the row (E = frexp exponent
+// of the largest).  Every x / 2^E is then a BF16 number below 448 in magnitude,
+// which splits exactly into hi = e4m3(x/2^E) and lo = e4m3(x/2^E - hi) whenever
+// |x/2^E| >= 2^-2 (smaller elements lose at most 2^-10 * 2^E).  The tensor core
+// multiplies both planes with the weights (activation scale factor 1), and the
+// epilogue multiplies the FP32 sum by 2^E, exactly: sum_k (hi+lo) * w * 2^E = sum_k x * w.
 // =====================================================================================
 struct PrepArgs {
   const uint8_t* a;  // e4m3 [M, K]
@@ -93,8 +94,9 @@ struct PrepArgs {
   int M, K, E;
   int nblk;
   uint8_t* hilo;           // [2][nblk*128][K]
-  uint32_t* sfa_atoms;     // [nblk][K/128][128] words
-  int4* blk_info;          // [nblk]
+  int32_t* row_exp;        // [nblk*128] exponent E of each routed row's activation planes
+  int4* blk_info;          // [nblk] {expert (-1 none, -2 several), rows spanned, class, 0}
+  uint4* blk_mask;         // [nblk] bit r set when row r of the block has the block's expert
   int* ctrl;               // control words (zeroed by the host before launch)
   int* lists;              // [kNumClasses][nblk]
 };
@@ -114,10 +116,19 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   return __half2float(__half(h));
 }
 
+// Grid: (nblk, ceil(K / kPrepK)).  CTA (b, y) converts K columns [y*kPrepK, (y+1)*kPrepK)
+// of block b; CTA (b, 0) also publishes the block's plan, and the last of those
+// orders the blocks of each class into lists.
+constexpr int kPrepK = 1024;
+
 template <typename IdT>
 __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ int s_min_id, s_max_id, s_max_row;
   __shared__ int s_last;
+  __shared__ int s_id[128];
+  __shared__ uint32_t s_mask[4];
+  __shared__ float s_scale[128][kPrepK / 128];
+  __shared__ int s_exp[128];
   __shared__ int s_cls_count[kNumClasses][257];
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
@@ -126,16 +137,20 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     s_max_id = -1;
     s_max_row = -1;
   }
+  if (tid < 4) s_mask[tid] = 0u;
   __syncthreads();
   if (tid < 128) {
     const int r = b * 128 + tid;
+    int id = -1;
     if (r < p.M) {
-      const int64_t id = load_id(p.ids, sizeof(IdT) == 8, r);
-      if (id >= 0 && id < p.E) {
-        atomicMin(&s_min_id, static_cast<int>(id));
-        atomicMax(&s_max_id, static_cast<int>(id));
-        atomicMax(&s_max_row, tid);
-      }
+      const int64_t v = load_id(p.ids, sizeof(IdT) == 8, r);
+      id = (v >= 0 && v < p.E) ? static_cast<int>(v) : -1;
+    }
+    s_id[tid] = id;
+    if (id >= 0) {
+      atomicMin(&s_min_id, id);
+      atomicMax(&s_max_id, id);
+      atomicMax(&s_max_row, tid);
     }
   }
   __syncthreads();
@@ -148,84 +163,94 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     cls = kClassIrregular;
     expert = -2;
   } else {
-    cls = eff <= kNarrowTok ? kClassNarrow : kClassWide;
+    cls = eff <= kTinyTok ? kClassTiny : eff <= kNarrowTok ? kClassNarrow : kClassWide;
     expert = s_min_id;
   }
 
-  if (cls == kClassNarrow || cls == kClassWide) {
+  if (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide) {
     const int ntok = (eff + 15) & ~15;
     const int K = p.K;
     const int kb_count = K / 128;
+    const int kb0 = blockIdx.y * (kPrepK / 128);
+    const int kbn = min(kPrepK / 128, kb_count - kb0);
     const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
-    // (1) activation planes, 16 bytes per step
-    const int chunks_per_row = K / 16;
-    const int total = ntok * chunks_per_row;
-    for (int c = tid; c < total; c += blockDim.x) {
-      const int rr = c / chunks_per_row;
-      const int kc = c - rr * chunks_per_row;
+    if (tid < 128 && s_id[tid] == expert) atomicOr(&s_mask[tid >> 5], 1u << (tid & 31));
+    // (1) per routed row: the exponent E with |bf16(sa[r,kb])| < 2^E for every K block of
+    //     the row (frexp exponent of the largest scale); and the BF16-rounded scales of
+    //     this CTA's K blocks.
+    if (tid < ntok) {
+      int emax = 0;
+      const int r = b * 128 + tid;
+      if (s_id[tid] == expert) {
+        float smax = 0.0f;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          const float sbf = __bfloat162float(__float2bfloat16_rn(p.sa[r * p.sa_stride_m + kb * p.sa_stride_k]));
+          if (isfinite(sbf)) smax = fmaxf(smax, fabsf(sbf));
+        }
+        if (smax > 0.0f) frexpf(smax, &emax);
+      }
+      s_exp[tid] = emax;
+      if (blockIdx.y == 0) p.row_exp[r] = emax;
+    }
+    for (int it = tid; it < ntok * kbn; it += blockDim.x) {
+      const int rr = it / kbn;
+      const int kl = it - rr * kbn;
       const int r = b * 128 + rr;
+      s_scale[rr][kl] = s_id[rr] == expert
+          ? __bfloat162float(__float2bfloat16_rn(p.sa[r * p.sa_stride_m + (kb0 + kl) * p.sa_stride_k]))
+          : 0.0f;
+    }
+    __syncthreads();
+    // (2) activation planes, one 16-byte chunk per item; consecutive threads read
+    //     consecutive chunks of a row (coalesced).  Rows without the block's id are zeros.
+    const int chunks = kbn * 8;
+    for (int it = tid; it < ntok * chunks; it += blockDim.x) {
+      const int rr = it / chunks;
+      const int c = it - rr * chunks;
+      const int kl = c >> 3;
+      const int r = b * 128 + rr;
+      const int64_t col = static_cast<int64_t>(kb0) * 128 + c * 16;
       uint4 hi4 = make_uint4(0, 0, 0, 0), lo4 = make_uint4(0, 0, 0, 0);
-      bool valid = false;
-      if (r < p.M) valid = load_id(p.ids, sizeof(IdT) == 8, r) == expert;
-      if (valid) {
-        const int kb = (kc * 16) / 128;
-        const float s = p.sa[r * p.sa_stride_m + kb * p.sa_stride_k];
-        const float sbf = __bfloat162float(__float2bfloat16_rn(s));
-        int ex = 0;
-        if (sbf != 0.0f && isfinite(sbf)) frexpf(fabsf(sbf), &ex);
-        const float inv = ldexpf(1.0f, -ex);
-        const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + kc * 16);
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(&raw);
+      if (s_id[rr] == expert) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + col);
+        const float sbf = s_scale[rr][kl];
+        const float inv = ldexpf(1.0f, -s_exp[rr]);
+        const uint8_t* sb8 = reinterpret_cast<const uint8_t*>(&raw);
         uint8_t* hb = reinterpret_cast<uint8_t*>(&hi4);
         uint8_t* lb = reinterpret_cast<uint8_t*>(&lo4);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float xf = e4m3_to_f32(src[i]);
-          const float x = __bfloat162float(__float2bfloat16_rn(xf * sbf));
+          const float x = __bfloat162float(__float2bfloat16_rn(e4m3_to_f32(sb8[i]) * sbf));
           const float v = x * inv;
           const uint8_t h = f32_to_e4m3(v);
           hb[i] = h;
           lb[i] = f32_to_e4m3(v - e4m3_to_f32(h));
         }
       }
-      uint8_t* dst = p.hilo + static_cast<int64_t>(r) * K + kc * 16;
+      uint8_t* dst = p.hilo + static_cast<int64_t>(r) * K + col;
       *reinterpret_cast<uint4*>(dst) = hi4;
       *reinterpret_cast<uint4*>(dst + plane) = lo4;
     }
-    // (2) UE8M0 scale atoms of the activation planes (value replicated over the 4 sub-blocks of 32)
-    for (int w = tid; w < kb_count * 128; w += blockDim.x) {
-      const int kb = w >> 7;
-      const int j = w & 127;
-      const int rr = (j & 3) * 32 + (j >> 2);
-      const int r = b * 128 + rr;
-      uint32_t byte = 127u;
-      if (rr < eff && r < p.M && load_id(p.ids, sizeof(IdT) == 8, r) == expert) {
-        const float s = p.sa[r * p.sa_stride_m + kb * p.sa_stride_k];
-        const float sbf = __bfloat162float(__float2bfloat16_rn(s));
-        int ex = 0;
-        if (sbf != 0.0f && isfinite(sbf)) frexpf(fabsf(sbf), &ex);
-        byte = static_cast<uint32_t>(min(max(ex + 127, 0), 255));
-      }
-      p.sfa_atoms[(static_cast<int64_t>(b) * kb_count + kb) * 128 + j] = byte * 0x01010101u;
-    }
   }
-  if (tid == 0) p.blk_info[b] = make_int4(expert, eff, cls, 0);
+  if (blockIdx.y != 0) return;
 
-  // Last CTA: stable per-class ordering of the blocks (block order = expert order
+  // Publish the plan (thread 0 orders its own store before the ticket), then the
+  // last block to arrive orders each class's blocks (block order = expert order
   // in the contiguous layout, which keeps blocks of one expert adjacent).
-  __threadfence();
   __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(&p.ctrl[kCtrlTicket], 1) == p.nblk - 1);
+  if (tid == 0) {
+    p.blk_info[b] = make_int4(expert, eff, cls, 0);
+    p.blk_mask[b] = make_uint4(s_mask[0], s_mask[1], s_mask[2], s_mask[3]);
+    __threadfence();
+    s_last = (atomicAdd(&p.ctrl[kCtrlTicket], 1) == p.nblk - 1);
+  }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const int per = (p.nblk + blockDim.x - 1) / blockDim.x;
   const int lo = min(p.nblk, tid * per), hi = min(p.nblk, lo + per);
-  int cnt[kNumClasses] = {0, 0, 0, 0};
-  for (int i = lo; i < hi; ++i) {
-    const int c = __ldcg(&p.blk_info[i].z);
-    cnt[c]++;
-  }
+  int cnt[kNumClasses] = {};
+  for (int i = lo; i < hi; ++i) cnt[__ldcg(&p.blk_info[i].z)]++;
 #pragma unroll
   for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][tid + 1] = cnt[c];
   if (tid == 0) {
@@ -256,48 +281,50 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
 // Persistent tcgen05 grouped GEMM, weights as the MMA's M side ("swap AB").
 //
 // A work tile is (128-row block of one expert, 128 output columns).  Per K step
-// of 128: the weight tile [128 n x 128 k] arrives through TMA with the
-// 16U4_ALIGN16B type (packed E2M1 in global memory, one byte per element in
-// shared memory, 128-byte swizzle), the two activation planes [ntok x 128] and
-// the two scale atoms through TMA/bulk copies.  One elected thread issues, per
-// 32-wide K slice, tcgen05.mma.kind::mxf8f6f4.block_scale twice (hi and lo
-// planes) into a TMEM accumulator of 128 lanes (n) x ntok columns (rows of D).
-// Four epilogue warps drain TMEM, cast to BF16 and store D[row, n]; rows of the
-// block without a valid id, and blocks without any, are written as zeros.
+// of 128 the producer issues three copies into one pipeline stage: the weight
+// tile [128 n x 128 k] (TMA, 16U4_ALIGN16B type: packed E2M1 in global memory,
+// one byte per element in shared memory, 128-byte swizzle), one 3-D TMA box
+// holding both activation planes [hi TOK rows; lo TOK rows], and the weights'
+// 512-byte scale atom (bulk copy).  The activation scale factor is the constant
+// 1.0 (the planes carry the per-row power of two, applied by the epilogue).  One
+// thread issues tcgen05.cp of the weight atom and, per 32-wide K slice,
+// tcgen05.mma.kind::mxf8f6f4.block_scale: once over the stacked planes
+// (N = 2*TOK) for TOK <= 32, or once per plane (N = ntok) for TOK = 128, into a
+// TMEM accumulator of 128 lanes (n) x tokens.  Each tcgen05 instruction holds
+// the tensor pipe ~45 cycles, so the issue stream per K step (1 cp, 4 or 8 MMAs,
+// 1 commit) is kept minimal.  Four epilogue warps drain TMEM, add the hi and lo parts, cast to
+// BF16 and store D[row, n]; rows of the block without the block's id, and blocks
+// without any, are written as zeros.
 //
 // Warp roles: 0 = TMA producer, 1 = MMA issuer (also owns TMEM), 2-3 idle,
 // 4-7 = epilogue.
 // =====================================================================================
 struct GemmArgs {
   const int4* blk_info;
+  const uint4* blk_mask;
   const int* ctrl;
   const int* list;        // blocks of this kernel's class, in order
-  const int* zero_list;   // all-padding blocks (zero-filled by the narrow kernel only)
-  const void* ids;        // per-row ids (to zero rows without a valid id)
-  int ids_is_64;
+  const int* zero_list;   // all-padding blocks (zero-filled by the kernel with do_zero_blocks)
   const uint32_t* sfw_atoms;  // [E][N/128][K/128][128] words
-  const uint32_t* sfa_atoms;  // [nblk][K/128][128] words
+  const int32_t* row_exp;     // [nblk*128] per-row exponent of the activation planes
   __nv_bfloat16* d;
   int64_t d_row_stride;
   int M, N, K, E, nblk;
   int count_slot;        // ctrl index of this class's block count
-  int do_zero_blocks;    // 1 for the narrow kernel
+  int do_zero_blocks;
   int* status;
 };
 
 template <int TOK>
 struct GemmSmem {
-  static constexpr int kStages = TOK <= 32 ? 8 : 4;
-  static constexpr int kW = 128 * 128;       // bytes per stage, weight tile
-  static constexpr int kA = TOK * 128;       // bytes per stage, per activation plane
-  static constexpr int kStageBytes = kW + 2 * kA + 1024;
-  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kStages = TOK <= 16 ? 10 : TOK <= 32 ? 8 : 4;
+  static constexpr int kW = 128 * 128;                   // weight tile, bytes per stage
+  static constexpr int kA = TOK * 128;                   // one activation plane, bytes per stage
+  static constexpr int kStageBytes = kW + 2 * kA + 1024;  // + weight scale atom (512 B, padded)
+  static constexpr int kOneAtom = kStages * kStageBytes;  // constant activation scale atom (all 127)
+  static constexpr int kBarOffset = kOneAtom + 512;
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
-
-__device__ __forceinline__ bool row_has_id(const void* ids, int is64, int r, int expert) {
-  return load_id(ids, is64, r) == expert;
-}
 
 template <int TOK>
 __global__ void __launch_bounds__(256, 1)
@@ -305,24 +332,38 @@ __global__ void __launch_bounds__(256, 1)
                     GemmArgs p) {
   using L = GemmSmem<TOK>;
   constexpr int S = L::kStages;
+  // TOK <= 32: the two planes are stacked along N ([hi rows; lo rows], N = 2*TOK), so one
+  // MMA per K slice covers both; TOK = 128: one MMA per plane (N = ntok).
+  constexpr bool kStacked = TOK <= 32;
+  constexpr uint32_t kAccCols = 128;  // TMEM columns per accumulator stage
+
+  const int n_tiles = p.N / 128;
+  const int k_steps = p.K / 128;
+  const int count = __ldcg(&p.ctrl[p.count_slot]);
+  const int zero_count = p.do_zero_blocks ? __ldcg(&p.ctrl[kCtrlCount0 + kClassZero]) : 0;
+  const int reg_tiles = count * n_tiles;
+  const int total_tiles = reg_tiles + zero_count * n_tiles;
+  if (total_tiles == 0) return;  // nothing of this class in the call: leave before any set-up
+
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   auto stage_w = [&](int s) { return smem + s * L::kStageBytes; };
-  auto stage_hi = [&](int s) { return smem + s * L::kStageBytes + L::kW; };
-  auto stage_lo = [&](int s) { return smem + s * L::kStageBytes + L::kW + L::kA; };
-  auto stage_sfw = [&](int s) { return smem + s * L::kStageBytes + L::kW + 2 * L::kA; };
-  auto stage_sfa = [&](int s) { return smem + s * L::kStageBytes + L::kW + 2 * L::kA + 512; };
+  auto stage_a = [&](int s) { return smem + s * L::kStageBytes + L::kW; };  // [hi TOK rows][lo TOK rows]
+  auto stage_sf = [&](int s) { return smem + s * L::kStageBytes + L::kW + 2 * L::kA; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + S;
+  uint64_t* full = bars;       // [S] stage landed
+  uint64_t* empty = bars + S;  // [S] stage consumed
   uint64_t* tfull = bars + 2 * S;
-  uint64_t* tempty = bars + 2 * S + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tfull + 4);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kSfwCol = 256, kSfaCol = 260;
+  // Weight scale-factor columns, double-buffered by K-step parity so that the copy
+  // for step kb+1 does not overwrite what the MMAs of step kb still read; the
+  // activation scale factor is the constant 1.0 (byte 127), copied once.
+  constexpr uint32_t kSfwCol = 256, kSfSetCols = 4, kSfaCol = 264;
 
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_w);
@@ -341,18 +382,17 @@ __global__ void __launch_bounds__(256, 1)
     tmem_alloc(tmem_holder, kTmemCols);
     tmem_relinquish();
   }
+  if (warp == 2) {
+    reinterpret_cast<uint32_t*>(smem + L::kOneAtom)[lane] = 0x7F7F7F7Fu;
+    reinterpret_cast<uint32_t*>(smem + L::kOneAtom)[lane + 32] = 0x7F7F7F7Fu;
+    reinterpret_cast<uint32_t*>(smem + L::kOneAtom)[lane + 64] = 0x7F7F7F7Fu;
+    reinterpret_cast<uint32_t*>(smem + L::kOneAtom)[lane + 96] = 0x7F7F7F7Fu;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to tcgen05.cp
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-
-  const int n_tiles = p.N / 128;
-  const int k_steps = p.K / 128;
-  const int count = __ldcg(&p.ctrl[p.count_slot]);
-  const int zero_count = p.do_zero_blocks ? __ldcg(&p.ctrl[kCtrlCount0 + kClassZero]) : 0;
-  const int reg_tiles = count * n_tiles;
-  const int total_tiles = reg_tiles + zero_count * n_tiles;
-  const int64_t plane_rows = static_cast<int64_t>(p.nblk) * 128;
   bool ok = true;
 
   if (warp == 0) {
@@ -363,24 +403,15 @@ __global__ void __launch_bounds__(256, 1)
       for (int t = blockIdx.x; t < reg_tiles && ok; t += gridDim.x) {
         const int blk = p.list[t / n_tiles];
         const int nt = t % n_tiles;
-        const int4 info = p.blk_info[blk];
-        const int expert = info.x;
-        const int ntok = (info.y + 15) & ~15;
+        const int expert = p.blk_info[blk].x;
         const int wrow = expert * p.N + nt * 128;
-        const uint32_t a_bytes = static_cast<uint32_t>(ntok) * 128u;
+        const uint32_t* sfw_tile = p.sfw_atoms + (static_cast<int64_t>(expert) * n_tiles + nt) * k_steps * 128;
         for (int kb = 0; kb < k_steps; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], 128u * 64u + 2u * a_bytes + 1024u);
+          mbar_arrive_expect_tx(&full[stage], 128u * 64u + 2u * L::kA + 512u);
           tma_load_2d(stage_w(stage), &tmap_w, &full[stage], kb * 128, wrow);
-          for (int r = 0; r < ntok; r += 16) {
-            tma_load_2d(stage_hi(stage) + r * 128, &tmap_a, &full[stage], kb * 128, blk * 128 + r);
-            tma_load_2d(stage_lo(stage) + r * 128, &tmap_a, &full[stage], kb * 128,
-                        static_cast<int32_t>(plane_rows + blk * 128 + r));
-          }
-          const uint32_t* sfw = p.sfw_atoms + ((static_cast<int64_t>(expert) * n_tiles + nt) * k_steps + kb) * 128;
-          const uint32_t* sfa = p.sfa_atoms + (static_cast<int64_t>(blk) * k_steps + kb) * 128;
-          bulk_load(stage_sfw(stage), sfw, 512, &full[stage]);
-          bulk_load(stage_sfa(stage), sfa, 512, &full[stage]);
+          tma_load_3d(stage_a(stage), &tmap_a, &full[stage], kb * 128, blk * 128, 0);
+          bulk_load(stage_sf(stage), sfw_tile + kb * 128, 512, &full[stage]);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
@@ -395,31 +426,32 @@ __global__ void __launch_bounds__(256, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
+      const uint32_t sfa_t = tmem_base + kSfaCol;
+      tc_cp_sf_atom(sfa_t, smem_desc_sf(smem_u32(smem + L::kOneAtom)));
       for (int t = blockIdx.x; t < reg_tiles && ok; t += gridDim.x, ++local) {
         const int blk = p.list[t / n_tiles];
-        const int4 info = p.blk_info[blk];
-        const uint32_t ntok = static_cast<uint32_t>((info.y + 15) & ~15);
+        const uint32_t ntok = static_cast<uint32_t>((p.blk_info[blk].y + 15) & ~15);
+        const uint32_t n_mma = kStacked ? 2u * TOK : ntok;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * 128;
+        const uint32_t d_tmem = tmem_base + acc * kAccCols;
         for (int kb = 0; kb < k_steps; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status)) { ok = false; break; }
           tc_fence_after();
-          tc_cp_sf_atom(tmem_base + kSfwCol, smem_desc_sf(smem_u32(stage_sfw(stage))));
-          tc_cp_sf_atom(tmem_base + kSfaCol, smem_desc_sf(smem_u32(stage_sfa(stage))));
+          const uint32_t sfw_t = tmem_base + kSfwCol + (kb & 1) * kSfSetCols;
+          tc_cp_sf_atom(sfw_t, smem_desc_sf(smem_u32(stage_sf(stage))));
           const uint32_t w_addr = smem_u32(stage_w(stage));
-          const uint32_t hi_addr = smem_u32(stage_hi(stage));
-          const uint32_t lo_addr = smem_u32(stage_lo(stage));
+          const uint32_t a_addr = smem_u32(stage_a(stage));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint32_t idesc = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 128, ntok, k, k);
             const uint64_t wd = smem_desc_sw128(w_addr + k * 32);
-            tc_mma_mxf8f6f4(d_tmem, wd, smem_desc_sw128(hi_addr + k * 32), idesc, (kb | k) != 0,
-                            tmem_base + kSfwCol, tmem_base + kSfaCol);
-            tc_mma_mxf8f6f4(d_tmem, wd, smem_desc_sw128(lo_addr + k * 32), idesc, 1u, tmem_base + kSfwCol,
-                            tmem_base + kSfaCol);
+            const uint32_t idesc = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 128, n_mma, k, k);
+            const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
+            tc_mma_mxf8f6f4(d_tmem, wd, smem_desc_sw128(a_addr + k * 32), idesc, accumulate, sfw_t, sfa_t);
+            if (!kStacked)
+              tc_mma_mxf8f6f4(d_tmem, wd, smem_desc_sw128(a_addr + L::kA + k * 32), idesc, 1u, sfw_t, sfa_t);
           }
           tc_commit(&empty[stage]);
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -441,7 +473,7 @@ __global__ void __launch_bounds__(256, 1)
       int zero_from = 0;
       if (regular) {
         const int4 info = p.blk_info[blk];
-        const int expert = info.x;
+        const uint4 mask = p.blk_mask[blk];
         const int ntok = (info.y + 15) & ~15;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -449,16 +481,30 @@ __global__ void __launch_bounds__(256, 1)
         if (!mbar_wait(&tfull[acc], acc_phase, p.status)) { ok = false; break; }
         tc_fence_after();
         const int n = nt * 128 + q * 32 + lane;
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 128;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
         for (int j0 = 0; j0 < ntok; j0 += 16) {
+          // 2^E of the chunk's 16 rows: lane j (mod 16) loads row j's exponent, shuffles share it
+          const int re = min(row0 + j0 + (lane & 15), p.M - 1);
+          const float my_scale = __uint_as_float(static_cast<uint32_t>(min(max(__ldg(p.row_exp + re) + 127, 1), 254)) << 23);
           uint32_t v[16];
           tmem_ld16(taddr + j0, v);
-          tmem_ld_wait();
+          if (kStacked) {
+            uint32_t w[16];
+            tmem_ld16(taddr + TOK + j0, w);  // the lo-plane columns of the same tokens
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+          } else {
+            tmem_ld_wait();
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int r = row0 + j0 + j;
+            const int rb = j0 + j;
+            const uint32_t word = rb < 32 ? mask.x : rb < 64 ? mask.y : rb < 96 ? mask.z : mask.w;
+            const float sc = __shfl_sync(0xffffffffu, my_scale, j);
             if (r < p.M) {
-              const float x = row_has_id(p.ids, p.ids_is_64, r, expert) ? __uint_as_float(v[j]) : 0.0f;
+              const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
               p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
             }
           }

@@ -10,12 +10,14 @@ namespace cdg {
 
 // Classes of 128-row blocks, decided by cdg_prep_kernel.
 enum : int {
-  kClassNarrow = 0,     // one expert, at most kNarrowTok leading rows -> cdg_gemm_kernel<32>
-  kClassWide = 1,       // one expert, more rows                        -> cdg_gemm_kernel<128>
-  kClassZero = 2,       // no row with a valid id                       -> zero fill
-  kClassIrregular = 3,  // rows of two or more experts                  -> cdg_generic_kernel
-  kNumClasses = 4,
+  kClassTiny = 0,       // one expert, rows within the first kTinyTok   -> cdg_gemm_kernel<16>
+  kClassNarrow = 1,     // one expert, rows within the first kNarrowTok -> cdg_gemm_kernel<32>
+  kClassWide = 2,       // one expert, more rows                        -> cdg_gemm_kernel<128>
+  kClassZero = 3,       // no row with a valid id                       -> zero fill (tiny kernel)
+  kClassIrregular = 4,  // rows of two or more experts                  -> cdg_generic_kernel
+  kNumClasses = 5,
 };
+constexpr int kTinyTok = 16;
 constexpr int kNarrowTok = 32;
 
 // Control words at the start of the workspace (int32 slots, zeroed before each call).
@@ -30,7 +32,7 @@ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Workspace regions of one GEMM call.
 struct WorkspaceLayout {
-  size_t ctrl = 0, blk_info = 0, lists = 0, row_ids = 0, sfa_atoms = 0, hilo = 0, sfw_atoms = 0, total = 0;
+  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, row_ids = 0, row_exp = 0, hilo = 0, sfw_atoms = 0, total = 0;
 
   static WorkspaceLayout make(int64_t M, int64_t K, int64_t N, int64_t E, bool fast, bool psum, bool sfw_from_rows) {
     WorkspaceLayout w;
@@ -40,6 +42,8 @@ struct WorkspaceLayout {
     off = align_up(off + kCtrlWords * 4, 1024);
     w.blk_info = off;
     off = align_up(off + static_cast<size_t>(nblk) * 16, 1024);
+    w.blk_mask = off;
+    off = align_up(off + static_cast<size_t>(nblk) * 16, 1024);
     w.lists = off;
     off = align_up(off + static_cast<size_t>(nblk) * 4 * kNumClasses, 1024);
     if (psum) {
@@ -47,8 +51,8 @@ struct WorkspaceLayout {
       off = align_up(off + static_cast<size_t>(M) * 4, 1024);
     }
     if (fast) {
-      w.sfa_atoms = off;
-      off = align_up(off + static_cast<size_t>(nblk) * (K / 128) * 512, 1024);
+      w.row_exp = off;
+      off = align_up(off + static_cast<size_t>(nblk) * 128 * 4, 1024);
       w.hilo = off;
       off = align_up(off + static_cast<size_t>(2) * nblk * 128 * K, 1024);
       if (sfw_from_rows) {

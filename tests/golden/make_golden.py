@@ -153,6 +153,10 @@ def main():
     rand_case("edge_n40_m200", 200, 128, 40, 3, torch.randint(0, 3, (200,), generator=torch.Generator().manual_seed(9)).to(torch.int32))
     rand_case("edge_aligned_3groups", 384, 512, 256, 3, add_ids([2] * 128 + [0] * 128 + [1] * 90 + [-1] * 38), seed=3)
     rand_case("edge_int64_ids", 256, 256, 128, 2, torch.tensor([1] * 128 + [0] * 128, dtype=torch.int64))
+    # one block per size class: 20 rows (narrow), 30 rows (narrow), 7 rows (tiny), 100 rows (wide)
+    sizes = torch.tensor(([1] * 20 + [-1] * 108) + ([0] * 30 + [-1] * 98) + ([2] * 7 + [-1] * 121)
+                         + ([3] * 100 + [-1] * 28), dtype=torch.int32)
+    rand_case("edge_block_classes", 512, 384, 256, 4, sizes, seed=8)
 
     # --- byte-level helpers -----------------------------------------------------------------
     sf = torch.arange(128 * 8, dtype=torch.uint8).reshape(128, 8)
