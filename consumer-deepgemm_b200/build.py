@@ -29,7 +29,8 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB = os.path.join(PKG, "libcdg_b200.so")
 EXT = os.path.join(PKG, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 
-LIB_SOURCES = [os.path.join(CSRC, f) for f in ("cdg_abi.cu", "cdg_kernels.cuh", "cdg_ptx.cuh", "cdg_layout.h")]
+LIB_SOURCES = [os.path.join(CSRC, f)
+               for f in ("cdg_abi.cu", "cdg_moe.cu", "cdg_kernels.cuh", "cdg_ptx.cuh", "cdg_layout.h")]
 LIB_SOURCES.append(os.path.join(INCLUDE, "cdg_b200.h"))
 EXT_SOURCES = [os.path.join(CSRC, "torch_ext.cpp"), os.path.join(INCLUDE, "cdg_b200.h")]
 
@@ -50,7 +51,7 @@ def build_lib(force: bool = False, extra=()) -> str:
     if force or _stale(LIB, LIB_SOURCES):
         _run([NVCC, *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
               "-cudart", "shared", "-Xptxas", "-v", "-I", INCLUDE, "-I", CSRC,
-              "-o", LIB, os.path.join(CSRC, "cdg_abi.cu"), *extra])
+              "-o", LIB, os.path.join(CSRC, "cdg_abi.cu"), os.path.join(CSRC, "cdg_moe.cu"), *extra])
     return LIB
 
 

@@ -1,0 +1,158 @@
+"""Mixture-of-experts layer on the grouped FP8 x MXFP4 GEMM, with expert parallelism.
+
+``MoELayer.forward(x, topk_ids, topk_w)`` computes, for every token t::
+
+    y[t] = sum_j topk_w[t, j] * FC2_e( act( FC1_e( q(x[t]) ) ) ),   e = topk_ids[t, j]
+
+with q = 1x128 e4m3 quantisation (per_block_cast_to_fp8 semantics), FC1/FC2 the
+grouped GEMM of this package (MXFP4 weights, gate = first half of FC1's output),
+and act = 1x128 e4m3 quantisation of silu(gate) * up.  This is the sequence vLLM's
+DeepGemmFP4Experts runs around ``m_grouped_fp8_fp4_gemm_nt_contiguous``
+(vllm/model_executor/layers/fused_moe/experts/deep_gemm_moe.py:485-545).
+
+Expert parallelism: with a process group of N ranks, rank r owns experts
+[r*E/N, (r+1)*E/N).  Each rank quantises its own tokens, exchanges per-expert row
+counts (one small all-to-all and the only host synchronisation), sends every
+routed row to the rank owning its expert (all-to-all of e4m3 rows, scales and
+local expert ids), lays the received rows out per local expert with 128-row
+alignment, runs FC1 -> act -> FC2, and sends the rows back (all-to-all of BF16
+rows) for the weighted top-k sum.  Collectives go through torch.distributed
+(NCCL on GPUs); all compute runs in libcdg_b200.so kernels.
+
+The device steps sit behind a small ``ops`` interface so that the exchange
+logic can also be exercised with CPU implementations (tests do that with the
+gloo backend).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import native
+from .gemm import m_grouped_fp8_fp4_gemm_nt_contiguous
+from .layout import transform_sf_into_required_layout
+
+ALIGN = 128
+
+
+class NativeOps:
+    """Device kernels of libcdg_b200.so through the torch binding."""
+
+    def __init__(self):
+        self.C = native.require()
+
+    def quant(self, x):
+        return self.C.quant_fp8_rows(x)
+
+    def count(self, topk_ids, num_experts):
+        return self.C.ep_count(topk_ids, num_experts)
+
+    def pack(self, xq, xs, topk_ids, num_experts, ranks, send_off, rows):
+        return self.C.ep_pack(xq, xs, topk_ids, num_experts, ranks, send_off, rows)
+
+    def permute(self, rq, rs, re, local_experts, expert_off, m_pad):
+        return self.C.ep_permute(rq, rs, re, local_experts, expert_off, m_pad)
+
+    def gemm(self, a, sa, w, w_sf, m_indices):
+        d = torch.empty(a.shape[0], w.shape[1], dtype=torch.bfloat16, device=a.device)
+        m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices)
+        return d
+
+    def act(self, h, m_indices):
+        return self.C.silu_mul_quant(h, m_indices)
+
+    def unpermute(self, y, perm_pos):
+        return self.C.ep_unpermute(y, perm_pos)
+
+    def combine(self, rows, send_index, topk_w):
+        return self.C.ep_combine(rows, send_index, topk_w)
+
+
+def _all_to_all(out, inp, out_splits, in_splits, group):
+    import torch.distributed as dist
+
+    dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits, group=group)
+    return out
+
+
+class MoELayer:
+    """An MoE layer whose experts are sharded over the ranks of ``group``.
+
+    w1: packed e2m1 [E_local, 2*I, H/2] (gate rows first), w1_scale UE8M0 [E_local, 2*I, H/32];
+    w2: packed e2m1 [E_local, H, I/2], w2_scale UE8M0 [E_local, H, I/32].
+    ``num_experts`` is the global E; E_local = E / world size.
+    """
+
+    def __init__(self, w1, w1_scale, w2, w2_scale, num_experts: int, group=None, ops=None):
+        self.ops = ops or NativeOps()
+        self.group = group
+        if group is not None:
+            import torch.distributed as dist
+
+            self.world = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        if num_experts % self.world:
+            raise ValueError("the number of experts must divide evenly over the ranks")
+        self.num_experts = num_experts
+        self.local_experts = num_experts // self.world
+        if w1.shape[0] != self.local_experts or w2.shape[0] != self.local_experts:
+            raise ValueError("w1/w2 must hold this rank's experts")
+        self.w1, self.w2 = w1.view(torch.uint8), w2.view(torch.uint8)
+        # weight scale layout prepared once (the weight-load hook)
+        self.w1_sf = transform_sf_into_required_layout(w1_scale) if w1.is_cuda else w1_scale
+        self.w2_sf = transform_sf_into_required_layout(w2_scale) if w2.is_cuda else w2_scale
+        self.hidden = w2.shape[1]
+        self.inter = w1.shape[1] // 2
+
+    def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor) -> torch.Tensor:
+        ops, world, E, E_loc = self.ops, self.world, self.num_experts, self.local_experts
+        dev = x.device
+        topk_ids = topk_ids.contiguous()
+        topk_w = topk_w.to(torch.float32).contiguous()
+        xq, xs = ops.quant(x)
+        counts = ops.count(topk_ids, E)                                  # [E] rows per global expert
+        if world > 1:
+            recv_counts = _all_to_all(torch.empty_like(counts), counts, None, None, self.group)
+        else:
+            recv_counts = counts
+        # the one host synchronisation of the layer: split sizes and the local layout
+        send_mat = counts.view(world, E_loc).to("cpu", torch.int64)
+        recv_mat = recv_counts.view(world, E_loc).to("cpu", torch.int64)
+        send_splits = send_mat.sum(1).tolist()
+        recv_splits = recv_mat.sum(1).tolist()
+        per_expert = recv_mat.sum(0)
+        aligned = (per_expert + ALIGN - 1) // ALIGN * ALIGN
+        m_pad = int(aligned.sum())
+        expert_off = (torch.cumsum(aligned, 0) - aligned).to(dev)
+        send_off = torch.tensor([0] + send_splits[:-1], dtype=torch.int64).cumsum(0).to(dev)
+
+        sq, ss, se, send_index = ops.pack(xq, xs, topk_ids, E, world, send_off, sum(send_splits))
+        R = sum(recv_splits)
+        if world > 1:
+            # e4m3 rows travel as bytes (not every backend has a float8 type)
+            rq = _all_to_all(torch.empty(R, sq.shape[1], dtype=torch.uint8, device=dev), sq.view(torch.uint8),
+                             recv_splits, send_splits, self.group).view(sq.dtype)
+            rs = _all_to_all(torch.empty(R, ss.shape[1], dtype=ss.dtype, device=dev), ss, recv_splits, send_splits,
+                             self.group)
+            re = _all_to_all(torch.empty(R, dtype=se.dtype, device=dev), se, recv_splits, send_splits, self.group)
+        else:
+            rq, rs, re = sq, ss, se
+
+        if m_pad > 0:
+            a, sa, m_indices, perm_pos = ops.permute(rq, rs, re, E_loc, expert_off, m_pad)
+            h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices)
+            aq, asc = ops.act(h, m_indices)
+            y2 = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
+            back = ops.unpermute(y2, perm_pos)
+        else:
+            back = torch.empty(0, self.hidden, dtype=torch.bfloat16, device=dev)
+        if world > 1:
+            out_rows = _all_to_all(torch.empty(sq.shape[0], self.hidden, dtype=back.dtype, device=dev), back,
+                                   send_splits, recv_splits, self.group)
+        else:
+            out_rows = back
+        return ops.combine(out_rows, send_index, topk_w)
+
+    __call__ = forward

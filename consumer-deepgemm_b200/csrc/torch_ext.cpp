@@ -10,6 +10,7 @@
 #include <torch/extension.h>
 
 #include <string>
+#include <vector>
 
 #include "cdg_b200.h"
 
@@ -169,6 +170,118 @@ torch::Tensor transform_sf_atoms(const torch::Tensor& sf) {
   return out;
 }
 
+cdg_stream_t cur_stream(const torch::Tensor& t) {
+  return reinterpret_cast<cdg_stream_t>(at::cuda::getCurrentCUDAStream(t.get_device()).stream());
+}
+
+// ------------------------------------------------------------------ MoE layer / expert parallelism
+std::vector<torch::Tensor> quant_fp8_rows(const torch::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [M, K] tensor with unit last stride");
+  TORCH_CHECK_VALUE(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat32, "x must be BF16/FP32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t M = x.size(0), K = x.size(1);
+  auto q = torch::empty({M, K}, x.options().dtype(torch::kFloat8_e4m3fn));
+  auto s = torch::empty({M, K / 128}, x.options().dtype(torch::kFloat32));
+  check_status(cdg_quant_fp8_rows(x.data_ptr(), dtype_code(x), x.stride(0), M, K,
+                                  reinterpret_cast<uint8_t*>(q.data_ptr()), K, s.data_ptr<float>(), K / 128, 1,
+                                  cur_stream(x)),
+               "quant_fp8_rows");
+  return {q, s};
+}
+
+std::vector<torch::Tensor> silu_mul_quant(const torch::Tensor& h, const c10::optional<torch::Tensor>& m_indices) {
+  TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.stride(1) == 1 && h.scalar_type() == torch::kBFloat16,
+              "h must be a CUDA BF16 [M, 2I] tensor with unit last stride");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int64_t M = h.size(0), I = h.size(1) / 2;
+  auto q = torch::empty({M, I}, h.options().dtype(torch::kFloat8_e4m3fn));
+  auto s = torch::empty({M, I / 128}, h.options().dtype(torch::kFloat32));
+  const int32_t* ids = nullptr;
+  if (m_indices.has_value()) {
+    TORCH_CHECK(m_indices->scalar_type() == torch::kInt32 && m_indices->numel() == M, "m_indices must be int32 [M]");
+    ids = m_indices->data_ptr<int32_t>();
+  }
+  check_status(cdg_silu_mul_quant_fp8(h.data_ptr(), h.stride(0), M, I, ids, reinterpret_cast<uint8_t*>(q.data_ptr()),
+                                      I, s.data_ptr<float>(), I / 128, 1, cur_stream(h)),
+               "silu_mul_quant");
+  return {q, s};
+}
+
+torch::Tensor ep_count(const torch::Tensor& ids, int64_t E) {
+  TORCH_CHECK(ids.is_cuda() && ids.is_contiguous(), "topk ids must be a contiguous CUDA tensor");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  auto cnt = torch::empty({E}, ids.options().dtype(torch::kInt32));
+  check_status(cdg_ep_count(ids.data_ptr(), dtype_code(ids), ids.numel(), E, cnt.data_ptr<int32_t>(), cur_stream(ids)),
+               "ep_count");
+  return cnt;
+}
+
+// Returns (rows e4m3 [R, H], scales [R, H/128], local expert ids [R], send_index [T*topk]).
+std::vector<torch::Tensor> ep_pack(const torch::Tensor& xq, const torch::Tensor& xs, const torch::Tensor& ids,
+                                   int64_t E, int64_t ranks, const torch::Tensor& send_off, int64_t rows) {
+  TORCH_CHECK(xq.is_cuda() && xq.dim() == 2 && xq.is_contiguous(), "xq must be contiguous [T, H]");
+  TORCH_CHECK(xs.is_contiguous() && ids.is_contiguous() && ids.dim() == 2, "xs and topk ids must be contiguous");
+  TORCH_CHECK(send_off.scalar_type() == torch::kInt64 && send_off.numel() == ranks, "send_off must be int64 [ranks]");
+  const c10::cuda::CUDAGuard guard(xq.device());
+  const int64_t T = xq.size(0), H = xq.size(1), topk = ids.size(1);
+  auto out_q = torch::empty({rows, H}, xq.options());
+  auto out_s = torch::empty({rows, H / 128}, xs.options());
+  auto out_e = torch::empty({rows}, ids.options().dtype(torch::kInt32));
+  auto send_index = torch::empty({T * topk}, ids.options().dtype(torch::kInt32));
+  auto fill = torch::empty({ranks}, ids.options().dtype(torch::kInt32));
+  check_status(cdg_ep_pack(reinterpret_cast<const uint8_t*>(xq.data_ptr()), H, xs.data_ptr<float>(), H / 128,
+                           ids.data_ptr(), dtype_code(ids), T, topk, E, ranks, H, send_off.data_ptr<int64_t>(),
+                           fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(out_q.data_ptr()),
+                           out_s.data_ptr<float>(), out_e.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(),
+                           cur_stream(xq)),
+               "ep_pack");
+  return {out_q, out_s, out_e, send_index};
+}
+
+// Returns (A e4m3 [M_pad, H], SA [M_pad, H/128], m_indices [M_pad], perm_pos [R]).
+std::vector<torch::Tensor> ep_permute(const torch::Tensor& rq, const torch::Tensor& rs, const torch::Tensor& re,
+                                      int64_t E_local, const torch::Tensor& expert_off, int64_t M_pad) {
+  TORCH_CHECK(rq.is_cuda() && rq.dim() == 2 && rq.is_contiguous() && rs.is_contiguous() && re.is_contiguous(),
+              "received rows must be contiguous");
+  TORCH_CHECK(expert_off.scalar_type() == torch::kInt64 && expert_off.numel() == E_local, "expert_off: int64 [E]");
+  const c10::cuda::CUDAGuard guard(rq.device());
+  const int64_t R = rq.size(0), H = rq.size(1);
+  auto A = torch::empty({M_pad, H}, rq.options());
+  auto SA = torch::ones({M_pad, H / 128}, rs.options());
+  auto mi = torch::empty({M_pad}, re.options());
+  auto pos = torch::empty({R}, re.options());
+  auto fill = torch::empty({E_local}, re.options());
+  check_status(cdg_ep_permute(reinterpret_cast<const uint8_t*>(rq.data_ptr()), rs.data_ptr<float>(),
+                              re.data_ptr<int32_t>(), R, H, E_local, expert_off.data_ptr<int64_t>(),
+                              fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()), SA.data_ptr<float>(),
+                              mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(), cur_stream(rq)),
+               "ep_permute");
+  return {A, SA, mi, pos};
+}
+
+torch::Tensor ep_unpermute(const torch::Tensor& Y, const torch::Tensor& perm_pos) {
+  TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
+  const c10::cuda::CUDAGuard guard(Y.device());
+  const int64_t R = perm_pos.numel(), H = Y.size(1);
+  auto out = torch::empty({R, H}, Y.options());
+  check_status(cdg_ep_unpermute(Y.data_ptr(), Y.stride(0), perm_pos.data_ptr<int32_t>(), R, H, out.data_ptr(),
+                                cur_stream(Y)),
+               "ep_unpermute");
+  return out;
+}
+
+torch::Tensor ep_combine(const torch::Tensor& rows, const torch::Tensor& send_index, const torch::Tensor& topk_w) {
+  TORCH_CHECK(rows.is_cuda() && rows.is_contiguous() && rows.scalar_type() == torch::kBFloat16, "rows: BF16");
+  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() && topk_w.dim() == 2, "topk_w: f32");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  const int64_t T = topk_w.size(0), topk = topk_w.size(1), H = rows.size(1);
+  auto y = torch::empty({T, H}, rows.options());
+  check_status(cdg_ep_combine(rows.data_ptr(), send_index.data_ptr<int32_t>(), topk_w.data_ptr<float>(), T, topk, H,
+                              y.data_ptr(), cur_stream(rows)),
+               "ep_combine");
+  return y;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -188,4 +301,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                      "set_profile_events");
       },
       py::arg("start"), py::arg("stop"));
+  m.def("quant_fp8_rows", &quant_fp8_rows, py::arg("x"));
+  m.def("silu_mul_quant", &silu_mul_quant, py::arg("h"), py::arg("m_indices") = py::none());
+  m.def("ep_count", &ep_count, py::arg("topk_ids"), py::arg("num_experts"));
+  m.def("ep_pack", &ep_pack, py::arg("xq"), py::arg("xs"), py::arg("topk_ids"), py::arg("num_experts"),
+        py::arg("ranks"), py::arg("send_off"), py::arg("rows"));
+  m.def("ep_permute", &ep_permute, py::arg("rq"), py::arg("rs"), py::arg("re"), py::arg("local_experts"),
+        py::arg("expert_off"), py::arg("m_pad"));
+  m.def("ep_unpermute", &ep_unpermute, py::arg("y"), py::arg("perm_pos"));
+  m.def("ep_combine", &ep_combine, py::arg("rows"), py::arg("send_index"), py::arg("topk_w"));
 }

@@ -186,6 +186,56 @@ int cdg_set_profile_events(void* start_event, void* stop_event);
  *   - No cudaMalloc, cudaFree or allocating library routine is called. */
 int cdg_grouped_fp8_fp4_gemm_nt_contiguous_noalloc(const cdg_gemm_args* args, cdg_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Mixture-of-experts layer around the grouped GEMM, and expert parallelism.
+ * None of these exist in the reference (it ships the GEMM only); they are the
+ * steps vLLM runs on either side of it, restated for this library:
+ *   activation quantisation  deep_gemm/utils/math.py:21-37 (per_block_cast_to_fp8)
+ *   SiLU-mul + requant       vLLM DeepGemmFP4Experts._act_mul_quant (experts/deep_gemm_moe.py:420-453),
+ *                            gate = first half of FC1's output (consumer_deep_gemm/mega.py:19-22)
+ *   permute / unpermute      vLLM deepgemm_moe_permute / deepgemm_unpermute_and_reduce
+ *                            (fused_moe/deep_gemm_utils.py:347, 420)
+ * Strides are in elements; e4m3 tensors are bytes.
+ * ------------------------------------------------------------------------------------------- */
+
+/* q[r, :] = e4m3(x[r, :] / amax * 448), s[r, kb] = amax / 448 per 128-column block (amax clamped
+ * at 1e-12), FP32 arithmetic; x is BF16 or F32 (x_dtype), K a multiple of 128. */
+int cdg_quant_fp8_rows(const void* x, int32_t x_dtype, int64_t x_stride, int64_t M, int64_t K, uint8_t* q,
+                       int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k, cdg_stream_t stream);
+
+/* in = [gate | up] BF16 [M, 2I]: q, s = 1x128 e4m3 quantisation of silu(gate) * up (FP32).
+ * Rows whose m_indices entry is negative are skipped (m_indices may be NULL). */
+int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t I, const int32_t* m_indices,
+                           uint8_t* q, int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k,
+                           cdg_stream_t stream);
+
+/* counts[e] = number of entries of topk_ids (n of them, int32 or int64) equal to e, e in [0, E). */
+int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, int32_t* counts, cdg_stream_t stream);
+
+/* Send buffer of expert parallelism: every (token t, slot j) with expert e in [0, E) copies
+ * token t's e4m3 row and scales to a row of destination rank e / (E / ranks), starting at
+ * send_off[dest]; out_e gets the expert's local id e % (E / ranks); send_index[t*topk + j]
+ * is that row (-1 for skipped slots).  `fill` is [ranks] scratch. */
+int cdg_ep_pack(const uint8_t* xq, int64_t xq_stride, const float* xs, int64_t xs_stride, const void* topk_ids,
+                int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H,
+                const int64_t* send_off, int32_t* fill, uint8_t* out_q, float* out_s, int32_t* out_e,
+                int32_t* send_index, cdg_stream_t stream);
+
+/* Received rows -> contiguous layout: row i of local expert e lands in [expert_off[e], +count),
+ * expert_off being the 128-aligned offsets; m_indices[M_pad] is -1 except on placed rows;
+ * perm_pos[i] is row i's position.  `fill` is [E_local] scratch. */
+int cdg_ep_permute(const uint8_t* recv_q, const float* recv_s, const int32_t* recv_e, int64_t R, int64_t H,
+                   int64_t E_local, const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA,
+                   int32_t* m_indices, int64_t M_pad, int32_t* perm_pos, cdg_stream_t stream);
+
+/* out[i, :] = Y[perm_pos[i], :] (BF16 rows of length H). */
+int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R, int64_t H, void* out,
+                     cdg_stream_t stream);
+
+/* y[t, :] = bf16(sum_j topk_w[t, j] * rows[send_index[t*topk + j], :]) in FP32, skipping -1 slots. */
+int cdg_ep_combine(const void* rows, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
+                   int64_t H, void* y, cdg_stream_t stream);
+
 /* Human-readable name of a cdg_status value. */
 const char* cdg_status_string(int status);
 

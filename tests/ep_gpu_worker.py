@@ -1,0 +1,50 @@
+"""Worker of the 2-GPU expert-parallel test (launched by torchrun from test_gpu_moe.py).
+
+Each rank builds the same layer inputs, keeps its half of the experts and of the
+tokens, runs the EP layer over NCCL, and rank 0 compares the gathered output with
+the single-GPU layer (all experts on one GPU): per-row relative L2 <= 1e-3.
+"""
+
+import datetime
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(os.path.dirname(HERE), "consumer-deepgemm_b200"), os.path.dirname(HERE), HERE):
+    sys.path.insert(0, p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from consumer_deep_gemm.moe import MoELayer  # noqa: E402
+from metrics import errors  # noqa: E402
+from moe_ref import make_layer_inputs  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    cfg = dict(tokens=256, experts=16, hidden=1024, inter=512, topk=4)
+    x, ids, w, w1, w1s, w2, w2s = (t.to(dev) for t in make_layer_inputs(**cfg))
+    e_loc = cfg["experts"] // world
+    sl = slice(rank * e_loc, (rank + 1) * e_loc)
+    layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], cfg["experts"], group=dist.group.WORLD)
+    tpr = cfg["tokens"] // world
+    ts = slice(rank * tpr, (rank + 1) * tpr)
+    y = layer(x[ts], ids[ts], w[ts])
+    parts = [torch.empty_like(y) for _ in range(world)]
+    dist.all_gather(parts, y)
+    if rank == 0:
+        y_ep = torch.cat(parts)
+        y_one = MoELayer(w1, w1s, w2, w2s, cfg["experts"])(x, ids, w)
+        nw, rl2 = errors(y_ep, y_one)
+        assert nw <= 1e-3 and rl2 <= 1e-3, (nw, rl2)
+        print("EP_OK", nw, rl2, flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

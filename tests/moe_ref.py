@@ -1,0 +1,87 @@
+"""CPU reference of the MoE layer steps (test infrastructure).
+
+``TorchRefOps`` implements the ``ops`` interface of consumer_deep_gemm.moe.MoELayer
+on CPU tensors with plain torch and the oracle GEMM, in a fixed row order.  With
+it, ``MoELayer`` over world size 1 is the reference layer, and over a gloo
+process group it exercises the expert-parallel exchange logic without a GPU.
+"""
+
+import torch
+
+from deep_gemm.utils.math import per_block_cast_to_fp8
+from oracle import cdg_oracle as oracle
+
+
+class TorchRefOps:
+    def quant(self, x):
+        return per_block_cast_to_fp8(x.float())
+
+    def count(self, topk_ids, num_experts):
+        ids = topk_ids.flatten().long()
+        ids = ids[(ids >= 0) & (ids < num_experts)]
+        return torch.bincount(ids, minlength=num_experts).to(torch.int32)
+
+    def pack(self, xq, xs, topk_ids, num_experts, ranks, send_off, rows):
+        T, k = topk_ids.shape
+        per_rank = num_experts // ranks
+        out_q = torch.empty(rows, xq.shape[1], dtype=xq.dtype)
+        out_s = torch.empty(rows, xs.shape[1], dtype=xs.dtype)
+        out_e = torch.empty(rows, dtype=torch.int32)
+        send_index = torch.full((T * k,), -1, dtype=torch.int32)
+        fill = [0] * ranks
+        for i, e in enumerate(topk_ids.flatten().tolist()):
+            if not 0 <= e < num_experts:
+                continue
+            d = e // per_rank
+            r = int(send_off[d]) + fill[d]
+            fill[d] += 1
+            out_q[r], out_s[r], out_e[r] = xq[i // k], xs[i // k], e % per_rank
+            send_index[i] = r
+        return out_q, out_s, out_e, send_index
+
+    def permute(self, rq, rs, re, local_experts, expert_off, m_pad):
+        a = torch.zeros(m_pad, rq.shape[1], dtype=rq.dtype)
+        sa = torch.ones(m_pad, rs.shape[1], dtype=rs.dtype)
+        m_indices = torch.full((m_pad,), -1, dtype=torch.int32)
+        pos = torch.empty(rq.shape[0], dtype=torch.int32)
+        fill = [0] * local_experts
+        for i, e in enumerate(re.tolist()):
+            p = int(expert_off[e]) + fill[e]
+            fill[e] += 1
+            a[p], sa[p], m_indices[p], pos[i] = rq[i], rs[i], e, p
+        return a, sa, m_indices, pos
+
+    def gemm(self, a, sa, w, w_sf, m_indices):
+        d = torch.empty(a.shape[0], w.shape[1], dtype=torch.bfloat16)
+        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices)
+        return d
+
+    def act(self, h, m_indices):
+        i = h.shape[1] // 2
+        g, u = h[:, :i].float(), h[:, i:].float()
+        return per_block_cast_to_fp8(torch.nn.functional.silu(g) * u)
+
+    def unpermute(self, y, perm_pos):
+        return y[perm_pos.long()]
+
+    def combine(self, rows, send_index, topk_w):
+        T, k = topk_w.shape
+        y = torch.zeros(T, rows.shape[1], dtype=torch.float32)
+        for i, r in enumerate(send_index.tolist()):
+            if r >= 0:
+                y[i // k] += topk_w[i // k, i % k] * rows[r].float()
+        return y.to(torch.bfloat16)
+
+
+def make_layer_inputs(tokens, experts, hidden, inter, topk, seed=0):
+    """Seeded tokens, routing and MXFP4 expert weights for a small layer."""
+    from deep_gemm.utils.math import per_block_cast_to_fp4
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(tokens, hidden, generator=g).to(torch.bfloat16)
+    ids = torch.rand(tokens, experts, generator=g).topk(topk, dim=1).indices.to(torch.int32)
+    w = torch.rand(tokens, topk, generator=g)
+    w = w / w.sum(1, keepdim=True)
+    w1, w1s = per_block_cast_to_fp4(torch.randn(experts, 2 * inter, hidden, generator=g) * 0.05)
+    w2, w2s = per_block_cast_to_fp4(torch.randn(experts, hidden, inter, generator=g) * 0.05)
+    return x, ids, w, w1, w1s, w2, w2s

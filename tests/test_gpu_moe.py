@@ -1,0 +1,117 @@
+"""GPU checks of the MoE-layer kernels and of the layer itself (through the torch binding).
+
+Tolerances:
+  * FP8 row quantisation: bit-exact against per_block_cast_to_fp8 (deep_gemm/utils/math.py:21-37).
+  * SiLU-mul + requant: scales within 1e-6 relative; e4m3 codes equal except where the
+    CUDA and CPU exponentials differ by an ulp (at most 1 in 1000 codes, each within one e4m3 step).
+  * Dispatch / permute / unpermute: exact (bytes).
+  * Whole layer (two GEMMs with an e4m3 requantisation between them, which turns last-bit
+    differences of FC1 into e4m3 rounding flips): max |y - ref| / max |ref| <= 1e-2 and
+    per-row relative L2 <= 1e-2 against the CPU reference layer.
+"""
+
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+from moe_ref import TorchRefOps, make_layer_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _ext():
+    from consumer_deep_gemm import native
+
+    return native.require()
+
+
+def test_quant_fp8_rows_bit_exact():
+    from deep_gemm.utils.math import per_block_cast_to_fp8
+
+    g = torch.Generator().manual_seed(1)
+    x = (torch.randn(300, 1024, generator=g) * torch.rand(300, 1, generator=g) * 10).to(torch.bfloat16)
+    x[7] = 0  # all-zero row: amax clamps at 1e-12
+    q, s = _ext().quant_fp8_rows(x.to(DEV))
+    rq, rs = per_block_cast_to_fp8(x.float())
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+    assert torch.equal(s.cpu(), rs)
+
+
+def test_silu_mul_quant_matches_reference():
+    g = torch.Generator().manual_seed(2)
+    h = torch.randn(200, 2 * 512, generator=g).to(torch.bfloat16)
+    q, s = _ext().silu_mul_quant(h.to(DEV), None)
+    rq, rs = TorchRefOps().act(h, None)
+    assert torch.allclose(s.cpu(), rs, rtol=1e-6, atol=0)
+    a, b = q.cpu().view(torch.uint8).to(torch.int32), rq.view(torch.uint8).to(torch.int32)
+    diff = (a != b)
+    assert diff.float().mean().item() <= 1e-3
+    assert ((a - b).abs()[diff] <= 1).all()
+
+
+def test_dispatch_and_permute_are_exact():
+    C = _ext()
+    T, H, k, E = 64, 512, 4, 16
+    g = torch.Generator().manual_seed(3)
+    xq = torch.randint(0, 256, (T, H), dtype=torch.uint8, generator=g).to(DEV).view(torch.float8_e4m3fn)
+    xs = torch.rand(T, H // 128, generator=g).to(DEV)
+    ids = torch.rand(T, E, generator=g).topk(k, dim=1).indices.to(torch.int32)
+    ids[3, 1] = -1  # a masked slot
+    counts = C.ep_count(ids.to(DEV), E).cpu()
+    ref_counts = torch.bincount(ids[ids >= 0].long(), minlength=E)
+    assert torch.equal(counts.long(), ref_counts)
+    rows = int(counts.sum())
+    sq, ss, se, send_index = C.ep_pack(xq, xs, ids.to(DEV), E, 1, torch.zeros(1, dtype=torch.int64, device=DEV), rows)
+    si = send_index.cpu()
+    assert int(si[3 * k + 1]) == -1 and int((si >= 0).sum()) == rows
+    flat = ids.flatten()
+    for i in range(T * k):
+        if si[i] >= 0:
+            r = int(si[i])
+            assert torch.equal(sq[r].cpu().view(torch.uint8), xq[i // k].cpu().view(torch.uint8))
+            assert int(se[r]) == int(flat[i])
+    aligned = (ref_counts + 127) // 128 * 128
+    off = (torch.cumsum(aligned, 0) - aligned).to(DEV)
+    m_pad = int(aligned.sum())
+    a, sa, mi, pos = C.ep_permute(sq, ss, se, E, off, m_pad)
+    pos, mi = pos.cpu().long(), mi.cpu()
+    assert torch.equal(a.cpu().view(torch.uint8)[pos], sq.cpu().view(torch.uint8))
+    assert torch.equal(mi[pos], se.cpu())
+    assert int((mi >= 0).sum()) == rows
+    for e in range(E):
+        seg = mi[int(off[e]):int(off[e]) + int(aligned[e])]
+        assert int((seg == e).sum()) == int(ref_counts[e]) and bool((seg[: int(ref_counts[e])] == e).all())
+    y = torch.randn(m_pad, H, generator=g).to(torch.bfloat16).to(DEV)
+    back = C.ep_unpermute(y, pos.to(torch.int32).to(DEV))
+    assert torch.equal(back.cpu().view(torch.int16), y.cpu()[pos].view(torch.int16))
+
+
+def test_layer_single_gpu_matches_cpu_reference():
+    from consumer_deep_gemm.moe import MoELayer
+    from metrics import errors
+
+    cfg = dict(tokens=96, experts=8, hidden=512, inter=256, topk=2)
+    x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**cfg)
+    y_ref = MoELayer(w1, w1s, w2, w2s, cfg["experts"], ops=TorchRefOps())(x, ids, w)
+    layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), cfg["experts"])
+    y = layer(x.to(DEV), ids.to(DEV), w.to(DEV))
+    y2 = layer(x.to(DEV), ids.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), y2.view(torch.int16)), "repeat runs differ"
+    nw, rl2 = errors(y.cpu(), y_ref)
+    assert nw <= 1e-2 and rl2 <= 1e-2, (nw, rl2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_layer_expert_parallel_two_gpus():
+    here = os.path.dirname(os.path.abspath(__file__))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr", "127.0.0.1", "--master-port", "29613", os.path.join(here, "ep_gpu_worker.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "EP_OK" in r.stdout
