@@ -1,28 +1,39 @@
 #!/usr/bin/env python
 """Benchmark of the grouped FP8 x MXFP4 MoE GEMM (m_grouped_fp8_fp4_gemm_nt_contiguous).
 
-One step = one call of the public API on one batch of a benchmark config
-(default c1: the decode FC1 shape E=256, K=N=4096, 64 tokens x top-8, the
-HBM-bound case the metric is quoted on).  Inputs are seeded synthetic data with
-the config's shapes and distributions (consumer_deep_gemm.synthetic); weights
-are transformed once (weight-load time) and stay resident, as in serving.
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3|c4] [--impl ours|reference]
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3] [--impl ours|reference]
+Workloads (seeded synthetic data with the configs' shapes and distributions,
+consumer_deep_gemm.synthetic; weights transformed once at load and resident):
 
-Prints one JSON line on rank 0.  `value` is the algorithmic HBM throughput (GB/s;
-bytes of the routed rows of A and their scales, the weights and scales of the
-experts that receive rows, and the routed rows of D) of the whole job divided
-by the device time of K steps (max over ranks).  `e2e` times the same calls
-with the step's inputs copied from pinned host memory and D copied back inside
-the timed region.  `roofline` relates the tensor-core GEMM kernels' own duration
-(CUDA events recorded by the library around them) to the measured HBM copy
-bandwidth.  With --gpus N > 1 every rank runs its own batch (rank-seeded
-routing) on its own GPU: weak scaling, no collective on the data path.
+* N = 1, default c1: one step = one call of the public API on the decode FC1
+  batch (E=256, K=N=4096, 64 tokens x top-8, 222 active experts), the HBM-bound
+  case the metric is quoted on.  --config c2/c3 run the prefill shapes.
+* N > 1 (launched by torchrun), default: every rank serves its own c1-sized
+  decode batch (rank-seeded tokens and routing); the 256 experts are sharded
+  over the ranks (expert parallelism).  One step = quantise the rank's tokens,
+  exchange per-expert counts and dispatch the routed rows to the experts'
+  owners (NCCL all-to-all), run the grouped GEMM on the local experts, return
+  the rows (all-to-all) and combine them per token.  Weak scaling: per-rank
+  tokens fixed, the expert weights divided.
+* --config c4: the full expert-parallel MoE layer (FC1 -> SiLU-mul + requant ->
+  FC2), 32768 tokens x top-8 split over the ranks, E=256, hidden 4096,
+  intermediate 2048.  Strong scaling; reported in TFLOP/s.
+
+One JSON line on rank 0.  `value` = algorithmic bytes (or FLOPs for c4) of the
+whole job per step / device time of K steps (max over ranks).  Algorithmic bytes
+count routed rows of A and their scales, the weights and scales of experts that
+receive rows, and routed rows of D; padding-row zeros are not counted.  `e2e`
+times the same steps with the per-step inputs copied from pinned host memory and
+the result copied back.  `roofline` relates the tensor-core GEMM kernels' own
+duration (CUDA events the library records around them) to the measured HBM copy
+bandwidth (or 2x the measured BF16 GEMM rate for c4).
 """
 
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -37,19 +48,24 @@ sys.path.insert(0, HERE)
 import torch  # noqa: E402
 
 METRIC = "grouped FP8×FP4 MoE GEMM TFLOPS and HBM GB/s vs roofline at 1/2/4/8 B200"
-# cdg_prep_kernel, cdg_gemm_kernel<16>, cdg_gemm_kernel<32>, cdg_gemm_kernel<128>, cdg_generic_kernel
-LAUNCHES_PER_CALL = 5
+DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
+# library kernels per GEMM call: cdg_prep_kernel, cdg_gemm_kernel<16>, <32>, <128>, cdg_generic_kernel
+GEMM_LAUNCHES = 5
+# per EP step on top of the GEMM(s): quant_rows, ep_count, ep_pack, ep_permute, ep_unpermute, ep_combine
+EP_LAUNCHES = 6
+
+
+def gemm_bytes(rows, e_act, n, k):
+    return rows * k + rows * (k // 128) * 4 + e_act * n * k // 2 + e_act * n * k // 32 + rows * n * 2
 
 
 def algorithmic(inp):
-    """(bytes, flops) of one call counted on routed rows and active experts only."""
+    """(bytes, flops, active experts) of one GEMM call on routed rows and active experts only."""
     cfg = inp["cfg"]
     ids = inp["m_indices"]
-    r = inp["rows"]
     e_act = int(torch.unique(ids[ids >= 0]).numel())
-    n, k = cfg.n, cfg.k
-    nbytes = r * k + r * (k // 128) * 4 + e_act * n * k // 2 + e_act * n * k // 32 + r * n * 2
-    return nbytes, 2 * r * n * k, e_act
+    r = inp["rows"]
+    return gemm_bytes(r, e_act, cfg.n, cfg.k), 2 * r * cfg.n * cfg.k, e_act
 
 
 def measured_peaks():
@@ -123,21 +139,16 @@ def cpu_port_sample(inp, budget_s: float = 4.0):
     def run(n_exp):
         sel = experts[:n_exp]
         rows = torch.isin(ids, sel).nonzero().flatten()
-        sub = torch.full((experts.max().item() + 1,), -1, dtype=torch.int32)
+        sub = torch.full((int(experts.max()) + 1,), -1, dtype=torch.int32)
         sub[sel] = torch.arange(sel.numel(), dtype=torch.int32)
         b = inp["b"][sel.to(inp["b"].device)].cpu()
         sb = inp["sb"][sel.to(inp["sb"].device)].cpu()
         d = torch.empty(rows.numel(), cfg.n, dtype=torch.bfloat16)
         t0 = time.perf_counter()
         oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a[rows], sa[rows]), (b, sb), d, sub[ids[rows].long()])
-        dt = time.perf_counter() - t0
-        r = rows.numel()
-        k, n = cfg.k, cfg.n
-        nbytes = r * k + r * (k // 128) * 4 + sel.numel() * n * k // 2 + sel.numel() * n * k // 32 + r * n * 2
-        return dt, nbytes, r
+        return time.perf_counter() - t0, gemm_bytes(rows.numel(), sel.numel(), cfg.n, cfg.k), rows.numel()
 
-    n_exp = 1
-    dt, _, _ = run(n_exp)
+    dt, _, _ = run(1)
     n_exp = max(1, min(int(experts.numel()), int(budget_s / max(dt, 1e-3))))
     times = []
     for _ in range(3):
@@ -149,20 +160,20 @@ def cpu_port_sample(inp, budget_s: float = 4.0):
     return nbytes / dt / 1e9, torch.get_num_threads(), desc
 
 
-def run_reference(args, cfg_name):
+def run_reference(args):
     """The reference's CPU path (oracle port) on rank 0: each step is a bounded sample."""
     from consumer_deep_gemm import synthetic
 
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
+    cfg_name = args.config if args.config in ("c1", "c2", "c3") else "c1"
     inp = synthetic.make_inputs(synthetic.CONFIGS[cfg_name], device="cpu", seed=0,
                                 weight_device="cuda" if torch.cuda.is_available() else "cpu")
     gbs, cores, desc = cpu_port_sample(inp, budget_s=max(1.0, 20.0 / max(1, args.steps)))
     line = {
         "metric": METRIC, "impl": "reference", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp8e4m3 x e2m1 -> fp32 acc -> bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": cfg_name, "parallelism": "cpu"},
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -170,22 +181,49 @@ def run_reference(args, cfg_name):
     print(json.dumps(line), flush=True)
 
 
+class Timed:
+    """Device time of K steps (CUDA events on the current stream) and of the GEMM kernels inside them."""
+
+    def __init__(self, dev, steps):
+        from consumer_deep_gemm import native
+
+        self.ext = native.require()
+        self.stream = torch.cuda.current_stream(dev)
+        self.kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(steps)]
+        for s, e in self.kev:  # materialise the raw event handles
+            s.record(self.stream)
+            e.record(self.stream)
+        torch.cuda.synchronize(dev)
+
+    def run(self, step, steps, with_kernel_events=True):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(self.stream)
+        for i in range(steps):
+            if with_kernel_events:
+                self.ext.set_profile_events(self.kev[i][0].cuda_event, self.kev[i][1].cuda_event)
+            step()
+        self.ext.set_profile_events(0, 0)
+        t1.record(self.stream)
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / steps
+        kms = statistics.fmean(s.elapsed_time(e) for s, e in self.kev[:steps]) if with_kernel_events else None
+        return ms, kms
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c1", choices=["c1", "c2", "c3"])
+    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
-        run_reference(args, args.config)
+        run_reference(args)
         return
-
-    import consumer_deep_gemm as cdg
-    from consumer_deep_gemm import native, synthetic
-
+    assert args.warmup >= 3, "at least 3 warm-up steps"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -193,52 +231,61 @@ def main():
     dev = torch.device("cuda", local)
     dist = None
     if world > 1:
-        import datetime
-
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    assert args.warmup >= 3, "at least 3 warm-up steps"
 
-    cfg = synthetic.CONFIGS[args.config]
-    inp = synthetic.make_inputs(cfg, device=dev, seed=rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        if args.config == "c4":
+            line = bench_layer(args, dev, world, rank, dist)
+        elif world > 1:
+            line = bench_ep_decode(args, dev, world, rank, dist)
+        else:
+            line = bench_gemm(args, dev, args.config or "c1")
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+def _max_over_ranks(dist, dev, *vals):
+    if dist is None:
+        return vals
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return tuple(t.tolist())
+
+
+def _sum_over_ranks(dist, dev, val):
+    if dist is None:
+        return val
+    t = torch.tensor([val], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return t.item()
+
+
+def bench_gemm(args, dev, cfg_name):
+    """N = 1: the public GEMM on one config."""
+    import consumer_deep_gemm as cdg
+    from consumer_deep_gemm import synthetic
+
+    cfg = synthetic.CONFIGS[cfg_name]
+    inp = synthetic.make_inputs(cfg, device=dev, seed=0)
     a, sa, b, sb, ids = inp["a"], inp["sa"], inp["b"], inp["sb"], inp["m_indices"]
     atoms = cdg.transform_sf_into_required_layout(sb, num_groups=b.shape[0], recipe=(1, 32))
     d = torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=dev)
     nbytes, flops, e_act = algorithmic(inp)
-    ext = native.require()
 
     def call():
         cdg.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (b, atoms), d, ids, recipe_a=(1, 128), recipe_b=(1, 32))
 
-    stream = torch.cuda.current_stream(dev)
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(dev.index)
     for _ in range(args.warmup):
         call()
-    torch.cuda.synchronize(dev)
+    timer = Timed(dev, args.steps)
+    ms, kernel_ms = timer.run(call, args.steps)
 
-    # ---------------------------------------------------------------- device-resident timing
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for s, e in kev:  # materialise the raw event handles
-        s.record(stream)
-        e.record(stream)
-    torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(args.steps):
-        ext.set_profile_events(kev[i][0].cuda_event, kev[i][1].cuda_event)
-        call()
-    ext.set_profile_events(0, 0)
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    ms = t0.elapsed_time(t1) / args.steps
-    kernel_ms = statistics.fmean(s.elapsed_time(e) for s, e in kev)
-
-    # ---------------------------------------------------------------- end to end from pinned host memory
     h_a, h_sa, h_ids = a.cpu().pin_memory(), sa.cpu().pin_memory(), ids.cpu().pin_memory()
     h_d = torch.empty(d.shape, dtype=d.dtype).pin_memory()
     a2, sa2, ids2 = torch.empty_like(a), torch.empty_like(sa), torch.empty_like(ids)
@@ -252,58 +299,174 @@ def main():
 
     for _ in range(args.warmup):
         e2e_call()
-    torch.cuda.synchronize(dev)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    t0.record(stream)
-    for _ in range(args.steps):
-        e2e_call()
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = t0.elapsed_time(t1) / args.steps
+    e2e_ms, _ = timer.run(e2e_call, args.steps, with_kernel_events=False)
     clocks = sampler.stop()
-    h2d = h_a.numel() * h_a.element_size() + h_sa.numel() * 4 + h_ids.numel() * h_ids.element_size()
-    d2h = h_d.numel() * h_d.element_size()
-
-    # max over ranks of the device times
-    if dist:
-        t = torch.tensor([ms, e2e_ms, kernel_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms, kernel_ms = t.tolist()
-    if rank != 0:
-        if dist:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-
     hbm_peak, _, peak_src = measured_peaks()
-    gbs = nbytes * world / (ms * 1e-3) / 1e9
     achieved = nbytes / (kernel_ms * 1e-3) / 1e9
     line = {
-        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp8e4m3 x e2m1 -> fp32 acc -> bf16", "data": "synthetic",
+        "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": cfg.name, "experts": cfg.num_experts, "k": cfg.k, "n": cfg.n,
                    "routed_rows": inp["rows"], "m_pad": inp["m_pad"], "active_experts": e_act,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2 (weights %.2f GB)" % (b.numel() / 1e9)},
-        "tflops": flops * world / (ms * 1e-3) / 1e12,
+                   "parallelism": "single", "l2": "inputs larger than L2 (weights %.2f GB)" % (b.numel() / 1e9)},
+        "tflops": flops / (ms * 1e-3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
                      "kernel_ms": kernel_ms, "algorithmic_bytes": nbytes},
-        "e2e": {"value": nbytes * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": LAUNCHES_PER_CALL * args.steps,
+        "e2e": {"value": nbytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": h_a.numel() + h_sa.numel() * 4 + h_ids.numel() * h_ids.element_size(),
+                "d2h_bytes_per_step": h_d.numel() * 2, "ms_per_step": e2e_ms},
+        "gpu_launches": GEMM_LAUNCHES * args.steps,
         "clocks": clocks,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if not args.no_cpu_baseline:
         v, cores, desc = cpu_port_sample(inp)
         line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc}
-    print(json.dumps(line), flush=True)
+    return line
+
+
+def _ep_inputs(cfg, dev, rank, world, tokens, seed_base=0):
+    """A rank's tokens, routing and its shard of the expert weights."""
+    from consumer_deep_gemm import synthetic
+
+    g = torch.Generator().manual_seed(seed_base + rank)
+    x = torch.randn(tokens, cfg.k, generator=g).to(torch.bfloat16)
+    ids = torch.rand(tokens, cfg.num_experts, generator=g).topk(cfg.topk, dim=1).indices.to(torch.int32)
+    w = torch.rand(tokens, cfg.topk, generator=g)
+    w = w / w.sum(1, keepdim=True)
+    e_loc = cfg.num_experts // world
+    b, sb = synthetic.make_weights(e_loc, cfg.n, cfg.k, dev, seed=100 + rank)
+    return x.to(dev), ids.to(dev), w.to(dev), b, sb
+
+
+def _local_gemm_work(counts, n, k):
+    """Algorithmic (bytes, flops) of a local grouped GEMM given per-local-expert received row counts."""
+    rows = int(counts.sum())
+    e_act = int((counts > 0).sum())
+    return gemm_bytes(rows, e_act, n, k), 2 * rows * n * k
+
+
+def _global_counts(ids, num_experts, dev, dist):
+    counts = torch.zeros(num_experts, dtype=torch.int32, device=dev)
+    counts.index_add_(0, ids.flatten().long(), torch.ones(ids.numel(), dtype=torch.int32, device=dev))
+    if dist:
+        dist.all_reduce(counts)
+    return counts
+
+
+def bench_ep_decode(args, dev, world, rank, dist):
+    """N > 1: every rank a c1 decode batch, experts sharded, NCCL dispatch/combine around the GEMM."""
+    from consumer_deep_gemm import synthetic
+    from consumer_deep_gemm.moe import MoELayer
+
+    cfg = synthetic.CONFIGS["c1"]
+    x, ids, w, b, sb = _ep_inputs(cfg, dev, rank, world, cfg.tokens)
+    layer = MoELayer(b, sb, num_experts=cfg.num_experts, group=dist.group.WORLD)
+    e_loc = cfg.num_experts // world
+    mine = _global_counts(ids, cfg.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
+    local_bytes, local_flops = _local_gemm_work(mine, cfg.n, cfg.k)
+    job_bytes = _sum_over_ranks(dist, dev, local_bytes)
+    job_flops = _sum_over_ranks(dist, dev, local_flops)
+
+    def step():
+        layer(x, ids, w)
+
+    sampler = ClockSampler(dev.index)
+    for _ in range(args.warmup):
+        step()
+    timer = Timed(dev, args.steps)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    ms, kernel_ms = timer.run(step, args.steps)
+    dist.barrier()
+
+    h_x, h_ids, h_w = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
+    h_y = torch.empty(x.shape[0], cfg.n, dtype=torch.bfloat16).pin_memory()
+    x2, ids2, w2 = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
+
+    def e2e_step():
+        x2.copy_(h_x, non_blocking=True)
+        ids2.copy_(h_ids, non_blocking=True)
+        w2.copy_(h_w, non_blocking=True)
+        h_y.copy_(layer(x2, ids2, w2), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    e2e_ms, _ = timer.run(e2e_step, args.steps, with_kernel_events=False)
+    clocks = sampler.stop()
+    ms, e2e_ms, kernel_ms = _max_over_ranks(dist, dev, ms, e2e_ms, kernel_ms)
+    hbm_peak, _, peak_src = measured_peaks()
+    achieved = local_bytes / (kernel_ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": job_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
+        "config": {"workload": "c1-ep", "experts": cfg.num_experts, "k": cfg.k, "n": cfg.n,
+                   "tokens_per_rank": cfg.tokens, "topk": cfg.topk, "parallelism": f"ep{world}",
+                   "step": "quant, count all-to-all, dispatch all-to-all, grouped GEMM on local experts, "
+                           "return all-to-all, weighted combine",
+                   "l2": "weights per rank larger than L2"},
+        "tflops": job_flops / (ms * 1e-3) / 1e12,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
+                     "kernel_ms": kernel_ms, "algorithmic_bytes": local_bytes, "note": "rank 0's GEMM kernels"},
+        "e2e": {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": h_x.numel() * 2 + h_ids.numel() * 4 + h_w.numel() * 4,
+                "d2h_bytes_per_step": h_y.numel() * 2, "ms_per_step": e2e_ms},
+        "gpu_launches": (GEMM_LAUNCHES + EP_LAUNCHES) * args.steps,
+        "clocks": clocks,
+    }
+
+
+def bench_layer(args, dev, world, rank, dist):
+    """--config c4: the full expert-parallel MoE layer, 32768 tokens split over the ranks."""
+    from consumer_deep_gemm import synthetic
+    from consumer_deep_gemm.moe import MoELayer
+
+    c1 = synthetic.CONFIGS["c4_fc1"]
+    c2 = synthetic.CONFIGS["c4_fc2"]
+    tokens = c1.tokens // world
+    x, ids, w, b1, s1 = _ep_inputs(c1, dev, rank, world, tokens)
+    b2, s2 = synthetic.make_weights(c1.num_experts // world, c2.n, c2.k, dev, seed=200 + rank)
+    layer = MoELayer(b1, s1, b2, s2, num_experts=c1.num_experts, group=dist.group.WORLD if dist else None)
+    e_loc = c1.num_experts // world
+    mine = _global_counts(ids, c1.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
+    _, f_fc1 = _local_gemm_work(mine, c1.n, c1.k)
+    _, f_fc2 = _local_gemm_work(mine, c2.n, c2.k)
+    job_flops = _sum_over_ranks(dist, dev, f_fc1 + f_fc2)
+
+    def step():
+        layer(x, ids, w)
+
+    sampler = ClockSampler(dev.index)
+    for _ in range(args.warmup):
+        step()
+    timer = Timed(dev, args.steps)
     if dist:
         dist.barrier()
-        dist.destroy_process_group()
+    torch.cuda.synchronize(dev)
+    # the library's profile events bracket the last GEMM call of a step (FC2)
+    ms, fc2_ms = timer.run(step, args.steps)
+    clocks = sampler.stop()
+    ms, fc2_ms = _max_over_ranks(dist, dev, ms, fc2_ms)
+    _, bf16_peak, peak_src = measured_peaks()
+    fp8_peak = 2 * bf16_peak
+    achieved = f_fc2 / (fc2_ms * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": job_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
+        "config": {"workload": "c4", "experts": c1.num_experts, "hidden": c1.k, "intermediate": c2.k,
+                   "tokens": c1.tokens, "topk": c1.topk, "parallelism": f"ep{world}"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": achieved / fp8_peak, "traffic": None, "kernel": "FC2 GEMM kernels (rank 0)",
+                     "peak_source": f"2 x {peak_src} bf16 GEMM rate (dense FP8:BF16 = 2:1)"},
+        "gpu_launches": (2 * GEMM_LAUNCHES + EP_LAUNCHES + 1) * args.steps,
+        "clocks": clocks,
+    }
 
 
 if __name__ == "__main__":

@@ -80,10 +80,11 @@ class MoELayer:
 
     w1: packed e2m1 [E_local, 2*I, H/2] (gate rows first), w1_scale UE8M0 [E_local, 2*I, H/32];
     w2: packed e2m1 [E_local, H, I/2], w2_scale UE8M0 [E_local, H, I/32].
-    ``num_experts`` is the global E; E_local = E / world size.
+    ``num_experts`` is the global E; E_local = E / world size.  With ``w2=None`` the layer
+    is the expert-parallel grouped GEMM alone: y[t] = sum_j topk_w[t, j] * FC1_e(q(x[t])).
     """
 
-    def __init__(self, w1, w1_scale, w2, w2_scale, num_experts: int, group=None, ops=None):
+    def __init__(self, w1, w1_scale, w2=None, w2_scale=None, num_experts: int = 0, group=None, ops=None):
         self.ops = ops or NativeOps()
         self.group = group
         if group is not None:
@@ -97,13 +98,15 @@ class MoELayer:
             raise ValueError("the number of experts must divide evenly over the ranks")
         self.num_experts = num_experts
         self.local_experts = num_experts // self.world
-        if w1.shape[0] != self.local_experts or w2.shape[0] != self.local_experts:
+        if w1.shape[0] != self.local_experts or (w2 is not None and w2.shape[0] != self.local_experts):
             raise ValueError("w1/w2 must hold this rank's experts")
-        self.w1, self.w2 = w1.view(torch.uint8), w2.view(torch.uint8)
         # weight scale layout prepared once (the weight-load hook)
+        self.w1 = w1.view(torch.uint8)
         self.w1_sf = transform_sf_into_required_layout(w1_scale) if w1.is_cuda else w1_scale
-        self.w2_sf = transform_sf_into_required_layout(w2_scale) if w2.is_cuda else w2_scale
-        self.hidden = w2.shape[1]
+        self.w2 = w2.view(torch.uint8) if w2 is not None else None
+        if w2 is not None:
+            self.w2_sf = transform_sf_into_required_layout(w2_scale) if w2.is_cuda else w2_scale
+        self.out_dim = w2.shape[1] if w2 is not None else w1.shape[1]
         self.inter = w1.shape[1] // 2
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor) -> torch.Tensor:
@@ -143,13 +146,14 @@ class MoELayer:
         if m_pad > 0:
             a, sa, m_indices, perm_pos = ops.permute(rq, rs, re, E_loc, expert_off, m_pad)
             h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices)
-            aq, asc = ops.act(h, m_indices)
-            y2 = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
-            back = ops.unpermute(y2, perm_pos)
+            if self.w2 is not None:
+                aq, asc = ops.act(h, m_indices)
+                h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
+            back = ops.unpermute(h, perm_pos)
         else:
-            back = torch.empty(0, self.hidden, dtype=torch.bfloat16, device=dev)
+            back = torch.empty(0, self.out_dim, dtype=torch.bfloat16, device=dev)
         if world > 1:
-            out_rows = _all_to_all(torch.empty(sq.shape[0], self.hidden, dtype=back.dtype, device=dev), back,
+            out_rows = _all_to_all(torch.empty(sq.shape[0], self.out_dim, dtype=back.dtype, device=dev), back,
                                    send_splits, recv_splits, self.group)
         else:
             out_rows = back

@@ -30,7 +30,7 @@ def main():
     x, ids, w, w1, w1s, w2, w2s = (t.to(dev) for t in make_layer_inputs(**cfg))
     e_loc = cfg["experts"] // world
     sl = slice(rank * e_loc, (rank + 1) * e_loc)
-    layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], cfg["experts"], group=dist.group.WORLD)
+    layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=cfg["experts"], group=dist.group.WORLD)
     tpr = cfg["tokens"] // world
     ts = slice(rank * tpr, (rank + 1) * tpr)
     y = layer(x[ts], ids[ts], w[ts])
@@ -38,7 +38,7 @@ def main():
     dist.all_gather(parts, y)
     if rank == 0:
         y_ep = torch.cat(parts)
-        y_one = MoELayer(w1, w1s, w2, w2s, cfg["experts"])(x, ids, w)
+        y_one = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"])(x, ids, w)
         nw, rl2 = errors(y_ep, y_one)
         assert nw <= 1e-3 and rl2 <= 1e-3, (nw, rl2)
         print("EP_OK", nw, rl2, flush=True)

@@ -96,8 +96,8 @@ def test_layer_single_gpu_matches_cpu_reference():
 
     cfg = dict(tokens=96, experts=8, hidden=512, inter=256, topk=2)
     x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**cfg)
-    y_ref = MoELayer(w1, w1s, w2, w2s, cfg["experts"], ops=TorchRefOps())(x, ids, w)
-    layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), cfg["experts"])
+    y_ref = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"], ops=TorchRefOps())(x, ids, w)
+    layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), num_experts=cfg["experts"])
     y = layer(x.to(DEV), ids.to(DEV), w.to(DEV))
     y2 = layer(x.to(DEV), ids.to(DEV), w.to(DEV))
     torch.cuda.synchronize()

@@ -52,7 +52,7 @@ def _run(rank, world, q):
         x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**CFG)
         e_loc = CFG["experts"] // world
         sl = slice(rank * e_loc, (rank + 1) * e_loc)
-        layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], CFG["experts"], group=dist.group.WORLD, ops=TorchRefOps())
+        layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=CFG["experts"], group=dist.group.WORLD, ops=TorchRefOps())
         tpr = CFG["tokens"] // world
         ts = slice(rank * tpr, (rank + 1) * tpr)
         y = layer(x[ts], ids[ts], w[ts])
@@ -77,7 +77,7 @@ def test_ep_two_ranks_matches_single_process():
         assert p.exitcode == 0
     y_ep = torch.cat([outs[0], outs[1]])
     x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**CFG)
-    y_ref = MoELayer(w1, w1s, w2, w2s, CFG["experts"], ops=TorchRefOps())(x, ids, w)
+    y_ref = MoELayer(w1, w1s, w2, w2s, num_experts=CFG["experts"], ops=TorchRefOps())(x, ids, w)
     assert torch.equal(y_ep.view(torch.int16), y_ref.view(torch.int16))
     assert y_ref.abs().max() > 0
 
@@ -90,7 +90,7 @@ def test_single_process_layer_composition():
     from oracle import cdg_oracle as oracle
 
     x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**CFG)
-    y = MoELayer(w1, w1s, w2, w2s, CFG["experts"], ops=TorchRefOps())(x, ids, w)
+    y = MoELayer(w1, w1s, w2, w2s, num_experts=CFG["experts"], ops=TorchRefOps())(x, ids, w)
     xq, xs = per_block_cast_to_fp8(x.float())
     t = 5
     acc = torch.zeros(CFG["hidden"])
