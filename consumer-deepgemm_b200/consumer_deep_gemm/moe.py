@@ -13,8 +13,9 @@ DeepGemmFP4Experts runs around ``m_grouped_fp8_fp4_gemm_nt_contiguous``
 Expert parallelism: with a process group of N ranks, rank r owns experts
 [r*E/N, (r+1)*E/N).  Each rank quantises its own tokens, exchanges per-expert row
 counts (one small all-to-all and the only host synchronisation), sends every
-routed row to the rank owning its expert (all-to-all of e4m3 rows, scales and
-local expert ids), lays the received rows out per local expert with 128-row
+routed row to the rank owning its expert (one all-to-all of packed rows: e4m3
+data, FP32 scales and the local expert id in one byte row of
+``native row_bytes(H)``), lays the received rows out per local expert with 128-row
 alignment, runs FC1 -> act -> FC2, and sends the rows back (all-to-all of BF16
 rows) for the weighted top-k sum.  Collectives go through torch.distributed
 (NCCL on GPUs); all compute runs in libcdg_b200.so kernels.
@@ -26,6 +27,7 @@ gloo backend).
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import native
@@ -50,8 +52,8 @@ class NativeOps:
     def pack(self, xq, xs, topk_ids, num_experts, ranks, send_off, rows):
         return self.C.ep_pack(xq, xs, topk_ids, num_experts, ranks, send_off, rows)
 
-    def permute(self, rq, rs, re, local_experts, expert_off, m_pad):
-        return self.C.ep_permute(rq, rs, re, local_experts, expert_off, m_pad)
+    def permute(self, rows, hidden, local_experts, expert_off, m_pad):
+        return self.C.ep_permute(rows, hidden, local_experts, expert_off, m_pad)
 
     def gemm(self, a, sa, w, w_sf, m_indices):
         d = torch.empty(a.shape[0], w.shape[1], dtype=torch.bfloat16, device=a.device)
@@ -117,34 +119,31 @@ class MoELayer:
         xq, xs = ops.quant(x)
         counts = ops.count(topk_ids, E)                                  # [E] rows per global expert
         if world > 1:
-            recv_counts = _all_to_all(torch.empty_like(counts), counts, None, None, self.group)
+            both = torch.empty(2, E, dtype=counts.dtype, device=dev)
+            both[0] = counts
+            _all_to_all(both[1], counts, None, None, self.group)
         else:
-            recv_counts = counts
-        # the one host synchronisation of the layer: split sizes and the local layout
-        send_mat = counts.view(world, E_loc).to("cpu", torch.int64)
-        recv_mat = recv_counts.view(world, E_loc).to("cpu", torch.int64)
-        send_splits = send_mat.sum(1).tolist()
-        recv_splits = recv_mat.sum(1).tolist()
-        per_expert = recv_mat.sum(0)
-        aligned = (per_expert + ALIGN - 1) // ALIGN * ALIGN
+            both = counts.expand(2, E)
+        # the one host synchronisation of the layer (one copy): split sizes and the local layout
+        mats = both.cpu().numpy().astype(np.int64).reshape(2, world, E_loc)
+        send_splits = mats[0].sum(1)
+        recv_splits = mats[1].sum(1)
+        aligned = (mats[1].sum(0) + ALIGN - 1) // ALIGN * ALIGN
         m_pad = int(aligned.sum())
-        expert_off = (torch.cumsum(aligned, 0) - aligned).to(dev)
-        send_off = torch.tensor([0] + send_splits[:-1], dtype=torch.int64).cumsum(0).to(dev)
+        offs = np.concatenate([np.cumsum(aligned) - aligned, np.cumsum(send_splits) - send_splits])
+        offs = torch.from_numpy(offs).to(dev, non_blocking=False)
+        expert_off, send_off = offs[:E_loc], offs[E_loc:]
+        send_splits, recv_splits = send_splits.tolist(), recv_splits.tolist()
 
-        sq, ss, se, send_index = ops.pack(xq, xs, topk_ids, E, world, send_off, sum(send_splits))
-        R = sum(recv_splits)
+        sent, send_index = ops.pack(xq, xs, topk_ids, E, world, send_off, sum(send_splits))
         if world > 1:
-            # e4m3 rows travel as bytes (not every backend has a float8 type)
-            rq = _all_to_all(torch.empty(R, sq.shape[1], dtype=torch.uint8, device=dev), sq.view(torch.uint8),
-                             recv_splits, send_splits, self.group).view(sq.dtype)
-            rs = _all_to_all(torch.empty(R, ss.shape[1], dtype=ss.dtype, device=dev), ss, recv_splits, send_splits,
-                             self.group)
-            re = _all_to_all(torch.empty(R, dtype=se.dtype, device=dev), se, recv_splits, send_splits, self.group)
+            recv = _all_to_all(torch.empty(sum(recv_splits), sent.shape[1], dtype=sent.dtype, device=dev), sent,
+                               recv_splits, send_splits, self.group)
         else:
-            rq, rs, re = sq, ss, se
+            recv = sent
 
         if m_pad > 0:
-            a, sa, m_indices, perm_pos = ops.permute(rq, rs, re, E_loc, expert_off, m_pad)
+            a, sa, m_indices, perm_pos = ops.permute(recv, x.shape[1], E_loc, expert_off, m_pad)
             h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices)
             if self.w2 is not None:
                 aq, asc = ops.act(h, m_indices)
@@ -153,7 +152,7 @@ class MoELayer:
         else:
             back = torch.empty(0, self.out_dim, dtype=torch.bfloat16, device=dev)
         if world > 1:
-            out_rows = _all_to_all(torch.empty(sq.shape[0], self.out_dim, dtype=back.dtype, device=dev), back,
+            out_rows = _all_to_all(torch.empty(sent.shape[0], self.out_dim, dtype=back.dtype, device=dev), back,
                                    send_splits, recv_splits, self.group)
         else:
             out_rows = back

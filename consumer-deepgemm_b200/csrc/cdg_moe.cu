@@ -95,11 +95,13 @@ __global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64
   }
 }
 
-// One warp per routed (token, slot): copies the token's e4m3 row and scales.
+// Bytes of one dispatched row: [e4m3 data H][FP32 scales H/128][int32 local expert][pad to 16].
+__host__ __device__ __forceinline__ int64_t packed_row_bytes(int64_t H) { return (H + 4 * (H / 128) + 4 + 15) / 16 * 16; }
+
+// One warp per routed (token, slot): copies the token's e4m3 row and scales into one packed row.
 __global__ void ep_pack_kernel(const uint8_t* xq, int64_t xq_stride, const float* xs, int64_t xs_stride, const void* ids,
                                int ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t e_per_rank, int64_t H,
-                               const int64_t* send_off, int32_t* fill, uint8_t* out_q, float* out_s, int32_t* out_e,
-                               int32_t* send_index) {
+                               const int64_t* send_off, int32_t* fill, uint8_t* out_rows, int32_t* send_index) {
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= T * topk) return;
@@ -114,28 +116,31 @@ __global__ void ep_pack_kernel(const uint8_t* xq, int64_t xq_stride, const float
   if (lane == 0) send_index[w] = static_cast<int32_t>(row);
   if (row < 0) return;
   const int64_t t = w / topk;
+  uint8_t* out = out_rows + row * packed_row_bytes(H);
   const uint4* src = reinterpret_cast<const uint4*>(xq + t * xq_stride);
-  uint4* dst = reinterpret_cast<uint4*>(out_q + row * H);
+  uint4* dst = reinterpret_cast<uint4*>(out);
   for (int64_t c = lane; c < H / 16; c += 32) dst[c] = src[c];
-  for (int64_t c = lane; c < H / 128; c += 32) out_s[row * (H / 128) + c] = xs[t * xs_stride + c];
-  if (lane == 0) out_e[row] = static_cast<int32_t>(e % e_per_rank);
+  float* out_s = reinterpret_cast<float*>(out + H);
+  for (int64_t c = lane; c < H / 128; c += 32) out_s[c] = xs[t * xs_stride + c];
+  if (lane == 0) *reinterpret_cast<int32_t*>(out + H + 4 * (H / 128)) = static_cast<int32_t>(e % e_per_rank);
 }
 
-// One warp per received row.
-__global__ void ep_permute_kernel(const uint8_t* rq, const float* rs, const int32_t* re, int64_t R, int64_t H,
-                                  const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA,
-                                  int32_t* m_indices, int32_t* perm_pos) {
+// One warp per received packed row.
+__global__ void ep_permute_kernel(const uint8_t* rows, int64_t R, int64_t H, const int64_t* expert_off, int32_t* fill,
+                                  uint8_t* A, float* SA, int32_t* m_indices, int32_t* perm_pos) {
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= R) return;
-  const int e = re[w];
+  const uint8_t* in = rows + w * packed_row_bytes(H);
+  const int e = *reinterpret_cast<const int32_t*>(in + H + 4 * (H / 128));
   int slot = 0;
   if (lane == 0) slot = atomicAdd(&fill[e], 1);
   const int64_t pos = expert_off[e] + __shfl_sync(0xffffffffu, slot, 0);
-  const uint4* src = reinterpret_cast<const uint4*>(rq + w * H);
+  const uint4* src = reinterpret_cast<const uint4*>(in);
   uint4* dst = reinterpret_cast<uint4*>(A + pos * H);
   for (int64_t c = lane; c < H / 16; c += 32) dst[c] = src[c];
-  for (int64_t c = lane; c < H / 128; c += 32) SA[pos * (H / 128) + c] = rs[w * (H / 128) + c];
+  const float* rs = reinterpret_cast<const float*>(in + H);
+  for (int64_t c = lane; c < H / 128; c += 32) SA[pos * (H / 128) + c] = rs[c];
   if (lane == 0) {
     m_indices[pos] = e;
     perm_pos[w] = static_cast<int32_t>(pos);
@@ -210,34 +215,35 @@ int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, 
   return cdg::launched();
 }
 
+int64_t cdg_ep_row_bytes(int64_t H) { return H > 0 && H % 128 == 0 ? cdg::packed_row_bytes(H) : 0; }
+
 int cdg_ep_pack(const uint8_t* xq, int64_t xq_stride, const float* xs, int64_t xs_stride, const void* topk_ids,
                 int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H,
-                const int64_t* send_off, int32_t* fill, uint8_t* out_q, float* out_s, int32_t* out_e,
-                int32_t* send_index, cdg_stream_t stream) {
+                const int64_t* send_off, int32_t* fill, uint8_t* out_rows, int32_t* send_index, cdg_stream_t stream) {
   if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || E % ranks || H <= 0 || H % 128) return CDG_ERR_INVALID_ARGUMENT;
   if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
-  if (reinterpret_cast<uintptr_t>(xq) % 16 || xq_stride % 16 || reinterpret_cast<uintptr_t>(out_q) % 16)
+  if (reinterpret_cast<uintptr_t>(xq) % 16 || xq_stride % 16 || reinterpret_cast<uintptr_t>(out_rows) % 16)
     return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(fill, 0, ranks * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (T == 0) return CDG_OK;
   cdg::ep_pack_kernel<<<cdg::warp_grid(T * topk), 256, 0, st>>>(xq, xq_stride, xs, xs_stride, topk_ids, ids_dtype, T,
-                                                                topk, E, E / ranks, H, send_off, fill, out_q, out_s,
-                                                                out_e, send_index);
+                                                                topk, E, E / ranks, H, send_off, fill, out_rows,
+                                                                send_index);
   return cdg::launched();
 }
 
-int cdg_ep_permute(const uint8_t* recv_q, const float* recv_s, const int32_t* recv_e, int64_t R, int64_t H,
-                   int64_t E_local, const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA,
-                   int32_t* m_indices, int64_t M_pad, int32_t* perm_pos, cdg_stream_t stream) {
+int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_local, const int64_t* expert_off,
+                   int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+                   cdg_stream_t stream) {
   if (R < 0 || H <= 0 || H % 128 || E_local <= 0 || M_pad < 0) return CDG_ERR_INVALID_ARGUMENT;
-  if (reinterpret_cast<uintptr_t>(recv_q) % 16 || reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
+  if (reinterpret_cast<uintptr_t>(recv_rows) % 16 || reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (R == 0) return CDG_OK;
-  cdg::ep_permute_kernel<<<cdg::warp_grid(R), 256, 0, st>>>(recv_q, recv_s, recv_e, R, H, expert_off, fill, A, SA,
-                                                            m_indices, perm_pos);
+  cdg::ep_permute_kernel<<<cdg::warp_grid(R), 256, 0, st>>>(recv_rows, R, H, expert_off, fill, A, SA, m_indices,
+                                                            perm_pos);
   return cdg::launched();
 }
 

@@ -216,7 +216,7 @@ torch::Tensor ep_count(const torch::Tensor& ids, int64_t E) {
   return cnt;
 }
 
-// Returns (rows e4m3 [R, H], scales [R, H/128], local expert ids [R], send_index [T*topk]).
+// Returns (packed rows uint8 [R, cdg_ep_row_bytes(H)], send_index [T*topk]).
 std::vector<torch::Tensor> ep_pack(const torch::Tensor& xq, const torch::Tensor& xs, const torch::Tensor& ids,
                                    int64_t E, int64_t ranks, const torch::Tensor& send_off, int64_t rows) {
   TORCH_CHECK(xq.is_cuda() && xq.dim() == 2 && xq.is_contiguous(), "xq must be contiguous [T, H]");
@@ -224,37 +224,35 @@ std::vector<torch::Tensor> ep_pack(const torch::Tensor& xq, const torch::Tensor&
   TORCH_CHECK(send_off.scalar_type() == torch::kInt64 && send_off.numel() == ranks, "send_off must be int64 [ranks]");
   const c10::cuda::CUDAGuard guard(xq.device());
   const int64_t T = xq.size(0), H = xq.size(1), topk = ids.size(1);
-  auto out_q = torch::empty({rows, H}, xq.options());
-  auto out_s = torch::empty({rows, H / 128}, xs.options());
-  auto out_e = torch::empty({rows}, ids.options().dtype(torch::kInt32));
+  auto out = torch::empty({rows, cdg_ep_row_bytes(H)}, xq.options().dtype(torch::kUInt8));
   auto send_index = torch::empty({T * topk}, ids.options().dtype(torch::kInt32));
   auto fill = torch::empty({ranks}, ids.options().dtype(torch::kInt32));
   check_status(cdg_ep_pack(reinterpret_cast<const uint8_t*>(xq.data_ptr()), H, xs.data_ptr<float>(), H / 128,
                            ids.data_ptr(), dtype_code(ids), T, topk, E, ranks, H, send_off.data_ptr<int64_t>(),
-                           fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(out_q.data_ptr()),
-                           out_s.data_ptr<float>(), out_e.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(),
+                           fill.data_ptr<int32_t>(), out.data_ptr<uint8_t>(), send_index.data_ptr<int32_t>(),
                            cur_stream(xq)),
                "ep_pack");
-  return {out_q, out_s, out_e, send_index};
+  return {out, send_index};
 }
 
 // Returns (A e4m3 [M_pad, H], SA [M_pad, H/128], m_indices [M_pad], perm_pos [R]).
-std::vector<torch::Tensor> ep_permute(const torch::Tensor& rq, const torch::Tensor& rs, const torch::Tensor& re,
-                                      int64_t E_local, const torch::Tensor& expert_off, int64_t M_pad) {
-  TORCH_CHECK(rq.is_cuda() && rq.dim() == 2 && rq.is_contiguous() && rs.is_contiguous() && re.is_contiguous(),
-              "received rows must be contiguous");
+std::vector<torch::Tensor> ep_permute(const torch::Tensor& rows, int64_t H, int64_t E_local,
+                                      const torch::Tensor& expert_off, int64_t M_pad) {
+  TORCH_CHECK(rows.is_cuda() && rows.dim() == 2 && rows.is_contiguous() && rows.scalar_type() == torch::kUInt8 &&
+                  rows.size(1) == cdg_ep_row_bytes(H),
+              "received rows must be contiguous packed rows");
   TORCH_CHECK(expert_off.scalar_type() == torch::kInt64 && expert_off.numel() == E_local, "expert_off: int64 [E]");
-  const c10::cuda::CUDAGuard guard(rq.device());
-  const int64_t R = rq.size(0), H = rq.size(1);
-  auto A = torch::empty({M_pad, H}, rq.options());
-  auto SA = torch::ones({M_pad, H / 128}, rs.options());
-  auto mi = torch::empty({M_pad}, re.options());
-  auto pos = torch::empty({R}, re.options());
-  auto fill = torch::empty({E_local}, re.options());
-  check_status(cdg_ep_permute(reinterpret_cast<const uint8_t*>(rq.data_ptr()), rs.data_ptr<float>(),
-                              re.data_ptr<int32_t>(), R, H, E_local, expert_off.data_ptr<int64_t>(),
+  const c10::cuda::CUDAGuard guard(rows.device());
+  const int64_t R = rows.size(0);
+  auto i32 = rows.options().dtype(torch::kInt32);
+  auto A = torch::empty({M_pad, H}, rows.options().dtype(torch::kFloat8_e4m3fn));
+  auto SA = torch::ones({M_pad, H / 128}, rows.options().dtype(torch::kFloat32));
+  auto mi = torch::empty({M_pad}, i32);
+  auto pos = torch::empty({R}, i32);
+  auto fill = torch::empty({E_local}, i32);
+  check_status(cdg_ep_permute(rows.data_ptr<uint8_t>(), R, H, E_local, expert_off.data_ptr<int64_t>(),
                               fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()), SA.data_ptr<float>(),
-                              mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(), cur_stream(rq)),
+                              mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(), cur_stream(rows)),
                "ep_permute");
   return {A, SA, mi, pos};
 }
@@ -306,8 +304,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_count", &ep_count, py::arg("topk_ids"), py::arg("num_experts"));
   m.def("ep_pack", &ep_pack, py::arg("xq"), py::arg("xs"), py::arg("topk_ids"), py::arg("num_experts"),
         py::arg("ranks"), py::arg("send_off"), py::arg("rows"));
-  m.def("ep_permute", &ep_permute, py::arg("rq"), py::arg("rs"), py::arg("re"), py::arg("local_experts"),
+  m.def("ep_permute", &ep_permute, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("expert_off"), py::arg("m_pad"));
+  m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
   m.def("ep_unpermute", &ep_unpermute, py::arg("y"), py::arg("perm_pos"));
   m.def("ep_combine", &ep_combine, py::arg("rows"), py::arg("send_index"), py::arg("topk_w"));
 }

@@ -212,21 +212,25 @@ int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t
 /* counts[e] = number of entries of topk_ids (n of them, int32 or int64) equal to e, e in [0, E). */
 int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, int32_t* counts, cdg_stream_t stream);
 
-/* Send buffer of expert parallelism: every (token t, slot j) with expert e in [0, E) copies
- * token t's e4m3 row and scales to a row of destination rank e / (E / ranks), starting at
- * send_off[dest]; out_e gets the expert's local id e % (E / ranks); send_index[t*topk + j]
- * is that row (-1 for skipped slots).  `fill` is [ranks] scratch. */
+/* Bytes of one dispatched row for hidden size H: [e4m3 data H][FP32 scales H/128]
+ * [int32 local expert id], padded to 16 (0 for an invalid H). */
+int64_t cdg_ep_row_bytes(int64_t H);
+
+/* Send buffer of expert parallelism: every (token t, slot j) with expert e in [0, E) writes
+ * token t's e4m3 row, its scales and the expert's local id e % (E / ranks) as one packed row
+ * (cdg_ep_row_bytes) of destination rank e / (E / ranks), rows of a destination starting at
+ * send_off[dest]; send_index[t*topk + j] is that row (-1 for skipped slots).
+ * `fill` is [ranks] scratch. */
 int cdg_ep_pack(const uint8_t* xq, int64_t xq_stride, const float* xs, int64_t xs_stride, const void* topk_ids,
                 int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H,
-                const int64_t* send_off, int32_t* fill, uint8_t* out_q, float* out_s, int32_t* out_e,
-                int32_t* send_index, cdg_stream_t stream);
+                const int64_t* send_off, int32_t* fill, uint8_t* out_rows, int32_t* send_index, cdg_stream_t stream);
 
-/* Received rows -> contiguous layout: row i of local expert e lands in [expert_off[e], +count),
- * expert_off being the 128-aligned offsets; m_indices[M_pad] is -1 except on placed rows;
- * perm_pos[i] is row i's position.  `fill` is [E_local] scratch. */
-int cdg_ep_permute(const uint8_t* recv_q, const float* recv_s, const int32_t* recv_e, int64_t R, int64_t H,
-                   int64_t E_local, const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA,
-                   int32_t* m_indices, int64_t M_pad, int32_t* perm_pos, cdg_stream_t stream);
+/* Received packed rows -> contiguous layout: row i of local expert e lands in
+ * [expert_off[e], +count), expert_off being the 128-aligned offsets; m_indices[M_pad] is -1
+ * except on placed rows; perm_pos[i] is row i's position.  `fill` is [E_local] scratch. */
+int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_local, const int64_t* expert_off,
+                   int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+                   cdg_stream_t stream);
 
 /* out[i, :] = Y[perm_pos[i], :] (BF16 rows of length H). */
 int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R, int64_t H, void* out,

@@ -12,6 +12,11 @@ from deep_gemm.utils.math import per_block_cast_to_fp8
 from oracle import cdg_oracle as oracle
 
 
+def row_bytes(hidden):
+    """Bytes of one dispatched row: e4m3 data, FP32 scale per 128 columns, int32 expert id, padded to 16."""
+    return (hidden + 4 * (hidden // 128) + 4 + 15) // 16 * 16
+
+
 class TorchRefOps:
     def quant(self, x):
         return per_block_cast_to_fp8(x.float())
@@ -22,11 +27,11 @@ class TorchRefOps:
         return torch.bincount(ids, minlength=num_experts).to(torch.int32)
 
     def pack(self, xq, xs, topk_ids, num_experts, ranks, send_off, rows):
+        """Packed rows [rows, row_bytes(H)] uint8: e4m3 data | FP32 scales | int32 local expert."""
         T, k = topk_ids.shape
+        H = xq.shape[1]
         per_rank = num_experts // ranks
-        out_q = torch.empty(rows, xq.shape[1], dtype=xq.dtype)
-        out_s = torch.empty(rows, xs.shape[1], dtype=xs.dtype)
-        out_e = torch.empty(rows, dtype=torch.int32)
+        out = torch.zeros(rows, row_bytes(H), dtype=torch.uint8)
         send_index = torch.full((T * k,), -1, dtype=torch.int32)
         fill = [0] * ranks
         for i, e in enumerate(topk_ids.flatten().tolist()):
@@ -35,20 +40,27 @@ class TorchRefOps:
             d = e // per_rank
             r = int(send_off[d]) + fill[d]
             fill[d] += 1
-            out_q[r], out_s[r], out_e[r] = xq[i // k], xs[i // k], e % per_rank
+            out[r, :H] = xq[i // k].view(torch.uint8)
+            out[r, H:H + 4 * (H // 128)] = xs[i // k].contiguous().view(torch.uint8)
+            out[r, H + 4 * (H // 128):H + 4 * (H // 128) + 4] = torch.tensor([e % per_rank], dtype=torch.int32).view(
+                torch.uint8)
             send_index[i] = r
-        return out_q, out_s, out_e, send_index
+        return out, send_index
 
-    def permute(self, rq, rs, re, local_experts, expert_off, m_pad):
-        a = torch.zeros(m_pad, rq.shape[1], dtype=rq.dtype)
-        sa = torch.ones(m_pad, rs.shape[1], dtype=rs.dtype)
+    def permute(self, rows, hidden, local_experts, expert_off, m_pad):
+        H, nkb = hidden, hidden // 128
+        a = torch.zeros(m_pad, H, dtype=torch.float8_e4m3fn)
+        sa = torch.ones(m_pad, nkb, dtype=torch.float32)
         m_indices = torch.full((m_pad,), -1, dtype=torch.int32)
-        pos = torch.empty(rq.shape[0], dtype=torch.int32)
+        pos = torch.empty(rows.shape[0], dtype=torch.int32)
         fill = [0] * local_experts
-        for i, e in enumerate(re.tolist()):
+        for i in range(rows.shape[0]):
+            e = int(rows[i, H + 4 * nkb:H + 4 * nkb + 4].contiguous().view(torch.int32)[0])
             p = int(expert_off[e]) + fill[e]
             fill[e] += 1
-            a[p], sa[p], m_indices[p], pos[i] = rq[i], rs[i], e, p
+            a[p] = rows[i, :H].contiguous().view(torch.float8_e4m3fn)
+            sa[p] = rows[i, H:H + 4 * nkb].contiguous().view(torch.float32)
+            m_indices[p], pos[i] = e, p
         return a, sa, m_indices, pos
 
     def gemm(self, a, sa, w, w_sf, m_indices):

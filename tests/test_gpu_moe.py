@@ -17,7 +17,7 @@ import sys
 import pytest
 import torch
 
-from moe_ref import TorchRefOps, make_layer_inputs
+from moe_ref import TorchRefOps, make_layer_inputs, row_bytes
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -65,22 +65,29 @@ def test_dispatch_and_permute_are_exact():
     ref_counts = torch.bincount(ids[ids >= 0].long(), minlength=E)
     assert torch.equal(counts.long(), ref_counts)
     rows = int(counts.sum())
-    sq, ss, se, send_index = C.ep_pack(xq, xs, ids.to(DEV), E, 1, torch.zeros(1, dtype=torch.int64, device=DEV), rows)
+    sent, send_index = C.ep_pack(xq, xs, ids.to(DEV), E, 1, torch.zeros(1, dtype=torch.int64, device=DEV), rows)
+    nkb = H // 128
+    assert sent.shape == (rows, C.ep_row_bytes(H)) and C.ep_row_bytes(H) == row_bytes(H)
+    sent_h = sent.cpu()
     si = send_index.cpu()
     assert int(si[3 * k + 1]) == -1 and int((si >= 0).sum()) == rows
     flat = ids.flatten()
+    xq_h, xs_h = xq.cpu().view(torch.uint8), xs.cpu()
+    row_e = sent_h[:, H + 4 * nkb:H + 4 * nkb + 4].contiguous().view(torch.int32).flatten()
     for i in range(T * k):
         if si[i] >= 0:
             r = int(si[i])
-            assert torch.equal(sq[r].cpu().view(torch.uint8), xq[i // k].cpu().view(torch.uint8))
-            assert int(se[r]) == int(flat[i])
+            assert torch.equal(sent_h[r, :H], xq_h[i // k])
+            assert torch.equal(sent_h[r, H:H + 4 * nkb].contiguous().view(torch.float32), xs_h[i // k])
+            assert int(row_e[r]) == int(flat[i])
     aligned = (ref_counts + 127) // 128 * 128
     off = (torch.cumsum(aligned, 0) - aligned).to(DEV)
     m_pad = int(aligned.sum())
-    a, sa, mi, pos = C.ep_permute(sq, ss, se, E, off, m_pad)
+    a, sa, mi, pos = C.ep_permute(sent, H, E, off, m_pad)
     pos, mi = pos.cpu().long(), mi.cpu()
-    assert torch.equal(a.cpu().view(torch.uint8)[pos], sq.cpu().view(torch.uint8))
-    assert torch.equal(mi[pos], se.cpu())
+    assert torch.equal(a.cpu().view(torch.uint8)[pos], sent_h[:, :H])
+    assert torch.equal(sa.cpu()[pos], sent_h[:, H:H + 4 * nkb].contiguous().view(torch.float32))
+    assert torch.equal(mi[pos], row_e)
     assert int((mi >= 0).sum()) == rows
     for e in range(E):
         seg = mi[int(off[e]):int(off[e]) + int(aligned[e])]
