@@ -1,12 +1,13 @@
 """Consumer-DeepGEMM for B200: the grouped FP8 x MXFP4 MoE GEMM on sm_100a.
 
 Drop-in for the reference's hot path (``import consumer_deep_gemm as deep_gemm``):
-``m_grouped_fp8_fp4_gemm_nt_contiguous`` with the same arguments and tensor
+``m_grouped_fp8_fp4_gemm_nt_contiguous`` (and its masked-layout sibling
+``m_grouped_fp8_fp4_gemm_nt_masked``) with the same arguments and tensor
 layouts, plus the layout and runtime hooks vLLM calls around it
 (consumer_deep_gemm/__init__.py:11-48 of the reference, restricted to that path).
 """
 
-from .gemm import m_grouped_fp8_fp4_gemm_nt_contiguous
+from .gemm import m_grouped_fp8_fp4_gemm_nt_contiguous, m_grouped_fp8_fp4_gemm_nt_masked
 from .layout import (
     get_mk_alignment_for_contiguous_layout,
     get_mn_major_tma_aligned_tensor,
@@ -22,6 +23,7 @@ __version__ = "0.2.0"
 
 __all__ = [
     "m_grouped_fp8_fp4_gemm_nt_contiguous",
+    "m_grouped_fp8_fp4_gemm_nt_masked",
     "transform_sf_into_required_layout",
     "get_mn_major_tma_aligned_tensor",
     "get_mk_alignment_for_contiguous_layout",

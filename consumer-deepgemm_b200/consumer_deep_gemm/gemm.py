@@ -28,7 +28,7 @@ import torch
 
 from . import native
 
-__all__ = ["m_grouped_fp8_fp4_gemm_nt_contiguous"]
+__all__ = ["m_grouped_fp8_fp4_gemm_nt_contiguous", "m_grouped_fp8_fp4_gemm_nt_masked"]
 
 _FLOAT_SCALES = (torch.float32, torch.float16, torch.bfloat16, torch.float64)
 
@@ -104,3 +104,51 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs) -> N
     x, sa, bt, bs, d, ids = _normalize(a, b, d, m_indices)
     flags = 1 if kwargs.get("_force_exact_path") else 0
     native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags)
+
+
+def _flatten_groups(t):
+    """[G, S, ...] -> [G*S, ...] (a view when the tensor allows one)."""
+    if t is None or t.dim() != 3:
+        return t
+    return t.reshape(t.shape[0] * t.shape[1], t.shape[2])
+
+
+def m_grouped_fp8_fp4_gemm_nt_masked(a, b, d, masked_m=None, **kwargs) -> None:
+    """M-grouped FP8 x FP4 GEMM, masked layout (reference: consumer_deep_gemm/gemm.py:529-551).
+
+    ``a`` holds G blocks of S rows, as ``[G*S, K]`` (the reference's form) or
+    ``[G, S, K]``; ``d`` is ``[G*S, N]`` or ``[G, S, N]`` alike.  Group g multiplies
+    rows ``[g*S, g*S + masked_m[g])`` by ``b[g]``; every other row of ``d`` is 0.
+    With a 2-D ``b`` every row is multiplied by it and ``masked_m`` is not used.
+    ``masked_m`` (int32/int64 ``[G]``) is read on the device, so the call does not
+    synchronise with the host.  ``expected_m`` (a scheduling hint in DeepGEMM's
+    signature) is accepted and not needed.
+    """
+    _check_recipes(kwargs)
+    if isinstance(a, tuple):
+        if len(a) != 2:
+            raise ValueError("a must be a (tensor, scale) tuple")
+        a = (_flatten_groups(a[0]), _flatten_groups(a[1]))
+    else:
+        a = _flatten_groups(a)
+    d2 = d
+    if d.dim() == 3:
+        try:
+            d2 = d.view(d.shape[0] * d.shape[1], d.shape[2])
+        except RuntimeError as exc:
+            raise ValueError("a 3-D d must be viewable as [G*S, N]") from exc
+    single = (b[0] if isinstance(b, tuple) else b).dim() == 2
+    if masked_m is None and not single:
+        raise ValueError("masked_m is required when b has multiple groups")
+    x, sa, bt, bs, d2, _ = _normalize(a, b, d2, masked_m)
+    if single:
+        ids, masked = None, False
+    else:
+        if masked_m.dim() != 1 or masked_m.numel() != bt.shape[0]:
+            raise ValueError(f"masked_m must be [G] with G = {bt.shape[0]}, got {tuple(masked_m.shape)}")
+        if masked_m.dtype not in (torch.int32, torch.int64):
+            masked_m = masked_m.to(torch.int32)
+        ids = masked_m.to(x.device).contiguous()
+        masked = True
+    flags = 1 if kwargs.get("_force_exact_path") else 0
+    native.require().grouped_gemm(x, sa, bt, bs, d2, ids, flags, masked)

@@ -112,6 +112,7 @@ int validate(const cdg_gemm_args* g) {
       if (g->m_indices_len != g->M) return CDG_ERR_INVALID_ARGUMENT;
       break;
     case CDG_INDEX_PSUM:
+    case CDG_INDEX_MASKED:
       if (!g->m_indices || g->m_indices_len != g->E) return CDG_ERR_INVALID_ARGUMENT;
       break;
     default:
@@ -136,9 +137,15 @@ bool fast_path(const cdg_gemm_args* g) {
 
 bool sfw_needs_transform(const cdg_gemm_args* g) { return g->sfb_layout == CDG_SF_ROW_MAJOR; }
 
+TileMap tile_map(const cdg_gemm_args* g) {
+  return g->index_form == CDG_INDEX_MASKED ? TileMap::masked(static_cast<int>(g->M), static_cast<int>(g->E))
+                                           : TileMap::contiguous(static_cast<int>(g->M));
+}
+
 WorkspaceLayout layout_for(const cdg_gemm_args* g) {
   const bool fast = fast_path(g);
-  return WorkspaceLayout::make(g->M, g->K, g->N, g->E, fast, g->index_form == CDG_INDEX_PSUM,
+  return WorkspaceLayout::make(g->M, tile_map(g).tiles(), g->K, g->N, g->E, fast,
+                               g->index_form == CDG_INDEX_PSUM || g->index_form == CDG_INDEX_MASKED,
                                fast && sfw_needs_transform(g));
 }
 
@@ -206,18 +213,26 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   int* ctrl = reinterpret_cast<int*>(ws + wl.ctrl);
   if (cudaMemsetAsync(ctrl, 0, kCtrlWords * 4, stream) != cudaSuccess) return CDG_ERR_CUDA;
 
-  const int64_t nblk = (g->M + 127) / 128;
+  const TileMap tm = tile_map(g);
+  const int64_t nblk = tm.tiles();
   const void* ids = g->index_form == CDG_INDEX_NONE ? nullptr : g->m_indices;
   int ids_dtype = g->m_indices_dtype;
-  if (g->index_form == CDG_INDEX_PSUM) {
+  if (g->index_form == CDG_INDEX_PSUM || g->index_form == CDG_INDEX_MASKED) {
     int32_t* rows = reinterpret_cast<int32_t*>(ws + wl.row_ids);
     const unsigned blocks = static_cast<unsigned>((g->M + 255) / 256);
-    if (ids_dtype == CDG_DTYPE_I64)
-      cdg_psum_rows_kernel<int64_t><<<blocks, 256, 0, stream>>>(static_cast<const int64_t*>(ids),
-                                                                 static_cast<int>(g->E), static_cast<int>(g->M), rows);
-    else
-      cdg_psum_rows_kernel<int32_t><<<blocks, 256, 0, stream>>>(static_cast<const int32_t*>(ids),
-                                                                 static_cast<int>(g->E), static_cast<int>(g->M), rows);
+    const int G = static_cast<int>(g->E), M = static_cast<int>(g->M);
+    if (g->index_form == CDG_INDEX_MASKED) {
+      if (ids_dtype == CDG_DTYPE_I64)
+        cdg_masked_rows_kernel<int64_t><<<blocks, 256, 0, stream>>>(static_cast<const int64_t*>(ids), G,
+                                                                     tm.seg_rows, M, rows);
+      else
+        cdg_masked_rows_kernel<int32_t><<<blocks, 256, 0, stream>>>(static_cast<const int32_t*>(ids), G,
+                                                                     tm.seg_rows, M, rows);
+    } else if (ids_dtype == CDG_DTYPE_I64) {
+      cdg_psum_rows_kernel<int64_t><<<blocks, 256, 0, stream>>>(static_cast<const int64_t*>(ids), G, M, rows);
+    } else {
+      cdg_psum_rows_kernel<int32_t><<<blocks, 256, 0, stream>>>(static_cast<const int32_t*>(ids), G, M, rows);
+    }
     ids = rows;
     ids_dtype = CDG_DTYPE_I32;
   }
@@ -249,6 +264,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ga.K = static_cast<int>(g->K);
   ga.E = static_cast<int>(g->E);
   ga.nblk = static_cast<int>(nblk);
+  ga.tm = tm;
   const size_t generic_smem = static_cast<size_t>(g->K) * 4;
   if (generic_smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
   const int64_t generic_units = nblk * ((g->N + 255) / 256);
@@ -286,6 +302,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.K = static_cast<int>(g->K);
   pa.E = static_cast<int>(g->E);
   pa.nblk = static_cast<int>(nblk);
+  pa.tm = tm;
   pa.hilo = hilo;
   pa.row_exp = row_exp;
   pa.blk_info = blk_info;
@@ -316,6 +333,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.K = static_cast<int>(g->K);
   ka.E = static_cast<int>(g->E);
   ka.nblk = static_cast<int>(nblk);
+  ka.tm = tm;
   ka.status = ctrl + kCtrlStatus;
   ka.zero_list = lists + kClassZero * nblk;
 
@@ -358,6 +376,13 @@ extern "C" {
 
 int cdg_grouped_fp8_fp4_gemm_nt_contiguous(const cdg_gemm_args* args, void* workspace, size_t workspace_bytes,
                                            cdg_stream_t stream) {
+  return cdg::run(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cdg_grouped_fp8_fp4_gemm_nt_masked(const cdg_gemm_args* args, void* workspace, size_t workspace_bytes,
+                                       cdg_stream_t stream) {
+  if (!args || (args->index_form != CDG_INDEX_MASKED && args->index_form != CDG_INDEX_NONE))
+    return CDG_ERR_INVALID_ARGUMENT;
   return cdg::run(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -59,6 +59,25 @@ __global__ void cdg_sf_atom_kernel(const uint8_t* __restrict__ src, int64_t src_
 // [end[g-1], end[g]) with end[-1] = 0).  Later groups win where ranges overlap, as
 // in the reference's per-group index_copy_ (consumer_deep_gemm/gemm.py:318-324, 358-367).
 // =====================================================================================
+// masked form: counts[g] rows of group g start at row g*S (S = M / G); where a count
+// exceeds S the rows run on into the next block and later groups win, as in the
+// reference's sequential per-group copies (consumer_deep_gemm/gemm.py:541-551).
+template <typename IdT>
+__global__ void cdg_masked_rows_kernel(const IdT* __restrict__ counts, int G, int S, int M,
+                                       int32_t* __restrict__ row_ids) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= M) return;
+  int32_t id = -1;
+  const int top = S > 0 ? min(G - 1, r / S) : G - 1;
+  for (int g = top; g >= 0; --g) {
+    if (static_cast<int64_t>(r) < static_cast<int64_t>(g) * S + static_cast<int64_t>(counts[g])) {
+      id = g;
+      break;
+    }
+  }
+  row_ids[r] = id;
+}
+
 template <typename IdT>
 __global__ void cdg_psum_rows_kernel(const IdT* __restrict__ ends, int G, int M, int32_t* __restrict__ row_ids) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
@@ -93,6 +112,7 @@ struct PrepArgs {
   const void* ids;  // per-row group ids (int32 or int64)
   int M, K, E;
   int nblk;
+  TileMap tm;              // rows of each block
   uint8_t* hilo;           // [2][nblk*128][K]
   int32_t* row_exp;        // [nblk*128] exponent E of each routed row's activation planes
   int4* blk_info;          // [nblk] {expert (-1 none, -2 several), rows spanned, class, 0}
@@ -138,11 +158,13 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     s_max_row = -1;
   }
   if (tid < 4) s_mask[tid] = 0u;
+  int row0, nrows;
+  p.tm.rows(b, row0, nrows);
   __syncthreads();
   if (tid < 128) {
-    const int r = b * 128 + tid;
+    const int r = row0 + tid;
     int id = -1;
-    if (r < p.M) {
+    if (tid < nrows) {
       const int64_t v = load_id(p.ids, sizeof(IdT) == 8, r);
       id = (v >= 0 && v < p.E) ? static_cast<int>(v) : -1;
     }
@@ -180,7 +202,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     //     this CTA's K blocks.
     if (tid < ntok) {
       int emax = 0;
-      const int r = b * 128 + tid;
+      const int r = row0 + tid;
       if (s_id[tid] == expert) {
         float smax = 0.0f;
         for (int kb = 0; kb < kb_count; ++kb) {
@@ -190,12 +212,12 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
         if (smax > 0.0f) frexpf(smax, &emax);
       }
       s_exp[tid] = emax;
-      if (blockIdx.y == 0) p.row_exp[r] = emax;
+      if (blockIdx.y == 0) p.row_exp[b * 128 + tid] = emax;
     }
     for (int it = tid; it < ntok * kbn; it += blockDim.x) {
       const int rr = it / kbn;
       const int kl = it - rr * kbn;
-      const int r = b * 128 + rr;
+      const int r = row0 + rr;
       s_scale[rr][kl] = s_id[rr] == expert
           ? __bfloat162float(__float2bfloat16_rn(p.sa[r * p.sa_stride_m + (kb0 + kl) * p.sa_stride_k]))
           : 0.0f;
@@ -208,7 +230,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       const int rr = it / chunks;
       const int c = it - rr * chunks;
       const int kl = c >> 3;
-      const int r = b * 128 + rr;
+      const int r = row0 + rr;
       const int64_t col = static_cast<int64_t>(kb0) * 128 + c * 16;
       uint4 hi4 = make_uint4(0, 0, 0, 0), lo4 = make_uint4(0, 0, 0, 0);
       if (s_id[rr] == expert) {
@@ -227,7 +249,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
           lb[i] = f32_to_e4m3(v - e4m3_to_f32(h));
         }
       }
-      uint8_t* dst = p.hilo + static_cast<int64_t>(r) * K + col;
+      uint8_t* dst = p.hilo + (static_cast<int64_t>(b) * 128 + rr) * K + col;
       *reinterpret_cast<uint4*>(dst) = hi4;
       *reinterpret_cast<uint4*>(dst + plane) = lo4;
     }
@@ -310,6 +332,7 @@ struct GemmArgs {
   __nv_bfloat16* d;
   int64_t d_row_stride;
   int M, N, K, E, nblk;
+  TileMap tm;            // rows of each block
   int count_slot;        // ctrl index of this class's block count
   int do_zero_blocks;
   int* status;
@@ -469,7 +492,8 @@ __global__ void __launch_bounds__(256, 1)
       const bool regular = t < reg_tiles;
       const int blk = regular ? p.list[t / n_tiles] : p.zero_list[(t - reg_tiles) / n_tiles];
       const int nt = t % n_tiles;
-      const int row0 = blk * 128;
+      int row0, nrows;
+      p.tm.rows(blk, row0, nrows);
       int zero_from = 0;
       if (regular) {
         const int4 info = p.blk_info[blk];
@@ -484,7 +508,7 @@ __global__ void __launch_bounds__(256, 1)
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
         for (int j0 = 0; j0 < ntok; j0 += 16) {
           // 2^E of the chunk's 16 rows: lane j (mod 16) loads row j's exponent, shuffles share it
-          const int re = min(row0 + j0 + (lane & 15), p.M - 1);
+          const int re = blk * 128 + j0 + (lane & 15);
           const float my_scale = __uint_as_float(static_cast<uint32_t>(min(max(__ldg(p.row_exp + re) + 127, 1), 254)) << 23);
           uint32_t v[16];
           tmem_ld16(taddr + j0, v);
@@ -503,7 +527,7 @@ __global__ void __launch_bounds__(256, 1)
             const int rb = j0 + j;
             const uint32_t word = rb < 32 ? mask.x : rb < 64 ? mask.y : rb < 96 ? mask.z : mask.w;
             const float sc = __shfl_sync(0xffffffffu, my_scale, j);
-            if (r < p.M) {
+            if (rb < nrows) {
               const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
               p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
             }
@@ -514,7 +538,7 @@ __global__ void __launch_bounds__(256, 1)
         zero_from = ntok;
       }
       // zero rows [zero_from, 128) of this block, columns [nt*128, nt*128+128), 16 B per store
-      const int rows = min(128, p.M - row0) - zero_from;
+      const int rows = nrows - zero_from;
       const uint4 z = make_uint4(0, 0, 0, 0);
       for (int c = tid; c < rows * 16; c += 128) {
         const int r = row0 + zero_from + (c >> 4);
@@ -562,6 +586,7 @@ struct GenericArgs {
   int64_t d_row_stride;
   int M, N, K, E;
   int nblk;
+  TileMap tm;        // rows of each block
   const int* list;   // nullptr: every block; else the listed blocks
   const int* count;  // number of listed blocks (device)
 };
@@ -584,7 +609,9 @@ __global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
     const int bi = u / n_chunks;
     const int blk = p.list ? p.list[bi] : bi;
     const int n = (u % n_chunks) * 256 + threadIdx.x;
-    for (int r = blk * 128; r < min(p.M, blk * 128 + 128); ++r) {
+    int row0, nrows;
+    p.tm.rows(blk, row0, nrows);
+    for (int r = row0; r < row0 + nrows; ++r) {
       const int64_t id = load_id(p.ids, p.ids_is_64, r);
       const bool valid = id >= 0 && id < p.E;
       if (valid) {

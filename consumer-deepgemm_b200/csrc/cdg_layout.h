@@ -30,13 +30,54 @@ enum : int {
 
 constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Row ranges of the 128-row work tiles ("blocks").  The rows of A form `nseg`
+// segments of `seg_rows` rows (the per-group blocks of the masked layout; a single
+// segment of all M rows otherwise), each cut into ceil(seg_rows / 128) tiles that
+// never cross a segment boundary, followed by the rows past the last segment in
+// plain 128-row tiles.  Block b of the kernels covers rows [row0, row0 + n) of A
+// and D; its activation planes and row exponents stay at rows [b*128, b*128 + n).
+struct TileMap {
+  int M = 0, seg_rows = 0, tiles_per_seg = 0, nseg = 0;
+
+  __host__ __device__ static TileMap contiguous(int M) {
+    TileMap t;
+    t.M = M;
+    t.seg_rows = M;
+    t.tiles_per_seg = (M + 127) / 128;
+    t.nseg = M > 0 ? 1 : 0;
+    return t;
+  }
+  // M rows in G groups of M / G rows each (rows past G * (M / G) form the tail).
+  __host__ __device__ static TileMap masked(int M, int G) {
+    TileMap t;
+    t.M = M;
+    t.seg_rows = G > 0 ? M / G : 0;
+    t.tiles_per_seg = (t.seg_rows + 127) / 128;
+    t.nseg = t.seg_rows > 0 ? G : 0;
+    return t;
+  }
+  __host__ __device__ int tail_start() const { return nseg * seg_rows; }
+  __host__ __device__ int tiles() const { return nseg * tiles_per_seg + (M - tail_start() + 127) / 128; }
+  __host__ __device__ void rows(int b, int& row0, int& n) const {
+    const int seg_tiles = nseg * tiles_per_seg;
+    if (b < seg_tiles) {
+      const int s = b / tiles_per_seg, j = b - s * tiles_per_seg;
+      row0 = s * seg_rows + j * 128;
+      n = seg_rows - j * 128 < 128 ? seg_rows - j * 128 : 128;
+    } else {
+      row0 = tail_start() + (b - seg_tiles) * 128;
+      n = M - row0 < 128 ? M - row0 : 128;
+    }
+  }
+};
+
 // Workspace regions of one GEMM call.
 struct WorkspaceLayout {
   size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, row_ids = 0, row_exp = 0, hilo = 0, sfw_atoms = 0, total = 0;
 
-  static WorkspaceLayout make(int64_t M, int64_t K, int64_t N, int64_t E, bool fast, bool psum, bool sfw_from_rows) {
+  static WorkspaceLayout make(int64_t M, int64_t nblk, int64_t K, int64_t N, int64_t E, bool fast, bool row_ids,
+                              bool sfw_from_rows) {
     WorkspaceLayout w;
-    const int64_t nblk = (M + 127) / 128;
     size_t off = 0;
     w.ctrl = off;
     off = align_up(off + kCtrlWords * 4, 1024);
@@ -46,7 +87,7 @@ struct WorkspaceLayout {
     off = align_up(off + static_cast<size_t>(nblk) * 16, 1024);
     w.lists = off;
     off = align_up(off + static_cast<size_t>(nblk) * 4 * kNumClasses, 1024);
-    if (psum) {
+    if (row_ids) {
       w.row_ids = off;
       off = align_up(off + static_cast<size_t>(M) * 4, 1024);
     }

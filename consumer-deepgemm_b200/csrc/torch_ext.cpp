@@ -49,7 +49,7 @@ void check_cuda(const torch::Tensor& t, const char* name, const torch::Device& d
 //   sfb: [E,N,K/32] uint8/f32 or int32 atoms [E,N/128,K/128,128];  d: [M,N] bf16/f32
 cdg_gemm_args make_args(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
                         const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids,
-                        int64_t flags) {
+                        int64_t flags, bool masked = false) {
   const auto dev = a.device();
   check_cuda(a, "a", dev);
   check_cuda(b, "b", dev);
@@ -113,11 +113,15 @@ cdg_gemm_args make_args(const torch::Tensor& a, const c10::optional<torch::Tenso
     g.m_indices_dtype = dtype_code(t);
     TORCH_CHECK_VALUE(g.m_indices_dtype == CDG_DTYPE_I32 || g.m_indices_dtype == CDG_DTYPE_I64,
                       "m_indices must be int32/int64, got ", t.scalar_type());
-    TORCH_CHECK_VALUE(t.numel() == M || t.numel() == E, "m_indices length must be M or G, got ", t.numel(), ", M=", M,
-                      ", G=", E);
+    if (masked) {
+      TORCH_CHECK_VALUE(t.numel() == E, "masked_m length must be G, got ", t.numel(), ", G=", E);
+    } else {
+      TORCH_CHECK_VALUE(t.numel() == M || t.numel() == E, "m_indices length must be M or G, got ", t.numel(),
+                        ", M=", M, ", G=", E);
+    }
     g.m_indices = t.data_ptr();
     g.m_indices_len = t.numel();
-    g.index_form = t.numel() == M ? CDG_INDEX_PER_ROW : CDG_INDEX_PSUM;
+    g.index_form = masked ? CDG_INDEX_MASKED : t.numel() == M ? CDG_INDEX_PER_ROW : CDG_INDEX_PSUM;
   } else {
     TORCH_CHECK_VALUE(E == 1, "m_indices is required when b has multiple groups");
     g.index_form = CDG_INDEX_NONE;
@@ -137,8 +141,8 @@ cdg_gemm_args make_args(const torch::Tensor& a, const c10::optional<torch::Tenso
 
 void grouped_gemm(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
                   const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids,
-                  int64_t flags) {
-  const cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, flags);
+                  int64_t flags, bool masked) {
+  const cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, flags, masked);
   const c10::cuda::CUDAGuard guard(a.device());
   const size_t ws_bytes = cdg_grouped_fp8_fp4_workspace_bytes(&g);
   TORCH_CHECK(ws_bytes > 0, "invalid GEMM arguments");
@@ -146,8 +150,12 @@ void grouped_gemm(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa
   auto ws = torch::empty({static_cast<int64_t>(ws_bytes + 1024)}, a.options().dtype(torch::kUInt8));
   auto* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 1023) & ~uintptr_t(1023));
   const auto stream = at::cuda::getCurrentCUDAStream(a.get_device()).stream();
-  check_status(cdg_grouped_fp8_fp4_gemm_nt_contiguous(&g, base, ws_bytes, reinterpret_cast<cdg_stream_t>(stream)),
-               "m_grouped_fp8_fp4_gemm_nt_contiguous");
+  if (masked)
+    check_status(cdg_grouped_fp8_fp4_gemm_nt_masked(&g, base, ws_bytes, reinterpret_cast<cdg_stream_t>(stream)),
+                 "m_grouped_fp8_fp4_gemm_nt_masked");
+  else
+    check_status(cdg_grouped_fp8_fp4_gemm_nt_contiguous(&g, base, ws_bytes, reinterpret_cast<cdg_stream_t>(stream)),
+                 "m_grouped_fp8_fp4_gemm_nt_contiguous");
 }
 
 int64_t can_implement(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
@@ -288,7 +296,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("build_info", []() { return std::string(cdg_build_info()); });
   m.def("mk_alignment_for_contiguous_layout", []() { return cdg_mk_alignment_for_contiguous_layout(); });
   m.def("grouped_gemm", &grouped_gemm, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
-        py::arg("m_indices"), py::arg("flags") = 0);
+        py::arg("m_indices"), py::arg("flags") = 0, py::arg("masked") = false);
   m.def("can_implement", &can_implement, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
         py::arg("m_indices"));
   m.def("transform_sf_atoms", &transform_sf_atoms, py::arg("sf"));

@@ -65,7 +65,10 @@ typedef enum cdg_sf_layout {
 typedef enum cdg_index_form {
   CDG_INDEX_PER_ROW = 0, /* one group id per row of A, -1 (any id outside [0,E)) = no group */
   CDG_INDEX_PSUM = 1,    /* E cumulative row ends: group g owns rows [end[g-1], end[g]) */
-  CDG_INDEX_NONE = 2     /* no ids: E must be 1 and every row belongs to group 0 */
+  CDG_INDEX_NONE = 2,    /* no ids: E must be 1 and every row belongs to group 0 */
+  CDG_INDEX_MASKED = 3   /* E per-group row counts (masked_m): with S = M / E, group g owns rows
+                            [g*S, g*S + count[g]); a count above S runs on into the following rows,
+                            later groups winning; every other row of D is written as 0 */
 } cdg_index_form;
 
 /*
@@ -113,6 +116,16 @@ typedef struct cdg_gemm_args {
  * (csrc/cutlass_mxfp8_mxfp4_probe.cu:444-614, exported at :660-673). */
 int cdg_grouped_fp8_fp4_gemm_nt_contiguous(const cdg_gemm_args* args, void* workspace, size_t workspace_bytes,
                                            cdg_stream_t stream);
+
+/* Grouped FP8 x MXFP4 GEMM, masked layout: args->index_form is CDG_INDEX_MASKED with
+ * m_indices = masked_m [E] (int32/int64, on the device; read by the kernels, no host
+ * synchronisation), or CDG_INDEX_NONE for one group over all rows.  A and D are the
+ * [E * S, K] / [E * S, N] row-major views of the [E, S, ...] tensors.  Blocks of 128
+ * rows never cross a group's block of S rows.  Workspace as for the contiguous entry
+ * (cdg_grouped_fp8_fp4_workspace_bytes with the same args).
+ * Replaces m_grouped_fp8_fp4_gemm_nt_masked (consumer_deep_gemm/gemm.py:529-551). */
+int cdg_grouped_fp8_fp4_gemm_nt_masked(const cdg_gemm_args* args, void* workspace, size_t workspace_bytes,
+                                       cdg_stream_t stream);
 
 /* Workspace the call above needs for these arguments (0 on invalid arguments).
  * Replaces the launcher's process-global workspace and segment buffers

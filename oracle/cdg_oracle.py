@@ -180,6 +180,39 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d: torch.Tensor, m_indices=None) 
         d.index_copy_(0, rows, res.to(d.dtype))
 
 
+def m_grouped_fp8_fp4_gemm_nt_masked(a, b, d: torch.Tensor, masked_m=None) -> None:
+    """Oracle for ``m_grouped_fp8_fp4_gemm_nt_masked`` (gemm.py:529-551).
+
+    ``a`` is ``[G*S, K]`` (G = number of weight groups, S = rows // G); group g
+    multiplies rows ``[g*S, g*S + masked_m[g])`` by ``b[g]``, groups in order, so a
+    count above S overwrites the next block's rows until that group writes its own;
+    every other row of ``d`` is 0.  A 2-D ``b`` (or no ``masked_m``) is one plain
+    product over all rows (gemm.py:534-537).
+    """
+    a_deq = _dequant_fp8_arg(a)
+    b_tensor, b_scale = b if isinstance(b, tuple) else (b, None)
+    if b_tensor.dtype == torch.int8:
+        b_tensor = b_tensor.view(torch.uint8)
+    if b_tensor.dim() != 3 or masked_m is None:
+        w = dequant_fp4_block(b_tensor, b_scale)
+        d.copy_(torch.mm(a_deq.to(torch.float32), w.to(torch.float32).t()))
+        return
+    num_groups = b_tensor.shape[0]
+    block = a_deq.shape[0] // num_groups
+    counts = [int(c) for c in masked_m.to("cpu").tolist()]
+    d.zero_()
+    for g in range(num_groups):
+        if counts[g] <= 0:
+            continue
+        start = g * block
+        sg = None
+        if b_scale is not None:
+            sg = b_scale[g] if b_scale.dim() == 3 else b_scale
+        w = dequant_fp4_block(b_tensor[g], sg)
+        res = torch.mm(a_deq[start:start + counts[g]].to(torch.float32), w.to(torch.float32).t())
+        d[start:start + counts[g]].copy_(res.to(d.dtype))
+
+
 def reference_fp64(a, b, m_indices) -> np.ndarray:
     """Exact product of the quantised operands in FP64 (no BF16 rounding of ``a``).
 

@@ -19,7 +19,7 @@ HEADER = os.path.join(REPO, "include", "cdg_b200.h")
 CDG_OK = 0
 DT = {"e4m3": 1, "bf16": 2, "f32": 3, "ue8m0": 4, "i32": 5, "i64": 6}
 SF_ROW_MAJOR, SF_ATOMS = 0, 1
-INDEX_PER_ROW, INDEX_PSUM, INDEX_NONE = 0, 1, 2
+INDEX_PER_ROW, INDEX_PSUM, INDEX_NONE, INDEX_MASKED = 0, 1, 2, 3
 FLAG_FORCE_GENERIC = 1
 
 
@@ -54,6 +54,7 @@ def lib():
         l = ctypes.CDLL(LIB_PATH)
         P = ctypes.POINTER(GemmArgs)
         l.cdg_grouped_fp8_fp4_gemm_nt_contiguous.argtypes = [P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        l.cdg_grouped_fp8_fp4_gemm_nt_masked.argtypes = [P, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         l.cdg_grouped_fp8_fp4_workspace_bytes.argtypes = [P]
         l.cdg_grouped_fp8_fp4_workspace_bytes.restype = ctypes.c_size_t
         l.cdg_can_implement.argtypes = [P]
@@ -73,7 +74,7 @@ def _code(t: torch.Tensor) -> int:
             torch.uint8: DT["ue8m0"], torch.int32: DT["i32"], torch.int64: DT["i64"]}[t.dtype]
 
 
-def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False) -> GemmArgs:
+def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, masked=False) -> GemmArgs:
     g = GemmArgs()
     M, K = a.shape
     E, N = b.shape[0], b.shape[1]
@@ -91,23 +92,25 @@ def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False) -> GemmArgs:
         g.index_form = INDEX_NONE
     else:
         g.m_indices, g.m_indices_dtype, g.m_indices_len = m_indices.data_ptr(), _code(m_indices), m_indices.numel()
-        g.index_form = INDEX_PER_ROW if m_indices.numel() == M else INDEX_PSUM
+        g.index_form = INDEX_MASKED if masked else INDEX_PER_ROW if m_indices.numel() == M else INDEX_PSUM
     g.d, g.d_dtype, g.d_row_stride = d.data_ptr(), _code(d), d.stride(0)
     g.M, g.N, g.K, g.E, g.flags = M, N, K, E, flags
     return g
 
 
-def gemm(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, stream=None, check_status=True):
-    """Run the GEMM through the C ABI on `stream` (default: torch's current stream)."""
+def gemm(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, stream=None, check_status=True, masked=False):
+    """Run the GEMM through the C ABI on `stream` (default: torch's current stream).
+
+    masked=True: `m_indices` is masked_m [G] and the masked entry point runs."""
     l = lib()
-    g = make_args(a, sa, b, sb, d, m_indices, flags, sb_atoms)
+    g = make_args(a, sa, b, sb, d, m_indices, flags, sb_atoms, masked)
     nbytes = l.cdg_grouped_fp8_fp4_workspace_bytes(ctypes.byref(g))
     assert nbytes > 0, "invalid arguments"
     ws = torch.empty(nbytes + 1024, dtype=torch.uint8, device=d.device)
     base = (ws.data_ptr() + 1023) // 1024 * 1024
     s = stream if stream is not None else torch.cuda.current_stream(d.device)
-    st = l.cdg_grouped_fp8_fp4_gemm_nt_contiguous(ctypes.byref(g), ctypes.c_void_p(base), nbytes,
-                                                  ctypes.c_void_p(s.cuda_stream))
+    entry = l.cdg_grouped_fp8_fp4_gemm_nt_masked if masked else l.cdg_grouped_fp8_fp4_gemm_nt_contiguous
+    st = entry(ctypes.byref(g), ctypes.c_void_p(base), nbytes, ctypes.c_void_p(s.cuda_stream))
     if st != CDG_OK:
         raise RuntimeError(f"cdg status {st}: {l.cdg_status_string(st).decode()}")
     if check_status:

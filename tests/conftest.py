@@ -48,6 +48,7 @@ def load_gemm_case(name: str) -> dict:
         "d": to_torch(z["d"], str(z["d_dtype"])),
         "d_dtype": _DTYPES[str(z["d_dtype"])][1],
         "m_indices": torch.from_numpy(z["m_indices"]) if bool(z["has_m_indices"]) else None,
+        "masked": bool(z["masked"]) if "masked" in z.files else False,
     }
     case["sa"] = torch.from_numpy(z["sa"]) if "sa" in z.files else None
     return case
@@ -56,6 +57,9 @@ def load_gemm_case(name: str) -> dict:
 GEMM_CASES = sorted(
     os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
     if os.path.basename(p).startswith(("kat_", "edge_", "c0")))
+
+MASKED_CASES = sorted(
+    os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "masked_*.npz")))
 
 
 @pytest.fixture(params=GEMM_CASES)

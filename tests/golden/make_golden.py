@@ -13,6 +13,7 @@ seeded inputs:
 * ``_reorder_scale_to_cutlass_sf_atom``    (gemm.py:76-116)
 * ``_dequant_fp4_block``                   (gemm.py:147-187)
 * ``_float_scale_to_e8m0``                 (gemm.py:62-73)
+* ``m_grouped_fp8_fp4_gemm_nt_masked``     (gemm.py:529-551)
 
 Cases cover the reference's own known answers (tests/test_fp4_fallback.py:15-73,
 tests/test_native_abi.py:144-196, tests/test_scale_reorder.py:53-68,
@@ -65,6 +66,8 @@ def gemm_case(gemm, name, a, sa, b, sb, m_indices, d_dtype=torch.bfloat16, fn="f
     a_arg = (a, sa) if sa is not None else a
     if fn == "fallback":
         gemm._m_grouped_fp8_fp4_fallback_nt(a_arg, (b, sb), d, m_indices)
+    elif fn == "masked":
+        gemm.m_grouped_fp8_fp4_gemm_nt_masked(a_arg, (b, sb), d, m_indices)
     else:
         gemm._m_grouped_fp8_fp4_dequant_mm_nt(a_arg, (b, sb), d, m_indices)
     out = {"a": raw(a), "a_dtype": str(a.dtype), "b": raw(b), "d": raw(d), "d_dtype": str(d_dtype)}
@@ -74,6 +77,7 @@ def gemm_case(gemm, name, a, sa, b, sb, m_indices, d_dtype=torch.bfloat16, fn="f
     out["sb_dtype"] = str(sb.dtype)
     out["m_indices"] = raw(m_indices) if m_indices is not None else np.zeros(0, np.int32)
     out["has_m_indices"] = np.array(m_indices is not None)
+    out["masked"] = np.array(fn == "masked")
     return name, out
 
 
@@ -119,7 +123,8 @@ def main():
     cases[name] = c0
 
     # --- edge cases -------------------------------------------------------------------------
-    def rand_case(name, m, k, n, e, ids, a_kind="fp8", sb_kind="u8", d_dtype=torch.bfloat16, sa_cols=None, seed=1):
+    def rand_case(name, m, k, n, e, ids, a_kind="fp8", sb_kind="u8", d_dtype=torch.bfloat16, sa_cols=None, seed=1,
+                  fn="fallback", single_b=False):
         g = torch.Generator().manual_seed(seed)
         x = torch.randn(m, k, generator=g)
         w = torch.randn(e, n, k, generator=g) * 0.02
@@ -133,7 +138,9 @@ def main():
             aq, saq = x.to(torch.bfloat16), torch.ones(m, 1)
         else:
             aq, saq = x.float(), torch.ones(m, 1)
-        add(gemm_case(gemm, name, aq, saq, bq, sbq, ids, d_dtype=d_dtype))
+        if single_b:
+            bq, sbq = bq[0], sbq[0]
+        add(gemm_case(gemm, name, aq, saq, bq, sbq, ids, d_dtype=d_dtype, fn=fn))
 
     add_ids = lambda v: torch.tensor(v, dtype=torch.int32)  # noqa: E731
     rand_case("edge_empty", 256, 256, 128, 4, torch.full((256,), -1, dtype=torch.int32))
@@ -157,6 +164,18 @@ def main():
     sizes = torch.tensor(([1] * 20 + [-1] * 108) + ([0] * 30 + [-1] * 98) + ([2] * 7 + [-1] * 121)
                          + ([3] * 100 + [-1] * 28), dtype=torch.int32)
     rand_case("edge_block_classes", 512, 384, 256, 4, sizes, seed=8)
+
+    # --- masked layout: G blocks of S = M // G rows, masked_m[g] leading rows each -----------
+    rand_case("masked_aligned", 512, 256, 128, 4, add_ids([5, 128, 0, 77]), fn="masked", seed=11)
+    rand_case("masked_s64", 384, 256, 256, 6, add_ids([1, 64, 33, 0, 16, 2]), fn="masked", seed=12)
+    rand_case("masked_s160", 480, 256, 128, 3, add_ids([150, 3, 160]), fn="masked", seed=13)
+    # counts above S run on into the next block (later groups win) and into the tail rows
+    rand_case("masked_overspill", 305, 256, 128, 3, add_ids([130, 20, 110]), fn="masked", seed=14)
+    rand_case("masked_int64_negative", 256, 256, 128, 4, torch.tensor([3, -5, 64, 0], dtype=torch.int64),
+              fn="masked", seed=15)
+    rand_case("masked_decode_classes", 2048, 512, 256, 8, add_ids([1, 16, 17, 32, 33, 128, 129, 256]), fn="masked",
+              seed=16)
+    rand_case("masked_single_b", 192, 256, 128, 1, add_ids([7]), fn="masked", single_b=True, seed=17)
 
     # --- byte-level helpers -----------------------------------------------------------------
     sf = torch.arange(128 * 8, dtype=torch.uint8).reshape(128, 8)

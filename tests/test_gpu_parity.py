@@ -17,7 +17,7 @@ import pytest
 import torch
 
 import cabi
-from conftest import GEMM_CASES, load_gemm_case
+from conftest import GEMM_CASES, MASKED_CASES, load_gemm_case
 from metrics import TOL_NORMWISE, TOL_ROW_L2, errors
 from oracle import cdg_oracle as oracle
 
@@ -72,6 +72,61 @@ def test_golden_case(name, flags):
         return
     nw, rl2 = errors(out, ref, ~bad)
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+
+
+def _masked_covered(m, counts, groups):
+    """Rows the masked layout writes from a group (the rest must be zero)."""
+    covered = torch.zeros(m, dtype=torch.bool)
+    block = m // groups
+    for g, cnt in enumerate(counts.tolist()):
+        if cnt > 0:
+            covered[g * block:min(m, g * block + cnt)] = True
+    return covered
+
+
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_FORCE_GENERIC], ids=["dispatch", "simt"])
+@pytest.mark.parametrize("name", MASKED_CASES)
+def test_masked_golden_case(name, flags):
+    """Masked layout through cdg_grouped_fp8_fp4_gemm_nt_masked against the reference."""
+    c = load_gemm_case(name)
+    a = c["a"].to(DEV)
+    sa = c["sa"].to(DEV).float()
+    b, sb = c["b"].to(DEV), c["sb"].to(DEV)
+    single = b.dim() == 2
+    if single:
+        b, sb = b.unsqueeze(0), sb.unsqueeze(0)
+    d = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    ids = None if single else c["m_indices"].to(DEV)
+    cabi.gemm(a, sa, b, sb, d, ids, flags=flags, masked=True)
+    torch.cuda.synchronize()
+    out, ref = d.cpu(), c["d"]
+    assert not torch.isnan(out).any(), "rows left unwritten"
+    rows = torch.ones(a.shape[0], dtype=torch.bool) if single else _masked_covered(a.shape[0], c["m_indices"],
+                                                                                   b.shape[0])
+    if bool((~rows).any()):
+        assert bool((out[~rows].float() == 0).all())
+    nw, rl2 = errors(out, ref, rows)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+
+
+def test_masked_public_api_3d_views():
+    """[G, S, K] activations and [G, S, N] output through the Python entry, masked_m on the host."""
+    import consumer_deep_gemm as cdg
+    from metrics import errors as _errors
+
+    c = load_gemm_case("masked_decode_classes")
+    G = c["b"].shape[0]
+    a3 = c["a"].view(G, -1, c["a"].shape[1]).to(DEV)
+    sa3 = c["sa"].float().view(G, -1, c["sa"].shape[1]).to(DEV)
+    d3 = torch.full((G, a3.shape[1], c["d"].shape[1]), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cdg.m_grouped_fp8_fp4_gemm_nt_masked((a3, sa3), (c["b"].to(DEV), c["sb"].to(DEV)), d3, c["m_indices"],
+                                         expected_m=64)
+    torch.cuda.synchronize()
+    out = d3.view(-1, d3.shape[2]).cpu()
+    rows = _masked_covered(out.shape[0], c["m_indices"], G)
+    assert bool((out[~rows].float() == 0).all())
+    nw, rl2 = _errors(out, c["d"], rows)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (nw, rl2)
 
 
 def test_sf_transform_bit_exact_vs_oracle():

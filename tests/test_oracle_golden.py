@@ -5,7 +5,9 @@ import os
 import numpy as np
 import torch
 
-from conftest import GOLDEN
+import pytest
+
+from conftest import GOLDEN, MASKED_CASES, load_gemm_case
 from oracle import cdg_oracle as oracle
 
 
@@ -16,6 +18,16 @@ def test_oracle_matches_reference_gemm(gemm_case):
     oracle.m_grouped_fp8_fp4_gemm_nt_contiguous(a, (c["b"], c["sb"]), d, c["m_indices"])
     assert torch.equal(d.view(torch.int16) if d.dtype == torch.bfloat16 else d,
                        c["d"].view(torch.int16) if d.dtype == torch.bfloat16 else c["d"]), c["name"]
+
+
+@pytest.mark.parametrize("name", MASKED_CASES)
+def test_oracle_masked_matches_reference(name):
+    c = load_gemm_case(name)
+    assert c["masked"]
+    d = torch.full_like(c["d"], 7.0)
+    a = (c["a"], c["sa"]) if c["sa"] is not None else c["a"]
+    oracle.m_grouped_fp8_fp4_gemm_nt_masked(a, (c["b"], c["sb"]), d, c["m_indices"])
+    assert torch.equal(d.view(torch.int16), c["d"].view(torch.int16)), name
 
 
 def _z(name):
