@@ -16,6 +16,7 @@
 
 #include "cdg_b200.h"
 #include "cdg_kernels.cuh"
+#include "cdg_pair.cuh"
 #include "cdg_layout.h"
 
 namespace cdg {
@@ -61,6 +62,15 @@ const DeviceInfo& device_info(int dev) {
         return;
       if (cudaFuncSetAttribute(cdg_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                GemmSmem<128>::kBytes) != cudaSuccess)
+        return;
+      if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PairSmem<16, 4>::kBytes) != cudaSuccess)
+        return;
+      if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PairSmem<32, 2>::kBytes) != cudaSuccess)
+        return;
+      if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PairSmem<128, 1>::kBytes) != cudaSuccess)
         return;
       if (cudaFuncSetAttribute(cdg_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
           cudaSuccess)
@@ -161,12 +171,12 @@ int launch_sf_atoms(const uint8_t* sf, int64_t se, int64_t sn, int64_t E, int64_
 }
 
 // Activation planes: 3-D view [2 planes][nblk*128 rows][K] e4m3 bytes; one box brings
-// `tok` rows of both planes, landing as [hi tok rows][lo tok rows] in shared memory.
+// `tok` rows of `planes` planes, landing as [hi tok rows][lo tok rows] in shared memory.
 int make_plane_tmap(EncodeTiledFn enc, const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, uint32_t tok,
-                    CUtensorMap* ta) {
+                    CUtensorMap* ta, uint32_t planes = 2) {
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(nblk * 128), 2};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(nblk * 128 * g->K)};
-  cuuint32_t box[3] = {128, tok, 2};
+  cuuint32_t box[3] = {128, tok, planes};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, hilo, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -194,6 +204,29 @@ int make_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap*
   if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 32, ta32);
   if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 128, ta128);
   return st;
+}
+
+// Tensor maps of the CTA-pair kernels: one plane of TOK rows per CTA (tiny, narrow),
+// 64 rows of both planes per CTA (wide), and the weight scale atoms as a 2-D array
+// [atoms][128 words] read one 512-byte atom per box.
+int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const uint32_t* sfw, CUtensorMap* p16,
+                    CUtensorMap* p32, CUtensorMap* p128, CUtensorMap* tsf) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return CDG_ERR_CUDA;
+  int st = make_plane_tmap(enc, g, hilo, nblk, 16, p16, 1);
+  if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 32, p32, 1);
+  if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 64, p128, 2);
+  if (st != CDG_OK) return st;
+  const int64_t atoms = g->E * (g->N / 128) * (g->K / 128);
+  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(atoms)};
+  cuuint64_t strides[1] = {512};
+  cuuint32_t box[2] = {128, 1};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(tsf, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(sfw), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? CDG_OK
+             : CDG_ERR_CUDA;
 }
 
 int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -236,7 +269,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     ids = rows;
     ids_dtype = CDG_DTYPE_I32;
   }
-  int* lists = reinterpret_cast<int*>(ws + wl.lists);
+  int4* lists = reinterpret_cast<int4*>(ws + wl.lists);
   int4* blk_info = reinterpret_cast<int4*>(ws + wl.blk_info);
   uint4* blk_mask = reinterpret_cast<uint4*>(ws + wl.blk_mask);
 
@@ -338,23 +371,46 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.zero_list = lists + kClassZero * nblk;
 
   if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
-  // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.
-  ka.list = lists + kClassTiny * nblk;
-  ka.count_slot = kCtrlCount0 + kClassTiny;
-  ka.do_zero_blocks = 1;
-  cdg_gemm_kernel<16><<<di.sm_count, 256, GemmSmem<16>::kBytes, stream>>>(tw, ta16, ka);
-  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
-  // Narrow blocks (17 to 32 routed rows).
-  ka.do_zero_blocks = 0;
-  ka.list = lists + kClassNarrow * nblk;
-  ka.count_slot = kCtrlCount0 + kClassNarrow;
-  cdg_gemm_kernel<32><<<di.sm_count, 256, GemmSmem<32>::kBytes, stream>>>(tw, ta32, ka);
-  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
-  // Wide blocks (prefill-like).
-  ka.list = lists + kClassWide * nblk;
-  ka.count_slot = kCtrlCount0 + kClassWide;
-  cdg_gemm_kernel<128><<<di.sm_count, 256, GemmSmem<128>::kBytes, stream>>>(tw, ta128, ka);
-  if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  if (g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2) {
+    // CTA pairs (tcgen05 cta_group::2): two adjacent 128-column tiles per cluster; four MMA
+    // issuers for tiny blocks, two for narrow, one for wide (math-bound) blocks.
+    CUtensorMap p16, p32, p128, tsf;
+    st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &p128, &tsf);
+    if (st != CDG_OK) return st;
+    const unsigned grid = static_cast<unsigned>(di.sm_count / 2 * 2);
+    ka.list = lists + kClassTiny * nblk;
+    ka.count_slot = kCtrlCount0 + kClassTiny;
+    ka.do_zero_blocks = 1;
+    cdg_gemm_pair_kernel<16, 4><<<grid, PairSmem<16, 4>::kThreads, PairSmem<16, 4>::kBytes, stream>>>(tw, p16, tsf, ka);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    ka.do_zero_blocks = 0;
+    ka.list = lists + kClassNarrow * nblk;
+    ka.count_slot = kCtrlCount0 + kClassNarrow;
+    cdg_gemm_pair_kernel<32, 2><<<grid, PairSmem<32, 2>::kThreads, PairSmem<32, 2>::kBytes, stream>>>(tw, p32, tsf, ka);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    ka.list = lists + kClassWide * nblk;
+    ka.count_slot = kCtrlCount0 + kClassWide;
+    cdg_gemm_pair_kernel<128, 1><<<grid, PairSmem<128, 1>::kThreads, PairSmem<128, 1>::kBytes, stream>>>(tw, p128, tsf, ka);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  } else {
+    // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.
+    ka.list = lists + kClassTiny * nblk;
+    ka.count_slot = kCtrlCount0 + kClassTiny;
+    ka.do_zero_blocks = 1;
+    cdg_gemm_kernel<16><<<di.sm_count, 256, GemmSmem<16>::kBytes, stream>>>(tw, ta16, ka);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    // Narrow blocks (17 to 32 routed rows).
+    ka.do_zero_blocks = 0;
+    ka.list = lists + kClassNarrow * nblk;
+    ka.count_slot = kCtrlCount0 + kClassNarrow;
+    cdg_gemm_kernel<32><<<di.sm_count, 256, GemmSmem<32>::kBytes, stream>>>(tw, ta32, ka);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    // Wide blocks (prefill-like).
+    ka.list = lists + kClassWide * nblk;
+    ka.count_slot = kCtrlCount0 + kClassWide;
+    cdg_gemm_kernel<128><<<di.sm_count, 256, GemmSmem<128>::kBytes, stream>>>(tw, ta128, ka);
+    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+  }
   if (t_prof_stop && cudaEventRecord(t_prof_stop, stream) != cudaSuccess) return CDG_ERR_CUDA;
   // Blocks holding rows of several experts: exact SIMT path over the listed blocks.
   ga.ids = ids;

@@ -118,7 +118,7 @@ struct PrepArgs {
   int4* blk_info;          // [nblk] {expert (-1 none, -2 several), rows spanned, class, 0}
   uint4* blk_mask;         // [nblk] bit r set when row r of the block has the block's expert
   int* ctrl;               // control words (zeroed by the host before launch)
-  int* lists;              // [kNumClasses][nblk]
+  int4* lists;             // [kNumClasses][nblk] {block, expert, rows spanned, 0}
 };
 
 // Group id of row r; a null id vector means every row belongs to group 0.
@@ -295,7 +295,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   for (int c = 0; c < kNumClasses; ++c) pos[c] = s_cls_count[c][tid + 1];
   for (int i = lo; i < hi; ++i) {
     const int c = __ldcg(&p.blk_info[i].z);
-    p.lists[c * p.nblk + pos[c]++] = i;
+    const int4 info = __ldcg(&p.blk_info[i]);
+    p.lists[c * p.nblk + pos[c]++] = make_int4(i, info.x, info.y, 0);
   }
 }
 
@@ -325,8 +326,8 @@ struct GemmArgs {
   const int4* blk_info;
   const uint4* blk_mask;
   const int* ctrl;
-  const int* list;        // blocks of this kernel's class, in order
-  const int* zero_list;   // all-padding blocks (zero-filled by the kernel with do_zero_blocks)
+  const int4* list;       // blocks of this kernel's class, in order: {block, expert, rows spanned, 0}
+  const int4* zero_list;  // all-padding blocks (zero-filled by the kernel with do_zero_blocks)
   const uint32_t* sfw_atoms;  // [E][N/128][K/128][128] words
   const int32_t* row_exp;     // [nblk*128] per-row exponent of the activation planes
   __nv_bfloat16* d;
@@ -423,10 +424,14 @@ __global__ void __launch_bounds__(256, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      // the next tile's list entry is loaded one tile ahead, off the issue path
+      int4 next = blockIdx.x < reg_tiles ? __ldg(&p.list[blockIdx.x / n_tiles]) : make_int4(0, 0, 0, 0);
       for (int t = blockIdx.x; t < reg_tiles && ok; t += gridDim.x) {
-        const int blk = p.list[t / n_tiles];
+        const int4 cur = next;
+        if (t + static_cast<int>(gridDim.x) < reg_tiles) next = __ldg(&p.list[(t + gridDim.x) / n_tiles]);
+        const int blk = cur.x;
         const int nt = t % n_tiles;
-        const int expert = p.blk_info[blk].x;
+        const int expert = cur.y;
         const int wrow = expert * p.N + nt * 128;
         const uint32_t* sfw_tile = p.sfw_atoms + (static_cast<int64_t>(expert) * n_tiles + nt) * k_steps * 128;
         for (int kb = 0; kb < k_steps; ++kb) {
@@ -451,9 +456,11 @@ __global__ void __launch_bounds__(256, 1)
       int local = 0;
       const uint32_t sfa_t = tmem_base + kSfaCol;
       tc_cp_sf_atom(sfa_t, smem_desc_sf(smem_u32(smem + L::kOneAtom)));
+      int4 next = blockIdx.x < reg_tiles ? __ldg(&p.list[blockIdx.x / n_tiles]) : make_int4(0, 0, 0, 0);
       for (int t = blockIdx.x; t < reg_tiles && ok; t += gridDim.x, ++local) {
-        const int blk = p.list[t / n_tiles];
-        const uint32_t ntok = static_cast<uint32_t>((p.blk_info[blk].y + 15) & ~15);
+        const int4 cur = next;
+        if (t + static_cast<int>(gridDim.x) < reg_tiles) next = __ldg(&p.list[(t + gridDim.x) / n_tiles]);
+        const uint32_t ntok = static_cast<uint32_t>((cur.z + 15) & ~15);
         const uint32_t n_mma = kStacked ? 2u * TOK : ntok;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -490,7 +497,7 @@ __global__ void __launch_bounds__(256, 1)
     int local = 0;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       const bool regular = t < reg_tiles;
-      const int blk = regular ? p.list[t / n_tiles] : p.zero_list[(t - reg_tiles) / n_tiles];
+      const int blk = regular ? __ldg(&p.list[t / n_tiles]).x : __ldg(&p.zero_list[(t - reg_tiles) / n_tiles]).x;
       const int nt = t % n_tiles;
       int row0, nrows;
       p.tm.rows(blk, row0, nrows);
@@ -587,7 +594,7 @@ struct GenericArgs {
   int M, N, K, E;
   int nblk;
   TileMap tm;        // rows of each block
-  const int* list;   // nullptr: every block; else the listed blocks
+  const int4* list;  // nullptr: every block; else the listed blocks ({block, ...})
   const int* count;  // number of listed blocks (device)
 };
 
@@ -607,7 +614,7 @@ __global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
   const int units = (p.list ? __ldcg(p.count) : p.nblk) * n_chunks;
   for (int u = blockIdx.x; u < units; u += gridDim.x) {
     const int bi = u / n_chunks;
-    const int blk = p.list ? p.list[bi] : bi;
+    const int blk = p.list ? p.list[bi].x : bi;
     const int n = (u % n_chunks) * 256 + threadIdx.x;
     int row0, nrows;
     p.tm.rows(blk, row0, nrows);

@@ -24,7 +24,7 @@ constexpr int kNarrowTok = 32;
 enum : int {
   kCtrlTicket = 0,
   kCtrlCount0 = 1,  // kCtrlCount0 + class = number of blocks in that class
-  kCtrlStatus = 8,  // device status bits (kStatus*)
+  kCtrlStatus = 8,  // device status bits (kStatus*); kCtrlStatus + 1: code of the first wait that gave up
   kCtrlWords = 64,
 };
 
@@ -86,7 +86,7 @@ struct WorkspaceLayout {
     w.blk_mask = off;
     off = align_up(off + static_cast<size_t>(nblk) * 16, 1024);
     w.lists = off;
-    off = align_up(off + static_cast<size_t>(nblk) * 4 * kNumClasses, 1024);
+    off = align_up(off + static_cast<size_t>(nblk) * 16 * kNumClasses, 1024);
     if (row_ids) {
       w.row_ids = off;
       off = align_up(off + static_cast<size_t>(M) * 4, 1024);

@@ -109,6 +109,8 @@ typedef struct cdg_gemm_args {
 } cdg_gemm_args;
 
 #define CDG_FLAG_FORCE_GENERIC 1 /* run the exact SIMT path even where the tensor-core path applies */
+#define CDG_FLAG_SINGLE_CTA 2    /* tensor-core path: one CTA per 128-column tile even where N % 256 == 0
+                                    would allow CTA pairs (for comparisons; same results) */
 
 /* Grouped FP8 x MXFP4 GEMM, contiguous layout.
  * Replaces m_grouped_fp8_fp4_gemm_nt_contiguous (consumer_deep_gemm/gemm.py:467-470),

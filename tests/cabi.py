@@ -21,6 +21,7 @@ DT = {"e4m3": 1, "bf16": 2, "f32": 3, "ue8m0": 4, "i32": 5, "i64": 6}
 SF_ROW_MAJOR, SF_ATOMS = 0, 1
 INDEX_PER_ROW, INDEX_PSUM, INDEX_NONE, INDEX_MASKED = 0, 1, 2, 3
 FLAG_FORCE_GENERIC = 1
+FLAG_SINGLE_CTA = 2
 
 
 class GemmArgs(ctypes.Structure):
@@ -116,7 +117,9 @@ def gemm(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, stream=None, check
     if check_status:
         st = l.cdg_read_device_status(ctypes.c_void_p(base), ctypes.c_void_p(s.cuda_stream))
         if st != CDG_OK:
-            raise RuntimeError(f"device status {st}: {l.cdg_status_string(st).decode()}")
+            off = base - ws.data_ptr()
+            where = int(ws[off + 36:off + 40].cpu().view(torch.int32)[0])  # control word 9
+            raise RuntimeError(f"device status {st}: {l.cdg_status_string(st).decode()}; wait code {where:#010x}")
     return ws
 
 

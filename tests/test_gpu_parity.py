@@ -1,8 +1,10 @@
 """GPU parity of the grouped FP8 x MXFP4 GEMM, driven through the C ABI (ctypes).
 
 Every golden case (outputs of the reference itself, see tests/golden/make_golden.py)
-is run twice: through the default dispatch (tensor-core kernel where the inputs
-fit it, exact SIMT kernel for the rest) and with the SIMT kernel forced.
+is run three times: through the default dispatch (tensor-core kernels where the
+inputs fit them -- CTA pairs when N is a multiple of 256 -- and the exact SIMT
+kernel for the rest), with single-CTA tensor-core kernels, and with the SIMT
+kernel forced.
 
 Tolerances, against the reference's BF16 output over the routed rows:
   * max |out - ref| / max |ref|      <= 1e-2   (TOL_NORMWISE)
@@ -57,7 +59,8 @@ def _run_case(c, flags):
     return d.cpu()
 
 
-@pytest.mark.parametrize("flags", [0, cabi.FLAG_FORCE_GENERIC], ids=["dispatch", "simt"])
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_SINGLE_CTA, cabi.FLAG_FORCE_GENERIC],
+                         ids=["dispatch", "single_cta", "simt"])
 @pytest.mark.parametrize("name", GEMM_CASES)
 def test_golden_case(name, flags):
     c = load_gemm_case(name)
@@ -84,7 +87,8 @@ def _masked_covered(m, counts, groups):
     return covered
 
 
-@pytest.mark.parametrize("flags", [0, cabi.FLAG_FORCE_GENERIC], ids=["dispatch", "simt"])
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_SINGLE_CTA, cabi.FLAG_FORCE_GENERIC],
+                         ids=["dispatch", "single_cta", "simt"])
 @pytest.mark.parametrize("name", MASKED_CASES)
 def test_masked_golden_case(name, flags):
     """Masked layout through cdg_grouped_fp8_fp4_gemm_nt_masked against the reference."""
@@ -208,3 +212,10 @@ def test_benchmark_config_sampled_rows(cfg):
     ref = _sampled_oracle(inp, rows)
     nw, rl2 = errors(d[rows.to(DEV)], ref)
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (cfg, nw, rl2)
+    # the single-CTA kernels (same tiles, one SM each) agree on the same rows
+    d1 = torch.full_like(d, float("nan"))
+    cabi.gemm(a, sa, b, sb, d1, ids, flags=cabi.FLAG_SINGLE_CTA)
+    torch.cuda.synchronize()
+    assert bool((d1[pad] == 0).all()) and not bool(torch.isnan(d1).any())
+    nw1, rl21 = errors(d1[rows.to(DEV)], ref)
+    assert nw1 <= TOL_NORMWISE and rl21 <= TOL_ROW_L2, (cfg, "single CTA", nw1, rl21)
