@@ -46,14 +46,17 @@ struct PairSmem {
   static constexpr int kPlanes = kWide ? 2 : 1;    // planes held by one CTA
   // A multiple of NI: stage s is always consumed by issuer s % NI, in order, so an
   // issuer never waits on a stage use whose predecessor it did not consume itself.
-  static constexpr int kStages = kWide ? 6 : NI == 4 ? 8 : 10;
+  static constexpr int kStages = kWide ? 6 : NI == 4 ? 12 : 10;
   static_assert(kStages % NI == 0, "stage ring must split evenly over the issuers");
   static constexpr int kW = 128 * 128;             // weight tile, bytes per stage
   static constexpr int kA = kRowsA * 128;          // one plane's rows, bytes per stage
-  static constexpr int kStageBytes = kW + kPlanes * kA + 1024;  // + scale atom (512 B, padded)
-  static constexpr int kOneAtom = kStages * kStageBytes;        // constant activation scale atom
+  static constexpr int kStageBytes = kW + kPlanes * kA;  // operand tiles (1024-byte multiple)
+  static constexpr int kSfRing = kStages * kStageBytes;  // then one 512-byte scale atom per stage
+  static constexpr int kOneAtom = kSfRing + kStages * 512;  // constant activation scale atom
   static constexpr int kBarOffset = kOneAtom + 512;
-  static constexpr int kBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
+  static constexpr int kBarBytes = (2 * kStages + 4 + NI) * 8 + 16;  // barriers + TMEM address
+  static constexpr int kBytes = kBarOffset + kBarBytes + 1024;          // + alignment slack
+  static_assert(kBytes <= 232448, "shared memory per CTA");
   // bytes one CTA's copies of one stage add to the even CTA's `full` barrier
   static constexpr uint32_t kTxPerCta = 128u * 64u + kPlanes * kA + 512u;
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned for SW128 tiles");
@@ -95,7 +98,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   auto stage_w = [&](int s) { return smem + s * L::kStageBytes; };
   auto stage_a = [&](int s) { return smem + s * L::kStageBytes + L::kW; };
-  auto stage_sf = [&](int s) { return smem + s * L::kStageBytes + L::kW + L::kPlanes * L::kA; };
+  auto stage_sf = [&](int s) { return smem + L::kSfRing + s * 512; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* full = bars;       // [S] (even CTA's count both CTAs' copies)
   uint64_t* empty = bars + S;  // [S] stage consumed (multicast by the MMA commit)
