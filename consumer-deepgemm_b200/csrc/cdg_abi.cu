@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "cdg_b200.h"
 #include "cdg_kernels.cuh"
@@ -229,6 +230,25 @@ int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const u
              : CDG_ERR_CUDA;
 }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled while
+// the previous kernel of the stream drains and waits for it on the device
+// (griddepcontrol.wait), which hides the launch gap between the GEMM's kernels.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   int st = validate(g);
   if (st != CDG_OK) return st;
@@ -381,35 +401,38 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = 1;
-    cdg_gemm_pair_kernel<16, 4><<<grid, PairSmem<16, 4>::kThreads, PairSmem<16, 4>::kBytes, stream>>>(tw, p16, tsf, ka);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_gemm_pair_kernel<16, 4>, grid, PairSmem<16, 4>::kThreads, PairSmem<16, 4>::kBytes, stream, tw,
+                   p16, tsf, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
     ka.do_zero_blocks = 0;
     ka.list = lists + kClassNarrow * nblk;
     ka.count_slot = kCtrlCount0 + kClassNarrow;
-    cdg_gemm_pair_kernel<32, 2><<<grid, PairSmem<32, 2>::kThreads, PairSmem<32, 2>::kBytes, stream>>>(tw, p32, tsf, ka);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_gemm_pair_kernel<32, 2>, grid, PairSmem<32, 2>::kThreads, PairSmem<32, 2>::kBytes, stream, tw,
+                   p32, tsf, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
     ka.list = lists + kClassWide * nblk;
     ka.count_slot = kCtrlCount0 + kClassWide;
-    cdg_gemm_pair_kernel<128, 1><<<grid, PairSmem<128, 1>::kThreads, PairSmem<128, 1>::kBytes, stream>>>(tw, p128, tsf, ka);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_gemm_pair_kernel<128, 1>, grid, PairSmem<128, 1>::kThreads, PairSmem<128, 1>::kBytes, stream,
+                   tw, p128, tsf, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
   } else {
     // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = 1;
-    cdg_gemm_kernel<16><<<di.sm_count, 256, GemmSmem<16>::kBytes, stream>>>(tw, ta16, ka);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_gemm_kernel<16>, di.sm_count, 256, GemmSmem<16>::kBytes, stream, tw, ta16, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
     // Narrow blocks (17 to 32 routed rows).
     ka.do_zero_blocks = 0;
     ka.list = lists + kClassNarrow * nblk;
     ka.count_slot = kCtrlCount0 + kClassNarrow;
-    cdg_gemm_kernel<32><<<di.sm_count, 256, GemmSmem<32>::kBytes, stream>>>(tw, ta32, ka);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_gemm_kernel<32>, di.sm_count, 256, GemmSmem<32>::kBytes, stream, tw, ta32, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
     // Wide blocks (prefill-like).
     ka.list = lists + kClassWide * nblk;
     ka.count_slot = kCtrlCount0 + kClassWide;
-    cdg_gemm_kernel<128><<<di.sm_count, 256, GemmSmem<128>::kBytes, stream>>>(tw, ta128, ka);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_gemm_kernel<128>, di.sm_count, 256, GemmSmem<128>::kBytes, stream, tw, ta128, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
   }
   if (t_prof_stop && cudaEventRecord(t_prof_stop, stream) != cudaSuccess) return CDG_ERR_CUDA;
   // Blocks holding rows of several experts: exact SIMT path over the listed blocks.
@@ -419,8 +442,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ga.count = ctrl + kCtrlCount0 + kClassIrregular;
   {
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(di.sm_count)));
-    cdg_generic_kernel<<<grid, 256, generic_smem, stream>>>(ga);
-    if (cudaGetLastError() != cudaSuccess) return CDG_ERR_CUDA;
+    if (launch_pdl(cdg_generic_kernel, grid, 256, generic_smem, stream, ga) != cudaSuccess) return CDG_ERR_CUDA;
   }
   return CDG_OK;
 }

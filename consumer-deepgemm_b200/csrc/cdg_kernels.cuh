@@ -144,7 +144,8 @@ constexpr int kPrepK = 1024;
 template <typename IdT>
 __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ int s_min_id, s_max_id, s_max_row;
-  __shared__ int s_last;
+  __shared__ int s_last, s_nv;
+  __shared__ uint8_t s_vrow[128];  // the block's rows that carry its expert (compacted)
   __shared__ int s_id[128];
   __shared__ uint32_t s_mask[4];
   __shared__ float s_scale[128][kPrepK / 128];
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     s_min_id = 0x7fffffff;
     s_max_id = -1;
     s_max_row = -1;
+    s_nv = 0;
   }
   if (tid < 4) s_mask[tid] = 0u;
   int row0, nrows;
@@ -196,7 +198,10 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     const int kb0 = blockIdx.y * (kPrepK / 128);
     const int kbn = min(kPrepK / 128, kb_count - kb0);
     const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
-    if (tid < 128 && s_id[tid] == expert) atomicOr(&s_mask[tid >> 5], 1u << (tid & 31));
+    if (tid < 128 && s_id[tid] == expert) {
+      atomicOr(&s_mask[tid >> 5], 1u << (tid & 31));
+      s_vrow[atomicAdd(&s_nv, 1)] = static_cast<uint8_t>(tid);
+    }
     // (1) per routed row: the exponent E with |bf16(sa[r,kb])| < 2^E for every K block of
     //     the row (frexp exponent of the largest scale); and the BF16-rounded scales of
     //     this CTA's K blocks.
@@ -223,17 +228,20 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
           : 0.0f;
     }
     __syncthreads();
-    // (2) activation planes, one 16-byte chunk per item; consecutive threads read
-    //     consecutive chunks of a row (coalesced).  Rows without the block's id are zeros.
+    // (2) activation planes of the rows that carry the block's expert, one 16-byte chunk
+    //     per item; consecutive threads read consecutive chunks of a row (coalesced).
+    //     Other rows of the planes are not written: whatever they hold only reaches
+    //     accumulator columns the epilogue replaces by zeros.
     const int chunks = kbn * 8;
-    for (int it = tid; it < ntok * chunks; it += blockDim.x) {
-      const int rr = it / chunks;
-      const int c = it - rr * chunks;
+    const int nv = s_nv;
+    for (int it = tid; it < nv * chunks; it += blockDim.x) {
+      const int rr = s_vrow[it / chunks];
+      const int c = it % chunks;
       const int kl = c >> 3;
       const int r = row0 + rr;
       const int64_t col = static_cast<int64_t>(kb0) * 128 + c * 16;
       uint4 hi4 = make_uint4(0, 0, 0, 0), lo4 = make_uint4(0, 0, 0, 0);
-      if (s_id[rr] == expert) {
+      {
         const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + col);
         const float sbf = s_scale[rr][kl];
         const float inv = ldexpf(1.0f, -s_exp[rr]);
@@ -361,6 +369,8 @@ __global__ void __launch_bounds__(256, 1)
   constexpr bool kStacked = TOK <= 32;
   constexpr uint32_t kAccCols = 128;  // TMEM columns per accumulator stage
 
+  grid_dependency_wait();  // the block plan comes from the previous kernel of the stream
+  grid_launch_dependents();
   const int n_tiles = p.N / 128;
   const int k_steps = p.K / 128;
   const int count = __ldcg(&p.ctrl[p.count_slot]);
@@ -610,6 +620,7 @@ __device__ __forceinline__ float ue8m0_to_f32(uint32_t e) {
 
 __global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
   extern __shared__ float s_row[];  // K floats: the dequantised activation row
+  grid_dependency_wait();  // the block list comes from the previous kernel of the stream
   const int n_chunks = (p.N + 255) / 256;
   const int units = (p.list ? __ldcg(p.count) : p.nblk) * n_chunks;
   for (int u = blockIdx.x; u < units; u += gridDim.x) {

@@ -82,6 +82,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
   constexpr bool kWide = L::kWide;
   constexpr uint32_t kTmemCols = 512;
 
+  grid_dependency_wait();  // the block plan comes from the previous kernel of the stream
+  grid_launch_dependents();
   const uint32_t rank = cluster_ctarank();
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int npairs = static_cast<int>(gridDim.x >> 1);

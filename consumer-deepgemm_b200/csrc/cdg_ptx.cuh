@@ -137,6 +137,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with programmatic stream serialization may be scheduled before the
+// previous kernel of the stream finished; they wait here before reading its results.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the stream be scheduled (it still waits for this grid's end).
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- CTA pairs (clusters of 2)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
