@@ -51,6 +51,9 @@ METRIC = "grouped FP8×FP4 MoE GEMM TFLOPS and HBM GB/s vs roofline at 1/2/4/8 B
 DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
 # library kernels per GEMM call: cdg_prep_kernel, cdg_gemm_kernel<16>, <32>, <128>, cdg_generic_kernel
 GEMM_LAUNCHES = 5
+# DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
+# captures summarised under profiles/ (absent: no capture of the current kernels yet).
+NCU_TRAFFIC = {}
 # per EP step on top of the GEMM(s): quant_rows, ep_count, ep_pack, ep_permute, ep_unpermute, ep_combine
 EP_LAUNCHES = 6
 
@@ -122,11 +125,12 @@ class ClockSampler:
                 "samples": len(loaded), "reasons": reasons}
 
 
-def cpu_port_sample(inp, budget_s: float = 4.0):
+def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
     """Time the CPU oracle (the reference's dequant + matmul restated) on a bounded sample.
 
     The sample is the routed rows of the first few active experts, grown until
-    one call takes about `budget_s`.  Returns (GB/s, cores, description).
+    one call takes about `budget_s`.  Returns ({"GB/s": .., "TFLOP/s": ..}, cores,
+    description), rates of the median call.
     """
     from oracle import cdg_oracle as oracle
 
@@ -150,14 +154,17 @@ def cpu_port_sample(inp, budget_s: float = 4.0):
 
     dt, _, _ = run(1)
     n_exp = max(1, min(int(experts.numel()), int(budget_s / max(dt, 1e-3))))
+    for _ in range(warmup):
+        run(n_exp)
     times = []
-    for _ in range(3):
+    for _ in range(max(1, calls)):
         dt, nbytes, r = run(n_exp)
         times.append(dt)
     dt = statistics.median(times)
     desc = (f"{cfg.name}: {r} routed rows of {n_exp} of {experts.numel()} active experts, "
-            f"median of 3 calls ({dt:.2f} s each), torch CPU threads={torch.get_num_threads()}")
-    return nbytes / dt / 1e9, torch.get_num_threads(), desc
+            f"median of {len(times)} calls ({dt:.2f} s each), torch CPU threads={torch.get_num_threads()}")
+    rates = {"GB/s": nbytes / dt / 1e9, "TFLOP/s": 2.0 * r * cfg.n * cfg.k / dt / 1e12}
+    return rates, torch.get_num_threads(), desc
 
 
 def run_reference(args):
@@ -169,14 +176,18 @@ def run_reference(args):
     cfg_name = args.config if args.config in ("c1", "c2", "c3") else "c1"
     inp = synthetic.make_inputs(synthetic.CONFIGS[cfg_name], device="cpu", seed=0,
                                 weight_device="cuda" if torch.cuda.is_available() else "cpu")
-    gbs, cores, desc = cpu_port_sample(inp, budget_s=max(1.0, 20.0 / max(1, args.steps)))
+    # K timed samples after W warm-up ones, about 60 s of CPU work in all
+    rates, cores, desc = cpu_port_sample(inp, budget_s=max(0.2, 60.0 / max(1, args.steps + args.warmup)),
+                                         calls=args.steps, warmup=args.warmup)
+    unit = "GB/s" if cfg_name == "c1" else "TFLOP/s"  # the unit of our arm's line for this workload
+    v = rates[unit]
     line = {
-        "metric": METRIC, "impl": "reference", "value": gbs, "unit": "GB/s", "n_gpus": args.gpus,
+        "metric": METRIC, "impl": "reference", "value": v, "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": cfg_name, "parallelism": "cpu"},
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc},
-        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -301,28 +312,43 @@ def bench_gemm(args, dev, cfg_name):
         e2e_call()
     e2e_ms, _ = timer.run(e2e_call, args.steps, with_kernel_events=False)
     clocks = sampler.stop()
-    hbm_peak, _, peak_src = measured_peaks()
-    achieved = nbytes / (kernel_ms * 1e-3) / 1e9
+    hbm_peak, bf16_peak, peak_src = measured_peaks()
+    achieved_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
+    achieved_tf = flops / (kernel_ms * 1e-3) / 1e12
+    hbm_roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved_gbs / hbm_peak, "traffic": NCU_TRAFFIC.get(cfg.name),
+                "peak_source": peak_src, "kernel_ms": kernel_ms, "algorithmic_bytes": nbytes}
+    # dense FP8 (kind::mxf8f6f4) runs at twice the BF16 rate: the denominator is twice the
+    # measured cuBLAS BF16 burst rate
+    tensor_roof = {"bound": "tensor", "achieved": achieved_tf, "peak": 2 * bf16_peak, "unit": "TFLOP/s",
+                   "frac": achieved_tf / (2 * bf16_peak), "traffic": NCU_TRAFFIC.get(cfg.name),
+                   "peak_source": peak_src + " (2 x BF16 GEMM burst)", "kernel_ms": kernel_ms,
+                   "algorithmic_flops": flops}
+    hbm_bound = cfg.name == "c1"  # decode is HBM-bound; the prefill shapes are tensor-bound
     line = {
-        "metric": METRIC, "value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "metric": METRIC,
+        "value": nbytes / (ms * 1e-3) / 1e9 if hbm_bound else flops / (ms * 1e-3) / 1e12,
+        "unit": "GB/s" if hbm_bound else "TFLOP/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": cfg.name, "experts": cfg.num_experts, "k": cfg.k, "n": cfg.n,
                    "routed_rows": inp["rows"], "m_pad": inp["m_pad"], "active_experts": e_act,
                    "parallelism": "single", "l2": "inputs larger than L2 (weights %.2f GB)" % (b.numel() / 1e9)},
         "tflops": flops / (ms * 1e-3) / 1e12,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
-                     "kernel_ms": kernel_ms, "algorithmic_bytes": nbytes},
-        "e2e": {"value": nbytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+        "gbs": nbytes / (ms * 1e-3) / 1e9,
+        "roofline": hbm_roof if hbm_bound else tensor_roof,
+        "roofline_other": tensor_roof if hbm_bound else hbm_roof,
+        "e2e": {"value": (nbytes / (e2e_ms * 1e-3) / 1e9) if hbm_bound else flops / (e2e_ms * 1e-3) / 1e12,
+                "unit": "GB/s" if hbm_bound else "TFLOP/s",
                 "h2d_bytes_per_step": h_a.numel() + h_sa.numel() * 4 + h_ids.numel() * h_ids.element_size(),
                 "d2h_bytes_per_step": h_d.numel() * 2, "ms_per_step": e2e_ms},
         "gpu_launches": GEMM_LAUNCHES * args.steps,
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:
-        v, cores, desc = cpu_port_sample(inp)
-        line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc}
+        rates, cores, desc = cpu_port_sample(inp)
+        line["cpu_baseline"] = {"value": rates[line["unit"]], "unit": line["unit"], "cores": cores, "kind": "port",
+                                "sample": desc}
     return line
 
 
