@@ -53,7 +53,10 @@ DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
 GEMM_LAUNCHES = 5
 # DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
 # captures summarised under profiles/ (absent: no capture of the current kernels yet).
-NCU_TRAFFIC = {}
+NCU_TRAFFIC = {
+    "c1": 2.007860e9 + 0.223218e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
+    "c2": 1.413981e9 + 0.518562e9,  # cdg_gemm_pair_kernel<128, 1>: profiles/cdg_gemm_pair_kernel128_c2_prefill.md
+}
 # per EP step on top of the GEMM(s): quant_rows, ep_count, ep_pack, ep_permute, ep_unpermute, ep_combine
 EP_LAUNCHES = 6
 
