@@ -57,8 +57,8 @@ NCU_TRAFFIC = {
     "c1": 2.007860e9 + 0.223218e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
     "c2": 1.413981e9 + 0.518562e9,  # cdg_gemm_pair_kernel<128, 1>: profiles/cdg_gemm_pair_kernel128_c2_prefill.md
 }
-# per EP step on top of the GEMM(s): quant_rows, ep_count, ep_pack, ep_permute, ep_unpermute, ep_combine
-EP_LAUNCHES = 6
+# per EP step on top of the GEMM kernels: dispatch (quantise + pack), permute, return (or unpermute), combine
+EP_LAUNCHES = 4
 
 
 def gemm_bytes(rows, e_act, n, k):
@@ -391,7 +391,10 @@ def bench_ep_decode(args, dev, world, rank, dist):
 
     cfg = synthetic.CONFIGS["c1"]
     x, ids, w, b, sb = _ep_inputs(cfg, dev, rank, world, cfg.tokens)
-    layer = MoELayer(b, sb, num_experts=cfg.num_experts, group=dist.group.WORLD)
+    # fixed per-destination capacity, rows moved by the library's peer-memory stores over
+    # NVLink: no host synchronisation and no collective on the data path
+    layer = MoELayer(b, sb, num_experts=cfg.num_experts, group=dist.group.WORLD, max_tokens_per_rank=cfg.tokens,
+                     exchange=os.environ.get("CDG_EP_EXCHANGE", "p2p"))
     e_loc = cfg.num_experts // world
     mine = _global_counts(ids, cfg.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
     local_bytes, local_flops = _local_gemm_work(mine, cfg.n, cfg.k)
@@ -427,6 +430,9 @@ def bench_ep_decode(args, dev, world, rank, dist):
     e2e_ms, _ = timer.run(e2e_step, args.steps, with_kernel_events=False)
     clocks = sampler.stop()
     ms, e2e_ms, kernel_ms = _max_over_ranks(dist, dev, ms, e2e_ms, kernel_ms)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    layer.close()  # after every rank's last forward
     hbm_peak, _, peak_src = measured_peaks()
     achieved = local_bytes / (kernel_ms * 1e-3) / 1e9
     return {
@@ -437,6 +443,8 @@ def bench_ep_decode(args, dev, world, rank, dist):
                    "tokens_per_rank": cfg.tokens, "topk": cfg.topk, "parallelism": f"ep{world}",
                    "step": "quant, count all-to-all, dispatch all-to-all, grouped GEMM on local experts, "
                            "return all-to-all, weighted combine",
+                   "exchange": "fixed capacity per destination (tokens*topk rows), no host synchronisation; "
+                               + ("peer-memory stores over NVLink" if layer.exchange == "p2p" else "NCCL all-to-all"),
                    "l2": "weights per rank larger than L2"},
         "tflops": job_flops / (ms * 1e-3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",

@@ -102,7 +102,7 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs) -> N
     """M-grouped FP8 x FP4 GEMM for the MoE contiguous layout (see module docstring)."""
     _check_recipes(kwargs)
     x, sa, bt, bs, d, ids = _normalize(a, b, d, m_indices)
-    flags = 1 if kwargs.get("_force_exact_path") else 0
+    flags = (1 if kwargs.get("_force_exact_path") else 0) | (4 if kwargs.get("_skip_ungrouped_rows") else 0)
     native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags)
 
 

@@ -20,6 +20,20 @@ alignment, runs FC1 -> act -> FC2, and sends the rows back (all-to-all of BF16
 rows) for the weighted top-k sum.  Collectives go through torch.distributed
 (NCCL on GPUs); all compute runs in libcdg_b200.so kernels.
 
+With ``max_tokens_per_rank`` set, the exchange needs no host synchronisation: every
+rank quantises and packs its rows straight into a fixed-capacity region per
+destination (``max_tokens_per_rank * topk`` rows after a header row holding the
+per-expert counts), one equal-split all-to-all moves rows and counts together, the
+receiver derives the group layout from the headers on the device, and the GEMMs run
+over the worst-case padded row count, leaving rows outside every group unwritten.
+All ranks must use the same value and pass at most that many tokens.
+
+``exchange="p2p"`` (with ``max_tokens_per_rank``, GPUs of one NVLink domain) replaces
+the collectives by the library's own peer-memory exchange: each rank owns an exchange
+window shared through CUDA IPC; the dispatch kernel quantises and stores rows straight
+into the destination GPUs' windows, the return kernel stores GEMM rows straight back into
+the sources' windows, and release/acquire flags (bounded waits) order the steps.
+
 The device steps sit behind a small ``ops`` interface so that the exchange
 logic can also be exercised with CPU implementations (tests do that with the
 gloo backend).
@@ -55,9 +69,15 @@ class NativeOps:
     def permute(self, rows, hidden, local_experts, expert_off, m_pad):
         return self.C.ep_permute(rows, hidden, local_experts, expert_off, m_pad)
 
-    def gemm(self, a, sa, w, w_sf, m_indices):
+    def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap):
+        return self.C.ep_quant_pack_fixed(x, topk_ids, num_experts, ranks, cap)
+
+    def permute_fixed(self, rows, hidden, local_experts, ranks, cap, m_pad):
+        return self.C.ep_permute_fixed(rows, hidden, local_experts, ranks, cap, m_pad)
+
+    def gemm(self, a, sa, w, w_sf, m_indices, skip_ungrouped=False):
         d = torch.empty(a.shape[0], w.shape[1], dtype=torch.bfloat16, device=a.device)
-        m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices)
+        m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices, _skip_ungrouped_rows=skip_ungrouped)
         return d
 
     def act(self, h, m_indices):
@@ -77,6 +97,44 @@ def _all_to_all(out, inp, out_splits, in_splits, group):
     return out
 
 
+class PeerWindows:
+    """The exchange windows of all ranks of `group`, mapped into this process (CUDA IPC)."""
+
+    def __init__(self, group, cap: int, hidden: int, device):
+        import torch.distributed as dist
+
+        self.C = native.require()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        nbytes = self.C.ep_window_bytes(self.world, cap, hidden)
+        if nbytes == 0:
+            raise ValueError("unsupported peer exchange shape")
+        self.own, handle = self.C.ep_window_create(nbytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        ptrs, self.opened = [], []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self.own)
+            else:
+                ptrs.append(self.C.ep_window_open(h))
+                self.opened.append(ptrs[-1])
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        dist.barrier(group=group)  # every window is mapped everywhere before the first store
+
+    def status(self) -> int:
+        """0, or a nonzero code when a bounded wait on another rank's flag gave up."""
+        return self.C.ep_window_status(self.own)
+
+    def close(self):
+        for p in self.opened:
+            self.C.ep_window_close(p, True)
+        self.opened = []
+        if self.own:
+            self.C.ep_window_close(self.own, False)
+            self.own = 0
+
+
 class MoELayer:
     """An MoE layer whose experts are sharded over the ranks of ``group``.
 
@@ -86,8 +144,17 @@ class MoELayer:
     is the expert-parallel grouped GEMM alone: y[t] = sum_j topk_w[t, j] * FC1_e(q(x[t])).
     """
 
-    def __init__(self, w1, w1_scale, w2=None, w2_scale=None, num_experts: int = 0, group=None, ops=None):
+    def __init__(self, w1, w1_scale, w2=None, w2_scale=None, num_experts: int = 0, group=None, ops=None,
+                 max_tokens_per_rank: int | None = None, exchange: str = "nccl"):
         self.ops = ops or NativeOps()
+        self.max_tokens = max_tokens_per_rank
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        if exchange == "p2p" and max_tokens_per_rank is None:
+            raise ValueError("the peer-memory exchange needs max_tokens_per_rank (fixed capacity)")
+        self.exchange = exchange
+        self.windows = None
+        self.epoch = 0
         self.group = group
         if group is not None:
             import torch.distributed as dist
@@ -112,6 +179,10 @@ class MoELayer:
         self.inter = w1.shape[1] // 2
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor) -> torch.Tensor:
+        if self.world > 1 and self.exchange == "p2p":
+            return self._forward_p2p(x, topk_ids, topk_w)
+        if self.world > 1 and self.max_tokens is not None:
+            return self._forward_fixed(x, topk_ids, topk_w)
         ops, world, E, E_loc = self.ops, self.world, self.num_experts, self.local_experts
         dev = x.device
         topk_ids = topk_ids.contiguous()
@@ -157,5 +228,58 @@ class MoELayer:
         else:
             out_rows = back
         return ops.combine(out_rows, send_index, topk_w)
+
+    def _forward_fixed(self, x, topk_ids, topk_w):
+        """Exchange without a host synchronisation: fixed per-destination capacity."""
+        ops, world, E, E_loc, group = self.ops, self.world, self.num_experts, self.local_experts, self.group
+        dev = x.device
+        T, topk = topk_ids.shape
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens_per_rank={self.max_tokens}")
+        cap = self.max_tokens * topk  # rows any one destination can receive from this rank
+        topk_ids = topk_ids.contiguous()
+        topk_w = topk_w.to(torch.float32).contiguous()
+        sent, send_index = ops.quant_pack_fixed(x, topk_ids, E, world, cap)
+        recv = _all_to_all(torch.empty_like(sent), sent, None, None, group)
+        m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
+        a, sa, m_indices, perm_pos = ops.permute_fixed(recv, x.shape[1], E_loc, world, cap, m_pad)
+        h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        if self.w2 is not None:
+            aq, asc = ops.act(h, m_indices)
+            h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+        back = ops.unpermute(h, perm_pos)
+        out_rows = _all_to_all(torch.empty_like(back), back, None, None, group)
+        return ops.combine(out_rows, send_index, topk_w)
+
+    def _forward_p2p(self, x, topk_ids, topk_w):
+        """Fixed capacity, rows moved by the library's own peer-memory stores (no collective)."""
+        C, world, E, E_loc = native.require(), self.world, self.num_experts, self.local_experts
+        T, topk = topk_ids.shape
+        H = x.shape[1]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens_per_rank={self.max_tokens}")
+        if self.out_dim != H:
+            raise ValueError("the peer-memory exchange returns rows of the input width")
+        cap = self.max_tokens * topk
+        if self.windows is None:
+            self.windows = PeerWindows(self.group, cap, H, x.device)
+        win, me = self.windows, self.rank
+        self.epoch += 1
+        ep = self.epoch
+        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, me, ep)
+        m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
+        a, sa, m_indices, perm_pos = C.ep_permute_p2p(win.own, world, cap, H, E_loc, ep, m_pad, x)
+        h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        if self.w2 is not None:
+            aq, asc = self.ops.act(h, m_indices)
+            h = self.ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+        C.ep_return_p2p(h, perm_pos, world, cap, win.peers, me, ep)
+        return C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H, ep)
+
+    def close(self):
+        """Release the peer exchange windows (all ranks, after their last forward)."""
+        if self.windows is not None:
+            self.windows.close()
+            self.windows = None
 
     __call__ = forward

@@ -389,6 +389,8 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.tm = tm;
   ka.status = ctrl + kCtrlStatus;
   ka.zero_list = lists + kClassZero * nblk;
+  const bool skip_ungrouped = (g->flags & CDG_FLAG_SKIP_UNGROUPED) != 0;
+  ka.fill_rest = skip_ungrouped ? 0 : 1;
 
   if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
   if (g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2) {
@@ -400,7 +402,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     const unsigned grid = static_cast<unsigned>(di.sm_count / 2 * 2);
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
-    ka.do_zero_blocks = 1;
+    ka.do_zero_blocks = skip_ungrouped ? 0 : 1;
     if (launch_pdl(cdg_gemm_pair_kernel<16, 4>, grid, PairSmem<16, 4>::kThreads, PairSmem<16, 4>::kBytes, stream, tw,
                    p16, tsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
@@ -419,7 +421,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
-    ka.do_zero_blocks = 1;
+    ka.do_zero_blocks = skip_ungrouped ? 0 : 1;
     if (launch_pdl(cdg_gemm_kernel<16>, di.sm_count, 256, GemmSmem<16>::kBytes, stream, tw, ta16, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     // Narrow blocks (17 to 32 routed rows).

@@ -344,6 +344,7 @@ struct GemmArgs {
   TileMap tm;            // rows of each block
   int count_slot;        // ctrl index of this class's block count
   int do_zero_blocks;
+  int fill_rest;          // 1: zero the block's rows past its last routed row
   int* status;
 };
 
@@ -555,7 +556,7 @@ __global__ void __launch_bounds__(256, 1)
         zero_from = ntok;
       }
       // zero rows [zero_from, 128) of this block, columns [nt*128, nt*128+128), 16 B per store
-      const int rows = nrows - zero_from;
+      const int rows = p.fill_rest ? nrows - zero_from : 0;
       const uint4 z = make_uint4(0, 0, 0, 0);
       for (int c = tid; c < rows * 16; c += 128) {
         const int r = row0 + zero_from + (c >> 4);

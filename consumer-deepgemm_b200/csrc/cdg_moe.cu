@@ -7,6 +7,9 @@
 //   cdg_ep_count              routed rows per expert
 //   cdg_ep_pack               routed rows -> send buffer grouped by destination rank
 //   cdg_ep_permute            received rows -> 128-aligned contiguous layout per local expert
+//   cdg_ep_quant_pack_fixed   BF16 rows -> quantised packed rows in fixed-capacity regions
+//                             with per-expert count headers (exchange without host sync)
+//   cdg_ep_permute_fixed      fixed-capacity receive buffer -> contiguous layout
 //   cdg_ep_unpermute          GEMM rows -> received order
 //   cdg_ep_combine            returned rows -> weighted top-k sum per token
 //
@@ -17,7 +20,9 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <cstring>
 
 #include "cdg_b200.h"
 
@@ -32,6 +37,47 @@ __device__ __forceinline__ float load_f(const void* p, int dtype, int64_t i) {
 __device__ __forceinline__ int64_t load_idx(const void* p, int dtype, int64_t i) {
   return dtype == CDG_DTYPE_I64 ? static_cast<const int64_t*>(p)[i]
                                 : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
+}
+
+// ---- cross-GPU flags of the peer-memory exchange (system scope: the writer is another GPU)
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint64_t kPeerWaitNs = 2000000000ull;  // 2 s
+
+// Thread 0 of the CTA waits until flags[0 .. n) all reach `epoch` (bounded); the CTA then
+// proceeds only if they did.  A wait that gives up sets bit 0 of *status.
+__device__ bool wait_peer_flags(const int32_t* flags, int n, int32_t epoch, int32_t* status) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = now_ns();
+    for (int i = 0; i < n && ok; ++i) {
+      while (ld_acquire_sys(flags + i) < epoch) {
+        if (now_ns() - t0 > kPeerWaitNs) {
+          atomicOr(status, 1);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
 }
 
 // Quantise one 128-wide block held by a warp (4 values per lane) to e4m3 with the
@@ -147,20 +193,227 @@ __global__ void ep_permute_kernel(const uint8_t* rows, int64_t R, int64_t H, con
   }
 }
 
-// One warp per row: out[i, :] = Y[perm_pos[i], :].
+// Fixed-capacity exchange layout: per destination rank a region of 1 + cap packed rows.
+// Row 0 of a region is a header holding, as int32, the number of rows the sender
+// routed to each of the destination's local experts; rows 1 .. n follow (n = the sum of
+// the header), the rest of the region is unused.  The receive buffer has the same
+// layout per source rank, so the counts arrive with the rows in one all-to-all.
+constexpr int kFixedMaxExperts = 1024, kFixedMaxRanks = 256;
+
+// One CTA of 4 warps per routed (token, slot): thread 0 takes the row's slot in the
+// destination's region, then the warps quantise the token's row (per_block_cast_to_fp8
+// recipe, 128-column blocks dealt round-robin to the warps) straight into it.
+// Per-destination, per-local-expert counts go to `scratch`; the last CTA writes them into
+// the region headers.  scratch (zeroed by the host): [ranks] fill, [ranks * E_local]
+// counts, [1] ticket.
+// Peer variant (peers != nullptr): the region of destination d is in d's exchange window,
+// `peers[d] + region_off`; after every row and header landed, the last CTA raises this
+// rank's flag in each destination window (`peers[d] + flag_off`, index `me`) to `epoch`.
+__global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x, int x_dtype, int64_t x_stride,
+                                                                  const void* ids, int ids_dtype, int64_t T,
+                                                                  int64_t topk, int64_t E, int64_t e_per_rank,
+                                                                  int64_t ranks, int64_t H, int64_t cap,
+                                                                  int32_t* scratch, uint8_t* out_rows,
+                                                                  int32_t* send_index, const uint64_t* peers = nullptr,
+                                                                  int64_t region_off = 0, int64_t flag_off = 0,
+                                                                  int me = 0, int32_t epoch = 0) {
+  __shared__ int s_last;
+  __shared__ int64_t s_row, s_e;
+  int32_t* fill = scratch;
+  int32_t* cnt = scratch + ranks;
+  int32_t* ticket = cnt + ranks * e_per_rank;
+  const int64_t w = blockIdx.x;  // the (token, slot) of this CTA
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rb = packed_row_bytes(H);
+  if (threadIdx.x == 0) {
+    int64_t row = -1;
+    const int64_t e = w < T * topk ? load_idx(ids, ids_dtype, w) : -1;
+    if (e >= 0 && e < E) {
+      const int64_t dest = e / e_per_rank;
+      const int slot = atomicAdd(&fill[dest], 1);
+      atomicAdd(&cnt[dest * e_per_rank + e % e_per_rank], 1);
+      if (slot < cap) row = dest * (cap + 1) + 1 + slot;
+    }
+    if (w < T * topk) send_index[w] = static_cast<int32_t>(row);
+    s_row = row;
+    s_e = e;
+  }
+  __syncthreads();
+  const int64_t row = s_row;
+  // where a row of the send layout (region d = row / (cap + 1)) lands
+  auto row_ptr = [&](int64_t r) -> uint8_t* {
+    if (!peers) return out_rows + r * rb;
+    const int64_t d = r / (cap + 1);
+    return reinterpret_cast<uint8_t*>(peers[d]) + region_off + (r - d * (cap + 1)) * rb;
+  };
+  if (row >= 0) {
+    const int64_t t = w / topk;
+    uint8_t* out = row_ptr(row);
+    float* out_s = reinterpret_cast<float*>(out + H);
+    for (int64_t kb = warp; kb < H / 128; kb += blockDim.x / 32) {
+      float v[4];
+      const int64_t base = t * x_stride + kb * 128 + lane * 4;
+      if (x_dtype == CDG_DTYPE_BF16) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + base);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
+        v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+      } else {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + base);
+        v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+      }
+      quant_block_warp(v, out + kb * 128, out_s + kb, lane);
+    }
+    if (threadIdx.x == 0) *reinterpret_cast<int32_t*>(out + H + 4 * (H / 128)) = static_cast<int32_t>(s_e % e_per_rank);
+  }
+  // the last CTA to finish writes the region headers (and, peer variant, the flags); every
+  // thread fences its own row stores before the CTA takes its ticket
+  if (peers) __threadfence_system(); else __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int64_t i = threadIdx.x; i < ranks * e_per_rank; i += blockDim.x) {
+    const int64_t d = i / e_per_rank, e = i - d * e_per_rank;
+    reinterpret_cast<int32_t*>(row_ptr(d * (cap + 1)))[e] = __ldcg(&cnt[i]);
+  }
+  if (peers) {
+    __threadfence_system();
+    __syncthreads();
+    for (int64_t d = threadIdx.x; d < ranks; d += blockDim.x)
+      st_release_sys(reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(peers[d]) + flag_off) + me, epoch);
+  }
+}
+
+// Every CTA first derives, in shared memory, each source's row count and the 128-aligned
+// offsets of the local experts' groups (exclusive scan of the per-expert totals over all
+// sources, read from the region headers); then one warp per slot places valid rows as
+// ep_permute_kernel does.
+// Peer variant (flags != nullptr): first waits until every source raised its flag to `epoch`.
+__global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* rows, int64_t ranks, int64_t cap,
+                                                               int64_t H, int64_t E_local, int32_t* fill, uint8_t* A,
+                                                               float* SA, int32_t* m_indices, int32_t* perm_pos,
+                                                               const int32_t* flags = nullptr, int32_t epoch = 0,
+                                                               int32_t* status = nullptr) {
+  __shared__ int64_t s_off[kFixedMaxExperts];
+  __shared__ int32_t s_nsrc[kFixedMaxRanks];
+  __shared__ int64_t s_warp_sum[8];
+  if (flags && !wait_peer_flags(flags, static_cast<int>(ranks), epoch, status)) return;
+  const int tid = threadIdx.x;
+  const int64_t rb = packed_row_bytes(H);
+  auto header = [&](int64_t r) { return reinterpret_cast<const int32_t*>(rows + r * (cap + 1) * rb); };
+  // per-expert aligned totals, 4 consecutive experts per thread, then a block scan
+  int64_t part[4];
+  int64_t run = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t e = tid * 4 + i;
+    int64_t tot = 0;
+    if (e < E_local)
+      for (int64_t r = 0; r < ranks; ++r) tot += header(r)[e];
+    part[i] = (tot + 127) / 128 * 128;
+    run += part[i];
+  }
+  const int lane = tid & 31, warp = tid >> 5;
+  int64_t incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp_sum[warp] = incl;
+  for (int64_t r = tid; r < ranks; r += blockDim.x) {
+    int32_t n = 0;
+    for (int64_t e = 0; e < E_local; ++e) n += header(r)[e];
+    s_nsrc[r] = n;
+  }
+  __syncthreads();
+  int64_t base = 0;
+  for (int w = 0; w < warp; ++w) base += s_warp_sum[w];
+  int64_t off = base + incl - run;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t e = tid * 4 + i;
+    if (e < E_local) s_off[e] = off;
+    off += part[i];
+  }
+  __syncthreads();
+  const int64_t R = ranks * (cap + 1);
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + tid) >> 5; w < R;
+       w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t src = w / (cap + 1), slot = w - src * (cap + 1) - 1;
+    if (slot < 0 || slot >= s_nsrc[src]) {
+      if (lane == 0) perm_pos[w] = -1;
+      continue;
+    }
+    const uint8_t* in = rows + w * rb;
+    const int e = *reinterpret_cast<const int32_t*>(in + H + 4 * (H / 128));
+    int slot_e = 0;
+    if (lane == 0) slot_e = atomicAdd(&fill[e], 1);
+    const int64_t pos = s_off[e] + __shfl_sync(0xffffffffu, slot_e, 0);
+    const uint4* src4 = reinterpret_cast<const uint4*>(in);
+    uint4* dst = reinterpret_cast<uint4*>(A + pos * H);
+    for (int64_t c = lane; c < H / 16; c += 32) dst[c] = src4[c];
+    const float* rs = reinterpret_cast<const float*>(in + H);
+    for (int64_t c = lane; c < H / 128; c += 32) SA[pos * (H / 128) + c] = rs[c];
+    if (lane == 0) {
+      m_indices[pos] = e;
+      perm_pos[w] = static_cast<int32_t>(pos);
+    }
+  }
+}
+
+// Peer return: one warp per received slot (region src, slot s) whose row was placed at
+// perm_pos; the GEMM row goes straight to the source's window, at the row of its own
+// send layout (me * (cap + 1) + 1 + s) in `peers[src] + ret_off`.  The last CTA raises
+// this rank's flag in every source window (`peers[src] + flag_off`, index `me`).
+// scratch: [1] ticket, zeroed by the host.
+__global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* Y, int64_t y_stride,
+                                                            const int32_t* perm_pos, int64_t ranks, int64_t cap,
+                                                            int64_t H, const uint64_t* peers, int64_t ret_off,
+                                                            int64_t flag_off, int me, int32_t epoch,
+                                                            int32_t* scratch) {
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31;
+  const int64_t R = ranks * (cap + 1);
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < R;
+       w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const int32_t pos = perm_pos[w];
+    if (pos < 0) continue;
+    const int64_t src = w / (cap + 1), s = w - src * (cap + 1);
+    const uint4* from = reinterpret_cast<const uint4*>(Y + static_cast<int64_t>(pos) * y_stride);
+    uint4* to = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peers[src]) + ret_off +
+                                         (me * (cap + 1) + s) * H * static_cast<int64_t>(sizeof(__nv_bfloat16)));
+    for (int64_t c = lane; c < H / 8; c += 32) to[c] = from[c];
+  }
+  __threadfence_system();  // each thread's peer stores before the CTA takes its ticket
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(scratch, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  for (int64_t r = threadIdx.x; r < ranks; r += blockDim.x)
+    st_release_sys(reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(peers[r]) + flag_off) + me, epoch);
+}
+
+// One warp per row: out[i, :] = Y[perm_pos[i], :]; rows with perm_pos -1 are left as they are.
 __global__ void ep_unpermute_kernel(const __nv_bfloat16* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R,
                                     int64_t H, __nv_bfloat16* out) {
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (w >= R) return;
+  if (w >= R || perm_pos[w] < 0) return;
   const uint4* src = reinterpret_cast<const uint4*>(Y + static_cast<int64_t>(perm_pos[w]) * y_stride);
   uint4* dst = reinterpret_cast<uint4*>(out + w * H);
   for (int64_t c = lane; c < H / 8; c += 32) dst[c] = src[c];
 }
 
 // One CTA per token; y[t, :] = bf16(sum_j w[t, j] * rows[send_index[t*k + j], :]) in FP32, slots in order.
+// Peer variant (flags != nullptr): first waits until every rank returned its rows.
 __global__ void ep_combine_kernel(const __nv_bfloat16* rows, const int32_t* send_index, const float* topk_w, int64_t T,
-                                  int64_t topk, int64_t H, __nv_bfloat16* y) {
+                                  int64_t topk, int64_t H, __nv_bfloat16* y, const int32_t* flags = nullptr,
+                                  int ranks = 0, int32_t epoch = 0, int32_t* status = nullptr) {
+  if (flags && !wait_peer_flags(flags, ranks, epoch, status)) return;
   const int64_t t = blockIdx.x;
   if (t >= T) return;
   for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
@@ -174,6 +427,21 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, const int32_t* send
 }
 
 unsigned warp_grid(int64_t warps) { return static_cast<unsigned>((warps * 32 + 255) / 256); }
+
+// Exchange window of one rank: [0, 512) dispatch flags int32[ranks], [512, 1024) return
+// flags int32[ranks], [1024, 1028) status; from 4096 the receive regions
+// [2 parity][ranks source][1 + cap rows][row bytes]; then (256-aligned) the return rows
+// [2 parity][ranks * (1 + cap)][H] BF16 in this rank's own send layout.
+struct Window {
+  int64_t ranks, cap, H, rb;
+  static constexpr int64_t kDispatchFlags = 0, kReturnFlags = 512, kStatus = 1024, kRecv = 4096;
+  __host__ __device__ int64_t recv_parity(int64_t parity) const { return kRecv + parity * ranks * (cap + 1) * rb; }
+  __host__ __device__ int64_t ret_base() const { return (recv_parity(2) + 255) / 256 * 256; }
+  __host__ __device__ int64_t ret_parity(int64_t parity) const { return ret_base() + parity * ranks * (cap + 1) * H * 2; }
+  __host__ __device__ int64_t bytes() const { return ret_parity(2); }
+};
+
+Window make_window(int64_t ranks, int64_t cap, int64_t H) { return Window{ranks, cap, H, packed_row_bytes(H)}; }
 
 int launched() { return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA; }
 
@@ -247,6 +515,47 @@ int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_loc
   return cdg::launched();
 }
 
+int64_t cdg_ep_fixed_scratch_ints(int64_t ranks, int64_t E) {
+  return ranks > 0 && E > 0 && E % ranks == 0 ? ranks + E + 1 : 0;
+}
+
+int cdg_ep_quant_pack_fixed(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
+                            int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap, int32_t* scratch,
+                            uint8_t* out_rows, int32_t* send_index, cdg_stream_t stream) {
+  if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || ranks > cdg::kFixedMaxRanks || E % ranks || H <= 0 || H % 128 ||
+      cap < 0 || E / ranks > cdg::kFixedMaxExperts || !scratch || !out_rows)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (4 * (E / ranks) > cdg::packed_row_bytes(H)) return CDG_ERR_INVALID_ARGUMENT;  // header fits a row
+  if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
+  if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(out_rows) % 16) return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scratch, 0, cdg_ep_fixed_scratch_ints(ranks, E) * sizeof(int32_t), st) != cudaSuccess)
+    return CDG_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4) return CDG_ERR_ALIGNMENT;  // vector loads of 4 values
+  const unsigned grid = T * topk > 0 ? static_cast<unsigned>(T * topk) : 1u;
+  cdg::ep_quant_pack_fixed_kernel<<<grid, 128, 0, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E, E / ranks,
+                                                        ranks, H, cap, scratch, out_rows, send_index);
+  return cdg::launched();
+}
+
+int cdg_ep_permute_fixed(const uint8_t* recv_rows, int64_t ranks, int64_t cap, int64_t H, int64_t E_local,
+                         int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+                         cdg_stream_t stream) {
+  if (ranks <= 0 || ranks > cdg::kFixedMaxRanks || cap < 0 || H <= 0 || H % 128 || E_local <= 0 ||
+      E_local > cdg::kFixedMaxExperts || M_pad < ranks * cap + 127 * E_local)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(recv_rows) % 16 || reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const int64_t R = ranks * (cap + 1);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
+  cdg::ep_permute_fixed_kernel<<<grid, 256, 0, st>>>(recv_rows, ranks, cap, H, E_local, fill, A, SA, m_indices,
+                                                     perm_pos);
+  return cdg::launched();
+}
+
 int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R, int64_t H, void* out,
                      cdg_stream_t stream) {
   if (R < 0 || H <= 0 || H % 8) return CDG_ERR_INVALID_ARGUMENT;
@@ -264,6 +573,127 @@ int cdg_ep_combine(const void* rows, const int32_t* send_index, const float* top
   if (T == 0) return CDG_OK;
   cdg::ep_combine_kernel<<<static_cast<unsigned>(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(rows), send_index, topk_w, T, topk, H, static_cast<__nv_bfloat16*>(y));
+  return cdg::launched();
+}
+
+// ---------------------------------------------------------------- peer-memory exchange
+size_t cdg_ep_window_bytes(int64_t ranks, int64_t cap, int64_t H) {
+  if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128) return 0;
+  return static_cast<size_t>(cdg::make_window(ranks, cap, H).bytes());
+}
+
+int cdg_ep_window_create(size_t bytes, void** window, void* ipc_handle) {
+  if (!bytes || !window || !ipc_handle) return CDG_ERR_INVALID_ARGUMENT;
+  *window = nullptr;
+  if (cudaMalloc(window, bytes) != cudaSuccess) return CDG_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(*window, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, *window) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(*window);
+    *window = nullptr;
+    return CDG_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  return CDG_OK;
+}
+
+int cdg_ep_window_open(const void* ipc_handle, void** window) {
+  if (!ipc_handle || !window) return CDG_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(window, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
+}
+
+int cdg_ep_window_close(void* window, int32_t opened) {
+  if (!window) return CDG_OK;
+  return (opened ? cudaIpcCloseMemHandle(window) : cudaFree(window)) == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
+}
+
+int cdg_ep_window_status(const void* window, cdg_stream_t stream) {
+  if (!window) return CDG_ERR_INVALID_ARGUMENT;
+  int32_t word = 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&word, static_cast<const uint8_t*>(window) + cdg::Window::kStatus, 4, cudaMemcpyDeviceToHost,
+                      st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return CDG_ERR_CUDA;
+  return word ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
+}
+
+int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
+                        int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
+                        const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, int32_t* send_index,
+                        cdg_stream_t stream) {
+  if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || ranks > 128 || E % ranks || H <= 0 || H % 128 || cap < 0 ||
+      E / ranks > cdg::kFixedMaxExperts || !scratch || !peers || me < 0 || me >= ranks || epoch <= 0)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (4 * (E / ranks) > cdg::packed_row_bytes(H)) return CDG_ERR_INVALID_ARGUMENT;
+  if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
+  if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4) return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scratch, 0, cdg_ep_fixed_scratch_ints(ranks, E) * sizeof(int32_t), st) != cudaSuccess)
+    return CDG_ERR_CUDA;
+  const cdg::Window win = cdg::make_window(ranks, cap, H);
+  const int64_t parity = epoch & 1;
+  const int64_t region_off = win.recv_parity(parity) + static_cast<int64_t>(me) * (cap + 1) * win.rb;
+  const unsigned grid = T * topk > 0 ? static_cast<unsigned>(T * topk) : 1u;
+  cdg::ep_quant_pack_fixed_kernel<<<grid, 128, 0, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E,
+                                                        E / ranks, ranks, H, cap, scratch, nullptr, send_index, peers,
+                                                        region_off, cdg::Window::kDispatchFlags, me, epoch);
+  return cdg::launched();
+}
+
+int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t epoch,
+                       int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+                       cdg_stream_t stream) {
+  if (!window || ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || E_local <= 0 ||
+      E_local > cdg::kFixedMaxExperts || M_pad < ranks * cap + 127 * E_local || epoch <= 0)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::Window win = cdg::make_window(ranks, cap, H);
+  uint8_t* base = static_cast<uint8_t*>(window);
+  const int64_t R = ranks * (cap + 1);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
+  cdg::ep_permute_fixed_kernel<<<grid, 256, 0, st>>>(
+      base + win.recv_parity(epoch & 1), ranks, cap, H, E_local, fill, A, SA, m_indices, perm_pos,
+      reinterpret_cast<const int32_t*>(base + cdg::Window::kDispatchFlags), epoch,
+      reinterpret_cast<int32_t*>(base + cdg::Window::kStatus));
+  return cdg::launched();
+}
+
+int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t ranks, int64_t cap, int64_t H,
+                      const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, cdg_stream_t stream) {
+  if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || !peers || !scratch || me < 0 || me >= ranks ||
+      epoch <= 0)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(Y) % 16 || y_stride % 8) return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::Window win = cdg::make_window(ranks, cap, H);
+  const int64_t R = ranks * (cap + 1);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
+  cdg::ep_return_p2p_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(Y), y_stride, perm_pos, ranks, cap,
+                                                  H, peers, win.ret_parity(epoch & 1), cdg::Window::kReturnFlags, me,
+                                                  epoch, scratch);
+  return cdg::launched();
+}
+
+int cdg_ep_combine_p2p(const void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
+                       int64_t H, int64_t ranks, int64_t cap, int32_t epoch, void* y, cdg_stream_t stream) {
+  if (!window || T < 0 || topk <= 0 || H <= 0 || H % 128 || ranks <= 0 || ranks > 128 || cap < 0 || epoch <= 0)
+    return CDG_ERR_INVALID_ARGUMENT;
+  const cdg::Window win = cdg::make_window(ranks, cap, H);
+  const uint8_t* base = static_cast<const uint8_t*>(window);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = T > 0 ? static_cast<unsigned>(T) : 1u;
+  cdg::ep_combine_kernel<<<grid, 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(base + win.ret_parity(epoch & 1)), send_index, topk_w, T, topk, H,
+      static_cast<__nv_bfloat16*>(y), reinterpret_cast<const int32_t*>(base + cdg::Window::kReturnFlags),
+      static_cast<int>(ranks), epoch, reinterpret_cast<int32_t*>(const_cast<uint8_t*>(base) + cdg::Window::kStatus));
   return cdg::launched();
 }
 

@@ -314,7 +314,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
           mbar_arrive_cluster(tempty0 + acc * 8);
         zero_from = ntok;
       }
-      const int rows = nrows - zero_from;
+      const int rows = p.fill_rest ? nrows - zero_from : 0;
       const uint4 z = make_uint4(0, 0, 0, 0);
       for (int c = tid; c < rows * 16; c += 128) {
         const int r = row0 + zero_from + (c >> 4);

@@ -265,6 +265,125 @@ std::vector<torch::Tensor> ep_permute(const torch::Tensor& rows, int64_t H, int6
   return {A, SA, mi, pos};
 }
 
+// Fixed-capacity send buffer: (packed rows uint8 [ranks*(cap+1), row_bytes], send_index [T*topk]).
+std::vector<torch::Tensor> ep_quant_pack_fixed(const torch::Tensor& x, const torch::Tensor& ids, int64_t E,
+                                               int64_t ranks, int64_t cap) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
+  TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
+              "topk ids must be contiguous [T, topk]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), H = x.size(1), topk = ids.size(1);
+  auto out = torch::empty({ranks * (cap + 1), cdg_ep_row_bytes(H)}, x.options().dtype(torch::kUInt8));
+  auto send_index = torch::empty({T * topk}, ids.options().dtype(torch::kInt32));
+  auto scratch = torch::empty({std::max<int64_t>(cdg_ep_fixed_scratch_ints(ranks, E), 1)},
+                              ids.options().dtype(torch::kInt32));
+  check_status(cdg_ep_quant_pack_fixed(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T,
+                                       topk, E, ranks, H, cap, scratch.data_ptr<int32_t>(), out.data_ptr<uint8_t>(),
+                                       send_index.data_ptr<int32_t>(), cur_stream(x)),
+               "ep_quant_pack_fixed");
+  return {out, send_index};
+}
+
+// Fixed-capacity receive buffer -> (A, SA, m_indices, perm_pos).
+std::vector<torch::Tensor> ep_permute_fixed(const torch::Tensor& rows, int64_t H, int64_t E_local, int64_t ranks,
+                                            int64_t cap, int64_t M_pad) {
+  TORCH_CHECK(rows.is_cuda() && rows.dim() == 2 && rows.is_contiguous() && rows.scalar_type() == torch::kUInt8 &&
+                  rows.size(1) == cdg_ep_row_bytes(H) && rows.size(0) == ranks * (cap + 1),
+              "received rows must be a contiguous fixed-capacity buffer [ranks*(cap+1), row_bytes]");
+  const c10::cuda::CUDAGuard guard(rows.device());
+  auto i32 = rows.options().dtype(torch::kInt32);
+  auto A = torch::empty({M_pad, H}, rows.options().dtype(torch::kFloat8_e4m3fn));
+  auto SA = torch::empty({M_pad, H / 128}, rows.options().dtype(torch::kFloat32));
+  auto mi = torch::empty({M_pad}, i32);
+  auto pos = torch::empty({rows.size(0)}, i32);
+  auto fill = torch::empty({E_local}, i32);
+  check_status(cdg_ep_permute_fixed(rows.data_ptr<uint8_t>(), ranks, cap, H, E_local, fill.data_ptr<int32_t>(),
+                                    reinterpret_cast<uint8_t*>(A.data_ptr()), SA.data_ptr<float>(),
+                                    mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(), cur_stream(rows)),
+               "ep_permute_fixed");
+  return {A, SA, mi, pos};
+}
+
+// ------------------------------------------------------------------ peer-memory exchange
+py::tuple ep_window_create(int64_t bytes) {
+  void* w = nullptr;
+  char handle[64];
+  check_status(cdg_ep_window_create(static_cast<size_t>(bytes), &w, handle), "ep_window_create");
+  return py::make_tuple(reinterpret_cast<uint64_t>(w), py::bytes(handle, 64));
+}
+
+uint64_t ep_window_open(const py::bytes& handle) {
+  std::string h = handle;
+  TORCH_CHECK_VALUE(h.size() == 64, "an exchange window handle is 64 bytes");
+  void* w = nullptr;
+  check_status(cdg_ep_window_open(h.data(), &w), "ep_window_open");
+  return reinterpret_cast<uint64_t>(w);
+}
+
+torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, int64_t E, int64_t ranks, int64_t cap,
+                              const torch::Tensor& peers, int64_t me, int64_t epoch) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
+  TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
+              "topk ids must be contiguous [T, topk]");
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64 && peers.numel() == ranks,
+              "peers: int64 [ranks] window addresses on the device");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), H = x.size(1), topk = ids.size(1);
+  auto send_index = torch::empty({T * topk}, ids.options().dtype(torch::kInt32));
+  auto scratch = torch::empty({std::max<int64_t>(cdg_ep_fixed_scratch_ints(ranks, E), 1)},
+                              ids.options().dtype(torch::kInt32));
+  check_status(cdg_ep_dispatch_p2p(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T, topk,
+                                   E, ranks, H, cap, reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+                                   static_cast<int32_t>(me), static_cast<int32_t>(epoch), scratch.data_ptr<int32_t>(),
+                                   send_index.data_ptr<int32_t>(), cur_stream(x)),
+               "ep_dispatch_p2p");
+  return send_index;
+}
+
+std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local,
+                                          int64_t epoch, int64_t M_pad, const torch::Tensor& like) {
+  const c10::cuda::CUDAGuard guard(like.device());
+  auto i32 = like.options().dtype(torch::kInt32);
+  auto A = torch::empty({M_pad, H}, like.options().dtype(torch::kFloat8_e4m3fn));
+  auto SA = torch::empty({M_pad, H / 128}, like.options().dtype(torch::kFloat32));
+  auto mi = torch::empty({M_pad}, i32);
+  auto pos = torch::empty({ranks * (cap + 1)}, i32);
+  auto fill = torch::empty({E_local}, i32);
+  check_status(cdg_ep_permute_p2p(reinterpret_cast<void*>(window), ranks, cap, H, E_local, static_cast<int32_t>(epoch),
+                                  fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()),
+                                  SA.data_ptr<float>(), mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(),
+                                  cur_stream(like)),
+               "ep_permute_p2p");
+  return {A, SA, mi, pos};
+}
+
+void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& perm_pos, int64_t ranks, int64_t cap,
+                   const torch::Tensor& peers, int64_t me, int64_t epoch) {
+  TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
+  TORCH_CHECK(perm_pos.numel() == ranks * (cap + 1), "perm_pos: one entry per received slot");
+  const c10::cuda::CUDAGuard guard(Y.device());
+  auto scratch = torch::empty({1}, perm_pos.options());
+  check_status(cdg_ep_return_p2p(Y.data_ptr(), Y.stride(0), perm_pos.data_ptr<int32_t>(), ranks, cap, Y.size(1),
+                                 reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), static_cast<int32_t>(me),
+                                 static_cast<int32_t>(epoch), scratch.data_ptr<int32_t>(), cur_stream(Y)),
+               "ep_return_p2p");
+}
+
+torch::Tensor ep_combine_p2p(uint64_t window, const torch::Tensor& send_index, const torch::Tensor& topk_w,
+                             int64_t ranks, int64_t cap, int64_t H, int64_t epoch) {
+  TORCH_CHECK(topk_w.is_cuda() && topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() &&
+                  topk_w.dim() == 2 && send_index.numel() == topk_w.numel(),
+              "topk weights: FP32 [T, topk] matching send_index");
+  const c10::cuda::CUDAGuard guard(topk_w.device());
+  const int64_t T = topk_w.size(0), topk = topk_w.size(1);
+  auto y = torch::empty({T, H}, topk_w.options().dtype(torch::kBFloat16));
+  check_status(cdg_ep_combine_p2p(reinterpret_cast<void*>(window), send_index.data_ptr<int32_t>(),
+                                  topk_w.data_ptr<float>(), T, topk, H, ranks, cap, static_cast<int32_t>(epoch),
+                                  y.data_ptr(), cur_stream(topk_w)),
+               "ep_combine_p2p");
+  return y;
+}
+
 torch::Tensor ep_unpermute(const torch::Tensor& Y, const torch::Tensor& perm_pos) {
   TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
   const c10::cuda::CUDAGuard guard(Y.device());
@@ -314,6 +433,35 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ranks"), py::arg("send_off"), py::arg("rows"));
   m.def("ep_permute", &ep_permute, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("expert_off"), py::arg("m_pad"));
+  m.def("ep_quant_pack_fixed", &ep_quant_pack_fixed, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
+        py::arg("ranks"), py::arg("cap"));
+  m.def("ep_permute_fixed", &ep_permute_fixed, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
+        py::arg("ranks"), py::arg("cap"), py::arg("m_pad"));
+  m.def("ep_window_bytes", [](int64_t ranks, int64_t cap, int64_t H) { return cdg_ep_window_bytes(ranks, cap, H); },
+        py::arg("ranks"), py::arg("cap"), py::arg("hidden"));
+  m.def("ep_window_create", &ep_window_create, py::arg("bytes"));
+  m.def("ep_window_open", &ep_window_open, py::arg("handle"));
+  m.def(
+      "ep_window_close",
+      [](uint64_t w, bool opened) {
+        check_status(cdg_ep_window_close(reinterpret_cast<void*>(w), opened ? 1 : 0), "ep_window_close");
+      },
+      py::arg("window"), py::arg("opened"));
+  m.def(
+      "ep_window_status",
+      [](uint64_t w) {
+        return cdg_ep_window_status(reinterpret_cast<void*>(w),
+                                    reinterpret_cast<cdg_stream_t>(at::cuda::getCurrentCUDAStream().stream()));
+      },
+      py::arg("window"));
+  m.def("ep_dispatch_p2p", &ep_dispatch_p2p, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
+        py::arg("ranks"), py::arg("cap"), py::arg("peers"), py::arg("me"), py::arg("epoch"));
+  m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("cap"), py::arg("hidden"),
+        py::arg("local_experts"), py::arg("epoch"), py::arg("m_pad"), py::arg("like"));
+  m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("perm_pos"), py::arg("ranks"), py::arg("cap"),
+        py::arg("peers"), py::arg("me"), py::arg("epoch"));
+  m.def("ep_combine_p2p", &ep_combine_p2p, py::arg("window"), py::arg("send_index"), py::arg("topk_w"),
+        py::arg("ranks"), py::arg("cap"), py::arg("hidden"), py::arg("epoch"));
   m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
   m.def("ep_unpermute", &ep_unpermute, py::arg("y"), py::arg("perm_pos"));
   m.def("ep_combine", &ep_combine, py::arg("rows"), py::arg("send_index"), py::arg("topk_w"));

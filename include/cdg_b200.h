@@ -111,6 +111,9 @@ typedef struct cdg_gemm_args {
 #define CDG_FLAG_FORCE_GENERIC 1 /* run the exact SIMT path even where the tensor-core path applies */
 #define CDG_FLAG_SINGLE_CTA 2    /* tensor-core path: one CTA per 128-column tile even where N % 256 == 0
                                     would allow CTA pairs (for comparisons; same results) */
+#define CDG_FLAG_SKIP_UNGROUPED 4 /* rows of D outside every group may be left unwritten instead of
+                                     zeroed (for callers that never read them, e.g. a layer's own padded
+                                     buffers); the reference always zeroes them */
 
 /* Grouped FP8 x MXFP4 GEMM, contiguous layout.
  * Replaces m_grouped_fp8_fp4_gemm_nt_contiguous (consumer_deep_gemm/gemm.py:467-470),
@@ -247,7 +250,63 @@ int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_loc
                    int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                    cdg_stream_t stream);
 
-/* out[i, :] = Y[perm_pos[i], :] (BF16 rows of length H). */
+/* Fixed-capacity exchange (no host synchronisation).  The send (and receive) buffer holds
+ * per destination (source) rank a region of 1 + cap packed rows of cdg_ep_row_bytes(H):
+ * row 0 a header with the int32 number of rows routed to each of that rank's E/ranks local
+ * experts, then the rows themselves.
+ *
+ * cdg_ep_quant_pack_fixed quantises token t's BF16/FP32 row (1x128 e4m3 + FP32 scales, the
+ * per_block_cast_to_fp8 recipe) into a packed row of the region of rank e / (E / ranks) for
+ * every slot j with expert e = topk_ids[t, j] in [0, E); send_index[t*topk + j] is that row
+ * (-1 for skipped slots and for slots beyond `cap`, which the caller should size to
+ * T * topk to drop nothing).  `scratch` is int32 [cdg_ep_fixed_scratch_ints(ranks, E)],
+ * zeroed by the call. */
+int64_t cdg_ep_fixed_scratch_ints(int64_t ranks, int64_t E);
+int cdg_ep_quant_pack_fixed(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
+                            int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap, int32_t* scratch,
+                            uint8_t* out_rows, int32_t* send_index, cdg_stream_t stream);
+
+/* Fixed-capacity receive buffer -> contiguous layout (group offsets derived on the device
+ * from the headers).  M_pad must be at least ranks*cap + 127*E_local (the worst case);
+ * m_indices is -1 on every other row; perm_pos[i] is row i's position or -1 for headers and
+ * unused rows.  E_local <= 1024, ranks <= 256, 4*E_local <= cdg_ep_row_bytes(H). */
+int cdg_ep_permute_fixed(const uint8_t* recv_rows, int64_t ranks, int64_t cap, int64_t H, int64_t E_local,
+                         int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+                         cdg_stream_t stream);
+
+/* Peer-memory exchange (expert parallelism over NVLink without a collective library).
+ * Every rank owns an exchange window (cdg_ep_window_bytes) shared with the other ranks
+ * through CUDA IPC: create it with cdg_ep_window_create, send the 64-byte handle to the
+ * other ranks (any host channel), open theirs with cdg_ep_window_open, and pass the
+ * ranks' window addresses as a device array `peers` (uint64 [ranks], this rank's own
+ * window at index `me`).  A forward pass uses one `epoch` (1, 2, ... the same on every
+ * rank; windows are double-buffered by its parity):
+ *   cdg_ep_dispatch_p2p   quantise + pack (as cdg_ep_quant_pack_fixed) straight into each
+ *                         destination's window, then raise this rank's flag there;
+ *   cdg_ep_permute_p2p    wait (bounded) for every source's flag, then permute (as
+ *                         cdg_ep_permute_fixed) from the own window;
+ *   cdg_ep_return_p2p     store each GEMM row straight into its source's window, raise flags;
+ *   cdg_ep_combine_p2p    wait for every rank's rows, then combine (as cdg_ep_combine).
+ * Plain stores and loads over NVLink: no multicast.  A wait that gives up after 2 s skips
+ * its CTA's work and sets the window's status word (cdg_ep_window_status reports it). */
+size_t cdg_ep_window_bytes(int64_t ranks, int64_t cap, int64_t H);
+int cdg_ep_window_create(size_t bytes, void** window, void* ipc_handle /* 64 bytes out */);
+int cdg_ep_window_open(const void* ipc_handle, void** window);
+int cdg_ep_window_close(void* window, int32_t opened);
+int cdg_ep_window_status(const void* window, cdg_stream_t stream);
+int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
+                        int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
+                        const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, int32_t* send_index,
+                        cdg_stream_t stream);
+int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t epoch,
+                       int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+                       cdg_stream_t stream);
+int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t ranks, int64_t cap, int64_t H,
+                      const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, cdg_stream_t stream);
+int cdg_ep_combine_p2p(const void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
+                       int64_t H, int64_t ranks, int64_t cap, int32_t epoch, void* y, cdg_stream_t stream);
+
+/* out[i, :] = Y[perm_pos[i], :] (BF16 rows of length H); rows with perm_pos[i] = -1 are not written. */
 int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R, int64_t H, void* out,
                      cdg_stream_t stream);
 

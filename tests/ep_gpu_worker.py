@@ -30,18 +30,29 @@ def main():
     x, ids, w, w1, w1s, w2, w2s = (t.to(dev) for t in make_layer_inputs(**cfg))
     e_loc = cfg["experts"] // world
     sl = slice(rank * e_loc, (rank + 1) * e_loc)
-    layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=cfg["experts"], group=dist.group.WORLD)
     tpr = cfg["tokens"] // world
     ts = slice(rank * tpr, (rank + 1) * tpr)
-    y = layer(x[ts], ids[ts], w[ts])
-    parts = [torch.empty_like(y) for _ in range(world)]
-    dist.all_gather(parts, y)
-    if rank == 0:
-        y_ep = torch.cat(parts)
-        y_one = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"])(x, ids, w)
-        nw, rl2 = errors(y_ep, y_one)
-        assert nw <= 1e-3 and rl2 <= 1e-3, (nw, rl2)
-        print("EP_OK", nw, rl2, flush=True)
+    y_one = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"])(x, ids, w) if rank == 0 else None
+    # split-size exchange (one host sync) and fixed-capacity exchange (none)
+    # split-size exchange (one host sync), fixed-capacity NCCL exchange (none), and the
+    # library's peer-memory exchange (no collective), three forwards each (window parities)
+    for mode, max_tok, exchange in (("split_sizes", None, "nccl"), ("fixed_capacity", tpr, "nccl"),
+                                    ("peer_memory", tpr, "p2p")):
+        layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=cfg["experts"], group=dist.group.WORLD,
+                         max_tokens_per_rank=max_tok, exchange=exchange)
+        for it in range(3):
+            y = layer(x[ts], ids[ts], w[ts])
+            parts = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(parts, y)
+            if rank == 0:
+                nw, rl2 = errors(torch.cat(parts), y_one)
+                assert nw <= 1e-3 and rl2 <= 1e-3, (mode, it, nw, rl2)
+        if layer.windows is not None:
+            assert layer.windows.status() == 0, "a peer wait gave up"
+        dist.barrier()
+        layer.close()
+        if rank == 0:
+            print("EP_OK", mode, nw, rl2, flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

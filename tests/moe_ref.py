@@ -63,7 +63,60 @@ class TorchRefOps:
             m_indices[p], pos[i] = e, p
         return a, sa, m_indices, pos
 
-    def gemm(self, a, sa, w, w_sf, m_indices):
+    def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap):
+        """Regions of 1 + cap packed rows per destination: header (int32 counts per local expert), rows."""
+        T, k = topk_ids.shape
+        H = x.shape[1]
+        per_rank = num_experts // ranks
+        xq, xs = self.quant(x)
+        out = torch.zeros(ranks * (cap + 1), row_bytes(H), dtype=torch.uint8)
+        send_index = torch.full((T * k,), -1, dtype=torch.int32)
+        fill = [0] * ranks
+        cnt = torch.zeros(ranks, per_rank, dtype=torch.int32)
+        for i, e in enumerate(topk_ids.flatten().tolist()):
+            if not 0 <= e < num_experts:
+                continue
+            d = e // per_rank
+            slot = fill[d]
+            fill[d] += 1
+            cnt[d, e % per_rank] += 1
+            if slot >= cap:
+                continue
+            r = d * (cap + 1) + 1 + slot
+            out[r, :H] = xq[i // k].view(torch.uint8)
+            out[r, H:H + 4 * (H // 128)] = xs[i // k].contiguous().view(torch.uint8)
+            out[r, H + 4 * (H // 128):H + 4 * (H // 128) + 4] = torch.tensor([e % per_rank], dtype=torch.int32).view(
+                torch.uint8)
+            send_index[i] = r
+        for d in range(ranks):
+            out[d * (cap + 1), :4 * per_rank] = cnt[d].view(torch.uint8)
+        return out, send_index
+
+    def permute_fixed(self, rows, hidden, local_experts, ranks, cap, m_pad):
+        """Fixed-capacity receive buffer: source r's header at row r*(cap+1), its rows after it."""
+        H, nkb = hidden, hidden // 128
+        counts = torch.stack([rows[r * (cap + 1), :4 * local_experts].contiguous().view(torch.int32)
+                              for r in range(ranks)])
+        tot = counts.long().sum(0)
+        aligned = (tot + 127) // 128 * 128
+        off = torch.cumsum(aligned, 0) - aligned
+        a = torch.zeros(m_pad, H, dtype=torch.float8_e4m3fn)
+        sa = torch.ones(m_pad, nkb, dtype=torch.float32)
+        m_indices = torch.full((m_pad,), -1, dtype=torch.int32)
+        pos = torch.full((rows.shape[0],), -1, dtype=torch.int32)
+        fill = [0] * local_experts
+        for r in range(ranks):
+            for slot in range(int(counts[r].sum())):
+                i = r * (cap + 1) + 1 + slot
+                e = int(rows[i, H + 4 * nkb:H + 4 * nkb + 4].contiguous().view(torch.int32)[0])
+                p = int(off[e]) + fill[e]
+                fill[e] += 1
+                a[p] = rows[i, :H].contiguous().view(torch.float8_e4m3fn)
+                sa[p] = rows[i, H:H + 4 * nkb].contiguous().view(torch.float32)
+                m_indices[p], pos[i] = e, p
+        return a, sa, m_indices, pos
+
+    def gemm(self, a, sa, w, w_sf, m_indices, skip_ungrouped=False):
         d = torch.empty(a.shape[0], w.shape[1], dtype=torch.bfloat16)
         oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices)
         return d
@@ -74,7 +127,10 @@ class TorchRefOps:
         return per_block_cast_to_fp8(torch.nn.functional.silu(g) * u)
 
     def unpermute(self, y, perm_pos):
-        return y[perm_pos.long()]
+        out = torch.zeros(perm_pos.numel(), y.shape[1], dtype=y.dtype)
+        ok = perm_pos >= 0
+        out[ok] = y[perm_pos[ok].long()]
+        return out
 
     def combine(self, rows, send_index, topk_w):
         T, k = topk_w.shape

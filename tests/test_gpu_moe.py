@@ -97,6 +97,42 @@ def test_dispatch_and_permute_are_exact():
     assert torch.equal(back.cpu().view(torch.int16), y.cpu()[pos].view(torch.int16))
 
 
+def test_fixed_capacity_pack_and_permute_exact():
+    """Fused quant+pack into fixed-capacity regions, then the receive-side permute: bytes."""
+    C = _ext()
+    T, H, k, E, ranks = 40, 512, 2, 8, 2
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    ids = torch.rand(T, E, generator=g).topk(k, dim=1).indices.to(torch.int32)
+    ids[7, 0] = -1  # a skipped slot
+    cap = T * k
+    sent, si = C.ep_quant_pack_fixed(x.to(DEV), ids.to(DEV), E, ranks, cap)
+    ref_sent, ref_si = TorchRefOps().quant_pack_fixed(x, ids, E, ranks, cap)
+    sent, si = sent.cpu(), si.cpu()
+    nkb = H // 128
+    payload = H + 4 * nkb + 4
+    for d in range(ranks):  # headers: per-local-expert counts
+        assert torch.equal(sent[d * (cap + 1), :4 * (E // ranks)], ref_sent[d * (cap + 1), :4 * (E // ranks)])
+    assert torch.equal(si < 0, ref_si < 0)
+    for i in range(T * k):  # same row content wherever the atomics placed it
+        if si[i] >= 0:
+            assert int(si[i]) // (cap + 1) == int(ref_si[i]) // (cap + 1)
+            assert torch.equal(sent[int(si[i]), :payload], ref_sent[int(ref_si[i]), :payload])
+    # the receive side of rank 0 sees region 0 of both ranks' buffers; here one buffer stands for both
+    e_loc = E // ranks
+    recv = torch.cat([sent[:cap + 1], sent[:cap + 1]])
+    m_pad = (ranks * cap + 127 * e_loc + 127) // 128 * 128
+    a, sa, mi, pos = C.ep_permute_fixed(recv.to(DEV), H, e_loc, ranks, cap, m_pad)
+    ra, rsa, rmi, rpos = TorchRefOps().permute_fixed(recv, H, e_loc, ranks, cap, m_pad)
+    a, sa, mi, pos = a.cpu(), sa.cpu(), mi.cpu(), pos.cpu()
+    assert torch.equal(pos < 0, rpos < 0)
+    valid = (pos >= 0).nonzero().flatten()
+    assert torch.equal(a.view(torch.uint8)[pos[valid].long()], recv[valid, :H])
+    assert torch.equal(sa[pos[valid].long()], recv[valid, H:H + 4 * nkb].contiguous().view(torch.float32))
+    assert torch.equal(torch.sort(mi).values, torch.sort(rmi).values)  # same group sizes and offsets
+    assert torch.equal(mi >= 0, rmi >= 0)
+
+
 def test_layer_single_gpu_matches_cpu_reference():
     from consumer_deep_gemm.moe import MoELayer
     from metrics import errors
@@ -121,4 +157,5 @@ def test_layer_expert_parallel_two_gpus():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert "EP_OK" in r.stdout
+    for mode in ("split_sizes", "fixed_capacity", "peer_memory"):
+        assert f"EP_OK {mode}" in r.stdout, r.stdout[-3000:]

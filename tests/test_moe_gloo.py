@@ -20,7 +20,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, fixed=False):
     import sys
 
     here = os.path.dirname(os.path.abspath(__file__))
@@ -34,7 +34,7 @@ def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        _run(rank, world, q)
+        _run(rank, world, q, fixed)
     except Exception as exc:  # report instead of leaving the parent waiting
         q.put((rank, repr(exc)))
         raise
@@ -42,7 +42,7 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def _run(rank, world, q):
+def _run(rank, world, q, fixed=False):
     import torch.distributed as dist
 
     from consumer_deep_gemm.moe import MoELayer
@@ -52,21 +52,23 @@ def _run(rank, world, q):
         x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**CFG)
         e_loc = CFG["experts"] // world
         sl = slice(rank * e_loc, (rank + 1) * e_loc)
-        layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=CFG["experts"], group=dist.group.WORLD, ops=TorchRefOps())
         tpr = CFG["tokens"] // world
+        layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=CFG["experts"], group=dist.group.WORLD,
+                         ops=TorchRefOps(), max_tokens_per_rank=tpr if fixed else None)
         ts = slice(rank * tpr, (rank + 1) * tpr)
         y = layer(x[ts], ids[ts], w[ts])
         q.put((rank, y))
 
 
-def test_ep_two_ranks_matches_single_process():
+@pytest.mark.parametrize("fixed", [False, True], ids=["split_sizes", "fixed_capacity"])
+def test_ep_two_ranks_matches_single_process(fixed):
     from consumer_deep_gemm.moe import MoELayer
     from moe_ref import TorchRefOps, make_layer_inputs
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, fixed)) for r in range(2)]
     for p in procs:
         p.start()
     outs = dict(q.get(timeout=120) for _ in procs)
