@@ -12,7 +12,9 @@ stream without host synchronisation; this module only normalises the argument
 forms the reference accepts and never computes on the host.
 
 Accepted forms (as in the reference):
-  a          ``(fp8 [M,K], fp32 [M,K/128])``; ``(bf16|fp32 [M,K], any)`` (scale ignored);
+  a          ``(fp8 [M,K], fp32 [M,K/128])``; ``(fp8 [M,K], int32 [M,ceil(K/512)])`` with UE8M0 scales
+             packed four to a word (DeepGEMM's UE8M0 recipe; any strides, e.g. MN-major);
+             ``(bf16|fp32 [M,K], any)`` (scale ignored);
              a bare tensor (cast to BF16 like ``a.to(torch.bfloat16)``)
   b          ``(int8|uint8 [G,N,K/2], scale)`` or ``[N,K/2]`` for one group; scale is
              uint8/float8_e8m0fnu UE8M0 ``[G,N,K/32]``, a float ``[G,N,K/32]``, the
@@ -44,7 +46,8 @@ def _normalize(a, b, d, m_indices):
                 raise ValueError("FP8 a needs its scale")
             if sa.dim() != 2 or sa.shape[0] != x.shape[0]:
                 raise ValueError(f"a scale must be [M, K/128], got {tuple(sa.shape)}")
-            sa = sa.float() if sa.dtype != torch.float32 else sa
+            if sa.dtype != torch.int32:  # int32: UE8M0 scales packed four to a word
+                sa = sa.float() if sa.dtype != torch.float32 else sa
         elif x.dtype in (torch.bfloat16, torch.float32):
             sa = None  # the reference passes BF16/FP32 activations through unscaled (gemm.py:33-34)
         else:

@@ -100,12 +100,21 @@ int validate(const cdg_gemm_args* g) {
   if (!g->b || !g->sfb) return CDG_ERR_INVALID_ARGUMENT;
   if (g->a_dtype != CDG_DTYPE_E4M3 && g->a_dtype != CDG_DTYPE_BF16 && g->a_dtype != CDG_DTYPE_F32)
     return CDG_ERR_INVALID_ARGUMENT;
+  if (g->sa_dtype != 0 && g->sa_dtype != CDG_DTYPE_F32 && g->sa_dtype != CDG_DTYPE_UE8M0_X4)
+    return CDG_ERR_INVALID_ARGUMENT;
   if (g->a_dtype == CDG_DTYPE_E4M3) {
     if (!g->sa || g->sa_cols <= 0) return CDG_ERR_INVALID_ARGUMENT;
-    // Same rule as the reference: sa_cols > 1 gives blocks of K / sa_cols;
-    // a single column is one scale per row only when K fits one 128 block.
-    if (g->sa_cols == 1 && g->K > 128) return CDG_ERR_UNSUPPORTED;
-    if (g->sa_cols > 1 && (g->K % g->sa_cols)) return CDG_ERR_INVALID_ARGUMENT;
+    if (g->sa_dtype == CDG_DTYPE_UE8M0_X4) {
+      // one scale per 128-wide K block, four to a word
+      if (g->sa_cols != ((g->K + 127) / 128 + 3) / 4) return CDG_ERR_INVALID_ARGUMENT;
+    } else {
+      // Same rule as the reference: sa_cols > 1 gives blocks of K / sa_cols;
+      // a single column is one scale per row only when K fits one 128 block.
+      if (g->sa_cols == 1 && g->K > 128) return CDG_ERR_UNSUPPORTED;
+      if (g->sa_cols > 1 && (g->K % g->sa_cols)) return CDG_ERR_INVALID_ARGUMENT;
+    }
+  } else if (g->sa_dtype == CDG_DTYPE_UE8M0_X4) {
+    return CDG_ERR_INVALID_ARGUMENT;  // packed scales belong to e4m3 activations
   }
   if (g->sfb_dtype != CDG_DTYPE_UE8M0 && g->sfb_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
   if (g->sfb_layout != CDG_SF_ROW_MAJOR && g->sfb_layout != CDG_SF_ATOMS) return CDG_ERR_INVALID_ARGUMENT;
@@ -138,7 +147,8 @@ int validate(const cdg_gemm_args* g) {
 bool fast_path(const cdg_gemm_args* g) {
   if (g->flags & CDG_FLAG_FORCE_GENERIC) return false;
   if (g->a_dtype != CDG_DTYPE_E4M3 || g->sfb_dtype != CDG_DTYPE_UE8M0 || g->d_dtype != CDG_DTYPE_BF16) return false;
-  if (g->K % 128 || g->N % 128 || g->sa_cols != g->K / 128) return false;
+  const bool packed = g->sa_dtype == CDG_DTYPE_UE8M0_X4;
+  if (g->K % 128 || g->N % 128 || (!packed && g->sa_cols != g->K / 128)) return false;
   if (g->a_row_stride % 16 || !aligned(g->a, 16)) return false;
   if (g->b_stride_n != g->K / 2 || g->b_stride_e != g->b_stride_n * g->N || !aligned(g->b, 32)) return false;
   if (g->d_row_stride % 8 || !aligned(g->d, 16)) return false;
@@ -300,7 +310,10 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ga.sa = g->sa;
   ga.sa_stride_m = g->sa_stride_m;
   ga.sa_stride_k = g->sa_stride_k;
-  ga.sa_block_k = g->a_dtype == CDG_DTYPE_E4M3 ? (g->sa_cols > 1 ? static_cast<int>(g->K / g->sa_cols) : 128) : 128;
+  ga.sa_packed = g->sa_dtype == CDG_DTYPE_UE8M0_X4;
+  ga.sa_block_k = g->a_dtype == CDG_DTYPE_E4M3 && !ga.sa_packed
+                      ? (g->sa_cols > 1 ? static_cast<int>(g->K / g->sa_cols) : 128)
+                      : 128;
   ga.b = static_cast<const uint8_t*>(g->b);
   ga.b_stride_e = g->b_stride_e;
   ga.b_stride_n = g->b_stride_n;
@@ -350,6 +363,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.sa = g->sa;
   pa.sa_stride_m = g->sa_stride_m;
   pa.sa_stride_k = g->sa_stride_k;
+  pa.sa_packed = g->sa_dtype == CDG_DTYPE_UE8M0_X4;
   pa.ids = ids;
   pa.M = static_cast<int>(g->M);
   pa.K = static_cast<int>(g->K);

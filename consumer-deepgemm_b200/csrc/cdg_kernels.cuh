@@ -107,8 +107,9 @@ __global__ void cdg_psum_rows_kernel(const IdT* __restrict__ ends, int G, int M,
 struct PrepArgs {
   const uint8_t* a;  // e4m3 [M, K]
   int64_t a_row_stride;
-  const float* sa;  // [M, K/128]
+  const float* sa;  // [M, K/128] FP32, or int32 words of 4 UE8M0 scales (sa_packed)
   int64_t sa_stride_m, sa_stride_k;
+  int sa_packed;
   const void* ids;  // per-row group ids (int32 or int64)
   int M, K, E;
   int nblk;
@@ -120,6 +121,18 @@ struct PrepArgs {
   int* ctrl;               // control words (zeroed by the host before launch)
   int4* lists;             // [kNumClasses][nblk] {block, expert, rows spanned, 0}
 };
+
+// 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
+__device__ __forceinline__ float ue8m0_to_f32(uint32_t e) {
+  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
+// Activation scale of row r, 128-wide K block kb: FP32, or UE8M0 packed four to a word.
+__device__ __forceinline__ float load_sa(const float* sa, int packed, int64_t sm, int64_t sk, int64_t r, int64_t kb) {
+  if (!packed) return sa[r * sm + kb * sk];
+  const uint32_t w = reinterpret_cast<const uint32_t*>(sa)[r * sm + (kb >> 2) * sk];
+  return ue8m0_to_f32((w >> (8 * (kb & 3))) & 0xFFu);
+}
 
 // Group id of row r; a null id vector means every row belongs to group 0.
 __device__ __forceinline__ int64_t load_id(const void* ids, int is64, int r) {
@@ -211,7 +224,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       if (s_id[tid] == expert) {
         float smax = 0.0f;
         for (int kb = 0; kb < kb_count; ++kb) {
-          const float sbf = __bfloat162float(__float2bfloat16_rn(p.sa[r * p.sa_stride_m + kb * p.sa_stride_k]));
+          const float sbf =
+              __bfloat162float(__float2bfloat16_rn(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, kb)));
           if (isfinite(sbf)) smax = fmaxf(smax, fabsf(sbf));
         }
         if (smax > 0.0f) frexpf(smax, &emax);
@@ -224,7 +238,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       const int kl = it - rr * kbn;
       const int r = row0 + rr;
       s_scale[rr][kl] = s_id[rr] == expert
-          ? __bfloat162float(__float2bfloat16_rn(p.sa[r * p.sa_stride_m + (kb0 + kl) * p.sa_stride_k]))
+          ? __bfloat162float(
+                __float2bfloat16_rn(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, kb0 + kl)))
           : 0.0f;
     }
     __syncthreads();
@@ -590,7 +605,8 @@ struct GenericArgs {
   int64_t a_row_stride;
   const float* sa;
   int64_t sa_stride_m, sa_stride_k;
-  int sa_block_k;
+  int sa_block_k;   // K columns per scale (FP32 scales); 128 for packed UE8M0
+  int sa_packed;    // 1: sa holds int32 words of 4 UE8M0 scales
   const uint8_t* b;  // packed [E][N][K/2]
   int64_t b_stride_e, b_stride_n;
   const void* sb;
@@ -614,11 +630,6 @@ __constant__ float kE2M1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
-__device__ __forceinline__ float ue8m0_to_f32(uint32_t e) {
-  return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
-}
-
 __global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
   extern __shared__ float s_row[];  // K floats: the dequantised activation row
   grid_dependency_wait();  // the block list comes from the previous kernel of the stream
@@ -639,7 +650,7 @@ __global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
           float x;
           if (p.a_dtype == CDG_DTYPE_E4M3) {
             const uint8_t raw = static_cast<const uint8_t*>(p.a)[r * p.a_row_stride + k];
-            const float s = bf16r(p.sa[r * p.sa_stride_m + (k / p.sa_block_k) * p.sa_stride_k]);
+            const float s = bf16r(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, k / p.sa_block_k));
             x = bf16r(e4m3_to_f32(raw) * s);
           } else if (p.a_dtype == CDG_DTYPE_BF16) {
             x = __bfloat162float(static_cast<const __nv_bfloat16*>(p.a)[r * p.a_row_stride + k]);

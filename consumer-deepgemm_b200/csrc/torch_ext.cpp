@@ -77,9 +77,11 @@ cdg_gemm_args make_args(const torch::Tensor& a, const c10::optional<torch::Tenso
     TORCH_CHECK_VALUE(sa.has_value(), "FP8 a needs its scale");
     const auto& s = *sa;
     check_cuda(s, "a scale", dev);
-    TORCH_CHECK_VALUE(s.scalar_type() == torch::kFloat32 && s.dim() == 2 && s.size(0) == M,
-                      "a scale must be float32 [M, K/128]");
-    g.sa = s.data_ptr<float>();
+    TORCH_CHECK_VALUE((s.scalar_type() == torch::kFloat32 || s.scalar_type() == torch::kInt32) && s.dim() == 2 &&
+                          s.size(0) == M,
+                      "a scale must be float32 [M, K/128] or int32 [M, ceil(K/512)] (packed UE8M0)");
+    g.sa = static_cast<const float*>(s.data_ptr());
+    g.sa_dtype = s.scalar_type() == torch::kInt32 ? CDG_DTYPE_UE8M0_X4 : CDG_DTYPE_F32;
     g.sa_stride_m = s.stride(0);
     g.sa_stride_k = s.stride(1);
     g.sa_cols = static_cast<int32_t>(s.size(1));

@@ -52,7 +52,10 @@ typedef enum cdg_dtype {
   CDG_DTYPE_F32 = 3,    /* float32 */
   CDG_DTYPE_UE8M0 = 4,  /* unsigned 8-bit power-of-two scale, value 2^(b-127) */
   CDG_DTYPE_I32 = 5,    /* int32 group ids */
-  CDG_DTYPE_I64 = 6     /* int64 group ids */
+  CDG_DTYPE_I64 = 6,    /* int64 group ids */
+  CDG_DTYPE_UE8M0_X4 = 7 /* int32 words of four UE8M0 activation scales: the scale of 128-wide K
+                            block kb is byte kb % 4 of word kb / 4 (the packed format of DeepGEMM's
+                            UE8M0 recipe, e.g. vLLM's silu_mul_quant_fp8_packed) */
 } cdg_dtype;
 
 /* How the weight scales `sfb` are laid out. */
@@ -106,6 +109,8 @@ typedef struct cdg_gemm_args {
   int64_t d_row_stride;
   int64_t M, N, K, E;
   int32_t flags; /* CDG_FLAG_* */
+  int32_t sa_dtype; /* scales of an e4m3 `a`: CDG_DTYPE_F32 (0 reads as F32) or CDG_DTYPE_UE8M0_X4, whose
+                       sa_cols counts int32 words and whose strides are in words */
 } cdg_gemm_args;
 
 #define CDG_FLAG_FORCE_GENERIC 1 /* run the exact SIMT path even where the tensor-core path applies */

@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(REPO, "consumer-deepgemm_b200", "consumer_deep_gemm", "l
 HEADER = os.path.join(REPO, "include", "cdg_b200.h")
 
 CDG_OK = 0
-DT = {"e4m3": 1, "bf16": 2, "f32": 3, "ue8m0": 4, "i32": 5, "i64": 6}
+DT = {"e4m3": 1, "bf16": 2, "f32": 3, "ue8m0": 4, "i32": 5, "i64": 6, "ue8m0_x4": 7}
 SF_ROW_MAJOR, SF_ATOMS = 0, 1
 INDEX_PER_ROW, INDEX_PSUM, INDEX_NONE, INDEX_MASKED = 0, 1, 2, 3
 FLAG_FORCE_GENERIC = 1
@@ -36,7 +36,7 @@ class GemmArgs(ctypes.Structure):
         ("m_indices_len", ctypes.c_int64),
         ("d", ctypes.c_void_p), ("d_dtype", ctypes.c_int32), ("d_row_stride", ctypes.c_int64),
         ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64), ("E", ctypes.c_int64),
-        ("flags", ctypes.c_int32),
+        ("flags", ctypes.c_int32), ("sa_dtype", ctypes.c_int32),
     ]
 
 
@@ -82,6 +82,7 @@ def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, masked=False)
     g.a, g.a_dtype, g.a_row_stride = a.data_ptr(), _code(a), a.stride(0)
     if sa is not None:
         g.sa, g.sa_stride_m, g.sa_stride_k, g.sa_cols = sa.data_ptr(), sa.stride(0), sa.stride(1), sa.shape[1]
+        g.sa_dtype = DT["ue8m0_x4"] if sa.dtype == torch.int32 else DT["f32"]
     g.b, g.b_stride_e, g.b_stride_n = b.data_ptr(), b.stride(0), b.stride(1)
     g.sfb = sb.data_ptr()
     if sb_atoms:

@@ -51,12 +51,16 @@ def load_gemm_case(name: str) -> dict:
         "masked": bool(z["masked"]) if "masked" in z.files else False,
     }
     case["sa"] = torch.from_numpy(z["sa"]) if "sa" in z.files else None
+    case["sa_packed"] = torch.from_numpy(z["sa_packed"]) if "sa_packed" in z.files else None
     return case
 
 
 GEMM_CASES = sorted(
     os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz"))
     if os.path.basename(p).startswith(("kat_", "edge_", "c0")))
+
+PACKED_SCALE_CASES = sorted(
+    os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "ue8m0x4_*.npz")))
 
 MASKED_CASES = sorted(
     os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "masked_*.npz")))

@@ -15,6 +15,10 @@ seeded inputs:
 * ``_float_scale_to_e8m0``                 (gemm.py:62-73)
 * ``m_grouped_fp8_fp4_gemm_nt_masked``     (gemm.py:529-551)
 
+``ue8m0x4_*`` cases hold activation scales that are powers of two, stored both as the
+FP32 values the reference consumes and packed four UE8M0 bytes to an int32 word (the
+format DeepGEMM's UE8M0 recipe passes; the reference itself only reads FP32 scales).
+
 Cases cover the reference's own known answers (tests/test_fp4_fallback.py:15-73,
 tests/test_native_abi.py:144-196, tests/test_scale_reorder.py:53-68,
 tests/test_reorder_compare.py:8-35), benchmark config 0, and edge cases (empty
@@ -176,6 +180,28 @@ def main():
     rand_case("masked_decode_classes", 2048, 512, 256, 8, add_ids([1, 16, 17, 32, 33, 128, 129, 256]), fn="masked",
               seed=16)
     rand_case("masked_single_b", 192, 256, 128, 1, add_ids([7]), fn="masked", single_b=True, seed=17)
+
+    # --- power-of-two activation scales, also packed 4 UE8M0 bytes per int32 word ----------
+    def packed_case(name, m, k, n, e, ids, seed):
+        g = torch.Generator().manual_seed(seed)
+        kb = (k + 127) // 128
+        aq = (torch.randn(m, k, generator=g) * 64).to(torch.float8_e4m3fn)
+        sbytes = torch.randint(112, 136, (m, kb), generator=g, dtype=torch.int32)
+        sa_f32 = torch.pow(2.0, sbytes.float() - 127.0)
+        w = torch.randn(e, n, k, generator=g) * 0.02
+        bq, sbq = per_block_cast_to_fp4(w)
+        words = (kb + 3) // 4
+        padded = torch.full((m, words * 4), 127, dtype=torch.int32)
+        padded[:, :kb] = sbytes
+        packed = (padded[:, 0::4] | (padded[:, 1::4] << 8) | (padded[:, 2::4] << 16) | (padded[:, 3::4] << 24))
+        name, case = gemm_case(gemm, name, aq, sa_f32, bq, sbq, ids)
+        case["sa_packed"] = packed.to(torch.int32).numpy()
+        cases[name] = case
+
+    packed_case("ue8m0x4_ragged", 512, 512, 256, 4,
+                add_ids([0] * 100 + [-1] * 28 + [2] * 128 + [1] * 3 + [-1] * 125 + [3] * 128), seed=21)
+    packed_case("ue8m0x4_k1024", 256, 1024, 256, 2, add_ids([1] * 200 + [-1] * 56), seed=22)
+    packed_case("ue8m0x4_k640_n128", 256, 640, 128, 2, add_ids([0] * 128 + [1] * 64 + [-1] * 64), seed=23)
 
     # --- byte-level helpers -----------------------------------------------------------------
     sf = torch.arange(128 * 8, dtype=torch.uint8).reshape(128, 8)

@@ -19,7 +19,7 @@ import pytest
 import torch
 
 import cabi
-from conftest import GEMM_CASES, MASKED_CASES, load_gemm_case
+from conftest import GEMM_CASES, MASKED_CASES, PACKED_SCALE_CASES, load_gemm_case
 from metrics import TOL_NORMWISE, TOL_ROW_L2, errors
 from oracle import cdg_oracle as oracle
 
@@ -111,6 +111,46 @@ def test_masked_golden_case(name, flags):
         assert bool((out[~rows].float() == 0).all())
     nw, rl2 = errors(out, ref, rows)
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+
+
+@pytest.mark.parametrize("mn_major", [False, True], ids=["row_major", "mn_major"])
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_SINGLE_CTA, cabi.FLAG_FORCE_GENERIC],
+                         ids=["dispatch", "single_cta", "simt"])
+@pytest.mark.parametrize("name", PACKED_SCALE_CASES)
+def test_packed_ue8m0_activation_scales(name, flags, mn_major):
+    """int32 words of 4 UE8M0 scales (row-major, or MN-major as DeepGEMM lays them out)."""
+    c = load_gemm_case(name)
+    a = c["a"].to(DEV)
+    words = c["sa_packed"].to(DEV)
+    if mn_major:  # [words, M_aligned] storage viewed as [M, words]
+        m = words.shape[0]
+        store = torch.zeros(words.shape[1], (m + 3) // 4 * 4, dtype=torch.int32, device=DEV)
+        store[:, :m] = words.t()
+        words = store.t()[:m]
+    b, sb = c["b"].to(DEV), c["sb"].to(DEV)
+    ids = c["m_indices"].to(DEV)
+    d = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    cabi.gemm(a, words, b, sb, d, ids, flags=flags)
+    torch.cuda.synchronize()
+    out = d.cpu()
+    bad = _invalid_rows(c)
+    assert not torch.isnan(out).any()
+    assert bool((out[bad].float() == 0).all())
+    nw, rl2 = errors(out, c["d"], ~bad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+
+
+def test_packed_scales_public_api():
+    import consumer_deep_gemm as cdg
+
+    c = load_gemm_case("ue8m0x4_ragged")
+    d = torch.empty(c["d"].shape, dtype=torch.bfloat16, device=DEV)
+    cdg.m_grouped_fp8_fp4_gemm_nt_contiguous((c["a"].to(DEV), c["sa_packed"].to(DEV)), (c["b"].to(DEV), c["sb"].to(DEV)),
+                                             d, c["m_indices"].to(DEV), recipe_a=(1, 128), recipe_b=(1, 32))
+    torch.cuda.synchronize()
+    bad = _invalid_rows(c)
+    nw, rl2 = errors(d.cpu(), c["d"], ~bad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (nw, rl2)
 
 
 def test_masked_public_api_3d_views():

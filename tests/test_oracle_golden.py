@@ -7,7 +7,7 @@ import torch
 
 import pytest
 
-from conftest import GOLDEN, MASKED_CASES, load_gemm_case
+from conftest import GOLDEN, MASKED_CASES, PACKED_SCALE_CASES, load_gemm_case
 from oracle import cdg_oracle as oracle
 
 
@@ -27,6 +27,19 @@ def test_oracle_masked_matches_reference(name):
     d = torch.full_like(c["d"], 7.0)
     a = (c["a"], c["sa"]) if c["sa"] is not None else c["a"]
     oracle.m_grouped_fp8_fp4_gemm_nt_masked(a, (c["b"], c["sb"]), d, c["m_indices"])
+    assert torch.equal(d.view(torch.int16), c["d"].view(torch.int16)), name
+
+
+@pytest.mark.parametrize("name", PACKED_SCALE_CASES)
+def test_packed_scale_fixtures(name):
+    """Packed words unpack to the FP32 powers of two the reference consumed; the oracle reproduces D."""
+    c = load_gemm_case(name)
+    words = c["sa_packed"].to(torch.int64) & 0xFFFFFFFF
+    kb = c["sa"].shape[1]
+    e = torch.stack([(words >> (8 * i)) & 0xFF for i in range(4)], dim=2).reshape(words.shape[0], -1)[:, :kb]
+    assert torch.equal(torch.pow(2.0, e.float() - 127.0), c["sa"])
+    d = torch.full_like(c["d"], 7.0)
+    oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((c["a"], c["sa"]), (c["b"], c["sb"]), d, c["m_indices"])
     assert torch.equal(d.view(torch.int16), c["d"].view(torch.int16)), name
 
 
