@@ -15,6 +15,7 @@ from .layout import (
     set_mk_alignment_for_contiguous_layout,
     transform_sf_into_required_layout,
 )
+from .mega import fp8_fp4_mega_moe, get_symm_buffer_for_mega_moe, transform_weights_for_mega_moe
 from .native import build_info as native_build_info
 from .native import is_available as native_is_available
 from .utils import get_num_sms, get_pdl, get_tc_util, set_num_sms, set_pdl, set_tc_util
@@ -25,6 +26,9 @@ __all__ = [
     "m_grouped_fp8_fp4_gemm_nt_contiguous",
     "m_grouped_fp8_fp4_gemm_nt_masked",
     "transform_sf_into_required_layout",
+    "transform_weights_for_mega_moe",
+    "get_symm_buffer_for_mega_moe",
+    "fp8_fp4_mega_moe",
     "get_mn_major_tma_aligned_tensor",
     "get_mk_alignment_for_contiguous_layout",
     "set_mk_alignment_for_contiguous_layout",

@@ -426,6 +426,40 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, const int32_t* send
   }
 }
 
+// Weight-row gathers of transform_weights_for_mega_moe: destination row n of a group
+// takes source row src_row(n).  kind bit 0: gate/up interleave in granules of 8 rows
+// (rows [q*16, q*16+8) from the gate half, [q*16+8, q*16+16) from the up half);
+// bit 1: within every 128 rows, the [4 x 32] -> [32 x 4] transpose of scale rows that
+// tcgen05.cp's 32x128b.warpx4 pattern expects (applied after the interleave).
+__host__ __device__ __forceinline__ int64_t mega_src_row(int64_t n, int64_t N, int kind) {
+  if (kind & 2) {
+    const int64_t blk = n / 128, r = n - blk * 128;
+    n = blk * 128 + (r % 4) * 32 + r / 4;
+  }
+  if (kind & 1) {
+    const int64_t half = N / 2, q = n / 16, rem = n - q * 16;
+    n = (rem / 8) * half + q * 8 + rem % 8;
+  }
+  return n;
+}
+
+// One warp per (group, destination row); 16-byte copies when rows allow them.
+__global__ void mega_rows_kernel(const uint8_t* src, uint8_t* dst, int64_t G, int64_t N, int64_t row_bytes,
+                                 int64_t stride_g, int64_t stride_n, int kind) {
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= G * N) return;
+  const int64_t g = w / N, n = w - g * N;
+  const uint8_t* from = src + g * stride_g + mega_src_row(n, N, kind) * stride_n;
+  uint8_t* to = dst + (g * N + n) * row_bytes;
+  if (row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(from) % 16 == 0 && reinterpret_cast<uintptr_t>(to) % 16 == 0) {
+    for (int64_t c = lane; c < row_bytes / 16; c += 32)
+      reinterpret_cast<uint4*>(to)[c] = reinterpret_cast<const uint4*>(from)[c];
+  } else {
+    for (int64_t c = lane; c < row_bytes; c += 32) to[c] = from[c];
+  }
+}
+
 unsigned warp_grid(int64_t warps) { return static_cast<unsigned>((warps * 32 + 255) / 256); }
 
 // Exchange window of one rank: [0, 512) dispatch flags int32[ranks], [512, 1024) return
@@ -694,6 +728,20 @@ int cdg_ep_combine_p2p(const void* window, const int32_t* send_index, const floa
       reinterpret_cast<const __nv_bfloat16*>(base + win.ret_parity(epoch & 1)), send_index, topk_w, T, topk, H,
       static_cast<__nv_bfloat16*>(y), reinterpret_cast<const int32_t*>(base + cdg::Window::kReturnFlags),
       static_cast<int>(ranks), epoch, reinterpret_cast<int32_t*>(const_cast<uint8_t*>(base) + cdg::Window::kStatus));
+  return cdg::launched();
+}
+
+// ---------------------------------------------------------------- MegaMoE weight layout
+int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t stride_n, void* dst, int64_t G, int64_t N,
+                                int64_t row_bytes, int32_t kind, cdg_stream_t stream) {
+  if (!src || !dst || G < 0 || N <= 0 || row_bytes <= 0 || kind < 0 || kind > 3 || stride_n < row_bytes ||
+      stride_g < stride_n * N)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if ((kind & 1) && (N % 16)) return CDG_ERR_INVALID_ARGUMENT;   // gate and up halves of whole granules
+  if ((kind & 2) && (N % 128)) return CDG_ERR_INVALID_ARGUMENT;  // whole 128-row blocks
+  if (G == 0) return CDG_OK;
+  cdg::mega_rows_kernel<<<cdg::warp_grid(G * N), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), G, N, row_bytes, stride_g, stride_n, kind);
   return cdg::launched();
 }
 

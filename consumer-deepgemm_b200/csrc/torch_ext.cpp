@@ -306,6 +306,18 @@ std::vector<torch::Tensor> ep_permute_fixed(const torch::Tensor& rows, int64_t H
   return {A, SA, mi, pos};
 }
 
+// [G, N, ...] row gather of transform_weights_for_mega_moe; returns a new contiguous tensor.
+torch::Tensor mega_moe_transform_rows(const torch::Tensor& t, int64_t kind) {
+  TORCH_CHECK(t.is_cuda() && t.dim() == 3 && t.stride(2) == 1, "expects a CUDA [G, N, X] tensor with unit last stride");
+  const c10::cuda::CUDAGuard guard(t.device());
+  auto out = torch::empty(t.sizes(), t.options());
+  const int64_t es = t.element_size();
+  check_status(cdg_mega_moe_transform_rows(t.data_ptr(), t.stride(0) * es, t.stride(1) * es, out.data_ptr(), t.size(0),
+                                           t.size(1), t.size(2) * es, static_cast<int32_t>(kind), cur_stream(t)),
+               "transform_weights_for_mega_moe");
+  return out;
+}
+
 // ------------------------------------------------------------------ peer-memory exchange
 py::tuple ep_window_create(int64_t bytes) {
   void* w = nullptr;
@@ -439,6 +451,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ranks"), py::arg("cap"));
   m.def("ep_permute_fixed", &ep_permute_fixed, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("ranks"), py::arg("cap"), py::arg("m_pad"));
+  m.def("mega_moe_transform_rows", &mega_moe_transform_rows, py::arg("t"), py::arg("kind"));
   m.def("ep_window_bytes", [](int64_t ranks, int64_t cap, int64_t H) { return cdg_ep_window_bytes(ranks, cap, H); },
         py::arg("ranks"), py::arg("cap"), py::arg("hidden"));
   m.def("ep_window_create", &ep_window_create, py::arg("bytes"));

@@ -279,6 +279,15 @@ int cdg_ep_permute_fixed(const uint8_t* recv_rows, int64_t ranks, int64_t cap, i
                          int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                          cdg_stream_t stream);
 
+/* Row gathers of transform_weights_for_mega_moe (consumer_deep_gemm/mega.py:14-50):
+ * dst[g, n, :] = src[g, f(n), :] for G groups of N rows of row_bytes bytes (source strides in
+ * bytes, destination dense).  kind 1: interleave the gate half and the up half of the rows in
+ * granules of 8 (N % 16 == 0); kind 2: transpose each 128-row block as [4 x 32] -> [32 x 4]
+ * (N % 128 == 0); kind 3: both (the L1 scale transform).  The caller keeps tensors whose N is
+ * not a multiple of 128 unchanged for kind 2, as the reference does. */
+int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t stride_n, void* dst, int64_t G, int64_t N,
+                                int64_t row_bytes, int32_t kind, cdg_stream_t stream);
+
 /* Peer-memory exchange (expert parallelism over NVLink without a collective library).
  * Every rank owns an exchange window (cdg_ep_window_bytes) shared with the other ranks
  * through CUDA IPC: create it with cdg_ep_window_create, send the 64-byte handle to the

@@ -213,6 +213,30 @@ def m_grouped_fp8_fp4_gemm_nt_masked(a, b, d: torch.Tensor, masked_m=None) -> No
         d[start:start + counts[g]].copy_(res.to(d.dtype))
 
 
+def transform_weights_for_mega_moe(l1, l2):
+    """MegaMoE weight layout (mega.py:14-50) as numpy row permutations.
+
+    L1 rows: the gate half and the up half interleaved in granules of 8 rows
+    (mega.py:17-27); scales additionally, per 128-row block, [4 x 32] -> [32 x 4]
+    (mega.py:30-39), skipped when the row count is not a multiple of 128.
+    """
+    def interleave(t):
+        g, n = t.shape[:2]
+        half = n // 2
+        gate = t[:, :half].reshape(g, half // 8, 8, *t.shape[2:])
+        up = t[:, half:].reshape(g, half // 8, 8, *t.shape[2:])
+        return np.stack([gate, up], axis=2).reshape(t.shape)
+
+    def utccp(t):
+        g, n = t.shape[:2]
+        if n % 128:
+            return t.copy()
+        return np.swapaxes(t.reshape(g, n // 128, 4, 32, *t.shape[2:]), 2, 3).reshape(t.shape)
+
+    (w1, s1), (w2, s2) = l1, l2
+    return (interleave(w1), utccp(interleave(s1))), (w2.copy(), utccp(s2))
+
+
 def reference_fp64(a, b, m_indices) -> np.ndarray:
     """Exact product of the quantised operands in FP64 (no BF16 rounding of ``a``).
 

@@ -14,6 +14,7 @@ seeded inputs:
 * ``_dequant_fp4_block``                   (gemm.py:147-187)
 * ``_float_scale_to_e8m0``                 (gemm.py:62-73)
 * ``m_grouped_fp8_fp4_gemm_nt_masked``     (gemm.py:529-551)
+* ``transform_weights_for_mega_moe``       (mega.py:42-50)
 
 ``ue8m0x4_*`` cases hold activation scales that are powers of two, stored both as the
 FP32 values the reference consumes and packed four UE8M0 bytes to an int32 word (the
@@ -211,6 +212,18 @@ def main():
     allb = torch.arange(256, dtype=torch.uint8).repeat(4, 16).reshape(4, 16, 256)
     scl = torch.randint(100, 150, (4, 16, 16), dtype=torch.uint8, generator=torch.Generator().manual_seed(6))
     cases["fp4_dequant_all_bytes"] = {"src": raw(allb), "scale": raw(scl), "dst": raw(gemm._dequant_fp4_block(allb, scl))}
+    # MegaMoE weight layout (mega.py:42-50): L1 N=256 (gate|up), L2 N=128, plus an L2 whose
+    # row count is not a multiple of 128 (scales returned unchanged)
+    import ref_cdg.mega as ref_mega
+    gm = torch.Generator().manual_seed(31)
+    mk = lambda *shape: torch.randint(0, 256, shape, dtype=torch.uint8, generator=gm)  # noqa: E731
+    w1, s1, w2, s2 = mk(2, 256, 64), mk(2, 256, 8), mk(2, 128, 32), mk(2, 128, 4)
+    (ow1, os1), (ow2, os2) = ref_mega.transform_weights_for_mega_moe((w1, s1), (w2, s2))
+    w2b, s2b = mk(3, 96, 16), mk(3, 96, 2)
+    (_, _), (ow2b, os2b) = ref_mega.transform_weights_for_mega_moe((w1, s1), (w2b, s2b))
+    cases["mega_moe_transform"] = {
+        "w1": raw(w1), "s1": raw(s1), "w2": raw(w2), "s2": raw(s2), "w2b": raw(w2b), "s2b": raw(s2b),
+        "ow1": raw(ow1), "os1": raw(os1), "ow2": raw(ow2), "os2": raw(os2), "ow2b": raw(ow2b), "os2b": raw(os2b)}
     fs = torch.tensor([1.0, 2.0, 0.75, 3.0, 1e-30, 1e30, 0.0, 5.9e-39, 1.5, 2.9999])
     cases["float_scale_to_e8m0"] = {"src": raw(fs), "dst": raw(gemm._float_scale_to_e8m0(fs))}
 

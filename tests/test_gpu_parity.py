@@ -259,3 +259,25 @@ def test_benchmark_config_sampled_rows(cfg):
     assert bool((d1[pad] == 0).all()) and not bool(torch.isnan(d1).any())
     nw1, rl21 = errors(d1[rows.to(DEV)], ref)
     assert nw1 <= TOL_NORMWISE and rl21 <= TOL_ROW_L2, (cfg, "single CTA", nw1, rl21)
+
+
+def test_mega_moe_transform_bytes_match_reference():
+    import numpy as np
+
+    import consumer_deep_gemm as cdg
+    from conftest import GOLDEN
+
+    z = np.load(f"{GOLDEN}/mega_moe_transform.npz")
+    t = lambda k: torch.from_numpy(z[k]).to(DEV)  # noqa: E731
+    (w1, s1), (w2, s2) = cdg.transform_weights_for_mega_moe((t("w1"), t("s1")), (t("w2"), t("s2")))
+    for got, key in ((w1, "ow1"), (s1, "os1"), (w2, "ow2"), (s2, "os2")):
+        assert np.array_equal(got.cpu().numpy(), z[key]), key
+    _, (w2b, s2b) = cdg.transform_weights_for_mega_moe((t("w1"), t("s1")), (t("w2b"), t("s2b")))
+    assert np.array_equal(w2b.cpu().numpy(), z["ow2b"]) and np.array_equal(s2b.cpu().numpy(), z["os2b"])
+    # strided views (a weight slice of a larger tensor) take the same path
+    big = torch.zeros(2, 256, 80, dtype=torch.uint8, device=DEV)
+    big[:, :, :64] = t("w1")
+    (w1v, _), _ = cdg.transform_weights_for_mega_moe((big[:, :, :64], t("s1")), (t("w2"), t("s2")))
+    assert np.array_equal(w1v.cpu().numpy(), z["ow1"])
+    with pytest.raises(NotImplementedError):
+        cdg.fp8_fp4_mega_moe(None, None, None, None)

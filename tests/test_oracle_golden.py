@@ -43,6 +43,15 @@ def test_packed_scale_fixtures(name):
     assert torch.equal(d.view(torch.int16), c["d"].view(torch.int16)), name
 
 
+def test_oracle_mega_moe_transform():
+    z = _z("mega_moe_transform")
+    (w1, s1), (w2, s2) = oracle.transform_weights_for_mega_moe((z["w1"], z["s1"]), (z["w2"], z["s2"]))
+    for got, key in ((w1, "ow1"), (s1, "os1"), (w2, "ow2"), (s2, "os2")):
+        assert np.array_equal(got, z[key]), key
+    _, (w2b, s2b) = oracle.transform_weights_for_mega_moe((z["w1"], z["s1"]), (z["w2b"], z["s2b"]))
+    assert np.array_equal(w2b, z["ow2b"]) and np.array_equal(s2b, z["os2b"])
+
+
 def _z(name):
     return np.load(os.path.join(GOLDEN, f"{name}.npz"))
 
