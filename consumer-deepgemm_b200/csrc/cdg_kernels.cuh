@@ -535,14 +535,19 @@ __global__ void __launch_bounds__(256, 1)
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         ++local;
+        // 2^E of the tile's rows, loaded before the accumulator wait: lane l holds rows l + 32k
+        float row_sc[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          row_sc[k] = __uint_as_float(
+              static_cast<uint32_t>(min(max(__ldg(p.row_exp + blk * 128 + k * 32 + lane) + 127, 1), 254)) << 23);
         if (!mbar_wait(&tfull[acc], acc_phase, p.status)) { ok = false; break; }
         tc_fence_after();
         const int n = nt * 128 + q * 32 + lane;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kAccCols;
         for (int j0 = 0; j0 < ntok; j0 += 16) {
-          // 2^E of the chunk's 16 rows: lane j (mod 16) loads row j's exponent, shuffles share it
-          const int re = blk * 128 + j0 + (lane & 15);
-          const float my_scale = __uint_as_float(static_cast<uint32_t>(min(max(__ldg(p.row_exp + re) + 127, 1), 254)) << 23);
+          const int kq = j0 >> 5;  // which of the 32-row groups this chunk lies in
+          const float my_scale = kq == 0 ? row_sc[0] : kq == 1 ? row_sc[1] : kq == 2 ? row_sc[2] : row_sc[3];
           uint32_t v[16];
           tmem_ld16(taddr + j0, v);
           if (kStacked) {
@@ -559,7 +564,7 @@ __global__ void __launch_bounds__(256, 1)
             const int r = row0 + j0 + j;
             const int rb = j0 + j;
             const uint32_t word = rb < 32 ? mask.x : rb < 64 ? mask.y : rb < 96 ? mask.z : mask.w;
-            const float sc = __shfl_sync(0xffffffffu, my_scale, j);
+            const float sc = __shfl_sync(0xffffffffu, my_scale, (j0 & 31) + j);
             if (rb < nrows) {
               const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
               p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);

@@ -53,7 +53,12 @@ struct PairSmem {
   static constexpr int kStageBytes = kW + kPlanes * kA;  // operand tiles (1024-byte multiple)
   static constexpr int kSfRing = kStages * kStageBytes;  // then one 512-byte scale atom per stage
   static constexpr int kOneAtom = kSfRing + kStages * 512;  // constant activation scale atom
-  static constexpr int kBarOffset = kOneAtom + 512;
+  // narrow and wide tiles: per epilogue warp a [16 rows x 32 columns] BF16 staging tile, so
+  // that D leaves as 16-byte row segments instead of 2-byte column elements
+  static constexpr bool kStagedStores = TOK > 16;
+  static constexpr int kStaging = kOneAtom + 512;
+  static constexpr int kStagingBytes = kStagedStores ? 4 * 16 * 32 * 2 : 0;
+  static constexpr int kBarOffset = kStaging + kStagingBytes;
   static constexpr int kBarBytes = (2 * kStages + 4 + NI) * 8 + 16;  // barriers + TMEM address
   static constexpr int kBytes = kBarOffset + kBarBytes + 1024;          // + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
@@ -262,6 +267,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
         ++local;
         const int first = seq % NI;  // issuer of the tile's first K step
         seq += k_steps;
+        // 2^E of the tile's rows, loaded before the accumulator wait: lane l holds rows l + 32k
+        float row_sc[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          row_sc[k] = __uint_as_float(
+              static_cast<uint32_t>(min(max(__ldg(p.row_exp + blk * 128 + k * 32 + lane) + 127, 1), 254)) << 23);
         if (!mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
                                wait_code(4, static_cast<int>(rank), acc, acc_phase, local - 1))) {
           ok = false;
@@ -271,9 +282,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
         const int n = nt * 128 + q * 32 + lane;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * L::kAccCols;
         for (int j0 = 0; j0 < ntok; j0 += 16) {
-          const int re = blk * 128 + j0 + (lane & 15);
-          const float my_scale =
-              __uint_as_float(static_cast<uint32_t>(min(max(__ldg(p.row_exp + re) + 127, 1), 254)) << 23);
+          const int kq = j0 >> 5;  // which of the 32-row groups this chunk lies in
+          const float my_scale = kq == 0 ? row_sc[0] : kq == 1 ? row_sc[1] : kq == 2 ? row_sc[2] : row_sc[3];
           uint32_t v[16];
           tmem_ld16(taddr + first * L::kPartCols + j0, v);
           if (!kWide) {
@@ -295,15 +305,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
           } else {
             tmem_ld_wait();
           }
+          if (L::kStagedStores) {
+            // this warp's 32 columns x 16 rows through shared memory: each lane then stores two
+            // 16-byte row segments (rows past the block's end are skipped)
+            __nv_bfloat16* wst = reinterpret_cast<__nv_bfloat16*>(smem + L::kStaging) + q * 16 * 32;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int r = row0 + j0 + j;
-            const int rb = j0 + j;
-            const uint32_t word = rb < 32 ? mask.x : rb < 64 ? mask.y : rb < 96 ? mask.z : mask.w;
-            const float sc = __shfl_sync(0xffffffffu, my_scale, j);
-            if (rb < nrows) {
+            for (int j = 0; j < 16; ++j) {
+              const int rb = j0 + j;
+              const uint32_t word = rb < 32 ? mask.x : rb < 64 ? mask.y : rb < 96 ? mask.z : mask.w;
+              const float sc = __shfl_sync(0xffffffffu, my_scale, (j0 & 31) + j);
               const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
-              p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
+              wst[j * 32 + lane] = __float2bfloat16_rn(x);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const int vi = lane + 32 * i, rr = vi >> 2, part = vi & 3;
+              if (j0 + rr < nrows)
+                *reinterpret_cast<uint4*>(p.d + (row0 + j0 + rr) * p.d_row_stride + nt * 128 + q * 32 + part * 8) =
+                    *reinterpret_cast<const uint4*>(wst + rr * 32 + part * 8);
+            }
+            __syncwarp();
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int r = row0 + j0 + j;
+              const int rb = j0 + j;
+              const uint32_t word = rb < 32 ? mask.x : rb < 64 ? mask.y : rb < 96 ? mask.z : mask.w;
+              const float sc = __shfl_sync(0xffffffffu, my_scale, (j0 & 31) + j);
+              if (rb < nrows) {
+                const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
+                p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
+              }
             }
           }
         }
