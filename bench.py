@@ -407,22 +407,42 @@ def bench_ep_decode(args, dev, world, rank, dist):
     sampler = ClockSampler(dev.index)
     for _ in range(args.warmup):
         step()
+    # the GEMM kernels' device time, from eager steps with per-step events
     timer = Timed(dev, args.steps)
     dist.barrier()
     torch.cuda.synchronize(dev)
-    ms, kernel_ms = timer.run(step, args.steps)
+    _, kernel_ms = timer.run(step, args.steps)
+    dist.barrier()
+    # the step itself: one CUDA graph per rank (peer exchange: no host value per step)
+    use_graph = layer.exchange == "p2p"
+    if use_graph:
+        graph, _ = layer.capture(x, ids, w)
+        step = graph.replay
+        for _ in range(args.warmup):
+            step()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    ms, _ = timer.run(step, args.steps, with_kernel_events=False)
     dist.barrier()
 
     h_x, h_ids, h_w = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
     h_y = torch.empty(x.shape[0], cfg.n, dtype=torch.bfloat16).pin_memory()
     x2, ids2, w2 = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
+    x2.copy_(x)
+    ids2.copy_(ids)
+    w2.copy_(w)
+    if use_graph:
+        e2e_graph, y2 = layer.capture(x2, ids2, w2)
 
     def e2e_step():
         x2.copy_(h_x, non_blocking=True)
         ids2.copy_(h_ids, non_blocking=True)
         w2.copy_(h_w, non_blocking=True)
-        h_y.copy_(layer(x2, ids2, w2), non_blocking=True)
-
+        if use_graph:
+            e2e_graph.replay()
+            h_y.copy_(y2, non_blocking=True)
+        else:
+            h_y.copy_(layer(x2, ids2, w2), non_blocking=True)
     for _ in range(args.warmup):
         e2e_step()
     dist.barrier()
@@ -444,7 +464,8 @@ def bench_ep_decode(args, dev, world, rank, dist):
                    "step": "quant, count all-to-all, dispatch all-to-all, grouped GEMM on local experts, "
                            "return all-to-all, weighted combine",
                    "exchange": "fixed capacity per destination (tokens*topk rows), no host synchronisation; "
-                               + ("peer-memory stores over NVLink" if layer.exchange == "p2p" else "NCCL all-to-all"),
+                               + ("peer-memory stores over NVLink, step replayed as one CUDA graph per rank"
+                                  if layer.exchange == "p2p" else "NCCL all-to-all"),
                    "l2": "weights per rank larger than L2"},
         "tflops": job_flops / (ms * 1e-3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",

@@ -154,7 +154,6 @@ class MoELayer:
             raise ValueError("the peer-memory exchange needs max_tokens_per_rank (fixed capacity)")
         self.exchange = exchange
         self.windows = None
-        self.epoch = 0
         self.group = group
         if group is not None:
             import torch.distributed as dist
@@ -264,17 +263,32 @@ class MoELayer:
         if self.windows is None:
             self.windows = PeerWindows(self.group, cap, H, x.device)
         win, me = self.windows, self.rank
-        self.epoch += 1
-        ep = self.epoch
-        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, me, ep)
+        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, win.own, me)
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
-        a, sa, m_indices, perm_pos = C.ep_permute_p2p(win.own, world, cap, H, E_loc, ep, m_pad, x)
+        a, sa, m_indices, perm_pos = C.ep_permute_p2p(win.own, world, cap, H, E_loc, m_pad, x)
         h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         if self.w2 is not None:
             aq, asc = self.ops.act(h, m_indices)
             h = self.ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
-        C.ep_return_p2p(h, perm_pos, world, cap, win.peers, me, ep)
-        return C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H, ep)
+        C.ep_return_p2p(h, perm_pos, world, cap, win.peers, win.own, me)
+        return C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H)
+
+    def capture(self, x, topk_ids, topk_w):
+        """Record one forward on these (static) input tensors in a CUDA graph.
+
+        Returns (graph, output): ``graph.replay()`` reruns the forward on whatever the input
+        tensors then hold and writes the result into ``output``.  Needs the peer-memory
+        exchange (or a single rank): every step of it reads its step number on the device.
+        The first forward (window set-up, library initialisation) runs here, outside the graph.
+        """
+        if self.world > 1 and self.exchange != "p2p":
+            raise ValueError("graph capture needs exchange='p2p' (the collectives' split sizes are host values)")
+        self.forward(x, topk_ids, topk_w)  # set-up outside the graph
+        torch.cuda.synchronize(x.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = self.forward(x, topk_ids, topk_w)
+        return g, out
 
     def close(self):
         """Release the peer exchange windows (all ranks, after their last forward)."""

@@ -39,6 +39,39 @@ __device__ __forceinline__ int64_t load_idx(const void* p, int dtype, int64_t i)
                                 : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
 }
 
+// Bytes of one dispatched row: [e4m3 data H][FP32 scales H/128][int32 local expert][pad to 16].
+__host__ __device__ __forceinline__ int64_t packed_row_bytes(int64_t H) { return (H + 4 * (H / 128) + 4 + 15) / 16 * 16; }
+
+// Exchange window of one rank: [0, 512) dispatch flags int32[ranks], [512, 1024) return
+// flags int32[ranks], [1024, 1028) status, [1028, 1032) the number of completed exchanges
+// (the step counter: a step's epoch is its value + 1); from 4096 the receive regions
+// [2 parity][ranks source][1 + cap rows][row bytes]; then (256-aligned) the return rows
+// [2 parity][ranks * (1 + cap)][H] BF16 in this rank's own send layout.
+struct Window {
+  int64_t ranks, cap, H, rb;
+  static constexpr int64_t kDispatchFlags = 0, kReturnFlags = 512, kStatus = 1024, kEpoch = 1028, kRecv = 4096;
+  __host__ __device__ int64_t recv_parity(int64_t parity) const { return kRecv + parity * ranks * (cap + 1) * rb; }
+  __host__ __device__ int64_t ret_base() const { return (recv_parity(2) + 255) / 256 * 256; }
+  __host__ __device__ int64_t ret_parity(int64_t parity) const { return ret_base() + parity * ranks * (cap + 1) * H * 2; }
+  __host__ __device__ int64_t bytes() const { return ret_parity(2); }
+};
+
+__host__ __device__ inline Window make_window(int64_t ranks, int64_t cap, int64_t H) {
+  return Window{ranks, cap, H, packed_row_bytes(H)};
+}
+
+// What the peer variants of the exchange kernels need: every rank's window (device array),
+// this rank's window and index, and the window layout.  The step's epoch (flag value and
+// buffer parity) is read from the own window's counter, so the kernels take no per-step
+// host argument and a whole exchange step can be captured in a CUDA graph.
+struct PeerStep {
+  const uint64_t* peers = nullptr;
+  uint8_t* own = nullptr;
+  Window win{};
+  int me = 0;
+  __device__ int32_t epoch() const { return *reinterpret_cast<const volatile int32_t*>(own + Window::kEpoch) + 1; }
+};
+
 // ---- cross-GPU flags of the peer-memory exchange (system scope: the writer is another GPU)
 __device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
   int32_t v;
@@ -141,8 +174,6 @@ __global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64
   }
 }
 
-// Bytes of one dispatched row: [e4m3 data H][FP32 scales H/128][int32 local expert][pad to 16].
-__host__ __device__ __forceinline__ int64_t packed_row_bytes(int64_t H) { return (H + 4 * (H / 128) + 4 + 15) / 16 * 16; }
 
 // One warp per routed (token, slot): copies the token's e4m3 row and scales into one packed row.
 __global__ void ep_pack_kernel(const uint8_t* xq, int64_t xq_stride, const float* xs, int64_t xs_stride, const void* ids,
@@ -206,17 +237,20 @@ constexpr int kFixedMaxExperts = 1024, kFixedMaxRanks = 256;
 // Per-destination, per-local-expert counts go to `scratch`; the last CTA writes them into
 // the region headers.  scratch (zeroed by the host): [ranks] fill, [ranks * E_local]
 // counts, [1] ticket.
-// Peer variant (peers != nullptr): the region of destination d is in d's exchange window,
-// `peers[d] + region_off`; after every row and header landed, the last CTA raises this
-// rank's flag in each destination window (`peers[d] + flag_off`, index `me`) to `epoch`.
+// Peer variant (ps.peers != nullptr): the region of destination d is this rank's source
+// region in d's exchange window for the step's parity; after every row and header landed,
+// the last CTA raises this rank's flag in each destination window to the step's epoch.
 __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x, int x_dtype, int64_t x_stride,
                                                                   const void* ids, int ids_dtype, int64_t T,
                                                                   int64_t topk, int64_t E, int64_t e_per_rank,
                                                                   int64_t ranks, int64_t H, int64_t cap,
                                                                   int32_t* scratch, uint8_t* out_rows,
-                                                                  int32_t* send_index, const uint64_t* peers = nullptr,
-                                                                  int64_t region_off = 0, int64_t flag_off = 0,
-                                                                  int me = 0, int32_t epoch = 0) {
+                                                                  int32_t* send_index, PeerStep ps = PeerStep{}) {
+  const uint64_t* peers = ps.peers;
+  const int32_t epoch = peers ? ps.epoch() : 0;
+  const int64_t region_off = peers ? ps.win.recv_parity(epoch & 1) + ps.me * (cap + 1) * ps.win.rb : 0;
+  const int64_t flag_off = Window::kDispatchFlags;
+  const int me = ps.me;
   __shared__ int s_last;
   __shared__ int64_t s_row, s_e;
   int32_t* fill = scratch;
@@ -290,16 +324,22 @@ __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x,
 // offsets of the local experts' groups (exclusive scan of the per-expert totals over all
 // sources, read from the region headers); then one warp per slot places valid rows as
 // ep_permute_kernel does.
-// Peer variant (flags != nullptr): first waits until every source raised its flag to `epoch`.
+// Peer variant (ps.own != nullptr; `rows` unused): the received regions are the own
+// window's for the step's parity; first waits until every source raised its flag.
 __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* rows, int64_t ranks, int64_t cap,
                                                                int64_t H, int64_t E_local, int32_t* fill, uint8_t* A,
                                                                float* SA, int32_t* m_indices, int32_t* perm_pos,
-                                                               const int32_t* flags = nullptr, int32_t epoch = 0,
-                                                               int32_t* status = nullptr) {
+                                                               PeerStep ps = PeerStep{}) {
   __shared__ int64_t s_off[kFixedMaxExperts];
   __shared__ int32_t s_nsrc[kFixedMaxRanks];
   __shared__ int64_t s_warp_sum[8];
-  if (flags && !wait_peer_flags(flags, static_cast<int>(ranks), epoch, status)) return;
+  if (ps.own) {
+    const int32_t epoch = ps.epoch();
+    rows = ps.own + ps.win.recv_parity(epoch & 1);
+    if (!wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kDispatchFlags), static_cast<int>(ranks),
+                         epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus)))
+      return;
+  }
   const int tid = threadIdx.x;
   const int64_t rb = packed_row_bytes(H);
   auto header = [&](int64_t r) { return reinterpret_cast<const int32_t*>(rows + r * (cap + 1) * rb); };
@@ -365,16 +405,19 @@ __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* ro
 }
 
 // Peer return: one warp per received slot (region src, slot s) whose row was placed at
-// perm_pos; the GEMM row goes straight to the source's window, at the row of its own
-// send layout (me * (cap + 1) + 1 + s) in `peers[src] + ret_off`.  The last CTA raises
-// this rank's flag in every source window (`peers[src] + flag_off`, index `me`).
+// perm_pos; the GEMM row goes straight to the source's window (return rows of the step's
+// parity), at the row of its own send layout (me * (cap + 1) + 1 + s).  The last CTA raises
+// this rank's flag in every source window.
 // scratch: [1] ticket, zeroed by the host.
 __global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* Y, int64_t y_stride,
                                                             const int32_t* perm_pos, int64_t ranks, int64_t cap,
-                                                            int64_t H, const uint64_t* peers, int64_t ret_off,
-                                                            int64_t flag_off, int me, int32_t epoch,
-                                                            int32_t* scratch) {
+                                                            int64_t H, PeerStep ps, int32_t* scratch) {
   __shared__ int s_last;
+  const uint64_t* peers = ps.peers;
+  const int32_t epoch = ps.epoch();
+  const int64_t ret_off = ps.win.ret_parity(epoch & 1);
+  const int64_t flag_off = Window::kReturnFlags;
+  const int me = ps.me;
   const int lane = threadIdx.x & 31;
   const int64_t R = ranks * (cap + 1);
   for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < R;
@@ -409,21 +452,38 @@ __global__ void ep_unpermute_kernel(const __nv_bfloat16* Y, int64_t y_stride, co
 }
 
 // One CTA per token; y[t, :] = bf16(sum_j w[t, j] * rows[send_index[t*k + j], :]) in FP32, slots in order.
-// Peer variant (flags != nullptr): first waits until every rank returned its rows.
+// Peer variant (ps.own != nullptr; `rows` unused): the returned rows are the own window's
+// for the step's parity; first waits until every rank returned its rows; the last CTA then
+// advances the window's step counter (scratch: [1] ticket, zeroed by the host).
 __global__ void ep_combine_kernel(const __nv_bfloat16* rows, const int32_t* send_index, const float* topk_w, int64_t T,
-                                  int64_t topk, int64_t H, __nv_bfloat16* y, const int32_t* flags = nullptr,
-                                  int ranks = 0, int32_t epoch = 0, int32_t* status = nullptr) {
-  if (flags && !wait_peer_flags(flags, ranks, epoch, status)) return;
-  const int64_t t = blockIdx.x;
-  if (t >= T) return;
-  for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
-    float acc = 0.0f;
-    for (int64_t j = 0; j < topk; ++j) {
-      const int32_t r = send_index[t * topk + j];
-      if (r >= 0) acc = fmaf(topk_w[t * topk + j], __bfloat162float(rows[static_cast<int64_t>(r) * H + c]), acc);
-    }
-    y[t * H + c] = __float2bfloat16_rn(acc);
+                                  int64_t topk, int64_t H, __nv_bfloat16* y, PeerStep ps = PeerStep{},
+                                  int32_t* scratch = nullptr) {
+  int32_t epoch = 0;
+  bool ok = true;
+  if (ps.own) {
+    epoch = ps.epoch();
+    rows = reinterpret_cast<const __nv_bfloat16*>(ps.own + ps.win.ret_parity(epoch & 1));
+    ok = wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kReturnFlags),
+                         static_cast<int>(ps.win.ranks), epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus));
   }
+  const int64_t t = blockIdx.x;
+  if (ok && t < T) {
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
+      float acc = 0.0f;
+      for (int64_t j = 0; j < topk; ++j) {
+        const int32_t r = send_index[t * topk + j];
+        if (r >= 0) acc = fmaf(topk_w[t * topk + j], __bfloat162float(rows[static_cast<int64_t>(r) * H + c]), acc);
+      }
+      y[t * H + c] = __float2bfloat16_rn(acc);
+    }
+  }
+  if (!ps.own) return;
+  // every CTA read its rows (and every rank finished the step); the last advances the counter
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(scratch, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) *reinterpret_cast<volatile int32_t*>(ps.own + Window::kEpoch) = epoch;
 }
 
 // Weight-row gathers of transform_weights_for_mega_moe: destination row n of a group
@@ -462,20 +522,7 @@ __global__ void mega_rows_kernel(const uint8_t* src, uint8_t* dst, int64_t G, in
 
 unsigned warp_grid(int64_t warps) { return static_cast<unsigned>((warps * 32 + 255) / 256); }
 
-// Exchange window of one rank: [0, 512) dispatch flags int32[ranks], [512, 1024) return
-// flags int32[ranks], [1024, 1028) status; from 4096 the receive regions
-// [2 parity][ranks source][1 + cap rows][row bytes]; then (256-aligned) the return rows
-// [2 parity][ranks * (1 + cap)][H] BF16 in this rank's own send layout.
-struct Window {
-  int64_t ranks, cap, H, rb;
-  static constexpr int64_t kDispatchFlags = 0, kReturnFlags = 512, kStatus = 1024, kRecv = 4096;
-  __host__ __device__ int64_t recv_parity(int64_t parity) const { return kRecv + parity * ranks * (cap + 1) * rb; }
-  __host__ __device__ int64_t ret_base() const { return (recv_parity(2) + 255) / 256 * 256; }
-  __host__ __device__ int64_t ret_parity(int64_t parity) const { return ret_base() + parity * ranks * (cap + 1) * H * 2; }
-  __host__ __device__ int64_t bytes() const { return ret_parity(2); }
-};
 
-Window make_window(int64_t ranks, int64_t cap, int64_t H) { return Window{ranks, cap, H, packed_row_bytes(H)}; }
 
 int launched() { return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA; }
 
@@ -656,10 +703,10 @@ int cdg_ep_window_status(const void* window, cdg_stream_t stream) {
 
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
                         int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
-                        const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, int32_t* send_index,
+                        const uint64_t* peers, void* window, int32_t me, int32_t* scratch, int32_t* send_index,
                         cdg_stream_t stream) {
   if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || ranks > 128 || E % ranks || H <= 0 || H % 128 || cap < 0 ||
-      E / ranks > cdg::kFixedMaxExperts || !scratch || !peers || me < 0 || me >= ranks || epoch <= 0)
+      E / ranks > cdg::kFixedMaxExperts || !scratch || !peers || !window || me < 0 || me >= ranks)
     return CDG_ERR_INVALID_ARGUMENT;
   if (4 * (E / ranks) > cdg::packed_row_bytes(H)) return CDG_ERR_INVALID_ARGUMENT;
   if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
@@ -668,66 +715,69 @@ int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(scratch, 0, cdg_ep_fixed_scratch_ints(ranks, E) * sizeof(int32_t), st) != cudaSuccess)
     return CDG_ERR_CUDA;
-  const cdg::Window win = cdg::make_window(ranks, cap, H);
-  const int64_t parity = epoch & 1;
-  const int64_t region_off = win.recv_parity(parity) + static_cast<int64_t>(me) * (cap + 1) * win.rb;
+  cdg::PeerStep ps;
+  ps.peers = peers;
+  ps.own = static_cast<uint8_t*>(window);
+  ps.win = cdg::make_window(ranks, cap, H);
+  ps.me = me;
   const unsigned grid = T * topk > 0 ? static_cast<unsigned>(T * topk) : 1u;
   cdg::ep_quant_pack_fixed_kernel<<<grid, 128, 0, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E,
-                                                        E / ranks, ranks, H, cap, scratch, nullptr, send_index, peers,
-                                                        region_off, cdg::Window::kDispatchFlags, me, epoch);
+                                                        E / ranks, ranks, H, cap, scratch, nullptr, send_index, ps);
   return cdg::launched();
 }
 
-int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t epoch,
-                       int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t* fill,
+                       uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                        cdg_stream_t stream) {
   if (!window || ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || E_local <= 0 ||
-      E_local > cdg::kFixedMaxExperts || M_pad < ranks * cap + 127 * E_local || epoch <= 0)
+      E_local > cdg::kFixedMaxExperts || M_pad < ranks * cap + 127 * E_local)
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  const cdg::Window win = cdg::make_window(ranks, cap, H);
-  uint8_t* base = static_cast<uint8_t*>(window);
+  cdg::PeerStep ps;
+  ps.own = static_cast<uint8_t*>(window);
+  ps.win = cdg::make_window(ranks, cap, H);
   const int64_t R = ranks * (cap + 1);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
-  cdg::ep_permute_fixed_kernel<<<grid, 256, 0, st>>>(
-      base + win.recv_parity(epoch & 1), ranks, cap, H, E_local, fill, A, SA, m_indices, perm_pos,
-      reinterpret_cast<const int32_t*>(base + cdg::Window::kDispatchFlags), epoch,
-      reinterpret_cast<int32_t*>(base + cdg::Window::kStatus));
+  cdg::ep_permute_fixed_kernel<<<grid, 256, 0, st>>>(nullptr, ranks, cap, H, E_local, fill, A, SA, m_indices, perm_pos,
+                                                     ps);
   return cdg::launched();
 }
 
 int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t ranks, int64_t cap, int64_t H,
-                      const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, cdg_stream_t stream) {
-  if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || !peers || !scratch || me < 0 || me >= ranks ||
-      epoch <= 0)
+                      const uint64_t* peers, void* window, int32_t me, int32_t* scratch, cdg_stream_t stream) {
+  if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || !peers || !window || !scratch || me < 0 ||
+      me >= ranks)
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(Y) % 16 || y_stride % 8) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  const cdg::Window win = cdg::make_window(ranks, cap, H);
+  cdg::PeerStep ps;
+  ps.peers = peers;
+  ps.own = static_cast<uint8_t*>(window);
+  ps.win = cdg::make_window(ranks, cap, H);
+  ps.me = me;
   const int64_t R = ranks * (cap + 1);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
   cdg::ep_return_p2p_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(Y), y_stride, perm_pos, ranks, cap,
-                                                  H, peers, win.ret_parity(epoch & 1), cdg::Window::kReturnFlags, me,
-                                                  epoch, scratch);
+                                                  H, ps, scratch);
   return cdg::launched();
 }
 
-int cdg_ep_combine_p2p(const void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
-                       int64_t H, int64_t ranks, int64_t cap, int32_t epoch, void* y, cdg_stream_t stream) {
-  if (!window || T < 0 || topk <= 0 || H <= 0 || H % 128 || ranks <= 0 || ranks > 128 || cap < 0 || epoch <= 0)
+int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
+                       int64_t H, int64_t ranks, int64_t cap, int32_t* scratch, void* y, cdg_stream_t stream) {
+  if (!window || !scratch || T < 0 || topk <= 0 || H <= 0 || H % 128 || ranks <= 0 || ranks > 128 || cap < 0)
     return CDG_ERR_INVALID_ARGUMENT;
-  const cdg::Window win = cdg::make_window(ranks, cap, H);
-  const uint8_t* base = static_cast<const uint8_t*>(window);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  cdg::PeerStep ps;
+  ps.own = static_cast<uint8_t*>(window);
+  ps.win = cdg::make_window(ranks, cap, H);
   const unsigned grid = T > 0 ? static_cast<unsigned>(T) : 1u;
-  cdg::ep_combine_kernel<<<grid, 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(base + win.ret_parity(epoch & 1)), send_index, topk_w, T, topk, H,
-      static_cast<__nv_bfloat16*>(y), reinterpret_cast<const int32_t*>(base + cdg::Window::kReturnFlags),
-      static_cast<int>(ranks), epoch, reinterpret_cast<int32_t*>(const_cast<uint8_t*>(base) + cdg::Window::kStatus));
+  cdg::ep_combine_kernel<<<grid, 256, 0, st>>>(nullptr, send_index, topk_w, T, topk, H, static_cast<__nv_bfloat16*>(y),
+                                               ps, scratch);
   return cdg::launched();
 }
 

@@ -335,7 +335,7 @@ uint64_t ep_window_open(const py::bytes& handle) {
 }
 
 torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, int64_t E, int64_t ranks, int64_t cap,
-                              const torch::Tensor& peers, int64_t me, int64_t epoch) {
+                              const torch::Tensor& peers, uint64_t window, int64_t me) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
   TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
               "topk ids must be contiguous [T, topk]");
@@ -348,14 +348,14 @@ torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, 
                               ids.options().dtype(torch::kInt32));
   check_status(cdg_ep_dispatch_p2p(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T, topk,
                                    E, ranks, H, cap, reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
-                                   static_cast<int32_t>(me), static_cast<int32_t>(epoch), scratch.data_ptr<int32_t>(),
-                                   send_index.data_ptr<int32_t>(), cur_stream(x)),
+                                   reinterpret_cast<void*>(window), static_cast<int32_t>(me),
+                                   scratch.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(), cur_stream(x)),
                "ep_dispatch_p2p");
   return send_index;
 }
 
 std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local,
-                                          int64_t epoch, int64_t M_pad, const torch::Tensor& like) {
+                                          int64_t M_pad, const torch::Tensor& like) {
   const c10::cuda::CUDAGuard guard(like.device());
   auto i32 = like.options().dtype(torch::kInt32);
   auto A = torch::empty({M_pad, H}, like.options().dtype(torch::kFloat8_e4m3fn));
@@ -363,8 +363,7 @@ std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_
   auto mi = torch::empty({M_pad}, i32);
   auto pos = torch::empty({ranks * (cap + 1)}, i32);
   auto fill = torch::empty({E_local}, i32);
-  check_status(cdg_ep_permute_p2p(reinterpret_cast<void*>(window), ranks, cap, H, E_local, static_cast<int32_t>(epoch),
-                                  fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()),
+  check_status(cdg_ep_permute_p2p(reinterpret_cast<void*>(window), ranks, cap, H, E_local, fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()),
                                   SA.data_ptr<float>(), mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(),
                                   cur_stream(like)),
                "ep_permute_p2p");
@@ -372,27 +371,29 @@ std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_
 }
 
 void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& perm_pos, int64_t ranks, int64_t cap,
-                   const torch::Tensor& peers, int64_t me, int64_t epoch) {
+                   const torch::Tensor& peers, uint64_t window, int64_t me) {
   TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
   TORCH_CHECK(perm_pos.numel() == ranks * (cap + 1), "perm_pos: one entry per received slot");
   const c10::cuda::CUDAGuard guard(Y.device());
   auto scratch = torch::empty({1}, perm_pos.options());
   check_status(cdg_ep_return_p2p(Y.data_ptr(), Y.stride(0), perm_pos.data_ptr<int32_t>(), ranks, cap, Y.size(1),
-                                 reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()), static_cast<int32_t>(me),
-                                 static_cast<int32_t>(epoch), scratch.data_ptr<int32_t>(), cur_stream(Y)),
+                                 reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+                                 reinterpret_cast<void*>(window), static_cast<int32_t>(me), scratch.data_ptr<int32_t>(),
+                                 cur_stream(Y)),
                "ep_return_p2p");
 }
 
 torch::Tensor ep_combine_p2p(uint64_t window, const torch::Tensor& send_index, const torch::Tensor& topk_w,
-                             int64_t ranks, int64_t cap, int64_t H, int64_t epoch) {
+                             int64_t ranks, int64_t cap, int64_t H) {
   TORCH_CHECK(topk_w.is_cuda() && topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() &&
                   topk_w.dim() == 2 && send_index.numel() == topk_w.numel(),
               "topk weights: FP32 [T, topk] matching send_index");
   const c10::cuda::CUDAGuard guard(topk_w.device());
   const int64_t T = topk_w.size(0), topk = topk_w.size(1);
   auto y = torch::empty({T, H}, topk_w.options().dtype(torch::kBFloat16));
+  auto scratch = torch::empty({1}, send_index.options());
   check_status(cdg_ep_combine_p2p(reinterpret_cast<void*>(window), send_index.data_ptr<int32_t>(),
-                                  topk_w.data_ptr<float>(), T, topk, H, ranks, cap, static_cast<int32_t>(epoch),
+                                  topk_w.data_ptr<float>(), T, topk, H, ranks, cap, scratch.data_ptr<int32_t>(),
                                   y.data_ptr(), cur_stream(topk_w)),
                "ep_combine_p2p");
   return y;
@@ -470,13 +471,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("window"));
   m.def("ep_dispatch_p2p", &ep_dispatch_p2p, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
-        py::arg("ranks"), py::arg("cap"), py::arg("peers"), py::arg("me"), py::arg("epoch"));
+        py::arg("ranks"), py::arg("cap"), py::arg("peers"), py::arg("window"), py::arg("me"));
   m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("cap"), py::arg("hidden"),
-        py::arg("local_experts"), py::arg("epoch"), py::arg("m_pad"), py::arg("like"));
+        py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
   m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("perm_pos"), py::arg("ranks"), py::arg("cap"),
-        py::arg("peers"), py::arg("me"), py::arg("epoch"));
+        py::arg("peers"), py::arg("window"), py::arg("me"));
   m.def("ep_combine_p2p", &ep_combine_p2p, py::arg("window"), py::arg("send_index"), py::arg("topk_w"),
-        py::arg("ranks"), py::arg("cap"), py::arg("hidden"), py::arg("epoch"));
+        py::arg("ranks"), py::arg("cap"), py::arg("hidden"));
   m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
   m.def("ep_unpermute", &ep_unpermute, py::arg("y"), py::arg("perm_pos"));
   m.def("ep_combine", &ep_combine, py::arg("rows"), py::arg("send_index"), py::arg("topk_w"));

@@ -293,16 +293,20 @@ int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t strid
  * through CUDA IPC: create it with cdg_ep_window_create, send the 64-byte handle to the
  * other ranks (any host channel), open theirs with cdg_ep_window_open, and pass the
  * ranks' window addresses as a device array `peers` (uint64 [ranks], this rank's own
- * window at index `me`).  A forward pass uses one `epoch` (1, 2, ... the same on every
- * rank; windows are double-buffered by its parity):
+ * window `window` at index `me`).  Each rank runs, once per exchange step and in this order:
  *   cdg_ep_dispatch_p2p   quantise + pack (as cdg_ep_quant_pack_fixed) straight into each
  *                         destination's window, then raise this rank's flag there;
  *   cdg_ep_permute_p2p    wait (bounded) for every source's flag, then permute (as
  *                         cdg_ep_permute_fixed) from the own window;
  *   cdg_ep_return_p2p     store each GEMM row straight into its source's window, raise flags;
- *   cdg_ep_combine_p2p    wait for every rank's rows, then combine (as cdg_ep_combine).
- * Plain stores and loads over NVLink: no multicast.  A wait that gives up after 2 s skips
- * its CTA's work and sets the window's status word (cdg_ep_window_status reports it). */
+ *   cdg_ep_combine_p2p    wait for every rank's rows, combine (as cdg_ep_combine), and advance
+ *                         the window's step counter.
+ * The step number (flag value; the windows are double-buffered by its parity) lives in the
+ * window, so the calls take no per-step argument and a whole step can be captured in a CUDA
+ * graph; every rank must run the same number of steps.  Plain stores and loads over NVLink:
+ * no multicast.  A wait that gives up after 2 s skips its CTA's work and sets the window's
+ * status word (cdg_ep_window_status reports it).  scratch: int32
+ * [cdg_ep_fixed_scratch_ints(ranks, E)] for dispatch, int32 [1] for return and combine. */
 size_t cdg_ep_window_bytes(int64_t ranks, int64_t cap, int64_t H);
 int cdg_ep_window_create(size_t bytes, void** window, void* ipc_handle /* 64 bytes out */);
 int cdg_ep_window_open(const void* ipc_handle, void** window);
@@ -310,15 +314,15 @@ int cdg_ep_window_close(void* window, int32_t opened);
 int cdg_ep_window_status(const void* window, cdg_stream_t stream);
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
                         int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
-                        const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, int32_t* send_index,
+                        const uint64_t* peers, void* window, int32_t me, int32_t* scratch, int32_t* send_index,
                         cdg_stream_t stream);
-int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t epoch,
-                       int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t* fill,
+                       uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                        cdg_stream_t stream);
 int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t ranks, int64_t cap, int64_t H,
-                      const uint64_t* peers, int32_t me, int32_t epoch, int32_t* scratch, cdg_stream_t stream);
-int cdg_ep_combine_p2p(const void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
-                       int64_t H, int64_t ranks, int64_t cap, int32_t epoch, void* y, cdg_stream_t stream);
+                      const uint64_t* peers, void* window, int32_t me, int32_t* scratch, cdg_stream_t stream);
+int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
+                       int64_t H, int64_t ranks, int64_t cap, int32_t* scratch, void* y, cdg_stream_t stream);
 
 /* out[i, :] = Y[perm_pos[i], :] (BF16 rows of length H); rows with perm_pos[i] = -1 are not written. */
 int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R, int64_t H, void* out,

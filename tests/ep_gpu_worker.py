@@ -47,6 +47,19 @@ def main():
             if rank == 0:
                 nw, rl2 = errors(torch.cat(parts), y_one)
                 assert nw <= 1e-3 and rl2 <= 1e-3, (mode, it, nw, rl2)
+        if exchange == "p2p":
+            # the same step as a CUDA graph, replayed
+            xs, idss, ws = x[ts].clone(), ids[ts].clone(), w[ts].clone()
+            graph, y_g = layer.capture(xs, idss, ws)
+            for it in range(3):
+                graph.replay()
+                parts = [torch.empty_like(y_g) for _ in range(world)]
+                dist.all_gather(parts, y_g)
+                if rank == 0:
+                    nw, rl2 = errors(torch.cat(parts), y_one)
+                    assert nw <= 1e-3 and rl2 <= 1e-3, ("graph", it, nw, rl2)
+            torch.cuda.synchronize()
+            del graph
         if layer.windows is not None:
             assert layer.windows.status() == 0, "a peer wait gave up"
         dist.barrier()
