@@ -49,8 +49,9 @@ import torch  # noqa: E402
 
 METRIC = "grouped FP8×FP4 MoE GEMM TFLOPS and HBM GB/s vs roofline at 1/2/4/8 B200"
 DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
-# library kernels per GEMM call: cdg_prep_kernel, cdg_gemm_kernel<16>, <32>, <128>, cdg_generic_kernel
-GEMM_LAUNCHES = 5
+# library kernels per GEMM call on the CTA-pair path: cdg_prep_kernel, cdg_gemm_pair_kernel<16,4>,
+# <32,2>, <128,1>, <128,1,direct>, cdg_generic_kernel
+GEMM_LAUNCHES = 6
 # DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
 # captures summarised under profiles/ (absent: no capture of the current kernels yet).
 NCU_TRAFFIC = {
@@ -230,7 +231,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4"])
+    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c2u", "c3u"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -13,6 +13,9 @@ Configs (``CONFIGS``):
   c2  E=256, K=2048, N=4096, 8192 tokens x top-8 uniform, A = silu(g)*u (prefill FC2)
   c3  E=256, K=4096, N=4096, 16384 tokens x top-8, Zipf(1.2) expert popularity
   c4  the expert-parallel layer: 32768 tokens x top-8, FC1 K=N=4096, FC2 K=2048, N=4096
+  c2u, c3u  c2 and c3 with UE8M0 activation scales: each 1x128 scale rounded up to a
+      power of two and the block requantised with it (the DeepGEMM UE8M0 recipe for
+      SM100 activations); not a benchmark config of the reference, a second data format
 """
 
 from __future__ import annotations
@@ -36,6 +39,7 @@ class Config:
     topk: int
     routing: str  # "uniform" | "zipf" | "multinomial"
     swiglu_input: bool = False
+    ue8m0_scales: bool = False  # activation scales rounded up to powers of two
 
 
 CONFIGS = {
@@ -43,6 +47,8 @@ CONFIGS = {
     "c1": Config("c1", 256, 4096, 4096, 64, 8, "uniform"),
     "c2": Config("c2", 256, 2048, 4096, 8192, 8, "uniform", swiglu_input=True),
     "c3": Config("c3", 256, 4096, 4096, 16384, 8, "zipf"),
+    "c2u": Config("c2u", 256, 2048, 4096, 8192, 8, "uniform", swiglu_input=True, ue8m0_scales=True),
+    "c3u": Config("c3u", 256, 4096, 4096, 16384, 8, "zipf", ue8m0_scales=True),
     "c4_fc1": Config("c4_fc1", 256, 4096, 4096, 32768, 8, "uniform"),
     "c4_fc2": Config("c4_fc2", 256, 2048, 4096, 32768, 8, "uniform", swiglu_input=True),
 }
@@ -110,6 +116,10 @@ def make_inputs(cfg: Config, device="cpu", seed: int = 0, weight_device=None):
     else:
         x = torch.randn(cfg.tokens, cfg.k, generator=g, dtype=torch.float32).to(torch.bfloat16)
     xq, xs = per_block_cast_to_fp8(x.to(device).float())
+    if cfg.ue8m0_scales:
+        xs = torch.exp2(torch.ceil(torch.log2(xs)))
+        xb = x.to(device).float().view(cfg.tokens, cfg.k // 128, 128) / xs.unsqueeze(-1)
+        xq = xb.view(cfg.tokens, cfg.k).to(torch.float8_e4m3fn)
     valid = src >= 0
     m_pad = m_indices.numel()
     a = torch.zeros(m_pad, cfg.k, dtype=torch.float8_e4m3fn, device=device)

@@ -73,6 +73,9 @@ const DeviceInfo& device_info(int dev) {
       if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                PairSmem<128, 1>::kBytes) != cudaSuccess)
         return;
+      if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<128, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PairSmem<128, 1, true>::kBytes) != cudaSuccess)
+        return;
       if (cudaFuncSetAttribute(cdg_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
           cudaSuccess)
         return;
@@ -240,6 +243,34 @@ int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const u
              : CDG_ERR_CUDA;
 }
 
+// Tensor maps of the direct wide kernel: A itself ([M rows][K] e4m3, 64 rows of one
+// CTA per box) and the activation scale atoms the prep kernel wrote ([nblk * K/128][128
+// words], one 512-byte atom per box).
+int make_direct_tmaps(const cdg_gemm_args* g, const uint32_t* tok_sf, int64_t nblk, CUtensorMap* ta,
+                      CUtensorMap* tsf) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return CDG_ERR_CUDA;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(g->M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->a_row_stride)};
+    cuuint32_t box[2] = {128, 64};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g->a), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return CDG_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(nblk * (g->K / 128))};
+  cuuint64_t strides[1] = {512};
+  cuuint32_t box[2] = {128, 1};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(tsf, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(tok_sf), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? CDG_OK
+             : CDG_ERR_CUDA;
+}
+
 // Launch with programmatic stream serialization: the kernel may be scheduled while
 // the previous kernel of the stream drains and waits for it on the device
 // (griddepcontrol.wait), which hides the launch gap between the GEMM's kernels.
@@ -376,6 +407,10 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.blk_mask = blk_mask;
   pa.ctrl = ctrl;
   pa.lists = lists;
+  const bool pair_path = g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2;
+  uint32_t* tok_sf = reinterpret_cast<uint32_t*>(ws + wl.tok_sf);
+  pa.tok_sf = tok_sf;
+  pa.allow_direct = pair_path ? 1 : 0;
   const dim3 prep_grid(static_cast<unsigned>(nblk), static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
   if (ids_dtype == CDG_DTYPE_I64)
     cdg_prep_kernel<int64_t><<<prep_grid, 256, 0, stream>>>(pa);
@@ -407,7 +442,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.fill_rest = skip_ungrouped ? 0 : 1;
 
   if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
-  if (g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2) {
+  if (pair_path) {
     // CTA pairs (tcgen05 cta_group::2): two adjacent 128-column tiles per cluster; four MMA
     // issuers for tiny blocks, two for narrow, one for wide (math-bound) blocks.
     CUtensorMap p16, p32, p128, tsf;
@@ -418,18 +453,27 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = skip_ungrouped ? 0 : 1;
     if (launch_pdl(cdg_gemm_pair_kernel<16, 4>, grid, PairSmem<16, 4>::kThreads, PairSmem<16, 4>::kBytes, stream, tw,
-                   p16, tsf, ka) != cudaSuccess)
+                   p16, tsf, tsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     ka.do_zero_blocks = 0;
     ka.list = lists + kClassNarrow * nblk;
     ka.count_slot = kCtrlCount0 + kClassNarrow;
     if (launch_pdl(cdg_gemm_pair_kernel<32, 2>, grid, PairSmem<32, 2>::kThreads, PairSmem<32, 2>::kBytes, stream, tw,
-                   p32, tsf, ka) != cudaSuccess)
+                   p32, tsf, tsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     ka.list = lists + kClassWide * nblk;
     ka.count_slot = kCtrlCount0 + kClassWide;
     if (launch_pdl(cdg_gemm_pair_kernel<128, 1>, grid, PairSmem<128, 1>::kThreads, PairSmem<128, 1>::kBytes, stream,
-                   tw, p128, tsf, ka) != cudaSuccess)
+                   tw, p128, tsf, tsf, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
+    // Wide blocks whose activation scales are all powers of two: raw e4m3 rows.
+    CUtensorMap ad, tok;
+    st = make_direct_tmaps(g, tok_sf, nblk, &ad, &tok);
+    if (st != CDG_OK) return st;
+    ka.list = lists + kClassWideDirect * nblk;
+    ka.count_slot = kCtrlCount0 + kClassWideDirect;
+    if (launch_pdl(cdg_gemm_pair_kernel<128, 1, true>, grid, PairSmem<128, 1, true>::kThreads,
+                   PairSmem<128, 1, true>::kBytes, stream, tw, ad, tsf, tok, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
   } else {
     // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.

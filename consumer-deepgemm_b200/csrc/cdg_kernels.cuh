@@ -115,6 +115,8 @@ struct PrepArgs {
   int nblk;
   TileMap tm;              // rows of each block
   uint8_t* hilo;           // [2][nblk*128][K]
+  uint32_t* tok_sf;        // [nblk][K/128][128] words: activation scale atoms of direct blocks
+  int allow_direct;        // wide blocks with power-of-two scales may take the direct class
   int32_t* row_exp;        // [nblk*128] exponent E of each routed row's activation planes
   int4* blk_info;          // [nblk] {expert (-1 none, -2 several), rows spanned, class, 0}
   uint4* blk_mask;         // [nblk] bit r set when row r of the block has the block's expert
@@ -125,6 +127,16 @@ struct PrepArgs {
 // 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
 __device__ __forceinline__ float ue8m0_to_f32(uint32_t e) {
   return e == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(e << 23);
+}
+
+// UE8M0 code of an activation scale 2^s with s in [-117, 118], or -1.  In that range
+// every e4m3 value times 2^s (magnitudes 2^-9 .. 448) is a normal BF16 number, so
+// BF16 dequantisation of the row is exact and equals the product the tensor core forms
+// from the e4m3 value and the scale factor.
+__device__ __forceinline__ int pow2_code(float v) {
+  const uint32_t bits = __float_as_uint(v);
+  const uint32_t e = bits >> 23;  // sign bit 0 for positive values
+  return ((bits & 0x7FFFFFu) == 0 && e >= 10 && e <= 245) ? static_cast<int>(e) : -1;
 }
 
 // Activation scale of row r, 128-wide K block kb: FP32, or UE8M0 packed four to a word.
@@ -157,7 +169,7 @@ constexpr int kPrepK = 1024;
 template <typename IdT>
 __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ int s_min_id, s_max_id, s_max_row;
-  __shared__ int s_last, s_nv;
+  __shared__ int s_last, s_nv, s_pow2;
   __shared__ uint8_t s_vrow[128];  // the block's rows that carry its expert (compacted)
   __shared__ int s_id[128];
   __shared__ uint32_t s_mask[4];
@@ -171,6 +183,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     s_max_id = -1;
     s_max_row = -1;
     s_nv = 0;
+    s_pow2 = 1;
   }
   if (tid < 4) s_mask[tid] = 0u;
   int row0, nrows;
@@ -223,12 +236,15 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       const int r = row0 + tid;
       if (s_id[tid] == expert) {
         float smax = 0.0f;
+        bool pow2 = true;
         for (int kb = 0; kb < kb_count; ++kb) {
-          const float sbf =
-              __bfloat162float(__float2bfloat16_rn(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, kb)));
+          const float sraw = load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, kb);
+          const float sbf = __bfloat162float(__float2bfloat16_rn(sraw));
           if (isfinite(sbf)) smax = fmaxf(smax, fabsf(sbf));
+          pow2 = pow2 && pow2_code(sraw) >= 0;
         }
         if (smax > 0.0f) frexpf(smax, &emax);
+        if (!pow2) atomicAnd(&s_pow2, 0);
       }
       s_exp[tid] = emax;
       if (blockIdx.y == 0) p.row_exp[b * 128 + tid] = emax;
@@ -243,6 +259,22 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
           : 0.0f;
     }
     __syncthreads();
+    // Direct class: a wide block whose routed rows' scales are all powers of two.  The
+    // reference's bf16(bf16(a) * bf16(2^s)) is then the exact product a * 2^s, which the
+    // tensor core forms itself from the raw e4m3 rows and the scale as a UE8M0 scale factor:
+    // no planes, one MMA per K slice.  Write this CTA's K blocks' 512-byte atoms (row r's
+    // byte at (r%32)*16 + (r/32)*4 + c, the same byte for the four 32-wide sub-blocks c).
+    if (cls == kClassWide && p.allow_direct && s_pow2) {
+      cls = kClassWideDirect;
+      for (int it = tid; it < kbn * 128; it += blockDim.x) {
+        const int kl = it >> 7, rr = it & 127;
+        const int code =
+            s_id[rr] == expert ? pow2_code(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb0 + kl))
+                               : 127;
+        p.tok_sf[(static_cast<int64_t>(b) * kb_count + kb0 + kl) * 128 + (rr & 31) * 4 + (rr >> 5)] =
+            static_cast<uint32_t>(code) * 0x01010101u;
+      }
+    } else {
     // (2) activation planes of the rows that carry the block's expert, one 16-byte chunk
     //     per item; consecutive threads read consecutive chunks of a row (coalesced).
     //     Other rows of the planes are not written: whatever they hold only reaches
@@ -275,6 +307,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       uint8_t* dst = p.hilo + (static_cast<int64_t>(b) * 128 + rr) * K + col;
       *reinterpret_cast<uint4*>(dst) = hi4;
       *reinterpret_cast<uint4*>(dst + plane) = lo4;
+    }
     }
   }
   if (blockIdx.y != 0) return;

@@ -15,7 +15,9 @@ enum : int {
   kClassWide = 2,       // one expert, more rows                        -> cdg_gemm_kernel<128>
   kClassZero = 3,       // no row with a valid id                       -> zero fill (tiny kernel)
   kClassIrregular = 4,  // rows of two or more experts                  -> cdg_generic_kernel
-  kNumClasses = 5,
+  kClassWideDirect = 5, // a wide block whose activation scales are all powers of two: the raw
+                        // e4m3 rows with their scales as UE8M0 MMA scale factors (one plane)
+  kNumClasses = 6,
 };
 constexpr int kTinyTok = 16;
 constexpr int kNarrowTok = 32;
@@ -73,7 +75,8 @@ struct TileMap {
 
 // Workspace regions of one GEMM call.
 struct WorkspaceLayout {
-  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, row_ids = 0, row_exp = 0, hilo = 0, sfw_atoms = 0, total = 0;
+  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, row_ids = 0, row_exp = 0, hilo = 0, tok_sf = 0, sfw_atoms = 0,
+         total = 0;
 
   static WorkspaceLayout make(int64_t M, int64_t nblk, int64_t K, int64_t N, int64_t E, bool fast, bool row_ids,
                               bool sfw_from_rows) {
@@ -96,6 +99,8 @@ struct WorkspaceLayout {
       off = align_up(off + static_cast<size_t>(nblk) * 128 * 4, 1024);
       w.hilo = off;
       off = align_up(off + static_cast<size_t>(2) * nblk * 128 * K, 1024);
+      w.tok_sf = off;  // [nblk][K/128] 512-byte activation scale atoms of direct blocks
+      off = align_up(off + static_cast<size_t>(nblk) * (K / 128) * 512, 1024);
       if (sfw_from_rows) {
         w.sfw_atoms = off;
         off = align_up(off + static_cast<size_t>(E) * ((N + 127) / 128) * (K / 128) * 512, 1024);

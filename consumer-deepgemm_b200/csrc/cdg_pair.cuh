@@ -39,20 +39,22 @@
 
 namespace cdg {
 
-template <int TOK, int NI>
+template <int TOK, int NI, bool DIRECT = false>
 struct PairSmem {
   static constexpr bool kWide = TOK > 32;
+  static_assert(!DIRECT || kWide, "the direct (single-plane) variant serves wide blocks");
   static constexpr int kRowsA = kWide ? 64 : TOK;  // activation rows per plane held by one CTA
-  static constexpr int kPlanes = kWide ? 2 : 1;    // planes held by one CTA
+  static constexpr int kPlanes = kWide && !DIRECT ? 2 : 1;  // planes held by one CTA
   // A multiple of NI: stage s is always consumed by issuer s % NI, in order, so an
   // issuer never waits on a stage use whose predecessor it did not consume itself.
-  static constexpr int kStages = kWide ? 6 : NI == 4 ? 12 : 10;
+  static constexpr int kStages = DIRECT ? 8 : kWide ? 6 : NI == 4 ? 12 : 10;
   static_assert(kStages % NI == 0, "stage ring must split evenly over the issuers");
   static constexpr int kW = 128 * 128;             // weight tile, bytes per stage
   static constexpr int kA = kRowsA * 128;          // one plane's rows, bytes per stage
   static constexpr int kStageBytes = kW + kPlanes * kA;  // operand tiles (1024-byte multiple)
-  static constexpr int kSfRing = kStages * kStageBytes;  // then one 512-byte scale atom per stage
-  static constexpr int kOneAtom = kSfRing + kStages * 512;  // constant activation scale atom
+  static constexpr int kSfRing = kStages * kStageBytes;  // then one 512-byte weight scale atom per stage
+  static constexpr int kTsfRing = kSfRing + kStages * 512;  // direct: one activation scale atom per stage
+  static constexpr int kOneAtom = kTsfRing + (DIRECT ? kStages * 512 : 0);  // constant activation scale atom
   // narrow and wide tiles: per epilogue warp a [16 rows x 32 columns] BF16 staging tile, so
   // that D leaves as 16-byte row segments instead of 2-byte column elements
   static constexpr bool kStagedStores = TOK > 16;
@@ -63,26 +65,33 @@ struct PairSmem {
   static constexpr int kBytes = kBarOffset + kBarBytes + 1024;          // + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
   // bytes one CTA's copies of one stage add to the even CTA's `full` barrier
-  static constexpr uint32_t kTxPerCta = 128u * 64u + kPlanes * kA + 512u;
+  static constexpr uint32_t kTxPerCta = 128u * 64u + kPlanes * kA + 512u + (DIRECT ? 512u : 0u);
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned for SW128 tiles");
   // TMEM: per accumulator buffer NI partials of kPartCols columns; two buffers; then
   // per issuer two 4-column weight scale sets; then per issuer the constant activation
-  // scale set (each issuer copies its own, so no issuer reads another's TMEM writes).
+  // scale set (each issuer copies its own, so no issuer reads another's TMEM writes);
+  // direct: two 4-column activation scale sets.
   static constexpr uint32_t kPartCols = kWide ? 128 : 2 * TOK;
   static constexpr uint32_t kAccCols = NI * kPartCols;
   static constexpr uint32_t kSfwCol = 2 * kAccCols;
   static constexpr uint32_t kSfaCol = kSfwCol + 8 * NI;
-  static_assert(kSfaCol + 4 * NI <= 512, "TMEM columns");
+  static constexpr uint32_t kTsfCol = kSfaCol + 4 * NI;
+  static_assert(kTsfCol + 8 <= 512, "TMEM columns");
   static_assert(!kWide || NI == 1, "wide tiles are math-bound: one issuer");
   static constexpr int kEpiWarp0 = NI < 4 ? 4 : NI + 1;
   static constexpr int kThreads = (kEpiWarp0 + 4) * 32;
 };
 
-template <int TOK, int NI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::kThreads, 1)
+// DIRECT (wide blocks whose activation scales are powers of two): tmap_a covers A itself
+// ([M rows][K] e4m3), each CTA loads half of the block's rows; tmap_tsf covers the block's
+// activation scale atoms written by the prep kernel; one MMA per K slice with those atoms as
+// the B scale factors; no exponent in the epilogue.
+template <int TOK, int NI, bool DIRECT = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DIRECT>::kThreads, 1)
     cdg_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
-                         const __grid_constant__ CUtensorMap tmap_sf, GemmArgs p) {
-  using L = PairSmem<TOK, NI>;
+                         const __grid_constant__ CUtensorMap tmap_sf, const __grid_constant__ CUtensorMap tmap_tsf,
+                         GemmArgs p) {
+  using L = PairSmem<TOK, NI, DIRECT>;
   constexpr int S = L::kStages;
   constexpr bool kWide = L::kWide;
   constexpr uint32_t kTmemCols = 512;
@@ -106,6 +115,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
   auto stage_w = [&](int s) { return smem + s * L::kStageBytes; };
   auto stage_a = [&](int s) { return smem + s * L::kStageBytes + L::kW; };
   auto stage_sf = [&](int s) { return smem + L::kSfRing + s * 512; };
+  auto stage_tsf = [&](int s) { return smem + L::kTsfRing + s * 512; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* full = bars;       // [S] (even CTA's count both CTAs' copies)
   uint64_t* empty = bars + S;  // [S] stage consumed (multicast by the MMA commit)
@@ -121,6 +131,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_sf);
+    if (DIRECT) prefetch_tmap(&tmap_tsf);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -168,7 +179,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
         const int expert = cur.y;
         const int wrow = expert * p.N + nt * 128;
         const int atom0 = (expert * n_tiles + nt) * k_steps;
-        const int a_row = kWide ? blk * 128 + static_cast<int>(rank) * wide_half(cur.z) : blk * 128;
+        int a_row = kWide ? blk * 128 + static_cast<int>(rank) * wide_half(cur.z) : blk * 128;
+        if (DIRECT) {  // rows of A itself
+          int row0, nrows;
+          p.tm.rows(blk, row0, nrows);
+          a_row = row0 + static_cast<int>(rank) * wide_half(cur.z);
+        }
         for (int kb = 0; kb < k_steps; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, p.status,
                                  wait_code(1, static_cast<int>(rank), stage, phase ^ 1, kb))) {
@@ -178,10 +194,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
           const uint32_t fb = full0 + stage * 8;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * L::kTxPerCta);
           tma_load_2d_pair(stage_w(stage), &tmap_w, fb, kb * 128, wrow);
-          if (kWide)
+          if (DIRECT) {
+            tma_load_2d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row);
+            tma_load_2d_pair(stage_tsf(stage), &tmap_tsf, fb, 0, blk * k_steps + kb);
+          } else if (kWide) {
             tma_load_3d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row, 0);
-          else
+          } else {
             tma_load_3d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row, static_cast<int>(rank));
+          }
           tma_load_2d_pair(stage_sf(stage), &tmap_sf, fb, 0, atom0 + kb);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -223,6 +243,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
           tc_fence_after();
           const uint32_t sfw_t = tmem_base + L::kSfwCol + j * 8 + (n_own & 1) * 4;
           tc_cp_sf_atom_pair(sfw_t, smem_desc_sf(smem_u32(stage_sf(stage))));
+          const uint32_t sfb_t = DIRECT ? tmem_base + L::kTsfCol + (n_own & 1) * 4 : sfa_t;
+          if (DIRECT) tc_cp_sf_atom_pair(sfb_t, smem_desc_sf(smem_u32(stage_tsf(stage))));
           const uint32_t w_addr = smem_u32(stage_w(stage));
           const uint32_t a_addr = smem_u32(stage_a(stage));
 #pragma unroll
@@ -230,8 +252,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
             const uint64_t wd = smem_desc_sw128(w_addr + k * 32);
             const uint32_t idesc = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 256, n_mma, k, k);
             const uint32_t accumulate = (kb != kb0 || k != 0) ? 1u : 0u;
-            tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + k * 32), idesc, accumulate, sfw_t, sfa_t);
-            if (kWide)
+            tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + k * 32), idesc, accumulate, sfw_t, sfb_t);
+            if (kWide && !DIRECT)
               tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + L::kA + k * 32), idesc, 1u, sfw_t, sfa_t);
           }
           tc_commit_pair(&empty[stage], 0x3);
@@ -271,8 +293,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
         float row_sc[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          row_sc[k] = __uint_as_float(
-              static_cast<uint32_t>(min(max(__ldg(p.row_exp + blk * 128 + k * 32 + lane) + 127, 1), 254)) << 23);
+          row_sc[k] = DIRECT ? 1.0f  // direct: the scale factors already carry the scales
+                             : __uint_as_float(static_cast<uint32_t>(
+                                   min(max(__ldg(p.row_exp + blk * 128 + k * 32 + lane) + 127, 1), 254)) << 23);
         if (!mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
                                wait_code(4, static_cast<int>(rank), acc, acc_phase, local - 1))) {
           ok = false;

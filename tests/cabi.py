@@ -124,6 +124,17 @@ def gemm(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, stream=None, check
     return ws
 
 
+# Block classes of the prep kernel, in the order of their control words (1..6).
+BLOCK_CLASSES = ("tiny", "narrow", "wide", "zero", "irregular", "wide_direct")
+
+
+def block_classes(ws: torch.Tensor) -> dict:
+    """Blocks per class planned by the call that used workspace `ws` (as returned by gemm)."""
+    off = (ws.data_ptr() + 1023) // 1024 * 1024 - ws.data_ptr()
+    words = ws[off + 4:off + 4 + 4 * len(BLOCK_CLASSES)].cpu().view(torch.int32).tolist()
+    return dict(zip(BLOCK_CLASSES, words))
+
+
 def transform_sf(sb: torch.Tensor) -> torch.Tensor:
     l = lib()
     E, N, KB = sb.shape

@@ -140,6 +140,81 @@ def test_packed_ue8m0_activation_scales(name, flags, mn_major):
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
 
 
+def _pow2_scales(sa: torch.Tensor) -> torch.Tensor:
+    """FP32 activation scales rounded up to powers of two (as UE8M0 quantisation recipes do)."""
+    return torch.exp2(torch.ceil(torch.log2(sa.float().clamp(min=2.0 ** -100))))
+
+
+POW2_CASES = [n for n in GEMM_CASES + MASKED_CASES + PACKED_SCALE_CASES
+              if n.startswith(("c0", "edge_block_classes", "edge_ragged", "edge_interleaved", "edge_aligned",
+                               "edge_psum", "edge_n40", "edge_int64", "masked_", "ue8m0x4_"))]
+
+
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_SINGLE_CTA], ids=["dispatch", "single_cta"])
+@pytest.mark.parametrize("name", POW2_CASES)
+def test_power_of_two_fp32_scales(name, flags):
+    """FP32 activation scales that are all powers of two: wide blocks take the direct class
+    (raw e4m3 rows, scales as UE8M0 MMA scale factors) on the CTA-pair path.  Checked
+    against the oracle on the same inputs, same tolerances as the golden cases."""
+    c = load_gemm_case(name)
+    if c["a"].dtype != torch.float8_e4m3fn or c["sa"] is None:
+        pytest.skip("activation scales only apply to FP8 activations")
+    sa = _pow2_scales(c["sa"])
+    masked = c["masked"] or name.startswith("masked_")
+    b, sb = c["b"], c["sb"]
+    if masked and b.dim() == 2:
+        b, sb = b.unsqueeze(0), sb.unsqueeze(0)
+    ids = c["m_indices"]
+    if masked and c["b"].dim() == 2:
+        ids = None
+    ref = torch.empty(c["d"].shape, dtype=c["d_dtype"])
+    if masked:
+        oracle.m_grouped_fp8_fp4_gemm_nt_masked((c["a"], sa), (c["b"], c["sb"]), ref, ids)
+    else:
+        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((c["a"], sa), (b, sb), ref, ids)
+    d = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    ws = cabi.gemm(c["a"].to(DEV), sa.to(DEV), b.to(DEV), sb.to(DEV), d, None if ids is None else ids.to(DEV),
+                   flags=flags, masked=masked)
+    torch.cuda.synchronize()
+    out = d.cpu()
+    assert not torch.isnan(out).any(), "rows left unwritten"
+    if masked:
+        rows = (torch.ones(out.shape[0], dtype=torch.bool) if ids is None
+                else _masked_covered(out.shape[0], ids, b.shape[0]))
+    else:
+        rows = ~_invalid_rows(c)
+    assert bool((out[~rows].float() == 0).all())
+    nw, rl2 = errors(out, ref, rows)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+    cls = cabi.block_classes(ws)
+    if flags == 0 and b.shape[1] % 256 == 0:
+        assert cls["wide"] == 0, cls  # every wide block had power-of-two scales
+    else:
+        assert cls["wide_direct"] == 0, cls  # the direct class is a CTA-pair kernel
+
+
+def test_direct_class_is_per_block():
+    """One scale that is not a power of two keeps its block on the two-plane path while
+    the other wide blocks go direct; both kinds of block match the oracle."""
+    c = load_gemm_case("ue8m0x4_ragged")
+    sa = c["sa"].float().clone()
+    ids = c["m_indices"]
+    e0_rows = (ids == int(ids[ids >= 0][0])).nonzero().flatten()
+    sa[int(e0_rows[3]), 1] *= 1.5
+    ref = torch.empty(c["d"].shape, dtype=c["d_dtype"])
+    oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((c["a"], sa), (c["b"], c["sb"]), ref, ids)
+    d = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    ws = cabi.gemm(c["a"].to(DEV), sa.to(DEV), c["b"].to(DEV), c["sb"].to(DEV), d, ids.to(DEV))
+    torch.cuda.synchronize()
+    cls = cabi.block_classes(ws)
+    assert cls["wide"] >= 1 and cls["wide_direct"] >= 1, cls
+    bad = _invalid_rows(c)
+    out = d.cpu()
+    assert bool((out[bad].float() == 0).all())
+    nw, rl2 = errors(out, ref, ~bad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (nw, rl2)
+
+
 def test_packed_scales_public_api():
     import consumer_deep_gemm as cdg
 
