@@ -18,6 +18,7 @@
 #include "cdg_b200.h"
 #include "cdg_kernels.cuh"
 #include "cdg_pair.cuh"
+#include "cdg_wide.cuh"
 #include "cdg_layout.h"
 
 namespace cdg {
@@ -70,11 +71,11 @@ const DeviceInfo& device_info(int dev) {
       if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                PairSmem<32, 2>::kBytes) != cudaSuccess)
         return;
-      if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               PairSmem<128, 1>::kBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(cdg_gemm_wide_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               WideSmem<false>::kBytes) != cudaSuccess)
         return;
-      if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<128, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               PairSmem<128, 1, true>::kBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(cdg_gemm_wide_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               WideSmem<true>::kBytes) != cudaSuccess)
         return;
       if (cudaFuncSetAttribute(cdg_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
           cudaSuccess)
@@ -243,10 +244,10 @@ int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const u
              : CDG_ERR_CUDA;
 }
 
-// Tensor maps of the direct wide kernel: A itself ([M rows][K] e4m3, 64 rows of one
-// CTA per box) and the activation scale atoms the prep kernel wrote ([nblk * K/128][128
+// Tensor maps of the wide kernels: A itself ([M rows][K] e4m3, 64 rows of one CTA per
+// box; direct class) and the token scale atoms the prep kernel wrote ([nblk * K/128][128
 // words], one 512-byte atom per box).
-int make_direct_tmaps(const cdg_gemm_args* g, const uint32_t* tok_sf, int64_t nblk, CUtensorMap* ta,
+int make_wide_tmaps(const cdg_gemm_args* g, const uint32_t* tok_sf, int64_t nblk, CUtensorMap* ta,
                       CUtensorMap* tsf) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return CDG_ERR_CUDA;
@@ -410,7 +411,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   const bool pair_path = g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2;
   uint32_t* tok_sf = reinterpret_cast<uint32_t*>(ws + wl.tok_sf);
   pa.tok_sf = tok_sf;
-  pa.allow_direct = pair_path ? 1 : 0;
+  pa.pair_wide = pair_path ? 1 : 0;
   const dim3 prep_grid(static_cast<unsigned>(nblk), static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
   if (ids_dtype == CDG_DTYPE_I64)
     cdg_prep_kernel<int64_t><<<prep_grid, 256, 0, stream>>>(pa);
@@ -444,7 +445,8 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
   if (pair_path) {
     // CTA pairs (tcgen05 cta_group::2): two adjacent 128-column tiles per cluster; four MMA
-    // issuers for tiny blocks, two for narrow, one for wide (math-bound) blocks.
+    // issuers for tiny blocks, two for narrow; wide blocks in cdg_gemm_wide_kernel (planes,
+    // or the raw rows of the direct class).
     CUtensorMap p16, p32, p128, tsf;
     st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &p128, &tsf);
     if (st != CDG_OK) return st;
@@ -453,27 +455,27 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = skip_ungrouped ? 0 : 1;
     if (launch_pdl(cdg_gemm_pair_kernel<16, 4>, grid, PairSmem<16, 4>::kThreads, PairSmem<16, 4>::kBytes, stream, tw,
-                   p16, tsf, tsf, ka) != cudaSuccess)
+                   p16, tsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     ka.do_zero_blocks = 0;
     ka.list = lists + kClassNarrow * nblk;
     ka.count_slot = kCtrlCount0 + kClassNarrow;
     if (launch_pdl(cdg_gemm_pair_kernel<32, 2>, grid, PairSmem<32, 2>::kThreads, PairSmem<32, 2>::kBytes, stream, tw,
-                   p32, tsf, tsf, ka) != cudaSuccess)
+                   p32, tsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
+    CUtensorMap ad, tok;
+    st = make_wide_tmaps(g, tok_sf, nblk, &ad, &tok);
+    if (st != CDG_OK) return st;
     ka.list = lists + kClassWide * nblk;
     ka.count_slot = kCtrlCount0 + kClassWide;
-    if (launch_pdl(cdg_gemm_pair_kernel<128, 1>, grid, PairSmem<128, 1>::kThreads, PairSmem<128, 1>::kBytes, stream,
-                   tw, p128, tsf, tsf, ka) != cudaSuccess)
+    if (launch_pdl(cdg_gemm_wide_kernel<false>, grid, WideSmem<false>::kThreads, WideSmem<false>::kBytes, stream, tw,
+                   p128, tsf, tok, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     // Wide blocks whose activation scales are all powers of two: raw e4m3 rows.
-    CUtensorMap ad, tok;
-    st = make_direct_tmaps(g, tok_sf, nblk, &ad, &tok);
-    if (st != CDG_OK) return st;
     ka.list = lists + kClassWideDirect * nblk;
     ka.count_slot = kCtrlCount0 + kClassWideDirect;
-    if (launch_pdl(cdg_gemm_pair_kernel<128, 1, true>, grid, PairSmem<128, 1, true>::kThreads,
-                   PairSmem<128, 1, true>::kBytes, stream, tw, ad, tsf, tok, ka) != cudaSuccess)
+    if (launch_pdl(cdg_gemm_wide_kernel<true>, grid, WideSmem<true>::kThreads, WideSmem<true>::kBytes, stream, tw,
+                   ad, tsf, tok, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
   } else {
     // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.

@@ -115,8 +115,9 @@ struct PrepArgs {
   int nblk;
   TileMap tm;              // rows of each block
   uint8_t* hilo;           // [2][nblk*128][K]
-  uint32_t* tok_sf;        // [nblk][K/128][128] words: activation scale atoms of direct blocks
-  int allow_direct;        // wide blocks with power-of-two scales may take the direct class
+  uint32_t* tok_sf;        // [nblk][K/128][128] words: token scale atoms of wide blocks (CTA-pair path)
+  int pair_wide;           // wide blocks run cdg_gemm_wide_kernel: write their token scale atoms, and
+                           // blocks whose scales are all powers of two take the direct class
   int32_t* row_exp;        // [nblk*128] exponent E of each routed row's activation planes
   int4* blk_info;          // [nblk] {expert (-1 none, -2 several), rows spanned, class, 0}
   uint4* blk_mask;         // [nblk] bit r set when row r of the block has the block's expert
@@ -169,7 +170,7 @@ constexpr int kPrepK = 1024;
 template <typename IdT>
 __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ int s_min_id, s_max_id, s_max_row;
-  __shared__ int s_last, s_nv, s_pow2;
+  __shared__ int s_last, s_nv, s_pow2, s_exp_bad;
   __shared__ uint8_t s_vrow[128];  // the block's rows that carry its expert (compacted)
   __shared__ int s_id[128];
   __shared__ uint32_t s_mask[4];
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     s_max_row = -1;
     s_nv = 0;
     s_pow2 = 1;
+    s_exp_bad = 0;
   }
   if (tid < 4) s_mask[tid] = 0u;
   int row0, nrows;
@@ -223,7 +225,6 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     const int kb_count = K / 128;
     const int kb0 = blockIdx.y * (kPrepK / 128);
     const int kbn = min(kPrepK / 128, kb_count - kb0);
-    const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
     if (tid < 128 && s_id[tid] == expert) {
       atomicOr(&s_mask[tid >> 5], 1u << (tid & 31));
       s_vrow[atomicAdd(&s_nv, 1)] = static_cast<uint8_t>(tid);
@@ -245,6 +246,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
         }
         if (smax > 0.0f) frexpf(smax, &emax);
         if (!pow2) atomicAnd(&s_pow2, 0);
+        // 2^E must be a UE8M0 scale factor (and a normal FP32 factor in the epilogue)
+        if (emax < -126 || emax > 127) atomicOr(&s_exp_bad, 1);
       }
       s_exp[tid] = emax;
       if (blockIdx.y == 0) p.row_exp[b * 128 + tid] = emax;
@@ -259,21 +262,39 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
           : 0.0f;
     }
     __syncthreads();
+  }
+  if (s_exp_bad) {
+    // a row exponent outside the scale-factor range: the exact SIMT kernel takes the block
+    cls = kClassIrregular;
+    expert = -2;
+  }
+  if (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide) {
+    const int K = p.K;
+    const int kb_count = K / 128;
+    const int kb0 = blockIdx.y * (kPrepK / 128);
+    const int kbn = min(kPrepK / 128, kb_count - kb0);
+    const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
+    // Token scale atoms of a wide block on the CTA-pair path: this CTA's K blocks' 512-byte
+    // UE8M0 atoms (row r's byte at (r%32)*16 + (r/32)*4 + c, the same byte for the four
+    // 32-wide sub-blocks c), carrying 2^E for the planes, or 2^s for the direct class.
     // Direct class: a wide block whose routed rows' scales are all powers of two.  The
     // reference's bf16(bf16(a) * bf16(2^s)) is then the exact product a * 2^s, which the
-    // tensor core forms itself from the raw e4m3 rows and the scale as a UE8M0 scale factor:
-    // no planes, one MMA per K slice.  Write this CTA's K blocks' 512-byte atoms (row r's
-    // byte at (r%32)*16 + (r/32)*4 + c, the same byte for the four 32-wide sub-blocks c).
-    if (cls == kClassWide && p.allow_direct && s_pow2) {
-      cls = kClassWideDirect;
+    // tensor core forms itself from the raw e4m3 rows with 2^s as scale factor: no planes,
+    // one MMA per K slice.
+    const bool direct = cls == kClassWide && p.pair_wide && s_pow2;
+    if (cls == kClassWide && p.pair_wide) {
       for (int it = tid; it < kbn * 128; it += blockDim.x) {
         const int kl = it >> 7, rr = it & 127;
-        const int code =
-            s_id[rr] == expert ? pow2_code(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb0 + kl))
-                               : 127;
+        int code = 127;
+        if (s_id[rr] == expert)
+          code = direct ? pow2_code(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb0 + kl))
+                        : 127 + s_exp[rr];
         p.tok_sf[(static_cast<int64_t>(b) * kb_count + kb0 + kl) * 128 + (rr & 31) * 4 + (rr >> 5)] =
             static_cast<uint32_t>(code) * 0x01010101u;
       }
+    }
+    if (direct) {
+      cls = kClassWideDirect;
     } else {
     // (2) activation planes of the rows that carry the block's expert, one 16-byte chunk
     //     per item; consecutive threads read consecutive chunks of a row (coalesced).

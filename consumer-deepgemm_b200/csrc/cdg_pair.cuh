@@ -12,24 +12,20 @@
 // round-robin to NI issuing warps (K step i of the CTA's sequence to issuer i % NI,
 // which with a stage ring of a multiple of NI stages means each issuer owns fixed
 // stages), each accumulating into its own TMEM partial sum (a fixed assignment, so
-// results are deterministic); the epilogue adds the partials.  Wide tiles (N = 128
-// per MMA) are math-bound and use one issuer.
+// results are deterministic); the epilogue adds the partials.
 //
 // Operands per pipeline stage (K step of 128), in each CTA's own shared memory:
 //   * its weight tile [128 n x 128 k] (TMA, packed E2M1 unpacked to bytes, SW128);
-//   * its half of the MMA's B operand (N rows split between the CTAs):
-//       TOK <= 32 ("stacked"): CTA 0 holds the hi plane's TOK token rows and CTA 1 the
-//       lo plane's, one MMA per K slice with N = 2*TOK; TMEM columns [0, TOK) then hold
-//       the hi part and [TOK, 2*TOK) the lo part of each token;
-//       TOK = 128 ("wide"): each CTA holds h = ntok/2 (rounded up to 16) tokens of both
-//       planes (CTA 1 the tokens from h on), two MMAs per K slice (hi plane, lo plane)
-//       with N = 2h into the same accumulator, so TMEM column c is token c;
+//   * its half of the MMA's B operand (N rows split between the CTAs): CTA 0 holds the hi
+//     plane's TOK token rows and CTA 1 the lo plane's, one MMA per K slice with N = 2*TOK;
+//     TMEM columns [0, TOK) then hold the hi part and [TOK, 2*TOK) the lo part of each token;
 //   * its weights' 512-byte scale atom (TMA, 2-D view of the atom array).
 // Every copy of both CTAs completes on the even CTA's `full` barrier (cta_group::2
 // form of the TMA load, no multicast); the MMA commits arrive on the `empty` and
 // `tfull` barriers of both CTAs (tcgen05.commit multicast); each epilogue thread of
 // both CTAs drains its own TMEM lanes (its CTA's 128 output columns) and arrives on
-// the even CTA's `tempty` barrier.  All waits are bounded (kStatusTimeout).
+// the even CTA's `tempty` barrier.  All waits are bounded (kStatusTimeout).  Wide
+// blocks (more than 32 rows) run cdg_gemm_wide_kernel instead.
 //
 // Warp roles per CTA: 0 = TMA producer, 1..NI = MMA issuers (even CTA; warp 1 also
 // owns TMEM), then four epilogue warps (4-7, or 5-8 when NI = 4).
@@ -39,24 +35,20 @@
 
 namespace cdg {
 
-template <int TOK, int NI, bool DIRECT = false>
+template <int TOK, int NI>
 struct PairSmem {
-  static constexpr bool kWide = TOK > 32;
-  static_assert(!DIRECT || kWide, "the direct (single-plane) variant serves wide blocks");
-  static constexpr int kRowsA = kWide ? 64 : TOK;  // activation rows per plane held by one CTA
-  static constexpr int kPlanes = kWide && !DIRECT ? 2 : 1;  // planes held by one CTA
+  static_assert(TOK == 16 || TOK == 32, "tiny and narrow blocks");
   // A multiple of NI: stage s is always consumed by issuer s % NI, in order, so an
   // issuer never waits on a stage use whose predecessor it did not consume itself.
-  static constexpr int kStages = DIRECT ? 8 : kWide ? 6 : NI == 4 ? 12 : 10;
+  static constexpr int kStages = NI == 4 ? 12 : 10;
   static_assert(kStages % NI == 0, "stage ring must split evenly over the issuers");
   static constexpr int kW = 128 * 128;             // weight tile, bytes per stage
-  static constexpr int kA = kRowsA * 128;          // one plane's rows, bytes per stage
-  static constexpr int kStageBytes = kW + kPlanes * kA;  // operand tiles (1024-byte multiple)
+  static constexpr int kA = TOK * 128;             // one plane's rows, bytes per stage
+  static constexpr int kStageBytes = kW + kA;      // operand tiles (1024-byte multiple)
   static constexpr int kSfRing = kStages * kStageBytes;  // then one 512-byte weight scale atom per stage
-  static constexpr int kTsfRing = kSfRing + kStages * 512;  // direct: one activation scale atom per stage
-  static constexpr int kOneAtom = kTsfRing + (DIRECT ? kStages * 512 : 0);  // constant activation scale atom
-  // narrow and wide tiles: per epilogue warp a [16 rows x 32 columns] BF16 staging tile, so
-  // that D leaves as 16-byte row segments instead of 2-byte column elements
+  static constexpr int kOneAtom = kSfRing + kStages * 512;  // constant activation scale atom
+  // narrow tiles: per epilogue warp a [16 rows x 32 columns] BF16 staging tile, so that D
+  // leaves as 16-byte row segments instead of 2-byte column elements
   static constexpr bool kStagedStores = TOK > 16;
   static constexpr int kStaging = kOneAtom + 512;
   static constexpr int kStagingBytes = kStagedStores ? 4 * 16 * 32 * 2 : 0;
@@ -65,35 +57,26 @@ struct PairSmem {
   static constexpr int kBytes = kBarOffset + kBarBytes + 1024;          // + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
   // bytes one CTA's copies of one stage add to the even CTA's `full` barrier
-  static constexpr uint32_t kTxPerCta = 128u * 64u + kPlanes * kA + 512u + (DIRECT ? 512u : 0u);
+  static constexpr uint32_t kTxPerCta = 128u * 64u + kA + 512u;
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned for SW128 tiles");
   // TMEM: per accumulator buffer NI partials of kPartCols columns; two buffers; then
   // per issuer two 4-column weight scale sets; then per issuer the constant activation
-  // scale set (each issuer copies its own, so no issuer reads another's TMEM writes);
-  // direct: two 4-column activation scale sets.
-  static constexpr uint32_t kPartCols = kWide ? 128 : 2 * TOK;
+  // scale set (each issuer copies its own, so no issuer reads another's TMEM writes).
+  static constexpr uint32_t kPartCols = 2 * TOK;
   static constexpr uint32_t kAccCols = NI * kPartCols;
   static constexpr uint32_t kSfwCol = 2 * kAccCols;
   static constexpr uint32_t kSfaCol = kSfwCol + 8 * NI;
-  static constexpr uint32_t kTsfCol = kSfaCol + 4 * NI;
-  static_assert(kTsfCol + 8 <= 512, "TMEM columns");
-  static_assert(!kWide || NI == 1, "wide tiles are math-bound: one issuer");
+  static_assert(kSfaCol + 4 * NI <= 512, "TMEM columns");
   static constexpr int kEpiWarp0 = NI < 4 ? 4 : NI + 1;
   static constexpr int kThreads = (kEpiWarp0 + 4) * 32;
 };
 
-// DIRECT (wide blocks whose activation scales are powers of two): tmap_a covers A itself
-// ([M rows][K] e4m3), each CTA loads half of the block's rows; tmap_tsf covers the block's
-// activation scale atoms written by the prep kernel; one MMA per K slice with those atoms as
-// the B scale factors; no exponent in the epilogue.
-template <int TOK, int NI, bool DIRECT = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DIRECT>::kThreads, 1)
+template <int TOK, int NI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::kThreads, 1)
     cdg_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
-                         const __grid_constant__ CUtensorMap tmap_sf, const __grid_constant__ CUtensorMap tmap_tsf,
-                         GemmArgs p) {
-  using L = PairSmem<TOK, NI, DIRECT>;
+                         const __grid_constant__ CUtensorMap tmap_sf, GemmArgs p) {
+  using L = PairSmem<TOK, NI>;
   constexpr int S = L::kStages;
-  constexpr bool kWide = L::kWide;
   constexpr uint32_t kTmemCols = 512;
 
   grid_dependency_wait();  // the block plan comes from the previous kernel of the stream
@@ -115,7 +98,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
   auto stage_w = [&](int s) { return smem + s * L::kStageBytes; };
   auto stage_a = [&](int s) { return smem + s * L::kStageBytes + L::kW; };
   auto stage_sf = [&](int s) { return smem + L::kSfRing + s * 512; };
-  auto stage_tsf = [&](int s) { return smem + L::kTsfRing + s * 512; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* full = bars;       // [S] (even CTA's count both CTAs' copies)
   uint64_t* empty = bars + S;  // [S] stage consumed (multicast by the MMA commit)
@@ -131,7 +113,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_sf);
-    if (DIRECT) prefetch_tmap(&tmap_tsf);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -159,10 +140,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
   const uint32_t tmem_base = *tmem_holder;
   bool ok = true;
 
-  // Tokens per CTA of a wide block spanning `rows` rows: half, rounded up to 16 (N = 2h, a
-  // multiple of 32).
-  auto wide_half = [](int rows) { return (((rows + 1) >> 1) + 15) & ~15; };
-
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
@@ -179,12 +156,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
         const int expert = cur.y;
         const int wrow = expert * p.N + nt * 128;
         const int atom0 = (expert * n_tiles + nt) * k_steps;
-        int a_row = kWide ? blk * 128 + static_cast<int>(rank) * wide_half(cur.z) : blk * 128;
-        if (DIRECT) {  // rows of A itself
-          int row0, nrows;
-          p.tm.rows(blk, row0, nrows);
-          a_row = row0 + static_cast<int>(rank) * wide_half(cur.z);
-        }
+        const int a_row = blk * 128;
         for (int kb = 0; kb < k_steps; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, p.status,
                                  wait_code(1, static_cast<int>(rank), stage, phase ^ 1, kb))) {
@@ -194,14 +166,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
           const uint32_t fb = full0 + stage * 8;
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * L::kTxPerCta);
           tma_load_2d_pair(stage_w(stage), &tmap_w, fb, kb * 128, wrow);
-          if (DIRECT) {
-            tma_load_2d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row);
-            tma_load_2d_pair(stage_tsf(stage), &tmap_tsf, fb, 0, blk * k_steps + kb);
-          } else if (kWide) {
-            tma_load_3d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row, 0);
-          } else {
-            tma_load_3d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row, static_cast<int>(rank));
-          }
+          tma_load_3d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row, static_cast<int>(rank));
           tma_load_2d_pair(stage_sf(stage), &tmap_sf, fb, 0, atom0 + kb);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -218,11 +183,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
       const uint32_t sfa_t = tmem_base + L::kSfaCol + 4 * j;
       tc_cp_sf_atom_pair(sfa_t, smem_desc_sf(smem_u32(smem + L::kOneAtom)));
       int n_own = 0;  // K steps this issuer has taken (weight scale set parity)
-      int4 next = pair < reg_tiles ? __ldg(&p.list[pair / n_pt]) : make_int4(0, 0, 0, 0);
       for (int t = pair; t < reg_tiles && ok; t += npairs, ++local, seq += k_steps) {
-        const int4 cur = next;
-        if (t + npairs < reg_tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
-        const uint32_t n_mma = kWide ? 2u * static_cast<uint32_t>(wide_half(cur.z)) : 2u * TOK;
+        constexpr uint32_t n_mma = 2u * TOK;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.status, wait_code(2, j, acc, acc_phase ^ 1, local))) {
@@ -243,8 +205,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
           tc_fence_after();
           const uint32_t sfw_t = tmem_base + L::kSfwCol + j * 8 + (n_own & 1) * 4;
           tc_cp_sf_atom_pair(sfw_t, smem_desc_sf(smem_u32(stage_sf(stage))));
-          const uint32_t sfb_t = DIRECT ? tmem_base + L::kTsfCol + (n_own & 1) * 4 : sfa_t;
-          if (DIRECT) tc_cp_sf_atom_pair(sfb_t, smem_desc_sf(smem_u32(stage_tsf(stage))));
           const uint32_t w_addr = smem_u32(stage_w(stage));
           const uint32_t a_addr = smem_u32(stage_a(stage));
 #pragma unroll
@@ -252,9 +212,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
             const uint64_t wd = smem_desc_sw128(w_addr + k * 32);
             const uint32_t idesc = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 256, n_mma, k, k);
             const uint32_t accumulate = (kb != kb0 || k != 0) ? 1u : 0u;
-            tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + k * 32), idesc, accumulate, sfw_t, sfb_t);
-            if (kWide && !DIRECT)
-              tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + L::kA + k * 32), idesc, 1u, sfw_t, sfa_t);
+            tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + k * 32), idesc, accumulate, sfw_t, sfa_t);
           }
           tc_commit_pair(&empty[stage], 0x3);
         }
@@ -293,9 +251,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
         float row_sc[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          row_sc[k] = DIRECT ? 1.0f  // direct: the scale factors already carry the scales
-                             : __uint_as_float(static_cast<uint32_t>(
-                                   min(max(__ldg(p.row_exp + blk * 128 + k * 32 + lane) + 127, 1), 254)) << 23);
+          row_sc[k] = __uint_as_float(
+              static_cast<uint32_t>(min(max(__ldg(p.row_exp + blk * 128 + k * 32 + lane) + 127, 1), 254)) << 23);
         if (!mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
                                wait_code(4, static_cast<int>(rank), acc, acc_phase, local - 1))) {
           ok = false;
@@ -309,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
           const float my_scale = kq == 0 ? row_sc[0] : kq == 1 ? row_sc[1] : kq == 2 ? row_sc[2] : row_sc[3];
           uint32_t v[16];
           tmem_ld16(taddr + first * L::kPartCols + j0, v);
-          if (!kWide) {
+          {
             uint32_t w[16];
             tmem_ld16(taddr + first * L::kPartCols + TOK + j0, w);  // lo-plane columns of the same tokens
             tmem_ld_wait();
@@ -325,8 +282,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI, DI
               for (int j = 0; j < 16; ++j)
                 v[j] = __float_as_uint(__uint_as_float(v[j]) + (__uint_as_float(h[j]) + __uint_as_float(w[j])));
             }
-          } else {
-            tmem_ld_wait();
           }
           if (L::kStagedStores) {
             // this warp's 32 columns x 16 rows through shared memory: each lane then stores two

@@ -323,6 +323,24 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 lanes x 16 columns from TMEM lane `taddr.lane`, column `taddr.col` (shape 16x256b, x2).
+// Thread t receives, for lane l = t/4 and column c = 2*(t%4):
+//   r0, r1 = (l, c), (l, c+1);  r2, r3 = (l+8, c), (l+8, c+1);  r4..r7 = the same at c+8.
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+// Four 8x8 b16 matrices, stored transposed: register k of thread t holds row t/4, columns
+// 2*(t%4) and +1 (low half first) of matrix k; row i of the stored transpose of matrix k
+// (16 bytes) goes to the address given by thread 8*k + i.
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t m0, uint32_t m1, uint32_t m2, uint32_t m3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(m0), "r"(m1),
+               "r"(m2), "r"(m3)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 format, version 1): K-major operand
 // tile whose rows are 128 bytes, stored with the 128-byte swizzle; 8-row core

@@ -215,6 +215,35 @@ def test_direct_class_is_per_block():
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (nw, rl2)
 
 
+def test_exponent_outside_scale_factor_range_goes_to_simt():
+    """A wide block whose row exponent 2^E is below UE8M0's range (denormal FP32 scales) is
+    planned for the exact SIMT kernel; its rows match a forced-SIMT run bit for bit, and the
+    other blocks still match the oracle."""
+    c = load_gemm_case("c0")
+    sa = c["sa"].float().clone()
+    ids = c["m_indices"]
+    blk = 3  # a block of one expert with more than 32 routed rows
+    rows = torch.arange(blk * 128, blk * 128 + 128)
+    assert int((ids[rows] >= 0).sum()) > 32
+    sa[rows] *= 2.0 ** -124  # BF16 denormal scales: E near -130
+    a, b, sb = c["a"].to(DEV), c["b"].to(DEV), c["sb"].to(DEV)
+    d = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    ws = cabi.gemm(a, sa.to(DEV), b, sb, d, ids.to(DEV))
+    torch.cuda.synchronize()
+    assert cabi.block_classes(ws)["irregular"] >= 1
+    d_simt = torch.full(c["d"].shape, float("nan"), dtype=c["d_dtype"], device=DEV)
+    cabi.gemm(a, sa.to(DEV), b, sb, d_simt, ids.to(DEV), flags=cabi.FLAG_FORCE_GENERIC)
+    torch.cuda.synchronize()
+    out, out_simt = d.cpu(), d_simt.cpu()
+    assert torch.equal(out[rows].view(torch.int16), out_simt[rows].view(torch.int16))
+    ref = torch.empty(c["d"].shape, dtype=c["d_dtype"])
+    oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((c["a"], sa), (c["b"], c["sb"]), ref, ids)
+    keep = ~_invalid_rows(c)
+    keep[rows] = False
+    nw, rl2 = errors(out, ref, keep)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (nw, rl2)
+
+
 def test_packed_scales_public_api():
     import consumer_deep_gemm as cdg
 
