@@ -199,7 +199,8 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 // Code naming a wait for mbar_wait_cluster: role (1 producer/empty, 2 issuer/tempty,
-// 3 issuer/full, 4 epilogue/tfull, 5 issuer/done), CTA rank or issuer, stage, phase, step.
+// 3 issuer/full (or sfready), 4 epilogue/tfull, 5 issuer/done, 6 scale copier/full), CTA
+// rank or issuer, stage, phase, step.
 __device__ __forceinline__ int wait_code(int role, int who, int stage, uint32_t phase, int step) {
   return (role << 28) | ((who & 15) << 24) | ((stage & 255) << 16) | (static_cast<int>(phase & 1u) << 15) |
          (step & 0x7fff);

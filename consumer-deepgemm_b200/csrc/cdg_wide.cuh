@@ -20,7 +20,12 @@
 //
 // Pipeline: a stage holds kKS = 2 K steps (weights, tokens, weight and token scale
 // atoms of each), so the MMA issuer waits on one barrier per two K steps: a wait costs
-// the single issuing thread about as long as the four MMAs of one K step.
+// the single issuing thread about as long as the four MMAs of one K step.  The scale
+// atoms reach TMEM through a second thread (tcgen05.cp into the stage's own TMEM scale
+// columns, then a commit to the stage's `sfready` barrier), so the MMA thread issues
+// nothing but MMAs and commits.  A stage's scale columns are free again when its data
+// lands the next time: the producer refills a stage only after the MMAs that read it
+// completed.
 //
 // Epilogue (four warps per CTA, warp q owns TMEM lanes 32q..32q+31 = output columns):
 // tcgen05.ld 16x256b hands each thread two adjacent tokens of one column; packed to
@@ -30,7 +35,8 @@
 // (rows past the block's end skipped, rows without the block's expert written as zeros).
 //
 // Warp roles per CTA: 0 = TMA producer, 1 = MMA issuer (even CTA) and TMEM owner,
-// 2-3 idle, 4-7 = epilogue.  All waits are bounded (kStatusTimeout).
+// 2 = scale-factor copier (even CTA), 3 idle, 4-7 = epilogue.  All waits are bounded
+// (kStatusTimeout).
 #pragma once
 
 #include "cdg_kernels.cuh"
@@ -50,16 +56,17 @@ struct WideSmem {
   static constexpr int kTsfRing = kSfRing + kStages * kKS * 512;   // [stage][kKS] token scale atoms
   static constexpr int kStaging = kTsfRing + kStages * kKS * 512;  // 4 warps x [16 tokens][32 columns] bf16
   static constexpr int kBarOffset = kStaging + 4 * 1024;
-  static constexpr int kBarBytes = (2 * kStages + 5) * 8 + 16;  // full, empty, tfull[2], tempty[2], done; TMEM
+  static constexpr int kBarBytes = (3 * kStages + 5) * 8 + 16;  // full, empty, sfready, tfull[2], tempty[2], done; TMEM
   static constexpr int kBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
   static_assert(kStep % 1024 == 0, "K steps must stay 1024-byte aligned for SW128 tiles");
   // bytes one CTA's copies of one K step add to the even CTA's `full` barrier
   static constexpr uint32_t kTxPerStep = 128u * 64u + kPlanes * kA + 512u + 512u;
-  // TMEM: two 128-column accumulators, then [parity][kKS] 4-column weight scale sets and
-  // [parity][kKS] 4-column token scale sets
+  // TMEM: two 128-column accumulators, then [stage][kKS] 4-column weight scale sets and
+  // [stage][kKS] 4-column token scale sets
   static constexpr uint32_t kSfwCol = 256;
-  static constexpr uint32_t kTsfCol = kSfwCol + 2 * kKS * 4;
+  static constexpr uint32_t kTsfCol = kSfwCol + kStages * kKS * 4;
+  static_assert(kTsfCol + kStages * kKS * 4 <= 512, "TMEM columns");
   static constexpr int kThreads = 256;
 };
 
@@ -94,7 +101,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* full = bars;           // [S] even CTA: both CTAs' copies of a stage landed
   uint64_t* empty = bars + S;      // [S] stage consumed (multicast by the MMA commit)
-  uint64_t* tfull = bars + 2 * S;  // [2] accumulator complete
+  uint64_t* sfready = bars + 2 * S;  // [S] even CTA: the stage's scale atoms are in TMEM
+  uint64_t* tfull = bars + 3 * S;  // [2] accumulator complete
   uint64_t* tempty = tfull + 2;    // [2] even CTA: all 256 epilogue threads of the pair drained it
   uint64_t* done = tempty + 2;     // even CTA: every MMA completed
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done + 1);
@@ -110,6 +118,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&sfready[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
@@ -183,7 +192,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t par = 0;  // scale set parity, flips every stage
       int local = 0;
       int4 next = pair < tiles ? __ldg(&p.list[pair / n_pt]) : make_int4(0, 0, 0, 0);
       for (int t = pair; t < tiles && ok; t += npairs, ++local) {
@@ -199,17 +207,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * 128;
         for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
-          if (!mbar_wait_cluster(&full[stage], phase, p.status, wait_code(3, 0, stage, phase, kb0))) {
+          if (!mbar_wait_cluster(&sfready[stage], phase, p.status, wait_code(3, 0, stage, phase, kb0))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const int n = k_steps - kb0 < KS ? k_steps - kb0 : KS;
           for (int u = 0; u < n; ++u) {
-            const uint32_t sfw_t = tmem_base + L::kSfwCol + (par * KS + u) * 4;
-            const uint32_t tsf_t = tmem_base + L::kTsfCol + (par * KS + u) * 4;
-            tc_cp_sf_atom_pair(sfw_t, smem_desc_sf(smem_u32(step_sfw(stage, u))));
-            tc_cp_sf_atom_pair(tsf_t, smem_desc_sf(smem_u32(step_tsf(stage, u))));
+            const uint32_t sfw_t = tmem_base + L::kSfwCol + (stage * KS + u) * 4;
+            const uint32_t tsf_t = tmem_base + L::kTsfCol + (stage * KS + u) * 4;
             const uint32_t w_addr = smem_u32(step_w(stage, u));
             const uint32_t a_addr = smem_u32(step_a(stage, u));
 #pragma unroll
@@ -224,7 +230,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           }
           tc_commit_pair(&empty[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1; }
-          par ^= 1u;
         }
         if (!ok) break;
         tc_commit_pair(&tfull[acc], 0x3);
@@ -232,6 +237,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       // Every MMA (and its TMEM writes in both CTAs) completes before teardown.
       tc_commit_pair(done, 0x1);
       mbar_wait_cluster(done, 0, p.status, wait_code(5, 0, 0, 0, 0));
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ scale-factor copier (even CTA)
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
+          if (!mbar_wait_cluster(&full[stage], phase, p.status, wait_code(6, 0, stage, phase, kb0))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int n = k_steps - kb0 < KS ? k_steps - kb0 : KS;
+          for (int u = 0; u < n; ++u) {
+            tc_cp_sf_atom_pair(tmem_base + L::kSfwCol + (stage * KS + u) * 4,
+                               smem_desc_sf(smem_u32(step_sfw(stage, u))));
+            tc_cp_sf_atom_pair(tmem_base + L::kTsfCol + (stage * KS + u) * 4,
+                               smem_desc_sf(smem_u32(step_tsf(stage, u))));
+          }
+          tc_commit_pair(&sfready[stage], 0x1);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue (both CTAs)
