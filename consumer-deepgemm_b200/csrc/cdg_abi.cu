@@ -18,6 +18,7 @@
 #include "cdg_b200.h"
 #include "cdg_kernels.cuh"
 #include "cdg_pair.cuh"
+#include "cdg_planes.cuh"
 #include "cdg_wide.cuh"
 #include "cdg_layout.h"
 
@@ -71,8 +72,8 @@ const DeviceInfo& device_info(int dev) {
       if (cudaFuncSetAttribute(cdg_gemm_pair_kernel<32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                PairSmem<32, 2>::kBytes) != cudaSuccess)
         return;
-      if (cudaFuncSetAttribute(cdg_gemm_wide_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               WideSmem<false>::kBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(cdg_gemm_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               PlanesSmem::kBytes) != cudaSuccess)
         return;
       if (cudaFuncSetAttribute(cdg_gemm_wide_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                WideSmem<true>::kBytes) != cudaSuccess)
@@ -221,16 +222,14 @@ int make_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap*
   return st;
 }
 
-// Tensor maps of the CTA-pair kernels: one plane of TOK rows per CTA (tiny, narrow),
-// 64 rows of both planes per CTA (wide), and the weight scale atoms as a 2-D array
-// [atoms][128 words] read one 512-byte atom per box.
+// Tensor maps of the CTA-pair kernels: one plane of TOK rows per CTA (tiny, narrow), and
+// the weight scale atoms as a 2-D array [atoms][128 words] read one 512-byte atom per box.
 int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const uint32_t* sfw, CUtensorMap* p16,
-                    CUtensorMap* p32, CUtensorMap* p128, CUtensorMap* tsf) {
+                    CUtensorMap* p32, CUtensorMap* tsf) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return CDG_ERR_CUDA;
   int st = make_plane_tmap(enc, g, hilo, nblk, 16, p16, 1);
   if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 32, p32, 1);
-  if (st == CDG_OK) st = make_plane_tmap(enc, g, hilo, nblk, 64, p128, 2);
   if (st != CDG_OK) return st;
   const int64_t atoms = g->E * (g->N / 128) * (g->K / 128);
   cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(atoms)};
@@ -239,6 +238,25 @@ int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const u
   cuuint32_t estr[2] = {1, 1};
   return enc(tsf, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(sfw), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? CDG_OK
+             : CDG_ERR_CUDA;
+}
+
+// Tensor map of cdg_gemm_planes_kernel: a 4-D view (K, token % 8, plane, token / 8) of the
+// stacked planes [2][nblk*128][K], so that one box of the 7 token groups of a CTA's half
+// tile lands in shared memory as [group][plane][8 rows] -- 8 hi rows, then the same
+// tokens' 8 lo rows, per group.
+int make_planes_tmap(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap* ta) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return CDG_ERR_CUDA;
+  const cuuint64_t K = static_cast<cuuint64_t>(g->K);
+  cuuint64_t dims[4] = {K, 8, 2, static_cast<cuuint64_t>(nblk * 16)};
+  cuuint64_t strides[3] = {K, static_cast<cuuint64_t>(nblk * 128) * K, 8 * K};
+  cuuint32_t box[4] = {128, 8, 2, kPlanesTileTok / 16};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, hilo, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
              ? CDG_OK
              : CDG_ERR_CUDA;
@@ -408,6 +426,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.blk_mask = blk_mask;
   pa.ctrl = ctrl;
   pa.lists = lists;
+  pa.plane_tiles = reinterpret_cast<int4*>(ws + wl.plane_tiles);
   const bool pair_path = g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2;
   uint32_t* tok_sf = reinterpret_cast<uint32_t*>(ws + wl.tok_sf);
   pa.tok_sf = tok_sf;
@@ -447,8 +466,8 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     // CTA pairs (tcgen05 cta_group::2): two adjacent 128-column tiles per cluster; four MMA
     // issuers for tiny blocks, two for narrow; wide blocks in cdg_gemm_wide_kernel (planes,
     // or the raw rows of the direct class).
-    CUtensorMap p16, p32, p128, tsf;
-    st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &p128, &tsf);
+    CUtensorMap p16, p32, tsf;
+    st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &tsf);
     if (st != CDG_OK) return st;
     const unsigned grid = static_cast<unsigned>(di.sm_count / 2 * 2);
     ka.list = lists + kClassTiny * nblk;
@@ -466,10 +485,13 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     CUtensorMap ad, tok;
     st = make_wide_tmaps(g, tok_sf, nblk, &ad, &tok);
     if (st != CDG_OK) return st;
-    ka.list = lists + kClassWide * nblk;
-    ka.count_slot = kCtrlCount0 + kClassWide;
-    if (launch_pdl(cdg_gemm_wide_kernel<false>, grid, WideSmem<false>::kThreads, WideSmem<false>::kBytes, stream, tw,
-                   p128, tsf, tok, ka) != cudaSuccess)
+    CUtensorMap planes;
+    st = make_planes_tmap(g, hilo, nblk, &planes);
+    if (st != CDG_OK) return st;
+    ka.list = reinterpret_cast<const int4*>(ws + wl.plane_tiles);
+    ka.count_slot = kCtrlPlaneTiles;
+    if (launch_pdl(cdg_gemm_planes_kernel, grid, PlanesSmem::kThreads, PlanesSmem::kBytes, stream, tw, planes, tsf,
+                   ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     // Wide blocks whose activation scales are all powers of two: raw e4m3 rows.
     ka.list = lists + kClassWideDirect * nblk;

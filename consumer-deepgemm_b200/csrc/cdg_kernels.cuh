@@ -123,6 +123,8 @@ struct PrepArgs {
   uint4* blk_mask;         // [nblk] bit r set when row r of the block has the block's expert
   int* ctrl;               // control words (zeroed by the host before launch)
   int4* lists;             // [kNumClasses][nblk] {block, expert, rows spanned, 0}
+  int4* plane_tiles;       // [2*nblk] tiles of cdg_gemm_planes_kernel (pair_wide only):
+                           // {first plane row, rows, expert, 1 on the last tile of a run}
 };
 
 // 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
@@ -177,6 +179,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ float s_scale[128][kPrepK / 128];
   __shared__ int s_exp[128];
   __shared__ int s_cls_count[kNumClasses][257];
+  __shared__ int s_tile_count[257];
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   if (tid == 0) {
@@ -217,6 +220,13 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   } else {
     cls = eff <= kTinyTok ? kClassTiny : eff <= kNarrowTok ? kClassNarrow : kClassWide;
     expert = s_min_id;
+    // The last block of an expert that spans several blocks joins its wide blocks on the
+    // CTA-pair path: the wide kernels trim the MMA to the block's rows, and they read the
+    // expert's weights from L2 right after its other blocks did, where the tiny and narrow
+    // kernels would stream them from HBM again.
+    if (cls != kClassWide && p.pair_wide && row0 > 0 &&
+        load_id(p.ids, sizeof(IdT) == 8, row0 - 1) == static_cast<int64_t>(expert))
+      cls = kClassWide;
   }
 
   if (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide) {
@@ -274,21 +284,19 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     const int kb0 = blockIdx.y * (kPrepK / 128);
     const int kbn = min(kPrepK / 128, kb_count - kb0);
     const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
-    // Token scale atoms of a wide block on the CTA-pair path: this CTA's K blocks' 512-byte
-    // UE8M0 atoms (row r's byte at (r%32)*16 + (r/32)*4 + c, the same byte for the four
-    // 32-wide sub-blocks c), carrying 2^E for the planes, or 2^s for the direct class.
-    // Direct class: a wide block whose routed rows' scales are all powers of two.  The
+    // Direct class: a wide block (CTA-pair path) whose routed rows' scales are all powers
+    // of two.  Its token scale atoms: this CTA's K blocks' 512-byte UE8M0 atoms (row r's
+    // byte at (r%32)*16 + (r/32)*4 + c, the same byte 2^s for the four 32-wide sub-blocks c).  The
     // reference's bf16(bf16(a) * bf16(2^s)) is then the exact product a * 2^s, which the
     // tensor core forms itself from the raw e4m3 rows with 2^s as scale factor: no planes,
     // one MMA per K slice.
     const bool direct = cls == kClassWide && p.pair_wide && s_pow2;
-    if (cls == kClassWide && p.pair_wide) {
+    if (direct) {
       for (int it = tid; it < kbn * 128; it += blockDim.x) {
         const int kl = it >> 7, rr = it & 127;
         int code = 127;
         if (s_id[rr] == expert)
-          code = direct ? pow2_code(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb0 + kl))
-                        : 127 + s_exp[rr];
+          code = pow2_code(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb0 + kl));
         p.tok_sf[(static_cast<int64_t>(b) * kb_count + kb0 + kl) * 128 + (rr & 31) * 4 + (rr >> 5)] =
             static_cast<uint32_t>(code) * 0x01010101u;
       }
@@ -348,32 +356,71 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __threadfence();
   const int per = (p.nblk + blockDim.x - 1) / blockDim.x;
   const int lo = min(p.nblk, tid * per), hi = min(p.nblk, lo + per);
+  // Tiles of the planes kernel: a run is a maximal sequence of wide blocks of one expert
+  // whose rows follow each other, every block but the last full (128 routed rows spanned).
+  // A run of S rows is cut into the fewest tiles, n = ceil(S / kPlanesTileTok), of
+  // T = ceil16(S / n) rows each (the last one shorter): a tile costs the kernel about the
+  // same time at any width, so fewer tiles is faster, and equal widths spread the MMA work.
+  auto continues = [&](int i) -> bool {  // block i extends the run of block i - 1
+    if (i == 0) return false;
+    const int4 a = __ldcg(&p.blk_info[i - 1]), c = __ldcg(&p.blk_info[i]);
+    if (a.z != kClassWide || c.z != kClassWide || a.x != c.x || a.y != 128) return false;
+    int r0a, na, r0c, nc;
+    p.tm.rows(i - 1, r0a, na);
+    p.tm.rows(i, r0c, nc);
+    return na == 128 && r0c == r0a + 128;
+  };
+  auto run_span = [&](int i) -> int {  // rows spanned by the run that starts at block i
+    int j = i;
+    while (j + 1 < p.nblk && continues(j + 1)) ++j;
+    return 128 * (j - i) + __ldcg(&p.blk_info[j].y);
+  };
+  static_assert(kPlanesTileTok % 16 == 0, "tile cuts at multiples of 16 rows");
   int cnt[kNumClasses] = {};
-  for (int i = lo; i < hi; ++i) cnt[__ldcg(&p.blk_info[i].z)]++;
+  int ntiles = 0;
+  for (int i = lo; i < hi; ++i) {
+    const int c = __ldcg(&p.blk_info[i].z);
+    cnt[c]++;
+    if (p.pair_wide && c == kClassWide && !continues(i)) ntiles += (run_span(i) + kPlanesTileTok - 1) / kPlanesTileTok;
+  }
 #pragma unroll
   for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][tid + 1] = cnt[c];
+  s_tile_count[tid + 1] = ntiles;
   if (tid == 0) {
 #pragma unroll
     for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][0] = 0;
+    s_tile_count[0] = 0;
   }
   __syncthreads();
-  if (tid < kNumClasses) {
+  if (tid <= kNumClasses) {  // thread kNumClasses scans the tile counts
+    int* cs = tid < kNumClasses ? s_cls_count[tid] : s_tile_count;
     int run = 0;
     for (int t = 0; t <= static_cast<int>(blockDim.x); ++t) {
-      const int v = s_cls_count[tid][t];
-      s_cls_count[tid][t] = run;
+      const int v = cs[t];
+      cs[t] = run;
       run += v;
     }
-    p.ctrl[kCtrlCount0 + tid] = run;
+    p.ctrl[tid < kNumClasses ? kCtrlCount0 + tid : kCtrlPlaneTiles] = run;
   }
   __syncthreads();
   int pos[kNumClasses];
 #pragma unroll
   for (int c = 0; c < kNumClasses; ++c) pos[c] = s_cls_count[c][tid + 1];
+  int tpos = s_tile_count[tid + 1];
   for (int i = lo; i < hi; ++i) {
     const int c = __ldcg(&p.blk_info[i].z);
     const int4 info = __ldcg(&p.blk_info[i]);
     p.lists[c * p.nblk + pos[c]++] = make_int4(i, info.x, info.y, 0);
+    if (p.pair_wide && c == kClassWide && !continues(i)) {
+      const int span = run_span(i);
+      const int n = (span + kPlanesTileTok - 1) / kPlanesTileTok;
+      const int tile = ((span + n - 1) / n + 15) & ~15;
+      for (int k = 0; k < n; ++k) {
+        const int o = k * tile;
+        const int e = k + 1 == n ? span : o + tile;
+        p.plane_tiles[tpos++] = make_int4(i * 128 + o, e - o, info.x, k + 1 == n ? 1 : 0);
+      }
+    }
   }
 }
 

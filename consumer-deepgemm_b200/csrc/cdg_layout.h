@@ -21,11 +21,15 @@ enum : int {
 };
 constexpr int kTinyTok = 16;
 constexpr int kNarrowTok = 32;
+// Tokens per tile of cdg_gemm_planes_kernel: runs of consecutive wide blocks of one expert
+// are cut into tiles of this many rows (two accumulators of N = 2 x 112 fill TMEM).
+constexpr int kPlanesTileTok = 112;
 
 // Control words at the start of the workspace (int32 slots, zeroed before each call).
 enum : int {
   kCtrlTicket = 0,
   kCtrlCount0 = 1,  // kCtrlCount0 + class = number of blocks in that class
+  kCtrlPlaneTiles = 7,  // number of tiles in the planes kernel's tile list
   kCtrlStatus = 8,  // device status bits (kStatus*); kCtrlStatus + 1: code of the first wait that gave up
   kCtrlWords = 64,
 };
@@ -75,8 +79,8 @@ struct TileMap {
 
 // Workspace regions of one GEMM call.
 struct WorkspaceLayout {
-  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, row_ids = 0, row_exp = 0, hilo = 0, tok_sf = 0, sfw_atoms = 0,
-         total = 0;
+  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, plane_tiles = 0, row_ids = 0, row_exp = 0, hilo = 0,
+         tok_sf = 0, sfw_atoms = 0, total = 0;
 
   static WorkspaceLayout make(int64_t M, int64_t nblk, int64_t K, int64_t N, int64_t E, bool fast, bool row_ids,
                               bool sfw_from_rows) {
@@ -90,6 +94,8 @@ struct WorkspaceLayout {
     off = align_up(off + static_cast<size_t>(nblk) * 16, 1024);
     w.lists = off;
     off = align_up(off + static_cast<size_t>(nblk) * 16 * kNumClasses, 1024);
+    w.plane_tiles = off;  // at most one tile per 112 rows of a run plus one per run: 2 per block
+    off = align_up(off + static_cast<size_t>(nblk) * 2 * 16, 1024);
     if (row_ids) {
       w.row_ids = off;
       off = align_up(off + static_cast<size_t>(M) * 4, 1024);

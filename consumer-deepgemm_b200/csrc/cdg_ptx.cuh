@@ -179,6 +179,19 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_
   return done != 0;
 }
 
+// Non-blocking test of the phase with the given parity (acquire at cluster scope).
+__device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait whose completion may come from the other CTA of the pair (acquire at
 // cluster scope).  Returns false (and sets kStatusTimeout) when it gives up; the first
 // wait to give up also leaves `where` (a caller-chosen code naming the wait) in status[1].
@@ -199,8 +212,8 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 
 // Code naming a wait for mbar_wait_cluster: role (1 producer/empty, 2 issuer/tempty,
-// 3 issuer/full (or sfready), 4 epilogue/tfull, 5 issuer/done, 6 scale copier/full), CTA
-// rank or issuer, stage, phase, step.
+// 3 issuer/full (or sfready), 4 epilogue/tfull, 5 issuer/done, 6 scale copier/full (or the
+// TMEM scale slot), 7 scale-atom producer/slot free), CTA rank or issuer, stage, phase, step.
 __device__ __forceinline__ int wait_code(int role, int who, int stage, uint32_t phase, int step) {
   return (role << 28) | ((who & 15) << 24) | ((stage & 255) << 16) | (static_cast<int>(phase & 1u) << 15) |
          (step & 0x7fff);
@@ -223,6 +236,20 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* tmap, ui
       "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const void* tmap, uint32_t cluster_bar, int32_t x,
+                                                 int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+// (TMA, tcgen05.cp, tcgen05.mma operands).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- TMEM
@@ -310,6 +337,47 @@ __device__ __forceinline__ void tc_mma_mxf8f6f4_pair(uint32_t d_tmem, uint64_t a
       "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
+}
+
+// ---- warp-wide forms: every lane of the warp executes the call with the same
+// (warp-uniform) operands and the instruction is issued by the lane elect.sync picks (the
+// same lane every time, so its commits track its own tcgen05 operations).  A loop run by
+// the whole warp this way issues tcgen05.mma at about 50 cycles each; the same loop in a
+// branch taken by one lane needed about 75.
+__device__ __forceinline__ void tc_mma_mxf8f6f4_pair_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                          uint32_t idesc, uint32_t accumulate, uint32_t sfa_tmem,
+                                                          uint32_t sfb_tmem) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_pair_warp(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}"
+      ::"r"(smem_u32(bar)), "h"(cta_mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_cp_sf_atom_pair_warp(uint32_t taddr, uint64_t sdesc) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;\n\t}"
+      ::"r"(taddr), "l"(sdesc)
+      : "memory");
+}
+
+// mbar_wait_cluster by every lane of the warp; true for all lanes only if no lane gave up.
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity, int* status, int where = 0) {
+  const bool ok = mbar_wait_cluster(bar, parity, status, where);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Load 16 consecutive 32-bit TMEM columns of this warp's 32 lanes.
