@@ -29,9 +29,7 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB = os.path.join(PKG, "libcdg_b200.so")
 EXT = os.path.join(PKG, "_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 
-LIB_SOURCES = [os.path.join(CSRC, f)
-               for f in ("cdg_abi.cu", "cdg_moe.cu", "cdg_kernels.cuh", "cdg_pair.cuh", "cdg_wide.cuh", "cdg_ptx.cuh",
-                         "cdg_layout.h")]
+LIB_SOURCES = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h")))
 LIB_SOURCES.append(os.path.join(INCLUDE, "cdg_b200.h"))
 EXT_SOURCES = [os.path.join(CSRC, "torch_ext.cpp"), os.path.join(INCLUDE, "cdg_b200.h")]
 

@@ -238,12 +238,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
         for (int k = 0; k < 4; ++k) idk[k] = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 256, n_mma, k, 0);
         for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
           const int sub = kb0 % KSF;  // K step offset within the scale-atom stage
-          if (sub == 0 &&
-              !mbar_wait_cluster_warp(&sfready[sfs], sfphase, p.status, wait_code(3, 1, sfs, sfphase, kb0))) {
+          if (sub == 0 && !mbar_wait_cta_warp(&sfready[sfs], sfphase, p.status, wait_code(3, 1, sfs, sfphase, kb0))) {
             ok = false;
             break;
           }
-          if (!mbar_wait_cluster_warp(&full[stage], phase, p.status, wait_code(3, 0, stage, phase, kb0))) {
+          if (!mbar_wait_cta_warp(&full[stage], phase, p.status, wait_code(3, 0, stage, phase, kb0))) {
             ok = false;
             break;
           }

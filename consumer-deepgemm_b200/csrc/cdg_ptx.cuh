@@ -374,6 +374,31 @@ __device__ __forceinline__ void tc_cp_sf_atom_pair_warp(uint32_t taddr, uint64_t
       : "memory");
 }
 
+// Bounded wait for a barrier of this CTA, default (CTA) scope: for barriers completed by
+// TMA transactions or tcgen05.commit, which order the data the following tcgen05 operations
+// read.  Cheaper than the cluster-scope acquire of mbar_wait_cluster.
+__device__ __forceinline__ bool mbar_wait_cta(uint64_t* bar, uint32_t parity, int* status, int where = 0) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if (global_timer_ns() - t0 > CDG_WAIT_TIMEOUT_NS) {
+      if (status) {
+        atomicOr(status, kStatusTimeout);
+        atomicCAS(status + 1, 0, where);
+      }
+      return false;
+    }
+  }
+}
+
+// mbar_wait_cta by every lane of the warp; true for all lanes only if no lane gave up.
+__device__ __forceinline__ bool mbar_wait_cta_warp(uint64_t* bar, uint32_t parity, int* status, int where = 0) {
+  const bool ok = mbar_wait_cta(bar, parity, status, where);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // mbar_wait_cluster by every lane of the warp; true for all lanes only if no lane gave up.
 __device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity, int* status, int where = 0) {
   const bool ok = mbar_wait_cluster(bar, parity, status, where);
