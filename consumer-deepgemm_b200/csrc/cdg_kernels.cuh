@@ -178,6 +178,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ uint32_t s_mask[4];
   __shared__ float s_scale[128][kPrepK / 128];
   __shared__ int s_exp[128];
+  __shared__ float s_inv[128];              // 2^-E of each row
+  __shared__ uint32_t s_smax_bits[128];     // bits of the largest finite |bf16(sa)| of each row
   __shared__ int s_cls_count[kNumClasses][257];
   __shared__ int s_tile_count[257];
   const int b = blockIdx.x;
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     s_exp_bad = 0;
   }
   if (tid < 4) s_mask[tid] = 0u;
+  if (tid < 128) s_smax_bits[tid] = 0u;
   int row0, nrows;
   p.tm.rows(b, row0, nrows);
   __syncthreads();
@@ -241,25 +244,35 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     }
     // (1) per routed row: the exponent E with |bf16(sa[r,kb])| < 2^E for every K block of
     //     the row (frexp exponent of the largest scale); and the BF16-rounded scales of
-    //     this CTA's K blocks.
+    //     this CTA's K blocks.  The (row, K block) scales are read by all threads at once,
+    //     the K block fastest unless the scales are stored row-fastest (MN-major).
+    {
+      const bool mn_major = !p.sa_packed && p.sa_stride_m == 1;
+      const int items = ntok * kb_count;
+      bool pow2 = true;
+      for (int it = tid; it < items; it += blockDim.x) {
+        const int rr = mn_major ? it % ntok : it / kb_count;
+        const int kb = mn_major ? it / ntok : it % kb_count;
+        if (s_id[rr] != expert) continue;
+        const float sraw = load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb);
+        const float sbf = __bfloat162float(__float2bfloat16_rn(sraw));
+        // non-negative floats order as their bit patterns
+        if (isfinite(sbf)) atomicMax(&s_smax_bits[rr], __float_as_uint(fabsf(sbf)));
+        pow2 = pow2 && pow2_code(sraw) >= 0;
+      }
+      if (!pow2) atomicAnd(&s_pow2, 0);
+      __syncthreads();
+    }
     if (tid < ntok) {
       int emax = 0;
-      const int r = row0 + tid;
       if (s_id[tid] == expert) {
-        float smax = 0.0f;
-        bool pow2 = true;
-        for (int kb = 0; kb < kb_count; ++kb) {
-          const float sraw = load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, kb);
-          const float sbf = __bfloat162float(__float2bfloat16_rn(sraw));
-          if (isfinite(sbf)) smax = fmaxf(smax, fabsf(sbf));
-          pow2 = pow2 && pow2_code(sraw) >= 0;
-        }
+        const float smax = __uint_as_float(s_smax_bits[tid]);
         if (smax > 0.0f) frexpf(smax, &emax);
-        if (!pow2) atomicAnd(&s_pow2, 0);
         // 2^E must be a UE8M0 scale factor (and a normal FP32 factor in the epilogue)
         if (emax < -126 || emax > 127) atomicOr(&s_exp_bad, 1);
       }
       s_exp[tid] = emax;
+      s_inv[tid] = ldexpf(1.0f, -emax);
       if (blockIdx.y == 0) p.row_exp[b * 128 + tid] = emax;
     }
     for (int it = tid; it < ntok * kbn; it += blockDim.x) {
@@ -316,22 +329,32 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       const int kl = c >> 3;
       const int r = row0 + rr;
       const int64_t col = static_cast<int64_t>(kb0) * 128 + c * 16;
-      uint4 hi4 = make_uint4(0, 0, 0, 0), lo4 = make_uint4(0, 0, 0, 0);
+      uint4 hi4, lo4;
       {
+        // two elements per conversion instruction (e4m3x2 <-> f16x2, f32x2 -> bf16x2 / e4m3x2),
+        // the same roundings as one at a time; byte pairs taken from and put into 32-bit words
         const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + col);
         const float sbf = s_scale[rr][kl];
-        const float inv = ldexpf(1.0f, -s_exp[rr]);
-        const uint8_t* sb8 = reinterpret_cast<const uint8_t*>(&raw);
-        uint8_t* hb = reinterpret_cast<uint8_t*>(&hi4);
-        uint8_t* lb = reinterpret_cast<uint8_t*>(&lo4);
+        const float inv = s_inv[rr];
+        const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float x = __bfloat162float(__float2bfloat16_rn(e4m3_to_f32(sb8[i]) * sbf));
-          const float v = x * inv;
-          const uint8_t h = f32_to_e4m3(v);
-          hb[i] = h;
-          lb[i] = f32_to_e4m3(v - e4m3_to_f32(h));
+        for (int i = 0; i < 8; ++i) {
+          const __nv_fp8x2_storage_t a2 = static_cast<__nv_fp8x2_storage_t>(in[i >> 1] >> (16 * (i & 1)));
+          const __half2_raw ar = __nv_cvt_fp8x2_to_halfraw2(a2, __NV_E4M3);
+          const float2 af = __half22float2(__half2(ar));
+          const float2 x = __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(af.x, sbf), __fmul_rn(af.y, sbf)));
+          const float2 v = make_float2(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv));
+          const __nv_fp8x2_storage_t h = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
+          const float2 hf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(h, __NV_E4M3)));
+          const __nv_fp8x2_storage_t l =
+              __nv_cvt_float2_to_fp8x2(make_float2(__fsub_rn(v.x, hf.x), __fsub_rn(v.y, hf.y)), __NV_SATFINITE,
+                                       __NV_E4M3);
+          hw[i >> 1] |= static_cast<uint32_t>(h) << (16 * (i & 1));
+          lw[i >> 1] |= static_cast<uint32_t>(l) << (16 * (i & 1));
         }
+        hi4 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        lo4 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
       uint8_t* dst = p.hilo + (static_cast<int64_t>(b) * 128 + rr) * K + col;
       *reinterpret_cast<uint4*>(dst) = hi4;
