@@ -50,13 +50,13 @@ import torch  # noqa: E402
 METRIC = "grouped FP8×FP4 MoE GEMM TFLOPS and HBM GB/s vs roofline at 1/2/4/8 B200"
 DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
 # library kernels per GEMM call on the CTA-pair path: cdg_prep_kernel, cdg_gemm_pair_kernel<16,4>,
-# <32,2>, <128,1>, <128,1,direct>, cdg_generic_kernel
+# <32,2>, cdg_gemm_planes_kernel, cdg_gemm_wide_kernel<direct>, cdg_generic_kernel
 GEMM_LAUNCHES = 6
 # DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
 # captures summarised under profiles/ (absent: no capture of the current kernels yet).
 NCU_TRAFFIC = {
     "c1": 2.007860e9 + 0.223218e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
-    "c2": 1.413981e9 + 0.518562e9,  # cdg_gemm_pair_kernel<128, 1>: profiles/cdg_gemm_pair_kernel128_c2_prefill.md
+    "c2": 1.427530e9 + 0.654704e9,  # cdg_gemm_planes_kernel: profiles/cdg_gemm_planes_kernel_c2_prefill.md
 }
 # per EP step on top of the GEMM kernels: dispatch (quantise + pack), permute, return (or unpermute), combine
 EP_LAUNCHES = 4

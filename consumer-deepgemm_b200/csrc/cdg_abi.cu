@@ -75,8 +75,8 @@ const DeviceInfo& device_info(int dev) {
       if (cudaFuncSetAttribute(cdg_gemm_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                PlanesSmem::kBytes) != cudaSuccess)
         return;
-      if (cudaFuncSetAttribute(cdg_gemm_wide_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               WideSmem<true>::kBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(cdg_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               WideSmem::kBytes) != cudaSuccess)
         return;
       if (cudaFuncSetAttribute(cdg_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
           cudaSuccess)
@@ -464,8 +464,9 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   if (t_prof_start && cudaEventRecord(t_prof_start, stream) != cudaSuccess) return CDG_ERR_CUDA;
   if (pair_path) {
     // CTA pairs (tcgen05 cta_group::2): two adjacent 128-column tiles per cluster; four MMA
-    // issuers for tiny blocks, two for narrow; wide blocks in cdg_gemm_wide_kernel (planes,
-    // or the raw rows of the direct class).
+    // issuers for tiny blocks, two for narrow; wide blocks in token tiles of the plane kernel
+    // (cdg_gemm_planes_kernel), or, when their scales are powers of two, in
+    // cdg_gemm_wide_kernel on the raw rows (direct class).
     CUtensorMap p16, p32, tsf;
     st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &tsf);
     if (st != CDG_OK) return st;
@@ -496,7 +497,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     // Wide blocks whose activation scales are all powers of two: raw e4m3 rows.
     ka.list = lists + kClassWideDirect * nblk;
     ka.count_slot = kCtrlCount0 + kClassWideDirect;
-    if (launch_pdl(cdg_gemm_wide_kernel<true>, grid, WideSmem<true>::kThreads, WideSmem<true>::kBytes, stream, tw,
+    if (launch_pdl(cdg_gemm_wide_kernel, grid, WideSmem::kThreads, WideSmem::kBytes, stream, tw,
                    ad, tsf, tok, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
   } else {

@@ -1,31 +1,24 @@
-// CTA-pair tcgen05 kernel for wide blocks (more than 32 routed rows of one expert).
+// CTA-pair tcgen05 kernel for the direct class: wide blocks (more than 32 routed rows of one
+// expert, or the tail block of an expert spanning several blocks) whose activation scales are
+// all powers of two.
 //
 // A cluster of two CTAs computes a pair tile: 256 weight rows of one expert (CTA r holds
 // output-column tile 2*pt + r) x the block's tokens, with tcgen05.mma.cta_group::2
 // (M = 256, weights as the MMA's A operand: "swap AB").  The tokens are the MMA's N side:
 // N = 2h, h = the block's routed span halved and rounded up to 16; CTA 0 holds tokens
-// [0, h), CTA 1 tokens [h, 2h) of every K step.
+// [0, h), CTA 1 tokens [h, 2h) of every K step, the e4m3 rows of A themselves (one MMA per
+// 32-wide K slice).  The reference's bf16(bf16(a) * bf16(2^s)) is then the exact product
+// a * 2^s, which the tensor core forms from the raw rows with 2^s as the MMA's B scale factor:
+// the prep kernel writes a 512-byte UE8M0 atom per (block, K step), so the accumulator holds
+// the final values and the epilogue only converts and stores.
 //
-// Two forms of the token operand:
-//   * planes (DIRECT = false): the two e4m3 planes hi, lo of the BF16-dequantised rows,
-//     each row divided by 2^E (E per row, from the prep kernel); one MMA per plane and
-//     32-wide K slice, both into the same accumulator;
-//   * direct (DIRECT = true, every scale of the block a power of two): the e4m3 rows of A
-//     themselves, one MMA per K slice.
-// In both forms the per-token factor (2^E, or the K block's scale 2^s) is the MMA's B
-// scale factor: the prep kernel writes a 512-byte UE8M0 atom per (block, K step), so the
-// accumulator already holds the final values and the epilogue only converts and stores.
-// Multiplying by a power of two inside the MMA is exact, so this equals scaling after
-// the sum.
-//
-// Pipeline: a stage holds kKS = 2 K steps (weights, tokens, weight and token scale
-// atoms of each), so the MMA issuer waits on one barrier per two K steps: a wait costs
-// the single issuing thread about as long as the four MMAs of one K step.  The scale
-// atoms reach TMEM through a second thread (tcgen05.cp into the stage's own TMEM scale
-// columns, then a commit to the stage's `sfready` barrier), so the MMA thread issues
-// nothing but MMAs and commits.  A stage's scale columns are free again when its data
-// lands the next time: the producer refills a stage only after the MMAs that read it
-// completed.
+// Pipeline: a stage holds kKS = 2 K steps (weights, tokens, weight and token scale atoms of
+// each), so the MMA issuer waits on one barrier per two K steps.  The scale atoms reach TMEM
+// through a second thread (tcgen05.cp into the stage's own TMEM scale columns, then a commit
+// to the stage's `sfready` barrier), so the MMA warp issues nothing but MMAs and commits; the
+// MMA loop runs on the whole warp with each instruction issued by its elected lane.  A
+// stage's scale columns are free again when its data lands the next time: the producer
+// refills a stage only after the MMAs that read it completed.
 //
 // Epilogue (four warps per CTA, warp q owns TMEM lanes 32q..32q+31 = output columns):
 // tcgen05.ld 16x256b hands each thread two adjacent tokens of one column; packed to
@@ -43,14 +36,12 @@
 
 namespace cdg {
 
-template <bool DIRECT>
 struct WideSmem {
   static constexpr int kKS = 2;                    // K steps per stage
-  static constexpr int kPlanes = DIRECT ? 1 : 2;   // token planes per K step
   static constexpr int kW = 128 * 128;             // weight tile per K step (E2M1 unpacked to bytes)
-  static constexpr int kA = 64 * 128;              // one plane: 64 token rows per K step
-  static constexpr int kStep = kW + kPlanes * kA;  // operand bytes per K step
-  static constexpr int kStages = DIRECT ? 4 : 3;
+  static constexpr int kA = 64 * 128;              // 64 token rows per K step
+  static constexpr int kStep = kW + kA;            // operand bytes per K step
+  static constexpr int kStages = 4;
   static constexpr int kStageBytes = kKS * kStep;
   static constexpr int kSfRing = kStages * kStageBytes;            // [stage][kKS] weight scale atoms
   static constexpr int kTsfRing = kSfRing + kStages * kKS * 512;   // [stage][kKS] token scale atoms
@@ -61,7 +52,7 @@ struct WideSmem {
   static_assert(kBytes <= 232448, "shared memory per CTA");
   static_assert(kStep % 1024 == 0, "K steps must stay 1024-byte aligned for SW128 tiles");
   // bytes one CTA's copies of one K step add to the even CTA's `full` barrier
-  static constexpr uint32_t kTxPerStep = 128u * 64u + kPlanes * kA + 512u + 512u;
+  static constexpr uint32_t kTxPerStep = 128u * 64u + kA + 512u + 512u;
   // TMEM: two 128-column accumulators, then [stage][kKS] 4-column weight scale sets and
   // [stage][kKS] 4-column token scale sets
   static constexpr uint32_t kSfwCol = 256;
@@ -70,12 +61,11 @@ struct WideSmem {
   static constexpr int kThreads = 256;
 };
 
-template <bool DIRECT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     cdg_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_sfw, const __grid_constant__ CUtensorMap tmap_tsf,
                          GemmArgs p) {
-  using L = WideSmem<DIRECT>;
+  using L = WideSmem;
   constexpr int S = L::kStages;
   constexpr int KS = L::kKS;
   constexpr uint32_t kTmemCols = 512;
@@ -156,14 +146,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
         const int wrow = cur.y * p.N + nt * 128;
         const int atom0 = (cur.y * n_tiles + nt) * k_steps;
-        int a_row;
-        if (DIRECT) {  // rows of A itself
-          int row0, nrows;
-          p.tm.rows(blk, row0, nrows);
-          a_row = row0 + static_cast<int>(rank) * wide_half(cur.z);
-        } else {  // rows of the block's planes
-          a_row = blk * 128 + static_cast<int>(rank) * wide_half(cur.z);
-        }
+        int row0, nrows;
+        p.tm.rows(blk, row0, nrows);
+        const int a_row = row0 + static_cast<int>(rank) * wide_half(cur.z);  // rows of A itself
         for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, p.status,
                                  wait_code(1, static_cast<int>(rank), stage, phase ^ 1, kb0))) {
@@ -176,10 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           for (int u = 0; u < n; ++u) {
             const int kb = kb0 + u;
             tma_load_2d_pair(step_w(stage, u), &tmap_w, fb, kb * 128, wrow);
-            if (DIRECT)
-              tma_load_2d_pair(step_a(stage, u), &tmap_a, fb, kb * 128, a_row);
-            else
-              tma_load_3d_pair(step_a(stage, u), &tmap_a, fb, kb * 128, a_row, 0);
+            tma_load_2d_pair(step_a(stage, u), &tmap_a, fb, kb * 128, a_row);
             tma_load_2d_pair(step_sfw(stage, u), &tmap_sfw, fb, 0, atom0 + kb);
             tma_load_2d_pair(step_tsf(stage, u), &tmap_tsf, fb, 0, blk * k_steps + kb);
           }
@@ -188,8 +170,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (even CTA)
-    if (lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer (even CTA, whole warp)
+    if (rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -200,14 +182,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         const uint32_t n_mma = 2u * static_cast<uint32_t>(wide_half(cur.z));
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, p.status, wait_code(2, 0, acc, acc_phase ^ 1, local))) {
+        if (!mbar_wait_cluster_warp(&tempty[acc], acc_phase ^ 1, p.status, wait_code(2, 0, acc, acc_phase ^ 1, local))) {
           ok = false;
           break;
         }
-        tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * 128;
+        uint32_t idk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) idk[k] = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 256, n_mma, k, k);
         for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
-          if (!mbar_wait_cluster(&sfready[stage], phase, p.status, wait_code(3, 0, stage, phase, kb0))) {
+          if (!mbar_wait_cta_warp(&sfready[stage], phase, p.status, wait_code(3, 0, stage, phase, kb0))) {
             ok = false;
             break;
           }
@@ -216,48 +200,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
           for (int u = 0; u < n; ++u) {
             const uint32_t sfw_t = tmem_base + L::kSfwCol + (stage * KS + u) * 4;
             const uint32_t tsf_t = tmem_base + L::kTsfCol + (stage * KS + u) * 4;
-            const uint32_t w_addr = smem_u32(step_w(stage, u));
-            const uint32_t a_addr = smem_u32(step_a(stage, u));
+            const uint64_t wd0 = smem_desc_sw128(smem_u32(step_w(stage, u)));
+            const uint64_t ad0 = smem_desc_sw128(smem_u32(step_a(stage, u)));
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const uint64_t wd = smem_desc_sw128(w_addr + k * 32);
-              const uint32_t idesc = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 256, n_mma, k, k);
-              const uint32_t accumulate = (kb0 + u != 0 || k != 0) ? 1u : 0u;
-              tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + k * 32), idesc, accumulate, sfw_t, tsf_t);
-              if (!DIRECT)
-                tc_mma_mxf8f6f4_pair(d_tmem, wd, smem_desc_sw128(a_addr + L::kA + k * 32), idesc, 1u, sfw_t, tsf_t);
+              // descriptor start addresses are in 16-byte units: +32 bytes per K slice
+              tc_mma_mxf8f6f4_pair_warp(d_tmem, wd0 + 2 * k, ad0 + 2 * k, idk[k],
+                                        (kb0 + u != 0 || k != 0) ? 1u : 0u, sfw_t, tsf_t);
             }
           }
-          tc_commit_pair(&empty[stage], 0x3);
+          tc_commit_pair_warp(&empty[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        tc_commit_pair(&tfull[acc], 0x3);
+        tc_commit_pair_warp(&tfull[acc], 0x3);
       }
       // Every MMA (and its TMEM writes in both CTAs) completes before teardown.
-      tc_commit_pair(done, 0x1);
-      mbar_wait_cluster(done, 0, p.status, wait_code(5, 0, 0, 0, 0));
+      tc_commit_pair_warp(done, 0x1);
+      mbar_wait_cluster_warp(done, 0, p.status, wait_code(5, 0, 0, 0, 0));
     }
   } else if (warp == 2) {
-    // ------------------------------------------------------------ scale-factor copier (even CTA)
-    if (lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ scale-factor copier (even CTA, whole warp)
+    if (rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       for (int t = pair; t < tiles && ok; t += npairs) {
         for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
-          if (!mbar_wait_cluster(&full[stage], phase, p.status, wait_code(6, 0, stage, phase, kb0))) {
+          if (!mbar_wait_cta_warp(&full[stage], phase, p.status, wait_code(6, 0, stage, phase, kb0))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const int n = k_steps - kb0 < KS ? k_steps - kb0 : KS;
           for (int u = 0; u < n; ++u) {
-            tc_cp_sf_atom_pair(tmem_base + L::kSfwCol + (stage * KS + u) * 4,
-                               smem_desc_sf(smem_u32(step_sfw(stage, u))));
-            tc_cp_sf_atom_pair(tmem_base + L::kTsfCol + (stage * KS + u) * 4,
-                               smem_desc_sf(smem_u32(step_tsf(stage, u))));
+            tc_cp_sf_atom_pair_warp(tmem_base + L::kSfwCol + (stage * KS + u) * 4,
+                                    smem_desc_sf(smem_u32(step_sfw(stage, u))));
+            tc_cp_sf_atom_pair_warp(tmem_base + L::kTsfCol + (stage * KS + u) * 4,
+                                    smem_desc_sf(smem_u32(step_tsf(stage, u))));
           }
-          tc_commit_pair(&sfready[stage], 0x1);
+          tc_commit_pair_warp(&sfready[stage], 0x1);
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
