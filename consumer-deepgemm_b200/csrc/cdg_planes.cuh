@@ -217,7 +217,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA, whole warp)
     if (rank == 0) {
-      const uint32_t const_sf = tmem_base + L::kConstCol;
+      // All 512 columns are allocated, so the TMEM base address is 0 and the MMA operands below
+      // are compile-time constants plus warp-uniform offsets (operands the compiler cannot prove
+      // warp-uniform, e.g. loaded from memory, made the issuing loop measurably slower).  Any
+      // other base is reported as an error and the kernel leaves without issuing.
+      if (tmem_base != 0u) {
+        atomicOr(p.status, kStatusTimeout);
+        ok = false;
+      }
+      constexpr uint32_t const_sf = L::kConstCol;
       tc_cp_sf_atom_pair_warp(const_sf, smem_desc_sf(smem_u32(smem + L::kConstSf)));
       tc_cp_sf_atom_pair_warp(const_sf + 4, smem_desc_sf(smem_u32(smem + L::kConstSf)));
       int stage = 0, sfs = 0;
@@ -225,14 +233,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       int local = 0;
       for (int t = pair; t < tiles && ok; t += npairs, ++local) {
         const int4 cur = __ldg(&p.list[t / n_pt]);
-        const uint32_t n_mma = 4u * static_cast<uint32_t>(tile_half(cur.y));
+        const uint32_t n_mma = __shfl_sync(0xffffffffu, 4u * static_cast<uint32_t>(tile_half(cur.y)), 0);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_cluster_warp(&tempty[acc], acc_phase ^ 1, p.status, wait_code(2, 0, acc, acc_phase ^ 1, local))) {
           ok = false;
           break;
         }
-        const uint32_t d_tmem = tmem_base + acc * L::kAccCols;
+        const uint32_t d_tmem = acc * L::kAccCols;
         uint32_t idk[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) idk[k] = idesc_mxf8f6f4(/*a=E2M1*/ 5, /*b=E4M3*/ 0, 256, n_mma, k, 0);
@@ -249,7 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
           tc_fence_after();
           const int n = k_steps - kb0 < KS ? k_steps - kb0 : KS;
           for (int u = 0; u < n; ++u) {
-            const uint32_t sfw_t = tmem_base + L::kSfwCol + (sfs * KSF + sub + u) * 4;
+            const uint32_t sfw_t = L::kSfwCol + (sfs * KSF + sub + u) * 4;
             const uint64_t wd0 = smem_desc_sw128(smem_u32(step_w(stage, u)));
             const uint64_t ad0 = smem_desc_sw128(smem_u32(step_a(stage, u)));
 #pragma unroll
