@@ -1,0 +1,96 @@
+"""GPU parity of the wide-block paths on hand-made routings (CTA-pair path, N % 256 == 0).
+
+Wide blocks with FP32 activation scales run the plane kernel on token tiles: the prep
+kernel joins the consecutive wide blocks of one expert into runs and cuts each run into
+tiles of at most 112 rows, which may cross block boundaries; the last block of an expert
+that spans several blocks joins the wide class whatever its row count.  With power-of-two
+scales the same blocks run the direct-class kernel, one block per tile.  The cases below
+cover runs of one to three blocks, tiles crossing a block boundary, runs that end one row
+into a block, experts without rows, odd numbers of 128-wide K steps (a partial pipeline
+stage and a partial scale-atom stage) and a masked layout whose groups span blocks.  All
+outputs are compared with the CPU oracle over every row, with the golden cases'
+tolerances; rows outside every group must be exact zeros.
+"""
+
+import pytest
+import torch
+
+import cabi
+from deep_gemm.utils.math import per_block_cast_to_fp8
+from consumer_deep_gemm import synthetic
+from metrics import TOL_NORMWISE, TOL_ROW_L2, errors
+from oracle import cdg_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _contiguous(counts, k, pow2, seed):
+    """Contiguous layout (groups padded to 128 rows) with the given rows per expert."""
+    g = torch.Generator().manual_seed(seed)
+    ids = []
+    for e, n in enumerate(counts):
+        pad = (n + 127) // 128 * 128
+        ids += [e] * n + [-1] * (pad - n)
+    ids = torch.tensor(ids, dtype=torch.int32)
+    m = ids.numel()
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).float()
+    a, sa = per_block_cast_to_fp8(x)
+    if pow2:
+        sa = torch.exp2(torch.ceil(torch.log2(sa)))
+        a = (x.view(m, k // 128, 128) / sa.unsqueeze(-1)).view(m, k).to(torch.float8_e4m3fn)
+    a.view(torch.uint8)[ids < 0] = 0
+    sa[ids < 0] = 1.0
+    return a, sa, ids
+
+
+def _check(a, sa, b, sb, ids, masked=False):
+    m, n = a.shape[0], b.shape[1]
+    ref = torch.empty(m, n, dtype=torch.bfloat16)
+    if masked:
+        oracle.m_grouped_fp8_fp4_gemm_nt_masked((a, sa), (b, sb), ref, ids)
+        rows = torch.zeros(m, dtype=torch.bool)
+        seg = m // b.shape[0]
+        for gi, c in enumerate(ids.tolist()):
+            rows[gi * seg:gi * seg + min(c, seg)] = True
+    else:
+        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (b, sb), ref, ids)
+        rows = ids >= 0
+    d = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ws = cabi.gemm(a.to(DEV), sa.to(DEV), b.to(DEV), sb.to(DEV), d, ids.to(DEV), masked=masked)
+    torch.cuda.synchronize()
+    out = d.cpu()
+    assert not torch.isnan(out).any(), "rows left unwritten"
+    assert bool((out[~rows] == 0).all()), "rows outside every group must be zero"
+    nw, rl2 = errors(out, ref, rows)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (nw, rl2)
+    return cabi.block_classes(ws)
+
+
+@pytest.mark.parametrize("k", [384, 640, 1024], ids=["k384", "k640", "k1024"])
+@pytest.mark.parametrize("pow2", [False, True], ids=["planes", "direct"])
+def test_runs_across_blocks(k, pow2):
+    # rows per expert: three blocks (tiles cross both block boundaries), two blocks ending one
+    # row into the second, one wide block, a tail of 5 rows after a full block, no rows, one row
+    counts = [300, 129, 40, 133, 0, 1]
+    a, sa, ids = _contiguous(counts, k, pow2, seed=k)
+    b, sb = synthetic.make_weights(len(counts), 512, k, "cpu", seed=3)
+    cls = _check(a, sa, b, sb, ids)
+    if pow2:
+        assert cls["wide_direct"] >= 6 and cls["wide"] == 0, cls
+    else:
+        # the tail blocks (1 and 5 rows) of multi-block experts are wide too
+        assert cls["wide"] == 8 and cls["wide_direct"] == 0, cls
+
+
+def test_masked_groups_span_blocks():
+    # masked layout: 3 groups of 300 rows each (blocks of 128, 128 and 44 rows per group)
+    e, seg, k = 3, 300, 512
+    counts = torch.tensor([300, 200, 129], dtype=torch.int32)
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(e * seg, k, generator=g).to(torch.bfloat16).float()
+    a, sa = per_block_cast_to_fp8(x)
+    b, sb = synthetic.make_weights(e, 256, k, "cpu", seed=5)
+    cls = _check(a, sa, b, sb, counts, masked=True)
+    assert cls["wide"] >= 6, cls
