@@ -12,6 +12,7 @@
 //   cdg_ep_permute_fixed      fixed-capacity receive buffer -> contiguous layout
 //   cdg_ep_unpermute          GEMM rows -> received order
 //   cdg_ep_combine            returned rows -> weighted top-k sum per token
+//   cdg_ep_unpermute_combine  both in one pass, for a layer without an exchange
 //
 // Row order inside a destination or an expert group comes from atomics and is
 // not deterministic; every row is computed independently and returned to its
@@ -146,6 +147,9 @@ __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, 
 }
 
 // One warp per (row, 128-column block of the output); gate = columns [0, I), up = [I, 2I).
+// VEC: the lane's four gate and four up values arrive as one 8-byte load each (rows 8-byte
+// aligned); otherwise one 2-byte load per value.
+template <bool VEC>
 __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride, int64_t M, int64_t I,
                                       const int32_t* m_indices, uint8_t* q, int64_t q_stride, float* s,
                                       int64_t s_stride_m, int64_t s_stride_k) {
@@ -155,14 +159,27 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride
   if (w >= M * kb_count) return;
   const int64_t r = w / kb_count, kb = w - r * kb_count;
   if (m_indices && m_indices[r] < 0) return;  // padding row: never read by the next GEMM
+  const __nv_bfloat16* gp = in + r * in_stride + kb * 128 + lane * 4;
+  float gv[4], uv[4];
+  if (VEC) {
+    const uint2 g2 = *reinterpret_cast<const uint2*>(gp);
+    const uint2 u2 = *reinterpret_cast<const uint2*>(gp + I);
+    const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&g2.x));
+    const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&g2.y));
+    const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2.x));
+    const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2.y));
+    gv[0] = g01.x; gv[1] = g01.y; gv[2] = g23.x; gv[3] = g23.y;
+    uv[0] = u01.x; uv[1] = u01.y; uv[2] = u23.x; uv[3] = u23.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      gv[i] = __bfloat162float(gp[i]);
+      uv[i] = __bfloat162float(gp[I + i]);
+    }
+  }
   float v[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int64_t c = kb * 128 + lane * 4 + i;
-    const float g = __bfloat162float(in[r * in_stride + c]);
-    const float u = __bfloat162float(in[r * in_stride + I + c]);
-    v[i] = g / (1.0f + expf(-g)) * u;
-  }
+  for (int i = 0; i < 4; ++i) v[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
   quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane);
 }
 
@@ -451,13 +468,20 @@ __global__ void ep_unpermute_kernel(const __nv_bfloat16* Y, int64_t y_stride, co
   for (int64_t c = lane; c < H / 8; c += 32) dst[c] = src[c];
 }
 
-// One CTA per token; y[t, :] = bf16(sum_j w[t, j] * rows[send_index[t*k + j], :]) in FP32, slots in order.
+// One CTA per token; y[t, :] = bf16(sum_j w[t, j] * rows[row(send_index[t*k + j]), :]) in FP32,
+// slots in order (an fmaf per slot), where row(i) = perm_pos[i] when perm_pos is given (the
+// rows are then read where the grouped GEMM left them, fusing the unpermute) and i otherwise;
+// slots whose index or row is -1 add nothing.  VEC: each thread reads and writes 8 columns
+// at a time (16-byte accesses; H a multiple of 8, rows and y 16-byte aligned).
 // Peer variant (ps.own != nullptr; `rows` unused): the returned rows are the own window's
 // for the step's parity; first waits until every rank returned its rows; the last CTA then
 // advances the window's step counter (scratch: [1] ticket, zeroed by the host).
-__global__ void ep_combine_kernel(const __nv_bfloat16* rows, const int32_t* send_index, const float* topk_w, int64_t T,
-                                  int64_t topk, int64_t H, __nv_bfloat16* y, PeerStep ps = PeerStep{},
-                                  int32_t* scratch = nullptr) {
+constexpr int kCombineMaxTopk = 32;
+
+template <bool VEC>
+__global__ void ep_combine_kernel(const __nv_bfloat16* rows, int64_t row_stride, const int32_t* perm_pos,
+                                  const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk, int64_t H,
+                                  __nv_bfloat16* y, PeerStep ps = PeerStep{}, int32_t* scratch = nullptr) {
   int32_t epoch = 0;
   bool ok = true;
   if (ps.own) {
@@ -466,15 +490,50 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, const int32_t* send
     ok = wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kReturnFlags),
                          static_cast<int>(ps.win.ranks), epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus));
   }
+  __shared__ int64_t s_row[kCombineMaxTopk];
+  __shared__ float s_w[kCombineMaxTopk];
   const int64_t t = blockIdx.x;
   if (ok && t < T) {
-    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
-      float acc = 0.0f;
-      for (int64_t j = 0; j < topk; ++j) {
-        const int32_t r = send_index[t * topk + j];
-        if (r >= 0) acc = fmaf(topk_w[t * topk + j], __bfloat162float(rows[static_cast<int64_t>(r) * H + c]), acc);
+    if (threadIdx.x < topk) {
+      const int32_t i = send_index[t * topk + threadIdx.x];
+      const int32_t r = (i >= 0 && perm_pos) ? perm_pos[i] : i;
+      s_row[threadIdx.x] = r;
+      s_w[threadIdx.x] = topk_w[t * topk + threadIdx.x];
+    }
+    __syncthreads();
+    if (VEC) {
+      for (int64_t c8 = threadIdx.x; c8 < H / 8; c8 += blockDim.x) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int64_t j = 0; j < topk; ++j) {
+          const int64_t r = s_row[j];
+          if (r < 0) continue;
+          const uint4 v = *reinterpret_cast<const uint4*>(rows + r * row_stride + c8 * 8);
+          const float wj = s_w[j];
+          const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw[q2]));
+            acc[2 * q2] = fmaf(wj, f.x, acc[2 * q2]);
+            acc[2 * q2 + 1] = fmaf(wj, f.y, acc[2 * q2 + 1]);
+          }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) {
+          __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * q2], acc[2 * q2 + 1]);
+          o[q2] = *reinterpret_cast<uint32_t*>(&b);
+        }
+        *reinterpret_cast<uint4*>(y + t * H + c8 * 8) = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      y[t * H + c] = __float2bfloat16_rn(acc);
+    } else {
+      for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
+        float acc = 0.0f;
+        for (int64_t j = 0; j < topk; ++j) {
+          const int64_t r = s_row[j];
+          if (r >= 0) acc = fmaf(s_w[j], __bfloat162float(rows[r * row_stride + c]), acc);
+        }
+        y[t * H + c] = __float2bfloat16_rn(acc);
+      }
     }
   }
   if (!ps.own) return;
@@ -548,7 +607,9 @@ int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t
   if (M < 0 || I <= 0 || I % 128 || (M > 0 && (!in || !q || !s))) return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(q) % 4 || q_stride % 4) return CDG_ERR_ALIGNMENT;
   if (M == 0) return CDG_OK;
-  cdg::silu_mul_quant_kernel<<<cdg::warp_grid(M * (I / 128)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  const bool vec = reinterpret_cast<uintptr_t>(in) % 8 == 0 && in_stride % 4 == 0;
+  auto kernel = vec ? cdg::silu_mul_quant_kernel<true> : cdg::silu_mul_quant_kernel<false>;
+  kernel<<<cdg::warp_grid(M * (I / 128)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(in), in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k);
   return cdg::launched();
 }
@@ -648,13 +709,34 @@ int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, i
   return cdg::launched();
 }
 
+namespace cdg {
+namespace {
+int launch_combine(const void* rows, int64_t row_stride, const int32_t* perm_pos, const int32_t* send_index,
+                   const float* topk_w, int64_t T, int64_t topk, int64_t H, void* y, cudaStream_t st) {
+  if (T < 0 || topk <= 0 || topk > kCombineMaxTopk || H <= 0 || row_stride < H) return CDG_ERR_INVALID_ARGUMENT;
+  if (T == 0) return CDG_OK;
+  const bool vec = H % 8 == 0 && row_stride % 8 == 0 && reinterpret_cast<uintptr_t>(rows) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(y) % 16 == 0;
+  auto kernel = vec ? ep_combine_kernel<true> : ep_combine_kernel<false>;
+  kernel<<<static_cast<unsigned>(T), 256, 0, st>>>(static_cast<const __nv_bfloat16*>(rows), row_stride, perm_pos,
+                                                   send_index, topk_w, T, topk, H, static_cast<__nv_bfloat16*>(y),
+                                                   PeerStep{}, nullptr);
+  return launched();
+}
+}  // namespace
+}  // namespace cdg
+
 int cdg_ep_combine(const void* rows, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
                    int64_t H, void* y, cdg_stream_t stream) {
-  if (T < 0 || topk <= 0 || H <= 0) return CDG_ERR_INVALID_ARGUMENT;
-  if (T == 0) return CDG_OK;
-  cdg::ep_combine_kernel<<<static_cast<unsigned>(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(rows), send_index, topk_w, T, topk, H, static_cast<__nv_bfloat16*>(y));
-  return cdg::launched();
+  return cdg::launch_combine(rows, H, nullptr, send_index, topk_w, T, topk, H, y,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cdg_ep_unpermute_combine(const void* Y, int64_t y_stride, const int32_t* perm_pos, const int32_t* send_index,
+                             const float* topk_w, int64_t T, int64_t topk, int64_t H, void* y, cdg_stream_t stream) {
+  if (!perm_pos) return CDG_ERR_INVALID_ARGUMENT;
+  return cdg::launch_combine(Y, y_stride, perm_pos, send_index, topk_w, T, topk, H, y,
+                             reinterpret_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------- peer-memory exchange
@@ -776,8 +858,9 @@ int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* top
   ps.own = static_cast<uint8_t*>(window);
   ps.win = cdg::make_window(ranks, cap, H);
   const unsigned grid = T > 0 ? static_cast<unsigned>(T) : 1u;
-  cdg::ep_combine_kernel<<<grid, 256, 0, st>>>(nullptr, send_index, topk_w, T, topk, H, static_cast<__nv_bfloat16*>(y),
-                                               ps, scratch);
+  if (topk > cdg::kCombineMaxTopk) return CDG_ERR_INVALID_ARGUMENT;
+  cdg::ep_combine_kernel<true><<<grid, 256, 0, st>>>(nullptr, H, nullptr, send_index, topk_w, T, topk, H,
+                                                     static_cast<__nv_bfloat16*>(y), ps, scratch);
   return cdg::launched();
 }
 

@@ -422,6 +422,21 @@ torch::Tensor ep_combine(const torch::Tensor& rows, const torch::Tensor& send_in
   return y;
 }
 
+torch::Tensor ep_unpermute_combine(const torch::Tensor& Y, const torch::Tensor& perm_pos, const torch::Tensor& send_index,
+                                   const torch::Tensor& topk_w) {
+  TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
+  TORCH_CHECK(topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() && topk_w.dim() == 2, "topk_w: f32");
+  TORCH_CHECK(perm_pos.scalar_type() == torch::kInt32 && send_index.scalar_type() == torch::kInt32, "int32 indices");
+  const c10::cuda::CUDAGuard guard(Y.device());
+  const int64_t T = topk_w.size(0), topk = topk_w.size(1), H = Y.size(1);
+  auto y = torch::empty({T, H}, Y.options());
+  check_status(cdg_ep_unpermute_combine(Y.data_ptr(), Y.stride(0), perm_pos.data_ptr<int32_t>(),
+                                        send_index.data_ptr<int32_t>(), topk_w.data_ptr<float>(), T, topk, H,
+                                        y.data_ptr(), cur_stream(Y)),
+               "ep_unpermute_combine");
+  return y;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -481,4 +496,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
   m.def("ep_unpermute", &ep_unpermute, py::arg("y"), py::arg("perm_pos"));
   m.def("ep_combine", &ep_combine, py::arg("rows"), py::arg("send_index"), py::arg("topk_w"));
+  m.def("ep_unpermute_combine", &ep_unpermute_combine, py::arg("y"), py::arg("perm_pos"), py::arg("send_index"),
+        py::arg("topk_w"));
 }

@@ -332,6 +332,13 @@ int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, i
 int cdg_ep_combine(const void* rows, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
                    int64_t H, void* y, cdg_stream_t stream);
 
+/* Fused unpermute + combine for a layer without an exchange (one rank): y[t, :] =
+ * bf16(sum_j topk_w[t, j] * Y[perm_pos[send_index[t*topk + j]], :]) in FP32, skipping -1 slots; the
+ * same values as cdg_ep_unpermute followed by cdg_ep_combine, without the intermediate rows.
+ * Replaces vLLM deepgemm_unpermute_and_reduce (fused_moe/deep_gemm_utils.py:420) for this layout. */
+int cdg_ep_unpermute_combine(const void* Y, int64_t y_stride, const int32_t* perm_pos, const int32_t* send_index,
+                             const float* topk_w, int64_t T, int64_t topk, int64_t H, void* y, cdg_stream_t stream);
+
 /* Human-readable name of a cdg_status value. */
 const char* cdg_status_string(int status);
 

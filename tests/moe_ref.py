@@ -132,6 +132,9 @@ class TorchRefOps:
         out[ok] = y[perm_pos[ok].long()]
         return out
 
+    def unpermute_combine(self, y, perm_pos, send_index, topk_w):
+        return self.combine(self.unpermute(y, perm_pos), send_index, topk_w)
+
     def combine(self, rows, send_index, topk_w):
         T, k = topk_w.shape
         y = torch.zeros(T, rows.shape[1], dtype=torch.float32)

@@ -93,8 +93,32 @@ def test_dispatch_and_permute_are_exact():
         seg = mi[int(off[e]):int(off[e]) + int(aligned[e])]
         assert int((seg == e).sum()) == int(ref_counts[e]) and bool((seg[: int(ref_counts[e])] == e).all())
     y = torch.randn(m_pad, H, generator=g).to(torch.bfloat16).to(DEV)
-    back = C.ep_unpermute(y, pos.to(torch.int32).to(DEV))
+    pos32 = pos.to(torch.int32).to(DEV)
+    back = C.ep_unpermute(y, pos32)
     assert torch.equal(back.cpu().view(torch.int16), y.cpu()[pos].view(torch.int16))
+    # weighted top-k sum: the fused unpermute + combine gives the same bits as the two steps,
+    # and both agree with the CPU reference (FP32 sums in slot order)
+    w = torch.rand(T, k, generator=g)
+    w = (w / w.sum(1, keepdim=True)).to(DEV)
+    y1 = C.ep_combine(back, send_index, w)
+    y2 = C.ep_unpermute_combine(y, pos32, send_index, w)
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    ref = TorchRefOps().combine(back.cpu(), si, w.cpu()).float()
+    assert (y1.cpu().float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+
+
+def test_combine_scalar_path_matches_vector_path():
+    """Rows whose length is not a multiple of 8 take the per-element path; on the same
+    values its columns equal the 16-byte path's, bit for bit."""
+    C = _ext()
+    T, k, R, H = 40, 3, 90, 520
+    g = torch.Generator().manual_seed(9)
+    rows = torch.randn(R, H, generator=g).to(torch.bfloat16).to(DEV)
+    send_index = torch.randint(-1, R, (T * k,), generator=g, dtype=torch.int32).to(DEV)
+    w = torch.rand(T, k, generator=g).to(DEV)
+    y_vec = C.ep_combine(rows, send_index, w)                       # H % 8 == 0: 16-byte path
+    y_sc = C.ep_combine(rows[:, :H - 4].contiguous(), send_index, w)  # 516 columns: per element
+    assert torch.equal(y_vec[:, :H - 4].view(torch.int16), y_sc.view(torch.int16))
 
 
 def test_fixed_capacity_pack_and_permute_exact():
