@@ -42,3 +42,13 @@ __all__ = [
     "set_pdl",
     "get_pdl",
 ]
+
+# Per-call timing of the public functions (CDG_PROFILE=1, reference __init__.py:58-114).
+import os as _os
+
+if _os.environ.get("CDG_PROFILE", "0") == "1":
+    import sys as _sys
+
+    from . import profile as _profile
+
+    profiler = _profile.install(_sys.modules[__name__])
