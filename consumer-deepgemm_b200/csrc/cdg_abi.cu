@@ -243,23 +243,25 @@ int make_pair_tmaps(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, const u
              : CDG_ERR_CUDA;
 }
 
-// Tensor map of cdg_gemm_planes_kernel: a 4-D view (K, token % 8, plane, token / 8) of the
-// stacked planes [2][nblk*128][K], so that one box of the 7 token groups of a CTA's half
-// tile lands in shared memory as [group][plane][8 rows] -- 8 hi rows, then the same
-// tokens' 8 lo rows, per group.
-int make_planes_tmap(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, CUtensorMap* ta) {
+// Tensor maps of cdg_gemm_planes_kernel: a 4-D view (K, token % 8, plane, token / 8) of the
+// stacked planes [2][nblk*128][K], so that a box of g token groups (one map per g = 1..7, the
+// groups of a CTA's half tile) lands in shared memory as [group][plane][8 rows] -- 8 hi rows,
+// then the same tokens' 8 lo rows, per group.
+int make_planes_tmap(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, PlaneMaps* maps) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return CDG_ERR_CUDA;
   const cuuint64_t K = static_cast<cuuint64_t>(g->K);
   cuuint64_t dims[4] = {K, 8, 2, static_cast<cuuint64_t>(nblk * 16)};
   cuuint64_t strides[3] = {K, static_cast<cuuint64_t>(nblk * 128) * K, 8 * K};
-  cuuint32_t box[4] = {128, 8, 2, kPlanesTileTok / 16};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  return enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, hilo, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
-             ? CDG_OK
-             : CDG_ERR_CUDA;
+  for (int gi = 0; gi < kPlanesTileTok / 16; ++gi) {
+    cuuint32_t box[4] = {128, 8, 2, static_cast<cuuint32_t>(gi + 1)};
+    if (enc(&maps->m[gi], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, hilo, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return CDG_ERR_CUDA;
+  }
+  return CDG_OK;
 }
 
 // Tensor maps of the wide kernels: A itself ([M rows][K] e4m3, 64 rows of one CTA per
@@ -486,7 +488,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     CUtensorMap ad, tok;
     st = make_wide_tmaps(g, tok_sf, nblk, &ad, &tok);
     if (st != CDG_OK) return st;
-    CUtensorMap planes;
+    PlaneMaps planes;
     st = make_planes_tmap(g, hilo, nblk, &planes);
     if (st != CDG_OK) return st;
     ka.list = reinterpret_cast<const int4*>(ws + wl.plane_tiles);

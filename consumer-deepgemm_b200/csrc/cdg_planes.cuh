@@ -77,8 +77,13 @@ struct PlanesSmem {
   static constexpr int kThreads = 128 + 32 * kEpiWarps;
 };
 
+// Tensor maps of the planes, one per box height: m[g - 1] brings g groups of 8 tokens.
+struct PlaneMaps {
+  CUtensorMap m[kPlanesTileTok / 16];
+};
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads, 1)
-    cdg_gemm_planes_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+    cdg_gemm_planes_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ PlaneMaps tmaps_a,
                            const __grid_constant__ CUtensorMap tmap_sfw, GemmArgs p) {
   using L = PlanesSmem;
   constexpr int S = L::kStages;
@@ -120,7 +125,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
 
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_w);
-    prefetch_tmap(&tmap_a);
+    for (int g = 0; g < kPlanesTileTok / 16; ++g) prefetch_tmap(&tmaps_a.m[g]);
     prefetch_tmap(&tmap_sfw);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -169,8 +174,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
         if (t + npairs < tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
         const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
         const int wrow = cur.z * p.N + nt * 128;
-        // plane rows of this CTA's tokens, in groups of 8
+        // plane rows of this CTA's tokens, in groups of 8; a box of just the tile's groups
         const int grp = (cur.x + static_cast<int>(rank) * tile_half(cur.y)) >> 3;
+        const int ng_cta = tile_half(cur.y) >> 3;
+        const CUtensorMap* tmap_a = &tmaps_a.m[ng_cta - 1];
+        const uint32_t tx_step = 128u * 64u + static_cast<uint32_t>(ng_cta) * 2048u;
         for (int kb0 = 0; kb0 < k_steps; kb0 += KS) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, p.status,
                                  wait_code(1, static_cast<int>(rank), stage, phase ^ 1, kb0))) {
@@ -179,11 +187,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
           }
           const int n = k_steps - kb0 < KS ? k_steps - kb0 : KS;
           const uint32_t fb = full0 + stage * 8;
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * static_cast<uint32_t>(n) * L::kTxPerStep);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * static_cast<uint32_t>(n) * tx_step);
           for (int u = 0; u < n; ++u) {
             const int kb = kb0 + u;
             tma_load_2d_pair(step_w(stage, u), &tmap_w, fb, kb * 128, wrow);
-            tma_load_4d_pair(step_a(stage, u), &tmap_a, fb, kb * 128, 0, 0, grp);
+            tma_load_4d_pair(step_a(stage, u), tmap_a, fb, kb * 128, 0, 0, grp);
           }
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
