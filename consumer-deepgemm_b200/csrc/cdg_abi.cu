@@ -19,7 +19,7 @@
 #include "cdg_kernels.cuh"
 #include "cdg_pair.cuh"
 #include "cdg_planes.cuh"
-#include "cdg_wide.cuh"
+#include "cdg_direct.cuh"
 #include "cdg_layout.h"
 
 namespace cdg {
@@ -75,8 +75,8 @@ const DeviceInfo& device_info(int dev) {
       if (cudaFuncSetAttribute(cdg_gemm_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                PlanesSmem::kBytes) != cudaSuccess)
         return;
-      if (cudaFuncSetAttribute(cdg_gemm_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               WideSmem::kBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(cdg_gemm_direct_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               DirectSmem::kBytes) != cudaSuccess)
         return;
       if (cudaFuncSetAttribute(cdg_generic_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) !=
           cudaSuccess)
@@ -264,32 +264,22 @@ int make_planes_tmap(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, PlaneM
   return CDG_OK;
 }
 
-// Tensor maps of the wide kernels: A itself ([M rows][K] e4m3, 64 rows of one CTA per
-// box; direct class) and the token scale atoms the prep kernel wrote ([nblk * K/128][128
-// words], one 512-byte atom per box).
-int make_wide_tmaps(const cdg_gemm_args* g, const uint32_t* tok_sf, int64_t nblk, CUtensorMap* ta,
-                      CUtensorMap* tsf) {
+// Tensor maps of cdg_gemm_direct_kernel: A itself ([M rows][K] e4m3), a box of 8g rows per
+// map (g = 1..14, the rows of a CTA's half tile).
+int make_direct_tmaps(const cdg_gemm_args* g, DirectMaps* maps) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return CDG_ERR_CUDA;
-  {
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(g->M)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->a_row_stride)};
-    cuuint32_t box[2] = {128, 64};
-    cuuint32_t estr[2] = {1, 1};
-    if (enc(ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g->a), dims, strides, box, estr,
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(g->M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->a_row_stride)};
+  cuuint32_t estr[2] = {1, 1};
+  for (int gi = 0; gi < kDirectTileTok / 16; ++gi) {
+    cuuint32_t box[2] = {128, static_cast<cuuint32_t>(8 * (gi + 1))};
+    if (enc(&maps->m[gi], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(g->a), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return CDG_ERR_CUDA;
   }
-  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(nblk * (g->K / 128))};
-  cuuint64_t strides[1] = {512};
-  cuuint32_t box[2] = {128, 1};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(tsf, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(tok_sf), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
-             ? CDG_OK
-             : CDG_ERR_CUDA;
+  return CDG_OK;
 }
 
 // Launch with programmatic stream serialization: the kernel may be scheduled while
@@ -430,8 +420,9 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.lists = lists;
   pa.plane_tiles = reinterpret_cast<int4*>(ws + wl.plane_tiles);
   const bool pair_path = g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2;
-  uint32_t* tok_sf = reinterpret_cast<uint32_t*>(ws + wl.tok_sf);
-  pa.tok_sf = tok_sf;
+  uint8_t* tok_code = ws + wl.tok_code;
+  pa.tok_code = tok_code;
+  pa.direct_tiles = reinterpret_cast<int4*>(ws + wl.direct_tiles);
   pa.pair_wide = pair_path ? 1 : 0;
   const dim3 prep_grid(static_cast<unsigned>(nblk), static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
   if (ids_dtype == CDG_DTYPE_I64)
@@ -450,6 +441,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.ctrl = ctrl;
   ka.sfw_atoms = sfw;
   ka.row_exp = row_exp;
+  ka.tok_code = tok_code;
   ka.d = static_cast<__nv_bfloat16*>(g->d);
   ka.d_row_stride = g->d_row_stride;
   ka.M = static_cast<int>(g->M);
@@ -468,7 +460,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     // CTA pairs (tcgen05 cta_group::2): two adjacent 128-column tiles per cluster; four MMA
     // issuers for tiny blocks, two for narrow; wide blocks in token tiles of the plane kernel
     // (cdg_gemm_planes_kernel), or, when their scales are powers of two, in
-    // cdg_gemm_wide_kernel on the raw rows (direct class).
+    // token tiles of cdg_gemm_direct_kernel on the raw rows (direct class).
     CUtensorMap p16, p32, tsf;
     st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &tsf);
     if (st != CDG_OK) return st;
@@ -485,9 +477,6 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     if (launch_pdl(cdg_gemm_pair_kernel<32, 2>, grid, PairSmem<32, 2>::kThreads, PairSmem<32, 2>::kBytes, stream, tw,
                    p32, tsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
-    CUtensorMap ad, tok;
-    st = make_wide_tmaps(g, tok_sf, nblk, &ad, &tok);
-    if (st != CDG_OK) return st;
     PlaneMaps planes;
     st = make_planes_tmap(g, hilo, nblk, &planes);
     if (st != CDG_OK) return st;
@@ -497,10 +486,13 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
                    ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     // Wide blocks whose activation scales are all powers of two: raw e4m3 rows.
-    ka.list = lists + kClassWideDirect * nblk;
-    ka.count_slot = kCtrlCount0 + kClassWideDirect;
-    if (launch_pdl(cdg_gemm_wide_kernel, grid, WideSmem::kThreads, WideSmem::kBytes, stream, tw,
-                   ad, tsf, tok, ka) != cudaSuccess)
+    DirectMaps direct;
+    st = make_direct_tmaps(g, &direct);
+    if (st != CDG_OK) return st;
+    ka.list = reinterpret_cast<const int4*>(ws + wl.direct_tiles);
+    ka.count_slot = kCtrlDirectTiles;
+    if (launch_pdl(cdg_gemm_direct_kernel, grid, DirectSmem::kThreads, DirectSmem::kBytes, stream, tw, direct, tsf,
+                   ka) != cudaSuccess)
       return CDG_ERR_CUDA;
   } else {
     // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.

@@ -115,9 +115,9 @@ struct PrepArgs {
   int nblk;
   TileMap tm;              // rows of each block
   uint8_t* hilo;           // [2][nblk*128][K]
-  uint32_t* tok_sf;        // [nblk][K/128][128] words: token scale atoms of wide blocks (CTA-pair path)
-  int pair_wide;           // wide blocks run cdg_gemm_wide_kernel: write their token scale atoms, and
-                           // blocks whose scales are all powers of two take the direct class
+  uint8_t* tok_code;       // [M][tok_code_pitch(K)] UE8M0 code of each direct-class row's activation scale
+  int pair_wide;           // wide blocks run on the CTA-pair path (token tiles of the planes kernel, or
+                           // of the direct kernel when their scales are all powers of two)
   int32_t* row_exp;        // [nblk*128] exponent E of each routed row's activation planes
   int4* blk_info;          // [nblk] {expert (-1 none, -2 several), rows spanned, class, 0}
   uint4* blk_mask;         // [nblk] bit r set when row r of the block has the block's expert
@@ -125,6 +125,7 @@ struct PrepArgs {
   int4* lists;             // [kNumClasses][nblk] {block, expert, rows spanned, 0}
   int4* plane_tiles;       // [2*nblk] tiles of cdg_gemm_planes_kernel (pair_wide only):
                            // {first plane row, rows, expert, 1 on the last tile of a run}
+  int4* direct_tiles;      // [nblk] tiles of cdg_gemm_direct_kernel, the same form
 };
 
 // 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
@@ -182,6 +183,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ uint32_t s_smax_bits[128];     // bits of the largest finite |bf16(sa)| of each row
   __shared__ int s_cls_count[kNumClasses][257];
   __shared__ int s_tile_count[257];
+  __shared__ int s_dtile_count[257];
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   if (tid == 0) {
@@ -298,20 +300,20 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     const int kbn = min(kPrepK / 128, kb_count - kb0);
     const int64_t plane = static_cast<int64_t>(p.nblk) * 128 * K;
     // Direct class: a wide block (CTA-pair path) whose routed rows' scales are all powers
-    // of two.  Its token scale atoms: this CTA's K blocks' 512-byte UE8M0 atoms (row r's
-    // byte at (r%32)*16 + (r/32)*4 + c, the same byte 2^s for the four 32-wide sub-blocks c).  The
-    // reference's bf16(bf16(a) * bf16(2^s)) is then the exact product a * 2^s, which the
-    // tensor core forms itself from the raw e4m3 rows with 2^s as scale factor: no planes,
-    // one MMA per K slice.
+    // of two.  The reference's bf16(bf16(a) * bf16(2^s)) is then the exact product a * 2^s,
+    // which the tensor core forms itself from the raw e4m3 rows with 2^s as scale factor: no
+    // planes, one MMA per K slice.  The UE8M0 code of every row of the block (127 for rows
+    // without its expert) goes to tok_code (row major, one byte per K block), for this CTA's
+    // K blocks.
     const bool direct = cls == kClassWide && p.pair_wide && s_pow2;
     if (direct) {
-      for (int it = tid; it < kbn * 128; it += blockDim.x) {
-        const int kl = it >> 7, rr = it & 127;
+      const int pitch = tok_code_pitch(K);
+      for (int it = tid; it < kbn * nrows; it += blockDim.x) {
+        const int rr = it / kbn, kl = it - rr * kbn;
         int code = 127;
         if (s_id[rr] == expert)
           code = pow2_code(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb0 + kl));
-        p.tok_sf[(static_cast<int64_t>(b) * kb_count + kb0 + kl) * 128 + (rr & 31) * 4 + (rr >> 5)] =
-            static_cast<uint32_t>(code) * 0x01010101u;
+        p.tok_code[static_cast<int64_t>(row0 + rr) * pitch + kb0 + kl] = static_cast<uint8_t>(code);
       }
     }
     if (direct) {
@@ -384,10 +386,10 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   // A run of S rows is cut into the fewest tiles, n = ceil(S / kPlanesTileTok), of
   // T = ceil16(S / n) rows each (the last one shorter): a tile costs the kernel about the
   // same time at any width, so fewer tiles is faster, and equal widths spread the MMA work.
-  auto continues = [&](int i) -> bool {  // block i extends the run of block i - 1
+  auto continues = [&](int i) -> bool {  // block i extends the run of block i - 1 (same class)
     if (i == 0) return false;
     const int4 a = __ldcg(&p.blk_info[i - 1]), c = __ldcg(&p.blk_info[i]);
-    if (a.z != kClassWide || c.z != kClassWide || a.x != c.x || a.y != 128) return false;
+    if ((c.z != kClassWide && c.z != kClassWideDirect) || a.z != c.z || a.x != c.x || a.y != 128) return false;
     int r0a, na, r0c, nc;
     p.tm.rows(i - 1, r0a, na);
     p.tm.rows(i, r0c, nc);
@@ -400,36 +402,41 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   };
   static_assert(kPlanesTileTok % 16 == 0, "tile cuts at multiples of 16 rows");
   int cnt[kNumClasses] = {};
-  int ntiles = 0;
+  int ntiles = 0, dtiles = 0;
   for (int i = lo; i < hi; ++i) {
     const int c = __ldcg(&p.blk_info[i].z);
     cnt[c]++;
     if (p.pair_wide && c == kClassWide && !continues(i)) ntiles += (run_span(i) + kPlanesTileTok - 1) / kPlanesTileTok;
+    if (p.pair_wide && c == kClassWideDirect && !continues(i))
+      dtiles += (run_span(i) + kDirectTileTok - 1) / kDirectTileTok;
   }
 #pragma unroll
   for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][tid + 1] = cnt[c];
   s_tile_count[tid + 1] = ntiles;
+  s_dtile_count[tid + 1] = dtiles;
   if (tid == 0) {
 #pragma unroll
     for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][0] = 0;
     s_tile_count[0] = 0;
+    s_dtile_count[0] = 0;
   }
   __syncthreads();
-  if (tid <= kNumClasses) {  // thread kNumClasses scans the tile counts
-    int* cs = tid < kNumClasses ? s_cls_count[tid] : s_tile_count;
+  if (tid <= kNumClasses + 1) {  // threads kNumClasses, kNumClasses + 1 scan the tile counts
+    int* cs = tid < kNumClasses ? s_cls_count[tid] : tid == kNumClasses ? s_tile_count : s_dtile_count;
     int run = 0;
     for (int t = 0; t <= static_cast<int>(blockDim.x); ++t) {
       const int v = cs[t];
       cs[t] = run;
       run += v;
     }
-    p.ctrl[tid < kNumClasses ? kCtrlCount0 + tid : kCtrlPlaneTiles] = run;
+    p.ctrl[tid < kNumClasses ? kCtrlCount0 + tid : tid == kNumClasses ? kCtrlPlaneTiles : kCtrlDirectTiles] = run;
   }
   __syncthreads();
   int pos[kNumClasses];
 #pragma unroll
   for (int c = 0; c < kNumClasses; ++c) pos[c] = s_cls_count[c][tid + 1];
   int tpos = s_tile_count[tid + 1];
+  int dpos = s_dtile_count[tid + 1];
   for (int i = lo; i < hi; ++i) {
     const int c = __ldcg(&p.blk_info[i].z);
     const int4 info = __ldcg(&p.blk_info[i]);
@@ -442,6 +449,16 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
         const int o = k * tile;
         const int e = k + 1 == n ? span : o + tile;
         p.plane_tiles[tpos++] = make_int4(i * 128 + o, e - o, info.x, k + 1 == n ? 1 : 0);
+      }
+    }
+    if (p.pair_wide && c == kClassWideDirect && !continues(i)) {
+      const int span = run_span(i);
+      const int n = (span + kDirectTileTok - 1) / kDirectTileTok;
+      const int tile = ((span + n - 1) / n + 15) & ~15;
+      for (int k = 0; k < n; ++k) {
+        const int o = k * tile;
+        const int e = k + 1 == n ? span : o + tile;
+        p.direct_tiles[dpos++] = make_int4(i * 128 + o, e - o, info.x, k + 1 == n ? 1 : 0);
       }
     }
   }
@@ -477,6 +494,7 @@ struct GemmArgs {
   const int4* zero_list;  // all-padding blocks (zero-filled by the kernel with do_zero_blocks)
   const uint32_t* sfw_atoms;  // [E][N/128][K/128][128] words
   const int32_t* row_exp;     // [nblk*128] per-row exponent of the activation planes
+  const uint8_t* tok_code;    // [M][tok_code_pitch(K)] UE8M0 activation scale codes of direct-class rows
   __nv_bfloat16* d;
   int64_t d_row_stride;
   int M, N, K, E, nblk;

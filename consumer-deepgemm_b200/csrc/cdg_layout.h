@@ -24,6 +24,11 @@ constexpr int kNarrowTok = 32;
 // Tokens per tile of cdg_gemm_planes_kernel: runs of consecutive wide blocks of one expert
 // are cut into tiles of this many rows (two accumulators of N = 2 x 112 fill TMEM).
 constexpr int kPlanesTileTok = 112;
+// Tokens per tile of cdg_gemm_direct_kernel (one plane: N = 224).
+constexpr int kDirectTileTok = 224;
+// Bytes per row of the direct class's activation scale codes: one per 128-wide K block,
+// rounded up to 4 so that four consecutive K blocks of a row are one aligned 32-bit word.
+__host__ __device__ constexpr int tok_code_pitch(int K) { return ((K / 128) + 3) & ~3; }
 
 // Control words at the start of the workspace (int32 slots, zeroed before each call).
 enum : int {
@@ -31,6 +36,7 @@ enum : int {
   kCtrlCount0 = 1,  // kCtrlCount0 + class = number of blocks in that class
   kCtrlPlaneTiles = 7,  // number of tiles in the planes kernel's tile list
   kCtrlStatus = 8,  // device status bits (kStatus*); kCtrlStatus + 1: code of the first wait that gave up
+  kCtrlDirectTiles = 10,  // number of tiles in the direct kernel's tile list
   kCtrlWords = 64,
 };
 
@@ -79,8 +85,8 @@ struct TileMap {
 
 // Workspace regions of one GEMM call.
 struct WorkspaceLayout {
-  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, plane_tiles = 0, row_ids = 0, row_exp = 0, hilo = 0,
-         tok_sf = 0, sfw_atoms = 0, total = 0;
+  size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, plane_tiles = 0, direct_tiles = 0, row_ids = 0, row_exp = 0,
+         hilo = 0, tok_code = 0, sfw_atoms = 0, total = 0;
 
   static WorkspaceLayout make(int64_t M, int64_t nblk, int64_t K, int64_t N, int64_t E, bool fast, bool row_ids,
                               bool sfw_from_rows) {
@@ -96,6 +102,8 @@ struct WorkspaceLayout {
     off = align_up(off + static_cast<size_t>(nblk) * 16 * kNumClasses, 1024);
     w.plane_tiles = off;  // at most one tile per 112 rows of a run plus one per run: 2 per block
     off = align_up(off + static_cast<size_t>(nblk) * 2 * 16, 1024);
+    w.direct_tiles = off;  // tiles of up to 224 rows: at most one per block
+    off = align_up(off + static_cast<size_t>(nblk) * 16, 1024);
     if (row_ids) {
       w.row_ids = off;
       off = align_up(off + static_cast<size_t>(M) * 4, 1024);
@@ -105,8 +113,8 @@ struct WorkspaceLayout {
       off = align_up(off + static_cast<size_t>(nblk) * 128 * 4, 1024);
       w.hilo = off;
       off = align_up(off + static_cast<size_t>(2) * nblk * 128 * K, 1024);
-      w.tok_sf = off;  // [nblk][K/128] 512-byte activation scale atoms of direct blocks
-      off = align_up(off + static_cast<size_t>(nblk) * (K / 128) * 512, 1024);
+      w.tok_code = off;  // [M][tok_code_pitch(K)] UE8M0 activation scale codes of the direct class's rows
+      off = align_up(off + static_cast<size_t>(tok_code_pitch(K)) * static_cast<size_t>(M), 1024);
       if (sfw_from_rows) {
         w.sfw_atoms = off;
         off = align_up(off + static_cast<size_t>(E) * ((N + 127) / 128) * (K / 128) * 512, 1024);

@@ -25,7 +25,8 @@
 // `tfull` barriers of both CTAs (tcgen05.commit multicast); each epilogue thread of
 // both CTAs drains its own TMEM lanes (its CTA's 128 output columns) and arrives on
 // the even CTA's `tempty` barrier.  All waits are bounded (kStatusTimeout).  Wide
-// blocks (more than 32 rows) run cdg_gemm_wide_kernel instead.
+// blocks (more than 32 rows) run the token-tile kernels instead (cdg_gemm_planes_kernel,
+// cdg_gemm_direct_kernel).
 //
 // Warp roles per CTA: 0 = TMA producer, 1..NI = MMA issuers (even CTA; warp 1 also
 // owns TMEM), then four epilogue warps (4-7, or 5-8 when NI = 4).

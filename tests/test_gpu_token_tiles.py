@@ -4,10 +4,11 @@ Wide blocks with FP32 activation scales run the plane kernel on token tiles: the
 kernel joins the consecutive wide blocks of one expert into runs and cuts each run into
 tiles of at most 112 rows, which may cross block boundaries; the last block of an expert
 that spans several blocks joins the wide class whatever its row count.  With power-of-two
-scales the same blocks run the direct-class kernel, one block per tile.  The cases below
-cover runs of one to three blocks, tiles crossing a block boundary, runs that end one row
-into a block, experts without rows, odd numbers of 128-wide K steps (a partial pipeline
-stage and a partial scale-atom stage) and a masked layout whose groups span blocks.  All
+scales the same blocks run the direct-class kernel on tiles of at most 224 rows (a tile may
+then touch three blocks).  The cases below cover runs of one to five blocks, tiles crossing
+one or two block boundaries, runs that end one row into a block, experts without rows, odd
+numbers of 128-wide K steps (a partial pipeline stage and a partial scale-atom stage) and a
+masked layout whose groups span blocks.  All
 outputs are compared with the CPU oracle over every row, with the golden cases'
 tolerances; rows outside every group must be exact zeros.
 """
@@ -84,13 +85,29 @@ def test_runs_across_blocks(k, pow2):
         assert cls["wide"] == 8 and cls["wide_direct"] == 0, cls
 
 
-def test_masked_groups_span_blocks():
+@pytest.mark.parametrize("k", [512, 1152], ids=["k512", "k1152"])
+@pytest.mark.parametrize("pow2", [False, True], ids=["planes", "direct"])
+def test_long_runs(k, pow2):
+    # five blocks of one expert (direct tiles of 224 rows: the middle one touches three blocks),
+    # then runs of 449 and 257 rows
+    counts = [640, 449, 257]
+    a, sa, ids = _contiguous(counts, k, pow2, seed=k + 1)
+    b, sb = synthetic.make_weights(len(counts), 256, k, "cpu", seed=4)
+    cls = _check(a, sa, b, sb, ids)
+    assert cls["wide_direct" if pow2 else "wide"] == 5 + 4 + 3, cls
+
+
+@pytest.mark.parametrize("pow2", [False, True], ids=["planes", "direct"])
+def test_masked_groups_span_blocks(pow2):
     # masked layout: 3 groups of 300 rows each (blocks of 128, 128 and 44 rows per group)
     e, seg, k = 3, 300, 512
     counts = torch.tensor([300, 200, 129], dtype=torch.int32)
     g = torch.Generator().manual_seed(11)
     x = torch.randn(e * seg, k, generator=g).to(torch.bfloat16).float()
     a, sa = per_block_cast_to_fp8(x)
+    if pow2:
+        sa = torch.exp2(torch.ceil(torch.log2(sa)))
+        a = (x.view(e * seg, k // 128, 128) / sa.unsqueeze(-1)).view(e * seg, k).to(torch.float8_e4m3fn)
     b, sb = synthetic.make_weights(e, 256, k, "cpu", seed=5)
     cls = _check(a, sa, b, sb, counts, masked=True)
-    assert cls["wide"] >= 6, cls
+    assert cls["wide_direct" if pow2 else "wide"] >= 6, cls
