@@ -265,10 +265,22 @@ int make_planes_tmap(const cdg_gemm_args* g, uint8_t* hilo, int64_t nblk, PlaneM
 }
 
 // Tensor maps of cdg_gemm_direct_kernel: A itself ([M rows][K] e4m3), a box of 8g rows per
-// map (g = 1..14, the rows of a CTA's half tile).
-int make_direct_tmaps(const cdg_gemm_args* g, DirectMaps* maps) {
+// map (g = 1..14, the rows of a CTA's half tile), and the token scale atoms
+// ([tiles * K/512 * 2][128 words], two 512-byte atoms per box).
+int make_direct_tmaps(const cdg_gemm_args* g, uint32_t* tok_atoms, int64_t nblk, DirectMaps* maps,
+                      CUtensorMap* tsf) {
   EncodeTiledFn enc = encode_tiled();
   if (!enc) return CDG_ERR_CUDA;
+  {
+    cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(nblk * (tok_code_pitch(static_cast<int>(g->K)) / 4) * 2)};
+    cuuint64_t strides[1] = {512};
+    cuuint32_t box[2] = {128, 2};
+    cuuint32_t estr[2] = {1, 1};
+    if (enc(tsf, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, tok_atoms, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return CDG_ERR_CUDA;
+  }
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(g->K), static_cast<cuuint64_t>(g->M)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(g->a_row_stride)};
   cuuint32_t estr[2] = {1, 1};
@@ -442,6 +454,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.sfw_atoms = sfw;
   ka.row_exp = row_exp;
   ka.tok_code = tok_code;
+  ka.tok_atoms = reinterpret_cast<uint32_t*>(ws + wl.tok_atoms);
   ka.d = static_cast<__nv_bfloat16*>(g->d);
   ka.d_row_stride = g->d_row_stride;
   ka.M = static_cast<int>(g->M);
@@ -465,6 +478,11 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &tsf);
     if (st != CDG_OK) return st;
     const unsigned grid = static_cast<unsigned>(di.sm_count / 2 * 2);
+    // token scale atoms of the direct tiles, for cdg_gemm_direct_kernel
+    ka.list = reinterpret_cast<const int4*>(ws + wl.direct_tiles);
+    if (launch_pdl(cdg_direct_atoms_kernel, static_cast<unsigned>(std::min<int64_t>(nblk, 2 * di.sm_count)), 256, 0,
+                   stream, ka) != cudaSuccess)
+      return CDG_ERR_CUDA;
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = skip_ungrouped ? 0 : 1;
@@ -487,12 +505,13 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
       return CDG_ERR_CUDA;
     // Wide blocks whose activation scales are all powers of two: raw e4m3 rows.
     DirectMaps direct;
-    st = make_direct_tmaps(g, &direct);
+    CUtensorMap dtsf;
+    st = make_direct_tmaps(g, ka.tok_atoms, nblk, &direct, &dtsf);
     if (st != CDG_OK) return st;
     ka.list = reinterpret_cast<const int4*>(ws + wl.direct_tiles);
     ka.count_slot = kCtrlDirectTiles;
     if (launch_pdl(cdg_gemm_direct_kernel, grid, DirectSmem::kThreads, DirectSmem::kBytes, stream, tw, direct, tsf,
-                   ka) != cudaSuccess)
+                   dtsf, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
   } else {
     // Tiny blocks (decode: at most 16 routed rows) and all-padding blocks.

@@ -15,23 +15,26 @@
 // by one 2-D box of 8g rows of A per K step (one tensor map per g = h / 8).
 //
 // Token scale factors.  The prep kernel writes one UE8M0 code per (row, 128-wide K block),
-// row major with four K blocks per aligned 32-bit word.  For each scale stage of kKSF = 4 K
-// steps a producer warp builds two 512-byte scale atoms per CTA (tokens 0-127 and 128-255:
-// token n at byte (n%32)*16 + ((n%128)/32)*4 of atom n/128) whose byte j is the code of
-// K step j of the stage, so one 8-column TMEM set holds the token scales of four K steps and
-// the MMA of K step j selects byte j (b_sf_id).  The weight scale atoms (one per K step, byte
-// = 32-wide K slice) travel in the same ring, by TMA.  A copier thread moves both into TMEM
-// (tcgen05.cp) as soon as the MMAs that used the TMEM slot last completed.
+// row major with four K blocks per aligned 32-bit word; cdg_direct_atoms_kernel then writes,
+// per tile and scale stage of kKSF = 4 K steps, two 512-byte scale atoms (tokens 0-127 and
+// 128-255: token n at byte (n%32)*16 + ((n%128)/32)*4 of atom n/128) whose byte j is the
+// code of K step j of the stage.  One 8-column TMEM set then holds the token scales of four
+// K steps and the MMA of K step j selects byte j (b_sf_id).  The token atoms and the weight
+// scale atoms (one per K step, byte = 32-wide K slice) travel by TMA in a shared-memory ring
+// of their own, and a copier thread moves them into TMEM (tcgen05.cp) as soon as the MMAs
+// that used the TMEM slot last completed.  TMEM holds two scale stages, the shared-memory
+// ring four, so the loads run well ahead of the copies.  (Atoms built inside this kernel
+// from the per-row codes put the codes' global-load latency on the scale ring's critical
+// path: the MMA issuer then waited for its scale stage about a third of the time.)
 //
 // TMEM: two accumulators of 224 columns (the epilogue drains one while the MMAs fill the
-// other), 2 stages x 4 K steps x 4 weight scale columns, 2 stages x 8 token scale columns:
+// other), 2 slots x 4 K steps x 4 weight scale columns, 2 slots x 8 token scale columns:
 // 496 of 512 columns.
 //
 // Warp roles per CTA: 0 = operand TMA producer, 1 = MMA issuer (even CTA, whole warp) and
-// TMEM owner, 2 = scale-factor copier (even CTA, whole warp), 3 = scale-atom producer (whole
-// warp: weight atoms by TMA, token atoms built in shared memory), 4-11 = epilogue (two warps
-// per TMEM lane quadrant, each taking every other 16-token chunk).  All waits are bounded
-// (kStatusTimeout).
+// TMEM owner, 2 = scale-factor copier (even CTA, whole warp), 3 = scale-atom TMA producer,
+// 4-11 = epilogue (two warps per TMEM lane quadrant, each taking every other 16-token
+// chunk).  All waits are bounded (kStatusTimeout).
 #pragma once
 
 #include "cdg_kernels.cuh"
@@ -45,15 +48,16 @@ struct DirectSmem {
   static constexpr int kA = kDirectTileTok / 2 * 128;  // 112 token rows per K step
   static constexpr int kStep = kW + kA;
   static constexpr int kStages = 3;
-  static constexpr int kSfStages = 2;
+  static constexpr int kSfStages = 4;   // scale stages in shared memory
+  static constexpr int kSfSlots = 2;    // scale stages in TMEM
   static constexpr int kStageBytes = kKS * kStep;
   static constexpr int kSfRing = kStages * kStageBytes;              // [kSfStages][kKSF] weight scale atoms
   static constexpr int kTsfRing = kSfRing + kSfStages * kKSF * 512;  // [kSfStages][2] token scale atoms
   static constexpr int kEpiWarps = 8;                                // two per TMEM lane quadrant
   static constexpr int kStaging = kTsfRing + kSfStages * 2 * 512;    // kEpiWarps x [16 tokens][32 columns] bf16
   static constexpr int kBarOffset = kStaging + kEpiWarps * 1024;
-  // full, empty; sffull, sfready, sftfree; tfull[2], tempty[2], done
-  static constexpr int kNumBars = 2 * kStages + 3 * kSfStages + 5;
+  // full, empty; sffull, sfsfree; sfready, sftfree; tfull[2], tempty[2], done
+  static constexpr int kNumBars = 2 * kStages + 2 * kSfStages + 2 * kSfSlots + 5;
   static constexpr int kBarBytes = kNumBars * 8 + 16;                // + TMEM address
   static constexpr int kBytes = kBarOffset + kBarBytes + 1024;      // + alignment slack
   static_assert(kBytes <= 232448, "shared memory per CTA");
@@ -63,8 +67,8 @@ struct DirectSmem {
   // TMEM: two accumulators of kDirectTileTok columns, the weight and token scale rings
   static constexpr uint32_t kAccCols = kDirectTileTok;
   static constexpr uint32_t kSfwCol = 2 * kAccCols;
-  static constexpr uint32_t kTsfCol = kSfwCol + kSfStages * kKSF * 4;
-  static_assert(kTsfCol + kSfStages * 8 <= 512, "TMEM columns");
+  static constexpr uint32_t kTsfCol = kSfwCol + kSfSlots * kKSF * 4;
+  static_assert(kTsfCol + kSfSlots * 8 <= 512, "TMEM columns");
   static constexpr int kThreads = 128 + 32 * kEpiWarps;
 };
 
@@ -73,12 +77,38 @@ struct DirectMaps {
   CUtensorMap m[kDirectTileTok / 16];
 };
 
+// Token scale atoms of the direct tiles: for tile i (list order) and scale stage st, the
+// 1024 bytes at tok_atoms + (i * stages + st) * 256 words.  One thread per token slot n
+// (0..255) and stage: word (n/128)*128 + (n%32)*4 + (n%128)/32 holds the codes of the four
+// K steps of the stage, 127 (scale 1) for slots past the tile.
+__global__ void __launch_bounds__(256) cdg_direct_atoms_kernel(GemmArgs p) {
+  grid_dependency_wait();  // the tile list and the codes come from the prep kernel
+  grid_launch_dependents();
+  const int count = __ldcg(&p.ctrl[kCtrlDirectTiles]);
+  const int pitch = tok_code_pitch(p.K);
+  const int stages = pitch / 4;
+  const int n = threadIdx.x;
+  const int slot = (n >> 7) * 128 + (n & 31) * 4 + ((n & 127) >> 5);
+  for (int i = blockIdx.x; i < count; i += gridDim.x) {
+    const int4 cur = __ldcg(&p.list[i]);
+    int brow0, bn;
+    p.tm.rows(cur.x >> 7, brow0, bn);
+    const int row = brow0 + (cur.x & 127) + n;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.tok_code + static_cast<int64_t>(row) * pitch);
+    uint32_t* dst = p.tok_atoms + static_cast<int64_t>(i) * stages * 256 + slot;
+#pragma unroll 4
+    for (int st = 0; st < stages; ++st) dst[st * 256] = n < cur.y ? __ldcg(src + st) : 0x7F7F7F7Fu;
+  }
+}
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads, 1)
     cdg_gemm_direct_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ DirectMaps tmaps_a,
-                           const __grid_constant__ CUtensorMap tmap_sfw, GemmArgs p) {
+                           const __grid_constant__ CUtensorMap tmap_sfw, const __grid_constant__ CUtensorMap tmap_tsf,
+                           GemmArgs p) {
   using L = DirectSmem;
   constexpr int S = L::kStages;
-  constexpr int RS = L::kSfStages;
+  constexpr int SR = L::kSfStages;
+  constexpr int RS = L::kSfSlots;
   constexpr int KS = L::kKS;
   constexpr int KSF = L::kKSF;
   constexpr uint32_t kTmemCols = 512;
@@ -104,8 +134,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* full = bars;                // [S] even CTA: both CTAs' operand copies of a stage landed
   uint64_t* empty = bars + S;           // [S] stage consumed (multicast by the MMA commit)
-  uint64_t* sffull = bars + 2 * S;      // [RS] even CTA: both CTAs' scale atoms of a stage are in place
-  uint64_t* sfready = sffull + RS;      // [RS] the stage's scale atoms are in TMEM (multicast)
+  uint64_t* sffull = bars + 2 * S;      // [SR] even CTA: both CTAs' scale atoms of a stage are in place
+  uint64_t* sfsfree = sffull + SR;      // [SR] the copies out of the shared-memory stage completed (multicast)
+  uint64_t* sfready = sfsfree + SR;     // [RS] even CTA: the TMEM slot holds its scale stage
   uint64_t* sftfree = sfready + RS;     // [RS] even CTA: the MMAs that read the TMEM slot completed
   uint64_t* tfull = sftfree + RS;       // [2] accumulator complete (multicast)
   uint64_t* tempty = tfull + 2;         // [2] even CTA: all epilogue threads of the pair drained it
@@ -119,14 +150,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
     prefetch_tmap(&tmap_w);
     for (int g = 0; g < kDirectTileTok / 16; ++g) prefetch_tmap(&tmaps_a.m[g]);
     prefetch_tmap(&tmap_sfw);
+    prefetch_tmap(&tmap_tsf);
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    for (int s = 0; s < SR; ++s) {
+      mbar_init(&sffull[s], 1);
+      mbar_init(&sfsfree[s], 1);
+    }
     for (int s = 0; s < RS; ++s) {
-      // even CTA's arrive with the weight atoms' byte count, odd CTA's arrive once its token
-      // atoms are written
-      mbar_init(&sffull[s], 2);
       mbar_init(&sfready[s], 1);
       mbar_init(&sftfree[s], 1);
     }
@@ -192,50 +225,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
       }
     }
   } else if (warp == 3) {
-    // ------------------------------------------------------------ scale-atom producer (both CTAs, whole warp)
-    int sfs = 0;
-    uint32_t sfphase = 0;
-    const uint32_t sffull0 = cluster_addr(&sffull[0], 0);
-    const int pitch = tok_code_pitch(p.K);
-    for (int t = pair; t < tiles && ok; t += npairs) {
-      const int4 cur = __ldg(&p.list[t / n_pt]);
-      const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
-      const int atom0 = (cur.z * n_tiles + nt) * k_steps;
-      const int row0 = tile_row0(cur.x);
-      for (int kb0 = 0; kb0 < k_steps; kb0 += KSF) {
-        // this lane's token scale words: tokens lane + 32j of each atom, four K steps per word
-        // (loaded before the wait, so that their latency overlaps it); tokens past the tile
-        // are never stored, their scale is 1
-        uint32_t wv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int tok = j * 32 + lane;
-          wv[j] = tok < cur.y ? __ldg(reinterpret_cast<const uint32_t*>(
-                                    p.tok_code + static_cast<int64_t>(row0 + tok) * pitch + kb0))
-                              : 0x7F7F7F7Fu;
-        }
-        // the copies out of this slot (RS stages ago) completed
-        if (!mbar_wait_cluster_warp(&sfready[sfs], sfphase ^ 1, p.status,
-                                    wait_code(7, static_cast<int>(rank), sfs, sfphase ^ 1, kb0))) {
-          ok = false;
-          break;
-        }
-        const int n = k_steps - kb0 < KSF ? k_steps - kb0 : KSF;
-        const uint32_t fb = sffull0 + sfs * 8;
-        if (lane == 0)
+    // ------------------------------------------------------------ scale-atom TMA producer (both CTAs)
+    if (lane == 0) {
+      int sfs = 0;
+      uint32_t sfphase = 0;
+      const uint32_t sffull0 = cluster_addr(&sffull[0], 0);
+      const int stages = (k_steps + KSF - 1) / KSF;
+      for (int t = pair; t < tiles && ok; t += npairs) {
+        const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
+        const int expert = __ldg(&p.list[t / n_pt]).z;
+        const int atom0 = (expert * n_tiles + nt) * k_steps;
+        const int tatom0 = (t / n_pt) * stages * 2;  // the tile's token atoms, two per stage
+        for (int kb0 = 0, st = 0; kb0 < k_steps; kb0 += KSF, ++st) {
+          // the copies out of this stage (SR stages ago) completed
+          if (!mbar_wait_cluster(&sfsfree[sfs], sfphase ^ 1, p.status,
+                                 wait_code(7, static_cast<int>(rank), sfs, sfphase ^ 1, kb0))) {
+            ok = false;
+            break;
+          }
+          const int n = k_steps - kb0 < KSF ? k_steps - kb0 : KSF;
+          const uint32_t fb = sffull0 + sfs * 8;
+          if (rank == 0) mbar_arrive_expect_tx(&sffull[sfs], 2u * (static_cast<uint32_t>(n) * 512u + 1024u));
           for (int u = 0; u < n; ++u) tma_load_2d_pair(step_sfw(sfs, u), &tmap_sfw, fb, 0, atom0 + kb0 + u);
-        uint4* ts = reinterpret_cast<uint4*>(step_tsf(sfs));
-        ts[lane] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        ts[32 + lane] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
-        fence_proxy_async_shared();  // the token atoms are read by tcgen05.cp (async proxy)
-        __syncwarp();
-        if (lane == 0) {
-          if (rank == 0)
-            mbar_arrive_expect_tx(&sffull[sfs], 2u * static_cast<uint32_t>(n) * 512u);
-          else
-            mbar_arrive_cluster(fb);
+          tma_load_2d_pair(step_tsf(sfs), &tmap_tsf, fb, 0, tatom0 + 2 * st);
+          if (++sfs == SR) { sfs = 0; sfphase ^= 1; }
         }
-        if (++sfs == RS) { sfs = 0; sfphase ^= 1; }
       }
     }
   } else if (warp == 1) {
@@ -306,24 +320,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
   } else if (warp == 2) {
     // ------------------------------------------------------------ scale-factor copier (even CTA, whole warp)
     if (rank == 0) {
-      int sfs = 0;
-      uint32_t sfphase = 0;
+      int ss = 0, ts = 0;  // shared-memory stage, TMEM slot
+      uint32_t ssphase = 0, tsphase = 0;
       for (int t = pair; t < tiles && ok; t += npairs) {
         for (int kb0 = 0; kb0 < k_steps; kb0 += KSF) {
-          if (!mbar_wait_cluster_warp(&sffull[sfs], sfphase, p.status, wait_code(6, 0, sfs, sfphase, kb0)) ||
-              !mbar_wait_cluster_warp(&sftfree[sfs], sfphase ^ 1, p.status, wait_code(6, 1, sfs, sfphase ^ 1, kb0))) {
+          if (!mbar_wait_cluster_warp(&sffull[ss], ssphase, p.status, wait_code(6, 0, ss, ssphase, kb0)) ||
+              !mbar_wait_cluster_warp(&sftfree[ts], tsphase ^ 1, p.status, wait_code(6, 1, ts, tsphase ^ 1, kb0))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const int n = k_steps - kb0 < KSF ? k_steps - kb0 : KSF;
           for (int u = 0; u < n; ++u)
-            tc_cp_sf_atom_pair_warp(tmem_base + L::kSfwCol + (sfs * KSF + u) * 4,
-                                    smem_desc_sf(smem_u32(step_sfw(sfs, u))));
-          tc_cp_sf_atom_pair_warp(tmem_base + L::kTsfCol + sfs * 8, smem_desc_sf(smem_u32(step_tsf(sfs))));
-          tc_cp_sf_atom_pair_warp(tmem_base + L::kTsfCol + sfs * 8 + 4, smem_desc_sf(smem_u32(step_tsf(sfs) + 512)));
-          tc_commit_pair_warp(&sfready[sfs], 0x3);
-          if (++sfs == RS) { sfs = 0; sfphase ^= 1; }
+            tc_cp_sf_atom_pair_warp(tmem_base + L::kSfwCol + (ts * KSF + u) * 4,
+                                    smem_desc_sf(smem_u32(step_sfw(ss, u))));
+          tc_cp_sf_atom_pair_warp(tmem_base + L::kTsfCol + ts * 8, smem_desc_sf(smem_u32(step_tsf(ss))));
+          tc_cp_sf_atom_pair_warp(tmem_base + L::kTsfCol + ts * 8 + 4, smem_desc_sf(smem_u32(step_tsf(ss) + 512)));
+          tc_commit_pair_warp(&sfready[ts], 0x1);
+          tc_commit_pair_warp(&sfsfree[ss], 0x3);
+          if (++ss == SR) { ss = 0; ssphase ^= 1; }
+          if (++ts == RS) { ts = 0; tsphase ^= 1; }
         }
       }
     }

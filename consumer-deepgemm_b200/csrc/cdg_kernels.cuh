@@ -495,6 +495,7 @@ struct GemmArgs {
   const uint32_t* sfw_atoms;  // [E][N/128][K/128][128] words
   const int32_t* row_exp;     // [nblk*128] per-row exponent of the activation planes
   const uint8_t* tok_code;    // [M][tok_code_pitch(K)] UE8M0 activation scale codes of direct-class rows
+  uint32_t* tok_atoms;        // [direct tile][K/512][2][128] token scale atoms (cdg_direct_atoms_kernel)
   __nv_bfloat16* d;
   int64_t d_row_stride;
   int M, N, K, E, nblk;

@@ -86,7 +86,7 @@ struct TileMap {
 // Workspace regions of one GEMM call.
 struct WorkspaceLayout {
   size_t ctrl = 0, blk_info = 0, blk_mask = 0, lists = 0, plane_tiles = 0, direct_tiles = 0, row_ids = 0, row_exp = 0,
-         hilo = 0, tok_code = 0, sfw_atoms = 0, total = 0;
+         hilo = 0, tok_code = 0, tok_atoms = 0, sfw_atoms = 0, total = 0;
 
   static WorkspaceLayout make(int64_t M, int64_t nblk, int64_t K, int64_t N, int64_t E, bool fast, bool row_ids,
                               bool sfw_from_rows) {
@@ -115,6 +115,8 @@ struct WorkspaceLayout {
       off = align_up(off + static_cast<size_t>(2) * nblk * 128 * K, 1024);
       w.tok_code = off;  // [M][tok_code_pitch(K)] UE8M0 activation scale codes of the direct class's rows
       off = align_up(off + static_cast<size_t>(tok_code_pitch(K)) * static_cast<size_t>(M), 1024);
+      w.tok_atoms = off;  // [direct tile][K/512 scale stage][2][128] words: token scale atoms
+      off = align_up(off + static_cast<size_t>(nblk) * (tok_code_pitch(K) / 4) * 1024, 1024);
       if (sfw_from_rows) {
         w.sfw_atoms = off;
         off = align_up(off + static_cast<size_t>(E) * ((N + 127) / 128) * (K / 128) * 512, 1024);
