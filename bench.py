@@ -49,9 +49,9 @@ import torch  # noqa: E402
 
 METRIC = "grouped FP8×FP4 MoE GEMM TFLOPS and HBM GB/s vs roofline at 1/2/4/8 B200"
 DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
-# library kernels per GEMM call on the CTA-pair path: cdg_prep_kernel, cdg_direct_atoms_kernel,
-# cdg_gemm_pair_kernel<16,4>, <32,2>, cdg_gemm_planes_kernel, cdg_gemm_direct_kernel, cdg_generic_kernel
-GEMM_LAUNCHES = 7
+# library kernels per GEMM call on the CTA-pair path: cdg_prep_kernel, cdg_gemm_pair_kernel<16,4>,
+# <32,2>, cdg_gemm_planes_kernel, cdg_gemm_direct_kernel, cdg_generic_kernel
+GEMM_LAUNCHES = 6
 # DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
 # captures summarised under profiles/ (absent: no capture of the current kernels yet).
 NCU_TRAFFIC = {

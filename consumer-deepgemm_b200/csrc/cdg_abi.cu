@@ -478,11 +478,8 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &tsf);
     if (st != CDG_OK) return st;
     const unsigned grid = static_cast<unsigned>(di.sm_count / 2 * 2);
-    // token scale atoms of the direct tiles, for cdg_gemm_direct_kernel
-    ka.list = reinterpret_cast<const int4*>(ws + wl.direct_tiles);
-    if (launch_pdl(cdg_direct_atoms_kernel, static_cast<unsigned>(std::min<int64_t>(nblk, 2 * di.sm_count)), 256, 0,
-                   stream, ka) != cudaSuccess)
-      return CDG_ERR_CUDA;
+    // the planes kernel also writes the direct tiles' token scale atoms
+    ka.direct_list = reinterpret_cast<const int4*>(ws + wl.direct_tiles);
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = skip_ungrouped ? 0 : 1;

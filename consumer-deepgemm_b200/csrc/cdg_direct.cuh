@@ -15,8 +15,9 @@
 // by one 2-D box of 8g rows of A per K step (one tensor map per g = h / 8).
 //
 // Token scale factors.  The prep kernel writes one UE8M0 code per (row, 128-wide K block),
-// row major with four K blocks per aligned 32-bit word; cdg_direct_atoms_kernel then writes,
-// per tile and scale stage of kKSF = 4 K steps, two 512-byte scale atoms (tokens 0-127 and
+// row major with four K blocks per aligned 32-bit word; the planes kernel, which runs just
+// before this one, then writes (write_direct_atoms), per tile and scale stage of kKSF = 4 K
+// steps, two 512-byte scale atoms (tokens 0-127 and
 // 128-255: token n at byte (n%32)*16 + ((n%128)/32)*4 of atom n/128) whose byte j is the
 // code of K step j of the stage.  One 8-column TMEM set then holds the token scales of four
 // K steps and the MMA of K step j selects byte j (b_sf_id).  The token atoms and the weight
@@ -76,30 +77,6 @@ struct DirectSmem {
 struct DirectMaps {
   CUtensorMap m[kDirectTileTok / 16];
 };
-
-// Token scale atoms of the direct tiles: for tile i (list order) and scale stage st, the
-// 1024 bytes at tok_atoms + (i * stages + st) * 256 words.  One thread per token slot n
-// (0..255) and stage: word (n/128)*128 + (n%32)*4 + (n%128)/32 holds the codes of the four
-// K steps of the stage, 127 (scale 1) for slots past the tile.
-__global__ void __launch_bounds__(256) cdg_direct_atoms_kernel(GemmArgs p) {
-  grid_dependency_wait();  // the tile list and the codes come from the prep kernel
-  grid_launch_dependents();
-  const int count = __ldcg(&p.ctrl[kCtrlDirectTiles]);
-  const int pitch = tok_code_pitch(p.K);
-  const int stages = pitch / 4;
-  const int n = threadIdx.x;
-  const int slot = (n >> 7) * 128 + (n & 31) * 4 + ((n & 127) >> 5);
-  for (int i = blockIdx.x; i < count; i += gridDim.x) {
-    const int4 cur = __ldcg(&p.list[i]);
-    int brow0, bn;
-    p.tm.rows(cur.x >> 7, brow0, bn);
-    const int row = brow0 + (cur.x & 127) + n;
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.tok_code + static_cast<int64_t>(row) * pitch);
-    uint32_t* dst = p.tok_atoms + static_cast<int64_t>(i) * stages * 256 + slot;
-#pragma unroll 4
-    for (int st = 0; st < stages; ++st) dst[st * 256] = n < cur.y ? __ldcg(src + st) : 0x7F7F7F7Fu;
-  }
-}
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads, 1)
     cdg_gemm_direct_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ DirectMaps tmaps_a,

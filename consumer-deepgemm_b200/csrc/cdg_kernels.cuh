@@ -491,11 +491,12 @@ struct GemmArgs {
   const uint4* blk_mask;
   const int* ctrl;
   const int4* list;       // blocks of this kernel's class, in order: {block, expert, rows spanned, 0}
+  const int4* direct_list;  // tiles of cdg_gemm_direct_kernel (their token atoms: write_direct_atoms)
   const int4* zero_list;  // all-padding blocks (zero-filled by the kernel with do_zero_blocks)
   const uint32_t* sfw_atoms;  // [E][N/128][K/128][128] words
   const int32_t* row_exp;     // [nblk*128] per-row exponent of the activation planes
   const uint8_t* tok_code;    // [M][tok_code_pitch(K)] UE8M0 activation scale codes of direct-class rows
-  uint32_t* tok_atoms;        // [direct tile][K/512][2][128] token scale atoms (cdg_direct_atoms_kernel)
+  uint32_t* tok_atoms;        // [direct tile][K/512][2][128] token scale atoms (write_direct_atoms)
   __nv_bfloat16* d;
   int64_t d_row_stride;
   int M, N, K, E, nblk;
@@ -505,6 +506,30 @@ struct GemmArgs {
   int fill_rest;          // 1: zero the block's rows past its last routed row
   int* status;
 };
+
+// Token scale atoms of the direct tiles, written by the kernel that runs before
+// cdg_gemm_direct_kernel (the planes kernel, all its threads).  For tile i (list order) and
+// scale stage st of four K steps, the 1024 bytes at tok_atoms + (i * stages + st) * 256 words:
+// token slot n (0..255) at word (n/128)*128 + (n%32)*4 + (n%128)/32, the 4-byte word of its
+// row's codes for the stage's K steps (byte j = K step j), 127 (scale 1) for slots past the
+// tile.
+__device__ __forceinline__ void write_direct_atoms(const GemmArgs& p) {
+  const int count = __ldcg(&p.ctrl[kCtrlDirectTiles]);
+  const int pitch = tok_code_pitch(p.K);
+  const int stages = pitch / 4;
+  const int items = count * 256;
+  for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+    const int i = it >> 8, n = it & 255;
+    const int4 cur = __ldcg(&p.direct_list[i]);
+    int brow0, bn;
+    p.tm.rows(cur.x >> 7, brow0, bn);
+    const int row = brow0 + (cur.x & 127) + n;
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.tok_code + static_cast<int64_t>(row) * pitch);
+    uint32_t* dst = p.tok_atoms + static_cast<int64_t>(i) * stages * 256 + (n >> 7) * 128 + (n & 31) * 4 + ((n & 127) >> 5);
+#pragma unroll 4
+    for (int st = 0; st < stages; ++st) dst[st * 256] = n < cur.y ? __ldcg(src + st) : 0x7F7F7F7Fu;
+  }
+}
 
 template <int TOK>
 struct GemmSmem {

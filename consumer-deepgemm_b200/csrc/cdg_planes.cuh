@@ -94,6 +94,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
 
   grid_dependency_wait();  // the tile list comes from the previous kernel of the stream
   grid_launch_dependents();
+  write_direct_atoms(p);  // for cdg_gemm_direct_kernel, which runs next
   const uint32_t rank = cluster_ctarank();
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int npairs = static_cast<int>(gridDim.x >> 1);
