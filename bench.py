@@ -57,6 +57,7 @@ GEMM_LAUNCHES = 6
 NCU_TRAFFIC = {
     "c1": 2.007860e9 + 0.223218e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
     "c2": 1.427530e9 + 0.654704e9,  # cdg_gemm_planes_kernel: profiles/cdg_gemm_planes_kernel_c2_prefill.md
+    "c2u": 1.281316e9 + 0.648415e9,  # cdg_gemm_direct_kernel: profiles/cdg_gemm_direct_kernel_c2u_prefill.md
 }
 # per EP step on top of the GEMM kernels: dispatch (quantise + pack), permute, return (or unpermute), combine
 EP_LAUNCHES = 4
