@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the grouped FP8 x MXFP4 MoE GEMM (m_grouped_fp8_fp4_gemm_nt_contiguous).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3|c4] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3|c4|c2u|c3u|c4u] [--impl ours|reference]
 
 Workloads (seeded synthetic data with the configs' shapes and distributions,
 consumer_deep_gemm.synthetic; weights transformed once at load and resident):
@@ -19,6 +19,8 @@ consumer_deep_gemm.synthetic; weights transformed once at load and resident):
 * --config c4: the full expert-parallel MoE layer (FC1 -> SiLU-mul + requant ->
   FC2), 32768 tokens x top-8 split over the ranks, E=256, hidden 4096,
   intermediate 2048.  Strong scaling; reported in TFLOP/s.
+* --config c2u / c3u / c4u: c2, c3 and c4 with power-of-two (UE8M0) activation scales,
+  the format DeepGEMM's SM100 path quantises to (c4u: the layer quantises that way).
 
 One JSON line on rank 0.  `value` = algorithmic bytes (or FLOPs for c4) of the
 whole job per step / device time of K steps (max over ranks).  Algorithmic bytes
@@ -232,7 +234,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c2u", "c3u"])
+    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c4u", "c2u", "c3u"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -251,7 +253,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
-        if args.config == "c4":
+        if args.config in ("c4", "c4u"):
             line = bench_layer(args, dev, world, rank, dist)
         elif world > 1:
             line = bench_ep_decode(args, dev, world, rank, dist)
@@ -482,7 +484,8 @@ def bench_ep_decode(args, dev, world, rank, dist):
 
 
 def bench_layer(args, dev, world, rank, dist):
-    """--config c4: the full expert-parallel MoE layer, 32768 tokens split over the ranks."""
+    """--config c4: the full expert-parallel MoE layer, 32768 tokens split over the ranks.
+    --config c4u: the same layer quantising its activations with power-of-two (UE8M0) scales."""
     from consumer_deep_gemm import synthetic
     from consumer_deep_gemm.moe import MoELayer
 
@@ -491,7 +494,9 @@ def bench_layer(args, dev, world, rank, dist):
     tokens = c1.tokens // world
     x, ids, w, b1, s1 = _ep_inputs(c1, dev, rank, world, tokens)
     b2, s2 = synthetic.make_weights(c1.num_experts // world, c2.n, c2.k, dev, seed=200 + rank)
-    layer = MoELayer(b1, s1, b2, s2, num_experts=c1.num_experts, group=dist.group.WORLD if dist else None)
+    ue8m0 = args.config == "c4u"
+    layer = MoELayer(b1, s1, b2, s2, num_experts=c1.num_experts, group=dist.group.WORLD if dist else None,
+                     ue8m0=ue8m0)
     e_loc = c1.num_experts // world
     mine = _global_counts(ids, c1.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
     _, f_fc1 = _local_gemm_work(mine, c1.n, c1.k)
@@ -519,8 +524,9 @@ def bench_layer(args, dev, world, rank, dist):
         "metric": METRIC, "value": job_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
-        "config": {"workload": "c4", "experts": c1.num_experts, "hidden": c1.k, "intermediate": c2.k,
-                   "tokens": c1.tokens, "topk": c1.topk, "parallelism": f"ep{world}"},
+        "config": {"workload": args.config, "experts": c1.num_experts, "hidden": c1.k, "intermediate": c2.k,
+                   "tokens": c1.tokens, "topk": c1.topk, "parallelism": f"ep{world}",
+                   "activation_scales": "ue8m0 (power of two)" if ue8m0 else "fp32 1x128"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
                      "frac": achieved / fp8_peak, "traffic": None, "kernel": "FC2 GEMM kernels (rank 0)",
                      "peak_source": f"2 x {peak_src} bf16 GEMM rate (dense FP8:BF16 = 2:1)"},

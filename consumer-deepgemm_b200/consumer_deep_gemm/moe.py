@@ -57,8 +57,8 @@ class NativeOps:
     def __init__(self):
         self.C = native.require()
 
-    def quant(self, x):
-        return self.C.quant_fp8_rows(x)
+    def quant(self, x, ue8m0=False):
+        return self.C.quant_fp8_rows(x, ue8m0)
 
     def count(self, topk_ids, num_experts):
         return self.C.ep_count(topk_ids, num_experts)
@@ -69,8 +69,8 @@ class NativeOps:
     def permute(self, rows, hidden, local_experts, expert_off, m_pad):
         return self.C.ep_permute(rows, hidden, local_experts, expert_off, m_pad)
 
-    def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap):
-        return self.C.ep_quant_pack_fixed(x, topk_ids, num_experts, ranks, cap)
+    def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap, ue8m0=False):
+        return self.C.ep_quant_pack_fixed(x, topk_ids, num_experts, ranks, cap, ue8m0)
 
     def permute_fixed(self, rows, hidden, local_experts, ranks, cap, m_pad):
         return self.C.ep_permute_fixed(rows, hidden, local_experts, ranks, cap, m_pad)
@@ -80,8 +80,8 @@ class NativeOps:
         m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices, _skip_ungrouped_rows=skip_ungrouped)
         return d
 
-    def act(self, h, m_indices):
-        return self.C.silu_mul_quant(h, m_indices)
+    def act(self, h, m_indices, ue8m0=False):
+        return self.C.silu_mul_quant(h, m_indices, ue8m0)
 
     def unpermute(self, y, perm_pos):
         return self.C.ep_unpermute(y, perm_pos)
@@ -145,11 +145,15 @@ class MoELayer:
     w2: packed e2m1 [E_local, H, I/2], w2_scale UE8M0 [E_local, H, I/32].
     ``num_experts`` is the global E; E_local = E / world size.  With ``w2=None`` the layer
     is the expert-parallel grouped GEMM alone: y[t] = sum_j topk_w[t, j] * FC1_e(q(x[t])).
+    ``ue8m0=True`` quantises the activations (q and act) with power-of-two scales, the UE8M0
+    recipe DeepGEMM's SM100 path uses (1x128 scale amax/448 rounded up to a power of two,
+    kept as FP32); the GEMMs then run their direct class (one MMA per K slice).
     """
 
     def __init__(self, w1, w1_scale, w2=None, w2_scale=None, num_experts: int = 0, group=None, ops=None,
-                 max_tokens_per_rank: int | None = None, exchange: str = "nccl"):
+                 max_tokens_per_rank: int | None = None, exchange: str = "nccl", ue8m0: bool = False):
         self.ops = ops or NativeOps()
+        self.ue8m0 = bool(ue8m0)
         self.max_tokens = max_tokens_per_rank
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
@@ -189,7 +193,7 @@ class MoELayer:
         dev = x.device
         topk_ids = topk_ids.contiguous()
         topk_w = topk_w.to(torch.float32).contiguous()
-        xq, xs = ops.quant(x)
+        xq, xs = ops.quant(x, self.ue8m0)
         counts = ops.count(topk_ids, E)                                  # [E] rows per global expert
         if world > 1:
             both = torch.empty(2, E, dtype=counts.dtype, device=dev)
@@ -219,7 +223,7 @@ class MoELayer:
             a, sa, m_indices, perm_pos = ops.permute(recv, x.shape[1], E_loc, expert_off, m_pad)
             h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices)
             if self.w2 is not None:
-                aq, asc = ops.act(h, m_indices)
+                aq, asc = ops.act(h, m_indices, self.ue8m0)
                 h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
             if world == 1:
                 # no exchange: combine straight from the GEMM's rows (one pass instead of two)
@@ -244,13 +248,13 @@ class MoELayer:
         cap = self.max_tokens * topk  # rows any one destination can receive from this rank
         topk_ids = topk_ids.contiguous()
         topk_w = topk_w.to(torch.float32).contiguous()
-        sent, send_index = ops.quant_pack_fixed(x, topk_ids, E, world, cap)
+        sent, send_index = ops.quant_pack_fixed(x, topk_ids, E, world, cap, self.ue8m0)
         recv = _all_to_all(torch.empty_like(sent), sent, None, None, group)
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
         a, sa, m_indices, perm_pos = ops.permute_fixed(recv, x.shape[1], E_loc, world, cap, m_pad)
         h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         if self.w2 is not None:
-            aq, asc = ops.act(h, m_indices)
+            aq, asc = ops.act(h, m_indices, self.ue8m0)
             h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
         back = ops.unpermute(h, perm_pos)
         out_rows = _all_to_all(torch.empty_like(back), back, None, None, group)
@@ -269,12 +273,12 @@ class MoELayer:
         if self.windows is None:
             self.windows = PeerWindows(self.group, cap, H, x.device)
         win, me = self.windows, self.rank
-        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, win.own, me)
+        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, win.own, me, self.ue8m0)
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
         a, sa, m_indices, perm_pos = C.ep_permute_p2p(win.own, world, cap, H, E_loc, m_pad, x)
         h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         if self.w2 is not None:
-            aq, asc = self.ops.act(h, m_indices)
+            aq, asc = self.ops.act(h, m_indices, self.ue8m0)
             h = self.ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
         C.ep_return_p2p(h, perm_pos, world, cap, win.peers, win.own, me)
         return C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H)

@@ -114,27 +114,34 @@ __device__ bool wait_peer_flags(const int32_t* flags, int n, int32_t epoch, int3
   return s_ok != 0;
 }
 
-// Quantise one 128-wide block held by a warp (4 values per lane) to e4m3 with the
-// per_block_cast_to_fp8 recipe: amax clamped at 1e-12, scale = amax / 448,
-// q = e4m3(x / amax * 448) (FP32 arithmetic, round to nearest even).
-__device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* q, float* scale_out, int lane) {
+// Quantise one 128-wide block held by a warp (4 values per lane) to e4m3 (FP32 arithmetic,
+// round to nearest even; amax clamped at 1e-12).
+// pow2 == 0: the per_block_cast_to_fp8 recipe, scale = amax / 448, q = e4m3(x / amax * 448).
+// pow2 != 0: the UE8M0 recipe (DeepGEMM's per-token cast with use_ue8m0 on SM100): scale =
+//   amax / 448 rounded up to a power of two (exactly: next exponent unless the mantissa is
+//   zero), q = e4m3(x / scale).  Such scales make the GEMM take its direct class.
+__device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* q, float* scale_out, int lane,
+                                                 int pow2) {
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   amax = fmaxf(amax, 1e-12f);
+  uint32_t sb = __float_as_uint(amax / 448.0f);
+  if (sb & 0x007FFFFFu) sb = (sb & 0xFF800000u) + 0x00800000u;
+  const float s2 = __uint_as_float(sb);
   uint32_t packed = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float y = v[i] / amax * 448.0f;
+    const float y = pow2 ? v[i] / s2 : v[i] / amax * 448.0f;
     packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3)) << (8 * i);
   }
   reinterpret_cast<uint32_t*>(q)[lane] = packed;
-  if (lane == 0) *scale_out = amax / 448.0f;
+  if (lane == 0) *scale_out = pow2 ? s2 : amax / 448.0f;
 }
 
 // One warp per (row, 128-column block).
 __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, int64_t M, int64_t K, uint8_t* q,
-                                  int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k) {
+                                  int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k, int pow2) {
   const int64_t kb_count = K / 128;
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -143,7 +150,7 @@ __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, 
   float v[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) v[i] = load_f(x, x_dtype, r * x_stride + kb * 128 + lane * 4 + i);
-  quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane);
+  quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
 }
 
 // One warp per (row, 128-column block of the output); gate = columns [0, I), up = [I, 2I).
@@ -152,7 +159,7 @@ __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, 
 template <bool VEC>
 __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride, int64_t M, int64_t I,
                                       const int32_t* m_indices, uint8_t* q, int64_t q_stride, float* s,
-                                      int64_t s_stride_m, int64_t s_stride_k) {
+                                      int64_t s_stride_m, int64_t s_stride_k, int pow2) {
   const int64_t kb_count = I / 128;
   const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -180,7 +187,7 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride
   float v[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) v[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
-  quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane);
+  quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
 }
 
 __global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64_t E, int32_t* cnt) {
@@ -262,7 +269,8 @@ __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x,
                                                                   int64_t topk, int64_t E, int64_t e_per_rank,
                                                                   int64_t ranks, int64_t H, int64_t cap,
                                                                   int32_t* scratch, uint8_t* out_rows,
-                                                                  int32_t* send_index, PeerStep ps = PeerStep{}) {
+                                                                  int32_t* send_index, int pow2,
+                                                                  PeerStep ps = PeerStep{}) {
   const uint64_t* peers = ps.peers;
   const int32_t epoch = peers ? ps.epoch() : 0;
   const int64_t region_off = peers ? ps.win.recv_parity(epoch & 1) + ps.me * (cap + 1) * ps.win.rb : 0;
@@ -313,7 +321,7 @@ __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x,
         const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + base);
         v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
       }
-      quant_block_warp(v, out + kb * 128, out_s + kb, lane);
+      quant_block_warp(v, out + kb * 128, out_s + kb, lane, pow2);
     }
     if (threadIdx.x == 0) *reinterpret_cast<int32_t*>(out + H + 4 * (H / 128)) = static_cast<int32_t>(s_e % e_per_rank);
   }
@@ -591,26 +599,30 @@ int launched() { return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUD
 extern "C" {
 
 int cdg_quant_fp8_rows(const void* x, int32_t x_dtype, int64_t x_stride, int64_t M, int64_t K, uint8_t* q,
-                       int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k, cdg_stream_t stream) {
+                       int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k, int32_t scale_fmt,
+                       cdg_stream_t stream) {
   if (M < 0 || K <= 0 || K % 128 || (M > 0 && (!x || !q || !s))) return CDG_ERR_INVALID_ARGUMENT;
+  if (scale_fmt != CDG_SCALE_FP32 && scale_fmt != CDG_SCALE_POW2) return CDG_ERR_INVALID_ARGUMENT;
   if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(q) % 4 || q_stride % 4) return CDG_ERR_ALIGNMENT;
   if (M == 0) return CDG_OK;
   cdg::quant_rows_kernel<<<cdg::warp_grid(M * (K / 128)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, x_dtype, x_stride, M, K, q, q_stride, s, s_stride_m, s_stride_k);
+      x, x_dtype, x_stride, M, K, q, q_stride, s, s_stride_m, s_stride_k, scale_fmt);
   return cdg::launched();
 }
 
 int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t I, const int32_t* m_indices,
                            uint8_t* q, int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k,
-                           cdg_stream_t stream) {
+                           int32_t scale_fmt, cdg_stream_t stream) {
   if (M < 0 || I <= 0 || I % 128 || (M > 0 && (!in || !q || !s))) return CDG_ERR_INVALID_ARGUMENT;
+  if (scale_fmt != CDG_SCALE_FP32 && scale_fmt != CDG_SCALE_POW2) return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(q) % 4 || q_stride % 4) return CDG_ERR_ALIGNMENT;
   if (M == 0) return CDG_OK;
   const bool vec = reinterpret_cast<uintptr_t>(in) % 8 == 0 && in_stride % 4 == 0;
   auto kernel = vec ? cdg::silu_mul_quant_kernel<true> : cdg::silu_mul_quant_kernel<false>;
   kernel<<<cdg::warp_grid(M * (I / 128)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(in), in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k);
+      static_cast<const __nv_bfloat16*>(in), in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k,
+      scale_fmt);
   return cdg::launched();
 }
 
@@ -663,10 +675,11 @@ int64_t cdg_ep_fixed_scratch_ints(int64_t ranks, int64_t E) {
 
 int cdg_ep_quant_pack_fixed(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
                             int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap, int32_t* scratch,
-                            uint8_t* out_rows, int32_t* send_index, cdg_stream_t stream) {
+                            uint8_t* out_rows, int32_t* send_index, int32_t scale_fmt, cdg_stream_t stream) {
   if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || ranks > cdg::kFixedMaxRanks || E % ranks || H <= 0 || H % 128 ||
       cap < 0 || E / ranks > cdg::kFixedMaxExperts || !scratch || !out_rows)
     return CDG_ERR_INVALID_ARGUMENT;
+  if (scale_fmt != CDG_SCALE_FP32 && scale_fmt != CDG_SCALE_POW2) return CDG_ERR_INVALID_ARGUMENT;
   if (4 * (E / ranks) > cdg::packed_row_bytes(H)) return CDG_ERR_INVALID_ARGUMENT;  // header fits a row
   if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
   if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
@@ -677,7 +690,7 @@ int cdg_ep_quant_pack_fixed(const void* x, int32_t x_dtype, int64_t x_stride, co
   if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4) return CDG_ERR_ALIGNMENT;  // vector loads of 4 values
   const unsigned grid = T * topk > 0 ? static_cast<unsigned>(T * topk) : 1u;
   cdg::ep_quant_pack_fixed_kernel<<<grid, 128, 0, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E, E / ranks,
-                                                        ranks, H, cap, scratch, out_rows, send_index);
+                                                        ranks, H, cap, scratch, out_rows, send_index, scale_fmt);
   return cdg::launched();
 }
 
@@ -786,10 +799,11 @@ int cdg_ep_window_status(const void* window, cdg_stream_t stream) {
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
                         int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
                         const uint64_t* peers, void* window, int32_t me, int32_t* scratch, int32_t* send_index,
-                        cdg_stream_t stream) {
+                        int32_t scale_fmt, cdg_stream_t stream) {
   if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || ranks > 128 || E % ranks || H <= 0 || H % 128 || cap < 0 ||
       E / ranks > cdg::kFixedMaxExperts || !scratch || !peers || !window || me < 0 || me >= ranks)
     return CDG_ERR_INVALID_ARGUMENT;
+  if (scale_fmt != CDG_SCALE_FP32 && scale_fmt != CDG_SCALE_POW2) return CDG_ERR_INVALID_ARGUMENT;
   if (4 * (E / ranks) > cdg::packed_row_bytes(H)) return CDG_ERR_INVALID_ARGUMENT;
   if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
   if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
@@ -804,7 +818,8 @@ int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const 
   ps.me = me;
   const unsigned grid = T * topk > 0 ? static_cast<unsigned>(T * topk) : 1u;
   cdg::ep_quant_pack_fixed_kernel<<<grid, 128, 0, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E,
-                                                        E / ranks, ranks, H, cap, scratch, nullptr, send_index, ps);
+                                                        E / ranks, ranks, H, cap, scratch, nullptr, send_index, scale_fmt,
+                                                        ps);
   return cdg::launched();
 }
 

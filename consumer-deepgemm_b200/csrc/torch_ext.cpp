@@ -185,7 +185,7 @@ cdg_stream_t cur_stream(const torch::Tensor& t) {
 }
 
 // ------------------------------------------------------------------ MoE layer / expert parallelism
-std::vector<torch::Tensor> quant_fp8_rows(const torch::Tensor& x) {
+std::vector<torch::Tensor> quant_fp8_rows(const torch::Tensor& x, bool ue8m0) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [M, K] tensor with unit last stride");
   TORCH_CHECK_VALUE(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat32, "x must be BF16/FP32");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -194,12 +194,13 @@ std::vector<torch::Tensor> quant_fp8_rows(const torch::Tensor& x) {
   auto s = torch::empty({M, K / 128}, x.options().dtype(torch::kFloat32));
   check_status(cdg_quant_fp8_rows(x.data_ptr(), dtype_code(x), x.stride(0), M, K,
                                   reinterpret_cast<uint8_t*>(q.data_ptr()), K, s.data_ptr<float>(), K / 128, 1,
-                                  cur_stream(x)),
+                                  ue8m0 ? CDG_SCALE_POW2 : CDG_SCALE_FP32, cur_stream(x)),
                "quant_fp8_rows");
   return {q, s};
 }
 
-std::vector<torch::Tensor> silu_mul_quant(const torch::Tensor& h, const c10::optional<torch::Tensor>& m_indices) {
+std::vector<torch::Tensor> silu_mul_quant(const torch::Tensor& h, const c10::optional<torch::Tensor>& m_indices,
+                                          bool ue8m0) {
   TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.stride(1) == 1 && h.scalar_type() == torch::kBFloat16,
               "h must be a CUDA BF16 [M, 2I] tensor with unit last stride");
   const c10::cuda::CUDAGuard guard(h.device());
@@ -212,7 +213,8 @@ std::vector<torch::Tensor> silu_mul_quant(const torch::Tensor& h, const c10::opt
     ids = m_indices->data_ptr<int32_t>();
   }
   check_status(cdg_silu_mul_quant_fp8(h.data_ptr(), h.stride(0), M, I, ids, reinterpret_cast<uint8_t*>(q.data_ptr()),
-                                      I, s.data_ptr<float>(), I / 128, 1, cur_stream(h)),
+                                      I, s.data_ptr<float>(), I / 128, 1, ue8m0 ? CDG_SCALE_POW2 : CDG_SCALE_FP32,
+                                      cur_stream(h)),
                "silu_mul_quant");
   return {q, s};
 }
@@ -269,7 +271,7 @@ std::vector<torch::Tensor> ep_permute(const torch::Tensor& rows, int64_t H, int6
 
 // Fixed-capacity send buffer: (packed rows uint8 [ranks*(cap+1), row_bytes], send_index [T*topk]).
 std::vector<torch::Tensor> ep_quant_pack_fixed(const torch::Tensor& x, const torch::Tensor& ids, int64_t E,
-                                               int64_t ranks, int64_t cap) {
+                                               int64_t ranks, int64_t cap, bool ue8m0) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
   TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
               "topk ids must be contiguous [T, topk]");
@@ -281,7 +283,8 @@ std::vector<torch::Tensor> ep_quant_pack_fixed(const torch::Tensor& x, const tor
                               ids.options().dtype(torch::kInt32));
   check_status(cdg_ep_quant_pack_fixed(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T,
                                        topk, E, ranks, H, cap, scratch.data_ptr<int32_t>(), out.data_ptr<uint8_t>(),
-                                       send_index.data_ptr<int32_t>(), cur_stream(x)),
+                                       send_index.data_ptr<int32_t>(), ue8m0 ? CDG_SCALE_POW2 : CDG_SCALE_FP32,
+                                       cur_stream(x)),
                "ep_quant_pack_fixed");
   return {out, send_index};
 }
@@ -335,7 +338,7 @@ uint64_t ep_window_open(const py::bytes& handle) {
 }
 
 torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, int64_t E, int64_t ranks, int64_t cap,
-                              const torch::Tensor& peers, uint64_t window, int64_t me) {
+                              const torch::Tensor& peers, uint64_t window, int64_t me, bool ue8m0) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
   TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
               "topk ids must be contiguous [T, topk]");
@@ -349,7 +352,8 @@ torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, 
   check_status(cdg_ep_dispatch_p2p(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T, topk,
                                    E, ranks, H, cap, reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
                                    reinterpret_cast<void*>(window), static_cast<int32_t>(me),
-                                   scratch.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(), cur_stream(x)),
+                                   scratch.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(),
+                                   ue8m0 ? CDG_SCALE_POW2 : CDG_SCALE_FP32, cur_stream(x)),
                "ep_dispatch_p2p");
   return send_index;
 }
@@ -456,15 +460,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                      "set_profile_events");
       },
       py::arg("start"), py::arg("stop"));
-  m.def("quant_fp8_rows", &quant_fp8_rows, py::arg("x"));
-  m.def("silu_mul_quant", &silu_mul_quant, py::arg("h"), py::arg("m_indices") = py::none());
+  m.def("quant_fp8_rows", &quant_fp8_rows, py::arg("x"), py::arg("ue8m0") = false);
+  m.def("silu_mul_quant", &silu_mul_quant, py::arg("h"), py::arg("m_indices") = py::none(),
+        py::arg("ue8m0") = false);
   m.def("ep_count", &ep_count, py::arg("topk_ids"), py::arg("num_experts"));
   m.def("ep_pack", &ep_pack, py::arg("xq"), py::arg("xs"), py::arg("topk_ids"), py::arg("num_experts"),
         py::arg("ranks"), py::arg("send_off"), py::arg("rows"));
   m.def("ep_permute", &ep_permute, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("expert_off"), py::arg("m_pad"));
   m.def("ep_quant_pack_fixed", &ep_quant_pack_fixed, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
-        py::arg("ranks"), py::arg("cap"));
+        py::arg("ranks"), py::arg("cap"), py::arg("ue8m0") = false);
   m.def("ep_permute_fixed", &ep_permute_fixed, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("ranks"), py::arg("cap"), py::arg("m_pad"));
   m.def("mega_moe_transform_rows", &mega_moe_transform_rows, py::arg("t"), py::arg("kind"));
@@ -486,7 +491,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("window"));
   m.def("ep_dispatch_p2p", &ep_dispatch_p2p, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
-        py::arg("ranks"), py::arg("cap"), py::arg("peers"), py::arg("window"), py::arg("me"));
+        py::arg("ranks"), py::arg("cap"), py::arg("peers"), py::arg("window"), py::arg("me"),
+        py::arg("ue8m0") = false);
   m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("cap"), py::arg("hidden"),
         py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
   m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("perm_pos"), py::arg("ranks"), py::arg("cap"),

@@ -221,16 +221,26 @@ int cdg_grouped_fp8_fp4_gemm_nt_contiguous_noalloc(const cdg_gemm_args* args, cd
  * Strides are in elements; e4m3 tensors are bytes.
  * ------------------------------------------------------------------------------------------- */
 
-/* q[r, :] = e4m3(x[r, :] / amax * 448), s[r, kb] = amax / 448 per 128-column block (amax clamped
- * at 1e-12), FP32 arithmetic; x is BF16 or F32 (x_dtype), K a multiple of 128. */
-int cdg_quant_fp8_rows(const void* x, int32_t x_dtype, int64_t x_stride, int64_t M, int64_t K, uint8_t* q,
-                       int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k, cdg_stream_t stream);
+/* Activation scale recipes of the quantising steps (scale_fmt); amax = the largest |x| of the
+ * 128-column block, clamped at 1e-12; FP32 arithmetic, e4m3 round to nearest even:
+ *   CDG_SCALE_FP32  s = amax / 448, q = e4m3(x / amax * 448)   (per_block_cast_to_fp8)
+ *   CDG_SCALE_POW2  s = amax / 448 rounded up to a power of two (exactly), q = e4m3(x / s)
+ *                   (the UE8M0 recipe DeepGEMM's SM100 path uses; s is still stored as FP32,
+ *                   and such scales put the GEMM's blocks in its direct class) */
+#define CDG_SCALE_FP32 0
+#define CDG_SCALE_POW2 1
 
-/* in = [gate | up] BF16 [M, 2I]: q, s = 1x128 e4m3 quantisation of silu(gate) * up (FP32).
- * Rows whose m_indices entry is negative are skipped (m_indices may be NULL). */
+/* q[r, :], s[r, kb] = 1x128 e4m3 quantisation of x (scale_fmt recipe); x is BF16 or F32
+ * (x_dtype), K a multiple of 128. */
+int cdg_quant_fp8_rows(const void* x, int32_t x_dtype, int64_t x_stride, int64_t M, int64_t K, uint8_t* q,
+                       int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k, int32_t scale_fmt,
+                       cdg_stream_t stream);
+
+/* in = [gate | up] BF16 [M, 2I]: q, s = 1x128 e4m3 quantisation of silu(gate) * up (FP32,
+ * scale_fmt recipe).  Rows whose m_indices entry is negative are skipped (m_indices may be NULL). */
 int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t I, const int32_t* m_indices,
                            uint8_t* q, int64_t q_stride, float* s, int64_t s_stride_m, int64_t s_stride_k,
-                           cdg_stream_t stream);
+                           int32_t scale_fmt, cdg_stream_t stream);
 
 /* counts[e] = number of entries of topk_ids (n of them, int32 or int64) equal to e, e in [0, E). */
 int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, int32_t* counts, cdg_stream_t stream);
@@ -261,7 +271,7 @@ int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_loc
  * experts, then the rows themselves.
  *
  * cdg_ep_quant_pack_fixed quantises token t's BF16/FP32 row (1x128 e4m3 + FP32 scales, the
- * per_block_cast_to_fp8 recipe) into a packed row of the region of rank e / (E / ranks) for
+ * scale_fmt recipe) into a packed row of the region of rank e / (E / ranks) for
  * every slot j with expert e = topk_ids[t, j] in [0, E); send_index[t*topk + j] is that row
  * (-1 for skipped slots and for slots beyond `cap`, which the caller should size to
  * T * topk to drop nothing).  `scratch` is int32 [cdg_ep_fixed_scratch_ints(ranks, E)],
@@ -269,7 +279,7 @@ int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_loc
 int64_t cdg_ep_fixed_scratch_ints(int64_t ranks, int64_t E);
 int cdg_ep_quant_pack_fixed(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
                             int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap, int32_t* scratch,
-                            uint8_t* out_rows, int32_t* send_index, cdg_stream_t stream);
+                            uint8_t* out_rows, int32_t* send_index, int32_t scale_fmt, cdg_stream_t stream);
 
 /* Fixed-capacity receive buffer -> contiguous layout (group offsets derived on the device
  * from the headers).  M_pad must be at least ranks*cap + 127*E_local (the worst case);
@@ -315,7 +325,7 @@ int cdg_ep_window_status(const void* window, cdg_stream_t stream);
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
                         int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
                         const uint64_t* peers, void* window, int32_t me, int32_t* scratch, int32_t* send_index,
-                        cdg_stream_t stream);
+                        int32_t scale_fmt, cdg_stream_t stream);
 int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t* fill,
                        uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                        cdg_stream_t stream);

@@ -17,9 +17,20 @@ def row_bytes(hidden):
     return (hidden + 4 * (hidden // 128) + 4 + 15) // 16 * 16
 
 
+def cast_to_fp8_pow2(x):
+    """1x128 e4m3 quantisation with power-of-two scales (the UE8M0 recipe of DeepGEMM's SM100
+    path): s = amax / 448 (amax clamped at 1e-12) rounded up to a power of two, q = e4m3(x / s)."""
+    m, k = x.shape
+    xv = x.float().view(m, k // 128, 128)
+    s = xv.abs().amax(dim=2).clamp(min=1e-12) / 448.0
+    mant, ex = torch.frexp(s)  # s = mant * 2^ex, mant in [0.5, 1): a power of two iff mant == 0.5
+    s2 = torch.where(mant == 0.5, s, torch.ldexp(torch.ones_like(s), ex))
+    return (xv / s2.unsqueeze(-1)).to(torch.float8_e4m3fn).view(m, k), s2
+
+
 class TorchRefOps:
-    def quant(self, x):
-        return per_block_cast_to_fp8(x.float())
+    def quant(self, x, ue8m0=False):
+        return cast_to_fp8_pow2(x) if ue8m0 else per_block_cast_to_fp8(x.float())
 
     def count(self, topk_ids, num_experts):
         ids = topk_ids.flatten().long()
@@ -63,12 +74,12 @@ class TorchRefOps:
             m_indices[p], pos[i] = e, p
         return a, sa, m_indices, pos
 
-    def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap):
+    def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap, ue8m0=False):
         """Regions of 1 + cap packed rows per destination: header (int32 counts per local expert), rows."""
         T, k = topk_ids.shape
         H = x.shape[1]
         per_rank = num_experts // ranks
-        xq, xs = self.quant(x)
+        xq, xs = self.quant(x, ue8m0)
         out = torch.zeros(ranks * (cap + 1), row_bytes(H), dtype=torch.uint8)
         send_index = torch.full((T * k,), -1, dtype=torch.int32)
         fill = [0] * ranks
@@ -121,10 +132,11 @@ class TorchRefOps:
         oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices)
         return d
 
-    def act(self, h, m_indices):
+    def act(self, h, m_indices, ue8m0=False):
         i = h.shape[1] // 2
         g, u = h[:, :i].float(), h[:, i:].float()
-        return per_block_cast_to_fp8(torch.nn.functional.silu(g) * u)
+        v = torch.nn.functional.silu(g) * u
+        return cast_to_fp8_pow2(v) if ue8m0 else per_block_cast_to_fp8(v)
 
     def unpermute(self, y, perm_pos):
         out = torch.zeros(perm_pos.numel(), y.shape[1], dtype=y.dtype)

@@ -1,7 +1,8 @@
 """GPU checks of the MoE-layer kernels and of the layer itself (through the torch binding).
 
 Tolerances:
-  * FP8 row quantisation: bit-exact against per_block_cast_to_fp8 (deep_gemm/utils/math.py:21-37).
+  * FP8 row quantisation: bit-exact against per_block_cast_to_fp8 (deep_gemm/utils/math.py:21-37),
+    and, with power-of-two (UE8M0) scales, against moe_ref.cast_to_fp8_pow2.
   * SiLU-mul + requant: scales within 1e-6 relative; e4m3 codes equal except where the
     CUDA and CPU exponentials differ by an ulp (at most 1 in 1000 codes, each within one e4m3 step).
   * Dispatch / permute / unpermute: exact (bytes).
@@ -17,7 +18,7 @@ import sys
 import pytest
 import torch
 
-from moe_ref import TorchRefOps, make_layer_inputs, row_bytes
+from moe_ref import TorchRefOps, cast_to_fp8_pow2, make_layer_inputs, row_bytes
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -41,11 +42,26 @@ def test_quant_fp8_rows_bit_exact():
     assert torch.equal(s.cpu(), rs)
 
 
-def test_silu_mul_quant_matches_reference():
+def test_quant_fp8_rows_pow2_bit_exact():
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(300, 1024, generator=g) * torch.rand(300, 1, generator=g) * 10).to(torch.bfloat16)
+    x[7] = 0  # all-zero row: amax clamps at 1e-12
+    x[9, :128] = 448.0 * 2.0 ** -3  # amax / 448 exactly a power of two: kept, not doubled
+    q, s = _ext().quant_fp8_rows(x.to(DEV), ue8m0=True)
+    rq, rs = cast_to_fp8_pow2(x)
+    assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
+    assert torch.equal(s.cpu(), rs)
+    assert float(rs[9, 0]) == 2.0 ** -3
+    mant, _ = torch.frexp(s.cpu())
+    assert bool((mant == 0.5).all()), "every scale is a power of two"
+
+
+@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
+def test_silu_mul_quant_matches_reference(ue8m0):
     g = torch.Generator().manual_seed(2)
     h = torch.randn(200, 2 * 512, generator=g).to(torch.bfloat16)
-    q, s = _ext().silu_mul_quant(h.to(DEV), None)
-    rq, rs = TorchRefOps().act(h, None)
+    q, s = _ext().silu_mul_quant(h.to(DEV), None, ue8m0)
+    rq, rs = TorchRefOps().act(h, None, ue8m0)
     assert torch.allclose(s.cpu(), rs, rtol=1e-6, atol=0)
     a, b = q.cpu().view(torch.uint8).to(torch.int32), rq.view(torch.uint8).to(torch.int32)
     diff = (a != b)
@@ -121,7 +137,8 @@ def test_combine_scalar_path_matches_vector_path():
     assert torch.equal(y_vec[:, :H - 4].view(torch.int16), y_sc.view(torch.int16))
 
 
-def test_fixed_capacity_pack_and_permute_exact():
+@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
+def test_fixed_capacity_pack_and_permute_exact(ue8m0):
     """Fused quant+pack into fixed-capacity regions, then the receive-side permute: bytes."""
     C = _ext()
     T, H, k, E, ranks = 40, 512, 2, 8, 2
@@ -130,8 +147,8 @@ def test_fixed_capacity_pack_and_permute_exact():
     ids = torch.rand(T, E, generator=g).topk(k, dim=1).indices.to(torch.int32)
     ids[7, 0] = -1  # a skipped slot
     cap = T * k
-    sent, si = C.ep_quant_pack_fixed(x.to(DEV), ids.to(DEV), E, ranks, cap)
-    ref_sent, ref_si = TorchRefOps().quant_pack_fixed(x, ids, E, ranks, cap)
+    sent, si = C.ep_quant_pack_fixed(x.to(DEV), ids.to(DEV), E, ranks, cap, ue8m0)
+    ref_sent, ref_si = TorchRefOps().quant_pack_fixed(x, ids, E, ranks, cap, ue8m0)
     sent, si = sent.cpu(), si.cpu()
     nkb = H // 128
     payload = H + 4 * nkb + 4
@@ -157,14 +174,17 @@ def test_fixed_capacity_pack_and_permute_exact():
     assert torch.equal(mi >= 0, rmi >= 0)
 
 
-def test_layer_single_gpu_matches_cpu_reference():
+@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
+def test_layer_single_gpu_matches_cpu_reference(ue8m0):
+    # with ue8m0 the activations carry power-of-two scales and both GEMMs' wide blocks take the
+    # direct class: 1000 tokens x top-2 over 8 experts give each expert a run of two blocks
     from consumer_deep_gemm.moe import MoELayer
     from metrics import errors
 
-    cfg = dict(tokens=96, experts=8, hidden=512, inter=256, topk=2)
+    cfg = dict(tokens=1000 if ue8m0 else 96, experts=8, hidden=512, inter=256, topk=2)
     x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**cfg)
-    y_ref = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"], ops=TorchRefOps())(x, ids, w)
-    layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), num_experts=cfg["experts"])
+    y_ref = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"], ops=TorchRefOps(), ue8m0=ue8m0)(x, ids, w)
+    layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), num_experts=cfg["experts"], ue8m0=ue8m0)
     y = layer(x.to(DEV), ids.to(DEV), w.to(DEV))
     y2 = layer(x.to(DEV), ids.to(DEV), w.to(DEV))
     torch.cuda.synchronize()

@@ -106,3 +106,29 @@ def test_single_process_layer_composition():
         oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((aq, asc), (w2[e], w2s[e]), o)
         acc += w[t, j] * o[0].float()
     assert torch.equal(y[t].view(torch.int16), acc.to(torch.bfloat16).view(torch.int16))
+
+
+def test_pow2_quant_recipe():
+    """The power-of-two (UE8M0) activation recipe of the reference ops: every scale is
+    2^ceil(log2(amax / 448)), the codes stay within e4m3's range and dequantise to x within
+    e4m3 precision; the layer over it stays close to the FP32-scale layer."""
+    from consumer_deep_gemm.moe import MoELayer
+    from metrics import errors
+    from moe_ref import TorchRefOps, cast_to_fp8_pow2, make_layer_inputs
+
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(64, 512, generator=g) * torch.rand(64, 1, generator=g) * 100
+    q, s = cast_to_fp8_pow2(x)
+    amax = x.view(64, 4, 128).abs().amax(2).clamp(min=1e-12)
+    assert torch.equal(s, torch.exp2(torch.ceil(torch.log2(amax / 448.0))))
+    mant, _ = torch.frexp(s)
+    assert bool((mant == 0.5).all())
+    deq = q.float().view(64, 4, 128) * s.unsqueeze(-1)
+    assert float(q.float().abs().max()) <= 448.0
+    assert bool(((deq - x.view(64, 4, 128)).abs() <= x.view(64, 4, 128).abs() / 16 + s.unsqueeze(-1) * 2 ** -9).all())
+
+    xs, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**CFG)
+    y32 = MoELayer(w1, w1s, w2, w2s, num_experts=CFG["experts"], ops=TorchRefOps())(xs, ids, w)
+    y2 = MoELayer(w1, w1s, w2, w2s, num_experts=CFG["experts"], ops=TorchRefOps(), ue8m0=True)(xs, ids, w)
+    nw, rl2 = errors(y2, y32)
+    assert nw <= 0.1 and rl2 <= 0.1, (nw, rl2)
