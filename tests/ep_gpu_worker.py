@@ -32,14 +32,17 @@ def main():
     sl = slice(rank * e_loc, (rank + 1) * e_loc)
     tpr = cfg["tokens"] // world
     ts = slice(rank * tpr, (rank + 1) * tpr)
-    y_one = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"])(x, ids, w) if rank == 0 else None
-    # split-size exchange (one host sync) and fixed-capacity exchange (none)
+    y_ref = {u: MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"], ue8m0=u)(x, ids, w) if rank == 0 else None
+             for u in (False, True)}
     # split-size exchange (one host sync), fixed-capacity NCCL exchange (none), and the
-    # library's peer-memory exchange (no collective), three forwards each (window parities)
-    for mode, max_tok, exchange in (("split_sizes", None, "nccl"), ("fixed_capacity", tpr, "nccl"),
-                                    ("peer_memory", tpr, "p2p")):
+    # library's peer-memory exchange (no collective), three forwards each (window parities);
+    # the peer-memory exchange also with power-of-two activation scales
+    for mode, max_tok, exchange, ue8m0 in (("split_sizes", None, "nccl", False), ("fixed_capacity", tpr, "nccl", False),
+                                           ("peer_memory", tpr, "p2p", False),
+                                           ("peer_memory_ue8m0", tpr, "p2p", True)):
+        y_one = y_ref[ue8m0]
         layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=cfg["experts"], group=dist.group.WORLD,
-                         max_tokens_per_rank=max_tok, exchange=exchange)
+                         max_tokens_per_rank=max_tok, exchange=exchange, ue8m0=ue8m0)
         for it in range(3):
             y = layer(x[ts], ids[ts], w[ts])
             parts = [torch.empty_like(y) for _ in range(world)]

@@ -201,5 +201,5 @@ def test_layer_expert_parallel_two_gpus():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    for mode in ("split_sizes", "fixed_capacity", "peer_memory"):
+    for mode in ("split_sizes", "fixed_capacity", "peer_memory", "peer_memory_ue8m0"):
         assert f"EP_OK {mode}" in r.stdout, r.stdout[-3000:]
