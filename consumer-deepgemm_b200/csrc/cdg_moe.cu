@@ -153,10 +153,53 @@ __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, 
   quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
 }
 
-// One warp per (row, 128-column block of the output); gate = columns [0, I), up = [I, 2I).
-// VEC: the lane's four gate and four up values arrive as one 8-byte load each (rows 8-byte
-// aligned); otherwise one 2-byte load per value.
-template <bool VEC>
+// One warp per (row, kSiluBlocks 128-column blocks of the output); gate = columns [0, I),
+// up = [I, 2I); rows 8-byte aligned.  The lane's four gate and four up values of each block
+// arrive as one 8-byte load each, all of the warp's blocks issued before any is used, and the
+// row's m_indices entry is loaded alongside (a padding row's values are read and dropped), so
+// that a warp waits for memory once.
+constexpr int kSiluBlocks = 4;
+__global__ void __launch_bounds__(256) silu_mul_quant_vec_kernel(const __nv_bfloat16* in, int64_t in_stride,
+                                                                 int64_t M, int64_t I, const int32_t* m_indices,
+                                                                 uint8_t* q, int64_t q_stride, float* s,
+                                                                 int64_t s_stride_m, int64_t s_stride_k, int pow2) {
+  const int64_t kb_count = I / 128;
+  const int64_t chunks = (kb_count + kSiluBlocks - 1) / kSiluBlocks;
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= M * chunks) return;
+  const int64_t r = w / chunks, kb0 = (w - r * chunks) * kSiluBlocks;
+  const int nb = kb_count - kb0 < kSiluBlocks ? static_cast<int>(kb_count - kb0) : kSiluBlocks;
+  const int32_t id = m_indices ? __ldg(m_indices + r) : 0;
+  const __nv_bfloat16* gp = in + r * in_stride + kb0 * 128 + lane * 4;
+  uint2 g2[kSiluBlocks], u2[kSiluBlocks];
+#pragma unroll
+  for (int b = 0; b < kSiluBlocks; ++b) {
+    if (b < nb) {
+      g2[b] = __ldg(reinterpret_cast<const uint2*>(gp + b * 128));
+      u2[b] = __ldg(reinterpret_cast<const uint2*>(gp + I + b * 128));
+    }
+  }
+  if (id < 0) return;  // padding row: never read by the next GEMM
+#pragma unroll
+  for (int b = 0; b < kSiluBlocks; ++b) {
+    if (b < nb) {
+      const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&g2[b].x));
+      const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&g2[b].y));
+      const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2[b].x));
+      const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2[b].y));
+      const float gv[4] = {g01.x, g01.y, g23.x, g23.y}, uv[4] = {u01.x, u01.y, u23.x, u23.y};
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
+      quant_block_warp(v, q + r * q_stride + (kb0 + b) * 128, s + r * s_stride_m + (kb0 + b) * s_stride_k, lane,
+                       pow2);
+    }
+  }
+}
+
+// The same for rows that are not 8-byte aligned: one warp per (row, 128-column block), one
+// 2-byte load per value.
 __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride, int64_t M, int64_t I,
                                       const int32_t* m_indices, uint8_t* q, int64_t q_stride, float* s,
                                       int64_t s_stride_m, int64_t s_stride_k, int pow2) {
@@ -168,21 +211,10 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride
   if (m_indices && m_indices[r] < 0) return;  // padding row: never read by the next GEMM
   const __nv_bfloat16* gp = in + r * in_stride + kb * 128 + lane * 4;
   float gv[4], uv[4];
-  if (VEC) {
-    const uint2 g2 = *reinterpret_cast<const uint2*>(gp);
-    const uint2 u2 = *reinterpret_cast<const uint2*>(gp + I);
-    const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&g2.x));
-    const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&g2.y));
-    const float2 u01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2.x));
-    const float2 u23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2.y));
-    gv[0] = g01.x; gv[1] = g01.y; gv[2] = g23.x; gv[3] = g23.y;
-    uv[0] = u01.x; uv[1] = u01.y; uv[2] = u23.x; uv[3] = u23.y;
-  } else {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      gv[i] = __bfloat162float(gp[i]);
-      uv[i] = __bfloat162float(gp[I + i]);
-    }
+  for (int i = 0; i < 4; ++i) {
+    gv[i] = __bfloat162float(gp[i]);
+    uv[i] = __bfloat162float(gp[I + i]);
   }
   float v[4];
 #pragma unroll
@@ -619,10 +651,16 @@ int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t
   if (reinterpret_cast<uintptr_t>(q) % 4 || q_stride % 4) return CDG_ERR_ALIGNMENT;
   if (M == 0) return CDG_OK;
   const bool vec = reinterpret_cast<uintptr_t>(in) % 8 == 0 && in_stride % 4 == 0;
-  auto kernel = vec ? cdg::silu_mul_quant_kernel<true> : cdg::silu_mul_quant_kernel<false>;
-  kernel<<<cdg::warp_grid(M * (I / 128)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(in), in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k,
-      scale_fmt);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* h = static_cast<const __nv_bfloat16*>(in);
+  if (vec) {
+    const int64_t chunks = (I / 128 + cdg::kSiluBlocks - 1) / cdg::kSiluBlocks;
+    cdg::silu_mul_quant_vec_kernel<<<cdg::warp_grid(M * chunks), 256, 0, st>>>(
+        h, in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k, scale_fmt);
+  } else {
+    cdg::silu_mul_quant_kernel<<<cdg::warp_grid(M * (I / 128)), 256, 0, st>>>(
+        h, in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k, scale_fmt);
+  }
   return cdg::launched();
 }
 

@@ -57,10 +57,20 @@ def test_quant_fp8_rows_pow2_bit_exact():
 
 
 @pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
-def test_silu_mul_quant_matches_reference(ue8m0):
+@pytest.mark.parametrize("inter,aligned", [(512, True), (640, True), (384, True), (384, False)],
+                         ids=["i512", "i640", "i384", "i384_unaligned"])
+def test_silu_mul_quant_matches_reference(ue8m0, inter, aligned):
+    # rows 8-byte aligned: several 128-column blocks per warp (640: a partial group); unaligned
+    # rows (a view one column in): one block per warp with 2-byte loads
     g = torch.Generator().manual_seed(2)
-    h = torch.randn(200, 2 * 512, generator=g).to(torch.bfloat16)
-    q, s = _ext().silu_mul_quant(h.to(DEV), None, ue8m0)
+    h = torch.randn(200, 2 * inter, generator=g).to(torch.bfloat16)
+    if aligned:
+        hd = h.to(DEV)
+    else:
+        hd = torch.zeros(200, 2 * inter + 1, dtype=torch.bfloat16, device=DEV)
+        hd[:, 1:] = h.to(DEV)
+        hd = hd[:, 1:]
+    q, s = _ext().silu_mul_quant(hd, None, ue8m0)
     rq, rs = TorchRefOps().act(h, None, ue8m0)
     assert torch.allclose(s.cpu(), rs, rtol=1e-6, atol=0)
     a, b = q.cpu().view(torch.uint8).to(torch.int32), rq.view(torch.uint8).to(torch.int32)
