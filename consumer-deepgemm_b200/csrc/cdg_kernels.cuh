@@ -144,9 +144,10 @@ __device__ __forceinline__ int pow2_code(float v) {
 }
 
 // Activation scale of row r, 128-wide K block kb: FP32, or UE8M0 packed four to a word.
+// (Read-only loads: the scales are an input of the call, never written by it.)
 __device__ __forceinline__ float load_sa(const float* sa, int packed, int64_t sm, int64_t sk, int64_t r, int64_t kb) {
-  if (!packed) return sa[r * sm + kb * sk];
-  const uint32_t w = reinterpret_cast<const uint32_t*>(sa)[r * sm + (kb >> 2) * sk];
+  if (!packed) return __ldg(sa + r * sm + kb * sk);
+  const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(sa) + r * sm + (kb >> 2) * sk);
   return ue8m0_to_f32((w >> (8 * (kb & 3))) & 0xFFu);
 }
 
@@ -252,15 +253,28 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       const bool mn_major = !p.sa_packed && p.sa_stride_m == 1;
       const int items = ntok * kb_count;
       bool pow2 = true;
-      for (int it = tid; it < items; it += blockDim.x) {
-        const int rr = mn_major ? it % ntok : it / kb_count;
-        const int kb = mn_major ? it / ntok : it % kb_count;
-        if (s_id[rr] != expert) continue;
-        const float sraw = load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb);
-        const float sbf = __bfloat162float(__float2bfloat16_rn(sraw));
-        // non-negative floats order as their bit patterns
-        if (isfinite(sbf)) atomicMax(&s_smax_bits[rr], __float_as_uint(fabsf(sbf)));
-        pow2 = pow2 && pow2_code(sraw) >= 0;
+      // kU items per thread per round: their loads are all issued before any is used
+      constexpr int kU = 8;
+      for (int it0 = tid; it0 < items; it0 += kU * blockDim.x) {
+        float sraw[kU];
+        int rrs[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int it = it0 + u * blockDim.x;
+          const int rr = mn_major ? it % ntok : it / kb_count;
+          const int kb = mn_major ? it / ntok : it % kb_count;
+          const bool mine = it < items && s_id[rr] == expert;
+          rrs[u] = mine ? rr : -1;
+          sraw[u] = mine ? load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb) : 1.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          if (rrs[u] < 0) continue;
+          const float sbf = __bfloat162float(__float2bfloat16_rn(sraw[u]));
+          // non-negative floats order as their bit patterns
+          if (isfinite(sbf)) atomicMax(&s_smax_bits[rrs[u]], __float_as_uint(fabsf(sbf)));
+          pow2 = pow2 && pow2_code(sraw[u]) >= 0;
+        }
       }
       if (!pow2) atomicAnd(&s_pow2, 0);
       __syncthreads();
@@ -277,6 +291,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       s_inv[tid] = ldexpf(1.0f, -emax);
       if (blockIdx.y == 0) p.row_exp[b * 128 + tid] = emax;
     }
+#pragma unroll 4
     for (int it = tid; it < ntok * kbn; it += blockDim.x) {
       const int rr = it / kbn;
       const int kl = it - rr * kbn;
@@ -308,6 +323,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     const bool direct = cls == kClassWide && p.pair_wide && s_pow2;
     if (direct) {
       const int pitch = tok_code_pitch(K);
+#pragma unroll 4
       for (int it = tid; it < kbn * nrows; it += blockDim.x) {
         const int rr = it / kbn, kl = it - rr * kbn;
         int code = 127;
