@@ -72,6 +72,9 @@ class NativeOps:
     def quant_pack_fixed(self, x, topk_ids, num_experts, ranks, cap, ue8m0=False):
         return self.C.ep_quant_pack_fixed(x, topk_ids, num_experts, ranks, cap, ue8m0)
 
+    def quant_dispatch_local(self, x, topk_ids, num_experts, expert_off, m_pad, ue8m0=False):
+        return self.C.ep_quant_dispatch_local(x, topk_ids, num_experts, expert_off, m_pad, ue8m0)
+
     def permute_fixed(self, rows, hidden, local_experts, ranks, cap, m_pad):
         return self.C.ep_permute_fixed(rows, hidden, local_experts, ranks, cap, m_pad)
 
@@ -193,7 +196,8 @@ class MoELayer:
         dev = x.device
         topk_ids = topk_ids.contiguous()
         topk_w = topk_w.to(torch.float32).contiguous()
-        xq, xs = ops.quant(x, self.ue8m0)
+        if world > 1:
+            xq, xs = ops.quant(x, self.ue8m0)
         counts = ops.count(topk_ids, E)                                  # [E] rows per global expert
         if world > 1:
             both = torch.empty(2, E, dtype=counts.dtype, device=dev)
@@ -212,12 +216,22 @@ class MoELayer:
         expert_off, send_off = offs[:E_loc], offs[E_loc:]
         send_splits, recv_splits = send_splits.tolist(), recv_splits.tolist()
 
+        if world == 1:
+            # no exchange: quantise straight into the contiguous layout, combine straight from
+            # the GEMM's rows
+            a, sa, m_indices, perm_pos, send_index = ops.quant_dispatch_local(x, topk_ids, E, expert_off, m_pad,
+                                                                              self.ue8m0)
+            if m_pad == 0:
+                return ops.combine(torch.empty(0, self.out_dim, dtype=torch.bfloat16, device=dev), send_index, topk_w)
+            h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices)
+            if self.w2 is not None:
+                aq, asc = ops.act(h, m_indices, self.ue8m0)
+                h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
+            return ops.unpermute_combine(h, perm_pos, send_index, topk_w)
+
         sent, send_index = ops.pack(xq, xs, topk_ids, E, world, send_off, sum(send_splits))
-        if world > 1:
-            recv = _all_to_all(torch.empty(sum(recv_splits), sent.shape[1], dtype=sent.dtype, device=dev), sent,
-                               recv_splits, send_splits, self.group)
-        else:
-            recv = sent
+        recv = _all_to_all(torch.empty(sum(recv_splits), sent.shape[1], dtype=sent.dtype, device=dev), sent,
+                           recv_splits, send_splits, self.group)
 
         if m_pad > 0:
             a, sa, m_indices, perm_pos = ops.permute(recv, x.shape[1], E_loc, expert_off, m_pad)
@@ -225,17 +239,11 @@ class MoELayer:
             if self.w2 is not None:
                 aq, asc = ops.act(h, m_indices, self.ue8m0)
                 h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
-            if world == 1:
-                # no exchange: combine straight from the GEMM's rows (one pass instead of two)
-                return ops.unpermute_combine(h, perm_pos, send_index, topk_w)
             back = ops.unpermute(h, perm_pos)
         else:
             back = torch.empty(0, self.out_dim, dtype=torch.bfloat16, device=dev)
-        if world > 1:
-            out_rows = _all_to_all(torch.empty(sent.shape[0], self.out_dim, dtype=back.dtype, device=dev), back,
-                                   send_splits, recv_splits, self.group)
-        else:
-            out_rows = back
+        out_rows = _all_to_all(torch.empty(sent.shape[0], self.out_dim, dtype=back.dtype, device=dev), back,
+                               send_splits, recv_splits, self.group)
         return ops.combine(out_rows, send_index, topk_w)
 
     def _forward_fixed(self, x, topk_ids, topk_w):

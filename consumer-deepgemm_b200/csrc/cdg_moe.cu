@@ -120,8 +120,9 @@ __device__ bool wait_peer_flags(const int32_t* flags, int n, int32_t epoch, int3
 // pow2 != 0: the UE8M0 recipe (DeepGEMM's per-token cast with use_ue8m0 on SM100): scale =
 //   amax / 448 rounded up to a power of two (exactly: next exponent unless the mantissa is
 //   zero), q = e4m3(x / scale).  Such scales make the GEMM take its direct class.
-__device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* q, float* scale_out, int lane,
-                                                 int pow2) {
+// quant_block_values returns the lane's four codes (one 32-bit word) and the block's scale;
+// quant_block_warp stores them.
+__device__ __forceinline__ uint32_t quant_block_values(const float (&v)[4], int pow2, float& scale) {
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -135,8 +136,15 @@ __device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* q
     const float y = pow2 ? v[i] / s2 : v[i] / amax * 448.0f;
     packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3)) << (8 * i);
   }
-  reinterpret_cast<uint32_t*>(q)[lane] = packed;
-  if (lane == 0) *scale_out = pow2 ? s2 : amax / 448.0f;
+  scale = pow2 ? s2 : amax / 448.0f;
+  return packed;
+}
+
+__device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* q, float* scale_out, int lane,
+                                                 int pow2) {
+  float scale;
+  reinterpret_cast<uint32_t*>(q)[lane] = quant_block_values(v, pow2, scale);
+  if (lane == 0) *scale_out = scale;
 }
 
 // One warp per (row, 128-column block).
@@ -151,6 +159,56 @@ __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, 
 #pragma unroll
   for (int i = 0; i < 4; ++i) v[i] = load_f(x, x_dtype, r * x_stride + kb * 128 + lane * 4 + i);
   quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
+}
+
+// Quantise and lay out for the grouped GEMM in one pass, when there is no exchange (one rank):
+// one CTA per token reads its row once, quantises each 128-column block (one warp per block)
+// and writes the codes and scale to the contiguous-layout row of every routed slot (row
+// expert_off[e] + a per-expert counter, e = topk_ids[t, j] in [0, E)).  perm_pos[t*topk + j]
+// is that row and send_index[t*topk + j] the slot itself (-1 for skipped slots), the form
+// the combine step reads.  fill: [E] counters, zeroed by the host.
+__global__ void __launch_bounds__(128) ep_quant_dispatch_local_kernel(
+    const void* x, int x_dtype, int64_t x_stride, const void* ids, int ids_dtype, int64_t topk, int64_t E,
+    int64_t H, const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices,
+    int32_t* perm_pos, int32_t* send_index, int pow2) {
+  constexpr int kMaxTopk = 32;
+  __shared__ int64_t s_row[kMaxTopk];
+  const int64_t t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x < topk) {
+    const int64_t i = t * topk + threadIdx.x;
+    const int64_t e = load_idx(ids, ids_dtype, i);
+    int64_t row = -1;
+    if (e >= 0 && e < E) {
+      row = expert_off[e] + atomicAdd(&fill[e], 1);
+      m_indices[row] = static_cast<int32_t>(e);
+    }
+    s_row[threadIdx.x] = row;
+    perm_pos[i] = static_cast<int32_t>(row);
+    send_index[i] = row >= 0 ? static_cast<int32_t>(i) : -1;
+  }
+  __syncthreads();
+  for (int64_t kb = warp; kb < H / 128; kb += blockDim.x / 32) {
+    float v[4];
+    const int64_t base = t * x_stride + kb * 128 + lane * 4;
+    if (x_dtype == CDG_DTYPE_BF16) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + base);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
+      v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    } else {
+      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + base);
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    }
+    float scale;
+    const uint32_t packed = quant_block_values(v, pow2, scale);
+    for (int j = 0; j < topk; ++j) {
+      const int64_t row = s_row[j];
+      if (row < 0) continue;
+      reinterpret_cast<uint32_t*>(A + row * H + kb * 128)[lane] = packed;
+      if (lane == 0) SA[row * (H / 128) + kb] = scale;
+    }
+  }
 }
 
 // One warp per (row, kSiluBlocks 128-column blocks of the output); gate = columns [0, I),
@@ -781,6 +839,29 @@ int cdg_ep_combine(const void* rows, const int32_t* send_index, const float* top
                    int64_t H, void* y, cdg_stream_t stream) {
   return cdg::launch_combine(rows, H, nullptr, send_index, topk_w, T, topk, H, y,
                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cdg_ep_quant_dispatch_local(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids,
+                                int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t H,
+                                const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices,
+                                int64_t M_pad, int32_t* perm_pos, int32_t* send_index, int32_t scale_fmt,
+                                cdg_stream_t stream) {
+  if (T < 0 || topk <= 0 || topk > 32 || E <= 0 || H <= 0 || H % 128 || M_pad < 0 || !fill || !expert_off ||
+      (T > 0 && (!x || !topk_ids || !A || !SA || !m_indices || !perm_pos || !send_index)))
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (scale_fmt != CDG_SCALE_FP32 && scale_fmt != CDG_SCALE_POW2) return CDG_ERR_INVALID_ARGUMENT;
+  if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
+  if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4 || reinterpret_cast<uintptr_t>(A) % 16)
+    return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fill, 0, E * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (M_pad > 0 && cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (T == 0) return CDG_OK;
+  cdg::ep_quant_dispatch_local_kernel<<<static_cast<unsigned>(T), 128, 0, st>>>(
+      x, x_dtype, x_stride, topk_ids, ids_dtype, topk, E, H, expert_off, fill, A, SA, m_indices, perm_pos,
+      send_index, scale_fmt);
+  return cdg::launched();
 }
 
 int cdg_ep_unpermute_combine(const void* Y, int64_t y_stride, const int32_t* perm_pos, const int32_t* send_index,

@@ -269,6 +269,33 @@ std::vector<torch::Tensor> ep_permute(const torch::Tensor& rows, int64_t H, int6
   return {A, SA, mi, pos};
 }
 
+// One rank: quantise + contiguous layout in one pass -> (A, SA, m_indices, perm_pos, send_index).
+std::vector<torch::Tensor> ep_quant_dispatch_local(const torch::Tensor& x, const torch::Tensor& ids, int64_t E,
+                                                   const torch::Tensor& expert_off, int64_t M_pad, bool ue8m0) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
+  TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
+              "topk ids must be contiguous [T, topk]");
+  TORCH_CHECK(expert_off.is_cuda() && expert_off.scalar_type() == torch::kInt64 && expert_off.numel() == E,
+              "expert_off: int64 [E] on the device");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), H = x.size(1), topk = ids.size(1);
+  auto i32 = ids.options().dtype(torch::kInt32);
+  auto A = torch::empty({M_pad, H}, x.options().dtype(torch::kFloat8_e4m3fn));
+  auto SA = torch::ones({M_pad, H / 128}, x.options().dtype(torch::kFloat32));
+  auto mi = torch::empty({M_pad}, i32);
+  auto pos = torch::empty({T * topk}, i32);
+  auto send_index = torch::empty({T * topk}, i32);
+  auto fill = torch::empty({E}, i32);
+  check_status(cdg_ep_quant_dispatch_local(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T,
+                                           topk, E, H, expert_off.data_ptr<int64_t>(), fill.data_ptr<int32_t>(),
+                                           reinterpret_cast<uint8_t*>(A.data_ptr()), SA.data_ptr<float>(),
+                                           mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(),
+                                           send_index.data_ptr<int32_t>(), ue8m0 ? CDG_SCALE_POW2 : CDG_SCALE_FP32,
+                                           cur_stream(x)),
+               "ep_quant_dispatch_local");
+  return {A, SA, mi, pos, send_index};
+}
+
 // Fixed-capacity send buffer: (packed rows uint8 [ranks*(cap+1), row_bytes], send_index [T*topk]).
 std::vector<torch::Tensor> ep_quant_pack_fixed(const torch::Tensor& x, const torch::Tensor& ids, int64_t E,
                                                int64_t ranks, int64_t cap, bool ue8m0) {
@@ -470,6 +497,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("expert_off"), py::arg("m_pad"));
   m.def("ep_quant_pack_fixed", &ep_quant_pack_fixed, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
         py::arg("ranks"), py::arg("cap"), py::arg("ue8m0") = false);
+  m.def("ep_quant_dispatch_local", &ep_quant_dispatch_local, py::arg("x"), py::arg("topk_ids"),
+        py::arg("num_experts"), py::arg("expert_off"), py::arg("m_pad"), py::arg("ue8m0") = false);
   m.def("ep_permute_fixed", &ep_permute_fixed, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("ranks"), py::arg("cap"), py::arg("m_pad"));
   m.def("mega_moe_transform_rows", &mega_moe_transform_rows, py::arg("t"), py::arg("kind"));

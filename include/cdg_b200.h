@@ -265,6 +265,20 @@ int cdg_ep_permute(const uint8_t* recv_rows, int64_t R, int64_t H, int64_t E_loc
                    int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                    cdg_stream_t stream);
 
+/* One rank, no exchange: quantise each token's row once (1x128 e4m3, scale_fmt recipe) and
+ * write it straight into the contiguous layout, at row expert_off[e] + k of every slot (t, j)
+ * whose expert e = topk_ids[t, j] is in [0, E) (k counts the expert's rows; expert_off are the
+ * 128-aligned offsets from cdg_ep_count's counts).  m_indices[M_pad] is -1 except on placed
+ * rows; perm_pos[t*topk + j] is the slot's row and send_index[t*topk + j] the slot itself (-1
+ * for skipped slots): the arguments cdg_ep_unpermute_combine takes.  Replaces the
+ * quantise / pack / permute sequence (one read of x, no intermediate rows).  `fill` is [E]
+ * scratch; topk <= 32; row order within an expert depends on timing. */
+int cdg_ep_quant_dispatch_local(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids,
+                                int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t H,
+                                const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices,
+                                int64_t M_pad, int32_t* perm_pos, int32_t* send_index, int32_t scale_fmt,
+                                cdg_stream_t stream);
+
 /* Fixed-capacity exchange (no host synchronisation).  The send (and receive) buffer holds
  * per destination (source) rank a region of 1 + cap packed rows of cdg_ep_row_bytes(H):
  * row 0 a header with the int32 number of rows routed to each of that rank's E/ranks local

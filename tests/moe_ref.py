@@ -103,6 +103,26 @@ class TorchRefOps:
             out[d * (cap + 1), :4 * per_rank] = cnt[d].view(torch.uint8)
         return out, send_index
 
+    def quant_dispatch_local(self, x, topk_ids, num_experts, expert_off, m_pad, ue8m0=False):
+        """One rank: quantised rows straight into the contiguous layout, slots in order."""
+        T, k = topk_ids.shape
+        H = x.shape[1]
+        xq, xs = self.quant(x, ue8m0)
+        a = torch.zeros(m_pad, H, dtype=torch.float8_e4m3fn)
+        sa = torch.ones(m_pad, H // 128, dtype=torch.float32)
+        m_indices = torch.full((m_pad,), -1, dtype=torch.int32)
+        perm_pos = torch.full((T * k,), -1, dtype=torch.int32)
+        send_index = torch.full((T * k,), -1, dtype=torch.int32)
+        fill = [0] * num_experts
+        for i, e in enumerate(topk_ids.flatten().tolist()):
+            if not 0 <= e < num_experts:
+                continue
+            p = int(expert_off[e]) + fill[e]
+            fill[e] += 1
+            a[p], sa[p], m_indices[p] = xq[i // k], xs[i // k], e
+            perm_pos[i], send_index[i] = p, i
+        return a, sa, m_indices, perm_pos, send_index
+
     def permute_fixed(self, rows, hidden, local_experts, ranks, cap, m_pad):
         """Fixed-capacity receive buffer: source r's header at row r*(cap+1), its rows after it."""
         H, nkb = hidden, hidden // 128

@@ -148,6 +148,34 @@ def test_combine_scalar_path_matches_vector_path():
 
 
 @pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
+@pytest.mark.parametrize("xdtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+def test_quant_dispatch_local_exact(ue8m0, xdtype):
+    """One rank: quantise straight into the contiguous layout; the rows land in any order within
+    an expert's region, so each slot's row is compared with the reference's row of that slot."""
+    C = _ext()
+    T, H, k, E = 300, 512, 4, 12
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(T, H, generator=g).to(xdtype)
+    ids = torch.rand(T, E, generator=g).topk(k, dim=1).indices.to(torch.int32)
+    ids[5, 2] = -1  # a skipped slot
+    ids[6, 0] = E   # out of range: skipped too
+    counts = torch.bincount(ids[(ids >= 0) & (ids < E)].long(), minlength=E)
+    aligned = (counts + 127) // 128 * 128
+    off = torch.cumsum(aligned, 0) - aligned
+    m_pad = int(aligned.sum())
+    a, sa, mi, pos, si = C.ep_quant_dispatch_local(x.to(DEV), ids.to(DEV), E, off.to(DEV), m_pad, ue8m0)
+    ra, rsa, rmi, rpos, rsi = TorchRefOps().quant_dispatch_local(x, ids, E, off, m_pad, ue8m0)
+    a, sa, mi, pos, si = a.cpu().view(torch.uint8), sa.cpu(), mi.cpu(), pos.cpu(), si.cpu()
+    assert torch.equal(si, rsi) and torch.equal(pos < 0, rpos < 0)
+    ok = pos >= 0
+    assert torch.equal(a[pos[ok].long()], ra.view(torch.uint8)[rpos[ok].long()])
+    assert torch.equal(sa[pos[ok].long()], rsa[rpos[ok].long()])
+    assert torch.equal(mi[pos[ok].long()], rmi[rpos[ok].long()])
+    assert torch.equal(torch.sort(mi).values, torch.sort(rmi).values)  # same groups, same padding
+    assert len(set(pos[ok].tolist())) == int(ok.sum())  # every slot its own row
+
+
+@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
 def test_fixed_capacity_pack_and_permute_exact(ue8m0):
     """Fused quant+pack into fixed-capacity regions, then the receive-side permute: bytes."""
     C = _ext()
