@@ -88,11 +88,14 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 200 ms while the benchmark runs."""
+    """nvidia-smi clock/throttle samples every 50 ms while the benchmark runs; stop(window)
+    reports the samples taken inside the timed region (host wall-clock window of Timed.run,
+    widened by one sampling period), else the samples under load."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.hw_slowdown,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 50
 
     def __init__(self, device_index: int):
         self.proc = None
@@ -101,11 +104,11 @@ class ClockSampler:
             sel = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", sel,
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.PERIOD_MS)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def stop(self, window=None):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -117,19 +120,25 @@ class ClockSampler:
         rows = []
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 8:
+            if len(f) < 9:
                 continue
             try:
-                rows.append((float(f[0]), float(f[1]), float(f[2]), float(f[3]), f[4:8]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((float(f[1]), float(f[2]), float(f[3]), float(f[4]), f[5:9], ts))
             except ValueError:
                 continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        loaded = [r for r in rows if r[3] >= 50] or rows
+        chosen, where = [], "timed region"
+        if window is not None:
+            pad = self.PERIOD_MS / 1000.0
+            chosen = [r for r in rows if window[0] - pad <= r[5] <= window[1] + pad]
+        if not chosen:
+            chosen, where = [r for r in rows if r[3] >= 50] or rows, "samples under load (none in the timed region)"
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[4]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "samples": len(loaded), "reasons": reasons}
+        reasons = sorted({names[i] for r in chosen for i, v in enumerate(r[4]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in chosen), "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(chosen), "sampled": where, "reasons": reasons}
 
 
 def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
@@ -216,6 +225,7 @@ class Timed:
 
     def run(self, step, steps, with_kernel_events=True):
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        wall0 = time.time()
         t0.record(self.stream)
         for i in range(steps):
             if with_kernel_events:
@@ -224,6 +234,7 @@ class Timed:
         self.ext.set_profile_events(0, 0)
         t1.record(self.stream)
         torch.cuda.synchronize()
+        self.window = (wall0, time.time())  # host wall-clock span holding the timed device work
         ms = t0.elapsed_time(t1) / steps
         kms = statistics.fmean(s.elapsed_time(e) for s, e in self.kev[:steps]) if with_kernel_events else None
         return ms, kms
@@ -303,6 +314,7 @@ def bench_gemm(args, dev, cfg_name):
         call()
     timer = Timed(dev, args.steps)
     ms, kernel_ms = timer.run(call, args.steps)
+    timed_window = timer.window
 
     h_a, h_sa, h_ids = a.cpu().pin_memory(), sa.cpu().pin_memory(), ids.cpu().pin_memory()
     h_d = torch.empty(d.shape, dtype=d.dtype).pin_memory()
@@ -318,7 +330,7 @@ def bench_gemm(args, dev, cfg_name):
     for _ in range(args.warmup):
         e2e_call()
     e2e_ms, _ = timer.run(e2e_call, args.steps, with_kernel_events=False)
-    clocks = sampler.stop()
+    clocks = sampler.stop(timed_window)
     hbm_peak, bf16_peak, peak_src = measured_peaks()
     achieved_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
     achieved_tf = flops / (kernel_ms * 1e-3) / 1e12
@@ -427,6 +439,7 @@ def bench_ep_decode(args, dev, world, rank, dist):
     dist.barrier()
     torch.cuda.synchronize(dev)
     ms, _ = timer.run(step, args.steps, with_kernel_events=False)
+    timed_window = timer.window
     dist.barrier()
 
     h_x, h_ids, h_w = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
@@ -452,7 +465,7 @@ def bench_ep_decode(args, dev, world, rank, dist):
     dist.barrier()
     torch.cuda.synchronize(dev)
     e2e_ms, _ = timer.run(e2e_step, args.steps, with_kernel_events=False)
-    clocks = sampler.stop()
+    clocks = sampler.stop(timed_window)
     ms, e2e_ms, kernel_ms = _max_over_ranks(dist, dev, ms, e2e_ms, kernel_ms)
     torch.cuda.synchronize(dev)
     dist.barrier()
@@ -515,7 +528,7 @@ def bench_layer(args, dev, world, rank, dist):
     torch.cuda.synchronize(dev)
     # the library's profile events bracket the last GEMM call of a step (FC2)
     ms, fc2_ms = timer.run(step, args.steps)
-    clocks = sampler.stop()
+    clocks = sampler.stop(timer.window)
     ms, fc2_ms = _max_over_ranks(dist, dev, ms, fc2_ms)
     _, bf16_peak, peak_src = measured_peaks()
     fp8_peak = 2 * bf16_peak
