@@ -111,3 +111,19 @@ def test_masked_groups_span_blocks(pow2):
     b, sb = synthetic.make_weights(e, 256, k, "cpu", seed=5)
     cls = _check(a, sa, b, sb, counts, masked=True)
     assert cls["wide_direct" if pow2 else "wide"] >= 6, cls
+
+
+@pytest.mark.parametrize("k", [512, 1152], ids=["k512", "k1152"])
+def test_direct_and_plane_blocks_within_one_expert(k):
+    # power-of-two scales everywhere except one row of expert 0's second block and one row of
+    # expert 1's last block: those blocks take the plane kernel, which splits the experts'
+    # runs of direct blocks around them (direct | planes | direct, and direct ... | planes)
+    counts = [384, 300, 200]
+    a, sa, ids = _contiguous(counts, k, True, seed=k + 7)
+    for r in (128 + 5, 384 + 256 + 10):  # rows in expert 0's block 1 and expert 1's block 2
+        sa[r, 0] *= 1.5
+    b, sb = synthetic.make_weights(len(counts), 256, k, "cpu", seed=6)
+    cls = _check(a, sa, b, sb, ids)
+    # expert 0: blocks 0, 2 direct, 1 planes; expert 1: blocks 0, 1 direct, 2 planes (tail of 44
+    # rows); expert 2: two direct blocks (the 72-row tail joins the wide class)
+    assert cls["wide"] == 2 and cls["wide_direct"] == 2 + 2 + 2, cls
