@@ -28,8 +28,9 @@
 // blocks (more than 32 rows) run the token-tile kernels instead (cdg_gemm_planes_kernel,
 // cdg_gemm_direct_kernel).
 //
-// Warp roles per CTA: 0 = TMA producer, 1..NI = MMA issuers (even CTA; warp 1 also
-// owns TMEM), then four epilogue warps (4-7, or 5-8 when NI = 4).
+// Warp roles per CTA: 0 = TMA producer of the weight tiles, 1..NI = MMA issuers (even CTA;
+// warp 1 also owns TMEM), then four epilogue warps (4-7, or 5-8 when NI = 4), then the TMA
+// producer of the activation planes and weight scale atoms (8 or 9).
 #pragma once
 
 #include "cdg_kernels.cuh"
@@ -69,7 +70,8 @@ struct PairSmem {
   static constexpr uint32_t kSfaCol = kSfwCol + 8 * NI;
   static_assert(kSfaCol + 4 * NI <= 512, "TMEM columns");
   static constexpr int kEpiWarp0 = NI < 4 ? 4 : NI + 1;
-  static constexpr int kThreads = (kEpiWarp0 + 4) * 32;
+  static constexpr int kActWarp = kEpiWarp0 + 4;  // second TMA producer: activation plane + scale atom
+  static constexpr int kThreads = (kActWarp + 1) * 32;
 };
 
 template <int TOK, int NI>
@@ -152,12 +154,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
       for (int t = pair; t < reg_tiles && ok; t += npairs) {
         const int4 cur = next;
         if (t + npairs < reg_tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
-        const int blk = cur.x;
         const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
-        const int expert = cur.y;
-        const int wrow = expert * p.N + nt * 128;
-        const int atom0 = (expert * n_tiles + nt) * k_steps;
-        const int a_row = blk * 128;
+        const int wrow = cur.y * p.N + nt * 128;
         for (int kb = 0; kb < k_steps; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1, p.status,
                                  wait_code(1, static_cast<int>(rank), stage, phase ^ 1, kb))) {
@@ -165,8 +163,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
             break;
           }
           const uint32_t fb = full0 + stage * 8;
+          // this stage's weight tile; the activation plane and the weight scale atom come from
+          // the second producer (warp kActWarp), onto the same barrier
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * L::kTxPerCta);
           tma_load_2d_pair(stage_w(stage), &tmap_w, fb, kb * 128, wrow);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == L::kActWarp) {
+    // ------------------------------------------------------------ second TMA producer (both CTAs)
+    // A single thread issuing all three copies of a K step held the decode kernel at the rate it
+    // issues them (its time followed the SM clock); the copies of a stage are split over two.
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint32_t full0 = cluster_addr(&full[0], 0);
+      for (int t = pair; t < reg_tiles && ok; t += npairs) {
+        const int4 cur = __ldg(&p.list[t / n_pt]);
+        const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
+        const int atom0 = (cur.y * n_tiles + nt) * k_steps;
+        const int a_row = cur.x * 128;
+        for (int kb = 0; kb < k_steps; ++kb) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1, p.status,
+                                 wait_code(1, static_cast<int>(rank), stage, phase ^ 1, kb))) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + stage * 8;
           tma_load_3d_pair(stage_a(stage), &tmap_a, fb, kb * 128, a_row, static_cast<int>(rank));
           tma_load_2d_pair(stage_sf(stage), &tmap_sf, fb, 0, atom0 + kb);
           if (++stage == S) { stage = 0; phase ^= 1; }
