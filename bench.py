@@ -57,7 +57,7 @@ GEMM_LAUNCHES = 6
 # DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
 # captures summarised under profiles/ (absent: no capture of the current kernels yet).
 NCU_TRAFFIC = {
-    "c1": 2.007860e9 + 0.223218e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
+    "c1": 2.008183e9 + 0.223044e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
     "c2": 1.427530e9 + 0.654704e9,  # cdg_gemm_planes_kernel: profiles/cdg_gemm_planes_kernel_c2_prefill.md
     "c2u": 1.281316e9 + 0.648415e9,  # cdg_gemm_direct_kernel: profiles/cdg_gemm_direct_kernel_c2u_prefill.md
 }
