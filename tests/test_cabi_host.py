@@ -99,3 +99,26 @@ def test_sf_atoms_bytes():
     assert lib.cdg_sf_atoms_bytes(256, 4096, 128) == 256 * 32 * 32 * 512
     assert lib.cdg_sf_atoms_bytes(1, 300, 10) == 3 * 3 * 512
     assert lib.cdg_sf_atoms_bytes(0, 1, 1) == 0
+
+
+def test_quantising_entry_points_validate_scale_format_and_topk():
+    """scale_fmt outside {CDG_SCALE_FP32, CDG_SCALE_POW2} and the one-rank dispatch's limits are
+    refused on the host, before anything is launched (fake device addresses)."""
+    lib = cabi.lib()
+    P, I64, I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    lib.cdg_quant_fp8_rows.argtypes = [P, I32, I64, I64, I64, P, I64, P, I64, I64, I32, P]
+    lib.cdg_silu_mul_quant_fp8.argtypes = [P, I64, I64, I64, P, P, I64, P, I64, I64, I32, P]
+    lib.cdg_ep_quant_dispatch_local.argtypes = [P, I32, I64, P, I32, I64, I64, I64, I64, P, P, P, P, P, I64, P, P,
+                                                I32, P]
+    x = P(1 << 20)
+    bf16, i32 = cabi.DT["bf16"], cabi.DT["i32"]
+    invalid = 1  # CDG_ERR_INVALID_ARGUMENT
+    assert lib.cdg_quant_fp8_rows(x, bf16, 512, 4, 512, x, 512, x, 4, 1, 2, None) == invalid
+    assert lib.cdg_silu_mul_quant_fp8(x, 1024, 4, 512, None, x, 512, x, 4, 1, -1, None) == invalid
+    # topk above 32, then a bad scale format
+    assert lib.cdg_ep_quant_dispatch_local(x, bf16, 512, x, i32, 4, 33, 8, 512, x, x, x, x, x, 1024, x, x, 0,
+                                           None) == invalid
+    assert lib.cdg_ep_quant_dispatch_local(x, bf16, 512, x, i32, 4, 8, 8, 512, x, x, x, x, x, 1024, x, x, 7,
+                                           None) == invalid
+    # K not a multiple of 128
+    assert lib.cdg_quant_fp8_rows(x, bf16, 500, 4, 500, x, 500, x, 4, 1, 0, None) == invalid
