@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference checkout is importable::
 
-    python tests/golden/make_golden.py [--ref /path/to/Consumer-DeepGEMM]
+    python tests/golden/make_golden.py --ref /path/to/Consumer-DeepGEMM   (or CDG_REFERENCE_ROOT=...)
 
 The reference package is loaded under the alias ``ref_cdg`` (so it cannot clash
 with this repository's ``consumer_deep_gemm``) and its CPU path is called on
@@ -88,8 +88,11 @@ def gemm_case(gemm, name, a, sa, b, sb, m_indices, d_dtype=torch.bfloat16, fn="f
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("CDG_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("CDG_REFERENCE_ROOT"),
+                    help="checkout of the reference project (or set CDG_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the reference checkout with --ref or CDG_REFERENCE_ROOT")
     gemm = load_reference(args.ref)
     from consumer_deep_gemm import synthetic
     from deep_gemm.utils.math import per_block_cast_to_fp4, per_block_cast_to_fp8
