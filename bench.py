@@ -1,35 +1,34 @@
 #!/usr/bin/env python
 """Benchmark of the grouped FP8 x MXFP4 MoE GEMM (m_grouped_fp8_fp4_gemm_nt_contiguous).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1|c2|c3|c4|c2u|c3u|c4u] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4|c4u|c1|c2|c3|c2u|c3u|c1-ep]
+                    [--impl ours|reference]
 
 Workloads (seeded synthetic data with the configs' shapes and distributions,
 consumer_deep_gemm.synthetic; weights transformed once at load and resident):
 
-* N = 1, default c1: one step = one call of the public API on the decode FC1
-  batch (E=256, K=N=4096, 64 tokens x top-8, 222 active experts), the HBM-bound
-  case the metric is quoted on.  --config c2/c3 run the prefill shapes.
-* N > 1 (launched by torchrun), default: every rank serves its own c1-sized
-  decode batch (rank-seeded tokens and routing); the 256 experts are sharded
-  over the ranks (expert parallelism).  One step = quantise the rank's tokens,
-  exchange per-expert counts and dispatch the routed rows to the experts'
-  owners (NCCL all-to-all), run the grouped GEMM on the local experts, return
-  the rows (all-to-all) and combine them per token.  Weak scaling: per-rank
-  tokens fixed, the expert weights divided.
-* --config c4: the full expert-parallel MoE layer (FC1 -> SiLU-mul + requant ->
-  FC2), 32768 tokens x top-8 split over the ranks, E=256, hidden 4096,
-  intermediate 2048.  Strong scaling; reported in TFLOP/s.
-* --config c2u / c3u / c4u: c2, c3 and c4 with power-of-two (UE8M0) activation scales,
-  the format DeepGEMM's SM100 path quantises to (c4u: the layer quantises that way).
+* default, any N (N > 1 launched by torchrun): c4, the expert-parallel MoE layer
+  FC1 -> SiLU-mul + FP8 requant -> FC2 around two grouped GEMMs, 32768 tokens x top-8
+  split evenly over the ranks, E=256 experts sharded over the ranks, hidden 4096,
+  intermediate 2048.  One step = one forward of the layer: on one rank the tokens are
+  quantised straight into the contiguous layout; on N ranks the library's peer-memory
+  exchange moves the rows over NVLink (dispatch and return stores straight into the
+  other GPUs' windows, no collective and no host synchronisation on the data path).
+  Strong scaling: the whole job is fixed, value = its FLOPs / step time (max over ranks).
+  At N = 1 the line also carries `workloads`: the GEMM alone on c1 (decode, HBM-bound),
+  c2 and c3 (prefill, tensor-bound), each with its own time, roofline and CPU baseline.
+* --config c1|c2|c3|c2u|c3u (N = 1): the public GEMM call alone on that config.
+* --config c4u: c4 with power-of-two (UE8M0) activation scales.
+* --config c1-ep: each rank a c1-sized decode batch (64 tokens x top-8, FC1 only), experts
+  sharded; weak scaling, GB/s.
 
-One JSON line on rank 0.  `value` = algorithmic bytes (or FLOPs for c4) of the
-whole job per step / device time of K steps (max over ranks).  Algorithmic bytes
-count routed rows of A and their scales, the weights and scales of experts that
-receive rows, and routed rows of D; padding-row zeros are not counted.  `e2e`
-times the same steps with the per-step inputs copied from pinned host memory and
-the result copied back.  `roofline` relates the tensor-core GEMM kernels' own
-duration (CUDA events the library records around them) to the measured HBM copy
-bandwidth (or 2x the measured BF16 GEMM rate for c4).
+One JSON line on rank 0.  `value` = algorithmic FLOPs (bytes for the decode configs) of the
+whole job per step / device time of K steps (CUDA events, max over ranks).  `e2e` times the
+same steps through the public API with the step's inputs copied from pinned host memory and
+its result copied back.  `roofline` relates the dominant kernel's own time (CUDA events the
+library records around its tensor-core kernels) to the measured peaks.  `parity` compares
+sampled output rows with a float32 reference of the same computation (below), outside the
+timed region; a failed check fails the run.
 """
 
 from __future__ import annotations
@@ -39,8 +38,8 @@ import datetime
 import json
 import os
 import statistics
-import subprocess
 import sys
+import threading
 import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
@@ -54,6 +53,10 @@ DTYPE = "fp8e4m3 x e2m1 -> fp32 acc -> bf16"
 # library kernels per GEMM call on the CTA-pair path: cdg_prep_kernel, cdg_gemm_pair_kernel<16,4>,
 # <32,2>, cdg_gemm_planes_kernel, cdg_gemm_direct_kernel, cdg_generic_kernel
 GEMM_LAUNCHES = 6
+# library kernels of one layer step besides its two GEMM calls: one rank: count, quantise into
+# the layout, SiLU-mul requant, unpermute + combine; N ranks: dispatch, permute, SiLU-mul
+# requant, return, combine
+LAYER_LAUNCHES = {True: 4, False: 5}
 # DRAM bytes (read + write) of one GEMM call's dominant kernel per workload, from the ncu
 # captures summarised under profiles/ (absent: no capture of the current kernels yet).
 NCU_TRAFFIC = {
@@ -61,8 +64,7 @@ NCU_TRAFFIC = {
     "c2": 1.427530e9 + 0.654704e9,  # cdg_gemm_planes_kernel: profiles/cdg_gemm_planes_kernel_c2_prefill.md
     "c2u": 1.281316e9 + 0.648415e9,  # cdg_gemm_direct_kernel: profiles/cdg_gemm_direct_kernel_c2u_prefill.md
 }
-# per EP step on top of the GEMM kernels: dispatch (quantise + pack), permute, return (or unpermute), combine
-EP_LAUNCHES = 4
+LAYER_TOL = 1e-2  # end-to-end layer tolerance (normwise and per-row L2), see parity_layer
 
 
 def gemm_bytes(rows, e_act, n, k):
@@ -79,68 +81,90 @@ def algorithmic(inp):
 
 
 def measured_peaks():
+    """(HBM GB/s, BF16 TFLOP/s burst, BF16 TFLOP/s sustained, source)."""
     try:
         with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+        return (float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained", 0.0)) or None,
+                "measured")
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------ clocks
+_REASON_BITS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+                0x80: "hw_power_brake_slowdown"}
+
+
+def _nvml_reader(device_index: int):
+    """A function returning (sm_mhz, max_sm_mhz, power_w, util_pct, reasons_mask) of the CUDA
+    device `device_index` through NVML (matched by UUID), or None when NVML is unavailable."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+
+        def read():
+            return (pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), max_mhz,
+                    pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0, pynvml.nvmlDeviceGetUtilizationRates(h).gpu,
+                    int(reasons(h)))
+        read()
+        return read
+    except Exception:
+        return None
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples every 50 ms while the benchmark runs; stop(window)
-    reports the samples taken inside the timed region (host wall-clock window of Timed.run,
-    widened by one sampling period), else the samples under load."""
+    """SM clock, power and clock-event reasons sampled every 20 ms (NVML, read only) by a
+    background thread while the benchmark runs; stop(window) reports the samples taken inside
+    the timed region (host wall-clock window of the timed steps, widened by one period), else
+    the samples under load."""
 
-    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
-    PERIOD_MS = 50
+    PERIOD_S = 0.02
 
-    def __init__(self, device_index: int):
-        self.proc = None
-        try:
-            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
-            sel = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", sel,
-                 "-lms", str(self.PERIOD_MS)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+    def __init__(self, device_index: int | None = None, reader=None):
+        self.samples = []  # (t, sm_mhz, max_mhz, power_w, util, reasons_mask)
+        self.reader = reader if reader is not None else (_nvml_reader(device_index) if device_index is not None
+                                                          else None)
+        self._stop = threading.Event()
+        self.thread = None
+        if self.reader is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append((time.time(), *self.reader()))
+            except Exception:
+                pass
+            self._stop.wait(self.PERIOD_S)
 
     def stop(self, window=None):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except Exception:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        rows = []
-        for line in out.strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                rows.append((float(f[1]), float(f[2]), float(f[3]), float(f[4]), f[5:9], ts))
-            except ValueError:
-                continue
+        self._stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        rows = list(self.samples)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         chosen, where = [], "timed region"
         if window is not None:
-            pad = self.PERIOD_MS / 1000.0
-            chosen = [r for r in rows if window[0] - pad <= r[5] <= window[1] + pad]
+            pad = self.PERIOD_S
+            chosen = [r for r in rows if window[0] - pad <= r[0] <= window[1] + pad]
         if not chosen:
-            chosen, where = [r for r in rows if r[3] >= 50] or rows, "samples under load (none in the timed region)"
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in chosen for i, v in enumerate(r[4]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in chosen), "sm_max_mhz": max(r[1] for r in rows),
-                "samples": len(chosen), "sampled": where, "reasons": reasons}
+            chosen, where = [r for r in rows if r[4] >= 50] or rows, "samples under load (none in the timed region)"
+        reasons = sorted({name for r in chosen for bit, name in _REASON_BITS.items() if r[5] & bit})
+        return {"sm_mhz": statistics.median(r[1] for r in chosen), "sm_max_mhz": max(r[2] for r in rows),
+                "power_w_max": max(r[3] for r in chosen), "samples": len(chosen), "sampled": where,
+                "reasons": reasons}
 
 
+# ------------------------------------------------------------------------------------ CPU baselines
 def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
     """Time the CPU oracle (the reference's dequant + matmul restated) on a bounded sample.
 
@@ -183,23 +207,98 @@ def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0)
     return rates, torch.get_num_threads(), desc
 
 
+def cpu_layer_sample(x, ids, w1, s1, w2, s2, ue8m0=False, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
+    """Time the CPU reference of the MoE layer (the oracle's grouped GEMM for FC1 and FC2, the
+    reference quantisation and SiLU-mul between them) on the first tokens of a batch, grown
+    until one call takes about `budget_s`.  Weights are fetched per call for the experts the
+    sample touches.  Returns (TFLOP/s of the median call, cores, description)."""
+    from deep_gemm.utils.math import per_block_cast_to_fp8
+    from oracle import cdg_oracle as oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    I2, H = w1.shape[1], x.shape[1]
+    inter = w2.shape[2] * 2
+    ids = ids.cpu()
+
+    def quant(v):
+        return _quant_pow2(v) if ue8m0 else per_block_cast_to_fp8(v.float())
+
+    def run(n_tok):
+        tids = ids[:n_tok]
+        experts = torch.unique(tids.flatten())
+        sel = experts.to(w1.device)
+        b1, b1s, b2, b2s = w1[sel].cpu(), s1[sel].cpu(), w2[sel].cpu(), s2[sel].cpu()
+        local = torch.searchsorted(experts, tids.flatten())
+        order = torch.argsort(local, stable=True)
+        rows_tok = (torch.arange(n_tok).repeat_interleave(tids.shape[1]))[order]
+        m_idx = local[order].to(torch.int32)
+        xs = x[:n_tok].cpu()
+        t0 = time.perf_counter()
+        q, s = quant(xs)
+        h = torch.empty(rows_tok.numel(), I2, dtype=torch.bfloat16)
+        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((q[rows_tok], s[rows_tok]), (b1, b1s), h, m_idx)
+        v = torch.nn.functional.silu(h[:, :inter].float()) * h[:, inter:].float()
+        q2, s2_ = quant(v)
+        y = torch.empty(rows_tok.numel(), H, dtype=torch.bfloat16)
+        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((q2, s2_), (b2, b2s), y, m_idx)
+        dt = time.perf_counter() - t0
+        return dt, rows_tok.numel(), experts.numel()
+
+    dt, _, _ = run(1)
+    n_tok = max(1, min(x.shape[0], int(budget_s / max(dt, 1e-3))))
+    for _ in range(warmup):
+        run(n_tok)
+    times = []
+    for _ in range(max(1, calls)):
+        dt, rows, n_exp = run(n_tok)
+        times.append(dt)
+    dt = statistics.median(times)
+    flops = 2.0 * rows * (I2 * H + H * inter)
+    desc = (f"c4 layer: {n_tok} tokens ({rows} routed rows over {n_exp} experts), FC1 + SiLU-mul requant + FC2 "
+            f"with the oracle GEMM, median of {len(times)} calls ({dt:.2f} s each), "
+            f"torch CPU threads={torch.get_num_threads()}")
+    return flops / dt / 1e12, torch.get_num_threads(), desc
+
+
+def _layer_inputs(dev, rank, world, ue8m0=False):
+    """A rank's c4 tokens, routing and shard of the FC1 / FC2 expert weights."""
+    from consumer_deep_gemm import synthetic
+
+    c1 = synthetic.CONFIGS["c4_fc1"]
+    c2 = synthetic.CONFIGS["c4_fc2"]
+    tokens = c1.tokens // world
+    x, ids, w, b1, s1 = _ep_inputs(c1, dev, rank, world, tokens)
+    b2, s2 = synthetic.make_weights(c1.num_experts // world, c2.n, c2.k, dev, seed=200 + rank)
+    return c1, c2, x, ids, w, b1, s1, b2, s2
+
+
 def run_reference(args):
     """The reference's CPU path (oracle port) on rank 0: each step is a bounded sample."""
     from consumer_deep_gemm import synthetic
 
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    cfg_name = args.config if args.config in ("c1", "c2", "c3") else "c1"
-    inp = synthetic.make_inputs(synthetic.CONFIGS[cfg_name], device="cpu", seed=0,
-                                weight_device="cuda" if torch.cuda.is_available() else "cpu")
+    cfg_name = args.config or "c4"
     # K timed samples after W warm-up ones, about 60 s of CPU work in all
-    rates, cores, desc = cpu_port_sample(inp, budget_s=max(0.2, 60.0 / max(1, args.steps + args.warmup)),
-                                         calls=args.steps, warmup=args.warmup)
-    unit = "GB/s" if cfg_name == "c1" else "TFLOP/s"  # the unit of our arm's line for this workload
-    v = rates[unit]
+    budget = max(0.2, 60.0 / max(1, args.steps + args.warmup))
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if cfg_name in ("c4", "c4u"):
+        # the whole job's tokens and routing, as rank 0 of a one-rank run draws them
+        _, _, x, ids, _, b1, s1, b2, s2 = _layer_inputs(dev, 0, 1)
+        v, cores, desc = cpu_layer_sample(x, ids, b1, s1, b2, s2, ue8m0=cfg_name == "c4u", budget_s=budget,
+                                          calls=args.steps, warmup=args.warmup)
+        unit = "TFLOP/s"
+        scaling = "strong"
+    else:
+        base = cfg_name if cfg_name in ("c1", "c2", "c3", "c2u", "c3u") else "c1"
+        inp = synthetic.make_inputs(synthetic.CONFIGS[base], device="cpu", seed=0, weight_device=dev)
+        rates, cores, desc = cpu_port_sample(inp, budget_s=budget, calls=args.steps, warmup=args.warmup)
+        unit = "GB/s" if base == "c1" else "TFLOP/s"  # the unit of our arm's line for this workload
+        v = rates[unit]
+        scaling = "weak"
     line = {
         "metric": METRIC, "impl": "reference", "value": v, "unit": unit, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": cfg_name, "parallelism": "cpu"},
         "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
@@ -208,6 +307,110 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------ checker
+# Float32 reference of the layer for a few sampled tokens (the parity key of the layer's line).
+# It follows the reference's arithmetic: activations dequantised as bf16(bf16(e4m3) *
+# bf16(scale)) per 128 columns, E2M1 weights times 2^(s-127) rounded to BF16, FP32 products
+# rounded to BF16, SiLU-mul in FP32 then the same 1x128 quantisation, the top-k sum in FP32.
+# tests/test_bench_layer_reference.py pins it against the oracle-based CPU reference layer.
+_E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0)
+
+
+def _deq_weight(b, s):
+    """packed e2m1 [N, K/2] (low nibble = even k) + UE8M0 [N, K/32] -> BF16 [N, K]."""
+    t = torch.tensor(_E2M1, dtype=torch.float32, device=b.device)
+    v = torch.stack((t[(b & 15).long()], t[(b >> 4).long()]), -1).flatten(-2)
+    sc = torch.exp2(s.float() - 127.0)
+    return (v.view(v.shape[0], -1, 32) * sc.unsqueeze(-1)).view(v.shape[0], -1).to(torch.bfloat16)
+
+
+def _deq_act(q, s):
+    m, k = q.shape
+    return (q.view(m, k // 128, 128).to(torch.bfloat16) * s.to(torch.bfloat16).unsqueeze(-1)).view(m, k)
+
+
+def _quant_pow2(x):
+    """1x128 e4m3 with power-of-two scales: amax/448 (amax >= 1e-12) rounded up to a power of two."""
+    m, k = x.shape
+    xv = x.float().view(m, k // 128, 128)
+    s = xv.abs().amax(dim=2).clamp(min=1e-12) / 448.0
+    mant, ex = torch.frexp(s)
+    s2 = torch.where(mant == 0.5, s, torch.ldexp(torch.ones_like(s), ex))
+    return (xv / s2.unsqueeze(-1)).to(torch.float8_e4m3fn).view(m, k), s2
+
+
+def layer_reference(x, ids, w, b1, s1, b2, s2, ue8m0=False):
+    """y [T, H] BF16 of the MoE layer for tokens x [T, H] with global expert ids [T, k] and
+    weights [T, k]; b1/s1, b2/s2 are all experts' packed weights and row-major UE8M0 scales."""
+    from deep_gemm.utils.math import per_block_cast_to_fp8
+
+    def quant(v):
+        return _quant_pow2(v) if ue8m0 else per_block_cast_to_fp8(v.float())
+
+    inter = b2.shape[2] * 2
+    q, s = quant(x)
+    xa = _deq_act(q, s).float()
+    y = torch.zeros(x.shape[0], b2.shape[1], dtype=torch.float32, device=x.device)
+    for e in torch.unique(ids.flatten()).tolist():
+        tok, slot = (ids == e).nonzero(as_tuple=True)
+        h = (xa[tok] @ _deq_weight(b1[e], s1[e]).float().t()).to(torch.bfloat16)
+        v = torch.nn.functional.silu(h[:, :inter].float()) * h[:, inter:].float()
+        q2, sc2 = quant(v)
+        o = (_deq_act(q2, sc2).float() @ _deq_weight(b2[e], s2[e]).float().t()).to(torch.bfloat16)
+        y.index_put_((tok,), w[tok, slot].float().unsqueeze(1) * o.float(), accumulate=True)
+    return y.to(torch.bfloat16)
+
+
+def _row_errors(out, ref):
+    o, r = out.float(), ref.float()
+    nw = ((o - r).abs().max() / r.abs().max().clamp(min=1e-30)).item()
+    rl2 = ((o - r).norm(dim=1) / r.norm(dim=1).clamp(min=1e-30)).max().item()
+    return nw, rl2
+
+
+def parity_layer(dist, dev, world, rank, x, ids, w, y, b1, s1, b2, s2, ue8m0):
+    """Compare sampled tokens of every rank's output with layer_reference (on rank 0).
+
+    Every rank contributes max(2, 16 // N) seeded tokens; rank 0 gathers them, their outputs
+    and all ranks' expert weights, and checks max |y - ref| / max |ref| and the per-row
+    relative L2 against LAYER_TOL.  The two GEMMs meet 2e-3 per row each (tests); end to
+    end the bound is looser because the e4m3 requantisation between them turns last-bit
+    differences of FC1 into whole e4m3 steps of single FC2 inputs.
+    """
+    per = max(2, 16 // world)
+    g = torch.Generator().manual_seed(1234 + rank)
+    pick = torch.randperm(x.shape[0], generator=g)[:per].to(dev)
+    mine = [x[pick], ids[pick].to(torch.int64), w[pick].float(), y[pick]]
+    if dist is not None:
+        gathered = []
+        for t in mine:
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t.contiguous())
+            gathered.append(torch.cat(parts))
+        weights = []
+        for t in (b1, s1, b2, s2):
+            out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+            dist.all_gather_into_tensor(out, t.contiguous())
+            weights.append(out)
+    else:
+        gathered, weights = mine, [b1, s1, b2, s2]
+    result = None
+    if rank == 0:
+        xs, idss, ws, ys = gathered
+        ref = layer_reference(xs, idss, ws, *weights, ue8m0=ue8m0)
+        nw, rl2 = _row_errors(ys, ref)
+        e_loc = weights[0].shape[0] // world
+        covered = len(set((idss // e_loc).flatten().tolist()))
+        result = {"normwise": nw, "row_l2": rl2, "rows": int(xs.shape[0]), "ranks_sampled": world,
+                  "ranks_covered_by_routing": covered, "tolerance": LAYER_TOL,
+                  "reference": "float32 layer reference (bench.layer_reference) on the GPU",
+                  "ok": bool(nw <= LAYER_TOL and rl2 <= LAYER_TOL and covered == world)}
+    del weights
+    torch.cuda.empty_cache()
+    return result
+
+
+# ------------------------------------------------------------------------------------ timing
 class Timed:
     """Device time of K steps (CUDA events on the current stream) and of the GEMM kernels inside them."""
 
@@ -240,14 +443,64 @@ class Timed:
         return ms, kms
 
 
+class PhaseTimer:
+    """Per-phase device time of eager layer steps (MoELayer.on_phase), and the FC1 GEMM's
+    tensor-core kernels alone (the library's profile events around that one call)."""
+
+    def __init__(self, layer, steps):
+        from consumer_deep_gemm import native
+
+        self.ext = native.require()
+        self.layer = layer
+        self.steps = steps
+        self.marks = [[] for _ in range(steps)]
+        self.fc1 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(steps)]
+        for s, e in self.fc1:  # materialise the raw event handles the library records
+            s.record()
+            e.record()
+        torch.cuda.synchronize()
+        self.i = 0
+
+    def _hook(self, name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.marks[self.i].append((name, ev))
+        if name in ("dispatch", "permute") and not (name == "dispatch" and self.layer.world > 1):
+            s, e = self.fc1[self.i]
+            self.ext.set_profile_events(s.cuda_event, e.cuda_event)  # around the next GEMM call: FC1
+        elif name == "fc1":
+            self.ext.set_profile_events(0, 0)
+
+    def run(self, step):
+        self.layer.on_phase = self._hook
+        try:
+            for self.i in range(self.steps):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                self.marks[self.i].append(("start", ev))
+                step()
+        finally:
+            self.layer.on_phase = None
+            self.ext.set_profile_events(0, 0)
+        torch.cuda.synchronize()
+        phases = {}
+        for m in self.marks:
+            for (_, a), (name, b) in zip(m[:-1], m[1:]):
+                phases.setdefault(name, []).append(a.elapsed_time(b))
+        fc1_ms = statistics.fmean(s.elapsed_time(e) for s, e in self.fc1)
+        return {k: statistics.fmean(v) for k, v in phases.items()}, fc1_ms
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c4u", "c2u", "c3u"])
+    ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c4u", "c2u", "c3u", "c1-ep"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-workloads", action="store_true", help="N = 1 default: skip the GEMM-alone workloads")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -263,19 +516,36 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    ok = True
     try:
-        if args.config in ("c4", "c4u"):
-            line = bench_layer(args, dev, world, rank, dist)
-        elif world > 1:
+        cfg = args.config or "c4"
+        if cfg in ("c4", "c4u"):
+            line = bench_layer(args, dev, world, rank, dist, cfg)
+            if world == 1 and args.config is None and not args.no_workloads:
+                torch.cuda.empty_cache()
+                line["workloads"] = {}
+                for c in ("c1", "c2", "c3"):
+                    sub = bench_gemm(args, dev, c)
+                    line["workloads"][c] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "roofline",
+                                                                "roofline_other", "config", "cpu_baseline", "e2e",
+                                                                "clocks", "gpu_launches") if k in sub}
+                    torch.cuda.empty_cache()
+        elif cfg == "c1-ep":
             line = bench_ep_decode(args, dev, world, rank, dist)
         else:
-            line = bench_gemm(args, dev, args.config or "c1")
+            if world > 1:
+                raise SystemExit("--config c1/c2/c3/c2u/c3u run on one GPU; use c4, c4u or c1-ep with --gpus N")
+            line = bench_gemm(args, dev, cfg)
         if rank == 0:
             print(json.dumps(line), flush=True)
+            ok = (line.get("parity") or {}).get("ok", True)
     finally:
         if dist:
             dist.barrier()
             dist.destroy_process_group()
+    if not ok:
+        print("parity check failed", file=sys.stderr, flush=True)
+        sys.exit(1)
 
 
 def _max_over_ranks(dist, dev, *vals):
@@ -292,6 +562,12 @@ def _sum_over_ranks(dist, dev, val):
     t = torch.tensor([val], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return t.item()
+
+
+def _barrier(dist, dev):
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
 
 
 def bench_gemm(args, dev, cfg_name):
@@ -368,7 +644,7 @@ def bench_gemm(args, dev, cfg_name):
     e2e_steps(args.warmup)
     e2e_ms = e2e_steps(args.steps)
     clocks = sampler.stop(timed_window)
-    hbm_peak, bf16_peak, peak_src = measured_peaks()
+    hbm_peak, bf16_peak, _, peak_src = measured_peaks()
     achieved_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
     achieved_tf = flops / (kernel_ms * 1e-3) / 1e12
     hbm_roof = {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm_peak, "unit": "GB/s",
@@ -403,7 +679,7 @@ def bench_gemm(args, dev, cfg_name):
         "clocks": clocks,
     }
     if not args.no_cpu_baseline:
-        rates, cores, desc = cpu_port_sample(inp)
+        rates, cores, desc = cpu_port_sample(inp, budget_s=3.0)
         line["cpu_baseline"] = {"value": rates[line["unit"]], "unit": line["unit"], "cores": cores, "kind": "port",
                                 "sample": desc}
     return line
@@ -438,77 +714,188 @@ def _global_counts(ids, num_experts, dev, dist):
     return counts
 
 
+def _e2e_layer(layer, x, ids, w, dev, steps, warmup):
+    """End to end through the layer's public forward: every step uploads its tokens, routing and
+    routing weights from pinned host memory and reads the output rows back; two buffer sets and
+    two copy streams overlap step i's upload and step i-1's download with the compute."""
+    h_in = [t.cpu().pin_memory() for t in (x, ids, w)]
+    h_y = [torch.empty(x.shape[0], layer.out_dim, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    bufs = [[torch.empty_like(t) for t in (x, ids, w)] for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    i = [0]
+
+    def step():
+        p = i[0] & 1
+        i[0] += 1
+        up.wait_event(ev_used[p])
+        with torch.cuda.stream(up):
+            for dst, src in zip(bufs[p], h_in):
+                dst.copy_(src, non_blocking=True)
+        ev_in[p].record(up)
+        comp.wait_event(ev_in[p])
+        comp.wait_event(ev_out[p])
+        y = layer(*bufs[p])
+        ev_used[p].record(comp)
+        down.wait_event(ev_used[p])
+        with torch.cuda.stream(down):
+            h_y[p].copy_(y, non_blocking=True)
+        y.record_stream(down)
+        ev_out[p].record(down)
+
+    def finish():
+        comp.wait_event(ev_out[0])
+        comp.wait_event(ev_out[1])
+
+    for _ in range(warmup):
+        step()
+    finish()
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(comp)
+    up.wait_event(t0)
+    for _ in range(steps):
+        step()
+    finish()  # the last step's download is inside the timed region
+    t1.record(comp)
+    torch.cuda.synchronize(dev)
+    return t0.elapsed_time(t1) / steps, sum(t.numel() * t.element_size() for t in h_in), h_y[0].numel() * 2
+
+
+def bench_layer(args, dev, world, rank, dist, cfg_name):
+    """c4 / c4u: the MoE layer, 32768 tokens split over the ranks, experts sharded."""
+    from consumer_deep_gemm.moe import MoELayer
+
+    ue8m0 = cfg_name == "c4u"
+    c1, c2, x, ids, w, b1, s1, b2, s2 = _layer_inputs(dev, rank, world)
+    tokens = x.shape[0]
+    exchange = "p2p" if world > 1 else "nccl"
+    layer = MoELayer(b1, s1, b2, s2, num_experts=c1.num_experts, group=dist.group.WORLD if dist else None,
+                     ue8m0=ue8m0, max_tokens_per_rank=tokens if world > 1 else None, exchange=exchange)
+    e_loc = c1.num_experts // world
+    mine = _global_counts(ids, c1.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
+    _, f_fc1 = _local_gemm_work(mine, c1.n, c1.k)
+    _, f_fc2 = _local_gemm_work(mine, c2.n, c2.k)
+    job_flops = _sum_over_ranks(dist, dev, f_fc1 + f_fc2)
+
+    sampler = ClockSampler(dev.index)
+    for _ in range(args.warmup):
+        layer(x, ids, w)
+    # per-phase split of eager steps, and the FC1 GEMM's tensor-core kernels alone
+    _barrier(dist, dev)
+    phases, fc1_ms = PhaseTimer(layer, args.steps).run(lambda: layer(x, ids, w))
+    # the timed steps: the layer's forward captured once in a CUDA graph and replayed (no host
+    # synchronisation in the forward at any N: one rank computes its layout on the device, N
+    # ranks exchange through the peer-memory windows)
+    graph, y = layer.capture(x, ids, w)
+    for _ in range(args.warmup):
+        graph.replay()
+    timer = Timed(dev, args.steps)
+    _barrier(dist, dev)
+    ms, _ = timer.run(graph.replay, args.steps, with_kernel_events=False)
+    timed_window = timer.window
+    # end to end through the public forward, host copies included
+    _barrier(dist, dev)
+    e2e_ms, h2d, d2h = _e2e_layer(layer, x, ids, w, dev, args.steps, args.warmup)
+    clocks = sampler.stop(timed_window)
+    _barrier(dist, dev)
+    graph.replay()  # the checked output: one more replay on the resident inputs
+    torch.cuda.synchronize(dev)
+    status = layer.status()
+    parity = parity_layer(dist, dev, world, rank, x, ids, w, y, b1, s1, b2, s2, ue8m0)
+    del graph
+    ms, e2e_ms, fc1_ms, st_max = _max_over_ranks(dist, dev, ms, e2e_ms, fc1_ms, float(status))
+    names = list(phases)
+    phase_max = dict(zip(names, _max_over_ranks(dist, dev, *[phases[k] for k in names])))
+    _barrier(dist, dev)
+    layer.close()  # after every rank's last forward
+    if parity is not None:
+        parity["device_status"] = int(st_max)
+        parity["ok"] = parity["ok"] and st_max == 0
+    _, bf16_peak, bf16_sus, peak_src = measured_peaks()
+    fp8_peak = 2 * bf16_peak
+    achieved = f_fc1 / (fc1_ms * 1e-3) / 1e12
+    step_desc = ("quantise into the layout, FC1, SiLU-mul + requant, FC2, unpermute + combine" if world == 1 else
+                 "dispatch (quantise + store into the owners' windows), permute, FC1, SiLU-mul + requant, FC2, "
+                 "return (store into the sources' windows), combine")
+    return {
+        "metric": METRIC, "value": job_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
+        "config": {"workload": cfg_name, "experts": c1.num_experts, "hidden": c1.k, "intermediate": c2.k,
+                   "tokens": c1.tokens, "tokens_per_rank": tokens, "topk": c1.topk, "parallelism": f"ep{world}",
+                   "activation_scales": "ue8m0 (power of two)" if ue8m0 else "fp32 1x128",
+                   "step": step_desc,
+                   "exchange": "none (one rank)" if world == 1 else
+                   "peer-memory stores over NVLink into fixed-capacity windows (tokens_per_rank x topk rows per "
+                   "source), release/acquire flags; no collective, no host synchronisation",
+                   "timed": "the forward captured in one CUDA graph per rank, replayed",
+                   "l2": "inputs larger than L2 (weights %.2f GB per rank)" % ((b1.numel() + b2.numel()) / 1e9)},
+        "phases_ms": phase_max,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
+                     "frac": achieved / fp8_peak, "traffic": None, "kernel": "FC1 GEMM's tensor-core kernels",
+                     "kernel_ms": fc1_ms, "algorithmic_flops": f_fc1,
+                     "peak_source": f"2 x {peak_src} BF16 GEMM burst (dense FP8:BF16 = 2:1)",
+                     "frac_of_sustained": (achieved / (2 * bf16_sus)) if bf16_sus else None},
+        "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "copies": "per rank: its tokens, routing and weights up, its output rows down; step i's upload "
+                          "overlaps step i-1's download (two buffer sets, two copy streams)"},
+        "parity": parity,
+        "gpu_launches": (2 * GEMM_LAUNCHES + LAYER_LAUNCHES[world == 1]) * args.steps,
+        "clocks": clocks,
+        **({"cpu_baseline": _layer_cpu_baseline(x, ids, b1, s1, b2, s2, ue8m0)}
+           if (world == 1 and rank == 0 and not args.no_cpu_baseline) else {}),
+    }
+
+
+def _layer_cpu_baseline(x, ids, b1, s1, b2, s2, ue8m0):
+    v, cores, desc = cpu_layer_sample(x, ids, b1, s1, b2, s2, ue8m0=ue8m0, budget_s=3.0)
+    return {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": desc}
+
+
 def bench_ep_decode(args, dev, world, rank, dist):
-    """N > 1: every rank a c1 decode batch, experts sharded, NCCL dispatch/combine around the GEMM."""
+    """--config c1-ep: every rank a c1 decode batch, experts sharded, FC1 only."""
     from consumer_deep_gemm import synthetic
     from consumer_deep_gemm.moe import MoELayer
 
     cfg = synthetic.CONFIGS["c1"]
     x, ids, w, b, sb = _ep_inputs(cfg, dev, rank, world, cfg.tokens)
-    # fixed per-destination capacity, rows moved by the library's peer-memory stores over
-    # NVLink: no host synchronisation and no collective on the data path
-    layer = MoELayer(b, sb, num_experts=cfg.num_experts, group=dist.group.WORLD, max_tokens_per_rank=cfg.tokens,
-                     exchange=os.environ.get("CDG_EP_EXCHANGE", "p2p"))
+    layer = MoELayer(b, sb, num_experts=cfg.num_experts, group=dist.group.WORLD if dist else None,
+                     max_tokens_per_rank=cfg.tokens if world > 1 else None, exchange="p2p" if world > 1 else "nccl")
     e_loc = cfg.num_experts // world
     mine = _global_counts(ids, cfg.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
     local_bytes, local_flops = _local_gemm_work(mine, cfg.n, cfg.k)
     job_bytes = _sum_over_ranks(dist, dev, local_bytes)
     job_flops = _sum_over_ranks(dist, dev, local_flops)
 
-    def step():
-        layer(x, ids, w)
-
     sampler = ClockSampler(dev.index)
     for _ in range(args.warmup):
-        step()
-    # the GEMM kernels' device time, from eager steps with per-step events
-    timer = Timed(dev, args.steps)
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    _, kernel_ms = timer.run(step, args.steps)
-    dist.barrier()
-    # the step itself: one CUDA graph per rank (peer exchange: no host value per step)
-    use_graph = layer.exchange == "p2p"
-    if use_graph:
-        graph, _ = layer.capture(x, ids, w)
-        step = graph.replay
-        for _ in range(args.warmup):
-            step()
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    ms, _ = timer.run(step, args.steps, with_kernel_events=False)
-    timed_window = timer.window
-    dist.barrier()
-
-    h_x, h_ids, h_w = x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()
-    h_y = torch.empty(x.shape[0], cfg.n, dtype=torch.bfloat16).pin_memory()
-    x2, ids2, w2 = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
-    x2.copy_(x)
-    ids2.copy_(ids)
-    w2.copy_(w)
-    if use_graph:
-        e2e_graph, y2 = layer.capture(x2, ids2, w2)
-
-    def e2e_step():
-        x2.copy_(h_x, non_blocking=True)
-        ids2.copy_(h_ids, non_blocking=True)
-        w2.copy_(h_w, non_blocking=True)
-        if use_graph:
-            e2e_graph.replay()
-            h_y.copy_(y2, non_blocking=True)
-        else:
-            h_y.copy_(layer(x2, ids2, w2), non_blocking=True)
+        layer(x, ids, w)
+    _barrier(dist, dev)
+    phases, kernel_ms = PhaseTimer(layer, args.steps).run(lambda: layer(x, ids, w))
+    graph, _ = layer.capture(x, ids, w)
     for _ in range(args.warmup):
-        e2e_step()
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    e2e_ms, _ = timer.run(e2e_step, args.steps, with_kernel_events=False)
+        graph.replay()
+    timer = Timed(dev, args.steps)
+    _barrier(dist, dev)
+    ms, _ = timer.run(graph.replay, args.steps, with_kernel_events=False)
+    timed_window = timer.window
+    _barrier(dist, dev)
+    _barrier(dist, dev)
+    e2e_ms, h2d, d2h = _e2e_layer(layer, x, ids, w, dev, args.steps, args.warmup)
     clocks = sampler.stop(timed_window)
-    ms, e2e_ms, kernel_ms = _max_over_ranks(dist, dev, ms, e2e_ms, kernel_ms)
-    torch.cuda.synchronize(dev)
-    dist.barrier()
-    layer.close()  # after every rank's last forward
-    hbm_peak, _, peak_src = measured_peaks()
+    status = layer.status()
+    del graph
+    ms, e2e_ms, kernel_ms, st_max = _max_over_ranks(dist, dev, ms, e2e_ms, kernel_ms, float(status))
+    names = list(phases)
+    phase_max = dict(zip(names, _max_over_ranks(dist, dev, *[phases[k] for k in names])))
+    _barrier(dist, dev)
+    layer.close()
+    hbm_peak, _, _, peak_src = measured_peaks()
     achieved = local_bytes / (kernel_ms * 1e-3) / 1e9
     return {
         "metric": METRIC, "value": job_bytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": world,
@@ -516,72 +903,23 @@ def bench_ep_decode(args, dev, world, rank, dist):
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": "c1-ep", "experts": cfg.num_experts, "k": cfg.k, "n": cfg.n,
                    "tokens_per_rank": cfg.tokens, "topk": cfg.topk, "parallelism": f"ep{world}",
-                   "step": "quant, count all-to-all, dispatch all-to-all, grouped GEMM on local experts, "
-                           "return all-to-all, weighted combine",
-                   "exchange": "fixed capacity per destination (tokens*topk rows), no host synchronisation; "
-                               + ("peer-memory stores over NVLink, step replayed as one CUDA graph per rank"
-                                  if layer.exchange == "p2p" else "NCCL all-to-all"),
+                   "step": ("quantise into the layout, FC1, unpermute + combine" if world == 1 else
+                            "dispatch (quantise + store into the owners' windows), permute, FC1, return (store "
+                            "into the sources' windows), combine"),
+                   "exchange": "none (one rank)" if world == 1 else
+                   "peer-memory stores over NVLink into fixed-capacity windows, release/acquire flags; no "
+                   "collective, no host synchronisation",
+                   "timed": "the forward captured in one CUDA graph per rank, replayed",
                    "l2": "weights per rank larger than L2"},
         "tflops": job_flops / (ms * 1e-3) / 1e12,
+        "phases_ms": phase_max,
+        "device_status": int(st_max),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
                      "kernel_ms": kernel_ms, "algorithmic_bytes": local_bytes, "note": "rank 0's GEMM kernels"},
-        "e2e": {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-                "h2d_bytes_per_step": h_x.numel() * 2 + h_ids.numel() * 4 + h_w.numel() * 4,
-                "d2h_bytes_per_step": h_y.numel() * 2, "ms_per_step": e2e_ms},
-        "gpu_launches": (GEMM_LAUNCHES + EP_LAUNCHES) * args.steps,
-        "clocks": clocks,
-    }
-
-
-def bench_layer(args, dev, world, rank, dist):
-    """--config c4: the full expert-parallel MoE layer, 32768 tokens split over the ranks.
-    --config c4u: the same layer quantising its activations with power-of-two (UE8M0) scales."""
-    from consumer_deep_gemm import synthetic
-    from consumer_deep_gemm.moe import MoELayer
-
-    c1 = synthetic.CONFIGS["c4_fc1"]
-    c2 = synthetic.CONFIGS["c4_fc2"]
-    tokens = c1.tokens // world
-    x, ids, w, b1, s1 = _ep_inputs(c1, dev, rank, world, tokens)
-    b2, s2 = synthetic.make_weights(c1.num_experts // world, c2.n, c2.k, dev, seed=200 + rank)
-    ue8m0 = args.config == "c4u"
-    layer = MoELayer(b1, s1, b2, s2, num_experts=c1.num_experts, group=dist.group.WORLD if dist else None,
-                     ue8m0=ue8m0)
-    e_loc = c1.num_experts // world
-    mine = _global_counts(ids, c1.num_experts, dev, dist)[rank * e_loc:(rank + 1) * e_loc].cpu()
-    _, f_fc1 = _local_gemm_work(mine, c1.n, c1.k)
-    _, f_fc2 = _local_gemm_work(mine, c2.n, c2.k)
-    job_flops = _sum_over_ranks(dist, dev, f_fc1 + f_fc2)
-
-    def step():
-        layer(x, ids, w)
-
-    sampler = ClockSampler(dev.index)
-    for _ in range(args.warmup):
-        step()
-    timer = Timed(dev, args.steps)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    # the library's profile events bracket the last GEMM call of a step (FC2)
-    ms, fc2_ms = timer.run(step, args.steps)
-    clocks = sampler.stop(timer.window)
-    ms, fc2_ms = _max_over_ranks(dist, dev, ms, fc2_ms)
-    _, bf16_peak, peak_src = measured_peaks()
-    fp8_peak = 2 * bf16_peak
-    achieved = f_fc2 / (fc2_ms * 1e-3) / 1e12
-    return {
-        "metric": METRIC, "value": job_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
-        "config": {"workload": args.config, "experts": c1.num_experts, "hidden": c1.k, "intermediate": c2.k,
-                   "tokens": c1.tokens, "topk": c1.topk, "parallelism": f"ep{world}",
-                   "activation_scales": "ue8m0 (power of two)" if ue8m0 else "fp32 1x128"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp8_peak, "unit": "TFLOP/s",
-                     "frac": achieved / fp8_peak, "traffic": None, "kernel": "FC2 GEMM kernels (rank 0)",
-                     "peak_source": f"2 x {peak_src} bf16 GEMM rate (dense FP8:BF16 = 2:1)"},
-        "gpu_launches": (2 * GEMM_LAUNCHES + EP_LAUNCHES + 1) * args.steps,
+        "e2e": {"value": job_bytes / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": (GEMM_LAUNCHES + LAYER_LAUNCHES[world == 1] - 1) * args.steps,
         "clocks": clocks,
     }
 

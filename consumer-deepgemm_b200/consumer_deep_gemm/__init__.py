@@ -17,6 +17,7 @@ from .layout import (
 )
 from .mega import fp8_fp4_mega_moe, get_symm_buffer_for_mega_moe, transform_weights_for_mega_moe
 from .native import build_info as native_build_info
+from .native import check_device_status, read_device_status
 from .native import is_available as native_is_available
 from .utils import get_num_sms, get_pdl, get_tc_util, set_num_sms, set_pdl, set_tc_util
 
@@ -35,6 +36,8 @@ __all__ = [
     "get_theoretical_mk_alignment_for_contiguous_layout",
     "native_build_info",
     "native_is_available",
+    "read_device_status",
+    "check_device_status",
     "set_num_sms",
     "get_num_sms",
     "set_tc_util",

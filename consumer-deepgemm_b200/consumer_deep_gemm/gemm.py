@@ -28,7 +28,13 @@ from __future__ import annotations
 
 import torch
 
+import os
+
 from . import native
+
+# CDG_CHECK_STATUS=1: synchronise after every call and raise if a device wait gave up (a
+# debugging aid; the calls otherwise never wait for the device).
+_CHECK_STATUS = os.environ.get("CDG_CHECK_STATUS", "0") == "1"
 
 __all__ = ["m_grouped_fp8_fp4_gemm_nt_contiguous", "m_grouped_fp8_fp4_gemm_nt_masked"]
 
@@ -107,6 +113,8 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs) -> N
     x, sa, bt, bs, d, ids = _normalize(a, b, d, m_indices)
     flags = (1 if kwargs.get("_force_exact_path") else 0) | (4 if kwargs.get("_skip_ungrouped_rows") else 0)
     native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags)
+    if _CHECK_STATUS:
+        native.check_device_status()
 
 
 def _flatten_groups(t):
@@ -155,3 +163,5 @@ def m_grouped_fp8_fp4_gemm_nt_masked(a, b, d, masked_m=None, **kwargs) -> None:
         masked = True
     flags = 1 if kwargs.get("_force_exact_path") else 0
     native.require().grouped_gemm(x, sa, bt, bs, d2, ids, flags, masked)
+    if _CHECK_STATUS:
+        native.check_device_status()

@@ -10,6 +10,9 @@ and act = 1x128 e4m3 quantisation of silu(gate) * up.  This is the sequence vLLM
 DeepGemmFP4Experts runs around ``m_grouped_fp8_fp4_gemm_nt_contiguous``
 (vllm/model_executor/layers/fused_moe/experts/deep_gemm_moe.py:485-545).
 
+One rank: the forward has no host synchronisation (group offsets computed on the device,
+layout sized for the worst case), so it can be captured in a CUDA graph.
+
 Expert parallelism: with a process group of N ranks, rank r owns experts
 [r*E/N, (r+1)*E/N).  Each rank quantises its own tokens, exchanges per-expert row
 counts (one small all-to-all and the only host synchronisation), sends every
@@ -186,6 +189,22 @@ class MoELayer:
             self.w2_sf = transform_sf_into_required_layout(w2_scale) if w2.is_cuda else w2_scale
         self.out_dim = w2.shape[1] if w2 is not None else w1.shape[1]
         self.inter = w1.shape[1] // 2
+        # optional callable(name), called after each step of a forward has been launched
+        # (dispatch, permute, fc1, act, fc2, return, combine): a profiler records CUDA events
+        # there to split the step's device time by phase
+        self.on_phase = None
+
+    def _phase(self, name):
+        if self.on_phase is not None:
+            self.on_phase(name)
+
+    def status(self) -> int:
+        """0, or CDG_ERR_DEVICE_TIMEOUT (6) when one of this process's device waits gave up
+        since the last call: a wait on another rank's exchange flag (this layer's window) or a
+        GEMM pipeline wait.  Synchronises the device and clears the library's record."""
+        st = self.windows.status() if self.windows is not None else 0
+        dev, _ = native.read_device_status(True)
+        return st or dev
 
     def forward(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor) -> torch.Tensor:
         if self.world > 1 and self.exchange == "p2p":
@@ -196,15 +215,14 @@ class MoELayer:
         dev = x.device
         topk_ids = topk_ids.contiguous()
         topk_w = topk_w.to(torch.float32).contiguous()
-        if world > 1:
-            xq, xs = ops.quant(x, self.ue8m0)
+        if world == 1:
+            return self._forward_local(x, topk_ids, topk_w)
+        # split-size exchange
+        xq, xs = ops.quant(x, self.ue8m0)
         counts = ops.count(topk_ids, E)                                  # [E] rows per global expert
-        if world > 1:
-            both = torch.empty(2, E, dtype=counts.dtype, device=dev)
-            both[0] = counts
-            _all_to_all(both[1], counts, None, None, self.group)
-        else:
-            both = counts.expand(2, E)
+        both = torch.empty(2, E, dtype=counts.dtype, device=dev)
+        both[0] = counts
+        _all_to_all(both[1], counts, None, None, self.group)
         # the one host synchronisation of the layer (one copy): split sizes and the local layout
         mats = both.cpu().numpy().astype(np.int64).reshape(2, world, E_loc)
         send_splits = mats[0].sum(1)
@@ -215,19 +233,6 @@ class MoELayer:
         offs = torch.from_numpy(offs).to(dev, non_blocking=False)
         expert_off, send_off = offs[:E_loc], offs[E_loc:]
         send_splits, recv_splits = send_splits.tolist(), recv_splits.tolist()
-
-        if world == 1:
-            # no exchange: quantise straight into the contiguous layout, combine straight from
-            # the GEMM's rows
-            a, sa, m_indices, perm_pos, send_index = ops.quant_dispatch_local(x, topk_ids, E, expert_off, m_pad,
-                                                                              self.ue8m0)
-            if m_pad == 0:
-                return ops.combine(torch.empty(0, self.out_dim, dtype=torch.bfloat16, device=dev), send_index, topk_w)
-            h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices)
-            if self.w2 is not None:
-                aq, asc = ops.act(h, m_indices, self.ue8m0)
-                h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices)
-            return ops.unpermute_combine(h, perm_pos, send_index, topk_w)
 
         sent, send_index = ops.pack(xq, xs, topk_ids, E, world, send_off, sum(send_splits))
         recv = _all_to_all(torch.empty(sum(recv_splits), sent.shape[1], dtype=sent.dtype, device=dev), sent,
@@ -245,6 +250,31 @@ class MoELayer:
         out_rows = _all_to_all(torch.empty(sent.shape[0], self.out_dim, dtype=back.dtype, device=dev), back,
                                send_splits, recv_splits, self.group)
         return ops.combine(out_rows, send_index, topk_w)
+
+    def _forward_local(self, x, topk_ids, topk_w):
+        """One rank, no exchange, no host synchronisation: the group offsets are computed on the
+        device and the layout is sized for the worst case (every group 127 rows short of a
+        multiple of 128); each token's row is quantised once straight into it, and the combine
+        reads the GEMM's rows through the permutation."""
+        ops, E = self.ops, self.num_experts
+        T, topk = topk_ids.shape
+        counts = ops.count(topk_ids, E)                                  # [E] rows per expert
+        aligned = (counts.to(torch.int64) + ALIGN - 1) // ALIGN * ALIGN
+        expert_off = torch.cumsum(aligned, 0) - aligned
+        m_pad = (T * topk + (ALIGN - 1) * E + ALIGN - 1) // ALIGN * ALIGN
+        a, sa, m_indices, perm_pos, send_index = ops.quant_dispatch_local(x, topk_ids, E, expert_off, m_pad,
+                                                                          self.ue8m0)
+        self._phase("dispatch")
+        h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        self._phase("fc1")
+        if self.w2 is not None:
+            aq, asc = ops.act(h, m_indices, self.ue8m0)
+            self._phase("act")
+            h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+            self._phase("fc2")
+        y = ops.unpermute_combine(h, perm_pos, send_index, topk_w)
+        self._phase("combine")
+        return y
 
     def _forward_fixed(self, x, topk_ids, topk_w):
         """Exchange without a host synchronisation: fixed per-destination capacity."""
@@ -282,21 +312,30 @@ class MoELayer:
             self.windows = PeerWindows(self.group, cap, H, x.device)
         win, me = self.windows, self.rank
         send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, win.own, me, self.ue8m0)
+        self._phase("dispatch")
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
         a, sa, m_indices, perm_pos = C.ep_permute_p2p(win.own, world, cap, H, E_loc, m_pad, x)
+        self._phase("permute")
         h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        self._phase("fc1")
         if self.w2 is not None:
             aq, asc = self.ops.act(h, m_indices, self.ue8m0)
+            self._phase("act")
             h = self.ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+            self._phase("fc2")
         C.ep_return_p2p(h, perm_pos, world, cap, win.peers, win.own, me)
-        return C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H)
+        self._phase("return")
+        y = C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H)
+        self._phase("combine")
+        return y
 
     def capture(self, x, topk_ids, topk_w):
         """Record one forward on these (static) input tensors in a CUDA graph.
 
         Returns (graph, output): ``graph.replay()`` reruns the forward on whatever the input
         tensors then hold and writes the result into ``output``.  Needs the peer-memory
-        exchange (or a single rank): every step of it reads its step number on the device.
+        exchange (every step of it reads its step number on the device) or a single rank
+        (whose forward has no host synchronisation).
         The first forward (window set-up, library initialisation) runs here, outside the graph.
         """
         if self.world > 1 and self.exchange != "p2p":

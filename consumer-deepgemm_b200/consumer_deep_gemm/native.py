@@ -77,3 +77,25 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(*args, **kwargs):
 
     run(*args, **kwargs)
     return True
+
+
+def read_device_status(clear: bool = True) -> tuple[int, int]:
+    """Device-side errors of the library's kernels on the current device since the last clear.
+
+    Synchronises the device, then returns ``(status, where)``: status 0, or 6
+    (``CDG_ERR_DEVICE_TIMEOUT``) when a bounded wait gave up -- a GEMM pipeline wait, or a
+    wait on another rank's flag in the peer-memory exchange -- and ``where``, the first such
+    wait's code (0 when none; layout in ``cdg_device_status``).  The GEMM calls themselves
+    never synchronise, so a caller that wants to know checks here (after a batch of calls,
+    or every call with ``CDG_CHECK_STATUS=1``).
+    """
+    st, where = require().device_status(bool(clear))
+    return int(st), int(where) & 0xFFFFFFFF  # the code's bit pattern (roles >= 8 set the top bit)
+
+
+def check_device_status() -> None:
+    """``read_device_status()``, raising ``RuntimeError`` when a device wait gave up."""
+    st, where = read_device_status(True)
+    if st:
+        raise RuntimeError(f"a device wait of consumer_deep_gemm gave up (status {st}, wait code {where:#010x}); "
+                           "the outputs of the calls since the last check are not valid")

@@ -2,9 +2,11 @@
 // descriptors and kernel launches behind the C ABI declared in cdg_b200.h.
 //
 // No call here blocks the host or copies device data to the host (except
-// cdg_read_device_status, a diagnostic).  The only state kept between calls is a
-// per-device, initialise-once record (SM count, compute capability, kernel
-// attributes) and the resolved driver entry point for tensor-map encoding.
+// cdg_read_device_status and cdg_device_status, diagnostics).  The state kept between
+// calls: a per-device, initialise-once record (SM count, compute capability, kernel
+// attributes), the resolved driver entry point for tensor-map encoding, the process-wide
+// SM limit of cdg_set_num_sms, and on the device the sticky error record the bounded waits
+// write (g_sticky_status).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -85,6 +87,16 @@ const DeviceInfo& device_info(int dev) {
     d.ok = true;
   });
   return infos[dev];
+}
+
+// SMs the persistent GEMM kernels may use (cdg_set_num_sms; 0 = all of the device's), and
+// whether the GEMM kernels are launched with programmatic stream serialization (cdg_set_pdl).
+std::atomic<int> g_num_sms{0};
+std::atomic<int> g_pdl{1};
+
+int usable_sms(const DeviceInfo& di) {
+  const int n = g_num_sms.load(std::memory_order_relaxed);
+  return n > 0 && n < di.sm_count ? n : di.sm_count;
 }
 
 // Optional events recorded around the tensor-core GEMM launches (per host thread).
@@ -309,7 +321,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = g_pdl.load(std::memory_order_relaxed) ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -394,7 +406,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     ga.ids_is_64 = ids_dtype == CDG_DTYPE_I64;
     ga.list = nullptr;
     ga.count = nullptr;
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(di.sm_count) * 8));
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(usable_sms(di)) * 8));
     cdg_generic_kernel<<<grid, 256, generic_smem, stream>>>(ga);
     return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
   }
@@ -431,7 +443,8 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.ctrl = ctrl;
   pa.lists = lists;
   pa.plane_tiles = reinterpret_cast<int4*>(ws + wl.plane_tiles);
-  const bool pair_path = g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && di.sm_count >= 2;
+  const int sms = usable_sms(di);
+  const bool pair_path = g->N % 256 == 0 && !(g->flags & CDG_FLAG_SINGLE_CTA) && sms >= 2;
   uint8_t* tok_code = ws + wl.tok_code;
   pa.tok_code = tok_code;
   pa.direct_tiles = reinterpret_cast<int4*>(ws + wl.direct_tiles);
@@ -477,7 +490,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     CUtensorMap p16, p32, tsf;
     st = make_pair_tmaps(g, hilo, nblk, sfw, &p16, &p32, &tsf);
     if (st != CDG_OK) return st;
-    const unsigned grid = static_cast<unsigned>(di.sm_count / 2 * 2);
+    const unsigned grid = static_cast<unsigned>(sms / 2 * 2);
     // the planes kernel also writes the direct tiles' token scale atoms
     ka.direct_list = reinterpret_cast<const int4*>(ws + wl.direct_tiles);
     ka.list = lists + kClassTiny * nblk;
@@ -515,18 +528,18 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     ka.list = lists + kClassTiny * nblk;
     ka.count_slot = kCtrlCount0 + kClassTiny;
     ka.do_zero_blocks = skip_ungrouped ? 0 : 1;
-    if (launch_pdl(cdg_gemm_kernel<16>, di.sm_count, 256, GemmSmem<16>::kBytes, stream, tw, ta16, ka) != cudaSuccess)
+    if (launch_pdl(cdg_gemm_kernel<16>, sms, 256, GemmSmem<16>::kBytes, stream, tw, ta16, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     // Narrow blocks (17 to 32 routed rows).
     ka.do_zero_blocks = 0;
     ka.list = lists + kClassNarrow * nblk;
     ka.count_slot = kCtrlCount0 + kClassNarrow;
-    if (launch_pdl(cdg_gemm_kernel<32>, di.sm_count, 256, GemmSmem<32>::kBytes, stream, tw, ta32, ka) != cudaSuccess)
+    if (launch_pdl(cdg_gemm_kernel<32>, sms, 256, GemmSmem<32>::kBytes, stream, tw, ta32, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
     // Wide blocks (prefill-like).
     ka.list = lists + kClassWide * nblk;
     ka.count_slot = kCtrlCount0 + kClassWide;
-    if (launch_pdl(cdg_gemm_kernel<128>, di.sm_count, 256, GemmSmem<128>::kBytes, stream, tw, ta128, ka) != cudaSuccess)
+    if (launch_pdl(cdg_gemm_kernel<128>, sms, 256, GemmSmem<128>::kBytes, stream, tw, ta128, ka) != cudaSuccess)
       return CDG_ERR_CUDA;
   }
   if (t_prof_stop && cudaEventRecord(t_prof_stop, stream) != cudaSuccess) return CDG_ERR_CUDA;
@@ -536,7 +549,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ga.list = lists + kClassIrregular * nblk;
   ga.count = ctrl + kCtrlCount0 + kClassIrregular;
   {
-    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(di.sm_count)));
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(generic_units, int64_t(sms)));
     if (launch_pdl(cdg_generic_kernel, grid, 256, generic_smem, stream, ga) != cudaSuccess) return CDG_ERR_CUDA;
   }
   return CDG_OK;
@@ -598,6 +611,51 @@ int cdg_read_device_status(const void* workspace, cdg_stream_t stream) {
   return (word & cdg::kStatusTimeout) ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
 }
 
+}  // extern "C"
+
+namespace cdg {
+int ep_sticky_status(int clear, int32_t* out);  // cdg_moe.cu: the exchange kernels' record
+}  // namespace cdg
+
+extern "C" {
+
+int cdg_device_status(int32_t clear, int32_t* where) {
+  int32_t gemm[2] = {0, 0}, ep[2] = {0, 0};
+  if (cudaDeviceSynchronize() != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(gemm, cdg::g_sticky_status, sizeof(gemm)) != cudaSuccess) return CDG_ERR_CUDA;
+  if (clear) {
+    const int32_t z[2] = {0, 0};
+    if (cudaMemcpyToSymbol(cdg::g_sticky_status, z, sizeof(z)) != cudaSuccess) return CDG_ERR_CUDA;
+  }
+  const int st = cdg::ep_sticky_status(clear, ep);
+  if (st != CDG_OK) return st;
+  if (where) *where = gemm[1] ? gemm[1] : ep[1];
+  return (gemm[0] | ep[0]) ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
+}
+
+int cdg_set_num_sms(int32_t num_sms) {
+  if (num_sms < 0) return CDG_ERR_INVALID_ARGUMENT;
+  cdg::g_num_sms.store(num_sms, std::memory_order_relaxed);
+  return CDG_OK;
+}
+
+int cdg_set_pdl(int32_t enable) {
+  cdg::g_pdl.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return CDG_OK;
+}
+
+int cdg_get_pdl(void) { return cdg::g_pdl.load(std::memory_order_relaxed); }
+
+int cdg_get_num_sms(void) {
+  const int n = cdg::g_num_sms.load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                 cudaSuccess)
+    return 0;
+  return sms;
+}
+
 const char* cdg_build_info(void) {
   return "consumer-deepgemm-b200; arch=sm_100a; abi=1; kernels=tcgen05.mma.kind::mxf8f6f4.block_scale "
          "(TMA 16U4_ALIGN16B weights, e4m3 hi/lo activation planes), exact SIMT fallback";
@@ -652,6 +710,9 @@ const NoallocScratch& noalloc_scratch(int dev) {
     void* p = nullptr;
     slots[dev].err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     slots[dev].ptr = static_cast<uint8_t*>(p);
+    // a failed lookup is reported by every call through slots[dev].err; it must not stay
+    // behind as the thread's last error, where the launch checks that follow would see it
+    if (slots[dev].err != cudaSuccess) (void)cudaGetLastError();
   });
   return slots[dev];
 }
@@ -667,6 +728,10 @@ extern "C" int cdg_grouped_fp8_fp4_gemm_nt_contiguous_noalloc(const cdg_gemm_arg
   if (need > CDG_NOALLOC_SCRATCH_BYTES) return CDG_ERR_SCRATCH_TOO_SMALL;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= cdg::kMaxDevices) return CDG_ERR_CUDA;
+  // A device that is not a B200 is reported as such before the scratch is looked up there.
+  const cdg::DeviceInfo& di = cdg::device_info(dev);
+  if (!di.ok) return CDG_ERR_CUDA;
+  if (di.cc_major != 10) return CDG_ERR_NO_SM100;
   const cdg::NoallocScratch& sc = cdg::noalloc_scratch(dev);
   if (sc.err != cudaSuccess || sc.ptr == nullptr) return CDG_ERR_CUDA;
   const uintptr_t base = (reinterpret_cast<uintptr_t>(sc.ptr) + 1023) & ~uintptr_t(1023);

@@ -236,7 +236,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
       // are compile-time constants plus warp-uniform offsets.  Any other base is reported as an
       // error and the kernel leaves without issuing.
       if (tmem_base != 0u) {
-        atomicOr(p.status, kStatusTimeout);
+        record_timeout(p.status, wait_code(15, 0, 0, 0, 0));  // role 15: unexpected TMEM base
         ok = false;
       }
       int stage = 0, sfs = 0;

@@ -90,19 +90,35 @@ __device__ __forceinline__ uint64_t now_ns() {
   return t;
 }
 
+// Bound of every wait on another rank's flag, per device (cdg_ep_set_wait_timeout_ns).
 constexpr uint64_t kPeerWaitNs = 2000000000ull;  // 2 s
+__device__ uint64_t g_peer_wait_ns = kPeerWaitNs;
 
-// Thread 0 of the CTA waits until flags[0 .. n) all reach `epoch` (bounded); the CTA then
-// proceeds only if they did.  A wait that gives up sets bit 0 of *status.
-__device__ bool wait_peer_flags(const int32_t* flags, int n, int32_t epoch, int32_t* status) {
+// Sticky per-device record of the exchange's device-side errors ([0] status bits, [1] the first
+// wait code); cdg_device_status() reads it together with the GEMM's.
+__device__ int g_ep_sticky_status[2];
+
+// Wait codes of the peer waits: role 8 = dispatch flag (permute), 9 = return flag (combine),
+// then the source rank whose flag did not arrive.
+__device__ __forceinline__ int peer_wait_code(int role, int src) {
+  return static_cast<int>((static_cast<uint32_t>(role & 15) << 28) | static_cast<uint32_t>(src & 0xFFFF));
+}
+
+// Thread 0 of the CTA waits until flags[0 .. n) all reach `epoch` (bounded by
+// g_peer_wait_ns); the CTA then proceeds only if they did.  A wait that gives up sets bit 0
+// of *status (the window's status word) and the sticky per-device record.
+__device__ bool wait_peer_flags(const int32_t* flags, int n, int32_t epoch, int32_t* status, int role) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     int ok = 1;
+    const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_peer_wait_ns);
     const uint64_t t0 = now_ns();
     for (int i = 0; i < n && ok; ++i) {
       while (ld_acquire_sys(flags + i) < epoch) {
-        if (now_ns() - t0 > kPeerWaitNs) {
+        if (now_ns() - t0 > limit) {
           atomicOr(status, 1);
+          atomicOr(&g_ep_sticky_status[0], 1);
+          atomicCAS(&g_ep_sticky_status[1], 0, peer_wait_code(role, i));
           ok = 0;
           break;
         }
@@ -448,14 +464,21 @@ __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* ro
   __shared__ int64_t s_off[kFixedMaxExperts];
   __shared__ int32_t s_nsrc[kFixedMaxRanks];
   __shared__ int64_t s_warp_sum[8];
+  const int tid = threadIdx.x;
   if (ps.own) {
     const int32_t epoch = ps.epoch();
     rows = ps.own + ps.win.recv_parity(epoch & 1);
     if (!wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kDispatchFlags), static_cast<int>(ranks),
-                         epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus)))
+                         epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 8)) {
+      // The rows did not all arrive: place none of this CTA's slots.  Every slot still gets
+      // perm_pos = -1, so the return step (which reads rows at perm_pos) skips them.
+      const int64_t R = ranks * (cap + 1);
+      for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + tid) >> 5; w < R;
+           w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5)
+        if ((tid & 31) == 0) perm_pos[w] = -1;
       return;
+    }
   }
-  const int tid = threadIdx.x;
   const int64_t rb = packed_row_bytes(H);
   auto header = [&](int64_t r) { return reinterpret_cast<const int32_t*>(rows + r * (cap + 1) * rb); };
   // per-expert aligned totals, 4 consecutive experts per thread, then a block scan
@@ -521,10 +544,11 @@ __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* ro
 
 // Peer return: one warp per received slot (region src, slot s) whose row was placed at
 // perm_pos; the GEMM row goes straight to the source's window (return rows of the step's
-// parity), at the row of its own send layout (me * (cap + 1) + 1 + s).  The last CTA raises
-// this rank's flag in every source window.
+// parity), at the row of its own send layout (me * (cap + 1) + 1 + s).  Slots whose perm_pos
+// is negative or not below y_rows (the rows of Y) are skipped.  The last CTA raises this
+// rank's flag in every source window.
 // scratch: [1] ticket, zeroed by the host.
-__global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* Y, int64_t y_stride,
+__global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* Y, int64_t y_stride, int64_t y_rows,
                                                             const int32_t* perm_pos, int64_t ranks, int64_t cap,
                                                             int64_t H, PeerStep ps, int32_t* scratch) {
   __shared__ int s_last;
@@ -538,7 +562,7 @@ __global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16*
   for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < R;
        w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
     const int32_t pos = perm_pos[w];
-    if (pos < 0) continue;
+    if (pos < 0 || pos >= y_rows) continue;
     const int64_t src = w / (cap + 1), s = w - src * (cap + 1);
     const uint4* from = reinterpret_cast<const uint4*>(Y + static_cast<int64_t>(pos) * y_stride);
     uint4* to = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peers[src]) + ret_off +
@@ -586,7 +610,12 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, int64_t row_stride,
     epoch = ps.epoch();
     rows = reinterpret_cast<const __nv_bfloat16*>(ps.own + ps.win.ret_parity(epoch & 1));
     ok = wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kReturnFlags),
-                         static_cast<int>(ps.win.ranks), epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus));
+                         static_cast<int>(ps.win.ranks), epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 9);
+    if (!ok && blockIdx.x < T) {
+      // some rank's rows did not come back: the token's output is written as zeros (the
+      // window's status word and cdg_device_status() report the timeout)
+      for (int64_t c = threadIdx.x; c < H; c += blockDim.x) y[blockIdx.x * H + c] = __float2bfloat16_rn(0.0f);
+    }
   }
   __shared__ int64_t s_row[kCombineMaxTopk];
   __shared__ float s_w[kCombineMaxTopk];
@@ -962,10 +991,11 @@ int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int6
   return cdg::launched();
 }
 
-int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t ranks, int64_t cap, int64_t H,
-                      const uint64_t* peers, void* window, int32_t me, int32_t* scratch, cdg_stream_t stream) {
+int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* perm_pos, int64_t ranks,
+                      int64_t cap, int64_t H, const uint64_t* peers, void* window, int32_t me, int32_t* scratch,
+                      cdg_stream_t stream) {
   if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || !peers || !window || !scratch || me < 0 ||
-      me >= ranks)
+      me >= ranks || y_rows < 0 || y_stride < H)
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(Y) % 16 || y_stride % 8) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -977,8 +1007,8 @@ int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, 
   ps.me = me;
   const int64_t R = ranks * (cap + 1);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
-  cdg::ep_return_p2p_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(Y), y_stride, perm_pos, ranks, cap,
-                                                  H, ps, scratch);
+  cdg::ep_return_p2p_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(Y), y_stride, y_rows, perm_pos,
+                                                  ranks, cap, H, ps, scratch);
   return cdg::launched();
 }
 
@@ -997,6 +1027,30 @@ int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* top
                                                      static_cast<__nv_bfloat16*>(y), ps, scratch);
   return cdg::launched();
 }
+
+int cdg_ep_set_wait_timeout_ns(uint64_t ns) {
+  if (ns > 60ull * 1000000000ull) return CDG_ERR_INVALID_ARGUMENT;
+  const uint64_t v = ns ? ns : cdg::kPeerWaitNs;
+  return cudaMemcpyToSymbol(cdg::g_peer_wait_ns, &v, sizeof(v)) == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
+}
+
+}  // extern "C"
+
+namespace cdg {
+// The exchange kernels' half of cdg_device_status(): reads (after the device is idle) and
+// optionally clears this unit's sticky record on the current device.
+int ep_sticky_status(int clear, int32_t* out) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(out, g_ep_sticky_status, 2 * sizeof(int32_t)) != cudaSuccess) return CDG_ERR_CUDA;
+  if (clear) {
+    const int32_t z[2] = {0, 0};
+    if (cudaMemcpyToSymbol(g_ep_sticky_status, z, sizeof(z)) != cudaSuccess) return CDG_ERR_CUDA;
+  }
+  return CDG_OK;
+}
+}  // namespace cdg
+
+extern "C" {
 
 // ---------------------------------------------------------------- MegaMoE weight layout
 int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t stride_n, void* dst, int64_t G, int64_t N,

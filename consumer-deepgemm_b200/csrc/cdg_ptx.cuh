@@ -23,6 +23,22 @@ enum : int {
   kStatusBadIndex = 2,      // an index a kernel computed fell outside its buffer
 };
 
+// Sticky per-device record of device-side errors, kept by the library itself: every bounded
+// wait that gives up ORs its status bit into [0] and leaves the first wait code in [1],
+// whichever workspace the call used (caller memory, or the no-allocation entry's static
+// scratch).  cdg_device_status() reads and optionally clears it.  One copy per translation
+// unit that includes this header (the host side of that unit reads its own copy).
+static __device__ int g_sticky_status[2];
+
+__device__ __forceinline__ void record_timeout(int* status, int where) {
+  if (status) {
+    atomicOr(status, kStatusTimeout);
+    atomicCAS(status + 1, 0, where);
+  }
+  atomicOr(&g_sticky_status[0], kStatusTimeout);
+  atomicCAS(&g_sticky_status[1], 0, where);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -89,6 +105,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     if (mbar_try_wait(addr, parity)) return true;
     if (global_timer_ns() - t0 > CDG_WAIT_TIMEOUT_NS) {
       if (status) atomicOr(status, kStatusTimeout);
+      atomicOr(&g_sticky_status[0], kStatusTimeout);
       return false;
     }
   }
@@ -202,10 +219,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   while (true) {
     if (mbar_try_wait_cluster(addr, parity)) return true;
     if (global_timer_ns() - t0 > CDG_WAIT_TIMEOUT_NS) {
-      if (status) {
-        atomicOr(status, kStatusTimeout);
-        atomicCAS(status + 1, 0, where);
-      }
+      record_timeout(status, where);
       return false;
     }
   }
@@ -213,10 +227,13 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 
 // Code naming a wait for mbar_wait_cluster: role (1 producer/empty, 2 issuer/tempty,
 // 3 issuer/full (or sfready), 4 epilogue/tfull, 5 issuer/done, 6 scale copier/full (or the
-// TMEM scale slot), 7 scale-atom producer/slot free), CTA rank or issuer, stage, phase, step.
+// TMEM scale slot), 7 scale-atom producer/slot free; 15 is not a wait: the TMEM allocation
+// did not start at column 0), CTA rank or issuer, stage, phase, step.
 __device__ __forceinline__ int wait_code(int role, int who, int stage, uint32_t phase, int step) {
-  return (role << 28) | ((who & 15) << 24) | ((stage & 255) << 16) | (static_cast<int>(phase & 1u) << 15) |
-         (step & 0x7fff);
+  const uint32_t c = (static_cast<uint32_t>(role & 15) << 28) | (static_cast<uint32_t>(who & 15) << 24) |
+                     (static_cast<uint32_t>(stage & 255) << 16) | ((phase & 1u) << 15) |
+                     static_cast<uint32_t>(step & 0x7fff);
+  return static_cast<int>(c);  // the bit pattern; roles >= 8 read as negative int32
 }
 
 // Tiled TMA loads into this CTA's shared memory whose completion is counted on an
@@ -384,10 +401,7 @@ __device__ __forceinline__ bool mbar_wait_cta(uint64_t* bar, uint32_t parity, in
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
     if (global_timer_ns() - t0 > CDG_WAIT_TIMEOUT_NS) {
-      if (status) {
-        atomicOr(status, kStatusTimeout);
-        atomicCAS(status + 1, 0, where);
-      }
+      record_timeout(status, where);
       return false;
     }
   }

@@ -407,7 +407,8 @@ void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& perm_pos, int64_
   TORCH_CHECK(perm_pos.numel() == ranks * (cap + 1), "perm_pos: one entry per received slot");
   const c10::cuda::CUDAGuard guard(Y.device());
   auto scratch = torch::empty({1}, perm_pos.options());
-  check_status(cdg_ep_return_p2p(Y.data_ptr(), Y.stride(0), perm_pos.data_ptr<int32_t>(), ranks, cap, Y.size(1),
+  check_status(cdg_ep_return_p2p(Y.data_ptr(), Y.stride(0), Y.size(0), perm_pos.data_ptr<int32_t>(), ranks, cap,
+                                 Y.size(1),
                                  reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
                                  reinterpret_cast<void*>(window), static_cast<int32_t>(me), scratch.data_ptr<int32_t>(),
                                  cur_stream(Y)),
@@ -529,6 +530,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine_p2p", &ep_combine_p2p, py::arg("window"), py::arg("send_index"), py::arg("topk_w"),
         py::arg("ranks"), py::arg("cap"), py::arg("hidden"));
   m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
+  m.def(
+      "ep_set_wait_timeout_ns",
+      [](uint64_t ns) { check_status(cdg_ep_set_wait_timeout_ns(ns), "ep_set_wait_timeout_ns"); }, py::arg("ns"));
+  m.def(
+      "device_status",
+      [](bool clear) {
+        int32_t where = 0;
+        const int st = cdg_device_status(clear ? 1 : 0, &where);
+        if (st != CDG_OK && st != CDG_ERR_DEVICE_TIMEOUT) check_status(st, "device_status");
+        return py::make_tuple(st, where);
+      },
+      py::arg("clear") = true);
+  m.def(
+      "set_num_sms", [](int64_t n) { check_status(cdg_set_num_sms(static_cast<int32_t>(n)), "set_num_sms"); },
+      py::arg("num_sms"));
+  m.def("get_num_sms", []() { return cdg_get_num_sms(); });
+  m.def("set_pdl", [](bool v) { check_status(cdg_set_pdl(v ? 1 : 0), "set_pdl"); }, py::arg("enable"));
+  m.def("get_pdl", []() { return cdg_get_pdl() != 0; });
   m.def("ep_unpermute", &ep_unpermute, py::arg("y"), py::arg("perm_pos"));
   m.def("ep_combine", &ep_combine, py::arg("rows"), py::arg("send_index"), py::arg("topk_w"));
   m.def("ep_unpermute_combine", &ep_unpermute_combine, py::arg("y"), py::arg("perm_pos"), py::arg("send_index"),

@@ -166,6 +166,35 @@ size_t cdg_sf_atoms_bytes(int64_t E, int64_t N, int64_t KB);
  * (csrc/cutlass_mxfp8_mxfp4_probe.cu:598-613). */
 int cdg_read_device_status(const void* workspace, cdg_stream_t stream);
 
+/* Device-side errors of every call on the current device since the last clear, whatever
+ * workspace (or exchange window) the call used: after synchronising the device, returns
+ * CDG_OK or CDG_ERR_DEVICE_TIMEOUT (a bounded wait gave up: an mbarrier wait of a GEMM
+ * kernel, or a wait on another rank's flag in the peer-memory exchange), stores the first
+ * such wait's code in *where (may be NULL; 0 when none), and clears the record when `clear`
+ * is nonzero.  A wait code holds the role (bits 28-31: 1 producer/empty, 2 issuer/tempty,
+ * 3 issuer/full, 4 epilogue/tfull, 5 issuer/done, 6 scale copier, 7 scale producer,
+ * 8 exchange dispatch flag, 9 exchange return flag, 15 TMEM allocation not at column 0),
+ * then the CTA rank, issuer or source rank, stage, phase and step.  Also covers the
+ * no-allocation entry point, whose workspace is private.  No reference counterpart: the
+ * reference reports device failures only as a launch result
+ * (csrc/cutlass_mxfp8_mxfp4_probe.cu:598-613, csrc/bindings.cpp:113-127). */
+int cdg_device_status(int32_t clear, int32_t* where);
+
+/* SMs the persistent GEMM kernels may use (0 = all; values above the device's count mean
+ * all), e.g. to leave SMs to kernels that overlap the GEMM on another stream.  Process-wide,
+ * read at every launch.  Replaces set_num_sms / get_num_sms (consumer_deep_gemm/utils.py:12-22),
+ * which the reference stores without using.  cdg_get_num_sms returns the setting, or the
+ * current device's SM count when it is 0. */
+int cdg_set_num_sms(int32_t num_sms);
+int cdg_get_num_sms(void);
+
+/* Whether the GEMM's kernels after the first are launched with programmatic stream
+ * serialization (1, the default: each may be scheduled while its predecessor drains and
+ * waits for it on the device) or as plain stream-ordered launches (0).  Process-wide.
+ * Replaces set_pdl / get_pdl (consumer_deep_gemm/utils.py:44-50), stored there unused. */
+int cdg_set_pdl(int32_t enable);
+int cdg_get_pdl(void);
+
 /* Static description of the build ("sm_100a; ...").
  * Replaces native.build_info (consumer_deep_gemm/native.py:26-39) and the SM120
  * probes (csrc/cutlass_sm120_probe.cu:6-22). */
@@ -329,7 +358,7 @@ int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t strid
  * window, so the calls take no per-step argument and a whole step can be captured in a CUDA
  * graph; every rank must run the same number of steps.  Plain stores and loads over NVLink:
  * no multicast.  A wait that gives up after 2 s skips its CTA's work and sets the window's
- * status word (cdg_ep_window_status reports it).  scratch: int32
+ * status word (cdg_ep_window_status and cdg_device_status report it).  scratch: int32
  * [cdg_ep_fixed_scratch_ints(ranks, E)] for dispatch, int32 [1] for return and combine. */
 size_t cdg_ep_window_bytes(int64_t ranks, int64_t cap, int64_t H);
 int cdg_ep_window_create(size_t bytes, void** window, void* ipc_handle /* 64 bytes out */);
@@ -343,8 +372,15 @@ int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const 
 int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t* fill,
                        uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
                        cdg_stream_t stream);
-int cdg_ep_return_p2p(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t ranks, int64_t cap, int64_t H,
-                      const uint64_t* peers, void* window, int32_t me, int32_t* scratch, cdg_stream_t stream);
+int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* perm_pos, int64_t ranks,
+                      int64_t cap, int64_t H, const uint64_t* peers, void* window, int32_t me, int32_t* scratch,
+                      cdg_stream_t stream);
+/* Bound of the exchange's waits on other ranks' flags on the current device, in ns (0 = the
+ * default 2 s; at most 60 s).  A wait that runs out sets the window's status word and the
+ * record cdg_device_status() reads; the waiting step then places no rows (permute: every
+ * slot's perm_pos is -1) or writes zero rows (combine), so nothing downstream reads memory
+ * that was never written. */
+int cdg_ep_set_wait_timeout_ns(uint64_t ns);
 int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
                        int64_t H, int64_t ranks, int64_t cap, int32_t* scratch, void* y, cdg_stream_t stream);
 

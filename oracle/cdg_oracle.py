@@ -87,7 +87,7 @@ def dequant_fp4_block(x: torch.Tensor, scale, block_k: int = 32) -> torch.Tensor
         x = x.view(torch.uint8)
     if x.dtype != torch.uint8:
         return x.to(torch.bfloat16)
-    table = torch.from_numpy(E2M1_VALUES)
+    table = torch.from_numpy(E2M1_VALUES).to(x.device)  # the checker also runs on GPU tensors in tests
     low = table[(x & 0x0F).to(torch.long)]
     high = table[((x >> 4) & 0x0F).to(torch.long)]
     out = torch.stack((low, high), dim=-1).flatten(-2)

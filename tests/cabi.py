@@ -64,6 +64,10 @@ def lib():
         l.cdg_sf_atoms_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]
         l.cdg_sf_atoms_bytes.restype = ctypes.c_size_t
         l.cdg_read_device_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        l.cdg_device_status.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]
+        l.cdg_ep_set_wait_timeout_ns.argtypes = [ctypes.c_uint64]
+        l.cdg_set_num_sms.argtypes = [ctypes.c_int32]
+        l.cdg_set_pdl.argtypes = [ctypes.c_int32]
         l.cdg_build_info.restype = ctypes.c_char_p
         l.cdg_status_string.restype = ctypes.c_char_p
         _lib = l
@@ -143,3 +147,10 @@ def transform_sf(sb: torch.Tensor) -> torch.Tensor:
                             ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == CDG_OK, st
     return out
+
+
+def device_status(clear: bool = True) -> tuple[int, int]:
+    """(status, first wait code) of cdg_device_status on the current device."""
+    where = ctypes.c_int32(0)
+    st = lib().cdg_device_status(1 if clear else 0, ctypes.byref(where))
+    return st, where.value

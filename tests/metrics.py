@@ -10,9 +10,11 @@ TOL_ROW_L2 = 2e-3
 
 def errors(out: torch.Tensor, ref: torch.Tensor, rows=None):
     """(normwise max relative error, max per-row relative L2) over `rows` (default all)."""
-    o = out.detach().float().cpu()
-    r = ref.detach().float().cpu()
+    # computed where `out` lies (full-size GPU outputs stay on the GPU)
+    o = out.detach().float()
+    r = ref.detach().float().to(o.device)
     if rows is not None:
+        rows = rows.to(o.device) if isinstance(rows, torch.Tensor) else rows
         o, r = o[rows], r[rows]
     if r.numel() == 0:
         return 0.0, 0.0

@@ -6,9 +6,15 @@ Tolerances:
   * SiLU-mul + requant: scales within 1e-6 relative; e4m3 codes equal except where the
     CUDA and CPU exponentials differ by an ulp (at most 1 in 1000 codes, each within one e4m3 step).
   * Dispatch / permute / unpermute: exact (bytes).
-  * Whole layer (two GEMMs with an e4m3 requantisation between them, which turns last-bit
-    differences of FC1 into e4m3 rounding flips): max |y - ref| / max |ref| <= 1e-2 and
-    per-row relative L2 <= 1e-2 against the CPU reference layer.
+  * Layer stages, each fed the device's own input of that stage: FC1 and FC2 within the
+    GEMM's tolerances (max |d - ref| / max |ref| <= 1e-2, per-row relative L2 <= 2e-3) against
+    the oracle; SiLU-mul + requant as above; the top-k combine within 2e-3 per row.
+  * Whole layer end to end: max |y - ref| / max |ref| <= 1e-2 and per-row relative L2 <= 1e-2
+    against the CPU reference layer.  The 2e-3 bound of a single GEMM cannot hold end to end:
+    FC1's outputs agree with the reference's to ~1e-3, i.e. differ in the last BF16 bit for a
+    fraction of elements, and the e4m3 requantisation between the GEMMs turns each such
+    difference at a rounding boundary into a whole e4m3 step (2^-3 relative) of one FC2 input.
+  * A peer wait that nobody satisfies gives up within its configured limit and is reported.
 """
 
 import os
@@ -231,11 +237,133 @@ def test_layer_single_gpu_matches_cpu_reference(ue8m0):
     assert nw <= 1e-2 and rl2 <= 1e-2, (nw, rl2)
 
 
+class _RecordingOps:
+    """NativeOps that keep every stage's inputs and outputs of one forward."""
+
+    def __init__(self):
+        from consumer_deep_gemm.moe import NativeOps
+
+        self.inner = NativeOps()
+        self.rec = {"gemm": []}
+
+    def __getattr__(self, name):
+        return getattr(self.inner, name)
+
+    def quant_dispatch_local(self, *args, **kw):
+        out = self.inner.quant_dispatch_local(*args, **kw)
+        self.rec["dispatch"] = out
+        return out
+
+    def gemm(self, a, sa, w, w_sf, m_indices, skip_ungrouped=False):
+        d = self.inner.gemm(a, sa, w, w_sf, m_indices, skip_ungrouped)
+        self.rec["gemm"].append((a, sa, m_indices, d))
+        return d
+
+    def act(self, h, m_indices, ue8m0=False):
+        out = self.inner.act(h, m_indices, ue8m0)
+        self.rec["act"] = (h, m_indices, out)
+        return out
+
+    def unpermute_combine(self, y, perm_pos, send_index, topk_w):
+        out = self.inner.unpermute_combine(y, perm_pos, send_index, topk_w)
+        self.rec["combine"] = (y, perm_pos, send_index, topk_w, out)
+        return out
+
+
+@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
+def test_layer_stages_match_reference_at_gemm_tolerance(ue8m0):
+    """Each stage of the one-GPU layer against the reference of that stage, on the device's own
+    input to it: the GEMMs meet the single-GEMM bound (per-row L2 <= 2e-3)."""
+    from consumer_deep_gemm.moe import MoELayer
+    from metrics import TOL_NORMWISE, TOL_ROW_L2, errors
+    from oracle import cdg_oracle as oracle
+
+    cfg = dict(tokens=1000 if ue8m0 else 96, experts=8, hidden=512, inter=256, topk=2)
+    x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**cfg)
+    ops = _RecordingOps()
+    layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), num_experts=cfg["experts"], ops=ops,
+                     ue8m0=ue8m0)
+    layer(x.to(DEV), ids.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    ref_ops = TorchRefOps()
+    for (a, sa, mi, d), (wt, ws) in zip(ops.rec["gemm"], ((w1, w1s), (w2, w2s))):
+        ref = torch.empty(d.shape, dtype=torch.bfloat16)
+        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a.cpu(), sa.cpu()), (wt, ws), ref, mi.cpu())
+        rows = mi.cpu() >= 0
+        nw, rl2 = errors(d.cpu(), ref, rows)
+        assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, ("gemm", nw, rl2)
+    h, mi, (q, s) = ops.rec["act"]
+    rows = mi.cpu() >= 0
+    rq, rs = ref_ops.act(h.cpu()[rows], None, ue8m0)
+    assert torch.allclose(s.cpu()[rows], rs, rtol=1e-6, atol=0)
+    qa, qb = q.cpu()[rows].view(torch.uint8).to(torch.int32), rq.view(torch.uint8).to(torch.int32)
+    diff = qa != qb
+    assert diff.float().mean().item() <= 1e-3 and bool(((qa - qb).abs()[diff] <= 1).all())
+    y2, pos, si, tw, out = ops.rec["combine"]
+    ref_y = ref_ops.unpermute_combine(y2.cpu(), pos.cpu(), si.cpu(), tw.cpu())
+    nw, rl2 = errors(out.cpu(), ref_y)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, ("combine", nw, rl2)
+
+
+def test_peer_wait_runs_out_and_context_stays_usable():
+    """Bounded waits on other ranks' flags, on one GPU: a window whose flags nobody raises.
+
+    With the wait limit at 10 ms, the permute step gives up (it places no row and every
+    slot's perm_pos is -1), the combine step gives up (its output rows are zeros), the
+    window's status word and the library's device record report CDG_ERR_DEVICE_TIMEOUT with
+    the permute's wait code, and the context keeps working: a GEMM afterwards matches the
+    reference.  Nothing here faults or hangs: every wait has its limit."""
+    import consumer_deep_gemm as cdg
+    from conftest import load_gemm_case
+    from metrics import TOL_NORMWISE, TOL_ROW_L2, errors
+
+    C = _ext()
+    ranks, T, topk, H, e_loc = 2, 16, 2, 512, 4
+    cap = T * topk
+    cdg.read_device_status(True)  # start from a clean record
+    own, _ = C.ep_window_create(C.ep_window_bytes(ranks, cap, H))
+    try:
+        C.ep_set_wait_timeout_ns(10_000_000)
+        like = torch.zeros(1, device=DEV)
+        m_pad = (ranks * cap + 127 * e_loc + 127) // 128 * 128
+        a, sa, mi, pos = C.ep_permute_p2p(own, ranks, cap, H, e_loc, m_pad, like)
+        send_index = torch.arange(T * topk, dtype=torch.int32, device=DEV)
+        tw = torch.full((T, topk), 0.5, device=DEV)
+        y = C.ep_combine_p2p(own, send_index, tw, ranks, cap, H)
+        torch.cuda.synchronize()
+        assert C.ep_window_status(own) == 6
+        st, where = cdg.read_device_status(True)
+        assert st == 6 and (where >> 28) == 8, (st, hex(where))
+        assert bool((pos == -1).all()) and bool((mi == -1).all())
+        assert bool((y.float() == 0).all())
+        assert cdg.read_device_status(True) == (0, 0)
+    finally:
+        C.ep_set_wait_timeout_ns(0)
+        C.ep_window_close(own, False)
+    c = load_gemm_case("c0")
+    dev = [t.to(DEV) for t in (c["a"], c["sa"], c["b"], c["sb"], c["m_indices"])]
+    d = torch.empty(c["d"].shape, dtype=torch.bfloat16, device=DEV)
+    cdg.m_grouped_fp8_fp4_gemm_nt_contiguous((dev[0], dev[1]), (dev[2], dev[3]), d, dev[4])
+    torch.cuda.synchronize()
+    pad = c["m_indices"] < 0
+    nw, rl2 = errors(d.cpu(), c["d"], ~pad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2
+    assert cdg.read_device_status(True) == (0, 0)
+
+
+def _free_port() -> int:
+    import socket
+
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_layer_expert_parallel_two_gpus():
     here = os.path.dirname(os.path.abspath(__file__))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr", "127.0.0.1", "--master-port", "29613", os.path.join(here, "ep_gpu_worker.py")]
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), os.path.join(here, "ep_gpu_worker.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -5,8 +5,8 @@ owned by another allocator, or their host language has no way to reach it.  For
 them `cdg_grouped_fp8_fp4_gemm_nt_contiguous_noalloc` uses a 64 MiB scratch
 array that lives inside the library.  These tests drive it through the C ABI and
 check that two calls in a row give what the regular entry point (caller-owned
-workspace) gives, within the tolerances of the parity tests, and that a problem
-too large for the scratch is refused before any launch.
+workspace) gives -- bit for bit, since both run the same kernels on the same
+plan -- and that a problem too large for the scratch is refused before any launch.
 """
 
 import ctypes
@@ -50,6 +50,11 @@ def _check_against_regular(name):
     assert bool((out[pad].float() == 0).all())
     nw, rl2 = errors(out, ref, ~pad)
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
+    # the same kernels on the same plan: identical bits, padding rows included
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), name
+    # no device wait gave up (the scratch's own status word is private; the library's
+    # per-device record covers it)
+    assert cabi.device_status() == (0, 0)
 
 
 def test_noalloc_matches_regular_entry_two_calls_in_a_row():
