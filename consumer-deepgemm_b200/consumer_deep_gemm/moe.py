@@ -33,9 +33,11 @@ All ranks must use the same value and pass at most that many tokens.
 
 ``exchange="p2p"`` (with ``max_tokens_per_rank``, GPUs of one NVLink domain) replaces
 the collectives by the library's own peer-memory exchange: each rank owns an exchange
-window shared through CUDA IPC; the dispatch kernel quantises and stores rows straight
-into the destination GPUs' windows, the return kernel stores GEMM rows straight back into
-the sources' windows, and release/acquire flags (bounded waits) order the steps.
+window shared through CUDA IPC; the dispatch kernel quantises each token's row once and
+stores it straight into the window of every rank that owns one of its experts (one row per
+token and rank, listing the token's local experts there), the receiver expands it into the
+experts' groups, the return kernel stores GEMM rows straight back into the sources' windows
+at their slot, and release/acquire flags (bounded waits) order the steps.
 
 The device steps sit behind a small ``ops`` interface so that the exchange
 logic can also be exercised with CPU implementations (tests do that with the
@@ -109,13 +111,14 @@ def _all_to_all(out, inp, out_splits, in_splits, group):
 class PeerWindows:
     """The exchange windows of all ranks of `group`, mapped into this process (CUDA IPC)."""
 
-    def __init__(self, group, cap: int, hidden: int, device):
+    def __init__(self, group, max_tokens: int, topk: int, hidden: int, device):
         import torch.distributed as dist
 
         self.C = native.require()
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        nbytes = self.C.ep_window_bytes(self.world, cap, hidden)
+        self.max_tokens, self.topk = max_tokens, topk
+        nbytes = self.C.ep_window_bytes(self.world, max_tokens, topk, hidden)
         if nbytes == 0:
             raise ValueError("unsupported peer exchange shape")
         self.own, handle = self.C.ep_window_create(nbytes)
@@ -309,12 +312,15 @@ class MoELayer:
             raise ValueError("the peer-memory exchange returns rows of the input width")
         cap = self.max_tokens * topk
         if self.windows is None:
-            self.windows = PeerWindows(self.group, cap, H, x.device)
+            self.windows = PeerWindows(self.group, self.max_tokens, topk, H, x.device)
         win, me = self.windows, self.rank
-        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, cap, win.peers, win.own, me, self.ue8m0)
+        if win.topk != topk:
+            raise ValueError(f"the exchange windows were made for top-{win.topk} routing, got top-{topk}")
+        send_index = C.ep_dispatch_p2p(x, topk_ids.contiguous(), E, world, self.max_tokens, win.peers, win.own, me,
+                                       self.ue8m0)
         self._phase("dispatch")
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
-        a, sa, m_indices, perm_pos = C.ep_permute_p2p(win.own, world, cap, H, E_loc, m_pad, x)
+        a, sa, m_indices, ret_slot = C.ep_permute_p2p(win.own, world, self.max_tokens, topk, H, E_loc, m_pad, x)
         self._phase("permute")
         h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         self._phase("fc1")
@@ -323,9 +329,9 @@ class MoELayer:
             self._phase("act")
             h = self.ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
             self._phase("fc2")
-        C.ep_return_p2p(h, perm_pos, world, cap, win.peers, win.own, me)
+        C.ep_return_p2p(h, ret_slot, world, self.max_tokens, topk, win.peers, win.own, me)
         self._phase("return")
-        y = C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, cap, H)
+        y = C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, self.max_tokens, H)
         self._phase("combine")
         return y
 

@@ -43,28 +43,39 @@ __device__ __forceinline__ int64_t load_idx(const void* p, int dtype, int64_t i)
 // Bytes of one dispatched row: [e4m3 data H][FP32 scales H/128][int32 local expert][pad to 16].
 __host__ __device__ __forceinline__ int64_t packed_row_bytes(int64_t H) { return (H + 4 * (H / 128) + 4 + 15) / 16 * 16; }
 
+// Bytes of one row of the peer-memory exchange: [e4m3 data H][FP32 scales H/128][int32
+// source token][topk x int32: the local expert of the token's slot j, or -1 when slot j goes
+// to another rank][pad to 16].  A token sends one such row to each rank that owns at least
+// one of its experts; the receiver expands it into every listed expert's group.
+__host__ __device__ __forceinline__ int64_t p2p_row_bytes(int64_t H, int64_t topk) {
+  return (H + 4 * (H / 128) + 4 + 4 * topk + 15) / 16 * 16;
+}
+
 // Exchange window of one rank: [0, 512) dispatch flags int32[ranks], [512, 1024) return
 // flags int32[ranks], [1024, 1028) status, [1028, 1032) the number of completed exchanges
 // (the step counter: a step's epoch is its value + 1); from 4096 the receive regions
-// [2 parity][ranks source][1 + cap rows][row bytes]; then (256-aligned) the return rows
-// [2 parity][ranks * (1 + cap)][H] BF16 in this rank's own send layout.
+// [2 parity][ranks source][1 + tokens rows][row bytes] (row 0 of a region is a header:
+// int32 per-local-expert slot counts, then the number of rows), then (256-aligned) the
+// return rows [2 parity][tokens * topk][H] BF16, indexed by this rank's own slot t * topk + j.
 struct Window {
-  int64_t ranks, cap, H, rb;
+  int64_t ranks, tokens, topk, H, rb;
   static constexpr int64_t kDispatchFlags = 0, kReturnFlags = 512, kStatus = 1024, kEpoch = 1028, kRecv = 4096;
-  __host__ __device__ int64_t recv_parity(int64_t parity) const { return kRecv + parity * ranks * (cap + 1) * rb; }
-  __host__ __device__ int64_t ret_base() const { return (recv_parity(2) + 255) / 256 * 256; }
-  __host__ __device__ int64_t ret_parity(int64_t parity) const { return ret_base() + parity * ranks * (cap + 1) * H * 2; }
+  __host__ __device__ int64_t region(int64_t parity, int64_t src) const {
+    return kRecv + (parity * ranks + src) * (tokens + 1) * rb;
+  }
+  __host__ __device__ int64_t ret_base() const { return (region(2, 0) + 255) / 256 * 256; }
+  __host__ __device__ int64_t ret_parity(int64_t parity) const { return ret_base() + parity * tokens * topk * H * 2; }
   __host__ __device__ int64_t bytes() const { return ret_parity(2); }
 };
 
-__host__ __device__ inline Window make_window(int64_t ranks, int64_t cap, int64_t H) {
-  return Window{ranks, cap, H, packed_row_bytes(H)};
+__host__ __device__ inline Window make_window(int64_t ranks, int64_t tokens, int64_t topk, int64_t H) {
+  return Window{ranks, tokens, topk, H, p2p_row_bytes(H, topk)};
 }
 
-// What the peer variants of the exchange kernels need: every rank's window (device array),
-// this rank's window and index, and the window layout.  The step's epoch (flag value and
-// buffer parity) is read from the own window's counter, so the kernels take no per-step
-// host argument and a whole exchange step can be captured in a CUDA graph.
+// What the peer-memory exchange kernels need: every rank's window (device array), this
+// rank's window and index, and the window layout.  The step's epoch (flag value and buffer
+// parity) is read from the own window's counter, so the kernels take no per-step host
+// argument and a whole exchange step can be captured in a CUDA graph.
 struct PeerStep {
   const uint64_t* peers = nullptr;
   uint8_t* own = nullptr;
@@ -154,6 +165,38 @@ __device__ __forceinline__ uint32_t quant_block_values(const float (&v)[4], int 
   }
   scale = pow2 ? s2 : amax / 448.0f;
   return packed;
+}
+
+// The same block quantisation with one division per block instead of one per element: the
+// scale is the one above, the codes take x * (448 / amax) (FP32 recipe) or x * (1 / s)
+// (power-of-two recipe, where it equals x / s exactly).  For the FP32 recipe the code can
+// differ from e4m3(x / amax * 448) only where the two roundings fall on opposite sides of an
+// e4m3 rounding point (a 1-in-2^18 event); used where the input is itself computed (SiLU-mul).
+__device__ __forceinline__ uint32_t quant_block_values_mul(const float (&v)[4], int pow2, float& scale) {
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  amax = fmaxf(amax, 1e-12f);
+  uint32_t sb = __float_as_uint(amax / 448.0f);
+  if (sb & 0x007FFFFFu) sb = (sb & 0xFF800000u) + 0x00800000u;
+  const float s2 = __uint_as_float(sb);
+  const float r = pow2 ? 1.0f / s2 : 448.0f / amax;
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(v[i] * r, __NV_SATFINITE, __NV_E4M3)) << (8 * i);
+  scale = pow2 ? s2 : amax / 448.0f;
+  return packed;
+}
+
+// silu(g) * u in FP32 with the fast exponential and a correctly rounded reciprocal.
+__device__ __forceinline__ float silu_mul(float g, float u) { return g * __frcp_rn(1.0f + __expf(-g)) * u; }
+
+__device__ __forceinline__ void quant_block_warp_mul(const float (&v)[4], uint8_t* q, float* scale_out, int lane,
+                                                     int pow2) {
+  float scale;
+  reinterpret_cast<uint32_t*>(q)[lane] = quant_block_values_mul(v, pow2, scale);
+  if (lane == 0) *scale_out = scale;
 }
 
 __device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* q, float* scale_out, int lane,
@@ -265,9 +308,9 @@ __global__ void __launch_bounds__(256) silu_mul_quant_vec_kernel(const __nv_bflo
       const float gv[4] = {g01.x, g01.y, g23.x, g23.y}, uv[4] = {u01.x, u01.y, u23.x, u23.y};
       float v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
-      quant_block_warp(v, q + r * q_stride + (kb0 + b) * 128, s + r * s_stride_m + (kb0 + b) * s_stride_k, lane,
-                       pow2);
+      for (int i = 0; i < 4; ++i) v[i] = silu_mul(gv[i], uv[i]);
+      quant_block_warp_mul(v, q + r * q_stride + (kb0 + b) * 128, s + r * s_stride_m + (kb0 + b) * s_stride_k,
+                           lane, pow2);
     }
   }
 }
@@ -292,8 +335,8 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride
   }
   float v[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) v[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
-  quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
+  for (int i = 0; i < 4; ++i) v[i] = silu_mul(gv[i], uv[i]);
+  quant_block_warp_mul(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
 }
 
 __global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64_t E, int32_t* cnt) {
@@ -367,21 +410,12 @@ constexpr int kFixedMaxExperts = 1024, kFixedMaxRanks = 256;
 // Per-destination, per-local-expert counts go to `scratch`; the last CTA writes them into
 // the region headers.  scratch (zeroed by the host): [ranks] fill, [ranks * E_local]
 // counts, [1] ticket.
-// Peer variant (ps.peers != nullptr): the region of destination d is this rank's source
-// region in d's exchange window for the step's parity; after every row and header landed,
-// the last CTA raises this rank's flag in each destination window to the step's epoch.
 __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x, int x_dtype, int64_t x_stride,
                                                                   const void* ids, int ids_dtype, int64_t T,
                                                                   int64_t topk, int64_t E, int64_t e_per_rank,
                                                                   int64_t ranks, int64_t H, int64_t cap,
                                                                   int32_t* scratch, uint8_t* out_rows,
-                                                                  int32_t* send_index, int pow2,
-                                                                  PeerStep ps = PeerStep{}) {
-  const uint64_t* peers = ps.peers;
-  const int32_t epoch = peers ? ps.epoch() : 0;
-  const int64_t region_off = peers ? ps.win.recv_parity(epoch & 1) + ps.me * (cap + 1) * ps.win.rb : 0;
-  const int64_t flag_off = Window::kDispatchFlags;
-  const int me = ps.me;
+                                                                  int32_t* send_index, int pow2) {
   __shared__ int s_last;
   __shared__ int64_t s_row, s_e;
   int32_t* fill = scratch;
@@ -405,12 +439,7 @@ __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x,
   }
   __syncthreads();
   const int64_t row = s_row;
-  // where a row of the send layout (region d = row / (cap + 1)) lands
-  auto row_ptr = [&](int64_t r) -> uint8_t* {
-    if (!peers) return out_rows + r * rb;
-    const int64_t d = r / (cap + 1);
-    return reinterpret_cast<uint8_t*>(peers[d]) + region_off + (r - d * (cap + 1)) * rb;
-  };
+  auto row_ptr = [&](int64_t r) -> uint8_t* { return out_rows + r * rb; };
   if (row >= 0) {
     const int64_t t = w / topk;
     uint8_t* out = row_ptr(row);
@@ -431,9 +460,9 @@ __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x,
     }
     if (threadIdx.x == 0) *reinterpret_cast<int32_t*>(out + H + 4 * (H / 128)) = static_cast<int32_t>(s_e % e_per_rank);
   }
-  // the last CTA to finish writes the region headers (and, peer variant, the flags); every
-  // thread fences its own row stores before the CTA takes its ticket
-  if (peers) __threadfence_system(); else __threadfence();
+  // the last CTA to finish writes the region headers; every thread fences its own row
+  // stores before the CTA takes its ticket
+  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
   __syncthreads();
@@ -443,42 +472,19 @@ __global__ void __launch_bounds__(128) ep_quant_pack_fixed_kernel(const void* x,
     const int64_t d = i / e_per_rank, e = i - d * e_per_rank;
     reinterpret_cast<int32_t*>(row_ptr(d * (cap + 1)))[e] = __ldcg(&cnt[i]);
   }
-  if (peers) {
-    __threadfence_system();
-    __syncthreads();
-    for (int64_t d = threadIdx.x; d < ranks; d += blockDim.x)
-      st_release_sys(reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(peers[d]) + flag_off) + me, epoch);
-  }
 }
 
 // Every CTA first derives, in shared memory, each source's row count and the 128-aligned
 // offsets of the local experts' groups (exclusive scan of the per-expert totals over all
 // sources, read from the region headers); then one warp per slot places valid rows as
 // ep_permute_kernel does.
-// Peer variant (ps.own != nullptr; `rows` unused): the received regions are the own
-// window's for the step's parity; first waits until every source raised its flag.
 __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* rows, int64_t ranks, int64_t cap,
                                                                int64_t H, int64_t E_local, int32_t* fill, uint8_t* A,
-                                                               float* SA, int32_t* m_indices, int32_t* perm_pos,
-                                                               PeerStep ps = PeerStep{}) {
+                                                               float* SA, int32_t* m_indices, int32_t* perm_pos) {
   __shared__ int64_t s_off[kFixedMaxExperts];
   __shared__ int32_t s_nsrc[kFixedMaxRanks];
   __shared__ int64_t s_warp_sum[8];
   const int tid = threadIdx.x;
-  if (ps.own) {
-    const int32_t epoch = ps.epoch();
-    rows = ps.own + ps.win.recv_parity(epoch & 1);
-    if (!wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kDispatchFlags), static_cast<int>(ranks),
-                         epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 8)) {
-      // The rows did not all arrive: place none of this CTA's slots.  Every slot still gets
-      // perm_pos = -1, so the return step (which reads rows at perm_pos) skips them.
-      const int64_t R = ranks * (cap + 1);
-      for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + tid) >> 5; w < R;
-           w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5)
-        if ((tid & 31) == 0) perm_pos[w] = -1;
-      return;
-    }
-  }
   const int64_t rb = packed_row_bytes(H);
   auto header = [&](int64_t r) { return reinterpret_cast<const int32_t*>(rows + r * (cap + 1) * rb); };
   // per-expert aligned totals, 4 consecutive experts per thread, then a block scan
@@ -542,31 +548,254 @@ __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* ro
   }
 }
 
-// Peer return: one warp per received slot (region src, slot s) whose row was placed at
-// perm_pos; the GEMM row goes straight to the source's window (return rows of the step's
-// parity), at the row of its own send layout (me * (cap + 1) + 1 + s).  Slots whose perm_pos
-// is negative or not below y_rows (the rows of Y) are skipped.  The last CTA raises this
-// rank's flag in every source window.
-// scratch: [1] ticket, zeroed by the host.
-__global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* Y, int64_t y_stride, int64_t y_rows,
-                                                            const int32_t* perm_pos, int64_t ranks, int64_t cap,
-                                                            int64_t H, PeerStep ps, int32_t* scratch) {
+// ---------------------------------------------------------------- peer-memory exchange
+// Four values of a 128-column block for lane `lane` (BF16 or FP32 row, 16-byte aligned).
+__device__ __forceinline__ void load_block4(const void* x, int x_dtype, int64_t base, float (&v)[4]) {
+  if (x_dtype == CDG_DTYPE_BF16) {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + base));
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+  } else {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + base));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  }
+}
+
+// One warp quantises row x[row_off .. row_off + H) (quant_block_values: the
+// per_block_cast_to_fp8 or power-of-two recipe, bit for bit) into codes[H] and scales[H/128]
+// in shared memory; the loads of eight 128-column blocks are issued before the first is used.
+__device__ __forceinline__ void warp_quant_row(const void* x, int x_dtype, int64_t row_off, int64_t H, uint8_t* codes,
+                                               float* scales, int lane, int pow2) {
+  const int64_t nkb = H / 128;
+  for (int64_t kb0 = 0; kb0 < nkb; kb0 += 8) {
+    float v[8][4];
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+      if (kb0 + b < nkb) load_block4(x, x_dtype, row_off + (kb0 + b) * 128 + lane * 4, v[b]);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      if (kb0 + b < nkb) {
+        float sc;
+        reinterpret_cast<uint32_t*>(codes + (kb0 + b) * 128)[lane] = quant_block_values(v[b], pow2, sc);
+        if (lane == 0) scales[kb0 + b] = sc;
+      }
+    }
+  }
+}
+
+// Shared-memory stage of one quantised row: codes, then scales, 16-byte aligned.
+__host__ __device__ __forceinline__ int64_t row_stage_bytes(int64_t H) { return (H + 4 * (H / 128) + 15) / 16 * 16; }
+
+constexpr int kP2pWarps = 4;  // tokens per CTA of the peer dispatch, one warp each
+
+// Peer dispatch.  Warp w of CTA c takes token t = c * kP2pWarps + w; lane j holds the token's
+// slot j.  The slots are grouped by destination rank (__match_any_sync): the token sends one
+// row to each rank that owns any of its experts.  The CTA counts its rows per destination in
+// shared memory and claims them from the global counter with one atomic per destination.  The
+// warp quantises the token's row once into shared memory, then stores it with 16-byte stores
+// into each destination's region of this rank (over NVLink for the other GPUs), followed by
+// the token index and, per slot, its local expert (or -1 when the slot goes elsewhere).
+// send_index[t * topk + j] is the slot itself (where the combine finds its returned row), or
+// -1 for a slot whose expert lies outside [0, E).  Per-destination, per-local-expert slot
+// counts go to `scratch`; the last CTA writes each destination's header (those counts and
+// the number of rows) and raises this rank's flag there.
+// scratch (zeroed by the host): [ranks] rows per destination, [ranks * E_local] counts, [1] ticket.
+__global__ void __launch_bounds__(kP2pWarps * 32) ep_dispatch_p2p_kernel(const void* x, int x_dtype, int64_t x_stride,
+                                                                        const void* ids, int ids_dtype, int64_t T,
+                                                                        int64_t E, int64_t e_per_rank,
+                                                                        int32_t* scratch, int32_t* send_index, int pow2,
+                                                                        PeerStep ps) {
+  extern __shared__ __align__(16) uint8_t p2p_stage[];
+  __shared__ int s_cnt[kFixedMaxRanks];
+  __shared__ int s_base[kFixedMaxRanks];
   __shared__ int s_last;
-  const uint64_t* peers = ps.peers;
+  const int64_t ranks = ps.win.ranks, topk = ps.win.topk, H = ps.win.H, rb = ps.win.rb;
+  const int32_t epoch = ps.epoch();
+  int32_t* fill = scratch;
+  int32_t* cnt = scratch + ranks;
+  int32_t* ticket = cnt + ranks * e_per_rank;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kP2pWarps + warp;
+  const bool live = t < T;
+  for (int i = threadIdx.x; i < ranks; i += blockDim.x) s_cnt[i] = 0;
+  __syncthreads();
+  int64_t e = -1;
+  int dest = -1;
+  if (live && lane < topk) {
+    const int64_t v = load_idx(ids, ids_dtype, t * topk + lane);
+    if (v >= 0 && v < E) {
+      e = v;
+      dest = static_cast<int>(v / e_per_rank);
+    }
+    send_index[t * topk + lane] = dest >= 0 ? static_cast<int32_t>(t * topk + lane) : -1;
+  }
+  const unsigned same = __match_any_sync(0xffffffffu, dest);  // lanes sending to the same rank
+  const bool lead = dest >= 0 && lane == __ffs(same) - 1;
+  int local = 0;
+  if (lead) local = atomicAdd(&s_cnt[dest], 1);
+  if (dest >= 0) atomicAdd(&cnt[dest * e_per_rank + e % e_per_rank], 1);
+  __syncthreads();
+  for (int i = threadIdx.x; i < ranks; i += blockDim.x) s_base[i] = s_cnt[i] ? atomicAdd(&fill[i], s_cnt[i]) : 0;
+  uint8_t* stage = p2p_stage + warp * row_stage_bytes(H);
+  if (live) warp_quant_row(x, x_dtype, t * x_stride, H, stage, reinterpret_cast<float*>(stage + H), lane, pow2);
+  __syncthreads();  // s_base complete; the warp's stage written
+  const int64_t region = ps.win.region(epoch & 1, ps.me);
+  for (unsigned leaders = __ballot_sync(0xffffffffu, lead); leaders; leaders &= leaders - 1) {
+    const int l = __ffs(leaders) - 1;
+    const int d = __shfl_sync(0xffffffffu, dest, l);
+    const int64_t r = s_base[d] + __shfl_sync(0xffffffffu, local, l);
+    uint8_t* out = reinterpret_cast<uint8_t*>(ps.peers[d]) + region + (1 + r) * rb;
+    for (int64_t c = lane; c < H / 16; c += 32)
+      reinterpret_cast<uint4*>(out)[c] = reinterpret_cast<const uint4*>(stage)[c];
+    for (int64_t c = lane; c < H / 128; c += 32)
+      reinterpret_cast<float*>(out + H)[c] = reinterpret_cast<const float*>(stage + H)[c];
+    int32_t* tail = reinterpret_cast<int32_t*>(out + H + 4 * (H / 128));
+    if (lane == 0) tail[0] = static_cast<int32_t>(t);
+    if (lane < topk) tail[1 + lane] = dest == d ? static_cast<int32_t>(e % e_per_rank) : -1;
+  }
+  // the last CTA writes the headers and raises the flags; every thread fences its own peer
+  // stores before the CTA takes its ticket
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int64_t i = threadIdx.x; i < ranks * (e_per_rank + 1); i += blockDim.x) {
+    const int64_t d = i / (e_per_rank + 1), k = i - d * (e_per_rank + 1);
+    int32_t* hdr = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ps.peers[d]) + region);
+    hdr[k] = k < e_per_rank ? __ldcg(&cnt[d * e_per_rank + k]) : __ldcg(&fill[d]);
+  }
+  __threadfence_system();
+  __syncthreads();
+  for (int64_t d = threadIdx.x; d < ranks; d += blockDim.x)
+    st_release_sys(reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ps.peers[d]) + Window::kDispatchFlags) + ps.me,
+                   epoch);
+}
+
+// Peer permute.  Waits (bounded) until every source raised its flag for the step, derives the
+// local experts' 128-aligned group offsets from the region headers (exclusive scan of the
+// per-expert totals over all sources), then one warp per received row (region src, row r
+// below the header's row count) reads the row once and writes it into the group of each of
+// its slots' local experts: A, SA, m_indices, and ret_slot[pos] = src * cap + t * topk + j
+// (cap = tokens * topk), the place in the source's window where the return step sends GEMM
+// row pos.  A wait that gives up places nothing (m_indices and ret_slot keep the -1 the host
+// wrote).  fill: [E_local] counters, zeroed by the host.
+__global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, int32_t* fill, uint8_t* A, float* SA,
+                                                             int32_t* m_indices, int32_t* ret_slot, PeerStep ps) {
+  constexpr int kMaxTopk = 32;
+  __shared__ int64_t s_off[kFixedMaxExperts];
+  __shared__ int32_t s_tot[kFixedMaxExperts];
+  __shared__ int32_t s_nrows[kFixedMaxRanks];
+  __shared__ int64_t s_warp_sum[8];
+  __shared__ int64_t s_pos[8][kMaxTopk];
+  const int64_t ranks = ps.win.ranks, tokens = ps.win.tokens, topk = ps.win.topk, H = ps.win.H, rb = ps.win.rb;
+  const int64_t cap = tokens * topk;
+  const int32_t epoch = ps.epoch();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (!wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kDispatchFlags), static_cast<int>(ranks),
+                       epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 8))
+    return;
+  auto header = [&](int64_t src) {
+    return reinterpret_cast<const int32_t*>(ps.own + ps.win.region(epoch & 1, src));
+  };
+  int64_t part[4];
+  int64_t run = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t e = tid * 4 + i;
+    int64_t tot = 0;
+    if (e < E_local) {
+      for (int64_t r = 0; r < ranks; ++r) tot += header(r)[e];
+      s_tot[e] = static_cast<int32_t>(tot);
+    }
+    part[i] = (tot + 127) / 128 * 128;
+    run += part[i];
+  }
+  int64_t incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp_sum[warp] = incl;
+  for (int64_t r = tid; r < ranks; r += blockDim.x) s_nrows[r] = header(r)[E_local];
+  __syncthreads();
+  int64_t base = 0;
+  for (int w = 0; w < warp; ++w) base += s_warp_sum[w];
+  int64_t off = base + incl - run;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t e = tid * 4 + i;
+    if (e < E_local) s_off[e] = off;
+    off += part[i];
+  }
+  __syncthreads();
+  const int64_t R = ranks * tokens;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + tid) >> 5; w < R;
+       w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t src = w / tokens, r = w - src * tokens;
+    if (r >= s_nrows[src]) continue;  // warp-uniform
+    const uint8_t* in = ps.own + ps.win.region(epoch & 1, src) + (1 + r) * rb;
+    const int32_t* tail = reinterpret_cast<const int32_t*>(in + H + 4 * (H / 128));
+    int64_t pos = -1;
+    if (lane < topk) {
+      const int32_t el = tail[1 + lane];
+      const int32_t t = tail[0];
+      if (el >= 0 && el < E_local) {
+        const int32_t k = atomicAdd(&fill[el], 1);
+        if (k < s_tot[el] && t >= 0 && t < tokens) {  // inside the expert's group as the headers sized it
+          pos = s_off[el] + k;
+          m_indices[pos] = el;
+          ret_slot[pos] = static_cast<int32_t>(src * cap + static_cast<int64_t>(t) * topk + lane);
+        } else {
+          atomicOr(reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 2);
+          atomicOr(&g_ep_sticky_status[0], 2);
+          atomicCAS(&g_ep_sticky_status[1], 0, peer_wait_code(10, static_cast<int>(src)));
+        }
+      }
+      s_pos[warp][lane] = pos;
+    }
+    __syncwarp();
+    for (int64_t c = lane; c < H / 16; c += 32) {
+      const uint4 v = reinterpret_cast<const uint4*>(in)[c];
+      for (int j = 0; j < topk; ++j) {
+        const int64_t p = s_pos[warp][j];
+        if (p >= 0) reinterpret_cast<uint4*>(A + p * H)[c] = v;
+      }
+    }
+    for (int64_t c = lane; c < H / 128; c += 32) {
+      const float v = reinterpret_cast<const float*>(in + H)[c];
+      for (int j = 0; j < topk; ++j) {
+        const int64_t p = s_pos[warp][j];
+        if (p >= 0) SA[p * (H / 128) + c] = v;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Peer return: one warp per GEMM row pos < rows whose ret_slot is set; the row goes straight to
+// its source's window (return rows of the step's parity) at the source's slot index.  Entries
+// that decode to a rank or slot outside the window are skipped.  The last CTA raises this
+// rank's flag in every source window.  scratch: [1] ticket, zeroed by the host.
+__global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16* Y, int64_t y_stride, int64_t rows,
+                                                            const int32_t* ret_slot, PeerStep ps, int32_t* scratch) {
+  __shared__ int s_last;
+  const int64_t ranks = ps.win.ranks, H = ps.win.H, cap = ps.win.tokens * ps.win.topk;
   const int32_t epoch = ps.epoch();
   const int64_t ret_off = ps.win.ret_parity(epoch & 1);
-  const int64_t flag_off = Window::kReturnFlags;
-  const int me = ps.me;
   const int lane = threadIdx.x & 31;
-  const int64_t R = ranks * (cap + 1);
-  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < R;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < rows;
        w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
-    const int32_t pos = perm_pos[w];
-    if (pos < 0 || pos >= y_rows) continue;
-    const int64_t src = w / (cap + 1), s = w - src * (cap + 1);
-    const uint4* from = reinterpret_cast<const uint4*>(Y + static_cast<int64_t>(pos) * y_stride);
-    uint4* to = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peers[src]) + ret_off +
-                                         (me * (cap + 1) + s) * H * static_cast<int64_t>(sizeof(__nv_bfloat16)));
+    const int32_t rs = ret_slot[w];
+    if (rs < 0) continue;
+    const int64_t src = rs / cap, idx = rs - src * cap;
+    if (src >= ranks) continue;
+    const uint4* from = reinterpret_cast<const uint4*>(Y + w * y_stride);
+    uint4* to = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(ps.peers[src]) + ret_off +
+                                         idx * H * static_cast<int64_t>(sizeof(__nv_bfloat16)));
     for (int64_t c = lane; c < H / 8; c += 32) to[c] = from[c];
   }
   __threadfence_system();  // each thread's peer stores before the CTA takes its ticket
@@ -576,7 +805,8 @@ __global__ void __launch_bounds__(256) ep_return_p2p_kernel(const __nv_bfloat16*
   if (!s_last) return;
   __threadfence_system();
   for (int64_t r = threadIdx.x; r < ranks; r += blockDim.x)
-    st_release_sys(reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(peers[r]) + flag_off) + me, epoch);
+    st_release_sys(reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ps.peers[r]) + Window::kReturnFlags) + ps.me,
+                   epoch);
 }
 
 // One warp per row: out[i, :] = Y[perm_pos[i], :]; rows with perm_pos -1 are left as they are.
@@ -596,7 +826,8 @@ __global__ void ep_unpermute_kernel(const __nv_bfloat16* Y, int64_t y_stride, co
 // slots whose index or row is -1 add nothing.  VEC: each thread reads and writes 8 columns
 // at a time (16-byte accesses; H a multiple of 8, rows and y 16-byte aligned).
 // Peer variant (ps.own != nullptr; `rows` unused): the returned rows are the own window's
-// for the step's parity; first waits until every rank returned its rows; the last CTA then
+// return rows for the step's parity, indexed by slot; first waits until every rank returned
+// its rows (a wait that gives up writes the token's output as zeros); the last CTA then
 // advances the window's step counter (scratch: [1] ticket, zeroed by the host).
 constexpr int kCombineMaxTopk = 32;
 
@@ -900,10 +1131,36 @@ int cdg_ep_unpermute_combine(const void* Y, int64_t y_stride, const int32_t* per
                              reinterpret_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
 // ---------------------------------------------------------------- peer-memory exchange
-size_t cdg_ep_window_bytes(int64_t ranks, int64_t cap, int64_t H) {
-  if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128) return 0;
-  return static_cast<size_t>(cdg::make_window(ranks, cap, H).bytes());
+namespace cdg {
+namespace {
+// Shapes the peer exchange takes: ranks <= 128, topk <= 32, H a multiple of 128, every slot
+// index of a window (ranks * tokens * topk) an int32, the header (E_local counts and the row
+// count) inside one row.
+bool p2p_shape_ok(int64_t ranks, int64_t tokens, int64_t topk, int64_t H) {
+  return ranks > 0 && ranks <= 128 && tokens >= 0 && topk > 0 && topk <= 32 && H > 0 && H % 128 == 0 &&
+         ranks * tokens * topk < (int64_t(1) << 31);
+}
+
+PeerStep make_step(const uint64_t* peers, void* window, int32_t me, int64_t ranks, int64_t tokens, int64_t topk,
+                   int64_t H) {
+  PeerStep ps;
+  ps.peers = peers;
+  ps.own = static_cast<uint8_t*>(window);
+  ps.win = make_window(ranks, tokens, topk, H);
+  ps.me = me;
+  return ps;
+}
+}  // namespace
+}  // namespace cdg
+
+extern "C" {
+
+size_t cdg_ep_window_bytes(int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H) {
+  if (!cdg::p2p_shape_ok(ranks, max_tokens, topk, H)) return 0;
+  return static_cast<size_t>(cdg::make_window(ranks, max_tokens, topk, H).bytes());
 }
 
 int cdg_ep_window_create(size_t bytes, void** window, void* ipc_handle) {
@@ -945,84 +1202,80 @@ int cdg_ep_window_status(const void* window, cdg_stream_t stream) {
 }
 
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
-                        int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
+                        int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t max_tokens,
                         const uint64_t* peers, void* window, int32_t me, int32_t* scratch, int32_t* send_index,
                         int32_t scale_fmt, cdg_stream_t stream) {
-  if (T < 0 || topk <= 0 || E <= 0 || ranks <= 0 || ranks > 128 || E % ranks || H <= 0 || H % 128 || cap < 0 ||
-      E / ranks > cdg::kFixedMaxExperts || !scratch || !peers || !window || me < 0 || me >= ranks)
+  if (!cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || T < 0 || T > max_tokens || E <= 0 || E % ranks ||
+      E / ranks > cdg::kFixedMaxExperts || !scratch || !peers || !window || me < 0 || me >= ranks ||
+      (T > 0 && (!x || !topk_ids || !send_index)))
     return CDG_ERR_INVALID_ARGUMENT;
   if (scale_fmt != CDG_SCALE_FP32 && scale_fmt != CDG_SCALE_POW2) return CDG_ERR_INVALID_ARGUMENT;
-  if (4 * (E / ranks) > cdg::packed_row_bytes(H)) return CDG_ERR_INVALID_ARGUMENT;
+  const cdg::Window win = cdg::make_window(ranks, max_tokens, topk, H);
+  if (4 * (E / ranks + 1) > win.rb) return CDG_ERR_INVALID_ARGUMENT;  // the header fits a row
   if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
   if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4) return CDG_ERR_ALIGNMENT;
+  const size_t smem = static_cast<size_t>(cdg::kP2pWarps * cdg::row_stage_bytes(H));
+  if (smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(cdg::ep_dispatch_p2p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem)) != cudaSuccess)
+    return CDG_ERR_CUDA;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(scratch, 0, cdg_ep_fixed_scratch_ints(ranks, E) * sizeof(int32_t), st) != cudaSuccess)
     return CDG_ERR_CUDA;
-  cdg::PeerStep ps;
-  ps.peers = peers;
-  ps.own = static_cast<uint8_t*>(window);
-  ps.win = cdg::make_window(ranks, cap, H);
-  ps.me = me;
-  const unsigned grid = T * topk > 0 ? static_cast<unsigned>(T * topk) : 1u;
-  cdg::ep_quant_pack_fixed_kernel<<<grid, 128, 0, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E,
-                                                        E / ranks, ranks, H, cap, scratch, nullptr, send_index, scale_fmt,
-                                                        ps);
+  const cdg::PeerStep ps = cdg::make_step(peers, window, me, ranks, max_tokens, topk, H);
+  const unsigned grid = T > 0 ? static_cast<unsigned>((T + cdg::kP2pWarps - 1) / cdg::kP2pWarps) : 1u;
+  cdg::ep_dispatch_p2p_kernel<<<grid, cdg::kP2pWarps * 32, smem, st>>>(x, x_dtype, x_stride, topk_ids, ids_dtype, T, E,
+                                                                       E / ranks, scratch, send_index, scale_fmt, ps);
   return cdg::launched();
 }
 
-int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t* fill,
-                       uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, int64_t E_local,
+                       int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* ret_slot,
                        cdg_stream_t stream) {
-  if (!window || ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || E_local <= 0 ||
-      E_local > cdg::kFixedMaxExperts || M_pad < ranks * cap + 127 * E_local)
+  if (!window || !cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || E_local <= 0 ||
+      E_local > cdg::kFixedMaxExperts || M_pad < ranks * max_tokens * topk + 127 * E_local || !fill || !A || !SA ||
+      !m_indices || !ret_slot)
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  cdg::PeerStep ps;
-  ps.own = static_cast<uint8_t*>(window);
-  ps.win = cdg::make_window(ranks, cap, H);
-  const int64_t R = ranks * (cap + 1);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
-  cdg::ep_permute_fixed_kernel<<<grid, 256, 0, st>>>(nullptr, ranks, cap, H, E_local, fill, A, SA, m_indices, perm_pos,
-                                                     ps);
+  if (cudaMemsetAsync(ret_slot, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::PeerStep ps = cdg::make_step(nullptr, window, 0, ranks, max_tokens, topk, H);
+  const int64_t R = ranks * max_tokens;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, 1184)));
+  cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, A, SA, m_indices, ret_slot, ps);
   return cdg::launched();
 }
 
-int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* perm_pos, int64_t ranks,
-                      int64_t cap, int64_t H, const uint64_t* peers, void* window, int32_t me, int32_t* scratch,
-                      cdg_stream_t stream) {
-  if (ranks <= 0 || ranks > 128 || cap < 0 || H <= 0 || H % 128 || !peers || !window || !scratch || me < 0 ||
-      me >= ranks || y_rows < 0 || y_stride < H)
+int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* ret_slot, int64_t M_pad,
+                      int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, const uint64_t* peers, void* window,
+                      int32_t me, int32_t* scratch, cdg_stream_t stream) {
+  if (!cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || !peers || !window || !scratch || !ret_slot || me < 0 ||
+      me >= ranks || y_rows < 0 || M_pad < 0 || y_stride < H || (y_rows > 0 && !Y))
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(Y) % 16 || y_stride % 8) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  cdg::PeerStep ps;
-  ps.peers = peers;
-  ps.own = static_cast<uint8_t*>(window);
-  ps.win = cdg::make_window(ranks, cap, H);
-  ps.me = me;
-  const int64_t R = ranks * (cap + 1);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((R + 7) / 8, 1184));
-  cdg::ep_return_p2p_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(Y), y_stride, y_rows, perm_pos,
-                                                  ranks, cap, H, ps, scratch);
+  const cdg::PeerStep ps = cdg::make_step(peers, window, me, ranks, max_tokens, topk, H);
+  const int64_t rows = std::min(M_pad, y_rows);
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, 1184)));
+  cdg::ep_return_p2p_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(Y), y_stride, rows, ret_slot, ps,
+                                                  scratch);
   return cdg::launched();
 }
 
 int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
-                       int64_t H, int64_t ranks, int64_t cap, int32_t* scratch, void* y, cdg_stream_t stream) {
-  if (!window || !scratch || T < 0 || topk <= 0 || H <= 0 || H % 128 || ranks <= 0 || ranks > 128 || cap < 0)
+                       int64_t H, int64_t ranks, int64_t max_tokens, int32_t* scratch, void* y, cdg_stream_t stream) {
+  if (!window || !scratch || !cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || T < 0 || T > max_tokens ||
+      topk > cdg::kCombineMaxTopk || (T > 0 && (!send_index || !topk_w || !y)))
     return CDG_ERR_INVALID_ARGUMENT;
+  if (H % 8 || reinterpret_cast<uintptr_t>(y) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  cdg::PeerStep ps;
-  ps.own = static_cast<uint8_t*>(window);
-  ps.win = cdg::make_window(ranks, cap, H);
+  const cdg::PeerStep ps = cdg::make_step(nullptr, window, 0, ranks, max_tokens, topk, H);
   const unsigned grid = T > 0 ? static_cast<unsigned>(T) : 1u;
-  if (topk > cdg::kCombineMaxTopk) return CDG_ERR_INVALID_ARGUMENT;
   cdg::ep_combine_kernel<true><<<grid, 256, 0, st>>>(nullptr, H, nullptr, send_index, topk_w, T, topk, H,
                                                      static_cast<__nv_bfloat16*>(y), ps, scratch);
   return cdg::launched();

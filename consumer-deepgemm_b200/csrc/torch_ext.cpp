@@ -364,8 +364,8 @@ uint64_t ep_window_open(const py::bytes& handle) {
   return reinterpret_cast<uint64_t>(w);
 }
 
-torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, int64_t E, int64_t ranks, int64_t cap,
-                              const torch::Tensor& peers, uint64_t window, int64_t me, bool ue8m0) {
+torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, int64_t E, int64_t ranks,
+                              int64_t max_tokens, const torch::Tensor& peers, uint64_t window, int64_t me, bool ue8m0) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
   TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
               "topk ids must be contiguous [T, topk]");
@@ -377,7 +377,8 @@ torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, 
   auto scratch = torch::empty({std::max<int64_t>(cdg_ep_fixed_scratch_ints(ranks, E), 1)},
                               ids.options().dtype(torch::kInt32));
   check_status(cdg_ep_dispatch_p2p(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(), dtype_code(ids), T, topk,
-                                   E, ranks, H, cap, reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
+                                   E, ranks, H, max_tokens,
+                                   reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
                                    reinterpret_cast<void*>(window), static_cast<int32_t>(me),
                                    scratch.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(),
                                    ue8m0 ? CDG_SCALE_POW2 : CDG_SCALE_FP32, cur_stream(x)),
@@ -385,30 +386,32 @@ torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, 
   return send_index;
 }
 
-std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local,
-                                          int64_t M_pad, const torch::Tensor& like) {
+std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H,
+                                          int64_t E_local, int64_t M_pad, const torch::Tensor& like) {
   const c10::cuda::CUDAGuard guard(like.device());
   auto i32 = like.options().dtype(torch::kInt32);
   auto A = torch::empty({M_pad, H}, like.options().dtype(torch::kFloat8_e4m3fn));
   auto SA = torch::empty({M_pad, H / 128}, like.options().dtype(torch::kFloat32));
   auto mi = torch::empty({M_pad}, i32);
-  auto pos = torch::empty({ranks * (cap + 1)}, i32);
+  auto ret_slot = torch::empty({M_pad}, i32);
   auto fill = torch::empty({E_local}, i32);
-  check_status(cdg_ep_permute_p2p(reinterpret_cast<void*>(window), ranks, cap, H, E_local, fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()),
-                                  SA.data_ptr<float>(), mi.data_ptr<int32_t>(), M_pad, pos.data_ptr<int32_t>(),
+  check_status(cdg_ep_permute_p2p(reinterpret_cast<void*>(window), ranks, max_tokens, topk, H, E_local,
+                                  fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()),
+                                  SA.data_ptr<float>(), mi.data_ptr<int32_t>(), M_pad, ret_slot.data_ptr<int32_t>(),
                                   cur_stream(like)),
                "ep_permute_p2p");
-  return {A, SA, mi, pos};
+  return {A, SA, mi, ret_slot};
 }
 
-void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& perm_pos, int64_t ranks, int64_t cap,
-                   const torch::Tensor& peers, uint64_t window, int64_t me) {
+void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& ret_slot, int64_t ranks, int64_t max_tokens,
+                   int64_t topk, const torch::Tensor& peers, uint64_t window, int64_t me) {
   TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
-  TORCH_CHECK(perm_pos.numel() == ranks * (cap + 1), "perm_pos: one entry per received slot");
+  TORCH_CHECK(ret_slot.is_cuda() && ret_slot.scalar_type() == torch::kInt32 && ret_slot.is_contiguous(),
+              "ret_slot: int32, one entry per GEMM row");
   const c10::cuda::CUDAGuard guard(Y.device());
-  auto scratch = torch::empty({1}, perm_pos.options());
-  check_status(cdg_ep_return_p2p(Y.data_ptr(), Y.stride(0), Y.size(0), perm_pos.data_ptr<int32_t>(), ranks, cap,
-                                 Y.size(1),
+  auto scratch = torch::empty({1}, ret_slot.options());
+  check_status(cdg_ep_return_p2p(Y.data_ptr(), Y.stride(0), Y.size(0), ret_slot.data_ptr<int32_t>(), ret_slot.numel(),
+                                 ranks, max_tokens, topk, Y.size(1),
                                  reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>()),
                                  reinterpret_cast<void*>(window), static_cast<int32_t>(me), scratch.data_ptr<int32_t>(),
                                  cur_stream(Y)),
@@ -416,7 +419,7 @@ void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& perm_pos, int64_
 }
 
 torch::Tensor ep_combine_p2p(uint64_t window, const torch::Tensor& send_index, const torch::Tensor& topk_w,
-                             int64_t ranks, int64_t cap, int64_t H) {
+                             int64_t ranks, int64_t max_tokens, int64_t H) {
   TORCH_CHECK(topk_w.is_cuda() && topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() &&
                   topk_w.dim() == 2 && send_index.numel() == topk_w.numel(),
               "topk weights: FP32 [T, topk] matching send_index");
@@ -425,7 +428,7 @@ torch::Tensor ep_combine_p2p(uint64_t window, const torch::Tensor& send_index, c
   auto y = torch::empty({T, H}, topk_w.options().dtype(torch::kBFloat16));
   auto scratch = torch::empty({1}, send_index.options());
   check_status(cdg_ep_combine_p2p(reinterpret_cast<void*>(window), send_index.data_ptr<int32_t>(),
-                                  topk_w.data_ptr<float>(), T, topk, H, ranks, cap, scratch.data_ptr<int32_t>(),
+                                  topk_w.data_ptr<float>(), T, topk, H, ranks, max_tokens, scratch.data_ptr<int32_t>(),
                                   y.data_ptr(), cur_stream(topk_w)),
                "ep_combine_p2p");
   return y;
@@ -503,8 +506,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_permute_fixed", &ep_permute_fixed, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),
         py::arg("ranks"), py::arg("cap"), py::arg("m_pad"));
   m.def("mega_moe_transform_rows", &mega_moe_transform_rows, py::arg("t"), py::arg("kind"));
-  m.def("ep_window_bytes", [](int64_t ranks, int64_t cap, int64_t H) { return cdg_ep_window_bytes(ranks, cap, H); },
-        py::arg("ranks"), py::arg("cap"), py::arg("hidden"));
+  m.def(
+      "ep_window_bytes",
+      [](int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H) {
+        return cdg_ep_window_bytes(ranks, max_tokens, topk, H);
+      },
+      py::arg("ranks"), py::arg("max_tokens"), py::arg("topk"), py::arg("hidden"));
   m.def("ep_window_create", &ep_window_create, py::arg("bytes"));
   m.def("ep_window_open", &ep_window_open, py::arg("handle"));
   m.def(
@@ -521,14 +528,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("window"));
   m.def("ep_dispatch_p2p", &ep_dispatch_p2p, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
-        py::arg("ranks"), py::arg("cap"), py::arg("peers"), py::arg("window"), py::arg("me"),
+        py::arg("ranks"), py::arg("max_tokens"), py::arg("peers"), py::arg("window"), py::arg("me"),
         py::arg("ue8m0") = false);
-  m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("cap"), py::arg("hidden"),
-        py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
-  m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("perm_pos"), py::arg("ranks"), py::arg("cap"),
-        py::arg("peers"), py::arg("window"), py::arg("me"));
+  m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("max_tokens"),
+        py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
+  m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("ret_slot"), py::arg("ranks"), py::arg("max_tokens"),
+        py::arg("topk"), py::arg("peers"), py::arg("window"), py::arg("me"));
   m.def("ep_combine_p2p", &ep_combine_p2p, py::arg("window"), py::arg("send_index"), py::arg("topk_w"),
-        py::arg("ranks"), py::arg("cap"), py::arg("hidden"));
+        py::arg("ranks"), py::arg("max_tokens"), py::arg("hidden"));
   m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
   m.def(
       "ep_set_wait_timeout_ns",

@@ -18,7 +18,8 @@
  *   - Return values are cdg_status codes.  Input errors are detected on the host
  *     before anything is launched.  Errors seen on the device (a pipeline wait
  *     that timed out) are recorded in the workspace status word, readable with
- *     cdg_read_device_status().
+ *     cdg_read_device_status(), and in a per-device record of the library,
+ *     readable with cdg_device_status().
  */
 #ifndef CDG_B200_H_
 #define CDG_B200_H_
@@ -173,7 +174,8 @@ int cdg_read_device_status(const void* workspace, cdg_stream_t stream);
  * such wait's code in *where (may be NULL; 0 when none), and clears the record when `clear`
  * is nonzero.  A wait code holds the role (bits 28-31: 1 producer/empty, 2 issuer/tempty,
  * 3 issuer/full, 4 epilogue/tfull, 5 issuer/done, 6 scale copier, 7 scale producer,
- * 8 exchange dispatch flag, 9 exchange return flag, 15 TMEM allocation not at column 0),
+ * 8 exchange dispatch flag, 9 exchange return flag, 10 exchange rows not matching their
+ * header's counts (bit 2 of the status: such rows are dropped), 15 TMEM allocation not at column 0),
  * then the CTA rank, issuer or source rank, stage, phase and step.  Also covers the
  * no-allocation entry point, whose workspace is private.  No reference counterpart: the
  * reference reports device failures only as a launch result
@@ -346,43 +348,52 @@ int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t strid
  * through CUDA IPC: create it with cdg_ep_window_create, send the 64-byte handle to the
  * other ranks (any host channel), open theirs with cdg_ep_window_open, and pass the
  * ranks' window addresses as a device array `peers` (uint64 [ranks], this rank's own
- * window `window` at index `me`).  Each rank runs, once per exchange step and in this order:
- *   cdg_ep_dispatch_p2p   quantise + pack (as cdg_ep_quant_pack_fixed) straight into each
- *                         destination's window, then raise this rank's flag there;
- *   cdg_ep_permute_p2p    wait (bounded) for every source's flag, then permute (as
- *                         cdg_ep_permute_fixed) from the own window;
- *   cdg_ep_return_p2p     store each GEMM row straight into its source's window, raise flags;
- *   cdg_ep_combine_p2p    wait for every rank's rows, combine (as cdg_ep_combine), and advance
- *                         the window's step counter.
+ * window `window` at index `me`).  Windows are sized for at most `max_tokens` tokens per
+ * rank with `topk` slots each.  Each rank runs, once per exchange step and in this order:
+ *   cdg_ep_dispatch_p2p   quantise each token's row once (1x128 e4m3, scale_fmt recipe) and
+ *                         store it, with the token index and the local expert of each of its
+ *                         slots, into the window of every rank that owns one of its experts
+ *                         (one row per token and destination rank), then raise this rank's
+ *                         flag there; send_index[t*topk + j] = t*topk + j (-1: no expert);
+ *   cdg_ep_permute_p2p    wait (bounded) for every source's flag, then lay the received rows
+ *                         out per local expert (128-aligned groups, A / SA / m_indices as the
+ *                         grouped GEMM reads them; a row with several slots here is written
+ *                         to each slot's group); ret_slot[pos] says where GEMM row pos goes back;
+ *   cdg_ep_return_p2p     store each GEMM row straight into its source's window at the
+ *                         source's slot index, raise flags;
+ *   cdg_ep_combine_p2p    wait for every rank's rows, weighted top-k sum (as cdg_ep_combine),
+ *                         and advance the window's step counter.
  * The step number (flag value; the windows are double-buffered by its parity) lives in the
  * window, so the calls take no per-step argument and a whole step can be captured in a CUDA
  * graph; every rank must run the same number of steps.  Plain stores and loads over NVLink:
- * no multicast.  A wait that gives up after 2 s skips its CTA's work and sets the window's
- * status word (cdg_ep_window_status and cdg_device_status report it).  scratch: int32
- * [cdg_ep_fixed_scratch_ints(ranks, E)] for dispatch, int32 [1] for return and combine. */
-size_t cdg_ep_window_bytes(int64_t ranks, int64_t cap, int64_t H);
+ * no multicast.  A wait that gives up after its bound (2 s, cdg_ep_set_wait_timeout_ns)
+ * skips its CTA's work and sets the window's status word (cdg_ep_window_status and
+ * cdg_device_status report it).  scratch: int32 [cdg_ep_fixed_scratch_ints(ranks, E)] for
+ * dispatch, int32 [1] for return and combine.  Limits: ranks <= 128, topk <= 32, E / ranks <=
+ * 1024, H a multiple of 128, ranks * max_tokens * topk < 2^31; M_pad of the permute at least
+ * ranks * max_tokens * topk + 127 * E_local (the worst case). */
+size_t cdg_ep_window_bytes(int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H);
 int cdg_ep_window_create(size_t bytes, void** window, void* ipc_handle /* 64 bytes out */);
 int cdg_ep_window_open(const void* ipc_handle, void** window);
 int cdg_ep_window_close(void* window, int32_t opened);
 int cdg_ep_window_status(const void* window, cdg_stream_t stream);
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
-                        int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t cap,
+                        int64_t T, int64_t topk, int64_t E, int64_t ranks, int64_t H, int64_t max_tokens,
                         const uint64_t* peers, void* window, int32_t me, int32_t* scratch, int32_t* send_index,
                         int32_t scale_fmt, cdg_stream_t stream);
-int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t cap, int64_t H, int64_t E_local, int32_t* fill,
-                       uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* perm_pos,
+int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, int64_t E_local,
+                       int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* ret_slot,
                        cdg_stream_t stream);
-int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* perm_pos, int64_t ranks,
-                      int64_t cap, int64_t H, const uint64_t* peers, void* window, int32_t me, int32_t* scratch,
-                      cdg_stream_t stream);
+int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* ret_slot, int64_t M_pad,
+                      int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, const uint64_t* peers, void* window,
+                      int32_t me, int32_t* scratch, cdg_stream_t stream);
+int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
+                       int64_t H, int64_t ranks, int64_t max_tokens, int32_t* scratch, void* y, cdg_stream_t stream);
 /* Bound of the exchange's waits on other ranks' flags on the current device, in ns (0 = the
  * default 2 s; at most 60 s).  A wait that runs out sets the window's status word and the
- * record cdg_device_status() reads; the waiting step then places no rows (permute: every
- * slot's perm_pos is -1) or writes zero rows (combine), so nothing downstream reads memory
- * that was never written. */
+ * record cdg_device_status() reads; the waiting step then places no rows (permute) or writes
+ * zero rows (combine), so nothing downstream reads memory that was never written. */
 int cdg_ep_set_wait_timeout_ns(uint64_t ns);
-int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
-                       int64_t H, int64_t ranks, int64_t cap, int32_t* scratch, void* y, cdg_stream_t stream);
 
 /* out[i, :] = Y[perm_pos[i], :] (BF16 rows of length H); rows with perm_pos[i] = -1 are not written. */
 int cdg_ep_unpermute(const void* Y, int64_t y_stride, const int32_t* perm_pos, int64_t R, int64_t H, void* out,

@@ -308,8 +308,8 @@ def test_layer_stages_match_reference_at_gemm_tolerance(ue8m0):
 def test_peer_wait_runs_out_and_context_stays_usable():
     """Bounded waits on other ranks' flags, on one GPU: a window whose flags nobody raises.
 
-    With the wait limit at 10 ms, the permute step gives up (it places no row and every
-    slot's perm_pos is -1), the combine step gives up (its output rows are zeros), the
+    With the wait limit at 10 ms, the permute step gives up (it places no row: every
+    m_indices and ret_slot entry stays -1), the combine step gives up (its output rows are zeros), the
     window's status word and the library's device record report CDG_ERR_DEVICE_TIMEOUT with
     the permute's wait code, and the context keeps working: a GEMM afterwards matches the
     reference.  Nothing here faults or hangs: every wait has its limit."""
@@ -321,20 +321,20 @@ def test_peer_wait_runs_out_and_context_stays_usable():
     ranks, T, topk, H, e_loc = 2, 16, 2, 512, 4
     cap = T * topk
     cdg.read_device_status(True)  # start from a clean record
-    own, _ = C.ep_window_create(C.ep_window_bytes(ranks, cap, H))
+    own, _ = C.ep_window_create(C.ep_window_bytes(ranks, T, topk, H))
     try:
         C.ep_set_wait_timeout_ns(10_000_000)
         like = torch.zeros(1, device=DEV)
         m_pad = (ranks * cap + 127 * e_loc + 127) // 128 * 128
-        a, sa, mi, pos = C.ep_permute_p2p(own, ranks, cap, H, e_loc, m_pad, like)
+        a, sa, mi, ret_slot = C.ep_permute_p2p(own, ranks, T, topk, H, e_loc, m_pad, like)
         send_index = torch.arange(T * topk, dtype=torch.int32, device=DEV)
         tw = torch.full((T, topk), 0.5, device=DEV)
-        y = C.ep_combine_p2p(own, send_index, tw, ranks, cap, H)
+        y = C.ep_combine_p2p(own, send_index, tw, ranks, T, H)
         torch.cuda.synchronize()
         assert C.ep_window_status(own) == 6
         st, where = cdg.read_device_status(True)
         assert st == 6 and (where >> 28) == 8, (st, hex(where))
-        assert bool((pos == -1).all()) and bool((mi == -1).all())
+        assert bool((ret_slot == -1).all()) and bool((mi == -1).all())
         assert bool((y.float() == 0).all())
         assert cdg.read_device_status(True) == (0, 0)
     finally:
@@ -369,3 +369,62 @@ def test_layer_expert_parallel_two_gpus():
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     for mode in ("split_sizes", "fixed_capacity", "peer_memory", "peer_memory_ue8m0"):
         assert f"EP_OK {mode}" in r.stdout, r.stdout[-3000:]
+
+
+@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
+def test_peer_exchange_two_ranks_on_one_gpu(ue8m0):
+    """The peer-memory exchange kernels for two ranks whose windows both live on this GPU.
+
+    Each step runs rank 0's and rank 1's calls in order on one stream (dispatch, dispatch,
+    permute, permute, GEMMs, return, return, combine, combine), so every flag a wait looks
+    for was raised by an earlier launch: no kernel waits on one running beside it.  Three
+    steps (both window parities and a reuse); the gathered outputs equal the one-GPU layer's
+    (per-row relative L2 <= 1e-3) and no wait gave up."""
+    import consumer_deep_gemm as cdg
+    from consumer_deep_gemm.layout import transform_sf_into_required_layout
+    from consumer_deep_gemm.moe import MoELayer, NativeOps
+    from metrics import errors
+
+    C = _ext()
+    ranks, tpr, E, H, inter, topk = 2, 96, 8, 512, 256, 4
+    x, ids, w, w1, w1s, w2, w2s = (t.to(DEV) for t in make_layer_inputs(ranks * tpr, E, H, inter, topk, seed=3))
+    ids[5, 1] = -1  # a slot routed nowhere
+    y_ref = MoELayer(w1, w1s, w2, w2s, num_experts=E, ue8m0=ue8m0)(x, ids, w)
+    e_loc = E // ranks
+    cdg.read_device_status(True)
+    own = [C.ep_window_create(C.ep_window_bytes(ranks, tpr, topk, H))[0] for _ in range(ranks)]
+    peers = torch.tensor(own, dtype=torch.int64, device=DEV)
+    ops = NativeOps()
+    shard = [(w1[r * e_loc:(r + 1) * e_loc].contiguous(), transform_sf_into_required_layout(w1s[r * e_loc:(r + 1) * e_loc]),
+              w2[r * e_loc:(r + 1) * e_loc].contiguous(), transform_sf_into_required_layout(w2s[r * e_loc:(r + 1) * e_loc]))
+             for r in range(ranks)]
+    tok = [slice(r * tpr, (r + 1) * tpr) for r in range(ranks)]
+    m_pad = (ranks * tpr * topk + 127 * e_loc + 127) // 128 * 128
+    try:
+        for step in range(3):
+            si = [C.ep_dispatch_p2p(x[tok[r]], ids[tok[r]].contiguous(), E, ranks, tpr, peers, own[r], r, ue8m0)
+                  for r in range(ranks)]
+            placed = [C.ep_permute_p2p(own[r], ranks, tpr, topk, H, e_loc, m_pad, x) for r in range(ranks)]
+            outs = []
+            for r in range(ranks):
+                a, sa, mi, _ = placed[r]
+                b1, s1, b2, s2 = shard[r]
+                h = ops.gemm(a, sa, b1, s1, mi, skip_ungrouped=True)
+                aq, asc = ops.act(h, mi, ue8m0)
+                outs.append(ops.gemm(aq, asc, b2, s2, mi, skip_ungrouped=True))
+            for r in range(ranks):
+                C.ep_return_p2p(outs[r], placed[r][3], ranks, tpr, topk, peers, own[r], r)
+            y = torch.cat([C.ep_combine_p2p(own[r], si[r], w[tok[r]].float().contiguous(), ranks, tpr, H)
+                           for r in range(ranks)])
+            torch.cuda.synchronize()
+            nw, rl2 = errors(y, y_ref)
+            assert nw <= 1e-3 and rl2 <= 1e-3, (step, nw, rl2)
+            # every slot of a routed token was placed exactly once over the two ranks
+            n_rows = sum(int((p[2] >= 0).sum()) for p in placed)
+            assert n_rows == int((ids >= 0).sum()), (n_rows, int((ids >= 0).sum()))
+        for r in range(ranks):
+            assert C.ep_window_status(own[r]) == 0
+        assert cdg.read_device_status(True) == (0, 0)
+    finally:
+        for p in own:
+            C.ep_window_close(p, False)
