@@ -95,7 +95,27 @@ def _normalize(a, b, d, m_indices):
         raise ValueError(f"b scale must be [G, N, K/32], got {tuple(bs.shape)}")
     if m_indices is None and bt.shape[0] != 1:
         raise ValueError("m_indices is required when b has multiple groups")
+    if bs.dtype != torch.int32 and bt.shape[1] % 128 == 0 and k % 128 == 0 and bt.shape[0] * bt.shape[1] >= 65536:
+        _warn_row_major_scales(bs)
     return x, sa, bt, bs, d, m_indices
+
+
+_warned_row_major = False
+
+
+def _warn_row_major_scales(bs):
+    """Once per process: weight scales that arrive row-major are reordered into tensor-core atoms
+    inside every call (a read of all experts' scales, ~0.5 ms at E=256, N=K=4096), where
+    ``transform_sf_into_required_layout`` does it once at weight load."""
+    global _warned_row_major
+    if _warned_row_major:
+        return
+    _warned_row_major = True
+    import warnings
+
+    warnings.warn("consumer_deep_gemm: weight scales passed row-major (%s); every call reorders them for the "
+                  "tensor cores. Pass transform_sf_into_required_layout(scale) (done once at weight load) "
+                  "instead." % str(bs.dtype).replace("torch.", ""), RuntimeWarning, stacklevel=4)
 
 
 def _check_recipes(kwargs):
@@ -111,7 +131,8 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs) -> N
     """M-grouped FP8 x FP4 GEMM for the MoE contiguous layout (see module docstring)."""
     _check_recipes(kwargs)
     x, sa, bt, bs, d, ids = _normalize(a, b, d, m_indices)
-    flags = (1 if kwargs.get("_force_exact_path") else 0) | (4 if kwargs.get("_skip_ungrouped_rows") else 0)
+    flags = ((1 if kwargs.get("_force_exact_path") else 0) | (4 if kwargs.get("_skip_ungrouped_rows") else 0) |
+             (8 if kwargs.get("_round_weight_scales") else 0))
     native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags)
     if _CHECK_STATUS:
         native.check_device_status()

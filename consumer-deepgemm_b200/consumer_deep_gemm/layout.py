@@ -7,8 +7,11 @@ data pointer (csrc/cutlass_mxfp8_mxfp4_probe.cu:349-385).  Here it runs the
 sm_100a kernel ``cdg_sf_atom_kernel`` over all experts in one launch and returns
 an int32 tensor ``[G, N/128, K/128, 128]`` of 512-byte 128x4 atoms (the
 128x4 reorder of gemm.py:76-116, applied per expert), which the GEMM recognises
-by its dtype and shape.  Activation scales (``is_sfa=True``) stay FP32 and are
-returned unchanged: the GEMM applies them exactly.
+by its dtype and shape.  Float weight scales that are all powers of two (an MXFP4
+checkpoint's scales stored as float) become the same atoms, exactly; other float
+scales are returned unchanged (the GEMM then keeps them exact on its SIMT path).
+Activation scales (``is_sfa=True``) stay FP32 and are returned unchanged: the GEMM
+applies them exactly.
 """
 
 from __future__ import annotations
@@ -31,6 +34,11 @@ def transform_sf_into_required_layout(sf: torch.Tensor, mn=None, k=None, recipe=
         return sf
     if sf.dtype == torch.float8_e8m0fnu:
         sf = sf.view(torch.uint8)
+    if sf.dtype in (torch.float32, torch.float16, torch.bfloat16):
+        codes = _exact_ue8m0(sf)
+        if codes is None:
+            return sf
+        sf = codes
     if sf.dtype != torch.uint8:
         return sf
     if sf.dim() == 2:
@@ -41,6 +49,19 @@ def transform_sf_into_required_layout(sf: torch.Tensor, mn=None, k=None, recipe=
     if n % 128 or kb % 4:
         return sf  # outside the tensor-core envelope: the exact SIMT path reads row-major scales
     return native.require().transform_sf_atoms(sf)
+
+
+def _exact_ue8m0(sf: torch.Tensor):
+    """UE8M0 bytes of float scales that are all powers of two 2^(c-127), c in [0, 254]
+    (c = the FP32 exponent field; 2^-127 is code 0), else None.  Reads one bool back to the
+    host: a weight-load-time synchronisation."""
+    bits = sf.float().contiguous().view(torch.int32)
+    ex = (bits >> 23) & 0xFF
+    tiny = bits == 0x00400000
+    exact = ((bits & 0x807FFFFF) == 0) & (ex >= 1) & (ex <= 254) | tiny
+    if not bool(exact.all()):
+        return None
+    return torch.where(tiny, torch.zeros_like(ex), ex).to(torch.uint8)
 
 
 def get_mn_major_tma_aligned_tensor(x: torch.Tensor) -> torch.Tensor:

@@ -163,7 +163,12 @@ int validate(const cdg_gemm_args* g) {
 // True when the tensor-core kernel can run these (validated) arguments.
 bool fast_path(const cdg_gemm_args* g) {
   if (g->flags & CDG_FLAG_FORCE_GENERIC) return false;
-  if (g->a_dtype != CDG_DTYPE_E4M3 || g->sfb_dtype != CDG_DTYPE_UE8M0 || g->d_dtype != CDG_DTYPE_BF16) return false;
+  // float weight scales go through the tensor cores as UE8M0 codes: exactly when they are powers of
+  // two (decided on the device; otherwise the exact SIMT kernel takes every block), or rounded
+  // with CDG_FLAG_ROUND_SFB
+  const bool sfb_ok = g->sfb_dtype == CDG_DTYPE_UE8M0 || (g->sfb_dtype == CDG_DTYPE_F32 &&
+                                                          g->sfb_layout == CDG_SF_ROW_MAJOR);
+  if (g->a_dtype != CDG_DTYPE_E4M3 || !sfb_ok || g->d_dtype != CDG_DTYPE_BF16) return false;
   const bool packed = g->sa_dtype == CDG_DTYPE_UE8M0_X4;
   if (g->K % 128 || g->N % 128 || (!packed && g->sa_cols != g->K / 128)) return false;
   if (g->a_row_stride % 16 || !aligned(g->a, 16)) return false;
@@ -185,6 +190,17 @@ WorkspaceLayout layout_for(const cdg_gemm_args* g) {
   return WorkspaceLayout::make(g->M, tile_map(g).tiles(), g->K, g->N, g->E, fast,
                                g->index_form == CDG_INDEX_PSUM || g->index_form == CDG_INDEX_MASKED,
                                fast && sfw_needs_transform(g));
+}
+
+int launch_sf_atoms_f32(const float* sf, int64_t se, int64_t sn, int64_t E, int64_t N, int64_t KB, uint32_t* out,
+                        int* inexact, cudaStream_t stream, int sm_count) {
+  const int64_t words = E * ((N + 127) / 128) * ((KB + 3) / 4) * 128;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((words + threads - 1) / threads, int64_t(sm_count) * 32);
+  if (blocks <= 0) return CDG_OK;
+  cdg_sf_atom_f32_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+      sf, se, sn, out, static_cast<int>(E), static_cast<int>(N), static_cast<int>(KB), inexact);
+  return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA;
 }
 
 int launch_sf_atoms(const uint8_t* sf, int64_t se, int64_t sn, int64_t E, int64_t N, int64_t KB, uint32_t* out,
@@ -413,10 +429,15 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
 
   // ---------------------------------------------------------------- tensor-core path
   const uint32_t* sfw = static_cast<const uint32_t*>(g->sfb);
+  const bool float_sfb = g->sfb_dtype == CDG_DTYPE_F32;
   if (sfw_needs_transform(g)) {
     uint32_t* out = reinterpret_cast<uint32_t*>(ws + wl.sfw_atoms);
-    st = launch_sf_atoms(static_cast<const uint8_t*>(g->sfb), g->sfb_stride_e, g->sfb_stride_n, g->E, g->N, g->K / 32,
-                         out, stream, di.sm_count);
+    if (float_sfb)
+      st = launch_sf_atoms_f32(static_cast<const float*>(g->sfb), g->sfb_stride_e, g->sfb_stride_n, g->E, g->N,
+                               g->K / 32, out, ctrl + kCtrlSfInexact, stream, di.sm_count);
+    else
+      st = launch_sf_atoms(static_cast<const uint8_t*>(g->sfb), g->sfb_stride_e, g->sfb_stride_n, g->E, g->N,
+                           g->K / 32, out, stream, di.sm_count);
     if (st != CDG_OK) return st;
     sfw = out;
   }
@@ -449,6 +470,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.tok_code = tok_code;
   pa.direct_tiles = reinterpret_cast<int4*>(ws + wl.direct_tiles);
   pa.pair_wide = pair_path ? 1 : 0;
+  pa.sf_inexact = float_sfb && !(g->flags & CDG_FLAG_ROUND_SFB) ? ctrl + kCtrlSfInexact : nullptr;
   const dim3 prep_grid(static_cast<unsigned>(nblk), static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
   if (ids_dtype == CDG_DTYPE_I64)
     cdg_prep_kernel<int64_t><<<prep_grid, 256, 0, stream>>>(pa);

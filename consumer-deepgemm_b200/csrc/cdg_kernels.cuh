@@ -54,6 +54,66 @@ __global__ void cdg_sf_atom_kernel(const uint8_t* __restrict__ src, int64_t src_
   }
 }
 
+// UE8M0 code of a float weight scale.  A positive power of two 2^(c-127), c in [0, 254], is
+// exact (*exact = true): c is its FP32 exponent field (2^-127, a subnormal, is code 0).  Any
+// other value gets the reference's rounding, clamp(round(log2(s)) + 127, 0, 255) with s
+// clamped below at the smallest normal float (consumer_deep_gemm/gemm.py:62-73): for a normal
+// s = m * 2^e, m in [1, 2), round(log2(s)) is e + 1 when m >= sqrt(2) (m * m >= 2, exact in
+// double), else e.  NaN gets 255.
+__device__ __forceinline__ uint32_t float_scale_code(float s, bool* exact) {
+  const uint32_t bits = __float_as_uint(s);
+  const uint32_t ex = (bits >> 23) & 0xFFu, man = bits & 0x7FFFFFu;
+  if (!(bits >> 31) && man == 0 && ex >= 1 && ex <= 254) {
+    *exact = true;
+    return ex;
+  }
+  *exact = false;
+  if (bits == 0x00400000u) {  // 2^-127
+    *exact = true;
+    return 0;
+  }
+  if (s != s) return 255;
+  if (!(s >= 1.17549435e-38f)) return 1;  // zero, negative or subnormal: log2 of the smallest normal
+  if (ex == 255) return 255;              // +inf
+  const double m = 1.0 + static_cast<double>(man) * (1.0 / 8388608.0);
+  const int r = static_cast<int>(ex) - 127 + (m * m >= 2.0 ? 1 : 0);
+  return static_cast<uint32_t>(min(max(r + 127, 0), 255));
+}
+
+// Float weight scales [E, N, KB32] -> the same atoms as cdg_sf_atom_kernel, each byte
+// float_scale_code(s); sets *inexact when any scale of the tensor is not a power of two.
+__global__ void cdg_sf_atom_f32_kernel(const float* __restrict__ src, int64_t src_stride_e, int64_t src_stride_n,
+                                       uint32_t* __restrict__ dst, int E, int N, int KB32, int* inexact) {
+  const int n_tiles = (N + 127) / 128;
+  const int k_tiles = (KB32 + 3) / 4;
+  const int64_t words_per_e = static_cast<int64_t>(n_tiles) * k_tiles * 128;
+  const int64_t total = words_per_e * E;
+  bool all_exact = true;
+  for (int64_t w = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; w < total;
+       w += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = static_cast<int>(w / words_per_e);
+    const int64_t rem = w - e * words_per_e;
+    const int atom = static_cast<int>(rem >> 7);
+    const int j = static_cast<int>(rem & 127);
+    const int mt = atom / k_tiles, kt = atom - mt * k_tiles;
+    const int row = mt * 128 + (j & 3) * 32 + (j >> 2);
+    uint32_t v = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int col = kt * 4 + b;
+      uint32_t byte = 127u;
+      if (row < N && col < KB32) {
+        bool ex = true;
+        byte = float_scale_code(src[e * src_stride_e + row * src_stride_n + col], &ex);
+        all_exact = all_exact && ex;
+      }
+      v |= byte << (8 * b);
+    }
+    dst[w] = v;
+  }
+  if (!all_exact) atomicOr(inexact, 1);
+}
+
 // =====================================================================================
 // psum form: m_indices[g] is the cumulative end row of group g (group g owns rows
 // [end[g-1], end[g]) with end[-1] = 0).  Later groups win where ranges overlap, as
@@ -126,6 +186,8 @@ struct PrepArgs {
   int4* plane_tiles;       // [2*nblk] tiles of cdg_gemm_planes_kernel (pair_wide only):
                            // {first plane row, rows, expert, 1 on the last tile of a run}
   int4* direct_tiles;      // [nblk] tiles of cdg_gemm_direct_kernel, the same form
+  const int* sf_inexact;   // float weight scales: set when one is not a power of two, and the
+                           // exact SIMT kernel then takes every block (nullptr: not consulted)
 };
 
 // 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
@@ -233,6 +295,12 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     if (cls != kClassWide && p.pair_wide && row0 > 0 &&
         load_id(p.ids, sizeof(IdT) == 8, row0 - 1) == static_cast<int64_t>(expert))
       cls = kClassWide;
+    // float weight scales that are not all powers of two: the tensor cores' UE8M0 scale
+    // factors cannot hold them, the exact SIMT kernel takes the block
+    if (p.sf_inexact && __ldcg(p.sf_inexact)) {
+      cls = kClassIrregular;
+      expert = -2;
+    }
   }
 
   if (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide) {

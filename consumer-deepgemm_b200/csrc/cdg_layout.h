@@ -37,6 +37,7 @@ enum : int {
   kCtrlPlaneTiles = 7,  // number of tiles in the planes kernel's tile list
   kCtrlStatus = 8,  // device status bits (kStatus*); kCtrlStatus + 1: code of the first wait that gave up
   kCtrlDirectTiles = 10,  // number of tiles in the direct kernel's tile list
+  kCtrlSfInexact = 11,    // set when a float weight scale of the call is not a power of two
   kCtrlWords = 64,
 };
 

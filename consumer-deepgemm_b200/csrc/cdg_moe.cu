@@ -220,53 +220,86 @@ __global__ void quant_rows_kernel(const void* x, int x_dtype, int64_t x_stride, 
   quant_block_warp(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
 }
 
-// Quantise and lay out for the grouped GEMM in one pass, when there is no exchange (one rank):
-// one CTA per token reads its row once, quantises each 128-column block (one warp per block)
-// and writes the codes and scale to the contiguous-layout row of every routed slot (row
-// expert_off[e] + a per-expert counter, e = topk_ids[t, j] in [0, E)).  perm_pos[t*topk + j]
-// is that row and send_index[t*topk + j] the slot itself (-1 for skipped slots), the form
-// the combine step reads.  fill: [E] counters, zeroed by the host.
-__global__ void __launch_bounds__(128) ep_quant_dispatch_local_kernel(
-    const void* x, int x_dtype, int64_t x_stride, const void* ids, int ids_dtype, int64_t topk, int64_t E,
+// Four values of a 128-column block for lane `lane` (BF16 or FP32 row, 16-byte aligned).
+__device__ __forceinline__ void load_block4(const void* x, int x_dtype, int64_t base, float (&v)[4]) {
+  if (x_dtype == CDG_DTYPE_BF16) {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + base));
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+  } else {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + base));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  }
+}
+
+// One warp quantises row x[row_off .. row_off + H) (quant_block_values: the
+// per_block_cast_to_fp8 or power-of-two recipe, bit for bit) into codes[H] and scales[H/128]
+// in shared memory; the loads of eight 128-column blocks are issued before the first is used.
+__device__ __forceinline__ void warp_quant_row(const void* x, int x_dtype, int64_t row_off, int64_t H, uint8_t* codes,
+                                               float* scales, int lane, int pow2) {
+  const int64_t nkb = H / 128;
+  for (int64_t kb0 = 0; kb0 < nkb; kb0 += 8) {
+    float v[8][4];
+#pragma unroll
+    for (int b = 0; b < 8; ++b)
+      if (kb0 + b < nkb) load_block4(x, x_dtype, row_off + (kb0 + b) * 128 + lane * 4, v[b]);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      if (kb0 + b < nkb) {
+        float sc;
+        reinterpret_cast<uint32_t*>(codes + (kb0 + b) * 128)[lane] = quant_block_values(v[b], pow2, sc);
+        if (lane == 0) scales[kb0 + b] = sc;
+      }
+    }
+  }
+}
+
+// Shared-memory stage of one quantised row: codes, then scales, 16-byte aligned.
+__host__ __device__ __forceinline__ int64_t row_stage_bytes(int64_t H) { return (H + 4 * (H / 128) + 15) / 16 * 16; }
+
+constexpr int kP2pWarps = 4;  // tokens per CTA of the peer dispatch, one warp each
+
+// Quantise and lay out for the grouped GEMM in one pass, when there is no exchange (one rank).
+// Warp w of CTA c takes token t = c * kP2pWarps + w; lane j < topk claims slot j's row in
+// the contiguous layout (row expert_off[e] + a per-expert counter, e = topk_ids[t, j] in
+// [0, E)); the warp quantises the token's row once into shared memory (warp_quant_row, the
+// same bits as per_block_cast_to_fp8 or the power-of-two recipe) and copies the codes
+// (16-byte stores) and scales into every claimed row.  perm_pos[t*topk + j] is that row and
+// send_index[t*topk + j] the slot itself (-1 for skipped slots), the form the combine step
+// reads.  fill: [E] counters, zeroed by the host.
+__global__ void __launch_bounds__(kP2pWarps * 32) ep_quant_dispatch_local_kernel(
+    const void* x, int x_dtype, int64_t x_stride, const void* ids, int ids_dtype, int64_t T, int64_t topk, int64_t E,
     int64_t H, const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices,
     int32_t* perm_pos, int32_t* send_index, int pow2) {
   constexpr int kMaxTopk = 32;
-  __shared__ int64_t s_row[kMaxTopk];
-  const int64_t t = blockIdx.x;
+  extern __shared__ __align__(16) uint8_t local_stage[];
+  __shared__ int64_t s_row[kP2pWarps][kMaxTopk];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x < topk) {
-    const int64_t i = t * topk + threadIdx.x;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kP2pWarps + warp;
+  if (t >= T) return;  // warp-uniform; no block-wide barrier follows
+  if (lane < topk) {
+    const int64_t i = t * topk + lane;
     const int64_t e = load_idx(ids, ids_dtype, i);
     int64_t row = -1;
     if (e >= 0 && e < E) {
       row = expert_off[e] + atomicAdd(&fill[e], 1);
       m_indices[row] = static_cast<int32_t>(e);
     }
-    s_row[threadIdx.x] = row;
+    s_row[warp][lane] = row;
     perm_pos[i] = static_cast<int32_t>(row);
     send_index[i] = row >= 0 ? static_cast<int32_t>(i) : -1;
   }
-  __syncthreads();
-  for (int64_t kb = warp; kb < H / 128; kb += blockDim.x / 32) {
-    float v[4];
-    const int64_t base = t * x_stride + kb * 128 + lane * 4;
-    if (x_dtype == CDG_DTYPE_BF16) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + base);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-      const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
-      v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
-    } else {
-      const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + base);
-      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-    }
-    float scale;
-    const uint32_t packed = quant_block_values(v, pow2, scale);
-    for (int j = 0; j < topk; ++j) {
-      const int64_t row = s_row[j];
-      if (row < 0) continue;
-      reinterpret_cast<uint32_t*>(A + row * H + kb * 128)[lane] = packed;
-      if (lane == 0) SA[row * (H / 128) + kb] = scale;
-    }
+  uint8_t* stage = local_stage + warp * row_stage_bytes(H);
+  const float* scales = reinterpret_cast<const float*>(stage + H);
+  warp_quant_row(x, x_dtype, t * x_stride, H, stage, reinterpret_cast<float*>(stage + H), lane, pow2);
+  __syncwarp();
+  for (int j = 0; j < topk; ++j) {
+    const int64_t row = s_row[warp][j];
+    if (row < 0) continue;
+    for (int64_t c = lane; c < H / 16; c += 32)
+      reinterpret_cast<uint4*>(A + row * H)[c] = reinterpret_cast<const uint4*>(stage)[c];
+    for (int64_t c = lane; c < H / 128; c += 32) SA[row * (H / 128) + c] = scales[c];
   }
 }
 
@@ -315,6 +348,74 @@ __global__ void __launch_bounds__(256) silu_mul_quant_vec_kernel(const __nv_bflo
   }
 }
 
+// The 16-byte path (rows and codes 16-byte aligned): one warp per (row, four 128-column blocks
+// of the output), eight lanes per block and sixteen columns per lane: two 16-byte loads of gate
+// values, two of up values, one 16-byte store of codes, the block's amax over its eight lanes in
+// three shuffles, and two conversions to e4m3 per instruction.  A grid of a few CTAs per SM
+// strides over the items; a row whose m_indices entry is negative is skipped before any of its
+// values is read.  Same arithmetic as the paths above (silu_mul, quant_block_values_mul).
+__global__ void __launch_bounds__(256) silu_mul_quant_16b_kernel(const __nv_bfloat16* in, int64_t in_stride,
+                                                                 int64_t M, int64_t I, const int32_t* m_indices,
+                                                                 uint8_t* q, int64_t q_stride, float* s,
+                                                                 int64_t s_stride_m, int64_t s_stride_k, int pow2) {
+  const int64_t kb_count = I / 128;
+  const int64_t chunks = (kb_count + 3) / 4;
+  const int64_t items = M * chunks;
+  const int lane = threadIdx.x & 31, sub = lane & 7, blk = lane >> 3;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < items;
+       w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const int64_t r = w / chunks;
+    const int64_t kb = (w - r * chunks) * 4 + blk;
+    if (m_indices && __ldg(m_indices + r) < 0) continue;  // padding row (warp-uniform): never read by the next GEMM
+    const bool on = kb < kb_count;
+    const int64_t col = kb * 128 + sub * 16;
+    uint4 raw[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if (on) {
+      const uint4* gp = reinterpret_cast<const uint4*>(in + r * in_stride + col);
+      const uint4* up = reinterpret_cast<const uint4*>(in + r * in_stride + I + col);
+      raw[0] = __ldg(gp);
+      raw[1] = __ldg(gp + 1);
+      raw[2] = __ldg(up);
+      raw[3] = __ldg(up + 1);
+    }
+    float v[16];
+    float amax = 0.0f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t gw[4] = {raw[h].x, raw[h].y, raw[h].z, raw[h].w};
+      const uint32_t uw[4] = {raw[2 + h].x, raw[2 + h].y, raw[2 + h].z, raw[2 + h].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 g2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[i]));
+        const float2 u2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[i]));
+        v[h * 8 + 2 * i] = silu_mul(g2.x, u2.x);
+        v[h * 8 + 2 * i + 1] = silu_mul(g2.y, u2.y);
+        amax = fmaxf(amax, fmaxf(fabsf(v[h * 8 + 2 * i]), fabsf(v[h * 8 + 2 * i + 1])));
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));  // the block's 8 lanes
+    amax = fmaxf(amax, 1e-12f);
+    uint32_t sb = __float_as_uint(amax / 448.0f);
+    if (sb & 0x007FFFFFu) sb = (sb & 0xFF800000u) + 0x00800000u;
+    const float s2 = __uint_as_float(sb);
+    const float rcp = pow2 ? 1.0f / s2 : 448.0f / amax;
+    uint32_t packed[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * i] * rcp, v[4 * i + 1] * rcp), __NV_SATFINITE,
+                                                   __NV_E4M3);
+      const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * i + 2] * rcp, v[4 * i + 3] * rcp),
+                                                   __NV_SATFINITE, __NV_E4M3);
+      packed[i] = (lo & 0xFFFFu) | (hi << 16);
+    }
+    if (on) {
+      *reinterpret_cast<uint4*>(q + r * q_stride + col) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      if (sub == 0) s[r * s_stride_m + kb * s_stride_k] = pow2 ? s2 : amax / 448.0f;
+    }
+  }
+}
+
 // The same for rows that are not 8-byte aligned: one warp per (row, 128-column block), one
 // 2-byte load per value.
 __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride, int64_t M, int64_t I,
@@ -339,12 +440,25 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride
   quant_block_warp_mul(v, q + r * q_stride + kb * 128, s + r * s_stride_m + kb * s_stride_k, lane, pow2);
 }
 
+// Per-CTA histogram in shared memory (when E fits), then one global atomic per CTA and expert:
+// the global counters of a few hundred experts see a few hundred atomics each instead of one
+// per routed slot.
+constexpr int kCountSmemExperts = 4096;
 __global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64_t E, int32_t* cnt) {
+  __shared__ int32_t s_cnt[kCountSmemExperts];
+  const bool local = E <= kCountSmemExperts;
+  if (local)
+    for (int64_t e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t e = load_idx(ids, ids_dtype, i);
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    if (e >= 0 && e < E) atomicAdd(local ? &s_cnt[e] : &cnt[e], 1);
   }
+  if (!local) return;
+  __syncthreads();
+  for (int64_t e = threadIdx.x; e < E; e += blockDim.x)
+    if (s_cnt[e]) atomicAdd(&cnt[e], s_cnt[e]);
 }
 
 
@@ -549,46 +663,6 @@ __global__ void __launch_bounds__(256) ep_permute_fixed_kernel(const uint8_t* ro
 }
 
 // ---------------------------------------------------------------- peer-memory exchange
-// Four values of a 128-column block for lane `lane` (BF16 or FP32 row, 16-byte aligned).
-__device__ __forceinline__ void load_block4(const void* x, int x_dtype, int64_t base, float (&v)[4]) {
-  if (x_dtype == CDG_DTYPE_BF16) {
-    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + base));
-    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
-  } else {
-    const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + base));
-    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-  }
-}
-
-// One warp quantises row x[row_off .. row_off + H) (quant_block_values: the
-// per_block_cast_to_fp8 or power-of-two recipe, bit for bit) into codes[H] and scales[H/128]
-// in shared memory; the loads of eight 128-column blocks are issued before the first is used.
-__device__ __forceinline__ void warp_quant_row(const void* x, int x_dtype, int64_t row_off, int64_t H, uint8_t* codes,
-                                               float* scales, int lane, int pow2) {
-  const int64_t nkb = H / 128;
-  for (int64_t kb0 = 0; kb0 < nkb; kb0 += 8) {
-    float v[8][4];
-#pragma unroll
-    for (int b = 0; b < 8; ++b)
-      if (kb0 + b < nkb) load_block4(x, x_dtype, row_off + (kb0 + b) * 128 + lane * 4, v[b]);
-#pragma unroll
-    for (int b = 0; b < 8; ++b) {
-      if (kb0 + b < nkb) {
-        float sc;
-        reinterpret_cast<uint32_t*>(codes + (kb0 + b) * 128)[lane] = quant_block_values(v[b], pow2, sc);
-        if (lane == 0) scales[kb0 + b] = sc;
-      }
-    }
-  }
-}
-
-// Shared-memory stage of one quantised row: codes, then scales, 16-byte aligned.
-__host__ __device__ __forceinline__ int64_t row_stage_bytes(int64_t H) { return (H + 4 * (H / 128) + 15) / 16 * 16; }
-
-constexpr int kP2pWarps = 4;  // tokens per CTA of the peer dispatch, one warp each
-
 // Peer dispatch.  Warp w of CTA c takes token t = c * kP2pWarps + w; lane j holds the token's
 // slot j.  The slots are grouped by destination rank (__match_any_sync): the token sends one
 // row to each rank that owns any of its experts.  The CTA counts its rows per destination in
@@ -862,17 +936,26 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, int64_t row_stride,
     if (VEC) {
       for (int64_t c8 = threadIdx.x; c8 < H / 8; c8 += blockDim.x) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int64_t j = 0; j < topk; ++j) {
-          const int64_t r = s_row[j];
-          if (r < 0) continue;
-          const uint4 v = *reinterpret_cast<const uint4*>(rows + r * row_stride + c8 * 8);
-          const float wj = s_w[j];
-          const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+        // slots in batches of eight: the batch's loads are all issued before the first is used
+        for (int64_t j0 = 0; j0 < topk; j0 += 8) {
+          uint4 v[8];
 #pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw[q2]));
-            acc[2 * q2] = fmaf(wj, f.x, acc[2 * q2]);
-            acc[2 * q2 + 1] = fmaf(wj, f.y, acc[2 * q2 + 1]);
+          for (int jj = 0; jj < 8; ++jj) {
+            const int64_t r = j0 + jj < topk ? s_row[j0 + jj] : -1;
+            // L2 loads: in the peer variant the rows were written by other GPUs while this kernel waited
+            v[jj] = r >= 0 ? __ldcg(reinterpret_cast<const uint4*>(rows + r * row_stride + c8 * 8)) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            if (j0 + jj >= topk || s_row[j0 + jj] < 0) continue;
+            const float wj = s_w[j0 + jj];
+            const uint32_t vw[4] = {v[jj].x, v[jj].y, v[jj].z, v[jj].w};
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+              const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw[q2]));
+              acc[2 * q2] = fmaf(wj, f.x, acc[2 * q2]);
+              acc[2 * q2 + 1] = fmaf(wj, f.y, acc[2 * q2 + 1]);
+            }
           }
         }
         uint32_t o[4];
@@ -939,6 +1022,14 @@ __global__ void mega_rows_kernel(const uint8_t* src, uint8_t* dst, int64_t G, in
 
 unsigned warp_grid(int64_t warps) { return static_cast<unsigned>((warps * 32 + 255) / 256); }
 
+// SM count of the current device (looked up at each call: a cheap attribute query).
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return n > 0 ? n : 148;
+}
+
 
 
 int launched() { return cudaGetLastError() == cudaSuccess ? CDG_OK : CDG_ERR_CUDA; }
@@ -969,9 +1060,17 @@ int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t
   if (reinterpret_cast<uintptr_t>(q) % 4 || q_stride % 4) return CDG_ERR_ALIGNMENT;
   if (M == 0) return CDG_OK;
   const bool vec = reinterpret_cast<uintptr_t>(in) % 8 == 0 && in_stride % 4 == 0;
+  const bool wide = reinterpret_cast<uintptr_t>(in) % 16 == 0 && in_stride % 8 == 0 &&
+                    reinterpret_cast<uintptr_t>(q) % 16 == 0 && q_stride % 16 == 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const __nv_bfloat16* h = static_cast<const __nv_bfloat16*>(in);
-  if (vec) {
+  if (wide) {
+    const int64_t warps = M * ((I / 128 + 3) / 4);
+    const unsigned grid =
+        static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, int64_t(cdg::sm_count()) * 16)));
+    cdg::silu_mul_quant_16b_kernel<<<grid, 256, 0, st>>>(h, in_stride, M, I, m_indices, q, q_stride, s, s_stride_m,
+                                                          s_stride_k, scale_fmt);
+  } else if (vec) {
     const int64_t chunks = (I / 128 + cdg::kSiluBlocks - 1) / cdg::kSiluBlocks;
     cdg::silu_mul_quant_vec_kernel<<<cdg::warp_grid(M * chunks), 256, 0, st>>>(
         h, in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k, scale_fmt);
@@ -988,7 +1087,8 @@ int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(counts, 0, E * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (n == 0) return CDG_OK;
-  const unsigned blocks = static_cast<unsigned>(n < 256 * 1024 ? (n + 255) / 256 : 1024);
+  // a few CTAs per SM, each over many slots (its histogram is flushed once)
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 2047) / 2048, int64_t(cdg::sm_count()) * 2));
   cdg::ep_count_kernel<<<blocks, 256, 0, st>>>(topk_ids, ids_dtype, n, E, counts);
   return cdg::launched();
 }
@@ -1118,8 +1218,15 @@ int cdg_ep_quant_dispatch_local(const void* x, int32_t x_dtype, int64_t x_stride
   if (cudaMemsetAsync(fill, 0, E * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (M_pad > 0 && cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (T == 0) return CDG_OK;
-  cdg::ep_quant_dispatch_local_kernel<<<static_cast<unsigned>(T), 128, 0, st>>>(
-      x, x_dtype, x_stride, topk_ids, ids_dtype, topk, E, H, expert_off, fill, A, SA, m_indices, perm_pos,
+  const size_t smem = static_cast<size_t>(cdg::kP2pWarps * cdg::row_stage_bytes(H));
+  if (smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(cdg::ep_quant_dispatch_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return CDG_ERR_CUDA;
+  const unsigned grid = static_cast<unsigned>((T + cdg::kP2pWarps - 1) / cdg::kP2pWarps);
+  cdg::ep_quant_dispatch_local_kernel<<<grid, cdg::kP2pWarps * 32, smem, st>>>(
+      x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E, H, expert_off, fill, A, SA, m_indices, perm_pos,
       send_index, scale_fmt);
   return cdg::launched();
 }

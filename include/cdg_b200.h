@@ -120,6 +120,13 @@ typedef struct cdg_gemm_args {
 #define CDG_FLAG_SKIP_UNGROUPED 4 /* rows of D outside every group may be left unwritten instead of
                                      zeroed (for callers that never read them, e.g. a layer's own padded
                                      buffers); the reference always zeroes them */
+#define CDG_FLAG_ROUND_SFB 8       /* float32 weight scales: round each to the nearest power of two (the
+                                     reference's native path, _float_scale_to_e8m0 in
+                                     consumer_deep_gemm/gemm.py:62-73, used at :130-144) and run the
+                                     tensor cores.  Without it, float32 weight scales run the tensor
+                                     cores when every one is a power of two (exact) and the exact SIMT
+                                     kernel otherwise, the reference's dequant fallback; the device
+                                     decides, per call */
 
 /* Grouped FP8 x MXFP4 GEMM, contiguous layout.
  * Replaces m_grouped_fp8_fp4_gemm_nt_contiguous (consumer_deep_gemm/gemm.py:467-470),
@@ -144,7 +151,9 @@ int cdg_grouped_fp8_fp4_gemm_nt_masked(const cdg_gemm_args* args, void* workspac
 size_t cdg_grouped_fp8_fp4_workspace_bytes(const cdg_gemm_args* args);
 
 /* 1 if the tensor-core kernel takes these arguments, 0 if the exact SIMT path
- * will run them, -1 if they are invalid.
+ * will run them, -1 if they are invalid.  For float32 weight scales 1 means: the tensor cores
+ * run them when all are powers of two (or with CDG_FLAG_ROUND_SFB), which the device decides
+ * during the call; otherwise the exact SIMT kernel does.
  * Replaces cutlass_mxfp8_mxfp4_can_implement_probe (csrc/cutlass_mxfp8_mxfp4_probe.cu:158-188,633-639). */
 int cdg_can_implement(const cdg_gemm_args* args);
 

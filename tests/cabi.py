@@ -22,6 +22,7 @@ SF_ROW_MAJOR, SF_ATOMS = 0, 1
 INDEX_PER_ROW, INDEX_PSUM, INDEX_NONE, INDEX_MASKED = 0, 1, 2, 3
 FLAG_FORCE_GENERIC = 1
 FLAG_SINGLE_CTA = 2
+FLAG_ROUND_SFB = 8
 
 
 class GemmArgs(ctypes.Structure):

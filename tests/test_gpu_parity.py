@@ -369,6 +369,62 @@ def test_benchmark_config_every_row(cfg):
     assert cabi.device_status() == (0, 0)
 
 
+def _c0_on_device():
+    c = load_gemm_case("c0")
+    return [c[k].to(DEV) for k in ("a", "sa", "b", "sb", "m_indices")]
+
+
+def test_float_weight_scales_that_are_powers_of_two_run_on_the_tensor_cores():
+    """FP32 weight scales holding powers of two (2^(s-127) of the UE8M0 bytes): converted on the
+    device to the same codes, every block on the tensor-core kernels, output bit-identical to
+    the UE8M0 call; the weight-load hook turns them into the same atoms as the bytes."""
+    import consumer_deep_gemm as cdg
+
+    a, sa, b, sb, ids = _c0_on_device()
+    sbf = torch.exp2(sb.float() - 127.0)
+    d_u8 = torch.full((a.shape[0], b.shape[1]), float("nan"), dtype=torch.bfloat16, device=DEV)
+    d_f = torch.full_like(d_u8, float("nan"))
+    cabi.gemm(a, sa, b, sb, d_u8, ids)
+    ws = cabi.gemm(a, sa, b, sbf, d_f, ids)
+    classes = cabi.block_classes(ws)
+    torch.cuda.synchronize()
+    assert classes["irregular"] == 0 and classes["tiny"] + classes["narrow"] + classes["wide"] > 0, classes
+    assert torch.equal(d_f.view(torch.int16), d_u8.view(torch.int16))
+    assert torch.equal(cdg.transform_sf_into_required_layout(sbf), cdg.transform_sf_into_required_layout(sb))
+
+
+def test_float_weight_scales_otherwise_stay_exact_on_the_simt_kernel():
+    """FP32 weight scales that are not all powers of two: the device sends every block to the
+    exact SIMT kernel (the reference's dequant fallback), matching the reference's output."""
+    c = load_gemm_case("edge_fp32_sb")
+    a, sa, b, sb, ids = (c[k].to(DEV) for k in ("a", "sa", "b", "sb", "m_indices"))
+    assert sb.dtype == torch.float32
+    d = torch.full(c["d"].shape, float("nan"), dtype=torch.bfloat16, device=DEV)
+    ws = cabi.gemm(a, sa, b, sb, d, ids)
+    classes = cabi.block_classes(ws)
+    torch.cuda.synchronize()
+    assert classes["tiny"] + classes["narrow"] + classes["wide"] + classes["wide_direct"] == 0, classes
+    bad = _invalid_rows(c)
+    nw, rl2 = errors(d.cpu(), c["d"], ~bad)
+    assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2
+
+
+def test_round_weight_scales_flag_uses_the_references_rounding():
+    """CDG_FLAG_ROUND_SFB: float weight scales rounded to the nearest power of two on the device
+    give the same bits as the UE8M0 call on the oracle's _float_scale_to_e8m0 codes (pinned to
+    the reference's own outputs)."""
+    a, sa, b, sb, ids = _c0_on_device()
+    g = torch.Generator().manual_seed(21)
+    sbf = (torch.exp2(sb.float() - 127.0).cpu() * (0.75 + 0.7 * torch.rand(sb.shape, generator=g))).to(DEV)
+    codes = oracle.float_scale_to_e8m0(sbf.cpu()).to(DEV)
+    d_r = torch.full((a.shape[0], b.shape[1]), float("nan"), dtype=torch.bfloat16, device=DEV)
+    d_c = torch.full_like(d_r, float("nan"))
+    cabi.gemm(a, sa, b, sbf, d_r, ids, flags=cabi.FLAG_ROUND_SFB)
+    cabi.gemm(a, sa, b, codes, d_c, ids)
+    torch.cuda.synchronize()
+    assert torch.equal(d_r.view(torch.int16), d_c.view(torch.int16))
+
+
 def test_mega_moe_transform_bytes_match_reference():
     import numpy as np
 
