@@ -68,6 +68,9 @@ class NativeOps:
     def count(self, topk_ids, num_experts):
         return self.C.ep_count(topk_ids, num_experts)
 
+    def count_offsets(self, topk_ids, num_experts):
+        return self.C.ep_count_offsets(topk_ids, num_experts)
+
     def pack(self, xq, xs, topk_ids, num_experts, ranks, send_off, rows):
         return self.C.ep_pack(xq, xs, topk_ids, num_experts, ranks, send_off, rows)
 
@@ -261,9 +264,12 @@ class MoELayer:
         reads the GEMM's rows through the permutation."""
         ops, E = self.ops, self.num_experts
         T, topk = topk_ids.shape
-        counts = ops.count(topk_ids, E)                                  # [E] rows per expert
-        aligned = (counts.to(torch.int64) + ALIGN - 1) // ALIGN * ALIGN
-        expert_off = torch.cumsum(aligned, 0) - aligned
+        if hasattr(ops, "count_offsets"):
+            _, expert_off = ops.count_offsets(topk_ids, E)               # group starts, on the device
+        else:
+            counts = ops.count(topk_ids, E)                              # [E] rows per expert
+            aligned = (counts.to(torch.int64) + ALIGN - 1) // ALIGN * ALIGN
+            expert_off = torch.cumsum(aligned, 0) - aligned
         m_pad = (T * topk + (ALIGN - 1) * E + ALIGN - 1) // ALIGN * ALIGN
         a, sa, m_indices, perm_pos, send_index = ops.quant_dispatch_local(x, topk_ids, E, expert_off, m_pad,
                                                                           self.ue8m0)

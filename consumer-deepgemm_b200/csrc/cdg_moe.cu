@@ -442,10 +442,15 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* in, int64_t in_stride
 
 // Per-CTA histogram in shared memory (when E fits), then one global atomic per CTA and expert:
 // the global counters of a few hundred experts see a few hundred atomics each instead of one
-// per routed slot.
+// per routed slot.  With `offsets` (and `ticket`, zeroed by the host), the last CTA also writes
+// the start row of each expert's group in the 128-aligned contiguous layout,
+// offsets[e] = sum over e' < e of ceil128(cnt[e']).
 constexpr int kCountSmemExperts = 4096;
-__global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64_t E, int32_t* cnt) {
+__global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64_t E, int32_t* cnt,
+                                int64_t* offsets = nullptr, int32_t* ticket = nullptr) {
   __shared__ int32_t s_cnt[kCountSmemExperts];
+  __shared__ int64_t s_part[1024];
+  __shared__ int s_last;
   const bool local = E <= kCountSmemExperts;
   if (local)
     for (int64_t e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
@@ -455,10 +460,41 @@ __global__ void ep_count_kernel(const void* ids, int ids_dtype, int64_t n, int64
     const int64_t e = load_idx(ids, ids_dtype, i);
     if (e >= 0 && e < E) atomicAdd(local ? &s_cnt[e] : &cnt[e], 1);
   }
-  if (!local) return;
+  if (local) {
+    __syncthreads();
+    for (int64_t e = threadIdx.x; e < E; e += blockDim.x)
+      if (s_cnt[e]) atomicAdd(&cnt[e], s_cnt[e]);
+  }
+  if (!offsets) return;
+  __threadfence();
   __syncthreads();
-  for (int64_t e = threadIdx.x; e < E; e += blockDim.x)
-    if (s_cnt[e]) atomicAdd(&cnt[e], s_cnt[e]);
+  if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // exclusive scan of the aligned counts: a contiguous run of experts per thread, then the
+  // threads' totals in shared memory
+  const int64_t per = (E + blockDim.x - 1) / blockDim.x;
+  const int64_t e0 = (E < static_cast<int64_t>(threadIdx.x) * per ? E : static_cast<int64_t>(threadIdx.x) * per);
+  const int64_t e1 = E < e0 + per ? E : e0 + per;
+  int64_t tot = 0;
+  for (int64_t e = e0; e < e1; ++e) tot += (__ldcg(&cnt[e]) + 127) / 128 * 128;
+  s_part[threadIdx.x] = tot;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t run = 0;
+    for (int t = 0; t < static_cast<int>(blockDim.x); ++t) {
+      const int64_t v = s_part[t];
+      s_part[t] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  int64_t off = s_part[threadIdx.x];
+  for (int64_t e = e0; e < e1; ++e) {
+    offsets[e] = off;
+    off += (__ldcg(&cnt[e]) + 127) / 128 * 128;
+  }
 }
 
 
@@ -1090,6 +1126,19 @@ int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, 
   // a few CTAs per SM, each over many slots (its histogram is flushed once)
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((n + 2047) / 2048, int64_t(cdg::sm_count()) * 2));
   cdg::ep_count_kernel<<<blocks, 256, 0, st>>>(topk_ids, ids_dtype, n, E, counts);
+  return cdg::launched();
+}
+
+int cdg_ep_count_offsets(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, int32_t* counts,
+                         int64_t* expert_off, int32_t* scratch, cdg_stream_t stream) {
+  if (n < 0 || E <= 0 || !counts || !expert_off || !scratch || (n > 0 && !topk_ids)) return CDG_ERR_INVALID_ARGUMENT;
+  if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(counts, 0, E * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const unsigned blocks =
+      static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((n + 2047) / 2048, int64_t(cdg::sm_count()) * 2)));
+  cdg::ep_count_kernel<<<blocks, 256, 0, st>>>(topk_ids, ids_dtype, n, E, counts, expert_off, scratch);
   return cdg::launched();
 }
 

@@ -228,6 +228,18 @@ torch::Tensor ep_count(const torch::Tensor& ids, int64_t E) {
   return cnt;
 }
 
+std::vector<torch::Tensor> ep_count_offsets(const torch::Tensor& ids, int64_t E) {
+  TORCH_CHECK(ids.is_cuda() && ids.is_contiguous(), "topk ids must be a contiguous CUDA tensor");
+  const c10::cuda::CUDAGuard guard(ids.device());
+  auto cnt = torch::empty({E}, ids.options().dtype(torch::kInt32));
+  auto off = torch::empty({E}, ids.options().dtype(torch::kInt64));
+  auto scratch = torch::empty({1}, ids.options().dtype(torch::kInt32));
+  check_status(cdg_ep_count_offsets(ids.data_ptr(), dtype_code(ids), ids.numel(), E, cnt.data_ptr<int32_t>(),
+                                    off.data_ptr<int64_t>(), scratch.data_ptr<int32_t>(), cur_stream(ids)),
+               "ep_count_offsets");
+  return {cnt, off};
+}
+
 // Returns (packed rows uint8 [R, cdg_ep_row_bytes(H)], send_index [T*topk]).
 std::vector<torch::Tensor> ep_pack(const torch::Tensor& xq, const torch::Tensor& xs, const torch::Tensor& ids,
                                    int64_t E, int64_t ranks, const torch::Tensor& send_off, int64_t rows) {
@@ -495,6 +507,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("silu_mul_quant", &silu_mul_quant, py::arg("h"), py::arg("m_indices") = py::none(),
         py::arg("ue8m0") = false);
   m.def("ep_count", &ep_count, py::arg("topk_ids"), py::arg("num_experts"));
+  m.def("ep_count_offsets", &ep_count_offsets, py::arg("topk_ids"), py::arg("num_experts"));
   m.def("ep_pack", &ep_pack, py::arg("xq"), py::arg("xs"), py::arg("topk_ids"), py::arg("num_experts"),
         py::arg("ranks"), py::arg("send_off"), py::arg("rows"));
   m.def("ep_permute", &ep_permute, py::arg("rows"), py::arg("hidden"), py::arg("local_experts"),

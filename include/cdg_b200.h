@@ -284,6 +284,11 @@ int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t
 
 /* counts[e] = number of entries of topk_ids (n of them, int32 or int64) equal to e, e in [0, E). */
 int cdg_ep_count(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, int32_t* counts, cdg_stream_t stream);
+/* The same counts, and expert_off[e] (int64) = the start row of expert e's group in the 128-aligned
+ * contiguous layout (sum over e' < e of counts rounded up to 128), computed on the device: the offsets
+ * cdg_ep_quant_dispatch_local takes, without a host round trip.  scratch: int32 [1]. */
+int cdg_ep_count_offsets(const void* topk_ids, int32_t ids_dtype, int64_t n, int64_t E, int32_t* counts,
+                         int64_t* expert_off, int32_t* scratch, cdg_stream_t stream);
 
 /* Bytes of one dispatched row for hidden size H: [e4m3 data H][FP32 scales H/128]
  * [int32 local expert id], padded to 16 (0 for an invalid H). */

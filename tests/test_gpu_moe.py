@@ -430,3 +430,20 @@ def test_peer_exchange_two_ranks_on_one_gpu(ue8m0):
     finally:
         for p in own:
             C.ep_window_close(p, False)
+
+
+def test_count_offsets_match_host_layout():
+    """cdg_ep_count_offsets: per-expert counts and the 128-aligned group starts, on the device."""
+    C = _ext()
+    g = torch.Generator().manual_seed(13)
+    for T, k, E in ((4096, 8, 256), (37, 3, 10), (0, 2, 5)):
+        ids = torch.rand(T, E, generator=g).topk(k, dim=1).indices.to(torch.int32) if T else \
+            torch.empty(0, k, dtype=torch.int32)
+        if T:
+            ids[0, 0] = -1
+            ids[1, 0] = E  # outside [0, E): not counted
+        cnt, off = C.ep_count_offsets(ids.to(DEV), E)
+        ref = torch.bincount(ids[(ids >= 0) & (ids < E)].long(), minlength=E)
+        aligned = (ref + 127) // 128 * 128
+        assert torch.equal(cnt.cpu().long(), ref)
+        assert torch.equal(off.cpu(), torch.cumsum(aligned, 0) - aligned)
