@@ -406,36 +406,20 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     // (2) activation planes of the rows that carry the block's expert, one 16-byte chunk
     //     per item; consecutive threads read consecutive chunks of a row (coalesced).
     //     Other rows of the planes are not written: whatever they hold only reaches
-    //     accumulator columns the epilogue replaces by zeros.  Each thread issues the loads
-    //     of kConvU items before converting the first (one load at a time left the kernel
-    //     waiting on memory: 4.6 TB/s on c4's FC1).
+    //     accumulator columns the epilogue replaces by zeros.
     const int chunks = kbn * 8;
     const int nv = s_nv;
-    constexpr int kConvU = 4;
-    for (int it0 = tid; it0 < nv * chunks; it0 += kConvU * blockDim.x) {
-      uint4 raws[kConvU];
-#pragma unroll
-      for (int u = 0; u < kConvU; ++u) {
-        const int it = it0 + u * blockDim.x;
-        if (it < nv * chunks) {
-          const int rr = s_vrow[it / chunks];
-          const int64_t col = static_cast<int64_t>(kb0) * 128 + (it % chunks) * 16;
-          raws[u] = __ldg(reinterpret_cast<const uint4*>(p.a + (row0 + rr) * p.a_row_stride + col));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kConvU; ++u) {
-      const int it = it0 + u * blockDim.x;
-      if (it >= nv * chunks) break;
+    for (int it = tid; it < nv * chunks; it += blockDim.x) {
       const int rr = s_vrow[it / chunks];
       const int c = it % chunks;
       const int kl = c >> 3;
+      const int r = row0 + rr;
       const int64_t col = static_cast<int64_t>(kb0) * 128 + c * 16;
       uint4 hi4, lo4;
       {
         // two elements per conversion instruction (e4m3x2 <-> f16x2, f32x2 -> bf16x2 / e4m3x2),
         // the same roundings as one at a time; byte pairs taken from and put into 32-bit words
-        const uint4 raw = raws[u];
+        const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + col);
         const float sbf = s_scale[rr][kl];
         const float inv = s_inv[rr];
         const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -461,7 +445,6 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       uint8_t* dst = p.hilo + (static_cast<int64_t>(b) * 128 + rr) * K + col;
       *reinterpret_cast<uint4*>(dst) = hi4;
       *reinterpret_cast<uint4*>(dst + plane) = lo4;
-      }
     }
     }
   }
