@@ -59,8 +59,22 @@ ALIGN = 128
 class NativeOps:
     """Device kernels of libcdg_b200.so through the torch binding."""
 
+    # the quantising steps can write the GEMM's activation planes directly (FP32 1x128 recipe)
+    supports_planes = True
+
     def __init__(self):
         self.C = native.require()
+
+    def quant_dispatch_local_planes(self, x, topk_ids, num_experts, expert_off, m_pad):
+        return self.C.ep_quant_dispatch_local_planes(x, topk_ids, num_experts, expert_off, m_pad)
+
+    def act_planes(self, h, m_indices):
+        return self.C.silu_mul_quant_planes(h, m_indices)
+
+    def gemm_planes(self, planes, row_exp, w, w_sf, m_indices, skip_ungrouped=False):
+        d = torch.empty(planes.shape[1], w.shape[1], dtype=torch.bfloat16, device=planes.device)
+        self.C.grouped_gemm_planes(planes, row_exp, w, w_sf, d, m_indices, 4 if skip_ungrouped else 0)
+        return d
 
     def quant(self, x, ue8m0=False):
         return self.C.quant_fp8_rows(x, ue8m0)
@@ -163,9 +177,14 @@ class MoELayer:
     """
 
     def __init__(self, w1, w1_scale, w2=None, w2_scale=None, num_experts: int = 0, group=None, ops=None,
-                 max_tokens_per_rank: int | None = None, exchange: str = "nccl", ue8m0: bool = False):
+                 max_tokens_per_rank: int | None = None, exchange: str = "nccl", ue8m0: bool = False,
+                 planes: bool | None = None):
         self.ops = ops or NativeOps()
         self.ue8m0 = bool(ue8m0)
+        # FP32 activation scales: the quantising steps write the GEMMs' activation planes directly
+        # (the GEMMs then skip their own plane split); power-of-two scales need no planes
+        self.planes = (not self.ue8m0 and getattr(self.ops, "supports_planes", False)) if planes is None else \
+            bool(planes) and not self.ue8m0
         self.max_tokens = max_tokens_per_rank
         if exchange not in ("nccl", "p2p"):
             raise ValueError("exchange must be 'nccl' or 'p2p'")
@@ -271,19 +290,36 @@ class MoELayer:
             aligned = (counts.to(torch.int64) + ALIGN - 1) // ALIGN * ALIGN
             expert_off = torch.cumsum(aligned, 0) - aligned
         m_pad = (T * topk + (ALIGN - 1) * E + ALIGN - 1) // ALIGN * ALIGN
-        a, sa, m_indices, perm_pos, send_index = ops.quant_dispatch_local(x, topk_ids, E, expert_off, m_pad,
-                                                                          self.ue8m0)
-        self._phase("dispatch")
-        h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        if self.planes:
+            pl, rexp, m_indices, perm_pos, send_index = ops.quant_dispatch_local_planes(x, topk_ids, E, expert_off,
+                                                                                        m_pad)
+            self._phase("dispatch")
+            h = ops.gemm_planes(pl, rexp, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        else:
+            a, sa, m_indices, perm_pos, send_index = ops.quant_dispatch_local(x, topk_ids, E, expert_off, m_pad,
+                                                                              self.ue8m0)
+            self._phase("dispatch")
+            h = ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         self._phase("fc1")
         if self.w2 is not None:
-            aq, asc = ops.act(h, m_indices, self.ue8m0)
-            self._phase("act")
-            h = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
-            self._phase("fc2")
+            h = self._act_fc2(h, m_indices)
         y = ops.unpermute_combine(h, perm_pos, send_index, topk_w)
         self._phase("combine")
         return y
+
+    def _act_fc2(self, h, m_indices):
+        """SiLU-mul + requant of FC1's rows, then FC2 (rows outside every group left unwritten)."""
+        ops = self.ops
+        if self.planes:
+            pl, rexp = ops.act_planes(h, m_indices)
+            self._phase("act")
+            out = ops.gemm_planes(pl, rexp, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+        else:
+            aq, asc = ops.act(h, m_indices, self.ue8m0)
+            self._phase("act")
+            out = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+        self._phase("fc2")
+        return out
 
     def _forward_fixed(self, x, topk_ids, topk_w):
         """Exchange without a host synchronisation: fixed per-destination capacity."""
@@ -326,15 +362,18 @@ class MoELayer:
                                        self.ue8m0)
         self._phase("dispatch")
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
-        a, sa, m_indices, ret_slot = C.ep_permute_p2p(win.own, world, self.max_tokens, topk, H, E_loc, m_pad, x)
-        self._phase("permute")
-        h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        if self.planes:
+            pl, rexp, m_indices, ret_slot = C.ep_permute_p2p_planes(win.own, world, self.max_tokens, topk, H, E_loc,
+                                                                    m_pad, x)
+            self._phase("permute")
+            h = self.ops.gemm_planes(pl, rexp, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
+        else:
+            a, sa, m_indices, ret_slot = C.ep_permute_p2p(win.own, world, self.max_tokens, topk, H, E_loc, m_pad, x)
+            self._phase("permute")
+            h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         self._phase("fc1")
         if self.w2 is not None:
-            aq, asc = self.ops.act(h, m_indices, self.ue8m0)
-            self._phase("act")
-            h = self.ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
-            self._phase("fc2")
+            h = self._act_fc2(h, m_indices)
         C.ep_return_p2p(h, ret_slot, world, self.max_tokens, topk, win.peers, win.own, me)
         self._phase("return")
         y = C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, self.max_tokens, H)

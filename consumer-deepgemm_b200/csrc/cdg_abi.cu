@@ -115,10 +115,17 @@ int validate(const cdg_gemm_args* g) {
   if (g->K % 2) return CDG_ERR_INVALID_ARGUMENT;
   if (g->M > 0 && (!g->a || !g->d)) return CDG_ERR_INVALID_ARGUMENT;
   if (!g->b || !g->sfb) return CDG_ERR_INVALID_ARGUMENT;
-  if (g->a_dtype != CDG_DTYPE_E4M3 && g->a_dtype != CDG_DTYPE_BF16 && g->a_dtype != CDG_DTYPE_F32)
+  if (g->a_dtype != CDG_DTYPE_E4M3 && g->a_dtype != CDG_DTYPE_BF16 && g->a_dtype != CDG_DTYPE_F32 &&
+      g->a_dtype != CDG_DTYPE_E4M3_PLANES)
     return CDG_ERR_INVALID_ARGUMENT;
-  if (g->sa_dtype != 0 && g->sa_dtype != CDG_DTYPE_F32 && g->sa_dtype != CDG_DTYPE_UE8M0_X4)
+  if (g->a_dtype == CDG_DTYPE_E4M3_PLANES) {
+    // [2][M][K] planes and int32 row exponents, 128-aligned per-row groups
+    if (!g->sa || g->sa_dtype != CDG_DTYPE_I32 || g->a_row_stride != g->K || g->M % 128 ||
+        g->index_form != CDG_INDEX_PER_ROW)
+      return CDG_ERR_INVALID_ARGUMENT;
+  } else if (g->sa_dtype != 0 && g->sa_dtype != CDG_DTYPE_F32 && g->sa_dtype != CDG_DTYPE_UE8M0_X4) {
     return CDG_ERR_INVALID_ARGUMENT;
+  }
   if (g->a_dtype == CDG_DTYPE_E4M3) {
     if (!g->sa || g->sa_cols <= 0) return CDG_ERR_INVALID_ARGUMENT;
     if (g->sa_dtype == CDG_DTYPE_UE8M0_X4) {
@@ -168,9 +175,10 @@ bool fast_path(const cdg_gemm_args* g) {
   // with CDG_FLAG_ROUND_SFB
   const bool sfb_ok = g->sfb_dtype == CDG_DTYPE_UE8M0 || (g->sfb_dtype == CDG_DTYPE_F32 &&
                                                           g->sfb_layout == CDG_SF_ROW_MAJOR);
-  if (g->a_dtype != CDG_DTYPE_E4M3 || !sfb_ok || g->d_dtype != CDG_DTYPE_BF16) return false;
+  const bool planes = g->a_dtype == CDG_DTYPE_E4M3_PLANES;
+  if ((g->a_dtype != CDG_DTYPE_E4M3 && !planes) || !sfb_ok || g->d_dtype != CDG_DTYPE_BF16) return false;
   const bool packed = g->sa_dtype == CDG_DTYPE_UE8M0_X4;
-  if (g->K % 128 || g->N % 128 || (!packed && g->sa_cols != g->K / 128)) return false;
+  if (g->K % 128 || g->N % 128 || (!planes && !packed && g->sa_cols != g->K / 128)) return false;
   if (g->a_row_stride % 16 || !aligned(g->a, 16)) return false;
   if (g->b_stride_n != g->K / 2 || g->b_stride_e != g->b_stride_n * g->N || !aligned(g->b, 32)) return false;
   if (g->d_row_stride % 8 || !aligned(g->d, 16)) return false;
@@ -189,7 +197,7 @@ WorkspaceLayout layout_for(const cdg_gemm_args* g) {
   const bool fast = fast_path(g);
   return WorkspaceLayout::make(g->M, tile_map(g).tiles(), g->K, g->N, g->E, fast,
                                g->index_form == CDG_INDEX_PSUM || g->index_form == CDG_INDEX_MASKED,
-                               fast && sfw_needs_transform(g));
+                               fast && sfw_needs_transform(g), g->a_dtype == CDG_DTYPE_E4M3_PLANES);
 }
 
 int launch_sf_atoms_f32(const float* sf, int64_t se, int64_t sn, int64_t E, int64_t N, int64_t KB, uint32_t* out,
@@ -417,6 +425,8 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   if (generic_smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
   const int64_t generic_units = nblk * ((g->N + 255) / 256);
 
+  const bool planes_in = g->a_dtype == CDG_DTYPE_E4M3_PLANES;
+  if (planes_in && !fast_path(g)) return CDG_ERR_UNSUPPORTED;  // planes run on the tensor cores only
   if (!fast_path(g)) {
     ga.ids = ids;
     ga.ids_is_64 = ids_dtype == CDG_DTYPE_I64;
@@ -441,8 +451,9 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
     if (st != CDG_OK) return st;
     sfw = out;
   }
-  uint8_t* hilo = ws + wl.hilo;
-  int32_t* row_exp = reinterpret_cast<int32_t*>(ws + wl.row_exp);
+  uint8_t* hilo = planes_in ? static_cast<uint8_t*>(const_cast<void*>(g->a)) : ws + wl.hilo;
+  int32_t* row_exp = planes_in ? reinterpret_cast<int32_t*>(const_cast<float*>(g->sa))
+                               : reinterpret_cast<int32_t*>(ws + wl.row_exp);
 
   PrepArgs pa{};
   pa.a = static_cast<const uint8_t*>(g->a);
@@ -471,7 +482,9 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   pa.direct_tiles = reinterpret_cast<int4*>(ws + wl.direct_tiles);
   pa.pair_wide = pair_path ? 1 : 0;
   pa.sf_inexact = float_sfb && !(g->flags & CDG_FLAG_ROUND_SFB) ? ctrl + kCtrlSfInexact : nullptr;
-  const dim3 prep_grid(static_cast<unsigned>(nblk), static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
+  pa.planes_given = planes_in ? 1 : 0;
+  const dim3 prep_grid(static_cast<unsigned>(nblk),
+                       planes_in ? 1u : static_cast<unsigned>((g->K + kPrepK - 1) / kPrepK));
   if (ids_dtype == CDG_DTYPE_I64)
     cdg_prep_kernel<int64_t><<<prep_grid, 256, 0, stream>>>(pa);
   else

@@ -17,6 +17,7 @@
 
 #include "cdg_layout.h"
 #include "cdg_ptx.cuh"
+#include "cdg_split.cuh"
 
 namespace cdg {
 
@@ -188,6 +189,8 @@ struct PrepArgs {
   int4* direct_tiles;      // [nblk] tiles of cdg_gemm_direct_kernel, the same form
   const int* sf_inexact;   // float weight scales: set when one is not a power of two, and the
                            // exact SIMT kernel then takes every block (nullptr: not consulted)
+  int planes_given;        // the caller passed the activation planes and row exponents: plan the
+                           // blocks only (no plane split, no direct class)
 };
 
 // 2^(e-127) exactly, e in [0, 255] (255 gives +inf as in the reference's FP32 pow).
@@ -302,17 +305,30 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       expert = -2;
     }
   }
+  if (p.planes_given && cls == kClassIrregular) {
+    // planes given by the caller: the exact SIMT kernel has no e4m3 rows to read, and a block
+    // holding rows of several experts breaks the caller's promise of 128-aligned groups; the
+    // block is left out (written as zeros unless rows outside groups are skipped) and reported
+    cls = kClassZero;
+    expert = -1;
+    if (tid == 0 && blockIdx.y == 0) {
+      atomicOr(&p.ctrl[kCtrlStatus], kStatusBadIndex);
+      atomicOr(&g_sticky_status[0], kStatusBadIndex);
+    }
+  }
 
   if (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide) {
+    if (tid < 128 && s_id[tid] == expert) {
+      atomicOr(&s_mask[tid >> 5], 1u << (tid & 31));
+      s_vrow[atomicAdd(&s_nv, 1)] = static_cast<uint8_t>(tid);
+    }
+  }
+  if (!p.planes_given && (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide)) {
     const int ntok = (eff + 15) & ~15;
     const int K = p.K;
     const int kb_count = K / 128;
     const int kb0 = blockIdx.y * (kPrepK / 128);
     const int kbn = min(kPrepK / 128, kb_count - kb0);
-    if (tid < 128 && s_id[tid] == expert) {
-      atomicOr(&s_mask[tid >> 5], 1u << (tid & 31));
-      s_vrow[atomicAdd(&s_nv, 1)] = static_cast<uint8_t>(tid);
-    }
     // (1) per routed row: the exponent E with |bf16(sa[r,kb])| < 2^E for every K block of
     //     the row (frexp exponent of the largest scale); and the BF16-rounded scales of
     //     this CTA's K blocks.  The (row, K block) scales are read by all threads at once,
@@ -376,7 +392,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     cls = kClassIrregular;
     expert = -2;
   }
-  if (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide) {
+  if (!p.planes_given && (cls == kClassTiny || cls == kClassNarrow || cls == kClassWide)) {
     const int K = p.K;
     const int kb_count = K / 128;
     const int kb0 = blockIdx.y * (kPrepK / 128);
@@ -416,32 +432,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       const int r = row0 + rr;
       const int64_t col = static_cast<int64_t>(kb0) * 128 + c * 16;
       uint4 hi4, lo4;
-      {
-        // two elements per conversion instruction (e4m3x2 <-> f16x2, f32x2 -> bf16x2 / e4m3x2),
-        // the same roundings as one at a time; byte pairs taken from and put into 32-bit words
-        const uint4 raw = *reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + col);
-        const float sbf = s_scale[rr][kl];
-        const float inv = s_inv[rr];
-        const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
-        uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const __nv_fp8x2_storage_t a2 = static_cast<__nv_fp8x2_storage_t>(in[i >> 1] >> (16 * (i & 1)));
-          const __half2_raw ar = __nv_cvt_fp8x2_to_halfraw2(a2, __NV_E4M3);
-          const float2 af = __half22float2(__half2(ar));
-          const float2 x = __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(af.x, sbf), __fmul_rn(af.y, sbf)));
-          const float2 v = make_float2(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv));
-          const __nv_fp8x2_storage_t h = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
-          const float2 hf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(h, __NV_E4M3)));
-          const __nv_fp8x2_storage_t l =
-              __nv_cvt_float2_to_fp8x2(make_float2(__fsub_rn(v.x, hf.x), __fsub_rn(v.y, hf.y)), __NV_SATFINITE,
-                                       __NV_E4M3);
-          hw[i >> 1] |= static_cast<uint32_t>(h) << (16 * (i & 1));
-          lw[i >> 1] |= static_cast<uint32_t>(l) << (16 * (i & 1));
-        }
-        hi4 = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        lo4 = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      }
+      split_planes16(*reinterpret_cast<const uint4*>(p.a + r * p.a_row_stride + col), s_scale[rr][kl], s_inv[rr], hi4,
+                     lo4);
       uint8_t* dst = p.hilo + (static_cast<int64_t>(b) * 128 + rr) * K + col;
       *reinterpret_cast<uint4*>(dst) = hi4;
       *reinterpret_cast<uint4*>(dst + plane) = lo4;

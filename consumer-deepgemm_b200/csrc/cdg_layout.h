@@ -90,7 +90,7 @@ struct WorkspaceLayout {
          hilo = 0, tok_code = 0, tok_atoms = 0, sfw_atoms = 0, total = 0;
 
   static WorkspaceLayout make(int64_t M, int64_t nblk, int64_t K, int64_t N, int64_t E, bool fast, bool row_ids,
-                              bool sfw_from_rows) {
+                              bool sfw_from_rows, bool planes_given = false) {
     WorkspaceLayout w;
     size_t off = 0;
     w.ctrl = off;
@@ -110,10 +110,12 @@ struct WorkspaceLayout {
       off = align_up(off + static_cast<size_t>(M) * 4, 1024);
     }
     if (fast) {
-      w.row_exp = off;
-      off = align_up(off + static_cast<size_t>(nblk) * 128 * 4, 1024);
-      w.hilo = off;
-      off = align_up(off + static_cast<size_t>(2) * nblk * 128 * K, 1024);
+      if (!planes_given) {  // otherwise the caller's planes and row exponents are used
+        w.row_exp = off;
+        off = align_up(off + static_cast<size_t>(nblk) * 128 * 4, 1024);
+        w.hilo = off;
+        off = align_up(off + static_cast<size_t>(2) * nblk * 128 * K, 1024);
+      }
       w.tok_code = off;  // [M][tok_code_pitch(K)] UE8M0 activation scale codes of the direct class's rows
       off = align_up(off + static_cast<size_t>(tok_code_pitch(K)) * static_cast<size_t>(M), 1024);
       w.tok_atoms = off;  // [direct tile][K/512 scale stage][2][128] words: token scale atoms

@@ -26,6 +26,7 @@
 #include <cstring>
 
 #include "cdg_b200.h"
+#include "cdg_split.cuh"
 
 namespace cdg {
 namespace {
@@ -255,6 +256,23 @@ __device__ __forceinline__ void warp_quant_row(const void* x, int x_dtype, int64
   }
 }
 
+// The row exponent E of the activation planes (cdg_split.cuh) from a row's nkb FP32 scales,
+// by the whole warp: the frexp exponent of the largest finite |bf16(s)|, clamped to the range
+// the MMA scale factors take (scales produced by the 1x128 recipe from finite BF16/FP32 rows
+// always lie inside it).
+__device__ __forceinline__ int warp_plane_exponent(const float* scales, int64_t nkb, int lane) {
+  float m = 0.0f;
+  for (int64_t kb = lane; kb < nkb; kb += 32) {
+    const float sb = fabsf(bf16_round(scales[kb]));
+    if (isfinite(sb)) m = fmaxf(m, sb);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  bool in_range = true;
+  const int e = plane_exponent(m, &in_range);
+  return e < -126 ? -126 : e > 127 ? 127 : e;
+}
+
 // Shared-memory stage of one quantised row: codes, then scales, 16-byte aligned.
 __host__ __device__ __forceinline__ int64_t row_stage_bytes(int64_t H) { return (H + 4 * (H / 128) + 15) / 16 * 16; }
 
@@ -268,10 +286,14 @@ constexpr int kP2pWarps = 4;  // tokens per CTA of the peer dispatch, one warp e
 // (16-byte stores) and scales into every claimed row.  perm_pos[t*topk + j] is that row and
 // send_index[t*topk + j] the slot itself (-1 for skipped slots), the form the combine step
 // reads.  fill: [E] counters, zeroed by the host.
+// Planes form (planes != nullptr; A and SA unused): each claimed row gets the row's two e4m3
+// planes (planes[0][row], planes[1][row], plane stride M_pad * H) and row_exp[row] = E, the
+// split the GEMM's prep kernel would make of the codes and scales (cdg_split.cuh).
 __global__ void __launch_bounds__(kP2pWarps * 32) ep_quant_dispatch_local_kernel(
     const void* x, int x_dtype, int64_t x_stride, const void* ids, int ids_dtype, int64_t T, int64_t topk, int64_t E,
     int64_t H, const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices,
-    int32_t* perm_pos, int32_t* send_index, int pow2) {
+    int32_t* perm_pos, int32_t* send_index, int pow2, uint8_t* planes = nullptr, int32_t* row_exp = nullptr,
+    int64_t M_pad = 0) {
   constexpr int kMaxTopk = 32;
   extern __shared__ __align__(16) uint8_t local_stage[];
   __shared__ int64_t s_row[kP2pWarps][kMaxTopk];
@@ -294,6 +316,23 @@ __global__ void __launch_bounds__(kP2pWarps * 32) ep_quant_dispatch_local_kernel
   const float* scales = reinterpret_cast<const float*>(stage + H);
   warp_quant_row(x, x_dtype, t * x_stride, H, stage, reinterpret_cast<float*>(stage + H), lane, pow2);
   __syncwarp();
+  if (planes) {
+    const int e = warp_plane_exponent(scales, H / 128, lane);
+    const float inv = ldexpf(1.0f, -e);
+    const int64_t plane = M_pad * H;
+    for (int64_t c = lane; c < H / 16; c += 32) {
+      uint4 hi, lo;
+      split_planes16(reinterpret_cast<const uint4*>(stage)[c], bf16_round(scales[c >> 3]), inv, hi, lo);
+      for (int j = 0; j < topk; ++j) {
+        const int64_t row = s_row[warp][j];
+        if (row < 0) continue;
+        reinterpret_cast<uint4*>(planes + row * H)[c] = hi;
+        reinterpret_cast<uint4*>(planes + plane + row * H)[c] = lo;
+      }
+    }
+    if (lane < topk && s_row[warp][lane] >= 0) row_exp[s_row[warp][lane]] = e;
+    return;
+  }
   for (int j = 0; j < topk; ++j) {
     const int64_t row = s_row[warp][j];
     if (row < 0) continue;
@@ -413,6 +452,84 @@ __global__ void __launch_bounds__(256) silu_mul_quant_16b_kernel(const __nv_bflo
       *reinterpret_cast<uint4*>(q + r * q_stride + col) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
       if (sub == 0) s[r * s_stride_m + kb * s_stride_k] = pow2 ? s2 : amax / 448.0f;
     }
+  }
+}
+
+// Planes form of the SiLU-mul requant (16-byte aligned rows): one warp per row.  The row's
+// codes and scales are formed as in silu_mul_quant_16b_kernel (the same bits) into shared
+// memory, then the row is split into the GEMM's two e4m3 planes (cdg_split.cuh):
+// planes[0][r], planes[1][r] (plane stride M * I) and row_exp[r].  Rows whose m_indices entry
+// is negative are skipped.
+__global__ void __launch_bounds__(256) silu_mul_quant_planes_kernel(const __nv_bfloat16* in, int64_t in_stride,
+                                                                    int64_t M, int64_t I, const int32_t* m_indices,
+                                                                    uint8_t* planes, int32_t* row_exp) {
+  extern __shared__ __align__(16) uint8_t act_stage[];
+  const int64_t kb_count = I / 128;
+  const int64_t chunks = (kb_count + 3) / 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 7, blk = lane >> 3;
+  uint8_t* codes = act_stage + warp * row_stage_bytes(I);
+  float* scales = reinterpret_cast<float*>(codes + I);
+  const int64_t plane = M * I;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < M;
+       r += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    if (m_indices && __ldg(m_indices + r) < 0) continue;  // warp-uniform
+    for (int64_t ch = 0; ch < chunks; ++ch) {
+      const int64_t kb = ch * 4 + blk;
+      const bool on = kb < kb_count;
+      const int64_t col = kb * 128 + sub * 16;
+      uint4 raw[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if (on) {
+        const uint4* gp = reinterpret_cast<const uint4*>(in + r * in_stride + col);
+        const uint4* up = reinterpret_cast<const uint4*>(in + r * in_stride + I + col);
+        raw[0] = __ldg(gp);
+        raw[1] = __ldg(gp + 1);
+        raw[2] = __ldg(up);
+        raw[3] = __ldg(up + 1);
+      }
+      float v[16];
+      float amax = 0.0f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t gw[4] = {raw[h].x, raw[h].y, raw[h].z, raw[h].w};
+        const uint32_t uw[4] = {raw[2 + h].x, raw[2 + h].y, raw[2 + h].z, raw[2 + h].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 g2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[i]));
+          const float2 u2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&uw[i]));
+          v[h * 8 + 2 * i] = silu_mul(g2.x, u2.x);
+          v[h * 8 + 2 * i + 1] = silu_mul(g2.y, u2.y);
+          amax = fmaxf(amax, fmaxf(fabsf(v[h * 8 + 2 * i]), fabsf(v[h * 8 + 2 * i + 1])));
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      amax = fmaxf(amax, 1e-12f);
+      const float rcp = 448.0f / amax;
+      uint32_t packed[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * i] * rcp, v[4 * i + 1] * rcp), __NV_SATFINITE,
+                                                     __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v[4 * i + 2] * rcp, v[4 * i + 3] * rcp),
+                                                     __NV_SATFINITE, __NV_E4M3);
+        packed[i] = (lo & 0xFFFFu) | (hi << 16);
+      }
+      if (on) {
+        *reinterpret_cast<uint4*>(codes + col) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        if (sub == 0) scales[kb] = amax / 448.0f;
+      }
+    }
+    __syncwarp();
+    const int e = warp_plane_exponent(scales, kb_count, lane);
+    const float inv = ldexpf(1.0f, -e);
+    for (int64_t c = lane; c < I / 16; c += 32) {
+      uint4 hi, lo;
+      split_planes16(reinterpret_cast<const uint4*>(codes)[c], bf16_round(scales[c >> 3]), inv, hi, lo);
+      reinterpret_cast<uint4*>(planes + r * I)[c] = hi;
+      reinterpret_cast<uint4*>(planes + plane + r * I)[c] = lo;
+    }
+    if (lane == 0) row_exp[r] = e;
+    __syncwarp();  // the stage is rewritten for the next row
   }
 }
 
@@ -792,8 +909,12 @@ __global__ void __launch_bounds__(kP2pWarps * 32) ep_dispatch_p2p_kernel(const v
 // (cap = tokens * topk), the place in the source's window where the return step sends GEMM
 // row pos.  A wait that gives up places nothing (m_indices and ret_slot keep the -1 the host
 // wrote).  fill: [E_local] counters, zeroed by the host.
+// Planes form (planes != nullptr; A and SA unused): each placed row is written as the GEMM's two
+// e4m3 planes (plane stride M_pad * H) with row_exp[pos] = E (cdg_split.cuh).
 __global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, int32_t* fill, uint8_t* A, float* SA,
-                                                             int32_t* m_indices, int32_t* ret_slot, PeerStep ps) {
+                                                             int32_t* m_indices, int32_t* ret_slot, PeerStep ps,
+                                                             uint8_t* planes = nullptr, int32_t* row_exp = nullptr,
+                                                             int64_t M_pad = 0) {
   constexpr int kMaxTopk = 32;
   __shared__ int64_t s_off[kFixedMaxExperts];
   __shared__ int32_t s_tot[kFixedMaxExperts];
@@ -868,6 +989,25 @@ __global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, in
       s_pos[warp][lane] = pos;
     }
     __syncwarp();
+    if (planes) {
+      const float* rs = reinterpret_cast<const float*>(in + H);
+      const int e = warp_plane_exponent(rs, H / 128, lane);
+      const float inv = ldexpf(1.0f, -e);
+      const int64_t plane = M_pad * H;
+      for (int64_t c = lane; c < H / 16; c += 32) {
+        uint4 hi, lo;
+        split_planes16(reinterpret_cast<const uint4*>(in)[c], bf16_round(rs[c >> 3]), inv, hi, lo);
+        for (int j = 0; j < topk; ++j) {
+          const int64_t p = s_pos[warp][j];
+          if (p < 0) continue;
+          reinterpret_cast<uint4*>(planes + p * H)[c] = hi;
+          reinterpret_cast<uint4*>(planes + plane + p * H)[c] = lo;
+        }
+      }
+      if (lane < topk && s_pos[warp][lane] >= 0) row_exp[s_pos[warp][lane]] = e;
+      __syncwarp();
+      continue;
+    }
     for (int64_t c = lane; c < H / 16; c += 32) {
       const uint4 v = reinterpret_cast<const uint4*>(in)[c];
       for (int j = 0; j < topk; ++j) {
@@ -1280,6 +1420,54 @@ int cdg_ep_quant_dispatch_local(const void* x, int32_t x_dtype, int64_t x_stride
   return cdg::launched();
 }
 
+int cdg_ep_quant_dispatch_local_planes(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids,
+                                       int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t H,
+                                       const int64_t* expert_off, int32_t* fill, uint8_t* planes, int32_t* row_exp,
+                                       int32_t* m_indices, int64_t M_pad, int32_t* perm_pos, int32_t* send_index,
+                                       cdg_stream_t stream) {
+  if (T < 0 || topk <= 0 || topk > 32 || E <= 0 || H <= 0 || H % 128 || M_pad < 0 || M_pad % 128 || !fill ||
+      !expert_off || (T > 0 && (!x || !topk_ids || !planes || !row_exp || !m_indices || !perm_pos || !send_index)))
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (x_dtype != CDG_DTYPE_BF16 && x_dtype != CDG_DTYPE_F32) return CDG_ERR_INVALID_ARGUMENT;
+  if (ids_dtype != CDG_DTYPE_I32 && ids_dtype != CDG_DTYPE_I64) return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || x_stride % 4 || reinterpret_cast<uintptr_t>(planes) % 16)
+    return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fill, 0, E * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (M_pad > 0 && cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (T == 0) return CDG_OK;
+  const size_t smem = static_cast<size_t>(cdg::kP2pWarps * cdg::row_stage_bytes(H));
+  if (smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(cdg::ep_quant_dispatch_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return CDG_ERR_CUDA;
+  const unsigned grid = static_cast<unsigned>((T + cdg::kP2pWarps - 1) / cdg::kP2pWarps);
+  cdg::ep_quant_dispatch_local_kernel<<<grid, cdg::kP2pWarps * 32, smem, st>>>(
+      x, x_dtype, x_stride, topk_ids, ids_dtype, T, topk, E, H, expert_off, fill, nullptr, nullptr, m_indices,
+      perm_pos, send_index, CDG_SCALE_FP32, planes, row_exp, M_pad);
+  return cdg::launched();
+}
+
+int cdg_silu_mul_quant_planes(const void* in, int64_t in_stride, int64_t M, int64_t I, const int32_t* m_indices,
+                              uint8_t* planes, int32_t* row_exp, cdg_stream_t stream) {
+  if (M < 0 || I <= 0 || I % 128 || (M > 0 && (!in || !planes || !row_exp))) return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(in) % 16 || in_stride % 8 || reinterpret_cast<uintptr_t>(planes) % 16)
+    return CDG_ERR_ALIGNMENT;
+  if (M == 0) return CDG_OK;
+  const size_t smem = 8 * static_cast<size_t>(cdg::row_stage_bytes(I));
+  if (smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(cdg::silu_mul_quant_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return CDG_ERR_CUDA;
+  const unsigned grid =
+      static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, int64_t(cdg::sm_count()) * 8)));
+  cdg::silu_mul_quant_planes_kernel<<<grid, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(in), in_stride, M, I, m_indices, planes, row_exp);
+  return cdg::launched();
+}
+
 int cdg_ep_unpermute_combine(const void* Y, int64_t y_stride, const int32_t* perm_pos, const int32_t* send_index,
                              const float* topk_w, int64_t T, int64_t topk, int64_t H, void* y, cdg_stream_t stream) {
   if (!perm_pos) return CDG_ERR_INVALID_ARGUMENT;
@@ -1402,6 +1590,26 @@ int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t max_tokens, int64_t 
   const int64_t R = ranks * max_tokens;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, 1184)));
   cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, A, SA, m_indices, ret_slot, ps);
+  return cdg::launched();
+}
+
+int cdg_ep_permute_p2p_planes(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H,
+                              int64_t E_local, int32_t* fill, uint8_t* planes, int32_t* row_exp, int32_t* m_indices,
+                              int64_t M_pad, int32_t* ret_slot, cdg_stream_t stream) {
+  if (!window || !cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || E_local <= 0 ||
+      E_local > cdg::kFixedMaxExperts || M_pad < ranks * max_tokens * topk + 127 * E_local || M_pad % 128 || !fill ||
+      !planes || !row_exp || !m_indices || !ret_slot)
+    return CDG_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(planes) % 16) return CDG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  if (cudaMemsetAsync(ret_slot, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::PeerStep ps = cdg::make_step(nullptr, window, 0, ranks, max_tokens, topk, H);
+  const int64_t R = ranks * max_tokens;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, 1184)));
+  cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, nullptr, nullptr, m_indices, ret_slot, ps, planes,
+                                                   row_exp, M_pad);
   return cdg::launched();
 }
 

@@ -45,14 +45,27 @@
 
 namespace cdg {
 
+#ifndef CDG_PLANES_KS
+#define CDG_PLANES_KS 2
+#endif
+#ifndef CDG_PLANES_STAGES
+#define CDG_PLANES_STAGES 3
+#endif
+#ifndef CDG_PLANES_KSF
+#define CDG_PLANES_KSF 4
+#endif
+#ifndef CDG_PLANES_SF_STAGES
+#define CDG_PLANES_SF_STAGES 3
+#endif
+
 struct PlanesSmem {
-  static constexpr int kKS = 2;                   // K steps per operand stage
-  static constexpr int kKSF = 4;                  // K steps per scale-atom stage
+  static constexpr int kKS = CDG_PLANES_KS;       // K steps per operand stage
+  static constexpr int kKSF = CDG_PLANES_KSF;     // K steps per scale-atom stage
   static constexpr int kW = 128 * 128;            // weight tile per K step (E2M1 unpacked to bytes)
   static constexpr int kA = kPlanesTileTok * 128;  // 56 tokens x 2 planes per K step
   static constexpr int kStep = kW + kA;
-  static constexpr int kStages = 3;
-  static constexpr int kSfStages = 3;
+  static constexpr int kStages = CDG_PLANES_STAGES;
+  static constexpr int kSfStages = CDG_PLANES_SF_STAGES;
   static constexpr int kStageBytes = kKS * kStep;
   static constexpr int kSfRing = kStages * kStageBytes;              // [kSfStages][kKSF] weight scale atoms
   static constexpr int kConstSf = kSfRing + kSfStages * kKSF * 512;  // 512 bytes of UE8M0 127

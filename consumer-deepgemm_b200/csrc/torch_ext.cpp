@@ -160,6 +160,37 @@ void grouped_gemm(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa
                  "m_grouped_fp8_fp4_gemm_nt_contiguous");
 }
 
+cdg_stream_t cur_stream(const torch::Tensor& t);
+
+// The GEMM on activations given as e4m3 planes [2, M, K] (uint8) with int32 row exponents [M]
+// (CDG_DTYPE_E4M3_PLANES): the form the MoE layer's own quantising steps write.
+void grouped_gemm_planes(const torch::Tensor& planes, const torch::Tensor& row_exp, const torch::Tensor& b,
+                         const torch::Tensor& sfb, const torch::Tensor& d, const torch::Tensor& ids, int64_t flags) {
+  TORCH_CHECK_VALUE(planes.is_cuda() && planes.dim() == 3 && planes.size(0) == 2 && planes.is_contiguous() &&
+                        planes.scalar_type() == torch::kUInt8,
+                    "planes: contiguous uint8 [2, M, K] on the device");
+  const int64_t M = planes.size(1);
+  TORCH_CHECK_VALUE(row_exp.is_cuda() && row_exp.scalar_type() == torch::kInt32 && row_exp.is_contiguous() &&
+                        row_exp.numel() == M,
+                    "row exponents: contiguous int32 [M]");
+  // the argument block of the hi plane as an e4m3 [M, K] operand, then switched to the planes form
+  const torch::Tensor hi = planes.select(0, 0).view(torch::kFloat8_e4m3fn);
+  cdg_gemm_args g = make_args(hi, row_exp.view({M, 1}), b, sfb, d, ids, flags);
+  g.a_dtype = CDG_DTYPE_E4M3_PLANES;
+  g.sa = reinterpret_cast<const float*>(row_exp.data_ptr());
+  g.sa_dtype = CDG_DTYPE_I32;
+  g.sa_stride_m = 1;
+  g.sa_stride_k = 1;
+  g.sa_cols = 1;
+  const c10::cuda::CUDAGuard guard(planes.device());
+  const size_t ws_bytes = cdg_grouped_fp8_fp4_workspace_bytes(&g);
+  TORCH_CHECK_VALUE(ws_bytes > 0, "invalid GEMM arguments for the planes form");
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes + 1024)}, planes.options());
+  auto* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 1023) & ~uintptr_t(1023));
+  check_status(cdg_grouped_fp8_fp4_gemm_nt_contiguous(&g, base, ws_bytes, cur_stream(planes)),
+               "m_grouped_fp8_fp4_gemm_nt_contiguous (planes)");
+}
+
 int64_t can_implement(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
                       const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids) {
   const cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, 0);
@@ -282,6 +313,45 @@ std::vector<torch::Tensor> ep_permute(const torch::Tensor& rows, int64_t H, int6
 }
 
 // One rank: quantise + contiguous layout in one pass -> (A, SA, m_indices, perm_pos, send_index).
+std::vector<torch::Tensor> silu_mul_quant_planes(const torch::Tensor& h, const torch::Tensor& m_indices) {
+  TORCH_CHECK(h.is_cuda() && h.dim() == 2 && h.stride(1) == 1 && h.scalar_type() == torch::kBFloat16,
+              "h must be a CUDA BF16 [M, 2I] tensor with unit last stride");
+  TORCH_CHECK(m_indices.scalar_type() == torch::kInt32 && m_indices.numel() == h.size(0), "m_indices must be int32 [M]");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int64_t M = h.size(0), I = h.size(1) / 2;
+  auto planes = torch::empty({2, M, I}, h.options().dtype(torch::kUInt8));
+  auto row_exp = torch::empty({M}, h.options().dtype(torch::kInt32));
+  check_status(cdg_silu_mul_quant_planes(h.data_ptr(), h.stride(0), M, I, m_indices.data_ptr<int32_t>(),
+                                         planes.data_ptr<uint8_t>(), row_exp.data_ptr<int32_t>(), cur_stream(h)),
+               "silu_mul_quant_planes");
+  return {planes, row_exp};
+}
+
+std::vector<torch::Tensor> ep_quant_dispatch_local_planes(const torch::Tensor& x, const torch::Tensor& ids, int64_t E,
+                                                          const torch::Tensor& expert_off, int64_t M_pad) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
+  TORCH_CHECK(ids.is_cuda() && ids.is_contiguous() && ids.dim() == 2 && ids.size(0) == x.size(0),
+              "topk ids must be contiguous [T, topk]");
+  TORCH_CHECK(expert_off.is_cuda() && expert_off.scalar_type() == torch::kInt64 && expert_off.numel() == E,
+              "expert_off: int64 [E] on the device");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), H = x.size(1), topk = ids.size(1);
+  auto i32 = ids.options().dtype(torch::kInt32);
+  auto planes = torch::empty({2, M_pad, H}, x.options().dtype(torch::kUInt8));
+  auto row_exp = torch::empty({M_pad}, i32);
+  auto mi = torch::empty({M_pad}, i32);
+  auto pos = torch::empty({T * topk}, i32);
+  auto send_index = torch::empty({T * topk}, i32);
+  auto fill = torch::empty({E}, i32);
+  check_status(cdg_ep_quant_dispatch_local_planes(x.data_ptr(), dtype_code(x), x.stride(0), ids.data_ptr(),
+                                                  dtype_code(ids), T, topk, E, H, expert_off.data_ptr<int64_t>(),
+                                                  fill.data_ptr<int32_t>(), planes.data_ptr<uint8_t>(),
+                                                  row_exp.data_ptr<int32_t>(), mi.data_ptr<int32_t>(), M_pad,
+                                                  pos.data_ptr<int32_t>(), send_index.data_ptr<int32_t>(), cur_stream(x)),
+               "ep_quant_dispatch_local_planes");
+  return {planes, row_exp, mi, pos, send_index};
+}
+
 std::vector<torch::Tensor> ep_quant_dispatch_local(const torch::Tensor& x, const torch::Tensor& ids, int64_t E,
                                                    const torch::Tensor& expert_off, int64_t M_pad, bool ue8m0) {
   TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.stride(1) == 1, "x must be a CUDA [T, H] tensor with unit last stride");
@@ -415,6 +485,23 @@ std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_
   return {A, SA, mi, ret_slot};
 }
 
+std::vector<torch::Tensor> ep_permute_p2p_planes(uint64_t window, int64_t ranks, int64_t max_tokens, int64_t topk,
+                                                 int64_t H, int64_t E_local, int64_t M_pad, const torch::Tensor& like) {
+  const c10::cuda::CUDAGuard guard(like.device());
+  auto i32 = like.options().dtype(torch::kInt32);
+  auto planes = torch::empty({2, M_pad, H}, like.options().dtype(torch::kUInt8));
+  auto row_exp = torch::empty({M_pad}, i32);
+  auto mi = torch::empty({M_pad}, i32);
+  auto ret_slot = torch::empty({M_pad}, i32);
+  auto fill = torch::empty({E_local}, i32);
+  check_status(cdg_ep_permute_p2p_planes(reinterpret_cast<void*>(window), ranks, max_tokens, topk, H, E_local,
+                                         fill.data_ptr<int32_t>(), planes.data_ptr<uint8_t>(),
+                                         row_exp.data_ptr<int32_t>(), mi.data_ptr<int32_t>(), M_pad,
+                                         ret_slot.data_ptr<int32_t>(), cur_stream(like)),
+               "ep_permute_p2p_planes");
+  return {planes, row_exp, mi, ret_slot};
+}
+
 void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& ret_slot, int64_t ranks, int64_t max_tokens,
                    int64_t topk, const torch::Tensor& peers, uint64_t window, int64_t me) {
   TORCH_CHECK(Y.is_cuda() && Y.dim() == 2 && Y.stride(1) == 1 && Y.scalar_type() == torch::kBFloat16, "Y: BF16 rows");
@@ -493,6 +580,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mk_alignment_for_contiguous_layout", []() { return cdg_mk_alignment_for_contiguous_layout(); });
   m.def("grouped_gemm", &grouped_gemm, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
         py::arg("m_indices"), py::arg("flags") = 0, py::arg("masked") = false);
+  m.def("grouped_gemm_planes", &grouped_gemm_planes, py::arg("planes"), py::arg("row_exp"), py::arg("b"),
+        py::arg("sfb"), py::arg("d"), py::arg("m_indices"), py::arg("flags") = 0);
   m.def("can_implement", &can_implement, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
         py::arg("m_indices"));
   m.def("transform_sf_atoms", &transform_sf_atoms, py::arg("sf"));
@@ -543,6 +632,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch_p2p", &ep_dispatch_p2p, py::arg("x"), py::arg("topk_ids"), py::arg("num_experts"),
         py::arg("ranks"), py::arg("max_tokens"), py::arg("peers"), py::arg("window"), py::arg("me"),
         py::arg("ue8m0") = false);
+  m.def("ep_permute_p2p_planes", &ep_permute_p2p_planes, py::arg("window"), py::arg("ranks"), py::arg("max_tokens"),
+        py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
+  m.def("ep_quant_dispatch_local_planes", &ep_quant_dispatch_local_planes, py::arg("x"), py::arg("topk_ids"),
+        py::arg("num_experts"), py::arg("expert_off"), py::arg("m_pad"));
+  m.def("silu_mul_quant_planes", &silu_mul_quant_planes, py::arg("h"), py::arg("m_indices"));
   m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("max_tokens"),
         py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
   m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("ret_slot"), py::arg("ranks"), py::arg("max_tokens"),

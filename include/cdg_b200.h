@@ -54,9 +54,19 @@ typedef enum cdg_dtype {
   CDG_DTYPE_UE8M0 = 4,  /* unsigned 8-bit power-of-two scale, value 2^(b-127) */
   CDG_DTYPE_I32 = 5,    /* int32 group ids */
   CDG_DTYPE_I64 = 6,    /* int64 group ids */
-  CDG_DTYPE_UE8M0_X4 = 7 /* int32 words of four UE8M0 activation scales: the scale of 128-wide K
+  CDG_DTYPE_UE8M0_X4 = 7, /* int32 words of four UE8M0 activation scales: the scale of 128-wide K
                             block kb is byte kb % 4 of word kb / 4 (the packed format of DeepGEMM's
                             UE8M0 recipe, e.g. vLLM's silu_mul_quant_fp8_packed) */
+  CDG_DTYPE_E4M3_PLANES = 8 /* activations given as the two e4m3 planes the tensor cores read: `a` is
+                               uint8 [2][M][K] (hi plane, then lo plane; a_row_stride = K, M a multiple
+                               of 128), `sa` is int32 [M] row exponents E (sa_dtype = CDG_DTYPE_I32),
+                               and row r stands for (hi + lo) * 2^E, the reference's BF16 dequant of an
+                               e4m3 row with FP32 1x128 scales as cdg_ep_* producers split it (see
+                               cdg_ep_quant_dispatch_local).  Per-row m_indices with 128-aligned groups
+                               only; a block with rows of several experts is left out and reported
+                               (CDG_ERR_DEVICE_TIMEOUT from cdg_device_status, bit 2).  Used by the MoE
+                               layer, whose own quantising steps write the planes, so the GEMM skips its
+                               plane split */
 } cdg_dtype;
 
 /* How the weight scales `sfb` are laid out. */
@@ -323,6 +333,29 @@ int cdg_ep_quant_dispatch_local(const void* x, int32_t x_dtype, int64_t x_stride
                                 const int64_t* expert_off, int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices,
                                 int64_t M_pad, int32_t* perm_pos, int32_t* send_index, int32_t scale_fmt,
                                 cdg_stream_t stream);
+
+/* Planes forms of the layer's quantising steps (FP32 1x128 recipe only): instead of e4m3 rows and
+ * their scales they write the two e4m3 planes the grouped GEMM reads, planes uint8 [2][M_pad][H]
+ * (plane stride M_pad * H; M_pad a multiple of 128), and int32 row exponents row_exp [M_pad], the split
+ * the GEMM's prep kernel would make of those rows (hi = e4m3(x / 2^E), lo = e4m3(x / 2^E - hi) with
+ * x = bf16(bf16(q) * bf16(s)) and E the frexp exponent of the row's largest |bf16(s)|).  Passed to the
+ * GEMM as a_dtype CDG_DTYPE_E4M3_PLANES they spare it the plane split (a read of the rows and a write
+ * of both planes).  Same row placement, m_indices, perm_pos / send_index and ret_slot as the row
+ * forms; the rows' values equal theirs bit for bit.
+ *   cdg_ep_quant_dispatch_local_planes  as cdg_ep_quant_dispatch_local
+ *   cdg_silu_mul_quant_planes           as cdg_silu_mul_quant_fp8 (rows 16-byte aligned; rows with a
+ *                                        negative m_indices entry are skipped)
+ *   cdg_ep_permute_p2p_planes           as cdg_ep_permute_p2p */
+int cdg_ep_quant_dispatch_local_planes(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids,
+                                       int32_t ids_dtype, int64_t T, int64_t topk, int64_t E, int64_t H,
+                                       const int64_t* expert_off, int32_t* fill, uint8_t* planes, int32_t* row_exp,
+                                       int32_t* m_indices, int64_t M_pad, int32_t* perm_pos, int32_t* send_index,
+                                       cdg_stream_t stream);
+int cdg_silu_mul_quant_planes(const void* in, int64_t in_stride, int64_t M, int64_t I, const int32_t* m_indices,
+                              uint8_t* planes, int32_t* row_exp, cdg_stream_t stream);
+int cdg_ep_permute_p2p_planes(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H,
+                              int64_t E_local, int32_t* fill, uint8_t* planes, int32_t* row_exp, int32_t* m_indices,
+                              int64_t M_pad, int32_t* ret_slot, cdg_stream_t stream);
 
 /* Fixed-capacity exchange (no host synchronisation).  The send (and receive) buffer holds
  * per destination (source) rank a region of 1 + cap packed rows of cdg_ep_row_bytes(H):

@@ -284,7 +284,7 @@ def test_layer_stages_match_reference_at_gemm_tolerance(ue8m0):
     x, ids, w, w1, w1s, w2, w2s = make_layer_inputs(**cfg)
     ops = _RecordingOps()
     layer = MoELayer(w1.to(DEV), w1s.to(DEV), w2.to(DEV), w2s.to(DEV), num_experts=cfg["experts"], ops=ops,
-                     ue8m0=ue8m0)
+                     ue8m0=ue8m0, planes=False)  # the row form: its stage inputs are the oracle's inputs
     layer(x.to(DEV), ids.to(DEV), w.to(DEV))
     torch.cuda.synchronize()
     ref_ops = TorchRefOps()
@@ -373,8 +373,9 @@ def test_layer_expert_parallel_two_gpus():
         assert f"EP_OK {mode}" in r.stdout, r.stdout[-3000:]
 
 
-@pytest.mark.parametrize("ue8m0", [False, True], ids=["fp32", "ue8m0"])
-def test_peer_exchange_two_ranks_on_one_gpu(ue8m0):
+@pytest.mark.parametrize("ue8m0,planes", [(False, False), (False, True), (True, False)],
+                         ids=["fp32", "fp32_planes", "ue8m0"])
+def test_peer_exchange_two_ranks_on_one_gpu(ue8m0, planes):
     """The peer-memory exchange kernels for two ranks whose windows both live on this GPU.
 
     Each step runs rank 0's and rank 1's calls in order on one stream (dispatch, dispatch,
@@ -406,14 +407,20 @@ def test_peer_exchange_two_ranks_on_one_gpu(ue8m0):
         for step in range(3):
             si = [C.ep_dispatch_p2p(x[tok[r]], ids[tok[r]].contiguous(), E, ranks, tpr, peers, own[r], r, ue8m0)
                   for r in range(ranks)]
-            placed = [C.ep_permute_p2p(own[r], ranks, tpr, topk, H, e_loc, m_pad, x) for r in range(ranks)]
+            permute = C.ep_permute_p2p_planes if planes else C.ep_permute_p2p
+            placed = [permute(own[r], ranks, tpr, topk, H, e_loc, m_pad, x) for r in range(ranks)]
             outs = []
             for r in range(ranks):
-                a, sa, mi, _ = placed[r]
+                a, sa, mi, _ = placed[r]  # planes form: (planes, row exponents, ...)
                 b1, s1, b2, s2 = shard[r]
-                h = ops.gemm(a, sa, b1, s1, mi, skip_ungrouped=True)
-                aq, asc = ops.act(h, mi, ue8m0)
-                outs.append(ops.gemm(aq, asc, b2, s2, mi, skip_ungrouped=True))
+                if planes:
+                    h = ops.gemm_planes(a, sa, b1, s1, mi, skip_ungrouped=True)
+                    pl, rexp = ops.act_planes(h, mi)
+                    outs.append(ops.gemm_planes(pl, rexp, b2, s2, mi, skip_ungrouped=True))
+                else:
+                    h = ops.gemm(a, sa, b1, s1, mi, skip_ungrouped=True)
+                    aq, asc = ops.act(h, mi, ue8m0)
+                    outs.append(ops.gemm(aq, asc, b2, s2, mi, skip_ungrouped=True))
             for r in range(ranks):
                 C.ep_return_p2p(outs[r], placed[r][3], ranks, tpr, topk, peers, own[r], r)
             y = torch.cat([C.ep_combine_p2p(own[r], si[r], w[tok[r]].float().contiguous(), ranks, tpr, H)
@@ -447,3 +454,36 @@ def test_count_offsets_match_host_layout():
         aligned = (ref + 127) // 128 * 128
         assert torch.equal(cnt.cpu().long(), ref)
         assert torch.equal(off.cpu(), torch.cumsum(aligned, 0) - aligned)
+
+
+def test_layer_planes_form_equals_rows_form():
+    """FP32 activation scales: the layer's quantising steps writing the GEMMs' activation planes
+    (the default) give the bits of the layer on e4m3 rows and scales."""
+    from consumer_deep_gemm.moe import MoELayer
+
+    cfg = dict(tokens=700, experts=8, hidden=512, inter=256, topk=2)
+    x, ids, w, w1, w1s, w2, w2s = (t.to(DEV) for t in make_layer_inputs(**cfg))
+    ids[3, 0] = -1
+    rows = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"], planes=False)
+    pl = MoELayer(w1, w1s, w2, w2s, num_experts=cfg["experts"])
+    assert pl.planes and not rows.planes
+    y_rows = rows(x, ids, w)
+    y_pl = pl(x, ids, w)
+    torch.cuda.synchronize()
+    assert torch.equal(y_pl.view(torch.int16), y_rows.view(torch.int16))
+
+
+def test_silu_mul_planes_equal_split_of_rows_form():
+    """cdg_silu_mul_quant_planes writes the split the GEMM would make of cdg_silu_mul_quant_fp8's
+    codes and scales; rows with a negative m_indices entry are left out."""
+    import test_gpu_parity as gp
+
+    C = _ext()
+    g = torch.Generator().manual_seed(17)
+    h = torch.randn(384, 2 * 640, generator=g).to(torch.bfloat16).to(DEV)
+    mi = torch.zeros(384, dtype=torch.int32, device=DEV)
+    mi[250:] = -1
+    q, s = C.silu_mul_quant(h, mi, False)
+    planes, rexp = C.silu_mul_quant_planes(h, mi)
+    ref_planes, ref_exp = gp._torch_planes(q[:250], s[:250])
+    assert torch.equal(planes[:, :250], ref_planes) and torch.equal(rexp[:250], ref_exp)

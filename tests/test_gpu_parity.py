@@ -425,6 +425,43 @@ def test_round_weight_scales_flag_uses_the_references_rounding():
     assert torch.equal(d_r.view(torch.int16), d_c.view(torch.int16))
 
 
+def _torch_planes(a, sa):
+    """The two e4m3 activation planes and row exponents the GEMM forms from e4m3 rows with FP32
+    1x128 scales: x = bf16(bf16(a) * bf16(s)), E = frexp exponent of the row's largest |bf16(s)|,
+    hi = e4m3(x / 2^E), lo = e4m3(x / 2^E - hi)."""
+    m, k = a.shape
+    sb = sa.to(torch.bfloat16)
+    x = (a.to(torch.bfloat16).view(m, k // 128, 128) * sb.unsqueeze(-1)).view(m, k)
+    smax = sb.float().abs().nan_to_num(0.0, 0.0, 0.0).amax(dim=1)
+    e = torch.where(smax > 0, torch.frexp(smax).exponent, torch.zeros_like(smax, dtype=torch.int32))
+    v = x.float() * torch.exp2(-e.float()).unsqueeze(1)
+    hi = v.to(torch.float8_e4m3fn)
+    lo = (v - hi.float()).to(torch.float8_e4m3fn)
+    return torch.stack([hi.view(torch.uint8), lo.view(torch.uint8)]).contiguous(), e.to(torch.int32).contiguous()
+
+
+@pytest.mark.parametrize("name", ["c0", "edge_block_classes", "kat_vllm_padding_zero"])
+def test_planes_form_equals_rows_form(name):
+    """CDG_DTYPE_E4M3_PLANES: the GEMM on activation planes made outside it (as the MoE layer's
+    quantising steps make them) gives the bits of the call on the e4m3 rows and scales."""
+    from consumer_deep_gemm import native
+
+    c = load_gemm_case(name)
+    if c["a"].dtype != torch.float8_e4m3fn or c["a"].shape[0] % 128 or c["b"].shape[1] % 128 or \
+            c["a"].shape[1] % 128 or c["sb"].dtype != torch.uint8 or c["m_indices"] is None or \
+            c["m_indices"].numel() != c["a"].shape[0]:
+        pytest.skip("outside the planes form's envelope")
+    a, sa, b, sb, ids = (c[k].to(DEV) for k in ("a", "sa", "b", "sb", "m_indices"))
+    d_rows = torch.full((a.shape[0], b.shape[1]), float("nan"), dtype=torch.bfloat16, device=DEV)
+    cabi.gemm(a, sa.float(), b, sb, d_rows, ids)
+    planes, rexp = _torch_planes(a, sa.float())
+    d_pl = torch.full_like(d_rows, float("nan"))
+    native.require().grouped_gemm_planes(planes, rexp, b, sb, d_pl, ids.to(torch.int32).contiguous(), 0)
+    torch.cuda.synchronize()
+    assert torch.equal(d_pl.view(torch.int16), d_rows.view(torch.int16))
+    assert cabi.device_status() == (0, 0)
+
+
 def test_mega_moe_transform_bytes_match_reference():
     import numpy as np
 
