@@ -21,7 +21,12 @@ Accepted forms (as in the reference):
              int32 output of ``transform_sf_into_required_layout``, or absent (1.0)
   m_indices  int32/int64 per-row ids (-1 = padding), psum ends (length G), or None (G == 1)
   kwargs     ``recipe_a=(1,128)``, ``recipe_b=(1,32)``, ``disable_ue8m0_cast`` (accepted;
-             the FP32 activation scales are always used exactly)
+             the FP32 activation scales are always used exactly).  Library-internal ones:
+             ``_skip_ungrouped_rows`` (leave rows outside every group unwritten),
+             ``_round_weight_scales`` (float weight scales rounded to powers of two),
+             ``_force_exact_path`` (the SIMT kernel), ``_d_rows`` (int64 [M] device
+             addresses: row r of D is stored at ``_d_rows[r]``, 0 = not stored; ``d`` then
+             only gives the shape, e.g. an expanded [1, N] BF16 view)
 """
 
 from __future__ import annotations
@@ -133,7 +138,7 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(a, b, d, m_indices=None, **kwargs) -> N
     x, sa, bt, bs, d, ids = _normalize(a, b, d, m_indices)
     flags = ((1 if kwargs.get("_force_exact_path") else 0) | (4 if kwargs.get("_skip_ungrouped_rows") else 0) |
              (8 if kwargs.get("_round_weight_scales") else 0))
-    native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags)
+    native.require().grouped_gemm(x, sa, bt, bs, d, ids, flags, False, kwargs.get("_d_rows"))
     if _CHECK_STATUS:
         native.check_device_status()
 

@@ -56,6 +56,14 @@ from .layout import transform_sf_into_required_layout
 ALIGN = 128
 
 
+def _output(m, n, device, d_rows):
+    """The GEMM's BF16 [m, n] output, or, when a row table routes the rows elsewhere, a
+    [1, n] placeholder expanded to [m, n] that only gives the shape."""
+    if d_rows is None:
+        return torch.empty(m, n, dtype=torch.bfloat16, device=device)
+    return torch.empty(1, n, dtype=torch.bfloat16, device=device).expand(m, n)
+
+
 class NativeOps:
     """Device kernels of libcdg_b200.so through the torch binding."""
 
@@ -71,10 +79,10 @@ class NativeOps:
     def act_planes(self, h, m_indices):
         return self.C.silu_mul_quant_planes(h, m_indices)
 
-    def gemm_planes(self, planes, row_exp, w, w_sf, m_indices, skip_ungrouped=False):
-        d = torch.empty(planes.shape[1], w.shape[1], dtype=torch.bfloat16, device=planes.device)
-        self.C.grouped_gemm_planes(planes, row_exp, w, w_sf, d, m_indices, 4 if skip_ungrouped else 0)
-        return d
+    def gemm_planes(self, planes, row_exp, w, w_sf, m_indices, skip_ungrouped=False, d_rows=None):
+        d = _output(planes.shape[1], w.shape[1], planes.device, d_rows)
+        self.C.grouped_gemm_planes(planes, row_exp, w, w_sf, d, m_indices, 4 if skip_ungrouped else 0, d_rows)
+        return None if d_rows is not None else d
 
     def quant(self, x, ue8m0=False):
         return self.C.quant_fp8_rows(x, ue8m0)
@@ -100,10 +108,11 @@ class NativeOps:
     def permute_fixed(self, rows, hidden, local_experts, ranks, cap, m_pad):
         return self.C.ep_permute_fixed(rows, hidden, local_experts, ranks, cap, m_pad)
 
-    def gemm(self, a, sa, w, w_sf, m_indices, skip_ungrouped=False):
-        d = torch.empty(a.shape[0], w.shape[1], dtype=torch.bfloat16, device=a.device)
-        m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices, _skip_ungrouped_rows=skip_ungrouped)
-        return d
+    def gemm(self, a, sa, w, w_sf, m_indices, skip_ungrouped=False, d_rows=None):
+        d = _output(a.shape[0], w.shape[1], a.device, d_rows)
+        m_grouped_fp8_fp4_gemm_nt_contiguous((a, sa), (w, w_sf), d, m_indices, _skip_ungrouped_rows=skip_ungrouped,
+                                             _d_rows=d_rows)
+        return None if d_rows is not None else d
 
     def act(self, h, m_indices, ue8m0=False):
         return self.C.silu_mul_quant(h, m_indices, ue8m0)
@@ -178,7 +187,7 @@ class MoELayer:
 
     def __init__(self, w1, w1_scale, w2=None, w2_scale=None, num_experts: int = 0, group=None, ops=None,
                  max_tokens_per_rank: int | None = None, exchange: str = "nccl", ue8m0: bool = False,
-                 planes: bool | None = None):
+                 planes: bool | None = None, fused_return: bool = True):
         self.ops = ops or NativeOps()
         self.ue8m0 = bool(ue8m0)
         # FP32 activation scales: the quantising steps write the GEMMs' activation planes directly
@@ -191,6 +200,9 @@ class MoELayer:
         if exchange == "p2p" and max_tokens_per_rank is None:
             raise ValueError("the peer-memory exchange needs max_tokens_per_rank (fixed capacity)")
         self.exchange = exchange
+        # peer exchange: FC2's epilogue stores each row straight into its source's window
+        # (the GEMM's row table) instead of a separate return kernel
+        self.fused_return = bool(fused_return)
         self.windows = None
         self.group = group
         if group is not None:
@@ -215,7 +227,8 @@ class MoELayer:
         self.out_dim = w2.shape[1] if w2 is not None else w1.shape[1]
         self.inter = w1.shape[1] // 2
         # optional callable(name), called after each step of a forward has been launched
-        # (dispatch, permute, fc1, act, fc2, return, combine): a profiler records CUDA events
+        # (dispatch, permute, fc1, act, fc2, return, combine; no return with the fused return):
+        # a profiler records CUDA events
         # there to split the step's device time by phase
         self.on_phase = None
 
@@ -224,7 +237,8 @@ class MoELayer:
             self.on_phase(name)
 
     def status(self) -> int:
-        """0, or CDG_ERR_DEVICE_TIMEOUT (6) when one of this process's device waits gave up
+        """0, CDG_ERR_DEVICE_INDEX (9) when a kernel skipped an access it could not make, or
+        CDG_ERR_DEVICE_TIMEOUT (6) when one of this process's device waits gave up
         since the last call: a wait on another rank's exchange flag (this layer's window) or a
         GEMM pipeline wait.  Synchronises the device and clears the library's record."""
         st = self.windows.status() if self.windows is not None else 0
@@ -307,17 +321,19 @@ class MoELayer:
         self._phase("combine")
         return y
 
-    def _act_fc2(self, h, m_indices):
-        """SiLU-mul + requant of FC1's rows, then FC2 (rows outside every group left unwritten)."""
+    def _act_fc2(self, h, m_indices, d_rows=None):
+        """SiLU-mul + requant of FC1's rows, then FC2 (rows outside every group left unwritten;
+        with ``d_rows``, row r is stored at address d_rows[r] and nothing is returned)."""
         ops = self.ops
+        route = {} if d_rows is None else {"d_rows": d_rows}
         if self.planes:
             pl, rexp = ops.act_planes(h, m_indices)
             self._phase("act")
-            out = ops.gemm_planes(pl, rexp, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+            out = ops.gemm_planes(pl, rexp, self.w2, self.w2_sf, m_indices, skip_ungrouped=True, **route)
         else:
             aq, asc = ops.act(h, m_indices, self.ue8m0)
             self._phase("act")
-            out = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True)
+            out = ops.gemm(aq, asc, self.w2, self.w2_sf, m_indices, skip_ungrouped=True, **route)
         self._phase("fc2")
         return out
 
@@ -362,21 +378,30 @@ class MoELayer:
                                        self.ue8m0)
         self._phase("dispatch")
         m_pad = (world * cap + 127 * E_loc + ALIGN - 1) // ALIGN * ALIGN
+        # fused return: the permute also writes FC2's row table (each row's place in its source's
+        # window), FC2 stores there, and the combine raises this rank's return flags
+        fused = self.fused_return and self.w2 is not None
+        table_peers = win.peers if fused else None
         if self.planes:
-            pl, rexp, m_indices, ret_slot = C.ep_permute_p2p_planes(win.own, world, self.max_tokens, topk, H, E_loc,
-                                                                    m_pad, x)
+            pl, rexp, m_indices, ret_slot, ret_rows = C.ep_permute_p2p_planes(
+                win.own, world, self.max_tokens, topk, H, E_loc, m_pad, x, table_peers)
             self._phase("permute")
             h = self.ops.gemm_planes(pl, rexp, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         else:
-            a, sa, m_indices, ret_slot = C.ep_permute_p2p(win.own, world, self.max_tokens, topk, H, E_loc, m_pad, x)
+            a, sa, m_indices, ret_slot, ret_rows = C.ep_permute_p2p(win.own, world, self.max_tokens, topk, H, E_loc,
+                                                                    m_pad, x, table_peers)
             self._phase("permute")
             h = self.ops.gemm(a, sa, self.w1, self.w1_sf, m_indices, skip_ungrouped=True)
         self._phase("fc1")
-        if self.w2 is not None:
-            h = self._act_fc2(h, m_indices)
-        C.ep_return_p2p(h, ret_slot, world, self.max_tokens, topk, win.peers, win.own, me)
-        self._phase("return")
-        y = C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, self.max_tokens, H)
+        if fused:
+            self._act_fc2(h, m_indices, d_rows=ret_rows)
+        else:
+            if self.w2 is not None:
+                h = self._act_fc2(h, m_indices)
+            C.ep_return_p2p(h, ret_slot, world, self.max_tokens, topk, win.peers, win.own, me)
+            self._phase("return")
+        y = C.ep_combine_p2p(win.own, send_index, topk_w.to(torch.float32).contiguous(), world, self.max_tokens, H,
+                             table_peers, me)
         self._phase("combine")
         return y
 

@@ -82,10 +82,13 @@ def m_grouped_fp8_fp4_gemm_nt_contiguous(*args, **kwargs):
 def read_device_status(clear: bool = True) -> tuple[int, int]:
     """Device-side errors of the library's kernels on the current device since the last clear.
 
-    Synchronises the device, then returns ``(status, where)``: status 0, or 6
+    Synchronises the device, then returns ``(status, where)``: status 0; 6
     (``CDG_ERR_DEVICE_TIMEOUT``) when a bounded wait gave up -- a GEMM pipeline wait, or a
-    wait on another rank's flag in the peer-memory exchange -- and ``where``, the first such
-    wait's code (0 when none; layout in ``cdg_device_status``).  The GEMM calls themselves
+    wait on another rank's flag in the peer-memory exchange; or 9 (``CDG_ERR_DEVICE_INDEX``)
+    when no wait gave up but a kernel skipped an access it could not make (rows that do not
+    match their exchange header, a block the planes form cannot run, a misaligned D row
+    address) -- and ``where``, the first recorded code (0 when none; layout in
+    ``cdg_device_status``).  The GEMM calls themselves
     never synchronise, so a caller that wants to know checks here (after a batch of calls,
     or every call with ``CDG_CHECK_STATUS=1``).
     """
@@ -97,5 +100,7 @@ def check_device_status() -> None:
     """``read_device_status()``, raising ``RuntimeError`` when a device wait gave up."""
     st, where = read_device_status(True)
     if st:
-        raise RuntimeError(f"a device wait of consumer_deep_gemm gave up (status {st}, wait code {where:#010x}); "
+        what = "a device wait of consumer_deep_gemm gave up" if st == 6 else \
+            "a consumer_deep_gemm kernel skipped an access it could not make"
+        raise RuntimeError(f"{what} (status {st}, code {where:#010x}); "
                            "the outputs of the calls since the last check are not valid")

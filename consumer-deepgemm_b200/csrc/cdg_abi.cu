@@ -113,7 +113,8 @@ int validate(const cdg_gemm_args* g) {
       g->E > (int64_t(1) << 20))
     return CDG_ERR_UNSUPPORTED;
   if (g->K % 2) return CDG_ERR_INVALID_ARGUMENT;
-  if (g->M > 0 && (!g->a || !g->d)) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->M > 0 && (!g->a || (!g->d && !g->d_rows))) return CDG_ERR_INVALID_ARGUMENT;
+  if (g->d_rows && g->d_dtype != CDG_DTYPE_BF16) return CDG_ERR_INVALID_ARGUMENT;
   if (!g->b || !g->sfb) return CDG_ERR_INVALID_ARGUMENT;
   if (g->a_dtype != CDG_DTYPE_E4M3 && g->a_dtype != CDG_DTYPE_BF16 && g->a_dtype != CDG_DTYPE_F32 &&
       g->a_dtype != CDG_DTYPE_E4M3_PLANES)
@@ -415,6 +416,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ga.d = g->d;
   ga.d_dtype = g->d_dtype;
   ga.d_row_stride = g->d_row_stride;
+  ga.d_rows = g->d_rows;
   ga.M = static_cast<int>(g->M);
   ga.N = static_cast<int>(g->N);
   ga.K = static_cast<int>(g->K);
@@ -505,6 +507,7 @@ int run(const cdg_gemm_args* g, void* workspace, size_t workspace_bytes, cudaStr
   ka.tok_atoms = reinterpret_cast<uint32_t*>(ws + wl.tok_atoms);
   ka.d = static_cast<__nv_bfloat16*>(g->d);
   ka.d_row_stride = g->d_row_stride;
+  ka.d_rows = g->d_rows;
   ka.M = static_cast<int>(g->M);
   ka.N = static_cast<int>(g->N);
   ka.K = static_cast<int>(g->K);
@@ -643,7 +646,7 @@ int cdg_read_device_status(const void* workspace, cdg_stream_t stream) {
       cudaSuccess)
     return CDG_ERR_CUDA;
   if (cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess) return CDG_ERR_CUDA;
-  return (word & cdg::kStatusTimeout) ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
+  return (word & cdg::kStatusTimeout) ? CDG_ERR_DEVICE_TIMEOUT : word ? CDG_ERR_DEVICE_INDEX : CDG_OK;
 }
 
 }  // extern "C"
@@ -665,7 +668,8 @@ int cdg_device_status(int32_t clear, int32_t* where) {
   const int st = cdg::ep_sticky_status(clear, ep);
   if (st != CDG_OK) return st;
   if (where) *where = gemm[1] ? gemm[1] : ep[1];
-  return (gemm[0] | ep[0]) ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
+  const int bits = gemm[0] | ep[0];
+  return (bits & cdg::kStatusTimeout) ? CDG_ERR_DEVICE_TIMEOUT : bits ? CDG_ERR_DEVICE_INDEX : CDG_OK;
 }
 
 int cdg_set_num_sms(int32_t num_sms) {
@@ -717,6 +721,7 @@ const char* cdg_status_string(int status) {
     case CDG_ERR_NO_SM100: return "device is not compute capability 10.x (B200)";
     case CDG_ERR_SCRATCH_TOO_SMALL:
       return "problem needs more workspace than the 64 MiB static scratch of the no-allocation entry point";
+    case CDG_ERR_DEVICE_INDEX: return "a kernel skipped an access outside its buffer or misaligned";
     default: return "unknown status";
   }
 }

@@ -357,7 +357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * L::kAccCols;
-      __nv_bfloat16* dcol = p.d + nt * 128 + q * 32;
+      const int dcol = nt * 128 + q * 32;
       for (int c0 = half; c0 < nchunk; c0 += 4) {
         uint32_t ra[2][8], rb[2][8];  // lanes 0-15 and 16-31 of the quadrant, chunks c0 and c0 + 2
 #pragma unroll
@@ -397,7 +397,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if ((word >> (br & 31)) & 1u)
                   v = *reinterpret_cast<const uint4*>(wst + rr * 64 + ((part ^ ((rr >> 1) & 3)) << 4));
-                *reinterpret_cast<uint4*>(dcol + static_cast<int64_t>(drow0 + tok) * p.d_row_stride + part * 8) = v;
+                __nv_bfloat16* rp = d_row(p, static_cast<int64_t>(drow0 + tok));
+                if (rp) *reinterpret_cast<uint4*>(rp + dcol + part * 8) = v;
               }
             }
             __syncwarp();
@@ -420,12 +421,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
         const uint4 z = make_uint4(0, 0, 0, 0);
         for (int cc = tid; cc < rows * 16; cc += kEpiThreads) {
           const int r = r_first + (cc >> 4);
-          *reinterpret_cast<uint4*>(p.d + static_cast<int64_t>(r) * p.d_row_stride + nt * 128 + (cc & 15) * 8) = z;
+          __nv_bfloat16* rp = d_row(p, r);
+          if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + (cc & 15) * 8) = z;
         }
       }
     }
   }
 
+  if (p.d_rows) __threadfence_system();  // rows stored into other GPUs' memory
   tc_fence_before();
   const int any_fail = __syncthreads_or(!ok);
   cluster_sync();  // no CTA releases TMEM or exits while its pair still uses it

@@ -235,6 +235,7 @@ __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
 // of block b; CTA (b, 0) also publishes the block's plan, and the last of those
 // orders the blocks of each class into lists.
 constexpr int kPrepK = 1024;
+constexpr int kContBits = 16384;  // blocks whose run-continuation bits the last prep CTA keeps in shared memory
 
 template <typename IdT>
 __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ float s_inv[128];              // 2^-E of each row
   __shared__ uint32_t s_smax_bits[128];     // bits of the largest finite |bf16(sa)| of each row
   __shared__ int s_cls_count[kNumClasses][257];
+  __shared__ uint32_t s_cont[kContBits / 32];  // last CTA: which blocks continue a run (bitmask)
   __shared__ int s_tile_count[257];
   __shared__ int s_dtile_count[257];
   const int b = blockIdx.x;
@@ -462,7 +464,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   // A run of S rows is cut into the fewest tiles, n = ceil(S / kPlanesTileTok), of
   // T = ceil16(S / n) rows each (the last one shorter): a tile costs the kernel about the
   // same time at any width, so fewer tiles is faster, and equal widths spread the MMA work.
-  auto continues = [&](int i) -> bool {  // block i extends the run of block i - 1 (same class)
+  auto continues_g = [&](int i) -> bool {  // block i extends the run of block i - 1 (same class)
     if (i == 0) return false;
     const int4 a = __ldcg(&p.blk_info[i - 1]), c = __ldcg(&p.blk_info[i]);
     if ((c.z != kClassWide && c.z != kClassWideDirect) || a.z != c.z || a.x != c.x || a.y != 128) return false;
@@ -470,6 +472,20 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     p.tm.rows(i - 1, r0a, na);
     p.tm.rows(i, r0c, nc);
     return na == 128 && r0c == r0a + 128;
+  };
+  // The "continues" bit of every block, computed once by all threads (independent loads) into a
+  // shared bitmask, so that the run walks below read shared memory instead of chaining global
+  // loads (up to kContBits blocks; beyond, the bits are recomputed from global memory).
+  const bool cached = p.nblk <= kContBits;
+  if (cached) {
+    for (int w = tid; w < (p.nblk + 31) / 32; w += blockDim.x) s_cont[w] = 0u;
+    __syncthreads();
+    for (int i = tid; i < p.nblk; i += blockDim.x)
+      if (continues_g(i)) atomicOr(&s_cont[i >> 5], 1u << (i & 31));
+    __syncthreads();
+  }
+  auto continues = [&](int i) -> bool {
+    return cached ? ((s_cont[i >> 5] >> (i & 31)) & 1u) != 0u : continues_g(i);
   };
   auto run_span = [&](int i) -> int {  // rows spanned by the run that starts at block i
     int j = i;
@@ -581,7 +597,24 @@ struct GemmArgs {
   int do_zero_blocks;
   int fill_rest;          // 1: zero the block's rows past its last routed row
   int* status;
+  const uint64_t* d_rows;  // optional: D row r goes to the address d_rows[r] (not written when 0)
 };
+
+// Start of D row r: d + r * d_row_stride, or the address the row table lists (nullptr: the row
+// is not written; an address that is not 16-byte aligned is not written either and raises
+// kStatusBadIndex).
+__device__ __forceinline__ __nv_bfloat16* d_row(const GemmArgs& p, int64_t r) {
+  if (p.d_rows) {
+    const uint64_t a = __ldg(p.d_rows + r);
+    if (a & 15) {
+      atomicOr(p.status, kStatusBadIndex);
+      atomicOr(&g_sticky_status[0], kStatusBadIndex);
+      return nullptr;
+    }
+    return reinterpret_cast<__nv_bfloat16*>(a);
+  }
+  return p.d + r * p.d_row_stride;
+}
 
 // Token scale atoms of the direct tiles, written by the kernel that runs before
 // cdg_gemm_direct_kernel (the planes kernel, all its threads).  For tile i (list order) and
@@ -811,7 +844,8 @@ __global__ void __launch_bounds__(256, 1)
             const float sc = __shfl_sync(0xffffffffu, my_scale, (j0 & 31) + j);
             if (rb < nrows) {
               const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
-              p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
+              __nv_bfloat16* rp = d_row(p, r);
+              if (rp) rp[n] = __float2bfloat16_rn(x);
             }
           }
         }
@@ -824,11 +858,13 @@ __global__ void __launch_bounds__(256, 1)
       const uint4 z = make_uint4(0, 0, 0, 0);
       for (int c = tid; c < rows * 16; c += 128) {
         const int r = row0 + zero_from + (c >> 4);
-        *reinterpret_cast<uint4*>(p.d + r * p.d_row_stride + nt * 128 + (c & 15) * 8) = z;
+        __nv_bfloat16* rp = d_row(p, r);
+        if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + (c & 15) * 8) = z;
       }
     }
   }
 
+  if (p.d_rows) __threadfence_system();  // rows stored into other GPUs' memory
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -872,6 +908,7 @@ struct GenericArgs {
   TileMap tm;        // rows of each block
   const int4* list;  // nullptr: every block; else the listed blocks ({block, ...})
   const int* count;  // number of listed blocks (device)
+  const uint64_t* d_rows;  // optional row table, as in GemmArgs (BF16 output)
 };
 
 __constant__ float kE2M1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
@@ -933,12 +970,21 @@ __global__ void __launch_bounds__(256) cdg_generic_kernel(GenericArgs p) {
           if (k + 1 < p.K) acc = fmaf(s_row[k + 1], bf16r(kE2M1[byte >> 4] * sc), acc);
         }
       }
-      if (p.d_dtype == CDG_DTYPE_BF16)
+      if (p.d_rows) {
+        const uint64_t a = __ldg(p.d_rows + r);
+        if (a & 15) {
+          atomicOr(&g_sticky_status[0], kStatusBadIndex);
+        } else if (a) {
+          reinterpret_cast<__nv_bfloat16*>(a)[n] = __float2bfloat16_rn(acc);
+        }
+      } else if (p.d_dtype == CDG_DTYPE_BF16) {
         static_cast<__nv_bfloat16*>(p.d)[r * p.d_row_stride + n] = __float2bfloat16_rn(acc);
-      else
+      } else {
         static_cast<float*>(p.d)[r * p.d_row_stride + n] = acc;
+      }
     }
   }
+  if (p.d_rows) __threadfence_system();  // rows stored into other GPUs' memory
 }
 
 }  // namespace cdg

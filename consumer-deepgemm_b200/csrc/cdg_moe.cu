@@ -907,14 +907,17 @@ __global__ void __launch_bounds__(kP2pWarps * 32) ep_dispatch_p2p_kernel(const v
 // below the header's row count) reads the row once and writes it into the group of each of
 // its slots' local experts: A, SA, m_indices, and ret_slot[pos] = src * cap + t * topk + j
 // (cap = tokens * topk), the place in the source's window where the return step sends GEMM
-// row pos.  A wait that gives up places nothing (m_indices and ret_slot keep the -1 the host
-// wrote).  fill: [E_local] counters, zeroed by the host.
+// row pos.  With ret_rows (and ps.peers) set, ret_rows[pos] also gets that place's address
+// (the source's window, return rows of the step's parity, slot t * topk + j): the row table of
+// an FC2 GEMM that stores its rows straight into the sources' windows (cdg_gemm_args.d_rows).
+// A wait that gives up places nothing (m_indices and ret_slot keep the -1, ret_rows the 0 the
+// host wrote).  fill: [E_local] counters, zeroed by the host.
 // Planes form (planes != nullptr; A and SA unused): each placed row is written as the GEMM's two
 // e4m3 planes (plane stride M_pad * H) with row_exp[pos] = E (cdg_split.cuh).
 __global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, int32_t* fill, uint8_t* A, float* SA,
-                                                             int32_t* m_indices, int32_t* ret_slot, PeerStep ps,
-                                                             uint8_t* planes = nullptr, int32_t* row_exp = nullptr,
-                                                             int64_t M_pad = 0) {
+                                                             int32_t* m_indices, int32_t* ret_slot, uint64_t* ret_rows,
+                                                             PeerStep ps, uint8_t* planes = nullptr,
+                                                             int32_t* row_exp = nullptr, int64_t M_pad = 0) {
   constexpr int kMaxTopk = 32;
   __shared__ int64_t s_off[kFixedMaxExperts];
   __shared__ int32_t s_tot[kFixedMaxExperts];
@@ -924,6 +927,7 @@ __global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, in
   const int64_t ranks = ps.win.ranks, tokens = ps.win.tokens, topk = ps.win.topk, H = ps.win.H, rb = ps.win.rb;
   const int64_t cap = tokens * topk;
   const int32_t epoch = ps.epoch();
+  const int64_t ret_off = ps.win.ret_parity(epoch & 1);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (!wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kDispatchFlags), static_cast<int>(ranks),
                        epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 8))
@@ -979,7 +983,9 @@ __global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, in
         if (k < s_tot[el] && t >= 0 && t < tokens) {  // inside the expert's group as the headers sized it
           pos = s_off[el] + k;
           m_indices[pos] = el;
-          ret_slot[pos] = static_cast<int32_t>(src * cap + static_cast<int64_t>(t) * topk + lane);
+          const int64_t slot = static_cast<int64_t>(t) * topk + lane;
+          ret_slot[pos] = static_cast<int32_t>(src * cap + slot);
+          if (ret_rows) ret_rows[pos] = ps.peers[src] + ret_off + slot * H * 2;
         } else {
           atomicOr(reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 2);
           atomicOr(&g_ep_sticky_status[0], 2);
@@ -1078,7 +1084,10 @@ __global__ void ep_unpermute_kernel(const __nv_bfloat16* Y, int64_t y_stride, co
 // Peer variant (ps.own != nullptr; `rows` unused): the returned rows are the own window's
 // return rows for the step's parity, indexed by slot; first waits until every rank returned
 // its rows (a wait that gives up writes the token's output as zeros); the last CTA then
-// advances the window's step counter (scratch: [1] ticket, zeroed by the host).
+// advances the window's step counter (scratch: [2] tickets, zeroed by the host).  With
+// ps.peers set, the first CTA to run first raises this rank's return flag in every rank's
+// window: the rows this rank owes were stored into the windows by the FC2 GEMM before this
+// kernel (its epilogue stores through a row table, ending with a system-scope fence).
 constexpr int kCombineMaxTopk = 32;
 
 template <bool VEC>
@@ -1090,6 +1099,14 @@ __global__ void ep_combine_kernel(const __nv_bfloat16* rows, int64_t row_stride,
   if (ps.own) {
     epoch = ps.epoch();
     rows = reinterpret_cast<const __nv_bfloat16*>(ps.own + ps.win.ret_parity(epoch & 1));
+    if (ps.peers && threadIdx.x == 0 && atomicAdd(scratch + 1, 1) == 0) {
+      // a ticket rather than blockIdx 0: the CTA that raises is one that runs, whichever order
+      // the CTAs start in (the others wait for these flags too)
+      __threadfence_system();
+      for (int64_t r = 0; r < ps.win.ranks; ++r)
+        st_release_sys(
+            reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ps.peers[r]) + Window::kReturnFlags) + ps.me, epoch);
+    }
     ok = wait_peer_flags(reinterpret_cast<const int32_t*>(ps.own + Window::kReturnFlags),
                          static_cast<int>(ps.win.ranks), epoch, reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 9);
     if (!ok && blockIdx.x < T) {
@@ -1542,7 +1559,7 @@ int cdg_ep_window_status(const void* window, cdg_stream_t stream) {
                       st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess)
     return CDG_ERR_CUDA;
-  return word ? CDG_ERR_DEVICE_TIMEOUT : CDG_OK;
+  return (word & 1) ? CDG_ERR_DEVICE_TIMEOUT : word ? CDG_ERR_DEVICE_INDEX : CDG_OK;
 }
 
 int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const void* topk_ids, int32_t ids_dtype,
@@ -1576,40 +1593,43 @@ int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const 
 
 int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, int64_t E_local,
                        int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* ret_slot,
-                       cdg_stream_t stream) {
+                       const uint64_t* peers, uint64_t* ret_rows, cdg_stream_t stream) {
   if (!window || !cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || E_local <= 0 ||
       E_local > cdg::kFixedMaxExperts || M_pad < ranks * max_tokens * topk + 127 * E_local || !fill || !A || !SA ||
-      !m_indices || !ret_slot)
+      !m_indices || !ret_slot || (ret_rows && !peers))
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(A) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(ret_slot, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  const cdg::PeerStep ps = cdg::make_step(nullptr, window, 0, ranks, max_tokens, topk, H);
+  if (ret_rows && cudaMemsetAsync(ret_rows, 0, M_pad * sizeof(uint64_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::PeerStep ps = cdg::make_step(peers, window, 0, ranks, max_tokens, topk, H);
   const int64_t R = ranks * max_tokens;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, 1184)));
-  cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, A, SA, m_indices, ret_slot, ps);
+  cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, A, SA, m_indices, ret_slot, ret_rows, ps);
   return cdg::launched();
 }
 
 int cdg_ep_permute_p2p_planes(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H,
                               int64_t E_local, int32_t* fill, uint8_t* planes, int32_t* row_exp, int32_t* m_indices,
-                              int64_t M_pad, int32_t* ret_slot, cdg_stream_t stream) {
+                              int64_t M_pad, int32_t* ret_slot, const uint64_t* peers, uint64_t* ret_rows,
+                              cdg_stream_t stream) {
   if (!window || !cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || E_local <= 0 ||
       E_local > cdg::kFixedMaxExperts || M_pad < ranks * max_tokens * topk + 127 * E_local || M_pad % 128 || !fill ||
-      !planes || !row_exp || !m_indices || !ret_slot)
+      !planes || !row_exp || !m_indices || !ret_slot || (ret_rows && !peers))
     return CDG_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(planes) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(fill, 0, E_local * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(m_indices, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
   if (cudaMemsetAsync(ret_slot, 0xFF, M_pad * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  const cdg::PeerStep ps = cdg::make_step(nullptr, window, 0, ranks, max_tokens, topk, H);
+  if (ret_rows && cudaMemsetAsync(ret_rows, 0, M_pad * sizeof(uint64_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::PeerStep ps = cdg::make_step(peers, window, 0, ranks, max_tokens, topk, H);
   const int64_t R = ranks * max_tokens;
   const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, 1184)));
-  cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, nullptr, nullptr, m_indices, ret_slot, ps, planes,
-                                                   row_exp, M_pad);
+  cdg::ep_permute_p2p_kernel<<<grid, 256, 0, st>>>(E_local, fill, nullptr, nullptr, m_indices, ret_slot, ret_rows, ps,
+                                                   planes, row_exp, M_pad);
   return cdg::launched();
 }
 
@@ -1631,14 +1651,15 @@ int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int
 }
 
 int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
-                       int64_t H, int64_t ranks, int64_t max_tokens, int32_t* scratch, void* y, cdg_stream_t stream) {
+                       int64_t H, int64_t ranks, int64_t max_tokens, const uint64_t* peers, int32_t me,
+                       int32_t* scratch, void* y, cdg_stream_t stream) {
   if (!window || !scratch || !cdg::p2p_shape_ok(ranks, max_tokens, topk, H) || T < 0 || T > max_tokens ||
-      topk > cdg::kCombineMaxTopk || (T > 0 && (!send_index || !topk_w || !y)))
+      topk > cdg::kCombineMaxTopk || (T > 0 && (!send_index || !topk_w || !y)) || (peers && (me < 0 || me >= ranks)))
     return CDG_ERR_INVALID_ARGUMENT;
   if (H % 8 || reinterpret_cast<uintptr_t>(y) % 16) return CDG_ERR_ALIGNMENT;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
-  const cdg::PeerStep ps = cdg::make_step(nullptr, window, 0, ranks, max_tokens, topk, H);
+  if (cudaMemsetAsync(scratch, 0, 2 * sizeof(int32_t), st) != cudaSuccess) return CDG_ERR_CUDA;
+  const cdg::PeerStep ps = cdg::make_step(peers, window, peers ? me : 0, ranks, max_tokens, topk, H);
   const unsigned grid = T > 0 ? static_cast<unsigned>(T) : 1u;
   cdg::ep_combine_kernel<true><<<grid, 256, 0, st>>>(nullptr, H, nullptr, send_index, topk_w, T, topk, H,
                                                      static_cast<__nv_bfloat16*>(y), ps, scratch);

@@ -324,9 +324,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
               const int vi = lane + 32 * i, rr = vi >> 2, part = vi & 3;
-              if (j0 + rr < nrows)
-                *reinterpret_cast<uint4*>(p.d + (row0 + j0 + rr) * p.d_row_stride + nt * 128 + q * 32 + part * 8) =
-                    *reinterpret_cast<const uint4*>(wst + rr * 32 + part * 8);
+              if (j0 + rr < nrows) {
+                __nv_bfloat16* rp = d_row(p, row0 + j0 + rr);
+                if (rp)
+                  *reinterpret_cast<uint4*>(rp + nt * 128 + q * 32 + part * 8) =
+                      *reinterpret_cast<const uint4*>(wst + rr * 32 + part * 8);
+              }
             }
             __syncwarp();
           } else {
@@ -338,7 +341,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
               const float sc = __shfl_sync(0xffffffffu, my_scale, (j0 & 31) + j);
               if (rb < nrows) {
                 const float x = ((word >> (rb & 31)) & 1u) ? __uint_as_float(v[j]) * sc : 0.0f;
-                p.d[r * p.d_row_stride + n] = __float2bfloat16_rn(x);
+                __nv_bfloat16* rp = d_row(p, r);
+                if (rp) rp[n] = __float2bfloat16_rn(x);
               }
             }
           }
@@ -354,11 +358,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
       const uint4 z = make_uint4(0, 0, 0, 0);
       for (int c = tid; c < rows * 16; c += 128) {
         const int r = row0 + zero_from + (c >> 4);
-        *reinterpret_cast<uint4*>(p.d + r * p.d_row_stride + nt * 128 + (c & 15) * 8) = z;
+        __nv_bfloat16* rp = d_row(p, r);
+        if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + (c & 15) * 8) = z;
       }
     }
   }
 
+  if (p.d_rows) __threadfence_system();  // rows stored into other GPUs' memory
   tc_fence_before();
   const int any_fail = __syncthreads_or(!ok);
   cluster_sync();  // no CTA releases TMEM or exits while its pair still uses it

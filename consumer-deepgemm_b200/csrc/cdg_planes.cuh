@@ -373,7 +373,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * L::kAccCols;
-      __nv_bfloat16* dcol = p.d + nt * 128 + q * 32 + ld_part * 8;
+      const int dcol = nt * 128 + q * 32 + ld_part * 8;
 #pragma unroll
       for (int j0 = 0; j0 < kGroups; j0 += 2) {
         if (half + 2 * j0 < ng) {
@@ -415,7 +415,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
                 const uint32_t word = wi == 0 ? mk.x : wi == 1 ? mk.y : wi == 2 ? mk.z : mk.w;
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if ((word >> (pr & 31)) & 1u) v = *reinterpret_cast<const uint4*>(ld_src);
-                *reinterpret_cast<uint4*>(dcol + static_cast<int64_t>(drow0 + tok) * p.d_row_stride) = v;
+                __nv_bfloat16* rp = d_row(p, static_cast<int64_t>(drow0 + tok));
+                if (rp) *reinterpret_cast<uint4*>(rp + dcol) = v;
               }
               __syncwarp();
             }
@@ -438,12 +439,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
         const uint4 z = make_uint4(0, 0, 0, 0);
         for (int cc = tid; cc < rows * 16; cc += kEpiThreads) {
           const int r = r_first + (cc >> 4);
-          *reinterpret_cast<uint4*>(p.d + static_cast<int64_t>(r) * p.d_row_stride + nt * 128 + (cc & 15) * 8) = z;
+          __nv_bfloat16* rp = d_row(p, r);
+          if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + (cc & 15) * 8) = z;
         }
       }
     }
   }
 
+  if (p.d_rows) __threadfence_system();  // rows stored into other GPUs' memory
   tc_fence_before();
   const int any_fail = __syncthreads_or(!ok);
   cluster_sync();  // no CTA releases TMEM or exits while its pair still uses it

@@ -141,10 +141,24 @@ cdg_gemm_args make_args(const torch::Tensor& a, const c10::optional<torch::Tenso
   return g;
 }
 
+// D through a row table (cdg_gemm_args.d_rows): int64 [M] addresses on the device; `d` then only
+// gives the shape and dtype (an expanded [1, N] BF16 view will do) and is not written.
+void set_d_rows(cdg_gemm_args& g, const c10::optional<torch::Tensor>& d_rows) {
+  if (!d_rows.has_value()) return;
+  const auto& t = *d_rows;
+  TORCH_CHECK_VALUE(t.is_cuda() && t.scalar_type() == torch::kInt64 && t.is_contiguous() && t.numel() == g.M,
+                    "d_rows: contiguous int64 [M] row addresses on the device");
+  TORCH_CHECK_VALUE(g.d_dtype == CDG_DTYPE_BF16, "d_rows needs a BF16 output");
+  g.d_rows = reinterpret_cast<const uint64_t*>(t.data_ptr<int64_t>());
+  g.d = nullptr;
+  g.d_row_stride = g.N;
+}
+
 void grouped_gemm(const torch::Tensor& a, const c10::optional<torch::Tensor>& sa, const torch::Tensor& b,
                   const torch::Tensor& sfb, const torch::Tensor& d, const c10::optional<torch::Tensor>& ids,
-                  int64_t flags, bool masked) {
-  const cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, flags, masked);
+                  int64_t flags, bool masked, const c10::optional<torch::Tensor>& d_rows) {
+  cdg_gemm_args g = make_args(a, sa, b, sfb, d, ids, flags, masked);
+  set_d_rows(g, d_rows);
   const c10::cuda::CUDAGuard guard(a.device());
   const size_t ws_bytes = cdg_grouped_fp8_fp4_workspace_bytes(&g);
   TORCH_CHECK(ws_bytes > 0, "invalid GEMM arguments");
@@ -165,7 +179,8 @@ cdg_stream_t cur_stream(const torch::Tensor& t);
 // The GEMM on activations given as e4m3 planes [2, M, K] (uint8) with int32 row exponents [M]
 // (CDG_DTYPE_E4M3_PLANES): the form the MoE layer's own quantising steps write.
 void grouped_gemm_planes(const torch::Tensor& planes, const torch::Tensor& row_exp, const torch::Tensor& b,
-                         const torch::Tensor& sfb, const torch::Tensor& d, const torch::Tensor& ids, int64_t flags) {
+                         const torch::Tensor& sfb, const torch::Tensor& d, const torch::Tensor& ids, int64_t flags,
+                         const c10::optional<torch::Tensor>& d_rows) {
   TORCH_CHECK_VALUE(planes.is_cuda() && planes.dim() == 3 && planes.size(0) == 2 && planes.is_contiguous() &&
                         planes.scalar_type() == torch::kUInt8,
                     "planes: contiguous uint8 [2, M, K] on the device");
@@ -182,6 +197,7 @@ void grouped_gemm_planes(const torch::Tensor& planes, const torch::Tensor& row_e
   g.sa_stride_m = 1;
   g.sa_stride_k = 1;
   g.sa_cols = 1;
+  set_d_rows(g, d_rows);
   const c10::cuda::CUDAGuard guard(planes.device());
   const size_t ws_bytes = cdg_grouped_fp8_fp4_workspace_bytes(&g);
   TORCH_CHECK_VALUE(ws_bytes > 0, "invalid GEMM arguments for the planes form");
@@ -468,8 +484,19 @@ torch::Tensor ep_dispatch_p2p(const torch::Tensor& x, const torch::Tensor& ids, 
   return send_index;
 }
 
+// Optional row table of a fused return: uint64 [M_pad] when `peers` is given, else an empty tensor.
+std::pair<const uint64_t*, torch::Tensor> ret_rows_for(const c10::optional<torch::Tensor>& peers, int64_t M_pad,
+                                                       const torch::Tensor& like) {
+  if (!peers.has_value()) return {nullptr, torch::empty({0}, like.options().dtype(torch::kInt64))};
+  TORCH_CHECK(peers->is_cuda() && peers->scalar_type() == torch::kInt64 && peers->is_contiguous(),
+              "peers: int64 window addresses on the device");
+  return {reinterpret_cast<const uint64_t*>(peers->data_ptr<int64_t>()),
+          torch::empty({M_pad}, like.options().dtype(torch::kInt64))};
+}
+
 std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H,
-                                          int64_t E_local, int64_t M_pad, const torch::Tensor& like) {
+                                          int64_t E_local, int64_t M_pad, const torch::Tensor& like,
+                                          const c10::optional<torch::Tensor>& peers) {
   const c10::cuda::CUDAGuard guard(like.device());
   auto i32 = like.options().dtype(torch::kInt32);
   auto A = torch::empty({M_pad, H}, like.options().dtype(torch::kFloat8_e4m3fn));
@@ -477,16 +504,19 @@ std::vector<torch::Tensor> ep_permute_p2p(uint64_t window, int64_t ranks, int64_
   auto mi = torch::empty({M_pad}, i32);
   auto ret_slot = torch::empty({M_pad}, i32);
   auto fill = torch::empty({E_local}, i32);
+  auto [pp, ret_rows] = ret_rows_for(peers, M_pad, like);
   check_status(cdg_ep_permute_p2p(reinterpret_cast<void*>(window), ranks, max_tokens, topk, H, E_local,
                                   fill.data_ptr<int32_t>(), reinterpret_cast<uint8_t*>(A.data_ptr()),
                                   SA.data_ptr<float>(), mi.data_ptr<int32_t>(), M_pad, ret_slot.data_ptr<int32_t>(),
+                                  pp, pp ? reinterpret_cast<uint64_t*>(ret_rows.data_ptr<int64_t>()) : nullptr,
                                   cur_stream(like)),
                "ep_permute_p2p");
-  return {A, SA, mi, ret_slot};
+  return {A, SA, mi, ret_slot, ret_rows};
 }
 
 std::vector<torch::Tensor> ep_permute_p2p_planes(uint64_t window, int64_t ranks, int64_t max_tokens, int64_t topk,
-                                                 int64_t H, int64_t E_local, int64_t M_pad, const torch::Tensor& like) {
+                                                 int64_t H, int64_t E_local, int64_t M_pad, const torch::Tensor& like,
+                                                 const c10::optional<torch::Tensor>& peers) {
   const c10::cuda::CUDAGuard guard(like.device());
   auto i32 = like.options().dtype(torch::kInt32);
   auto planes = torch::empty({2, M_pad, H}, like.options().dtype(torch::kUInt8));
@@ -494,12 +524,15 @@ std::vector<torch::Tensor> ep_permute_p2p_planes(uint64_t window, int64_t ranks,
   auto mi = torch::empty({M_pad}, i32);
   auto ret_slot = torch::empty({M_pad}, i32);
   auto fill = torch::empty({E_local}, i32);
+  auto [pp, ret_rows] = ret_rows_for(peers, M_pad, like);
   check_status(cdg_ep_permute_p2p_planes(reinterpret_cast<void*>(window), ranks, max_tokens, topk, H, E_local,
                                          fill.data_ptr<int32_t>(), planes.data_ptr<uint8_t>(),
                                          row_exp.data_ptr<int32_t>(), mi.data_ptr<int32_t>(), M_pad,
-                                         ret_slot.data_ptr<int32_t>(), cur_stream(like)),
+                                         ret_slot.data_ptr<int32_t>(), pp,
+                                         pp ? reinterpret_cast<uint64_t*>(ret_rows.data_ptr<int64_t>()) : nullptr,
+                                         cur_stream(like)),
                "ep_permute_p2p_planes");
-  return {planes, row_exp, mi, ret_slot};
+  return {planes, row_exp, mi, ret_slot, ret_rows};
 }
 
 void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& ret_slot, int64_t ranks, int64_t max_tokens,
@@ -518,17 +551,24 @@ void ep_return_p2p(const torch::Tensor& Y, const torch::Tensor& ret_slot, int64_
 }
 
 torch::Tensor ep_combine_p2p(uint64_t window, const torch::Tensor& send_index, const torch::Tensor& topk_w,
-                             int64_t ranks, int64_t max_tokens, int64_t H) {
+                             int64_t ranks, int64_t max_tokens, int64_t H, const c10::optional<torch::Tensor>& peers,
+                             int64_t me) {
   TORCH_CHECK(topk_w.is_cuda() && topk_w.scalar_type() == torch::kFloat32 && topk_w.is_contiguous() &&
                   topk_w.dim() == 2 && send_index.numel() == topk_w.numel(),
               "topk weights: FP32 [T, topk] matching send_index");
   const c10::cuda::CUDAGuard guard(topk_w.device());
   const int64_t T = topk_w.size(0), topk = topk_w.size(1);
   auto y = torch::empty({T, H}, topk_w.options().dtype(torch::kBFloat16));
-  auto scratch = torch::empty({1}, send_index.options());
+  auto scratch = torch::empty({2}, send_index.options());
+  const uint64_t* pp = nullptr;
+  if (peers.has_value()) {
+    TORCH_CHECK(peers->is_cuda() && peers->scalar_type() == torch::kInt64 && peers->is_contiguous(),
+                "peers: int64 window addresses on the device");
+    pp = reinterpret_cast<const uint64_t*>(peers->data_ptr<int64_t>());
+  }
   check_status(cdg_ep_combine_p2p(reinterpret_cast<void*>(window), send_index.data_ptr<int32_t>(),
-                                  topk_w.data_ptr<float>(), T, topk, H, ranks, max_tokens, scratch.data_ptr<int32_t>(),
-                                  y.data_ptr(), cur_stream(topk_w)),
+                                  topk_w.data_ptr<float>(), T, topk, H, ranks, max_tokens, pp, static_cast<int32_t>(me),
+                                  scratch.data_ptr<int32_t>(), y.data_ptr(), cur_stream(topk_w)),
                "ep_combine_p2p");
   return y;
 }
@@ -579,9 +619,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("build_info", []() { return std::string(cdg_build_info()); });
   m.def("mk_alignment_for_contiguous_layout", []() { return cdg_mk_alignment_for_contiguous_layout(); });
   m.def("grouped_gemm", &grouped_gemm, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
-        py::arg("m_indices"), py::arg("flags") = 0, py::arg("masked") = false);
+        py::arg("m_indices"), py::arg("flags") = 0, py::arg("masked") = false, py::arg("d_rows") = py::none());
   m.def("grouped_gemm_planes", &grouped_gemm_planes, py::arg("planes"), py::arg("row_exp"), py::arg("b"),
-        py::arg("sfb"), py::arg("d"), py::arg("m_indices"), py::arg("flags") = 0);
+        py::arg("sfb"), py::arg("d"), py::arg("m_indices"), py::arg("flags") = 0, py::arg("d_rows") = py::none());
   m.def("can_implement", &can_implement, py::arg("a"), py::arg("sa"), py::arg("b"), py::arg("sfb"), py::arg("d"),
         py::arg("m_indices"));
   m.def("transform_sf_atoms", &transform_sf_atoms, py::arg("sf"));
@@ -633,16 +673,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ranks"), py::arg("max_tokens"), py::arg("peers"), py::arg("window"), py::arg("me"),
         py::arg("ue8m0") = false);
   m.def("ep_permute_p2p_planes", &ep_permute_p2p_planes, py::arg("window"), py::arg("ranks"), py::arg("max_tokens"),
-        py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
+        py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"),
+        py::arg("peers") = py::none());
   m.def("ep_quant_dispatch_local_planes", &ep_quant_dispatch_local_planes, py::arg("x"), py::arg("topk_ids"),
         py::arg("num_experts"), py::arg("expert_off"), py::arg("m_pad"));
   m.def("silu_mul_quant_planes", &silu_mul_quant_planes, py::arg("h"), py::arg("m_indices"));
   m.def("ep_permute_p2p", &ep_permute_p2p, py::arg("window"), py::arg("ranks"), py::arg("max_tokens"),
-        py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"));
+        py::arg("topk"), py::arg("hidden"), py::arg("local_experts"), py::arg("m_pad"), py::arg("like"),
+        py::arg("peers") = py::none());
   m.def("ep_return_p2p", &ep_return_p2p, py::arg("y"), py::arg("ret_slot"), py::arg("ranks"), py::arg("max_tokens"),
         py::arg("topk"), py::arg("peers"), py::arg("window"), py::arg("me"));
   m.def("ep_combine_p2p", &ep_combine_p2p, py::arg("window"), py::arg("send_index"), py::arg("topk_w"),
-        py::arg("ranks"), py::arg("max_tokens"), py::arg("hidden"));
+        py::arg("ranks"), py::arg("max_tokens"), py::arg("hidden"), py::arg("peers") = py::none(),
+        py::arg("me") = 0);
   m.def("ep_row_bytes", [](int64_t H) { return cdg_ep_row_bytes(H); }, py::arg("hidden"));
   m.def(
       "ep_set_wait_timeout_ns",
@@ -652,7 +695,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       [](bool clear) {
         int32_t where = 0;
         const int st = cdg_device_status(clear ? 1 : 0, &where);
-        if (st != CDG_OK && st != CDG_ERR_DEVICE_TIMEOUT) check_status(st, "device_status");
+        if (st != CDG_OK && st != CDG_ERR_DEVICE_TIMEOUT && st != CDG_ERR_DEVICE_INDEX)
+          check_status(st, "device_status");
         return py::make_tuple(st, where);
       },
       py::arg("clear") = true);

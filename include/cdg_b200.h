@@ -33,7 +33,7 @@ extern "C" {
 
 typedef struct CUstream_st* cdg_stream_t; /* == cudaStream_t */
 
-#define CDG_ABI_VERSION 1
+#define CDG_ABI_VERSION 2
 
 typedef enum cdg_status {
   CDG_OK = 0,
@@ -44,7 +44,9 @@ typedef enum cdg_status {
   CDG_ERR_CUDA = 5,             /* a CUDA runtime call failed (see cudaGetLastError) */
   CDG_ERR_DEVICE_TIMEOUT = 6,   /* a kernel gave up waiting on its pipeline */
   CDG_ERR_NO_SM100 = 7,         /* the current device is not compute capability 10.x */
-  CDG_ERR_SCRATCH_TOO_SMALL = 8 /* the problem needs more than the static scratch of the no-allocation entry */
+  CDG_ERR_SCRATCH_TOO_SMALL = 8, /* the problem needs more than the static scratch of the no-allocation entry */
+  CDG_ERR_DEVICE_INDEX = 9       /* a kernel met an index or address it cannot use (outside its buffer, or a
+                                    D row address that is not 16-byte aligned) and skipped that access */
 } cdg_status;
 
 typedef enum cdg_dtype {
@@ -64,7 +66,7 @@ typedef enum cdg_dtype {
                                e4m3 row with FP32 1x128 scales as cdg_ep_* producers split it (see
                                cdg_ep_quant_dispatch_local).  Per-row m_indices with 128-aligned groups
                                only; a block with rows of several experts is left out and reported
-                               (CDG_ERR_DEVICE_TIMEOUT from cdg_device_status, bit 2).  Used by the MoE
+                               (CDG_ERR_DEVICE_INDEX from cdg_device_status).  Used by the MoE
                                layer, whose own quantising steps write the planes, so the GEMM skips its
                                plane split */
 } cdg_dtype;
@@ -122,6 +124,14 @@ typedef struct cdg_gemm_args {
   int32_t flags; /* CDG_FLAG_* */
   int32_t sa_dtype; /* scales of an e4m3 `a`: CDG_DTYPE_F32 (0 reads as F32) or CDG_DTYPE_UE8M0_X4, whose
                        sa_cols counts int32 words and whose strides are in words */
+  const uint64_t* d_rows; /* optional (ABI 2), device memory: M row addresses; when set, row r of D is
+                             stored at d_rows[r] instead of d + r * d_row_stride (BF16 only; `d` may
+                             be NULL).  A zero address leaves the row unwritten; an address that is
+                             not 16-byte aligned is not written and raises the bad-index status.  The
+                             addresses may lie in another GPU's memory (peer or IPC mappings): the
+                             kernels end with a system-scope fence when the table is set.  This is
+                             how an expert-parallel layer returns FC2 rows straight into each
+                             source rank's window */
 } cdg_gemm_args;
 
 #define CDG_FLAG_FORCE_GENERIC 1 /* run the exact SIMT path even where the tensor-core path applies */
@@ -181,17 +191,20 @@ int cdg_transform_sf(const uint8_t* sf, int64_t stride_e, int64_t stride_n, int6
 size_t cdg_sf_atoms_bytes(int64_t E, int64_t N, int64_t KB);
 
 /* Reads (synchronising `stream`) the device status word a GEMM call left in its
- * workspace; returns CDG_OK or CDG_ERR_DEVICE_TIMEOUT.  No reference counterpart:
+ * workspace; returns CDG_OK, CDG_ERR_DEVICE_TIMEOUT or CDG_ERR_DEVICE_INDEX (as
+ * cdg_device_status).  No reference counterpart:
  * the reference reports device failures only as a launch result
  * (csrc/cutlass_mxfp8_mxfp4_probe.cu:598-613). */
 int cdg_read_device_status(const void* workspace, cdg_stream_t stream);
 
 /* Device-side errors of every call on the current device since the last clear, whatever
  * workspace (or exchange window) the call used: after synchronising the device, returns
- * CDG_OK or CDG_ERR_DEVICE_TIMEOUT (a bounded wait gave up: an mbarrier wait of a GEMM
- * kernel, or a wait on another rank's flag in the peer-memory exchange), stores the first
- * such wait's code in *where (may be NULL; 0 when none), and clears the record when `clear`
- * is nonzero.  A wait code holds the role (bits 28-31: 1 producer/empty, 2 issuer/tempty,
+ * CDG_OK, CDG_ERR_DEVICE_TIMEOUT (a bounded wait gave up: an mbarrier wait of a GEMM
+ * kernel, or a wait on another rank's flag in the peer-memory exchange) or, when no wait
+ * gave up, CDG_ERR_DEVICE_INDEX (a kernel skipped an access it could not make: a block the
+ * planes form cannot run, exchange rows that do not match their header, a misaligned D row
+ * address), stores the first recorded code in *where (may be NULL; 0 when none), and clears
+ * the record when `clear` is nonzero.  A wait code holds the role (bits 28-31: 1 producer/empty, 2 issuer/tempty,
  * 3 issuer/full, 4 epilogue/tfull, 5 issuer/done, 6 scale copier, 7 scale producer,
  * 8 exchange dispatch flag, 9 exchange return flag, 10 exchange rows not matching their
  * header's counts (bit 2 of the status: such rows are dropped), 15 TMEM allocation not at column 0),
@@ -355,7 +368,8 @@ int cdg_silu_mul_quant_planes(const void* in, int64_t in_stride, int64_t M, int6
                               uint8_t* planes, int32_t* row_exp, cdg_stream_t stream);
 int cdg_ep_permute_p2p_planes(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H,
                               int64_t E_local, int32_t* fill, uint8_t* planes, int32_t* row_exp, int32_t* m_indices,
-                              int64_t M_pad, int32_t* ret_slot, cdg_stream_t stream);
+                              int64_t M_pad, int32_t* ret_slot, const uint64_t* peers, uint64_t* ret_rows,
+                              cdg_stream_t stream);
 
 /* Fixed-capacity exchange (no host synchronisation).  The send (and receive) buffer holds
  * per destination (source) rank a region of 1 + cap packed rows of cdg_ep_row_bytes(H):
@@ -406,17 +420,23 @@ int cdg_mega_moe_transform_rows(const void* src, int64_t stride_g, int64_t strid
  *                         out per local expert (128-aligned groups, A / SA / m_indices as the
  *                         grouped GEMM reads them; a row with several slots here is written
  *                         to each slot's group); ret_slot[pos] says where GEMM row pos goes back;
- *   cdg_ep_return_p2p     store each GEMM row straight into its source's window at the
- *                         source's slot index, raise flags;
+ *                         with `peers` and `ret_rows` given (both or neither), ret_rows[pos]
+ *                         (uint64 [M_pad], 0 on unplaced rows) is that place's address in the
+ *                         source's window: the d_rows table of an FC2 GEMM that stores its rows
+ *                         straight back (cdg_gemm_args.d_rows), making the return step part of FC2;
+ *   cdg_ep_return_p2p     (when FC2 wrote into a local buffer) store each GEMM row into its
+ *                         source's window at the source's slot index, raise flags;
  *   cdg_ep_combine_p2p    wait for every rank's rows, weighted top-k sum (as cdg_ep_combine),
- *                         and advance the window's step counter.
+ *                         and advance the window's step counter; with `peers` given, it first
+ *                         raises this rank's return flags (for an FC2 that stored through
+ *                         ret_rows; NULL after cdg_ep_return_p2p, which raised them).
  * The step number (flag value; the windows are double-buffered by its parity) lives in the
  * window, so the calls take no per-step argument and a whole step can be captured in a CUDA
  * graph; every rank must run the same number of steps.  Plain stores and loads over NVLink:
  * no multicast.  A wait that gives up after its bound (2 s, cdg_ep_set_wait_timeout_ns)
  * skips its CTA's work and sets the window's status word (cdg_ep_window_status and
  * cdg_device_status report it).  scratch: int32 [cdg_ep_fixed_scratch_ints(ranks, E)] for
- * dispatch, int32 [1] for return and combine.  Limits: ranks <= 128, topk <= 32, E / ranks <=
+ * dispatch, int32 [1] for return, int32 [2] for combine.  Limits: ranks <= 128, topk <= 32, E / ranks <=
  * 1024, H a multiple of 128, ranks * max_tokens * topk < 2^31; M_pad of the permute at least
  * ranks * max_tokens * topk + 127 * E_local (the worst case). */
 size_t cdg_ep_window_bytes(int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H);
@@ -430,12 +450,13 @@ int cdg_ep_dispatch_p2p(const void* x, int32_t x_dtype, int64_t x_stride, const 
                         int32_t scale_fmt, cdg_stream_t stream);
 int cdg_ep_permute_p2p(void* window, int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, int64_t E_local,
                        int32_t* fill, uint8_t* A, float* SA, int32_t* m_indices, int64_t M_pad, int32_t* ret_slot,
-                       cdg_stream_t stream);
+                       const uint64_t* peers, uint64_t* ret_rows, cdg_stream_t stream);
 int cdg_ep_return_p2p(const void* Y, int64_t y_stride, int64_t y_rows, const int32_t* ret_slot, int64_t M_pad,
                       int64_t ranks, int64_t max_tokens, int64_t topk, int64_t H, const uint64_t* peers, void* window,
                       int32_t me, int32_t* scratch, cdg_stream_t stream);
 int cdg_ep_combine_p2p(void* window, const int32_t* send_index, const float* topk_w, int64_t T, int64_t topk,
-                       int64_t H, int64_t ranks, int64_t max_tokens, int32_t* scratch, void* y, cdg_stream_t stream);
+                       int64_t H, int64_t ranks, int64_t max_tokens, const uint64_t* peers, int32_t me,
+                       int32_t* scratch, void* y, cdg_stream_t stream);
 /* Bound of the exchange's waits on other ranks' flags on the current device, in ns (0 = the
  * default 2 s; at most 60 s).  A wait that runs out sets the window's status word and the
  * record cdg_device_status() reads; the waiting step then places no rows (permute) or writes

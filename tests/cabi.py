@@ -38,6 +38,7 @@ class GemmArgs(ctypes.Structure):
         ("d", ctypes.c_void_p), ("d_dtype", ctypes.c_int32), ("d_row_stride", ctypes.c_int64),
         ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64), ("E", ctypes.c_int64),
         ("flags", ctypes.c_int32), ("sa_dtype", ctypes.c_int32),
+        ("d_rows", ctypes.c_void_p),
     ]
 
 
@@ -80,7 +81,7 @@ def _code(t: torch.Tensor) -> int:
             torch.uint8: DT["ue8m0"], torch.int32: DT["i32"], torch.int64: DT["i64"]}[t.dtype]
 
 
-def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, masked=False) -> GemmArgs:
+def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, masked=False, d_rows=None) -> GemmArgs:
     g = GemmArgs()
     M, K = a.shape
     E, N = b.shape[0], b.shape[1]
@@ -101,16 +102,20 @@ def make_args(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, masked=False)
         g.m_indices, g.m_indices_dtype, g.m_indices_len = m_indices.data_ptr(), _code(m_indices), m_indices.numel()
         g.index_form = INDEX_MASKED if masked else INDEX_PER_ROW if m_indices.numel() == M else INDEX_PSUM
     g.d, g.d_dtype, g.d_row_stride = d.data_ptr(), _code(d), d.stride(0)
+    if d_rows is not None:  # rows stored through the table; `d` only gives dtype and width
+        g.d_rows, g.d, g.d_row_stride = d_rows.data_ptr(), None, N
     g.M, g.N, g.K, g.E, g.flags = M, N, K, E, flags
     return g
 
 
-def gemm(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, stream=None, check_status=True, masked=False):
+def gemm(a, sa, b, sb, d, m_indices, flags=0, sb_atoms=False, stream=None, check_status=True, masked=False,
+         d_rows=None):
     """Run the GEMM through the C ABI on `stream` (default: torch's current stream).
 
-    masked=True: `m_indices` is masked_m [G] and the masked entry point runs."""
+    masked=True: `m_indices` is masked_m [G] and the masked entry point runs.
+    d_rows: int64 [M] device addresses of D's rows (cdg_gemm_args.d_rows)."""
     l = lib()
-    g = make_args(a, sa, b, sb, d, m_indices, flags, sb_atoms, masked)
+    g = make_args(a, sa, b, sb, d, m_indices, flags, sb_atoms, masked, d_rows)
     nbytes = l.cdg_grouped_fp8_fp4_workspace_bytes(ctypes.byref(g))
     assert nbytes > 0, "invalid arguments"
     ws = torch.empty(nbytes + 1024, dtype=torch.uint8, device=d.device)

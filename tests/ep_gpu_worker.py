@@ -43,13 +43,16 @@ def main():
              for u in (False, True)}
     # split-size exchange (one host sync), fixed-capacity NCCL exchange (none), and the
     # library's peer-memory exchange (no collective), three forwards each (window parities);
-    # the peer-memory exchange also with power-of-two activation scales
-    for mode, max_tok, exchange, ue8m0 in (("split_sizes", None, "nccl", False), ("fixed_capacity", tpr, "nccl", False),
-                                           ("peer_memory", tpr, "p2p", False),
-                                           ("peer_memory_ue8m0", tpr, "p2p", True)):
+    # the peer-memory exchange also with power-of-two activation scales, and with FC2 writing a
+    # local buffer that a separate kernel returns (instead of storing into the windows itself)
+    for mode, max_tok, exchange, ue8m0, fused in (("split_sizes", None, "nccl", False, True),
+                                                  ("fixed_capacity", tpr, "nccl", False, True),
+                                                  ("peer_memory", tpr, "p2p", False, True),
+                                                  ("peer_memory_ue8m0", tpr, "p2p", True, True),
+                                                  ("peer_memory_return_kernel", tpr, "p2p", False, False)):
         y_one = y_ref[ue8m0]
         layer = MoELayer(w1[sl], w1s[sl], w2[sl], w2s[sl], num_experts=cfg["experts"], group=dist.group.WORLD,
-                         max_tokens_per_rank=max_tok, exchange=exchange, ue8m0=ue8m0)
+                         max_tokens_per_rank=max_tok, exchange=exchange, ue8m0=ue8m0, fused_return=fused)
         for it in range(3):
             y = layer(x[ts], ids[ts], w[ts])
             parts = [torch.empty_like(y) for _ in range(world)]

@@ -328,7 +328,7 @@ def test_peer_wait_runs_out_and_context_stays_usable():
         C.ep_set_wait_timeout_ns(10_000_000)
         like = torch.zeros(1, device=DEV)
         m_pad = (ranks * cap + 127 * e_loc + 127) // 128 * 128
-        a, sa, mi, ret_slot = C.ep_permute_p2p(own, ranks, T, topk, H, e_loc, m_pad, like)
+        a, sa, mi, ret_slot, _ = C.ep_permute_p2p(own, ranks, T, topk, H, e_loc, m_pad, like)
         send_index = torch.arange(T * topk, dtype=torch.int32, device=DEV)
         tw = torch.full((T, topk), 0.5, device=DEV)
         y = C.ep_combine_p2p(own, send_index, tw, ranks, T, H)
@@ -369,20 +369,24 @@ def test_layer_expert_parallel_two_gpus():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    for mode in ("split_sizes", "fixed_capacity", "peer_memory", "peer_memory_ue8m0"):
+    for mode in ("split_sizes", "fixed_capacity", "peer_memory", "peer_memory_ue8m0", "peer_memory_return_kernel"):
         assert f"EP_OK {mode}" in r.stdout, r.stdout[-3000:]
 
 
-@pytest.mark.parametrize("ue8m0,planes", [(False, False), (False, True), (True, False)],
-                         ids=["fp32", "fp32_planes", "ue8m0"])
-def test_peer_exchange_two_ranks_on_one_gpu(ue8m0, planes):
+@pytest.mark.parametrize("ue8m0,planes,fused", [(False, False, False), (False, True, False), (True, False, False),
+                                                (False, False, True), (False, True, True), (True, False, True)],
+                         ids=["fp32", "fp32_planes", "ue8m0", "fp32_fused", "fp32_planes_fused", "ue8m0_fused"])
+def test_peer_exchange_two_ranks_on_one_gpu(ue8m0, planes, fused):
     """The peer-memory exchange kernels for two ranks whose windows both live on this GPU.
 
     Each step runs rank 0's and rank 1's calls in order on one stream (dispatch, dispatch,
     permute, permute, GEMMs, return, return, combine, combine), so every flag a wait looks
-    for was raised by an earlier launch: no kernel waits on one running beside it.  Three
-    steps (both window parities and a reuse); the gathered outputs equal the one-GPU layer's
-    (per-row relative L2 <= 1e-3) and no wait gave up."""
+    for was raised by an earlier launch: no kernel waits on one running beside it.  Fused
+    return: FC2 stores its rows into the windows through the permute's row table; rank 1's
+    flags are then raised by a return call with no rows and rank 0's by its own combine
+    (whose wait finds rank 1's flag already up).  Three steps (both window parities and a
+    reuse); the gathered outputs equal the one-GPU layer's (per-row relative L2 <= 1e-3)
+    and no wait gave up."""
     import consumer_deep_gemm as cdg
     from consumer_deep_gemm.layout import transform_sf_into_required_layout
     from consumer_deep_gemm.moe import MoELayer, NativeOps
@@ -408,22 +412,33 @@ def test_peer_exchange_two_ranks_on_one_gpu(ue8m0, planes):
             si = [C.ep_dispatch_p2p(x[tok[r]], ids[tok[r]].contiguous(), E, ranks, tpr, peers, own[r], r, ue8m0)
                   for r in range(ranks)]
             permute = C.ep_permute_p2p_planes if planes else C.ep_permute_p2p
-            placed = [permute(own[r], ranks, tpr, topk, H, e_loc, m_pad, x) for r in range(ranks)]
+            placed = [permute(own[r], ranks, tpr, topk, H, e_loc, m_pad, x, peers if fused else None)
+                      for r in range(ranks)]
             outs = []
             for r in range(ranks):
-                a, sa, mi, _ = placed[r]  # planes form: (planes, row exponents, ...)
+                a, sa, mi, _, ret_rows = placed[r]  # planes form: (planes, row exponents, ...)
+                d_rows = ret_rows if fused else None
+                if fused:
+                    # placed rows have an address, the rest none
+                    assert bool(((ret_rows != 0) == (mi >= 0)).all())
                 b1, s1, b2, s2 = shard[r]
                 if planes:
                     h = ops.gemm_planes(a, sa, b1, s1, mi, skip_ungrouped=True)
                     pl, rexp = ops.act_planes(h, mi)
-                    outs.append(ops.gemm_planes(pl, rexp, b2, s2, mi, skip_ungrouped=True))
+                    outs.append(ops.gemm_planes(pl, rexp, b2, s2, mi, skip_ungrouped=True, d_rows=d_rows))
                 else:
                     h = ops.gemm(a, sa, b1, s1, mi, skip_ungrouped=True)
                     aq, asc = ops.act(h, mi, ue8m0)
-                    outs.append(ops.gemm(aq, asc, b2, s2, mi, skip_ungrouped=True))
-            for r in range(ranks):
-                C.ep_return_p2p(outs[r], placed[r][3], ranks, tpr, topk, peers, own[r], r)
-            y = torch.cat([C.ep_combine_p2p(own[r], si[r], w[tok[r]].float().contiguous(), ranks, tpr, H)
+                    outs.append(ops.gemm(aq, asc, b2, s2, mi, skip_ungrouped=True, d_rows=d_rows))
+            no_rows = torch.empty(0, H, dtype=torch.bfloat16, device=DEV)
+            if fused:
+                assert all(o is None for o in outs)
+                C.ep_return_p2p(no_rows, placed[1][3], ranks, tpr, topk, peers, own[1], 1)  # flags only
+            else:
+                for r in range(ranks):
+                    C.ep_return_p2p(outs[r], placed[r][3], ranks, tpr, topk, peers, own[r], r)
+            y = torch.cat([C.ep_combine_p2p(own[r], si[r], w[tok[r]].float().contiguous(), ranks, tpr, H,
+                                            peers if (fused and r == 0) else None, r)
                            for r in range(ranks)])
             torch.cuda.synchronize()
             nw, rl2 = errors(y, y_ref)

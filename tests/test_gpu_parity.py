@@ -79,6 +79,78 @@ def test_golden_case(name, flags):
     assert nw <= TOL_NORMWISE and rl2 <= TOL_ROW_L2, (name, nw, rl2)
 
 
+def _row_table(m, n, skip_every, seed):
+    """A destination buffer [m + 3, n] of NaNs and a row table that stores GEMM row r at
+    destination row perm[r] (a seeded permutation), except every `skip_every`-th row
+    (address 0: not stored)."""
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(m + 3, generator=g)[:m]
+    dst = torch.full((m + 3, n), float("nan"), dtype=torch.bfloat16, device=DEV)
+    addr = dst.data_ptr() + perm.to(torch.int64) * (n * 2)
+    skipped = torch.zeros(m, dtype=torch.bool)
+    if skip_every:
+        skipped[::skip_every] = True
+    addr[skipped] = 0
+    return dst, addr.to(DEV), perm, skipped
+
+
+@pytest.mark.parametrize("flags", [0, cabi.FLAG_SINGLE_CTA, cabi.FLAG_FORCE_GENERIC],
+                         ids=["dispatch", "single_cta", "simt"])
+@pytest.mark.parametrize("name", ["c0", "edge_block_classes", "kat_vllm_padding_zero", "pow2_c0"])
+def test_row_table_output_equals_plain_output(name, flags):
+    """D through a row table (cdg_gemm_args.d_rows, how the expert-parallel layer returns FC2
+    rows straight into the source ranks' windows): every stored row is bit-identical to the
+    same call's plain output (padding rows included, as zeros); rows whose address is 0 are
+    not written; `d` itself is not read or written (NULL).  pow2_c0: c0 with power-of-two
+    activation scales, so the direct class runs too."""
+    c = load_gemm_case(name[5:] if name.startswith("pow2_") else name)
+    if name.startswith("pow2_"):
+        c = dict(c, sa=_pow2_scales(c["sa"]))
+    plain = _run_case(c, flags)
+    a = c["a"].to(DEV)
+    sa = c["sa"].to(DEV).float()
+    b, sb = c["b"].to(DEV), c["sb"].to(DEV)
+    ids = c["m_indices"].to(DEV) if c["m_indices"] is not None else None
+    m, n = plain.shape
+    dst, addr, perm, skipped = _row_table(m, n, 5, seed=11)
+    shape_only = torch.empty(1, n, dtype=torch.bfloat16, device=DEV).expand(m, n)
+    cabi.gemm(a, sa, b, sb, shape_only, ids, flags=flags, d_rows=addr)
+    torch.cuda.synchronize()
+    out = dst.cpu()
+    kept = ~skipped
+    assert torch.equal(out[perm[kept]].view(torch.int16), plain[kept].view(torch.int16))
+    untouched = torch.ones(m + 3, dtype=torch.bool)
+    untouched[perm[kept]] = False
+    assert bool(torch.isnan(out[untouched].float()).all())
+    assert cabi.device_status() == (0, 0)
+
+
+def test_row_table_misaligned_address_is_skipped_and_reported():
+    """A D row address that is not 16-byte aligned: that row is not written, the call's other
+    rows are, and the device record reports CDG_ERR_DEVICE_INDEX (9).  Every kernel checks the
+    address before its store, so nothing faults."""
+    c = load_gemm_case("c0")
+    a, sa = c["a"].to(DEV), c["sa"].to(DEV).float()
+    b, sb, ids = c["b"].to(DEV), c["sb"].to(DEV), c["m_indices"].to(DEV)
+    plain = _run_case(c, 0)
+    m, n = plain.shape
+    dst, addr, perm, skipped = _row_table(m, n, 0, seed=12)
+    routed = (c["m_indices"] >= 0).nonzero().flatten()
+    bad = int(routed[0])
+    addr[bad] += 2  # inside the row's own bytes, but not 16-byte aligned
+    shape_only = torch.empty(1, n, dtype=torch.bfloat16, device=DEV).expand(m, n)
+    cabi.gemm(a, sa, b, sb, shape_only, ids, d_rows=addr, check_status=False)
+    torch.cuda.synchronize()
+    out = dst.cpu()
+    assert bool(torch.isnan(out[perm[bad]].float()).all())
+    keep = torch.ones(m, dtype=torch.bool)
+    keep[bad] = False
+    assert torch.equal(out[perm[keep]].view(torch.int16), plain[keep].view(torch.int16))
+    st, _ = cabi.device_status()
+    assert st == 9
+    assert cabi.device_status() == (0, 0)
+
+
 def _masked_covered(m, counts, groups):
     """Rows the masked layout writes from a group (the rest must be zero)."""
     covered = torch.zeros(m, dtype=torch.bool)
