@@ -819,8 +819,8 @@ def bench_layer(args, dev, world, rank, dist, cfg_name):
     fp8_peak = 2 * bf16_peak
     achieved = f_fc1 / (fc1_ms * 1e-3) / 1e12
     step_desc = ("quantise into the layout, FC1, SiLU-mul + requant, FC2, unpermute + combine" if world == 1 else
-                 "dispatch (quantise + store into the owners' windows), permute, FC1, SiLU-mul + requant, FC2, "
-                 "return (store into the sources' windows), combine")
+                 "dispatch (quantise + store into the owners' windows), permute, FC1, SiLU-mul + requant, "
+                 "FC2 (its epilogue stores each row into its source's window), combine")
     return {
         "metric": METRIC, "value": job_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
