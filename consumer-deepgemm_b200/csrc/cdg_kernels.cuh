@@ -248,10 +248,9 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ int s_exp[128];
   __shared__ float s_inv[128];              // 2^-E of each row
   __shared__ uint32_t s_smax_bits[128];     // bits of the largest finite |bf16(sa)| of each row
-  __shared__ int s_cls_count[kNumClasses][257];
+  constexpr int kScan = kNumClasses + 2;    // last CTA: per-class block counts, plane and direct tiles
+  __shared__ int s_warp_sum[8][kScan];      // last CTA: the scan's per-warp totals (256 threads)
   __shared__ uint32_t s_cont[kContBits / 32];  // last CTA: which blocks continue a run (bitmask)
-  __shared__ int s_tile_count[257];
-  __shared__ int s_dtile_count[257];
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   if (tid == 0) {
@@ -493,32 +492,40 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     return 128 * (j - i) + __ldcg(&p.blk_info[j].y);
   };
   static_assert(kPlanesTileTok % 16 == 0, "tile cuts at multiples of 16 rows");
-  int cnt[kNumClasses] = {};
-  int ntiles = 0, dtiles = 0;
+  // per thread (its blocks [lo, hi)): blocks of each class, then plane tiles, then direct tiles
+  int cnt[kScan] = {};
   for (int i = lo; i < hi; ++i) {
     const int c = __ldcg(&p.blk_info[i].z);
     cnt[c]++;
-    if (p.pair_wide && c == kClassWide && !continues(i)) ntiles += (run_span(i) + kPlanesTileTok - 1) / kPlanesTileTok;
+    if (p.pair_wide && c == kClassWide && !continues(i))
+      cnt[kNumClasses] += (run_span(i) + kPlanesTileTok - 1) / kPlanesTileTok;
     if (p.pair_wide && c == kClassWideDirect && !continues(i))
-      dtiles += (run_span(i) + kDirectTileTok - 1) / kDirectTileTok;
+      cnt[kNumClasses + 1] += (run_span(i) + kDirectTileTok - 1) / kDirectTileTok;
   }
+  // Exclusive scan of the eight counts over the 256 threads (in block order): shuffles within
+  // each warp, then the eight warp totals.
+  const int lane = tid & 31, warp = tid >> 5;
+  int incl[kScan];
 #pragma unroll
-  for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][tid + 1] = cnt[c];
-  s_tile_count[tid + 1] = ntiles;
-  s_dtile_count[tid + 1] = dtiles;
-  if (tid == 0) {
+  for (int k = 0; k < kScan; ++k) incl[k] = cnt[k];
 #pragma unroll
-    for (int c = 0; c < kNumClasses; ++c) s_cls_count[c][0] = 0;
-    s_tile_count[0] = 0;
-    s_dtile_count[0] = 0;
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int k = 0; k < kScan; ++k) {
+      const int v = __shfl_up_sync(0xffffffffu, incl[k], o);
+      if (lane >= o) incl[k] += v;
+    }
+  }
+  if (lane == 31) {
+#pragma unroll
+    for (int k = 0; k < kScan; ++k) s_warp_sum[warp][k] = incl[k];
   }
   __syncthreads();
-  if (tid <= kNumClasses + 1) {  // threads kNumClasses, kNumClasses + 1 scan the tile counts
-    int* cs = tid < kNumClasses ? s_cls_count[tid] : tid == kNumClasses ? s_tile_count : s_dtile_count;
+  if (tid < kScan) {  // thread k: exclusive scan of value k over the warps, and its total
     int run = 0;
-    for (int t = 0; t <= static_cast<int>(blockDim.x); ++t) {
-      const int v = cs[t];
-      cs[t] = run;
+    for (int w = 0; w < 8; ++w) {
+      const int v = s_warp_sum[w][tid];
+      s_warp_sum[w][tid] = run;
       run += v;
     }
     p.ctrl[tid < kNumClasses ? kCtrlCount0 + tid : tid == kNumClasses ? kCtrlPlaneTiles : kCtrlDirectTiles] = run;
@@ -526,9 +533,9 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __syncthreads();
   int pos[kNumClasses];
 #pragma unroll
-  for (int c = 0; c < kNumClasses; ++c) pos[c] = s_cls_count[c][tid + 1];
-  int tpos = s_tile_count[tid + 1];
-  int dpos = s_dtile_count[tid + 1];
+  for (int c = 0; c < kNumClasses; ++c) pos[c] = s_warp_sum[warp][c] + incl[c] - cnt[c];
+  int tpos = s_warp_sum[warp][kNumClasses] + incl[kNumClasses] - cnt[kNumClasses];
+  int dpos = s_warp_sum[warp][kNumClasses + 1] + incl[kNumClasses + 1] - cnt[kNumClasses + 1];
   for (int i = lo; i < hi; ++i) {
     const int c = __ldcg(&p.blk_info[i].z);
     const int4 info = __ldcg(&p.blk_info[i]);
