@@ -241,6 +241,7 @@ template <typename IdT>
 __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
   __shared__ int s_min_id, s_max_id, s_max_row;
   __shared__ int s_last, s_nv, s_pow2, s_exp_bad;
+  __shared__ int64_t s_prev_id;  // id of the row before the block (-1 for the first block)
   __shared__ uint8_t s_vrow[128];  // the block's rows that carry its expert (compacted)
   __shared__ int s_id[128];
   __shared__ uint32_t s_mask[4];
@@ -279,6 +280,9 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       atomicMax(&s_max_id, id);
       atomicMax(&s_max_row, tid);
     }
+  } else if (tid == 128) {
+    // read alongside the block's own ids (the class rule below needs it)
+    s_prev_id = row0 > 0 ? load_id(p.ids, sizeof(IdT) == 8, row0 - 1) : -1;
   }
   __syncthreads();
   const int eff = s_max_row + 1;
@@ -296,9 +300,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     // CTA-pair path: the wide kernels trim the MMA to the block's rows, and they read the
     // expert's weights from L2 right after its other blocks did, where the tiny and narrow
     // kernels would stream them from HBM again.
-    if (cls != kClassWide && p.pair_wide && row0 > 0 &&
-        load_id(p.ids, sizeof(IdT) == 8, row0 - 1) == static_cast<int64_t>(expert))
-      cls = kClassWide;
+    if (cls != kClassWide && p.pair_wide && row0 > 0 && s_prev_id == static_cast<int64_t>(expert)) cls = kClassWide;
     // float weight scales that are not all powers of two: the tensor cores' UE8M0 scale
     // factors cannot hold them, the exact SIMT kernel takes the block
     if (p.sf_inexact && __ldcg(p.sf_inexact)) {
@@ -332,8 +334,9 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
     const int kbn = min(kPrepK / 128, kb_count - kb0);
     // (1) per routed row: the exponent E with |bf16(sa[r,kb])| < 2^E for every K block of
     //     the row (frexp exponent of the largest scale); and the BF16-rounded scales of
-    //     this CTA's K blocks.  The (row, K block) scales are read by all threads at once,
-    //     the K block fastest unless the scales are stored row-fastest (MN-major).
+    //     this CTA's K blocks, kept from the same pass.  The (row, K block) scales are read
+    //     by all threads at once, the K block fastest unless the scales are stored row-fastest
+    //     (MN-major).
     {
       const bool mn_major = !p.sa_packed && p.sa_stride_m == 1;
       const int items = ntok * kb_count;
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       constexpr int kU = 8;
       for (int it0 = tid; it0 < items; it0 += kU * blockDim.x) {
         float sraw[kU];
-        int rrs[kU];
+        int rrs[kU], kbs[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
           const int it = it0 + u * blockDim.x;
@@ -350,6 +353,7 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
           const int kb = mn_major ? it / ntok : it % kb_count;
           const bool mine = it < items && s_id[rr] == expert;
           rrs[u] = mine ? rr : -1;
+          kbs[u] = kb;
           sraw[u] = mine ? load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, row0 + rr, kb) : 1.0f;
         }
 #pragma unroll
@@ -359,6 +363,8 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
           // non-negative floats order as their bit patterns
           if (isfinite(sbf)) atomicMax(&s_smax_bits[rrs[u]], __float_as_uint(fabsf(sbf)));
           pow2 = pow2 && pow2_code(sraw[u]) >= 0;
+          const int kl = kbs[u] - kb0;
+          if (kl >= 0 && kl < kbn) s_scale[rrs[u]][kl] = sbf;  // this CTA's K blocks (routed rows only)
         }
       }
       if (!pow2) atomicAnd(&s_pow2, 0);
@@ -375,16 +381,6 @@ __global__ void __launch_bounds__(256) cdg_prep_kernel(PrepArgs p) {
       s_exp[tid] = emax;
       s_inv[tid] = ldexpf(1.0f, -emax);
       if (blockIdx.y == 0) p.row_exp[b * 128 + tid] = emax;
-    }
-#pragma unroll 4
-    for (int it = tid; it < ntok * kbn; it += blockDim.x) {
-      const int rr = it / kbn;
-      const int kl = it - rr * kbn;
-      const int r = row0 + rr;
-      s_scale[rr][kl] = s_id[rr] == expert
-          ? __bfloat162float(
-                __float2bfloat16_rn(load_sa(p.sa, p.sa_packed, p.sa_stride_m, p.sa_stride_k, r, kb0 + kl)))
-          : 0.0f;
     }
     __syncthreads();
   }
