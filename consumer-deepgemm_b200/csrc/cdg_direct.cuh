@@ -35,8 +35,7 @@
 // Warp roles per CTA: 0 = operand TMA producer, 1 = MMA issuer (even CTA, whole warp) and
 // TMEM owner, 2 = scale-factor copier (even CTA, whole warp), 3 = scale-atom TMA producer,
 // 4-11 = epilogue (two warps per TMEM lane quadrant, each taking every other 16-token
-// chunk).  All waits are bounded (kStatusTimeout).  D leaves as whole 256-byte row segments
-// from a staging tile the four warps of an epilogue half share (as in cdg_gemm_planes_kernel).
+// chunk).  All waits are bounded (kStatusTimeout).
 #pragma once
 
 #include "cdg_kernels.cuh"
@@ -56,9 +55,8 @@ struct DirectSmem {
   static constexpr int kSfRing = kStages * kStageBytes;              // [kSfStages][kKSF] weight scale atoms
   static constexpr int kTsfRing = kSfRing + kSfStages * kKSF * 512;  // [kSfStages][2] token scale atoms
   static constexpr int kEpiWarps = 8;                                // two per TMEM lane quadrant
-  // per epilogue half (four warps, one per TMEM lane quadrant): two [16 tokens][128 columns] bf16
-  static constexpr int kStaging = kTsfRing + kSfStages * 2 * 512;
-  static constexpr int kBarOffset = kStaging + 2 * 2 * 4096;
+  static constexpr int kStaging = kTsfRing + kSfStages * 2 * 512;    // kEpiWarps x [16 tokens][32 columns] bf16
+  static constexpr int kBarOffset = kStaging + kEpiWarps * 1024;
   // full, empty; sffull, sfsfree; sfready, sftfree; tfull[2], tempty[2], done
   static constexpr int kNumBars = 2 * kStages + 2 * kSfStages + 2 * kSfSlots + 5;
   static constexpr int kBarBytes = kNumBars * 8 + 16;                // + TMEM address
@@ -329,19 +327,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
     const int tid = threadIdx.x - 128;
     constexpr int kEpiThreads = 32 * L::kEpiWarps;
     const uint32_t tempty0 = cluster_addr(&tempty[0], 0);
-    // the half's two staging tiles [16 tokens][16 x 16-byte column chunks]; chunk c of token
-    // row r sits at c ^ (r % 8), so that the eight rows of one stmatrix matrix hit distinct banks
-    uint8_t* hst = smem + L::kStaging + half * 2 * 4096;
-    const uint32_t hst_u32 = smem_u32(hst);
-    const int bar_id = 1 + half;  // named barrier of the half's 128 threads
+    uint8_t* wst = smem + L::kStaging + (warp - 4) * 1024;  // [16 tokens][4 x 16-byte column chunks], swizzled
+    const uint32_t wst_u32 = smem_u32(wst);
     // stmatrix row addresses: thread 8k + i gives row i of matrix k, i.e. token i + 8*(k/2),
-    // column chunk 4q + (k%2) (+2 for the second register set)
+    // column chunk (k%2) (+2 for the second 16-lane half); chunk c of row r sits at c ^ ((r/2)%4)
     const int sm_row = (lane & 7) + 8 * (lane >> 4);
-    const int sm_chunk = 4 * q + ((lane >> 3) & 1);
-    const uint32_t sm_off0 = sm_row * 256 + ((sm_chunk ^ (sm_row & 7)) << 4);
-    const uint32_t sm_off1 = sm_row * 256 + (((sm_chunk + 2) ^ (sm_row & 7)) << 4);
-    const int hth = q * 32 + lane;  // 0..127 within the half
-    int sbuf = 0;  // staging tile of the next chunk
+    const int sm_chunk = (lane >> 3) & 1;
+    const uint32_t sm_addr0 = wst_u32 + sm_row * 64 + ((sm_chunk ^ ((sm_row >> 1) & 3)) << 4);
+    const uint32_t sm_addr1 = wst_u32 + sm_row * 64 + (((sm_chunk + 2) ^ ((sm_row >> 1) & 3)) << 4);
     int local = 0;
     for (int t = pair; t < tiles && ok; t += npairs, ++local) {
       const int4 cur = __ldg(&p.list[t / n_pt]);
@@ -357,16 +350,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
       for (int i = 0; i < 3; ++i) mk[i] = b0 + i < p.nblk ? __ldg(p.blk_mask + b0 + i) : make_uint4(0, 0, 0, 0);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      const bool got = mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
-                                         wait_code(4, static_cast<int>(rank), acc, acc_phase, local));
-      // the half's four warps leave together (each wait is bounded, so each reaches this)
-      if (!bar_and(bar_id, 128, got)) {
+      if (!mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
+                             wait_code(4, static_cast<int>(rank), acc, acc_phase, local))) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * L::kAccCols;
-      for (int c0 = half; c0 < nchunk; c0 += 4) {  // uniform over the half's four warps
+      const int dcol = nt * 128 + q * 32;
+      for (int c0 = half; c0 < nchunk; c0 += 4) {
         uint32_t ra[2][8], rb[2][8];  // lanes 0-15 and 16-31 of the quadrant, chunks c0 and c0 + 2
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -388,16 +380,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
               m[k] = *reinterpret_cast<uint32_t*>(&a);
               m[4 + k] = *reinterpret_cast<uint32_t*>(&b);
             }
-            // matrices: (columns 0-7 | 8-15, tokens 0-7 | 8-15) of each 16-lane half; the
-            // staging tile written two chunks ago was read by every thread of the half before
-            // the last barrier, so it is free again
-            const uint32_t st0 = hst_u32 + sbuf * 4096;
-            stmatrix_x4_trans(st0 + sm_off0, m[0], m[1], m[2], m[3]);
-            stmatrix_x4_trans(st0 + sm_off1, m[4], m[5], m[6], m[7]);
-            bar_sync(bar_id, 128);
+            // matrices: (columns 0-7 | 8-15, tokens 0-7 | 8-15) of each 16-lane half
+            stmatrix_x4_trans(sm_addr0, m[0], m[1], m[2], m[3]);
+            stmatrix_x4_trans(sm_addr1, m[4], m[5], m[6], m[7]);
+            __syncwarp();
 #pragma unroll
             for (int s = 0; s < 2; ++s) {
-              const int vi = hth + 128 * s, rr = vi >> 4, part = vi & 15;
+              const int vi = lane + 32 * s, rr = vi >> 2, part = vi & 3;
               const int tok = j0 + rr;
               if (tok < cur.y) {  // tokens past the tile belong to the next tile of the run
                 const int br = br0 + tok;
@@ -407,12 +396,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
                 const uint32_t word = wi == 0 ? w4.x : wi == 1 ? w4.y : wi == 2 ? w4.z : w4.w;
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if ((word >> (br & 31)) & 1u)
-                  v = *reinterpret_cast<const uint4*>(hst + sbuf * 4096 + rr * 256 + ((part ^ (rr & 7)) << 4));
+                  v = *reinterpret_cast<const uint4*>(wst + rr * 64 + ((part ^ ((rr >> 1) & 3)) << 4));
                 __nv_bfloat16* rp = d_row(p, static_cast<int64_t>(drow0 + tok));
-                if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + part * 8) = v;
+                if (rp) *reinterpret_cast<uint4*>(rp + dcol + part * 8) = v;
               }
             }
-            sbuf ^= 1;
+            __syncwarp();
           }
         }
       }

@@ -39,13 +39,6 @@
 // TMEM owner, 2 = scale-factor copier (even CTA, whole warp), 3 = scale-atom TMA producer,
 // 4-11 = epilogue (two warps per TMEM lane quadrant, each taking every other group of 8
 // tokens).  All waits are bounded (kStatusTimeout).
-//
-// D stores.  The four warps of an epilogue half (one per lane quadrant, 32 output columns
-// each) put a group's [8 tokens][128 columns] into one shared staging tile, meet at a named
-// barrier, and store it as whole 256-byte row segments (16 threads per token row).  Rows that
-// go to other GPUs (the expert-parallel layer's FC2 writes its rows into the source ranks'
-// windows through a row table) then travel as full segments instead of four 64-byte pieces
-// from four warps, which is what the NVLink store rate depends on.
 #pragma once
 
 #include "cdg_kernels.cuh"
@@ -77,9 +70,8 @@ struct PlanesSmem {
   static constexpr int kSfRing = kStages * kStageBytes;              // [kSfStages][kKSF] weight scale atoms
   static constexpr int kConstSf = kSfRing + kSfStages * kKSF * 512;  // 512 bytes of UE8M0 127
   static constexpr int kEpiWarps = 8;                                // two per TMEM lane quadrant
-  // per epilogue half (four warps, one per TMEM lane quadrant): two [8 tokens][128 columns] bf16
-  static constexpr int kStaging = kConstSf + 512;
-  static constexpr int kBarOffset = kStaging + 2 * 2 * 2048;
+  static constexpr int kStaging = kConstSf + 512;                    // kEpiWarps x [8 tokens][32 columns] bf16
+  static constexpr int kBarOffset = kStaging + kEpiWarps * 512;
   // full, empty; sffull, sfready, sftfree; tfull[2], tempty[2], done
   static constexpr int kNumBars = 2 * kStages + 3 * kSfStages + 5;
   static constexpr int kBarBytes = kNumBars * 8 + 16;                // + TMEM address
@@ -340,24 +332,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
     const int tid = threadIdx.x - 128;
     constexpr int kEpiThreads = 32 * L::kEpiWarps;
     const uint32_t tempty0 = cluster_addr(&tempty[0], 0);
-    // the half's two staging tiles [8 tokens][16 x 16-byte column chunks]; chunk c of token
-    // row r sits at c ^ r, so that the eight rows of one stmatrix matrix hit distinct banks
-    uint8_t* hst = smem + L::kStaging + half * 2 * 2048;
-    const uint32_t hst_u32 = smem_u32(hst);
-    const int bar_id = 1 + half;  // named barrier of the half's 128 threads
+    uint8_t* wst = smem + L::kStaging + (warp - 4) * 512;  // [8 tokens][4 x 16-byte column chunks], swizzled
+    const uint32_t wst_u32 = smem_u32(wst);
     // stmatrix row addresses: thread 8k + i gives row i (token i) of the transpose of matrix
-    // k (output columns 8k..8k+7 of the warp's 32, chunk 4q + k of the 128)
+    // k (output columns 8k..8k+7 of the warp's 32); chunk c of row r sits at c ^ ((r/2)%4)
     const int sm_row = lane & 7;
-    const int sm_chunk = 4 * q + (lane >> 3);
-    const uint32_t sm_off = sm_row * 256 + ((sm_chunk ^ sm_row) << 4);
-    // the 16-byte piece of D this thread stores: token st_tok of the group, chunk st_part
-    const int hth = q * 32 + lane;  // 0..127 within the half
-    const int st_tok = hth >> 4, st_part = hth & 15;
-    const int st_off = st_tok * 256 + ((st_part ^ st_tok) << 4);
+    const int sm_chunk = lane >> 3;
+    const uint32_t sm_addr = wst_u32 + sm_row * 64 + ((sm_chunk ^ ((sm_row >> 1) & 3)) << 4);
+    const int ld_tok = lane >> 2, ld_part = lane & 3;  // the 16-byte piece of D this thread stores
+    const uint8_t* ld_src = wst + ld_tok * 64 + ((ld_part ^ ((ld_tok >> 1) & 3)) << 4);
     const int c = 2 * (lane & 3);                       // tokens c, c+1 of each group (tcgen05.ld 16x256b)
     constexpr int kGroups = (kPlanesTileTok / 8 + 1) / 2;  // groups per warp
     int local = 0;
-    int sbuf = 0;  // staging tile of the next group
     for (int t = pair; t < tiles && ok; t += npairs, ++local) {
       const int4 cur = __ldg(&p.list[t / n_pt]);
       const int pr0 = cur.x;  // first plane row of the tile
@@ -380,16 +366,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       const uint4 m1 = b0 + 1 < p.nblk ? __ldg(p.blk_mask + b0 + 1) : make_uint4(0, 0, 0, 0);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      const bool got = mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
-                                         wait_code(4, static_cast<int>(rank), acc, acc_phase, local));
-      // the half's four warps leave together (each wait is bounded, so each reaches this)
-      if (!bar_and(bar_id, 128, got)) {
+      if (!mbar_wait_cluster(&tfull[acc], acc_phase, p.status,
+                             wait_code(4, static_cast<int>(rank), acc, acc_phase, local))) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * L::kAccCols;
-      const int dcol = nt * 128 + st_part * 8;
+      const int dcol = nt * 128 + q * 32 + ld_part * 8;
 #pragma unroll
       for (int j0 = 0; j0 < kGroups; j0 += 2) {
         if (half + 2 * j0 < ng) {
@@ -407,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
           for (int i = 0; i < 2; ++i) {
             const int j = j0 + i;
             const int g = half + 2 * j;
-            if (j < kGroups && g < ng) {  // uniform over the half's four warps
+            if (j < kGroups && g < ng) {
               const float s0 = __uint_as_float(static_cast<uint32_t>(min(max(ev[j].x + 127, 1), 254)) << 23);
               const float s1 = __uint_as_float(static_cast<uint32_t>(min(max(ev[j].y + 127, 1), 254)) << 23);
               uint32_t frag[4];
@@ -421,22 +405,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
                 __nv_bfloat162 b = __floats2bfloat162_rn(x0, x1);
                 frag[m] = *reinterpret_cast<uint32_t*>(&b);
               }
-              // the staging tile written two groups ago was read by every thread of the half
-              // before the last barrier, so it is free again
-              stmatrix_x4_trans(hst_u32 + sbuf * 2048 + sm_off, frag[0], frag[1], frag[2], frag[3]);
-              bar_sync(bar_id, 128);
-              const int tok = g * 8 + st_tok;
+              stmatrix_x4_trans(sm_addr, frag[0], frag[1], frag[2], frag[3]);
+              __syncwarp();
+              const int tok = g * 8 + ld_tok;
               if (tok < cur.y) {  // tokens past the tile belong to the next tile of the run
                 const int pr = pr0 + tok;
                 const uint4 mk = (pr >> 7) == b0 ? m0 : m1;
                 const int wi = (pr >> 5) & 3;
                 const uint32_t word = wi == 0 ? mk.x : wi == 1 ? mk.y : wi == 2 ? mk.z : mk.w;
                 uint4 v = make_uint4(0, 0, 0, 0);
-                if ((word >> (pr & 31)) & 1u) v = *reinterpret_cast<const uint4*>(hst + sbuf * 2048 + st_off);
+                if ((word >> (pr & 31)) & 1u) v = *reinterpret_cast<const uint4*>(ld_src);
                 __nv_bfloat16* rp = d_row(p, static_cast<int64_t>(drow0 + tok));
                 if (rp) *reinterpret_cast<uint4*>(rp + dcol) = v;
               }
-              sbuf ^= 1;
+              __syncwarp();
             }
           }
         }

@@ -443,23 +443,6 @@ __device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)
 // Four 8x8 b16 matrices, stored transposed: register k of thread t holds row t/4, columns
 // 2*(t%4) and +1 (low half first) of matrix k; row i of the stored transpose of matrix k
 // (16 bytes) goes to the address given by thread 8*k + i.
-// Named barrier `id` over `count` threads (whole warps) that also ANDs a predicate across them.
-__device__ __forceinline__ bool bar_and(int id, int count, bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\tbar.red.and.pred po, %2, %3, pi;\n\t"
-      "selp.u32 %0, 1, 0, po;\n\t}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
-      : "memory");
-  return out != 0;
-}
-
-// Named barrier `id` over `count` threads (whole warps).
-__device__ __forceinline__ void bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, uint32_t m0, uint32_t m1, uint32_t m2, uint32_t m3) {
   asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(m0), "r"(m1),
                "r"(m2), "r"(m3)
