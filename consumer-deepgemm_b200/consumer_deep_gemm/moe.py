@@ -36,8 +36,10 @@ the collectives by the library's own peer-memory exchange: each rank owns an exc
 window shared through CUDA IPC; the dispatch kernel quantises each token's row once and
 stores it straight into the window of every rank that owns one of its experts (one row per
 token and rank, listing the token's local experts there), the receiver expands it into the
-experts' groups, the return kernel stores GEMM rows straight back into the sources' windows
-at their slot, and release/acquire flags (bounded waits) order the steps.
+experts' groups, FC2's epilogue stores each of its rows straight back into the source's
+window at the row's slot (a row table the receiver's permute writes; ``fused_return=False``
+uses a separate return kernel instead), and release/acquire flags (bounded waits) order the
+steps.
 
 The device steps sit behind a small ``ops`` interface so that the exchange
 logic can also be exercised with CPU implementations (tests do that with the
