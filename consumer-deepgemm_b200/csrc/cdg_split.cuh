@@ -27,22 +27,25 @@ __device__ __forceinline__ int plane_exponent(float smax, bool* in_range) {
 }
 
 // Sixteen e4m3 codes (one 16-byte chunk of a row) with their block's BF16 scale `sbf` and the
-// row's 2^-E `inv` -> the chunk of each plane.  Two elements per conversion instruction
-// (e4m3x2 <-> f16x2, f32x2 -> bf16x2 / e4m3x2), the same roundings as one at a time.
+// row's 2^-E `inv` -> the chunk of each plane.  Two elements per conversion instruction.
+//   * v = bf16(a * (sbf * 2^-E)) equals bf16(a * sbf) * 2^-E: a * sbf is exact in FP32 (4 + 8
+//     significant bits) and scaling by a power of two commutes with the rounding (outside
+//     BF16's subnormal range, which no scale of one row reaches relative to the row's largest);
+//   * lo = e4m3(v - hi) with the difference taken in f16x2: v and hi are f16 numbers whenever
+//     |v| >= 2^-17, and below that hi and lo are both zero either way, so the difference is
+//     exact and lo is the same code as from FP32.
 __device__ __forceinline__ void split_planes16(const uint4 raw, float sbf, float inv, uint4& hi4, uint4& lo4) {
+  const float sp = sbf * inv;
   const uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
   uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const __nv_fp8x2_storage_t a2 = static_cast<__nv_fp8x2_storage_t>(in[i >> 1] >> (16 * (i & 1)));
-    const __half2_raw ar = __nv_cvt_fp8x2_to_halfraw2(a2, __NV_E4M3);
-    const float2 af = __half22float2(__half2(ar));
-    const float2 x = __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(af.x, sbf), __fmul_rn(af.y, sbf)));
-    const float2 v = make_float2(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv));
+    const float2 af = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(a2, __NV_E4M3)));
+    const float2 v = __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(af.x, sp), __fmul_rn(af.y, sp)));
     const __nv_fp8x2_storage_t h = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
-    const float2 hf = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(h, __NV_E4M3)));
-    const __nv_fp8x2_storage_t l =
-        __nv_cvt_float2_to_fp8x2(make_float2(__fsub_rn(v.x, hf.x), __fsub_rn(v.y, hf.y)), __NV_SATFINITE, __NV_E4M3);
+    const __half2 d = __hsub2(__float22half2_rn(v), __half2(__nv_cvt_fp8x2_to_halfraw2(h, __NV_E4M3)));
+    const __nv_fp8x2_storage_t l = __nv_cvt_halfraw2_to_fp8x2(static_cast<__half2_raw>(d), __NV_SATFINITE, __NV_E4M3);
     hw[i >> 1] |= static_cast<uint32_t>(h) << (16 * (i & 1));
     lw[i >> 1] |= static_cast<uint32_t>(l) << (16 * (i & 1));
   }
