@@ -57,6 +57,9 @@ namespace cdg {
 #ifndef CDG_PLANES_SF_STAGES
 #define CDG_PLANES_SF_STAGES 3
 #endif
+#ifndef CDG_PLANES_EPI_WARPS
+#define CDG_PLANES_EPI_WARPS 8
+#endif
 
 struct PlanesSmem {
   static constexpr int kKS = CDG_PLANES_KS;       // K steps per operand stage
@@ -69,7 +72,9 @@ struct PlanesSmem {
   static constexpr int kStageBytes = kKS * kStep;
   static constexpr int kSfRing = kStages * kStageBytes;              // [kSfStages][kKSF] weight scale atoms
   static constexpr int kConstSf = kSfRing + kSfStages * kKSF * 512;  // 512 bytes of UE8M0 127
-  static constexpr int kEpiWarps = 8;                                // two per TMEM lane quadrant
+  static constexpr int kEpiWarps = CDG_PLANES_EPI_WARPS;             // kEpiSets per TMEM lane quadrant
+  static constexpr int kEpiSets = kEpiWarps / 4;
+  static_assert(kEpiWarps % 4 == 0, "whole sets of four quadrant warps");
   static constexpr int kStaging = kConstSf + 512;                    // kEpiWarps x [8 tokens][32 columns] bf16
   static constexpr int kBarOffset = kStaging + kEpiWarps * 512;
   // full, empty; sffull, sfready, sftfree; tfull[2], tempty[2], done
@@ -328,7 +333,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;            // TMEM lane quadrant this warp may access
-    const int half = (warp - 4) >> 2;  // this warp's token groups: half, half + 2, ...
+    const int half = (warp - 4) >> 2;  // this warp's token groups: half, half + kEpiSets, ...
+    constexpr int kSets = L::kEpiSets;
     const int tid = threadIdx.x - 128;
     constexpr int kEpiThreads = 32 * L::kEpiWarps;
     const uint32_t tempty0 = cluster_addr(&tempty[0], 0);
@@ -342,7 +348,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
     const int ld_tok = lane >> 2, ld_part = lane & 3;  // the 16-byte piece of D this thread stores
     const uint8_t* ld_src = wst + ld_tok * 64 + ((ld_part ^ ((ld_tok >> 1) & 3)) << 4);
     const int c = 2 * (lane & 3);                       // tokens c, c+1 of each group (tcgen05.ld 16x256b)
-    constexpr int kGroups = (kPlanesTileTok / 8 + 1) / 2;  // groups per warp
+    constexpr int kGroups = (kPlanesTileTok / 8 + kSets - 1) / kSets;  // groups per warp (of 2h / 8 <= 14)
     int local = 0;
     for (int t = pair; t < tiles && ok; t += npairs, ++local) {
       const int4 cur = __ldg(&p.list[t / n_pt]);
@@ -359,7 +365,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       int2 ev[kGroups];
 #pragma unroll
       for (int j = 0; j < kGroups; ++j) {
-        const int g = half + 2 * j;
+        const int g = half + kSets * j;
         ev[j] = g < ng ? __ldg(reinterpret_cast<const int2*>(p.row_exp + pr0 + g * 8 + c)) : make_int2(0, 0);
       }
       const uint4 m0 = __ldg(p.blk_mask + b0);
@@ -376,11 +382,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       const int dcol = nt * 128 + q * 32 + ld_part * 8;
 #pragma unroll
       for (int j0 = 0; j0 < kGroups; j0 += 2) {
-        if (half + 2 * j0 < ng) {
+        if (half + kSets * j0 < ng) {
           uint32_t ra[2][8], rb[2][8];  // lanes 0-15 and 16-31 of the quadrant, two groups
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
-            const int g = half + 2 * (j0 + i);
+            const int g = half + kSets * (j0 + i);
             if (j0 + i < kGroups && g < ng) {
               tmem_ld_16x256b_x2(taddr + g * 16, ra[i]);
               tmem_ld_16x256b_x2(taddr + (16u << 16) + g * 16, rb[i]);
@@ -390,7 +396,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int j = j0 + i;
-            const int g = half + 2 * j;
+            const int g = half + kSets * j;
             if (j < kGroups && g < ng) {
               const float s0 = __uint_as_float(static_cast<uint32_t>(min(max(ev[j].x + 127, 1), 254)) << 23);
               const float s1 = __uint_as_float(static_cast<uint32_t>(min(max(ev[j].y + 127, 1), 254)) << 23);
