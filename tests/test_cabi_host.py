@@ -78,6 +78,23 @@ def test_can_implement_envelope():
     assert lib.cdg_grouped_fp8_fp4_workspace_bytes(ctypes.byref(bad)) == 0
 
 
+def test_row_table_output_arguments():
+    """cdg_gemm_args.d_rows (ABI 2): a row table replaces `d` (which may then be NULL) for a BF16
+    output only; without either there is no output."""
+    lib = cabi.lib()
+    assert ctypes.sizeof(cabi.GemmArgs) == cabi.GemmArgs.d_rows.offset + 8  # the last field, as in the header
+    g = _args()
+    g.d_rows, g.d = 1 << 21, None
+    assert lib.cdg_can_implement(ctypes.byref(g)) == 1
+    g = _args(d_dtype=torch.float32)
+    g.d_rows = 1 << 21
+    assert lib.cdg_can_implement(ctypes.byref(g)) == -1
+    g = _args()
+    g.d = None
+    assert lib.cdg_can_implement(ctypes.byref(g)) == -1
+    assert lib.cdg_status_string(9) != lib.cdg_status_string(6)  # skipped access vs wait timeout
+
+
 def test_workspace_size_covers_activation_planes():
     lib = cabi.lib()
     g = _args(M=1000, N=256, K=512, E=4)
