@@ -465,10 +465,14 @@ __global__ void __launch_bounds__(256) silu_mul_quant_16b_kernel(const __nv_bflo
 // memory, then the row is split into the GEMM's two e4m3 planes (cdg_split.cuh):
 // planes[0][r], planes[1][r] (plane stride M * I) and row_exp[r].  Rows whose m_indices entry
 // is negative are skipped.
+// KB: the row's 128-column blocks when known at compile time (0: from I), so that the common
+// widths run fully unrolled loops (the kernel is issue-bound).
+template <int KB>
 __global__ void __launch_bounds__(256) silu_mul_quant_planes_kernel(const __nv_bfloat16* in, int64_t in_stride,
                                                                     int64_t M, int64_t I, const int32_t* m_indices,
                                                                     uint8_t* planes, int32_t* row_exp) {
   extern __shared__ __align__(16) uint8_t act_stage[];
+  if (KB) I = KB * 128;
   const int64_t kb_count = I / 128;
   const int64_t chunks = (kb_count + 3) / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 7, blk = lane >> 3;
@@ -1479,13 +1483,15 @@ int cdg_silu_mul_quant_planes(const void* in, int64_t in_stride, int64_t M, int6
   if (M == 0) return CDG_OK;
   const size_t smem = 8 * static_cast<size_t>(cdg::row_stage_bytes(I));
   if (smem > 200 * 1024) return CDG_ERR_UNSUPPORTED;
+  auto kernel = I == 2048 ? cdg::silu_mul_quant_planes_kernel<16>
+                : I == 1024 ? cdg::silu_mul_quant_planes_kernel<8>
+                            : cdg::silu_mul_quant_planes_kernel<0>;
   if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(cdg::silu_mul_quant_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return CDG_ERR_CUDA;
   const unsigned grid =
       static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((M + 7) / 8, int64_t(cdg::sm_count()) * 8)));
-  cdg::silu_mul_quant_planes_kernel<<<grid, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  kernel<<<grid, 256, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(in), in_stride, M, I, m_indices, planes, row_exp);
   return cdg::launched();
 }
