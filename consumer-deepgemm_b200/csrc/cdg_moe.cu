@@ -398,10 +398,14 @@ __global__ void __launch_bounds__(256) silu_mul_quant_vec_kernel(const __nv_bflo
 // three shuffles, and two conversions to e4m3 per instruction.  A grid of a few CTAs per SM
 // strides over the items; a row whose m_indices entry is negative is skipped before any of its
 // values is read.  Same arithmetic as the paths above (silu_mul, quant_block_values_mul).
+// KB: the row's 128-column blocks when known at compile time (0: from I); the warp's (row,
+// chunk) split is then a shift instead of a 64-bit division.
+template <int KB>
 __global__ void __launch_bounds__(256) silu_mul_quant_16b_kernel(const __nv_bfloat16* in, int64_t in_stride,
                                                                  int64_t M, int64_t I, const int32_t* m_indices,
                                                                  uint8_t* q, int64_t q_stride, float* s,
                                                                  int64_t s_stride_m, int64_t s_stride_k, int pow2) {
+  if (KB) I = KB * 128;
   const int64_t kb_count = I / 128;
   const int64_t chunks = (kb_count + 3) / 4;
   const int64_t items = M * chunks;
@@ -1270,8 +1274,10 @@ int cdg_silu_mul_quant_fp8(const void* in, int64_t in_stride, int64_t M, int64_t
     const int64_t warps = M * ((I / 128 + 3) / 4);
     const unsigned grid =
         static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, int64_t(cdg::sm_count()) * 16)));
-    cdg::silu_mul_quant_16b_kernel<<<grid, 256, 0, st>>>(h, in_stride, M, I, m_indices, q, q_stride, s, s_stride_m,
-                                                          s_stride_k, scale_fmt);
+    auto kernel = I == 2048 ? cdg::silu_mul_quant_16b_kernel<16>
+                  : I == 1024 ? cdg::silu_mul_quant_16b_kernel<8>
+                              : cdg::silu_mul_quant_16b_kernel<0>;
+    kernel<<<grid, 256, 0, st>>>(h, in_stride, M, I, m_indices, q, q_stride, s, s_stride_m, s_stride_k, scale_fmt);
   } else if (vec) {
     const int64_t chunks = (I / 128 + cdg::kSiluBlocks - 1) / cdg::kSiluBlocks;
     cdg::silu_mul_quant_vec_kernel<<<cdg::warp_grid(M * chunks), 256, 0, st>>>(
