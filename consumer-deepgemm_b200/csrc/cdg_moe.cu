@@ -998,7 +998,10 @@ __global__ void __launch_bounds__(256) ep_permute_p2p_kernel(int64_t E_local, in
           m_indices[pos] = el;
           const int64_t slot = static_cast<int64_t>(t) * topk + lane;
           ret_slot[pos] = static_cast<int32_t>(src * cap + slot);
-          if (ret_rows) ret_rows[pos] = ps.peers[src] + ret_off + slot * H * 2;
+          if (ret_rows) {  // a missing window (address 0) leaves the row unreturned rather than misdirected
+            const uint64_t base = ps.peers[src];
+            ret_rows[pos] = base ? base + ret_off + slot * H * 2 : 0;
+          }
         } else {
           atomicOr(reinterpret_cast<int32_t*>(ps.own + Window::kStatus), 2);
           atomicOr(&g_ep_sticky_status[0], 2);
