@@ -208,9 +208,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
       uint32_t sfphase = 0;
       const uint32_t sffull0 = cluster_addr(&sffull[0], 0);
       const int stages = (k_steps + KSF - 1) / KSF;
+      int next = pair < tiles ? __ldg(&p.list[pair / n_pt]).z : 0;
       for (int t = pair; t < tiles && ok; t += npairs) {
         const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
-        const int expert = __ldg(&p.list[t / n_pt]).z;
+        const int expert = next;  // read a tile ahead: the load stays off the tile boundary
+        if (t + npairs < tiles) next = __ldg(&p.list[(t + npairs) / n_pt]).z;
         const int atom0 = (expert * n_tiles + nt) * k_steps;
         const int tatom0 = (t / n_pt) * stages * 2;  // the tile's token atoms, two per stage
         for (int kb0 = 0, st = 0; kb0 < k_steps; kb0 += KSF, ++st) {
@@ -242,8 +244,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(DirectSmem::kThreads
       int stage = 0, sfs = 0;
       uint32_t phase = 0, sfphase = 0;
       int local = 0;
+      int4 next = pair < tiles ? __ldg(&p.list[pair / n_pt]) : make_int4(0, 0, 0, 0);
       for (int t = pair; t < tiles && ok; t += npairs, ++local) {
-        const int4 cur = __ldg(&p.list[t / n_pt]);
+        const int4 cur = next;  // read a tile ahead: the load stays off the tile boundary
+        if (t + npairs < tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
         const uint32_t n_mma = __shfl_sync(0xffffffffu, 2u * static_cast<uint32_t>(tile_half(cur.y)), 0);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;

@@ -179,8 +179,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
       int stage = 0;
       uint32_t phase = 0;
       const uint32_t full0 = cluster_addr(&full[0], 0);
+      int4 next = pair < reg_tiles ? __ldg(&p.list[pair / n_pt]) : make_int4(0, 0, 0, 0);
       for (int t = pair; t < reg_tiles && ok; t += npairs) {
-        const int4 cur = __ldg(&p.list[t / n_pt]);
+        const int4 cur = next;  // read a tile ahead: the load stays off the tile boundary
+        if (t + npairs < reg_tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
         const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
         const int atom0 = (cur.y * n_tiles + nt) * k_steps;
         const int a_row = cur.x * 128;

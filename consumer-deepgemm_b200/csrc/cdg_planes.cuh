@@ -222,8 +222,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       int sfs = 0;
       uint32_t sfphase = 0;
       const uint32_t sffull0 = cluster_addr(&sffull[0], 0);
+      int4 next = pair < tiles ? __ldg(&p.list[pair / n_pt]) : make_int4(0, 0, 0, 0);
       for (int t = pair; t < tiles && ok; t += npairs) {
-        const int4 cur = __ldg(&p.list[t / n_pt]);
+        const int4 cur = next;  // read a tile ahead: the load stays off the tile boundary
+        if (t + npairs < tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
         const int nt = 2 * (t % n_pt) + static_cast<int>(rank);
         const int atom0 = (cur.z * n_tiles + nt) * k_steps;
         for (int kb0 = 0; kb0 < k_steps; kb0 += KSF) {
@@ -258,8 +260,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PlanesSmem::kThreads
       int stage = 0, sfs = 0;
       uint32_t phase = 0, sfphase = 0;
       int local = 0;
+      int4 next = pair < tiles ? __ldg(&p.list[pair / n_pt]) : make_int4(0, 0, 0, 0);
       for (int t = pair; t < tiles && ok; t += npairs, ++local) {
-        const int4 cur = __ldg(&p.list[t / n_pt]);
+        const int4 cur = next;  // read a tile ahead: the load stays off the tile boundary
+        if (t + npairs < tiles) next = __ldg(&p.list[(t + npairs) / n_pt]);
         const uint32_t n_mma = __shfl_sync(0xffffffffu, 4u * static_cast<uint32_t>(tile_half(cur.y)), 0);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
