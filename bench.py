@@ -165,15 +165,61 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------ CPU baselines
+_REF_PKG = os.path.join(HERE, "baseline", "_ref", "consumer_deep_gemm")
+_REF_MATH = os.path.join(HERE, "baseline", "_ref", "deep_gemm", "utils", "math.py")
+_CPU_IMPL = None
+
+
+def cpu_impl():
+    """The CPU implementation of the path that the CPU baselines and the reference arm time.
+
+    When the reference is installed under baseline/_ref (pip --target, pure Python), its own
+    CPU path is loaded from there under private module names, so that it cannot collide with
+    this repository's package of the same name: the GEMM is the reference's dequant + FP32 mm
+    per active expert, `_m_grouped_fp8_fp4_dequant_mm_nt` (consumer_deep_gemm/gemm.py:411-464;
+    its public entry, gemm.py:467-470, needs Triton and a GPU), and the activation quantisation
+    is its `per_block_cast_to_fp8` (deep_gemm/utils/math.py:21-37); kind "reference".  Without
+    the install, the oracle's restatement of the same functions; kind "port".
+    Returns {"gemm": fn(a, b, d, m_indices), "quant": fn(x) -> (fp8, scale), "kind": ...}.
+    """
+    global _CPU_IMPL
+    if _CPU_IMPL is not None:
+        return _CPU_IMPL
+    if os.path.isfile(os.path.join(_REF_PKG, "gemm.py")) and os.path.isfile(_REF_MATH):
+        import importlib.util
+
+        spec = importlib.util.spec_from_file_location("_cdg_reference", os.path.join(_REF_PKG, "__init__.py"),
+                                                      submodule_search_locations=[_REF_PKG])
+        pkg = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = pkg
+        spec.loader.exec_module(pkg)
+        mspec = importlib.util.spec_from_file_location("_cdg_reference_math", _REF_MATH)
+        rmath = importlib.util.module_from_spec(mspec)
+        mspec.loader.exec_module(rmath)
+        _CPU_IMPL = {"gemm": pkg.gemm._m_grouped_fp8_fp4_dequant_mm_nt, "quant": rmath.per_block_cast_to_fp8,
+                     "kind": "reference"}
+    else:
+        from deep_gemm.utils.math import per_block_cast_to_fp8
+        from oracle import cdg_oracle as oracle
+
+        _CPU_IMPL = {"gemm": oracle.m_grouped_fp8_fp4_gemm_nt_contiguous, "quant": per_block_cast_to_fp8,
+                     "kind": "port"}
+    return _CPU_IMPL
+
+
+def _impl_name(impl):
+    return ("reference's own _m_grouped_fp8_fp4_dequant_mm_nt (baseline/_ref)" if impl["kind"] == "reference"
+            else "oracle port of the reference's GEMM")
+
+
 def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
-    """Time the CPU oracle (the reference's dequant + matmul restated) on a bounded sample.
+    """Time the CPU implementation (`cpu_impl`) of the GEMM on a bounded sample.
 
     The sample is the routed rows of the first few active experts, grown until
     one call takes about `budget_s`.  Returns ({"GB/s": .., "TFLOP/s": ..}, cores,
     description), rates of the median call.
     """
-    from oracle import cdg_oracle as oracle
-
+    impl = cpu_impl()
     torch.set_num_threads(os.cpu_count() or 1)
     cfg = inp["cfg"]
     ids = inp["m_indices"].cpu()
@@ -189,7 +235,7 @@ def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0)
         sb = inp["sb"][sel.to(inp["sb"].device)].cpu()
         d = torch.empty(rows.numel(), cfg.n, dtype=torch.bfloat16)
         t0 = time.perf_counter()
-        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((a[rows], sa[rows]), (b, sb), d, sub[ids[rows].long()])
+        impl["gemm"]((a[rows], sa[rows]), (b, sb), d, sub[ids[rows].long()])
         return time.perf_counter() - t0, gemm_bytes(rows.numel(), sel.numel(), cfg.n, cfg.k), rows.numel()
 
     dt, _, _ = run(1)
@@ -201,27 +247,26 @@ def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0)
         dt, nbytes, r = run(n_exp)
         times.append(dt)
     dt = statistics.median(times)
-    desc = (f"{cfg.name}: {r} routed rows of {n_exp} of {experts.numel()} active experts, "
-            f"median of {len(times)} calls ({dt:.2f} s each), torch CPU threads={torch.get_num_threads()}")
+    desc = (f"{cfg.name}: {r} routed rows of {n_exp} of {experts.numel()} active experts through the "
+            f"{_impl_name(impl)}, median of {len(times)} calls ({dt:.2f} s each), "
+            f"torch CPU threads={torch.get_num_threads()}")
     rates = {"GB/s": nbytes / dt / 1e9, "TFLOP/s": 2.0 * r * cfg.n * cfg.k / dt / 1e12}
     return rates, torch.get_num_threads(), desc
 
 
 def cpu_layer_sample(x, ids, w1, s1, w2, s2, ue8m0=False, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
-    """Time the CPU reference of the MoE layer (the oracle's grouped GEMM for FC1 and FC2, the
-    reference quantisation and SiLU-mul between them) on the first tokens of a batch, grown
-    until one call takes about `budget_s`.  Weights are fetched per call for the experts the
-    sample touches.  Returns (TFLOP/s of the median call, cores, description)."""
-    from deep_gemm.utils.math import per_block_cast_to_fp8
-    from oracle import cdg_oracle as oracle
-
+    """Time the CPU implementation (`cpu_impl`) of the MoE layer (its grouped GEMM for FC1 and
+    FC2, its 1x128 quantisation and a torch SiLU-mul between them) on the first tokens of a
+    batch, grown until one call takes about `budget_s`.  Weights are fetched per call for the
+    experts the sample touches.  Returns (TFLOP/s of the median call, cores, description)."""
+    impl = cpu_impl()
     torch.set_num_threads(os.cpu_count() or 1)
     I2, H = w1.shape[1], x.shape[1]
     inter = w2.shape[2] * 2
     ids = ids.cpu()
 
     def quant(v):
-        return _quant_pow2(v) if ue8m0 else per_block_cast_to_fp8(v.float())
+        return _quant_pow2(v) if ue8m0 else impl["quant"](v.float())
 
     def run(n_tok):
         tids = ids[:n_tok]
@@ -236,11 +281,11 @@ def cpu_layer_sample(x, ids, w1, s1, w2, s2, ue8m0=False, budget_s: float = 4.0,
         t0 = time.perf_counter()
         q, s = quant(xs)
         h = torch.empty(rows_tok.numel(), I2, dtype=torch.bfloat16)
-        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((q[rows_tok], s[rows_tok]), (b1, b1s), h, m_idx)
+        impl["gemm"]((q[rows_tok], s[rows_tok]), (b1, b1s), h, m_idx)
         v = torch.nn.functional.silu(h[:, :inter].float()) * h[:, inter:].float()
         q2, s2_ = quant(v)
         y = torch.empty(rows_tok.numel(), H, dtype=torch.bfloat16)
-        oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((q2, s2_), (b2, b2s), y, m_idx)
+        impl["gemm"]((q2, s2_), (b2, b2s), y, m_idx)
         dt = time.perf_counter() - t0
         return dt, rows_tok.numel(), experts.numel()
 
@@ -255,7 +300,7 @@ def cpu_layer_sample(x, ids, w1, s1, w2, s2, ue8m0=False, budget_s: float = 4.0,
     dt = statistics.median(times)
     flops = 2.0 * rows * (I2 * H + H * inter)
     desc = (f"c4 layer: {n_tok} tokens ({rows} routed rows over {n_exp} experts), FC1 + SiLU-mul requant + FC2 "
-            f"with the oracle GEMM, median of {len(times)} calls ({dt:.2f} s each), "
+            f"with the {_impl_name(impl)}, median of {len(times)} calls ({dt:.2f} s each), "
             f"torch CPU threads={torch.get_num_threads()}")
     return flops / dt / 1e12, torch.get_num_threads(), desc
 
@@ -273,7 +318,8 @@ def _layer_inputs(dev, rank, world, ue8m0=False):
 
 
 def run_reference(args):
-    """The reference's CPU path (oracle port) on rank 0: each step is a bounded sample."""
+    """The reference's CPU path (`cpu_impl`: its own code from baseline/_ref when installed, else
+    the oracle port) on rank 0, with all host threads: each step is a bounded sample."""
     from consumer_deep_gemm import synthetic
 
     if int(os.environ.get("RANK", "0")) != 0:
@@ -301,7 +347,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
         "config": {"workload": cfg_name, "parallelism": "cpu"},
-        "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": "port", "sample": desc},
+        "cpu_baseline": {"value": v, "unit": unit, "cores": cores, "kind": cpu_impl()["kind"], "sample": desc},
         "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -680,7 +726,8 @@ def bench_gemm(args, dev, cfg_name):
     }
     if not args.no_cpu_baseline:
         rates, cores, desc = cpu_port_sample(inp, budget_s=3.0)
-        line["cpu_baseline"] = {"value": rates[line["unit"]], "unit": line["unit"], "cores": cores, "kind": "port",
+        line["cpu_baseline"] = {"value": rates[line["unit"]], "unit": line["unit"], "cores": cores,
+                                "kind": cpu_impl()["kind"],
                                 "sample": desc}
     return line
 
@@ -854,7 +901,7 @@ def bench_layer(args, dev, world, rank, dist, cfg_name):
 
 def _layer_cpu_baseline(x, ids, b1, s1, b2, s2, ue8m0):
     v, cores, desc = cpu_layer_sample(x, ids, b1, s1, b2, s2, ue8m0=ue8m0, budget_s=3.0)
-    return {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": desc}
+    return {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": cpu_impl()["kind"], "sample": desc}
 
 
 def bench_ep_decode(args, dev, world, rank, dist):

@@ -34,3 +34,26 @@ def test_bench_pow2_quantiser_matches_the_tests_one():
     q1, s1 = bench._quant_pow2(x)
     q2, s2 = cast_to_fp8_pow2(x)
     assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2)
+
+
+def test_bench_cpu_impl_matches_the_oracle():
+    """The CPU implementation the bench times (the reference's own pure-torch path from
+    baseline/_ref when that install exists, else the oracle) gives the oracle's bits on a
+    golden case, so the timed CPU baseline computes what the parity tests check against."""
+    from conftest import load_gemm_case
+    from oracle import cdg_oracle as oracle
+
+    impl = bench.cpu_impl()
+    c = load_gemm_case("edge_aligned_3groups")
+    d = torch.empty(c["d"].shape, dtype=torch.bfloat16)
+    impl["gemm"]((c["a"], c["sa"]), (c["b"], c["sb"]), d, c["m_indices"])
+    d_or = torch.empty_like(d)
+    oracle.m_grouped_fp8_fp4_gemm_nt_contiguous((c["a"], c["sa"]), (c["b"], c["sb"]), d_or, c["m_indices"])
+    assert torch.equal(d.view(torch.int16), d_or.view(torch.int16)), impl["kind"]
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(8, 384, generator=g) * 2
+    from deep_gemm.utils.math import per_block_cast_to_fp8
+
+    q1, s1 = impl["quant"](x)
+    q2, s2 = per_block_cast_to_fp8(x)
+    assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2)
