@@ -701,7 +701,10 @@ def bench_gemm(args, dev, cfg_name):
     tensor_roof = {"bound": "tensor", "achieved": achieved_tf, "peak": 2 * bf16_peak, "unit": "TFLOP/s",
                    "frac": achieved_tf / (2 * bf16_peak), "traffic": NCU_TRAFFIC.get(cfg.name),
                    "peak_source": peak_src + " (2 x BF16 GEMM burst)", "kernel_ms": kernel_ms,
-                   "algorithmic_flops": flops}
+                   "algorithmic_flops": flops,
+                   # FP32 activation scales: two e4m3 planes per activation on the tensor cores
+                   "mma_planes": 1 if cfg.ue8m0_scales else 2,
+                   "issued_frac": achieved_tf * (1 if cfg.ue8m0_scales else 2) / (2 * bf16_peak)}
     hbm_bound = cfg.name == "c1"  # decode is HBM-bound; the prefill shapes are tensor-bound
     line = {
         "metric": METRIC,
@@ -886,7 +889,14 @@ def bench_layer(args, dev, world, rank, dist, cfg_name):
                      "frac": achieved / fp8_peak, "traffic": None, "kernel": "FC1 GEMM's tensor-core kernels",
                      "kernel_ms": fc1_ms, "algorithmic_flops": f_fc1,
                      "peak_source": f"2 x {peak_src} BF16 GEMM burst (dense FP8:BF16 = 2:1)",
-                     "frac_of_sustained": (achieved / (2 * bf16_sus)) if bf16_sus else None},
+                     "frac_of_sustained": (achieved / (2 * bf16_sus)) if bf16_sus else None,
+                     # with FP32 activation scales the tensor cores multiply two e4m3 planes (hi, lo)
+                     # per activation, twice the algorithmic MMA work: the plane path's ceiling is
+                     # half the FP8 peak; issued = what the tensor pipe actually executed
+                     "mma_planes": 1 if ue8m0 else 2,
+                     "issued_frac": achieved * (1 if ue8m0 else 2) / fp8_peak,
+                     "issued_frac_of_sustained": (achieved * (1 if ue8m0 else 2) / (2 * bf16_sus)) if bf16_sus
+                     else None},
         "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "copies": "per rank: its tokens, routing and weights up, its output rows down; step i's upload "
