@@ -63,6 +63,7 @@ NCU_TRAFFIC = {
     "c1": 2.008183e9 + 0.223044e9,  # cdg_gemm_pair_kernel<16, 4>: profiles/cdg_gemm_pair_kernel16_c1_decode.md
     "c2": 1.427530e9 + 0.654704e9,  # cdg_gemm_planes_kernel: profiles/cdg_gemm_planes_kernel_c2_prefill.md
     "c2u": 1.281316e9 + 0.648415e9,  # cdg_gemm_direct_kernel: profiles/cdg_gemm_direct_kernel_c2u_prefill.md
+    "c3": 3.371419e9 + 1.185789e9,  # cdg_gemm_planes_kernel: profiles/cdg_gemm_planes_kernel_c3_prefill.md
 }
 LAYER_TOL = 1e-2  # end-to-end layer tolerance (normwise and per-row L2), see parity_layer
 
