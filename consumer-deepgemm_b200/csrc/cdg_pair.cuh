@@ -358,10 +358,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairSmem<TOK, NI>::k
       }
       const int rows = p.fill_rest ? nrows - zero_from : 0;
       const uint4 z = make_uint4(0, 0, 0, 0);
-      for (int c = tid; c < rows * 16; c += 128) {
-        const int r = row0 + zero_from + (c >> 4);
-        __nv_bfloat16* rp = d_row(p, r);
-        if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + (c & 15) * 8) = z;
+      if (p.d_rows == nullptr) {  // the common case, without the row table's per-store branch
+        __nv_bfloat16* base = p.d + static_cast<int64_t>(row0 + zero_from) * p.d_row_stride + nt * 128;
+        for (int c = tid; c < rows * 16; c += 128)
+          *reinterpret_cast<uint4*>(base + (c >> 4) * p.d_row_stride + (c & 15) * 8) = z;
+      } else {
+        for (int c = tid; c < rows * 16; c += 128) {
+          const int r = row0 + zero_from + (c >> 4);
+          __nv_bfloat16* rp = d_row(p, r);
+          if (rp) *reinterpret_cast<uint4*>(rp + nt * 128 + (c & 15) * 8) = z;
+        }
       }
     }
   }
