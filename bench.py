@@ -186,31 +186,36 @@ def cpu_impl():
     global _CPU_IMPL
     if _CPU_IMPL is not None:
         return _CPU_IMPL
+    why = "no reference install under baseline/_ref"
     if os.path.isfile(os.path.join(_REF_PKG, "gemm.py")) and os.path.isfile(_REF_MATH):
-        import importlib.util
+        try:
+            import importlib.util
 
-        spec = importlib.util.spec_from_file_location("_cdg_reference", os.path.join(_REF_PKG, "__init__.py"),
-                                                      submodule_search_locations=[_REF_PKG])
-        pkg = importlib.util.module_from_spec(spec)
-        sys.modules[spec.name] = pkg
-        spec.loader.exec_module(pkg)
-        mspec = importlib.util.spec_from_file_location("_cdg_reference_math", _REF_MATH)
-        rmath = importlib.util.module_from_spec(mspec)
-        mspec.loader.exec_module(rmath)
-        _CPU_IMPL = {"gemm": pkg.gemm._m_grouped_fp8_fp4_dequant_mm_nt, "quant": rmath.per_block_cast_to_fp8,
-                     "kind": "reference"}
-    else:
-        from deep_gemm.utils.math import per_block_cast_to_fp8
-        from oracle import cdg_oracle as oracle
+            spec = importlib.util.spec_from_file_location("_cdg_reference", os.path.join(_REF_PKG, "__init__.py"),
+                                                          submodule_search_locations=[_REF_PKG])
+            pkg = importlib.util.module_from_spec(spec)
+            sys.modules[spec.name] = pkg
+            spec.loader.exec_module(pkg)
+            mspec = importlib.util.spec_from_file_location("_cdg_reference_math", _REF_MATH)
+            rmath = importlib.util.module_from_spec(mspec)
+            mspec.loader.exec_module(rmath)
+            _CPU_IMPL = {"gemm": pkg.gemm._m_grouped_fp8_fp4_dequant_mm_nt, "quant": rmath.per_block_cast_to_fp8,
+                         "kind": "reference"}
+            return _CPU_IMPL
+        except Exception as e:  # a broken install falls back to the port, and the line says why
+            sys.modules.pop("_cdg_reference", None)
+            why = f"baseline/_ref failed to import ({type(e).__name__}: {e})"
+    from deep_gemm.utils.math import per_block_cast_to_fp8
+    from oracle import cdg_oracle as oracle
 
-        _CPU_IMPL = {"gemm": oracle.m_grouped_fp8_fp4_gemm_nt_contiguous, "quant": per_block_cast_to_fp8,
-                     "kind": "port"}
+    _CPU_IMPL = {"gemm": oracle.m_grouped_fp8_fp4_gemm_nt_contiguous, "quant": per_block_cast_to_fp8,
+                 "kind": "port", "why": why}
     return _CPU_IMPL
 
 
 def _impl_name(impl):
     return ("reference's own _m_grouped_fp8_fp4_dequant_mm_nt (baseline/_ref)" if impl["kind"] == "reference"
-            else "oracle port of the reference's GEMM")
+            else f"oracle port of the reference's GEMM ({impl['why']})")
 
 
 def cpu_port_sample(inp, budget_s: float = 4.0, calls: int = 3, warmup: int = 0):
